@@ -1,0 +1,336 @@
+"""Benchmark of the exact flat search hot path (config C2: 1M x 128 euclidean, 10k queries, k=10).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one exact top-k search of all queries over the whole database
+(sharded by rows across N GPUs, one process per GPU under torchrun; local
+top-k, NCCL allgather of k candidates per query, device merge). Prints one
+JSON line on rank 0. Data are synthetic (csrc/fixtures.cpp) with the
+configuration's shapes; nothing reads the reference tree at run time.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "queries/s: exact 1M×128 k=10 (FlatIndex batched search, euclidean)"
+CONFIG = {"workload": "C2 exact flat search: 1,000,000 x 128 f32 (integers in [0,255], 1,024 blobs, sigma 20), "
+                      "10,000 queries, k=10, euclidean",
+          "n": 1_000_000, "dim": 128, "queries": 10_000, "k": 10}
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--n", type=int, default=1_000_000)
+    p.add_argument("--nq", type=int, default=10_000)
+    p.add_argument("--k", type=int, default=10)
+    p.add_argument("--dim", type=int, default=128)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=12.0)
+    return p.parse_args()
+
+
+def peaks():
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured (MEASURED_PEAKS.json)"
+    return 6650.0, 1590.0, "fallback (profiling recipe)"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None):
+        self.uuid = uuid
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+        self.t0 = self.t1 = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 10:
+                continue
+            if self.uuid and self.uuid not in parts[1]:
+                continue
+            rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return None
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        mx = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, v in zip(names, r[6:10]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def cpu_baseline(db: np.ndarray, queries: np.ndarray, k: int, seconds: float) -> dict:
+    """The oracle port of FlatIndex::search on all host cores, on a bounded query sample."""
+    from oracle import pxo
+
+    threads = os.cpu_count() or 1
+    batch = max(threads, 8)
+    pxo.flat_search(db, queries[:batch], k, pxo.EUCLIDEAN, nthreads=threads)  # warm
+    done, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds and done + batch <= len(queries):
+        pxo.flat_search(db, queries[done:done + batch], k, pxo.EUCLIDEAN, nthreads=threads)
+        done += batch
+    el = time.perf_counter() - t0
+    return {"value": done / el, "unit": "queries/s", "cores": threads, "kind": "port",
+            "sample": f"{done} of the {len(queries)} queries against the full {db.shape[0]:,}-row database "
+                      f"({el:.1f} s, C++ oracle restating FlatIndex::search, one query per thread at a time)"}
+
+
+def run_reference(args):
+    """--impl reference: the reference algorithm on the host cores (the oracle port; no Rust toolchain here)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from proxima_b200 import fixtures
+    from oracle import pxo
+
+    db = fixtures.c2_database(args.n, args.dim)
+    queries = fixtures.c2_queries(args.nq, args.dim)
+    threads = os.cpu_count() or 1
+    per_step = max(threads, 16)
+    for w in range(args.warmup):
+        pxo.flat_search(db, queries[w * per_step % args.nq:][:per_step], args.k, pxo.EUCLIDEAN, nthreads=threads)
+    t0 = time.perf_counter()
+    off = 0
+    for _ in range(args.steps):
+        q = queries[off:off + per_step]
+        if len(q) < per_step:
+            off, q = 0, queries[:per_step]
+        pxo.flat_search(db, q, args.k, pxo.EUCLIDEAN, nthreads=threads)
+        off += per_step
+    el = time.perf_counter() - t0
+    qps = args.steps * per_step / el
+    line = {"metric": METRIC, "value": qps, "unit": "queries/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": el * 1000 / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": dict(CONFIG, parallelism=f"host threads {threads}"), "impl": "reference",
+            "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": threads, "kind": "port",
+                             "sample": f"each step = {per_step} queries over the full {args.n:,}-row database "
+                                       "(C++ restatement of FlatIndex::search; the Rust reference cannot be built here)"},
+            "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+
+    from proxima_b200 import _native as N
+    from proxima_b200 import fixtures
+    from proxima_b200.index import Context
+
+    n, dim, nq, k = args.n, args.dim, args.nq, args.k
+    lo, hi = rank * n // world, (rank + 1) * n // world
+    shard = fixtures.blobs_u8(hi - lo, dim, 1024, fixtures.C2_CENTRES, fixtures.C2_BASE, row_begin=lo)
+    queries = fixtures.c2_queries(nq, dim)
+
+    ctx = Context(local)
+    lib = N.load()
+    h = N.vp()
+    N.call("pxc_flat_create", ctx.handle, dim, 0, C.byref(h))
+    gids = np.arange(lo, hi, dtype=np.uint64)
+    N.call("pxc_flat_sync", h, N.ptr(shard), N.ptr(gids), None, 0, hi - lo)
+    path = lib.pxc_flat_path(h)
+
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    q_host = torch.from_numpy(queries).pin_memory()
+    q_dev = q_host.to(dev)
+    ids = torch.empty((nq, k), dtype=torch.int64, device=dev)
+    dists = torch.empty((nq, k), dtype=torch.float32, device=dev)
+    lens = torch.empty(nq, dtype=torch.int32, device=dev)
+    if world > 1:
+        g_ids = torch.empty((world, nq, k), dtype=torch.int64, device=dev)
+        g_d = torch.empty((world, nq, k), dtype=torch.float32, device=dev)
+        g_l = torch.empty((world, nq), dtype=torch.int32, device=dev)
+        m_ids = torch.empty((nq, k), dtype=torch.int64, device=dev)
+        m_d = torch.empty((nq, k), dtype=torch.float32, device=dev)
+        m_l = torch.empty(nq, dtype=torch.int32, device=dev)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MiB > 126 MB L2
+
+    def step(q_ptr):
+        N.call("pxc_flat_search_device", h, q_ptr, nq, k, None, ids.data_ptr(), dists.data_ptr(),
+               lens.data_ptr(), sp)
+        if world > 1:
+            dist.all_gather_into_tensor(g_ids, ids)
+            dist.all_gather_into_tensor(g_d, dists)
+            dist.all_gather_into_tensor(g_l, lens)
+            N.call("pxc_topk_merge", ctx.handle, g_ids.data_ptr(), g_d.data_ptr(), g_l.data_ptr(), world, nq, k, k,
+                   m_ids.data_ptr(), m_d.data_ptr(), m_l.data_ptr(), sp)
+
+    N.call("pxc_ctx_set_profiling", ctx.handle, 1)
+    for _ in range(max(3, args.warmup)):
+        step(q_dev.data_ptr())
+    torch.cuda.synchronize(dev)
+
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    sampler = ClockSampler(uuid)
+    sampler.start()
+    launches0 = lib.pxc_ctx_launch_count(ctx.handle)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    scan_ms = []
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    for i in range(args.steps):
+        flush.zero_()  # evict L2 between timed steps (not timed)
+        ev[i][0].record(stream)
+        step(q_dev.data_ptr())
+        ev[i][1].record(stream)
+        scan_ms.append(lib.pxc_flat_last_scan_ms(h))
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    launches = lib.pxc_ctx_launch_count(ctx.handle) - launches0
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    total_ms = torch.tensor([sum(step_ms)], dtype=torch.float64, device=dev)
+    scan_mean = torch.tensor([sum(scan_ms) / len(scan_ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
+        dist.all_reduce(scan_mean, op=dist.ReduceOp.MAX)
+    ms_per_step = total_ms.item() / args.steps
+    clocks = sampler.stop()
+
+    # ---- e2e: host buffers in, host results out, every step ----
+    out_ids = torch.empty((nq, k), dtype=torch.int64).pin_memory()
+    out_d = torch.empty((nq, k), dtype=torch.float32).pin_memory()
+    out_l = torch.empty(nq, dtype=torch.int32).pin_memory()
+    h2d = nq * dim * 4
+    d2h = nq * k * 12 + nq * 4
+    e2e_steps = max(3, min(args.steps, 50))
+
+    def e2e_step():
+        if world == 1:
+            N.call("pxc_flat_search", h, q_host.data_ptr(), nq, k, None, out_ids.data_ptr(), out_d.data_ptr(),
+                   out_l.data_ptr())
+        else:
+            qd = q_host.to(dev, non_blocking=True)
+            step(qd.data_ptr())
+            out_ids.copy_(m_ids, non_blocking=True)
+            out_d.copy_(m_d, non_blocking=True)
+            out_l.copy_(m_l, non_blocking=True)
+            torch.cuda.synchronize(dev)
+
+    for _ in range(2):
+        e2e_step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    e2e_s = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
+    e2e_qps = nq * e2e_steps / e2e_s.item()
+
+    if rank == 0:
+        hbm, bf16, src = peaks()
+        # K1 is u8 x u8 -> s32 on tcgen05 (kind::i8); B200's dense int8 rate is twice its dense bf16 rate.
+        peak_tops = 2.0 * bf16 if path == 1 else None
+        ops = 2.0 * (hi - lo) * dim * nq  # per launch of the scan kernel on this rank
+        achieved = ops / (scan_mean.item() / 1e3) / 1e12 if scan_mean.item() > 0 else None
+        traffic = None
+        tf = ROOT / "profiles" / "traffic.json"
+        if tf.exists():
+            t = json.loads(tf.read_text()).get("flat_u8_kernel_c2_bytes_per_launch")
+            if t and world == 1:
+                traffic = t
+        roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_tops, "unit": "TOPS",
+                    "frac": (achieved / peak_tops) if (achieved and peak_tops) else None, "traffic": traffic,
+                    "kernel": "flat_u8_kernel (K1)" if path == 1 else "dist_chunk_kernel + select (K1g)",
+                    "kernel_ms": scan_mean.item(),
+                    "peak_source": f"2 x dense bf16 {src} = dense int8 rate",
+                    "algorithmic_ops_per_launch": ops}
+        line = {"metric": METRIC, "value": nq / (ms_per_step / 1e3), "unit": "queries/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "u8" if path == 1 else "f32",
+                "data": "synthetic",
+                "config": dict(CONFIG, l2="flushed (256 MiB write) between timed steps",
+                               parallelism=f"row shards x{world}" if world > 1 else "single GPU",
+                               scan_path="tensor-core u8 (exact)" if path == 1 else "fp32 reference order"),
+                "clocks": clocks, "gpu_launches": int(launches),
+                "e2e": {"value": e2e_qps, "unit": "queries/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                "roofline": roofline}
+        if world == 1 and not args.no_cpu_baseline:
+            db = shard
+            line["cpu_baseline"] = cpu_baseline(db, queries, k, args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    lib.pxc_flat_destroy(h)
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

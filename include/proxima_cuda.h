@@ -1,0 +1,154 @@
+/*
+ * proxima_cuda.h — C ABI of libproxima_cuda.so, the B200 (sm_100a) backend for
+ * Proxima's nearest-neighbour hot path.
+ *
+ * Plain C types only: pointers, sizes, integer codes. No C++ exception and no
+ * CUDA error crosses this boundary; every entry point returns a pxc_status and,
+ * when `err` is non-NULL, fills a pxc_error describing the failure.
+ *
+ * Each entry point names the reference interface (Liona-orph/proxima, Rust)
+ * it replaces. The Rust side keeps its types and calls these through a thin
+ * FFI crate (`proxima-cuda`); see INTEGRATION.md for the binding.
+ *
+ * Conventions shared by all entry points:
+ *  - Host pointers are borrowed for the duration of the call and copied; no
+ *    pointer is retained after return.
+ *  - Vectors are row-major f32, `dim` floats per row. "Prepared" means
+ *    VectorSpace::prepare has been applied (validated; cosine rows normalised),
+ *    crates/proxima-core/src/space.rs:130-138.
+ *  - Results are ordered ascending by (f32::total_cmp(distance), id), the
+ *    order of SearchResult (crates/proxima-core/src/topk.rs:63-67). Result row
+ *    q occupies out[q*k .. q*k+k); out_len[q] says how many entries are valid.
+ *  - Filters are bitmaps over slots: bit (s & 63) of word s/64 set means slot s
+ *    is accepted; NULL accepts all (the AcceptAll filter,
+ *    crates/proxima-index/src/index.rs:43-50).
+ *  - Handles are used by one thread at a time for mutation (sync/destroy); the
+ *    search entry points may be called concurrently on one handle.
+ */
+#ifndef PROXIMA_CUDA_H
+#define PROXIMA_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes: one per ProximaError variant (crates/proxima-core/src/error.rs:37-160),
+ *      plus device and timeout failures, which map to ProximaError::Internal ---- */
+typedef int32_t pxc_status;
+#define PXC_OK 0
+#define PXC_DIMENSION_MISMATCH 1 /* a = expected, b = actual */
+#define PXC_UNKNOWN_ID 2         /* a = id */
+#define PXC_DUPLICATE_ID 3       /* a = id */
+#define PXC_CAPACITY 4           /* a = limit, detail = what */
+#define PXC_NON_FINITE 5         /* a = component index */
+#define PXC_CORRUPTION 6
+#define PXC_CONFIGURATION 7      /* parameter, a = value, detail = reason */
+#define PXC_INTERNAL 8
+#define PXC_IO 9
+#define PXC_DEVICE 10            /* a CUDA error; detail holds its text */
+#define PXC_TIMEOUT 11           /* a device-side bounded wait gave up */
+
+typedef struct pxc_error {
+  int32_t code;
+  uint64_t a;
+  uint64_t b;
+  char parameter[32];
+  char detail[256];
+} pxc_error;
+
+/* metric codes, in the declaration order of proxima_core::Metric
+ * (crates/proxima-core/src/distance.rs:90-135) */
+#define PXC_EUCLIDEAN 0
+#define PXC_COSINE 1
+#define PXC_INNER_PRODUCT 2
+#define PXC_MANHATTAN 3
+
+/* Largest k a search accepts: check_k (crates/proxima-index/src/index.rs:212-224). */
+#define PXC_MAX_K (1u << 24)
+
+/* ---- version / capability ---- */
+/* Returns the ABI version (major << 16 | minor). */
+uint32_t pxc_abi_version(void);
+
+/* ---- context: one CUDA device, its streams and scratch ----
+ * Replaces nothing in the reference (which is single-threaded CPU code); it
+ * owns the device state every handle below is created on. Exactly one device
+ * per context: multi-GPU runs use one process (and one context) per GPU and
+ * exchange candidates with NCCL (see pxc_topk_merge). */
+typedef struct pxc_ctx pxc_ctx;
+pxc_status pxc_ctx_create(const int* devices, int n_devices, pxc_ctx** out, pxc_error* err);
+void pxc_ctx_destroy(pxc_ctx* ctx);
+/* Device-side wait limit in milliseconds for kernels with bounded spins
+ * (default 2000). A wait that runs out returns PXC_TIMEOUT. */
+pxc_status pxc_ctx_set_wait_limit(pxc_ctx* ctx, uint32_t milliseconds, pxc_error* err);
+
+/* ---- observability ----
+ * Count of kernels this library launched on the context since creation
+ * (every scan, selection, merge and mirror-maintenance kernel). */
+uint64_t pxc_ctx_launch_count(const pxc_ctx* ctx);
+/* When on, the searches record CUDA events around their dominant scan kernel
+ * on the launching stream; pxc_flat_last_scan_ms reads the last duration
+ * (milliseconds, synchronising on the end event). Off by default. */
+pxc_status pxc_ctx_set_profiling(pxc_ctx* ctx, int32_t on, pxc_error* err);
+
+/* ---- FlatIndex: exact filtered top-k ----
+ * Replaces the scan loop of FlatIndex::search
+ * (crates/proxima-index/src/flat.rs:153-169) and adds the batched form
+ * search_batch. The device holds a mirror of the VectorStore
+ * (crates/proxima-core/src/storage.rs:100-115): slot-major prepared rows,
+ * the VectorId of each slot and a live flag. */
+typedef struct pxc_flat pxc_flat;
+pxc_status pxc_flat_create(pxc_ctx* ctx, uint32_t dim, int32_t metric, pxc_flat** out,
+                           pxc_error* err);
+void pxc_flat_destroy(pxc_flat* h);
+/* Copy slots [slot_begin, slot_begin + nslots) of the host store into the
+ * mirror: `rows` nslots*dim prepared floats, `ids` the VectorId per slot
+ * (NULL means id == slot), `live` one byte per slot (NULL means all live).
+ * Slots beyond the current high-water mark grow the mirror. Rows must be
+ * finite (PXC_NON_FINITE otherwise, a = flat component index). */
+pxc_status pxc_flat_sync(pxc_flat* h, const float* rows, const uint64_t* ids,
+                         const uint8_t* live, uint64_t slot_begin, uint64_t nslots,
+                         pxc_error* err);
+/* Shrink the mirror to `nslots` slots (after VectorStore::clear or compaction). */
+pxc_status pxc_flat_truncate(pxc_flat* h, uint64_t nslots, pxc_error* err);
+/* Number of live slots in the mirror. */
+uint64_t pxc_flat_len(const pxc_flat* h);
+/* Batched exact search with HOST buffers: `queries` nq*dim prepared floats,
+ * `bitmap` over slots or NULL; outputs nq*k ids and distances and nq lengths.
+ * Dimension is fixed at create; k <= PXC_MAX_K. */
+pxc_status pxc_flat_search(pxc_flat* h, const float* queries, uint32_t nq, uint32_t k,
+                           const uint64_t* bitmap, uint64_t* out_ids, float* out_dist,
+                           uint32_t* out_len, pxc_error* err);
+/* Same, with DEVICE buffers on the context's device, ordered on `stream`
+ * (a cudaStream_t; NULL = the context's stream). Returns after the work is
+ * enqueued; the caller synchronises the stream. */
+pxc_status pxc_flat_search_device(pxc_flat* h, const float* d_queries, uint32_t nq,
+                                  uint32_t k, const uint64_t* d_bitmap, uint64_t* d_out_ids,
+                                  float* d_out_dist, uint32_t* d_out_len, void* stream,
+                                  pxc_error* err);
+/* Which scan kernel the next search will use: 1 = tensor-core u8 (every live
+ * row and the queries are integers in [0,255] under euclidean, so the u8
+ * product is exact), 0 = fp32 reference-order scan. Diagnostic only. */
+int32_t pxc_flat_path(const pxc_flat* h);
+/* Duration of the last search's scan kernel (K1 or K1g), with profiling on;
+ * -1 when not recorded. */
+float pxc_flat_last_scan_ms(pxc_flat* h);
+
+/* ---- multi-GPU merge ----
+ * After each rank searched its own row shard, an allgather leaves `nparts`
+ * candidate lists per query on every rank: part p of query q at
+ * [(p*nq + q)*k_in, ...), lengths at lens[p*nq + q]. Merges them into the
+ * top-k by (total_cmp(distance), id). DEVICE buffers. This is TopK::push over
+ * the union (crates/proxima-core/src/topk.rs:119-138). */
+pxc_status pxc_topk_merge(pxc_ctx* ctx, const uint64_t* d_ids, const float* d_dist,
+                          const uint32_t* d_lens, uint32_t nparts, uint32_t nq, uint32_t k_in,
+                          uint32_t k, uint64_t* d_out_ids, float* d_out_dist,
+                          uint32_t* d_out_len, void* stream, pxc_error* err);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PROXIMA_CUDA_H */

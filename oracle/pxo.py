@@ -1,0 +1,308 @@
+"""ctypes wrapper of the CPU oracle (oracle/lib/liboracle.so).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and the
+CPU legs of bench.py (cpu_baseline and --impl reference), as the checker or
+the timed CPU baseline. The product path never imports it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB = HERE / "lib" / "liboracle.so"
+
+EUCLIDEAN, COSINE, INNER_PRODUCT, MANHATTAN = 0, 1, 2, 3
+RANGE_GLOBAL, RANGE_PER_DIMENSION = 0, 1
+CODE_U8, CODE_I8 = 0, 1
+
+_lib = None
+vp, u64, i64, f32, f64, i32 = C.c_void_p, C.c_uint64, C.c_int64, C.c_float, C.c_double, C.c_int
+
+
+class Rng(C.Structure):
+    _fields_ = [("key", C.c_uint32 * 8), ("counter", C.c_uint64), ("buf", C.c_uint32 * 64),
+                ("index", C.c_uint32)]
+
+
+class IvfReport(C.Structure):
+    _fields_ = [("sampled", u64), ("coarse_iterations", u64), ("populated_lists", u64),
+                ("largest_list", u64), ("produced", u64), ("coarse_inertia", f64),
+                ("residual_inertia", f64)]
+
+
+def build() -> Path:
+    if not LIB.exists() or LIB.stat().st_mtime < (HERE / "pxo.cpp").stat().st_mtime:
+        subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    return LIB
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        L = C.CDLL(str(LIB))
+        sig = {
+            "pxo_squared_euclidean": (f32, [vp, vp, u64]),
+            "pxo_squared_euclidean_scalar": (f32, [vp, vp, u64]),
+            "pxo_dot": (f32, [vp, vp, u64]),
+            "pxo_manhattan": (f32, [vp, vp, u64]),
+            "pxo_cosine": (f32, [vp, vp, u64]),
+            "pxo_cosine_normalized": (f32, [vp, vp, u64]),
+            "pxo_normalize_in_place": (f32, [vp, u64]),
+            "pxo_space_distance": (f32, [i32, vp, vp, u64]),
+            "pxo_prepare": (i64, [i32, vp, u64, u64]),
+            "pxo_flat_search": (None, [vp, vp, vp, u64, u64, i32, vp, u64, u64, vp, vp, vp, vp, i32]),
+            "pxo_recall_overlap": (f32, [vp, C.c_uint32, vp, C.c_uint32]),
+            "pxo_rng_seed_from_u64": (None, [vp, u64]),
+            "pxo_rng_next_u32": (C.c_uint32, [vp]),
+            "pxo_rng_next_u64": (u64, [vp]),
+            "pxo_rng_gen_range_usize": (u64, [vp, u64]),
+            "pxo_rng_gen_range_f64": (f64, [vp, f64, f64]),
+            "pxo_kmeans": (u64, [vp, u64, u64, u64, u64, vp, u64, vp, vp, vp, vp, vp, i32]),
+            "pxo_kmeans_nearest": (C.c_uint32, [vp, vp, u64, u64, vp]),
+            "pxo_pq_layout": (None, [u64, u64, vp, vp]),
+            "pxo_pq_train": (i32, [vp, u64, u64, u64, u64, u64, vp, vp, vp, i32]),
+            "pxo_pq_encode": (None, [vp, u64, u64, vp, u64, vp]),
+            "pxo_pq_decode": (None, [vp, u64, u64, vp, u64, vp]),
+            "pxo_pq_distance_table": (None, [vp, u64, u64, vp, vp, vp]),
+            "pxo_pq_adc_squared": (f32, [vp, u64, vp]),
+            "pxo_pq_adc_inner": (f32, [vp, u64, vp]),
+            "pxo_sq_train": (i64, [vp, u64, u64, i32, vp, vp, vp]),
+            "pxo_sq_encode": (None, [vp, vp, u64, i32, i32, vp, u64, vp]),
+            "pxo_sq_decode": (None, [vp, vp, u64, i32, i32, vp, u64, vp]),
+            "pxo_sq_asymmetric_squared_l2": (f32, [vp, vp, u64, i32, i32, vp, vp]),
+            "pxo_sq_asymmetric_inner_product": (f32, [vp, vp, u64, i32, i32, vp, vp]),
+            "pxo_ivf_nearest_centroid": (C.c_uint32, [vp, vp, u64, u64]),
+            "pxo_ivfpq_train": (u64, [vp, vp, u64, u64, u64, u64, u64, u64, u64, vp, vp, vp, vp, vp,
+                                      vp, vp, i32]),
+            "pxo_ivfpq_encode_all": (None, [vp, vp, u64, u64, vp, u64, vp, u64, vp, vp, i32]),
+            "pxo_ivfpq_search": (None, [vp, vp, vp, u64, u64, i32, vp, u64, vp, u64, vp, vp, vp, u64,
+                                        u64, u64, u64, vp, vp, vp, vp, i32]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data
+
+
+def f32a(x) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(x, dtype=np.float32))
+
+
+def threads() -> int:
+    return os.cpu_count() or 1
+
+
+# ---- distance.rs ----
+def squared_euclidean(a, b) -> float:
+    a, b = f32a(a), f32a(b)
+    return lib().pxo_squared_euclidean(_p(a), _p(b), min(a.size, b.size))
+
+
+def squared_euclidean_scalar(a, b) -> float:
+    a, b = f32a(a), f32a(b)
+    return lib().pxo_squared_euclidean_scalar(_p(a), _p(b), min(a.size, b.size))
+
+
+def dot(a, b) -> float:
+    a, b = f32a(a), f32a(b)
+    return lib().pxo_dot(_p(a), _p(b), min(a.size, b.size))
+
+
+def manhattan(a, b) -> float:
+    a, b = f32a(a), f32a(b)
+    return lib().pxo_manhattan(_p(a), _p(b), min(a.size, b.size))
+
+
+def cosine(a, b) -> float:
+    a, b = f32a(a), f32a(b)
+    return lib().pxo_cosine(_p(a), _p(b), min(a.size, b.size))
+
+
+def cosine_normalized(a, b) -> float:
+    a, b = f32a(a), f32a(b)
+    return lib().pxo_cosine_normalized(_p(a), _p(b), min(a.size, b.size))
+
+
+def normalized(v) -> np.ndarray:
+    v = f32a(v).copy()
+    lib().pxo_normalize_in_place(_p(v), v.size)
+    return v
+
+
+def prepare(metric: int, rows) -> np.ndarray:
+    r = f32a(rows).copy()
+    if r.ndim == 1:
+        r = r[None, :]
+    bad = lib().pxo_prepare(metric, _p(r), r.shape[0], r.shape[1])
+    if bad >= 0:
+        raise ValueError(f"non-finite component {bad}")
+    return r
+
+
+def space_distance(metric: int, a, b) -> float:
+    a, b = f32a(a), f32a(b)
+    return lib().pxo_space_distance(metric, _p(a), _p(b), a.size)
+
+
+# ---- flat.rs ----
+def flat_search(data, queries, k: int, metric: int, ids=None, live=None, bitmap=None, nthreads=None):
+    """Exact top-k of prepared queries over prepared slot-major data."""
+    data, queries = f32a(data), f32a(queries)
+    nslots, dim = data.shape
+    nq = queries.shape[0]
+    kk = max(k, 1)
+    out_ids = np.zeros((nq, kk), dtype=np.uint64)
+    out_d = np.zeros((nq, kk), dtype=np.float32)
+    out_len = np.zeros(nq, dtype=np.uint32)
+    ids = None if ids is None else np.ascontiguousarray(ids, dtype=np.uint64)
+    live = None if live is None else np.ascontiguousarray(live, dtype=np.uint8)
+    bitmap = None if bitmap is None else np.ascontiguousarray(bitmap, dtype=np.uint64)
+    lib().pxo_flat_search(_p(data), _p(ids), _p(live), nslots, dim, metric, _p(queries), nq, k,
+                          _p(bitmap), _p(out_ids), _p(out_d), _p(out_len), nthreads or threads())
+    return out_ids[:, :k], out_d[:, :k], out_len
+
+
+# ---- kmeans.rs ----
+def kmeans(points, k: int, max_iterations: int, init=None, seed: int = 0, nthreads=None):
+    pts = f32a(points)
+    n, dim = pts.shape
+    kk = max(min(k, n), 1)
+    cent = np.zeros((kk, dim), dtype=np.float32)
+    assign = np.zeros(max(n, 1), dtype=np.uint32)
+    inertia = C.c_double()
+    iters = C.c_uint64()
+    init = None if init is None else f32a(init)
+    lib().pxo_kmeans(_p(pts), n, dim, k, max_iterations, _p(init), seed, None, _p(cent),
+                     _p(assign), C.byref(inertia), C.byref(iters), nthreads or threads())
+    return cent, assign[:n], inertia.value, iters.value
+
+
+# ---- product.rs ----
+def pq_layout(dim: int, m: int):
+    w = np.zeros(m, dtype=np.uint32)
+    o = np.zeros(m + 1, dtype=np.uint32)
+    lib().pxo_pq_layout(dim, m, _p(w), _p(o))
+    return w, o
+
+
+def pq_train(training, m: int, max_iterations: int = 25, seed: int = 0x5EED1EAF, nthreads=None):
+    t = f32a(training)
+    n, dim = t.shape
+    books = np.zeros(256 * dim, dtype=np.float32)
+    inertia = C.c_double()
+    iters = C.c_uint64()
+    rc = lib().pxo_pq_train(_p(t), n, dim, m, max_iterations, seed, _p(books), C.byref(inertia),
+                            C.byref(iters), nthreads or threads())
+    if rc != 0:
+        raise ValueError("invalid PQ configuration")
+    return books, inertia.value, iters.value
+
+
+def pq_encode(books, dim: int, m: int, vectors) -> np.ndarray:
+    v = f32a(vectors).reshape(-1, dim)
+    out = np.zeros((v.shape[0], m), dtype=np.uint8)
+    lib().pxo_pq_encode(_p(f32a(books)), dim, m, _p(v), v.shape[0], _p(out))
+    return out
+
+
+def pq_decode(books, dim: int, m: int, codes) -> np.ndarray:
+    c = np.ascontiguousarray(codes, dtype=np.uint8).reshape(-1, m)
+    out = np.zeros((c.shape[0], dim), dtype=np.float32)
+    lib().pxo_pq_decode(_p(f32a(books)), dim, m, _p(c), c.shape[0], _p(out))
+    return out
+
+
+def pq_tables(books, dim: int, m: int, query):
+    sq = np.zeros(m * 256, dtype=np.float32)
+    dt = np.zeros(m * 256, dtype=np.float32)
+    lib().pxo_pq_distance_table(_p(f32a(books)), dim, m, _p(f32a(query)), _p(sq), _p(dt))
+    return sq, dt
+
+
+def pq_adc_squared(table, m: int, code) -> float:
+    c = np.ascontiguousarray(code, dtype=np.uint8)
+    return lib().pxo_pq_adc_squared(_p(f32a(table)), m, _p(c))
+
+
+# ---- scalar.rs ----
+def sq_train(training, mode: int):
+    t = f32a(training)
+    n, dim = t.shape
+    g = 1 if mode == RANGE_GLOBAL else dim
+    mn, sc, inv = (np.zeros(g, dtype=np.float32) for _ in range(3))
+    bad = lib().pxo_sq_train(_p(t), n, dim, mode, _p(mn), _p(sc), _p(inv))
+    if bad >= 0:
+        raise ValueError(f"non-finite component {bad}")
+    return mn, sc, inv
+
+
+def sq_encode(mn, inv, dim: int, mode: int, code_type: int, vectors) -> np.ndarray:
+    v = f32a(vectors).reshape(-1, dim)
+    out = np.zeros((v.shape[0], dim), dtype=np.uint8)
+    lib().pxo_sq_encode(_p(mn), _p(inv), dim, mode, code_type, _p(v), v.shape[0], _p(out))
+    return out
+
+
+def sq_decode(mn, sc, dim: int, mode: int, code_type: int, codes) -> np.ndarray:
+    c = np.ascontiguousarray(codes, dtype=np.uint8).reshape(-1, dim)
+    out = np.zeros((c.shape[0], dim), dtype=np.float32)
+    lib().pxo_sq_decode(_p(mn), _p(sc), dim, mode, code_type, _p(c), c.shape[0], _p(out))
+    return out
+
+
+def sq_asym_l2(mn, sc, dim: int, mode: int, code_type: int, query, code) -> float:
+    c = np.ascontiguousarray(code, dtype=np.uint8)
+    return lib().pxo_sq_asymmetric_squared_l2(_p(mn), _p(sc), dim, mode, code_type, _p(f32a(query)), _p(c))
+
+
+# ---- ivfpq.rs ----
+def ivfpq_train(vectors, nlist: int, m: int, max_iterations: int = 25, training_sample: int = 100_000,
+                seed: int = 0x1FF9C0D, live=None, coarse_init=None, pq_init=None, nthreads=None):
+    v = f32a(vectors)
+    n, dim = v.shape
+    cent = np.zeros((nlist, dim), dtype=np.float32)
+    books = np.zeros(256 * dim, dtype=np.float32)
+    list_of = np.zeros(n, dtype=np.uint32)
+    codes = np.zeros((n, m), dtype=np.uint8)
+    rep = IvfReport()
+    live = None if live is None else np.ascontiguousarray(live, dtype=np.uint8)
+    ci = None if coarse_init is None else f32a(coarse_init)
+    pi = None if pq_init is None else f32a(pq_init)
+    produced = lib().pxo_ivfpq_train(_p(v), _p(live), n, dim, nlist, m, max_iterations, training_sample,
+                                     seed, _p(ci), _p(pi), _p(cent), _p(books), _p(list_of), _p(codes),
+                                     C.byref(rep), nthreads or threads())
+    return cent[:produced], books, list_of, codes, rep
+
+
+def ivfpq_search(vectors, centroids, books, m: int, list_of, codes, queries, k: int, nprobe: int,
+                 rerank: int = 0, metric: int = EUCLIDEAN, ids=None, live=None, bitmap=None, nthreads=None):
+    v = None if vectors is None else f32a(vectors)
+    q = f32a(queries)
+    nq, dim = q.shape
+    nslots = len(list_of)
+    cent = f32a(centroids)
+    kk = max(k, 1)
+    out_ids = np.zeros((nq, kk), dtype=np.uint64)
+    out_d = np.zeros((nq, kk), dtype=np.float32)
+    out_len = np.zeros(nq, dtype=np.uint32)
+    lo = np.ascontiguousarray(list_of, dtype=np.uint32)
+    cd = np.ascontiguousarray(codes, dtype=np.uint8)
+    ids = None if ids is None else np.ascontiguousarray(ids, dtype=np.uint64)
+    live = None if live is None else np.ascontiguousarray(live, dtype=np.uint8)
+    bitmap = None if bitmap is None else np.ascontiguousarray(bitmap, dtype=np.uint64)
+    lib().pxo_ivfpq_search(_p(v), _p(ids), _p(live), nslots, dim, metric, _p(cent), cent.shape[0],
+                           _p(f32a(books)), m, _p(lo), _p(cd), _p(q), nq, k, nprobe, rerank, _p(bitmap),
+                           _p(out_ids), _p(out_d), _p(out_len), nthreads or threads())
+    return out_ids[:, :k], out_d[:, :k], out_len

@@ -1,0 +1,91 @@
+"""ctypes bindings for ``libproxima_cuda.so`` (the C ABI in ``include/proxima_cuda.h``).
+
+The library is built in-tree by ``proxima_b200.build``. There is no fallback:
+if the library is missing or no B200 is visible, every call fails loudly.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+from .errors import raise_for_status
+
+LIB_DIR = Path(__file__).resolve().parent / "lib"
+LIB_PATH = LIB_DIR / "libproxima_cuda.so"
+
+u8p = C.POINTER(C.c_uint8)
+u32p = C.POINTER(C.c_uint32)
+u64p = C.POINTER(C.c_uint64)
+f32p = C.POINTER(C.c_float)
+f64p = C.POINTER(C.c_double)
+vp = C.c_void_p
+
+
+class PxcError(C.Structure):
+    _fields_ = [
+        ("code", C.c_int32),
+        ("a", C.c_uint64),
+        ("b", C.c_uint64),
+        ("parameter", C.c_char * 32),
+        ("detail", C.c_char * 256),
+    ]
+
+
+# name -> (restype, argtypes); every symbol include/proxima_cuda.h declares.
+SIGNATURES: dict[str, tuple] = {
+    "pxc_abi_version": (C.c_uint32, []),
+    "pxc_ctx_create": (C.c_int32, [C.POINTER(C.c_int), C.c_int, C.POINTER(vp), C.POINTER(PxcError)]),
+    "pxc_ctx_destroy": (None, [vp]),
+    "pxc_ctx_set_wait_limit": (C.c_int32, [vp, C.c_uint32, C.POINTER(PxcError)]),
+    "pxc_flat_create": (C.c_int32, [vp, C.c_uint32, C.c_int32, C.POINTER(vp), C.POINTER(PxcError)]),
+    "pxc_flat_destroy": (None, [vp]),
+    "pxc_flat_sync": (C.c_int32, [vp, vp, vp, vp, C.c_uint64, C.c_uint64, C.POINTER(PxcError)]),
+    "pxc_flat_truncate": (C.c_int32, [vp, C.c_uint64, C.POINTER(PxcError)]),
+    "pxc_flat_len": (C.c_uint64, [vp]),
+    "pxc_flat_search": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, vp, vp, vp, vp, C.POINTER(PxcError)]),
+    "pxc_flat_search_device": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, vp, vp, vp, vp, vp,
+                                           C.POINTER(PxcError)]),
+    "pxc_flat_path": (C.c_int32, [vp]),
+    "pxc_flat_last_scan_ms": (C.c_float, [vp]),
+    "pxc_ctx_launch_count": (C.c_uint64, [vp]),
+    "pxc_ctx_set_profiling": (C.c_int32, [vp, C.c_int32, C.POINTER(PxcError)]),
+    "pxc_topk_merge": (C.c_int32, [vp, vp, vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
+                                   vp, vp, vp, vp, C.POINTER(PxcError)]),
+}
+
+_lib = None
+
+
+def load() -> C.CDLL:
+    """Load the CUDA library (once). Raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python -m proxima_b200.build`; "
+                "there is no CPU fallback for the device path")
+        lib = C.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def call(name: str, *args) -> None:
+    """Invoke a status-returning entry point and raise the mapped ProximaError."""
+    err = PxcError()
+    status = getattr(load(), name)(*args, C.byref(err))
+    if status != 0:
+        raise_for_status(status, err.a, err.b, err.parameter.decode(errors="replace"),
+                         err.detail.decode(errors="replace"))
+
+
+def ptr(arr) -> int | None:
+    """Address of a numpy array or torch tensor (None passes through)."""
+    if arr is None:
+        return None
+    if hasattr(arr, "data_ptr"):
+        return arr.data_ptr()
+    return arr.ctypes.data

@@ -1,0 +1,944 @@
+// flat.cu — FlatIndex device mirror and exact batched search.
+//
+// Replaces the scan of FlatIndex::search (crates/proxima-index/src/flat.rs:153-169).
+// Two scan kernels produce the same answer:
+//   * K1 (flat_tc.cuh): tcgen05 u8 GEMM + fused top-k, used when the metric is
+//     euclidean and every live row and query is an integer in [0,255];
+//   * K1g (below): fp32 scan in the reference's exact operation order
+//     (8 lane accumulators, pairwise reduce, tail, no FMA), used otherwise.
+// Both rank candidates by (total_cmp(distance), id): the device mirror keeps
+// the live rows in ascending VectorId order ("rank" order), so a rank index
+// breaks ties exactly as the id does.
+#include <cub/block/block_reduce.cuh>
+#include <cub/block/block_scan.cuh>
+#include <cub/device/device_radix_sort.cuh>
+#include <cub/device/device_segmented_radix_sort.cuh>
+#include <cub/device/device_select.cuh>
+
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+#include <new>
+#include <vector>
+
+#include "common.cuh"
+#include "flat_tc.cuh"
+#include "tmap.cuh"
+#include "topk.cuh"
+
+namespace pxc {
+
+constexpr uint32_t SENTINEL = 0xFFFFFFFFu;  // excluded candidate (filtered / padding)
+
+// ---------------------------------------------------------------------------
+// Reference-order distance (crates/proxima-core/src/distance.rs). All float
+// operations use the _rn intrinsics so nvcc cannot contract them into FMAs.
+// ---------------------------------------------------------------------------
+template <int METRIC>
+__device__ __forceinline__ float lane_step(float acc, float q, float x) {
+  if (METRIC == PXC_EUCLIDEAN) {
+    float d = __fsub_rn(q, x);
+    return __fadd_rn(acc, __fmul_rn(d, d));
+  } else if (METRIC == PXC_MANHATTAN) {
+    return __fadd_rn(acc, fabsf(__fsub_rn(q, x)));
+  } else {
+    return __fadd_rn(acc, __fmul_rn(q, x));
+  }
+}
+
+template <int METRIC>
+__device__ __forceinline__ float finish(const float (&acc)[8], float tail) {
+  float a = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
+  float b = __fadd_rn(__fadd_rn(acc[4], acc[5]), __fadd_rn(acc[6], acc[7]));
+  float s = __fadd_rn(__fadd_rn(a, b), tail);
+  if (METRIC == PXC_COSINE) return __fsub_rn(1.0f, s);
+  if (METRIC == PXC_INNER_PRODUCT) return -s;
+  return s;
+}
+
+__device__ __forceinline__ bool accepted(const uint64_t* bitmap, uint32_t slot) {
+  return bitmap == nullptr || ((bitmap[slot >> 6] >> (slot & 63)) & 1ull);
+}
+
+__device__ __forceinline__ uint32_t candidate_key(float d) {
+  uint32_t k = order_key(d);
+  return k == SENTINEL ? SENTINEL - 1 : k;  // keep the sentinel unambiguous
+}
+
+// K1g: distance tile of 32 queries x 64 rank rows, written as order keys into
+// D[q][r - c0] (row stride C). Thread (tq, tr) owns queries {tq, tq+16} and
+// rows {tr, tr+16, tr+32, tr+48}, each pair with eight lane accumulators.
+template <int METRIC>
+__global__ void __launch_bounds__(256) dist_chunk_kernel(
+    const float* __restrict__ Q, uint32_t nq, const float* __restrict__ X, uint64_t nrank,
+    uint32_t dim, uint64_t c0, uint32_t C, const uint64_t* __restrict__ bitmap,
+    const uint32_t* __restrict__ rank_slot, uint32_t* __restrict__ D) {
+  __shared__ __align__(16) float sQ[32][36];
+  __shared__ __align__(16) float sX[64][36];
+  const int t = threadIdx.x, tq = t >> 4, tr = t & 15;
+  const uint32_t q0 = blockIdx.y * 32;
+  const uint64_t r0 = c0 + (uint64_t)blockIdx.x * 64;
+  float acc[2][4][8];
+#pragma unroll
+  for (int a = 0; a < 2; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b)
+#pragma unroll
+      for (int l = 0; l < 8; ++l) acc[a][b][l] = 0.0f;
+  const uint32_t full = dim / 8 * 8;
+  for (uint32_t k0 = 0; k0 < full; k0 += 32) {
+    const uint32_t kw = min(32u, full - k0);
+    for (int i = t; i < 32 * 32; i += 256) {
+      int row = i >> 5, col = i & 31;
+      uint32_t q = q0 + row;
+      sQ[row][col] = (q < nq && (uint32_t)col < kw) ? Q[(size_t)q * dim + k0 + col] : 0.0f;
+    }
+    for (int i = t; i < 64 * 32; i += 256) {
+      int row = i >> 5, col = i & 31;
+      uint64_t r = r0 + row;
+      sX[row][col] = (r < nrank && (uint32_t)col < kw) ? X[r * dim + k0 + col] : 0.0f;
+    }
+    __syncthreads();
+    for (uint32_t g = 0; g < kw; g += 8) {
+      float qv[2][8], xv[4][8];
+#pragma unroll
+      for (int a = 0; a < 2; ++a) {
+        float4 u = *reinterpret_cast<const float4*>(&sQ[tq + 16 * a][g]);
+        float4 w = *reinterpret_cast<const float4*>(&sQ[tq + 16 * a][g + 4]);
+        qv[a][0] = u.x; qv[a][1] = u.y; qv[a][2] = u.z; qv[a][3] = u.w;
+        qv[a][4] = w.x; qv[a][5] = w.y; qv[a][6] = w.z; qv[a][7] = w.w;
+      }
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        float4 u = *reinterpret_cast<const float4*>(&sX[tr + 16 * b][g]);
+        float4 w = *reinterpret_cast<const float4*>(&sX[tr + 16 * b][g + 4]);
+        xv[b][0] = u.x; xv[b][1] = u.y; xv[b][2] = u.z; xv[b][3] = u.w;
+        xv[b][4] = w.x; xv[b][5] = w.y; xv[b][6] = w.z; xv[b][7] = w.w;
+      }
+#pragma unroll
+      for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+#pragma unroll
+          for (int l = 0; l < 8; ++l) acc[a][b][l] = lane_step<METRIC>(acc[a][b][l], qv[a][l], xv[b][l]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int a = 0; a < 2; ++a) {
+    const uint32_t q = q0 + tq + 16 * a;
+    if (q >= nq) continue;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const uint64_t r = r0 + tr + 16 * b;
+      uint32_t key = SENTINEL;
+      if (r < nrank && accepted(bitmap, rank_slot[r])) {
+        float tail = 0.0f;  // the remainder loop starts from 0.0 (distance.rs:277-281)
+        for (uint32_t d = full; d < dim; ++d)
+          tail = lane_step<METRIC>(tail, Q[(size_t)q * dim + d], X[r * dim + d]);
+        key = candidate_key(finish<METRIC>(acc[a][b], tail));
+      }
+      D[(size_t)q * C + (r - c0)] = key;
+    }
+  }
+}
+
+// Selection step of K1g, one block per query. L_in holds the running top-k of
+// ranks below c0 as (key << 32 | rank) in ascending RANK order; the chunk adds
+// ranks c0.. . The new list is the k smallest of the union under
+// (key, rank), written in ascending rank order again, so equal keys resolve
+// to the smaller rank. Found with a 4-pass radix select on the key and a
+// stable block-wide compaction.
+constexpr int SEL_THREADS = 256;
+__global__ void __launch_bounds__(SEL_THREADS) select_chunk_kernel(
+    const uint64_t* __restrict__ L_in, const uint32_t* __restrict__ len_in,
+    uint64_t* __restrict__ L_out, uint32_t* __restrict__ len_out, const uint32_t* __restrict__ D,
+    uint32_t C, uint64_t c0, uint32_t cvalid, uint32_t k, uint32_t q_base) {
+  using Scan = cub::BlockScan<uint32_t, SEL_THREADS>;
+  using Reduce = cub::BlockReduce<uint32_t, SEL_THREADS>;
+  __shared__ typename Scan::TempStorage scan_tmp;
+  __shared__ typename Reduce::TempStorage red_tmp;
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t s_prefix, s_mask, s_remaining, s_take_all, s_thr, s_survivors;
+  const uint32_t q = q_base + blockIdx.x;
+  const uint64_t* Lq = L_in + (size_t)blockIdx.x * k;
+  uint64_t* Oq = L_out + (size_t)blockIdx.x * k;
+  const uint32_t* Dq = D + (size_t)q * C;
+  const uint32_t lin = len_in[blockIdx.x];
+  const uint32_t n = lin + cvalid;
+
+  // Fast path: a full list rejects every chunk key that is not strictly below
+  // its worst key (a chunk rank is larger than every listed rank).
+  if (lin == k) {
+    uint32_t worst = 0;
+    for (uint32_t i = threadIdx.x; i < lin; i += SEL_THREADS)
+      worst = max(worst, static_cast<uint32_t>(Lq[i] >> 32));
+    uint32_t w = Reduce(red_tmp).Reduce(worst, cub::Max());
+    if (threadIdx.x == 0) s_thr = w;
+    __syncthreads();
+    uint32_t cnt = 0;
+    for (uint32_t i = threadIdx.x; i < cvalid; i += SEL_THREADS) cnt += Dq[i] < s_thr;
+    uint32_t total = Reduce(red_tmp).Sum(cnt);
+    if (threadIdx.x == 0) s_survivors = total;
+    __syncthreads();
+    if (s_survivors == 0) {
+      for (uint32_t i = threadIdx.x; i < lin; i += SEL_THREADS) Oq[i] = Lq[i];
+      if (threadIdx.x == 0) len_out[blockIdx.x] = lin;
+      return;
+    }
+  }
+
+  auto key_at = [&](uint32_t i) -> uint32_t {
+    return i < lin ? static_cast<uint32_t>(Lq[i] >> 32) : Dq[i - lin];
+  };
+  if (threadIdx.x == 0) {
+    s_prefix = 0;
+    s_mask = 0;
+    s_remaining = k;
+    s_take_all = 0;
+  }
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (uint32_t i = threadIdx.x; i < 256; i += SEL_THREADS) hist[i] = 0;
+    __syncthreads();
+    if (s_take_all) break;
+    const uint32_t prefix = s_prefix, mask = s_mask;
+    for (uint32_t i = threadIdx.x; i < n; i += SEL_THREADS) {
+      uint32_t key = key_at(i);
+      if (key != SENTINEL && (key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t need = s_remaining, cum = 0, digit = 256;
+      for (uint32_t b = 0; b < 256; ++b) {
+        if (cum + hist[b] >= need) {
+          digit = b;
+          break;
+        }
+        cum += hist[b];
+      }
+      if (digit == 256) {
+        s_take_all = 1;  // fewer than `need` candidates share the prefix: all of them fit
+      } else {
+        s_prefix = prefix | (digit << shift);
+        s_mask = mask | (255u << shift);
+        s_remaining = need - cum;
+      }
+    }
+    __syncthreads();
+  }
+  const bool take_all = s_take_all != 0;
+  const uint32_t thr = s_prefix, quota_eq = s_remaining;
+  // Stable compaction in (list, chunk) = ascending rank order.
+  uint32_t out_base = 0, eq_base = 0;
+  for (uint32_t base = 0; base < n; base += SEL_THREADS) {
+    const uint32_t i = base + threadIdx.x;
+    uint32_t key = SENTINEL;
+    uint64_t packed = 0;
+    if (i < n) {
+      if (i < lin) {
+        packed = Lq[i];
+        key = static_cast<uint32_t>(packed >> 32);
+      } else {
+        key = Dq[i - lin];
+        packed = (static_cast<uint64_t>(key) << 32) | static_cast<uint32_t>(c0 + (i - lin));
+      }
+    }
+    const bool valid = key != SENTINEL;
+    uint32_t is_eq = (!take_all && valid && key == thr) ? 1u : 0u;
+    uint32_t eq_before, eq_total;
+    Scan(scan_tmp).ExclusiveSum(is_eq, eq_before, eq_total);
+    __syncthreads();
+    bool sel = valid && (take_all || key < thr || (is_eq && eq_base + eq_before < quota_eq));
+    uint32_t pos, sel_total;
+    Scan(scan_tmp).ExclusiveSum(sel ? 1u : 0u, pos, sel_total);
+    __syncthreads();
+    if (sel) Oq[out_base + pos] = packed;
+    out_base += sel_total;
+    eq_base += eq_total;
+  }
+  if (threadIdx.x == 0) len_out[blockIdx.x] = out_base;
+}
+
+// Final ordering of a K1g list (k <= 2048): sort by (key, rank), map rank to id.
+__global__ void finalize_small_kernel(const uint64_t* __restrict__ L, const uint32_t* __restrict__ len,
+                                      uint32_t k, uint32_t cap, const uint64_t* __restrict__ rank_id,
+                                      uint32_t q_base, uint64_t* __restrict__ out_ids,
+                                      float* __restrict__ out_dist, uint32_t* __restrict__ out_len) {
+  extern __shared__ uint64_t sl[];
+  const uint64_t* Lq = L + (size_t)blockIdx.x * k;
+  const uint32_t n = len[blockIdx.x];
+  for (uint32_t i = threadIdx.x; i < cap; i += blockDim.x) sl[i] = i < n ? Lq[i] : ~0ull;
+  __syncthreads();
+  block_bitonic_sort_u64(sl, cap);
+  const size_t q = q_base + blockIdx.x;
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+    uint64_t v = sl[i];
+    out_ids[q * k + i] = rank_id[static_cast<uint32_t>(v)];
+    out_dist[q * k + i] = key_to_float(static_cast<uint32_t>(v >> 32));
+  }
+  if (threadIdx.x == 0) out_len[q] = n;
+}
+
+// Same for already-sorted lists (large k, sorted with the segmented radix sort).
+__global__ void finalize_sorted_kernel(const uint64_t* __restrict__ L, const uint32_t* __restrict__ len,
+                                       uint32_t k, const uint64_t* __restrict__ rank_id,
+                                       uint32_t q_base, uint64_t* __restrict__ out_ids,
+                                       float* __restrict__ out_dist, uint32_t* __restrict__ out_len) {
+  const uint64_t* Lq = L + (size_t)blockIdx.x * k;
+  const uint32_t n = len[blockIdx.x];
+  const size_t q = q_base + blockIdx.x;
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+    uint64_t v = Lq[i];
+    out_ids[q * k + i] = rank_id[static_cast<uint32_t>(v)];
+    out_dist[q * k + i] = key_to_float(static_cast<uint32_t>(v >> 32));
+  }
+  if (threadIdx.x == 0) out_len[q] = n;
+}
+
+// Unused list tail must not be read as keys by the segmented sort.
+__global__ void pad_lists_kernel(uint64_t* L, const uint32_t* len, uint32_t k) {
+  uint64_t* Lq = L + (size_t)blockIdx.x * k;
+  for (uint32_t i = len[blockIdx.x] + threadIdx.x; i < k; i += blockDim.x) Lq[i] = ~0ull;
+}
+
+// ---------------------------------------------------------------------------
+// Mirror maintenance
+// ---------------------------------------------------------------------------
+// Validate a staged range (finite) and classify rows (integers in [0,255]).
+__global__ void validate_rows_kernel(const float* __restrict__ rows, uint64_t n, uint32_t dim,
+                                     unsigned long long* __restrict__ first_bad,
+                                     uint8_t* __restrict__ rowflag) {
+  uint64_t r = blockIdx.x;
+  if (r >= n) return;
+  __shared__ int not_u8;
+  if (threadIdx.x == 0) not_u8 = 0;
+  __syncthreads();
+  for (uint32_t d = threadIdx.x; d < dim; d += blockDim.x) {
+    float v = rows[r * dim + d];
+    if (!isfinite(v)) atomicMin(first_bad, (unsigned long long)(r * dim + d));
+    if (!(v >= 0.0f && v <= 255.0f && v == floorf(v))) not_u8 = 1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) rowflag[r] = not_u8 ? 0 : 1;
+}
+
+__global__ void iota_ids_kernel(uint64_t* ids, uint64_t begin, uint64_t n) {
+  uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) ids[i] = begin + i;
+}
+
+__global__ void iota_u32_kernel(uint32_t* v, uint64_t n) {
+  uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) v[i] = static_cast<uint32_t>(i);
+}
+
+__global__ void gather_ids_kernel(const uint32_t* slots, const uint64_t* ids, uint64_t* out, uint64_t n) {
+  uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = ids[slots[i]];
+}
+
+__global__ void gather_rows_kernel(const uint32_t* __restrict__ rank_slot, const float* __restrict__ rows,
+                                   const uint8_t* __restrict__ rowflag, uint32_t dim,
+                                   float* __restrict__ out, int* __restrict__ all_u8) {
+  uint64_t r = blockIdx.x;
+  uint32_t s = rank_slot[r];
+  for (uint32_t d = threadIdx.x; d < dim; d += blockDim.x) out[r * dim + d] = rows[(uint64_t)s * dim + d];
+  if (threadIdx.x == 0 && !rowflag[s]) atomicAnd(all_u8, 0);
+}
+
+// u8 operand for K1: row-major [nrank_pad][dp], zero-padded; norms with BIG
+// for padding rows.
+__global__ void build_u8_operand_kernel(const float* __restrict__ rank_rows, uint64_t nrank,
+                                        uint32_t dim, uint32_t dp, uint8_t* __restrict__ op,
+                                        int32_t* __restrict__ norms) {
+  uint64_t r = blockIdx.x;
+  __shared__ int32_t acc;
+  if (threadIdx.x == 0) acc = 0;
+  __syncthreads();
+  int32_t local = 0;
+  for (uint32_t d = threadIdx.x; d < dp; d += blockDim.x) {
+    uint8_t v = 0;
+    if (r < nrank && d < dim) v = static_cast<uint8_t>(rank_rows[r * dim + d]);
+    op[r * dp + d] = v;
+    local += static_cast<int32_t>(v) * static_cast<int32_t>(v);
+  }
+  atomicAdd(&acc, local);
+  __syncthreads();
+  if (threadIdx.x == 0) norms[r] = r < nrank ? acc : flat_tc::BIG;
+}
+
+// Queries for K1: u8 tile [nq_pad][dp], ||q||^2, and a flag if any query
+// component is not an integer in [0,255] (then K1 does not apply).
+__global__ void prep_queries_u8_kernel(const float* __restrict__ Q, uint32_t nq, uint32_t dim,
+                                       uint32_t dp, uint8_t* __restrict__ qop,
+                                       int32_t* __restrict__ qnorm, int* __restrict__ bad) {
+  uint32_t q = blockIdx.x;
+  __shared__ int32_t acc;
+  if (threadIdx.x == 0) acc = 0;
+  __syncthreads();
+  int32_t local = 0;
+  for (uint32_t d = threadIdx.x; d < dp; d += blockDim.x) {
+    uint8_t v = 0;
+    if (q < nq && d < dim) {
+      float f = Q[(size_t)q * dim + d];
+      if (f >= 0.0f && f <= 255.0f && f == floorf(f)) {
+        v = static_cast<uint8_t>(f);
+      } else {
+        atomicExch(bad, 1);
+      }
+    }
+    qop[(size_t)q * dp + d] = v;
+    local += static_cast<int32_t>(v) * static_cast<int32_t>(v);
+  }
+  atomicAdd(&acc, local);
+  __syncthreads();
+  if (threadIdx.x == 0) qnorm[q] = acc;
+}
+
+// Merge of K1's per-split lists: per query, nsplit*KT packed (r, rank) keys,
+// sort, keep k, distance = r + ||q||^2 (exact integer in f32).
+__global__ void merge_u8_kernel(const uint64_t* __restrict__ part, uint32_t nsplit, uint32_t KT,
+                                uint32_t cap, uint32_t k, const int32_t* __restrict__ qnorm,
+                                const uint64_t* __restrict__ rank_id, uint64_t* __restrict__ out_ids,
+                                float* __restrict__ out_dist, uint32_t* __restrict__ out_len) {
+  extern __shared__ uint64_t sl[];
+  const uint32_t q = blockIdx.x;
+  const uint32_t n = nsplit * KT;
+  const uint64_t empty_key = static_cast<uint64_t>(static_cast<uint32_t>(flat_tc::BIG) + flat_tc::R_OFFSET) << 32;
+  for (uint32_t i = threadIdx.x; i < cap; i += blockDim.x) {
+    uint64_t v = i < n ? part[(size_t)q * n + i] : ~0ull;
+    sl[i] = (v >= empty_key) ? ~0ull : v;
+  }
+  __syncthreads();
+  block_bitonic_sort_u64(sl, cap);
+  __shared__ uint32_t cnt;
+  if (threadIdx.x == 0) cnt = 0;
+  __syncthreads();
+  for (uint32_t i = threadIdx.x; i < k && i < cap; i += blockDim.x) {
+    uint64_t v = sl[i];
+    if (v != ~0ull) {
+      int32_t r = static_cast<int32_t>(static_cast<uint32_t>(v >> 32) - flat_tc::R_OFFSET);
+      out_ids[(size_t)q * k + i] = rank_id[static_cast<uint32_t>(v)];
+      out_dist[(size_t)q * k + i] = static_cast<float>(r + qnorm[q]);
+      atomicAdd(&cnt, 1u);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) out_len[q] = cnt;
+}
+
+__global__ void zero_u32_kernel(uint32_t* p, uint64_t n) {
+  uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) p[i] = 0;
+}
+
+inline unsigned grid1d(uint64_t n, unsigned block) { return (unsigned)((n + block - 1) / block); }
+
+}  // namespace pxc
+
+using namespace pxc;
+
+struct pxc_flat {
+  pxc_ctx* ctx = nullptr;
+  uint32_t dim = 0;
+  int32_t metric = 0;
+  uint64_t nslots = 0;  // mirror high-water mark
+  DBuf<float> rows;
+  DBuf<uint64_t> ids;
+  DBuf<uint8_t> live;
+  DBuf<uint8_t> rowflag;
+  bool dirty = true;
+  // rank mirror (live rows in ascending id order)
+  uint64_t nrank = 0;
+  DBuf<uint32_t> rank_slot;
+  DBuf<uint64_t> rank_id;
+  DBuf<float> rank_rows;
+  bool all_u8 = false;
+  uint32_t dp = 0;
+  uint64_t nrank_pad = 0;
+  DBuf<uint8_t> op_u8;
+  DBuf<int32_t> op_norm;
+  CUtensorMap tmap_x;
+  // scratch
+  DBuf<unsigned char> tmp;
+  DBuf<uint32_t> dchunk;
+  DBuf<uint64_t> lists_a, lists_b;
+  DBuf<uint32_t> lens_a, lens_b;
+  DBuf<uint8_t> q_u8;
+  DBuf<int32_t> q_norm;
+  DBuf<int> q_bad;
+  DBuf<uint64_t> part;
+  DBuf<float> stage_f;
+  DBuf<uint64_t> stage_id;
+  DBuf<unsigned long long> bad_idx;
+  // buffers of the host-pointer entry point, kept across calls
+  DBuf<float> io_q;
+  DBuf<uint64_t> io_bm, io_ids;
+  DBuf<float> io_dist;
+  DBuf<uint32_t> io_len;
+  // scan timing (profiling on): events around the dominant scan kernel
+  cudaEvent_t ev_begin = nullptr, ev_end = nullptr;
+  bool ev_recorded = false;
+  int* h_flag = nullptr;  // pinned
+  std::mutex mu;
+};
+
+namespace {
+
+// Events bracketing the scan kernel(s) of one search, when profiling is on.
+struct ScanTimer {
+  pxc_flat* h;
+  cudaStream_t s;
+  bool on;
+  ScanTimer(pxc_flat* h_, cudaStream_t s_) : h(h_), s(s_), on(h_->ctx->profiling) {
+    if (!on) return;
+    if (!h->ev_begin) {
+      PXC_CUDA(cudaEventCreate(&h->ev_begin));
+      PXC_CUDA(cudaEventCreate(&h->ev_end));
+    }
+    PXC_CUDA(cudaEventRecord(h->ev_begin, s));
+  }
+  void stop() {
+    if (!on) return;
+    PXC_CUDA(cudaEventRecord(h->ev_end, s));
+    h->ev_recorded = true;
+  }
+};
+
+void ensure_capacity(pxc_flat* h, uint64_t want, cudaStream_t s) {
+  uint64_t cap = h->ids.n;
+  if (want <= cap) return;
+  uint64_t ncap = std::max<uint64_t>(want, cap + cap / 2);
+  ncap = std::max<uint64_t>(ncap, 1024);
+  h->rows.grow_keep(ncap * h->dim, h->nslots * h->dim, s);
+  h->ids.grow_keep(ncap, h->nslots, s);
+  h->live.grow_keep(ncap, h->nslots, s);
+  h->rowflag.grow_keep(ncap, h->nslots, s);
+}
+
+void rebuild_mirror(pxc_flat* h, cudaStream_t s) {
+  const uint64_t n = h->nslots;
+  h->nrank = 0;
+  h->all_u8 = false;
+  if (n == 0) {
+    h->dirty = false;
+    return;
+  }
+  PXC_CONFIG(n < (1ull << 32), "slots", n, "the device mirror addresses at most 2^32 slots");
+  // 1. live slots in slot order
+  DBuf<uint32_t> slots_all, slots_live, sorted_slots;
+  DBuf<uint64_t> keys, sorted_keys;
+  DBuf<int> num;
+  slots_all.reserve(n);
+  slots_live.reserve(n);
+  num.reserve(2);
+  iota_u32_kernel<<<grid1d(n, 256), 256, 0, s>>>(slots_all.p, n);
+  size_t tb = 0;
+  PXC_CUDA(cub::DeviceSelect::Flagged(nullptr, tb, slots_all.p, h->live.p, slots_live.p, num.p, (int64_t)n, s));
+  h->tmp.reserve(tb);
+  PXC_CUDA(cub::DeviceSelect::Flagged(h->tmp.p, tb, slots_all.p, h->live.p, slots_live.p, num.p, (int64_t)n, s));
+  PXC_CUDA(cudaMemcpyAsync(h->h_flag, num.p, sizeof(int), cudaMemcpyDeviceToHost, s));
+  PXC_CUDA(cudaStreamSynchronize(s));
+  const uint64_t nl = static_cast<uint64_t>(*h->h_flag);
+  h->nrank = nl;
+  if (nl == 0) {
+    h->dirty = false;
+    return;
+  }
+  // 2. sort live slots by id
+  keys.reserve(nl);
+  sorted_keys.reserve(nl);
+  sorted_slots.reserve(nl);
+  gather_ids_kernel<<<grid1d(nl, 256), 256, 0, s>>>(slots_live.p, h->ids.p, keys.p, nl);
+  tb = 0;
+  PXC_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, tb, keys.p, sorted_keys.p, slots_live.p,
+                                           sorted_slots.p, (int64_t)nl, 0, 64, s));
+  h->tmp.reserve(tb);
+  PXC_CUDA(cub::DeviceRadixSort::SortPairs(h->tmp.p, tb, keys.p, sorted_keys.p, slots_live.p,
+                                           sorted_slots.p, (int64_t)nl, 0, 64, s));
+  h->rank_slot.reserve(nl);
+  h->rank_id.reserve(nl);
+  PXC_CUDA(cudaMemcpyAsync(h->rank_slot.p, sorted_slots.p, nl * sizeof(uint32_t), cudaMemcpyDeviceToDevice, s));
+  PXC_CUDA(cudaMemcpyAsync(h->rank_id.p, sorted_keys.p, nl * sizeof(uint64_t), cudaMemcpyDeviceToDevice, s));
+  // 3. rank-ordered rows and the u8 classification
+  h->rank_rows.reserve(nl * h->dim);
+  PXC_CUDA(cudaMemsetAsync(num.p, 0xFF, sizeof(int), s));
+  gather_rows_kernel<<<(unsigned)nl, 128, 0, s>>>(h->rank_slot.p, h->rows.p, h->rowflag.p, h->dim,
+                                                  h->rank_rows.p, num.p);
+  PXC_CUDA(cudaGetLastError());
+  PXC_CUDA(cudaMemcpyAsync(h->h_flag, num.p, sizeof(int), cudaMemcpyDeviceToHost, s));
+  PXC_CUDA(cudaStreamSynchronize(s));
+  h->all_u8 = (*h->h_flag != 0);
+  // 4. u8 operand for the tensor-core path
+  if (h->all_u8 && h->metric == PXC_EUCLIDEAN && h->dim <= 768) {
+    h->dp = (h->dim + 127) / 128 * 128;
+    h->nrank_pad = (nl + flat_tc::BN - 1) / flat_tc::BN * flat_tc::BN;
+    h->op_u8.reserve(h->nrank_pad * h->dp);
+    h->op_norm.reserve(h->nrank_pad);
+    build_u8_operand_kernel<<<(unsigned)h->nrank_pad, 128, 0, s>>>(h->rank_rows.p, nl, h->dim, h->dp,
+                                                                  h->op_u8.p, h->op_norm.p);
+    PXC_CUDA(cudaGetLastError());
+    make_tmap_u8_2d(&h->tmap_x, h->op_u8.p, h->dp, h->nrank_pad, flat_tc::KB_BYTES, flat_tc::BN);
+  }
+  PXC_CUDA(cudaStreamSynchronize(s));
+  h->dirty = false;
+}
+
+// Number of row splits for K1: balance waves of CTAs over the SMs.
+uint32_t choose_splits(uint32_t nqt, uint32_t ntiles, int sms) {
+  uint32_t smax = std::max<uint32_t>(1, std::min<uint32_t>(ntiles / 8, 512));
+  double best = 1e30;
+  uint32_t best_s = 1;
+  for (uint32_t s = 1; s <= smax; ++s) {
+    uint32_t tps = (ntiles + s - 1) / s;
+    uint32_t ctas = nqt * ((ntiles + tps - 1) / tps);
+    double waves = std::ceil((double)ctas / sms);
+    double cost = waves * (tps + 6.0);  // +6 tiles of fixed per-CTA cost
+    if (cost < best * 0.995) {
+      best = cost;
+      best_s = s;
+    }
+  }
+  return best_s;
+}
+
+void search_tc(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, uint64_t* d_ids,
+               float* d_dist, uint32_t* d_len, cudaStream_t s) {
+  const uint32_t KT = k <= 16 ? 16 : 32;
+  const uint32_t nq_pad = (nq + flat_tc::BM - 1) / flat_tc::BM * flat_tc::BM;
+  const uint32_t nqt = nq_pad / flat_tc::BM;
+  const uint32_t ntiles = (uint32_t)(h->nrank_pad / flat_tc::BN);
+  const uint32_t nsplit_req = choose_splits(nqt, ntiles, h->ctx->sm_count);
+  const uint32_t tps = (ntiles + nsplit_req - 1) / nsplit_req;
+  const uint32_t nsplit = (ntiles + tps - 1) / tps;
+  h->part.reserve((size_t)nq_pad * nsplit * KT);
+  flat_tc::Params p;
+  p.norms = h->op_norm.p;
+  p.out_part = h->part.p;
+  p.status = h->ctx->d_status;
+  p.nq = nq;
+  p.kblocks = h->dp / flat_tc::KB_BYTES;
+  p.ntiles = ntiles;
+  p.tiles_per_split = tps;
+  p.nsplit = nsplit;
+  p.stages = p.kblocks <= 4 ? 4 : 3;
+  p.wait_ns = (uint64_t)h->ctx->wait_ms * 1000000ull;
+  CUtensorMap tmap_q;
+  make_tmap_u8_2d(&tmap_q, h->q_u8.p, h->dp, nq_pad, flat_tc::KB_BYTES, flat_tc::BM);
+  size_t smem = flat_tc::smem_bytes(p.kblocks, p.stages);
+  dim3 grid(nqt, nsplit);
+  ScanTimer timer(h, s);
+  if (KT == 16) {
+    PXC_CUDA(cudaFuncSetAttribute(flat_tc::flat_u8_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    flat_tc::flat_u8_kernel<16><<<grid, flat_tc::NUM_THREADS, smem, s>>>(tmap_q, h->tmap_x, p);
+  } else {
+    PXC_CUDA(cudaFuncSetAttribute(flat_tc::flat_u8_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    flat_tc::flat_u8_kernel<32><<<grid, flat_tc::NUM_THREADS, smem, s>>>(tmap_q, h->tmap_x, p);
+  }
+  PXC_CUDA(cudaGetLastError());
+  timer.stop();
+  h->ctx->launches += 2;  // scan + merge
+  uint32_t cap = 32;
+  while (cap < nsplit * KT) cap <<= 1;
+  size_t msmem = cap * sizeof(uint64_t);
+  if (msmem > 48 * 1024)
+    PXC_CUDA(cudaFuncSetAttribute(merge_u8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msmem));
+  merge_u8_kernel<<<nq, 256, msmem, s>>>(h->part.p, nsplit, KT, cap, k, h->q_norm.p, h->rank_id.p,
+                                         d_ids, d_dist, d_len);
+  PXC_CUDA(cudaGetLastError());
+}
+
+template <int METRIC>
+void launch_dist(const float* d_q, uint32_t nqb, const pxc_flat* h, uint64_t c0, uint32_t C,
+                 const uint64_t* bitmap, uint32_t* D, cudaStream_t s) {
+  dim3 grid(C / 64, (nqb + 31) / 32);
+  dist_chunk_kernel<METRIC><<<grid, 256, 0, s>>>(d_q, nqb, h->rank_rows.p, h->nrank, h->dim, c0, C,
+                                                 bitmap, h->rank_slot.p, D);
+}
+
+void search_generic(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, const uint64_t* d_bitmap,
+                    uint64_t* d_ids, float* d_dist, uint32_t* d_len, cudaStream_t s) {
+  const uint64_t nrank = h->nrank;
+  const uint64_t list_budget = 1ull << 26;  // entries per list buffer (512 MiB)
+  const uint32_t qbatch = (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>(nq, std::min<uint64_t>(65536, list_budget / k)));
+  const uint64_t dbudget = 1ull << 26;  // chunk keys (256 MiB)
+  uint64_t C64 = std::max<uint64_t>(64, dbudget / qbatch / 64 * 64);
+  uint64_t nr64 = (nrank + 63) / 64 * 64;
+  const uint32_t C = (uint32_t)std::min<uint64_t>(C64, nr64);
+  h->dchunk.reserve((size_t)qbatch * C);
+  h->lists_a.reserve((size_t)qbatch * k);
+  h->lists_b.reserve((size_t)qbatch * k);
+  h->lens_a.reserve(qbatch);
+  h->lens_b.reserve(qbatch);
+  ScanTimer timer(h, s);
+  for (uint32_t qb = 0; qb < nq; qb += qbatch) {
+    const uint32_t nqb = std::min(qbatch, nq - qb);
+    const float* q = d_q + (size_t)qb * h->dim;
+    uint64_t* La = h->lists_a.p;
+    uint64_t* Lb = h->lists_b.p;
+    uint32_t* la = h->lens_a.p;
+    uint32_t* lb = h->lens_b.p;
+    zero_u32_kernel<<<grid1d(nqb, 256), 256, 0, s>>>(la, nqb);
+    for (uint64_t c0 = 0; c0 < nrank; c0 += C) {
+      const uint32_t cvalid = (uint32_t)std::min<uint64_t>(C, nrank - c0);
+      switch (h->metric) {
+        case PXC_EUCLIDEAN: launch_dist<PXC_EUCLIDEAN>(q, nqb, h, c0, C, d_bitmap, h->dchunk.p, s); break;
+        case PXC_COSINE: launch_dist<PXC_COSINE>(q, nqb, h, c0, C, d_bitmap, h->dchunk.p, s); break;
+        case PXC_INNER_PRODUCT: launch_dist<PXC_INNER_PRODUCT>(q, nqb, h, c0, C, d_bitmap, h->dchunk.p, s); break;
+        default: launch_dist<PXC_MANHATTAN>(q, nqb, h, c0, C, d_bitmap, h->dchunk.p, s); break;
+      }
+      PXC_CUDA(cudaGetLastError());
+      select_chunk_kernel<<<nqb, SEL_THREADS, 0, s>>>(La, la, Lb, lb, h->dchunk.p, C, c0, cvalid, k, 0);
+      PXC_CUDA(cudaGetLastError());
+      h->ctx->launches += 2;
+      std::swap(La, Lb);
+      std::swap(la, lb);
+    }
+    h->ctx->launches += 2;  // list reset + finalize
+    if (k <= 2048) {
+      uint32_t cap = 32;
+      while (cap < k) cap <<= 1;
+      size_t smem = cap * sizeof(uint64_t);
+      if (smem > 48 * 1024)
+        PXC_CUDA(cudaFuncSetAttribute(finalize_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      finalize_small_kernel<<<nqb, 256, smem, s>>>(La, la, k, cap, h->rank_id.p, qb, d_ids, d_dist, d_len);
+    } else {
+      pad_lists_kernel<<<nqb, 256, 0, s>>>(La, la, k);
+      std::vector<int64_t> offs(nqb + 1);
+      for (uint32_t i = 0; i <= nqb; ++i) offs[i] = (int64_t)i * k;
+      DBuf<int64_t> d_offs;
+      d_offs.reserve(nqb + 1);
+      PXC_CUDA(cudaMemcpyAsync(d_offs.p, offs.data(), (nqb + 1) * sizeof(int64_t), cudaMemcpyHostToDevice, s));
+      size_t tb = 0;
+      PXC_CUDA(cub::DeviceSegmentedRadixSort::SortKeys(nullptr, tb, La, Lb, (int64_t)nqb * k, (int64_t)nqb,
+                                                      d_offs.p, d_offs.p + 1, 0, 64, s));
+      h->tmp.reserve(tb);
+      PXC_CUDA(cub::DeviceSegmentedRadixSort::SortKeys(h->tmp.p, tb, La, Lb, (int64_t)nqb * k, (int64_t)nqb,
+                                                      d_offs.p, d_offs.p + 1, 0, 64, s));
+      finalize_sorted_kernel<<<nqb, 256, 0, s>>>(Lb, la, k, h->rank_id.p, qb, d_ids, d_dist, d_len);
+      PXC_CUDA(cudaStreamSynchronize(s));  // d_offs is freed on return
+    }
+    PXC_CUDA(cudaGetLastError());
+  }
+  timer.stop();
+}
+
+void search_device(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, const uint64_t* d_bitmap,
+                   uint64_t* d_ids, float* d_dist, uint32_t* d_len, cudaStream_t s) {
+  PXC_CONFIG(k <= PXC_MAX_K, "k", k, "exceeds the 16777216 result ceiling");
+  if (h->dirty) rebuild_mirror(h, s);
+  if (nq == 0) return;
+  if (k == 0 || h->nrank == 0) {
+    PXC_CUDA(cudaMemsetAsync(d_len, 0, nq * sizeof(uint32_t), s));
+    return;
+  }
+  bool tc = h->all_u8 && h->metric == PXC_EUCLIDEAN && d_bitmap == nullptr && k <= 32 &&
+            h->dim <= 768 && h->nrank_pad > 0;
+  if (tc) {
+    const uint32_t nq_pad = (nq + flat_tc::BM - 1) / flat_tc::BM * flat_tc::BM;
+    h->q_u8.reserve((size_t)nq_pad * h->dp);
+    h->q_norm.reserve(nq_pad);
+    h->q_bad.reserve(1);
+    PXC_CUDA(cudaMemsetAsync(h->q_bad.p, 0, sizeof(int), s));
+    prep_queries_u8_kernel<<<nq_pad, 128, 0, s>>>(d_q, nq, h->dim, h->dp, h->q_u8.p, h->q_norm.p, h->q_bad.p);
+    PXC_CUDA(cudaGetLastError());
+    h->ctx->launches += 1;
+    PXC_CUDA(cudaMemcpyAsync(h->h_flag, h->q_bad.p, sizeof(int), cudaMemcpyDeviceToHost, s));
+    PXC_CUDA(cudaStreamSynchronize(s));
+    tc = (*h->h_flag == 0);
+  }
+  if (tc) {
+    search_tc(h, d_q, nq, k, d_ids, d_dist, d_len, s);
+    check_device_status(h->ctx, s, "flat search (tensor-core scan)");
+  } else {
+    search_generic(h, d_q, nq, k, d_bitmap, d_ids, d_dist, d_len, s);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+pxc_status pxc_flat_create(pxc_ctx* ctx, uint32_t dim, int32_t metric, pxc_flat** out, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(ctx != nullptr, "ctx", 0, "null context");
+    PXC_CONFIG(out != nullptr, "out", 0, "output handle pointer is null");
+    PXC_CONFIG(dim >= 1, "dim", dim, "must be at least 1; a 0-dimensional space makes all distances equal");
+    PXC_CONFIG(dim <= (1u << 20), "dim", dim, "exceeds the 1048576 dimension ceiling");
+    PXC_CONFIG(metric >= 0 && metric <= 3, "metric", metric, "unknown metric code");
+    DeviceGuard g(ctx->device);
+    pxc_flat* h = new (std::nothrow) pxc_flat();
+    if (!h) throw make_failure(PXC_INTERNAL, 0, 0, nullptr, "out of host memory");
+    h->ctx = ctx;
+    h->dim = dim;
+    h->metric = metric;
+    cudaError_t e = cudaMallocHost(&h->h_flag, sizeof(int));
+    if (e != cudaSuccess) {
+      delete h;
+      PXC_CUDA(e);
+    }
+    *out = h;
+  });
+}
+
+void pxc_flat_destroy(pxc_flat* h) {
+  if (!h) return;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(h->ctx->device);
+  cudaStreamSynchronize(h->ctx->stream);
+  if (h->ev_begin) cudaEventDestroy(h->ev_begin);
+  if (h->ev_end) cudaEventDestroy(h->ev_end);
+  if (h->h_flag) cudaFreeHost(h->h_flag);
+  delete h;
+  if (prev >= 0) cudaSetDevice(prev);
+}
+
+pxc_status pxc_flat_sync(pxc_flat* h, const float* rows, const uint64_t* ids, const uint8_t* live,
+                         uint64_t slot_begin, uint64_t nslots, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(h != nullptr, "handle", 0, "null flat handle");
+    if (nslots == 0) return;
+    PXC_CONFIG(rows != nullptr, "rows", 0, "null rows");
+    PXC_CONFIG(slot_begin <= h->nslots, "slot_begin", slot_begin, "leaves a gap after the mirror's last slot");
+    PXC_CONFIG(slot_begin + nslots < (1ull << 32), "slots", slot_begin + nslots, "the device mirror addresses at most 2^32 slots");
+    std::lock_guard<std::mutex> lock(h->mu);
+    DeviceGuard g(h->ctx->device);
+    cudaStream_t s = h->ctx->stream;
+    const uint64_t dim = h->dim;
+    // stage + validate before touching the mirror
+    h->stage_f.reserve(nslots * dim);
+    h->bad_idx.reserve(1);
+    DBuf<uint8_t> flags;
+    flags.reserve(nslots);
+    PXC_CUDA(cudaMemcpyAsync(h->stage_f.p, rows, nslots * dim * sizeof(float), cudaMemcpyHostToDevice, s));
+    PXC_CUDA(cudaMemsetAsync(h->bad_idx.p, 0xFF, sizeof(unsigned long long), s));
+    validate_rows_kernel<<<(unsigned)nslots, 128, 0, s>>>(h->stage_f.p, nslots, h->dim, h->bad_idx.p, flags.p);
+    PXC_CUDA(cudaGetLastError());
+    unsigned long long bad = 0;
+    PXC_CUDA(cudaMemcpyAsync(&bad, h->bad_idx.p, sizeof(bad), cudaMemcpyDeviceToHost, s));
+    PXC_CUDA(cudaStreamSynchronize(s));
+    if (bad != ~0ull)
+      throw make_failure(PXC_NON_FINITE, bad, 0, nullptr, "vector component %llu is not finite", bad);
+    ensure_capacity(h, slot_begin + nslots, s);
+    PXC_CUDA(cudaMemcpyAsync(h->rows.p + slot_begin * dim, h->stage_f.p, nslots * dim * sizeof(float), cudaMemcpyDeviceToDevice, s));
+    PXC_CUDA(cudaMemcpyAsync(h->rowflag.p + slot_begin, flags.p, nslots, cudaMemcpyDeviceToDevice, s));
+    if (ids) {
+      PXC_CUDA(cudaMemcpyAsync(h->ids.p + slot_begin, ids, nslots * sizeof(uint64_t), cudaMemcpyHostToDevice, s));
+    } else {
+      iota_ids_kernel<<<grid1d(nslots, 256), 256, 0, s>>>(h->ids.p + slot_begin, slot_begin, nslots);
+    }
+    if (live) {
+      PXC_CUDA(cudaMemcpyAsync(h->live.p + slot_begin, live, nslots, cudaMemcpyHostToDevice, s));
+    } else {
+      PXC_CUDA(cudaMemsetAsync(h->live.p + slot_begin, 1, nslots, s));
+    }
+    PXC_CUDA(cudaStreamSynchronize(s));
+    h->nslots = std::max(h->nslots, slot_begin + nslots);
+    h->dirty = true;
+  });
+}
+
+pxc_status pxc_flat_truncate(pxc_flat* h, uint64_t nslots, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(h != nullptr, "handle", 0, "null flat handle");
+    std::lock_guard<std::mutex> lock(h->mu);
+    PXC_CONFIG(nslots <= h->nslots, "nslots", nslots, "truncate cannot grow the mirror");
+    h->nslots = nslots;
+    h->dirty = true;
+  });
+}
+
+uint64_t pxc_flat_len(const pxc_flat* h) {
+  if (!h) return 0;
+  pxc_flat* m = const_cast<pxc_flat*>(h);
+  std::lock_guard<std::mutex> lock(m->mu);
+  if (m->dirty) {
+    try {
+      DeviceGuard g(m->ctx->device);
+      rebuild_mirror(m, m->ctx->stream);
+    } catch (...) {
+      return 0;
+    }
+  }
+  return m->nrank;
+}
+
+float pxc_flat_last_scan_ms(pxc_flat* h) {
+  if (!h || !h->ev_recorded) return -1.0f;
+  float ms = -1.0f;
+  if (cudaEventSynchronize(h->ev_end) != cudaSuccess) return -1.0f;
+  if (cudaEventElapsedTime(&ms, h->ev_begin, h->ev_end) != cudaSuccess) return -1.0f;
+  return ms;
+}
+
+int32_t pxc_flat_path(const pxc_flat* h) {
+  if (!h) return -1;
+  pxc_flat* m = const_cast<pxc_flat*>(h);
+  std::lock_guard<std::mutex> lock(m->mu);
+  if (m->dirty) {
+    try {
+      DeviceGuard g(m->ctx->device);
+      rebuild_mirror(m, m->ctx->stream);
+    } catch (...) {
+      return -1;
+    }
+  }
+  return (m->all_u8 && m->metric == PXC_EUCLIDEAN && m->dim <= 768 && m->nrank > 0) ? 1 : 0;
+}
+
+pxc_status pxc_flat_search_device(pxc_flat* h, const float* d_queries, uint32_t nq, uint32_t k,
+                                  const uint64_t* d_bitmap, uint64_t* d_out_ids, float* d_out_dist,
+                                  uint32_t* d_out_len, void* stream, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(h != nullptr, "handle", 0, "null flat handle");
+    std::lock_guard<std::mutex> lock(h->mu);
+    DeviceGuard g(h->ctx->device);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->ctx->stream;
+    search_device(h, d_queries, nq, k, d_bitmap, d_out_ids, d_out_dist, d_out_len, s);
+  });
+}
+
+pxc_status pxc_flat_search(pxc_flat* h, const float* queries, uint32_t nq, uint32_t k,
+                           const uint64_t* bitmap, uint64_t* out_ids, float* out_dist,
+                           uint32_t* out_len, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(h != nullptr, "handle", 0, "null flat handle");
+    PXC_CONFIG(k <= PXC_MAX_K, "k", k, "exceeds the 16777216 result ceiling");
+    if (nq == 0) return;
+    std::lock_guard<std::mutex> lock(h->mu);
+    DeviceGuard g(h->ctx->device);
+    cudaStream_t s = h->ctx->stream;
+    const uint64_t dim = h->dim;
+    DBuf<float>& dq = h->io_q;
+    DBuf<uint64_t>& dbm = h->io_bm;
+    DBuf<uint64_t>& dids = h->io_ids;
+    DBuf<float>& ddist = h->io_dist;
+    DBuf<uint32_t>& dlen = h->io_len;
+    dq.reserve((size_t)nq * dim);
+    dlen.reserve(nq);
+    if (k > 0) {
+      dids.reserve((size_t)nq * k);
+      ddist.reserve((size_t)nq * k);
+    }
+    PXC_CUDA(cudaMemcpyAsync(dq.p, queries, (size_t)nq * dim * sizeof(float), cudaMemcpyHostToDevice, s));
+    if (bitmap) {
+      if (h->dirty) rebuild_mirror(h, s);
+      uint64_t words = (h->nslots + 63) / 64;
+      if (words) {
+        dbm.reserve(words);
+        PXC_CUDA(cudaMemcpyAsync(dbm.p, bitmap, words * sizeof(uint64_t), cudaMemcpyHostToDevice, s));
+      }
+    }
+    search_device(h, dq.p, nq, k, bitmap ? dbm.p : nullptr, dids.p, ddist.p, dlen.p, s);
+    if (k > 0) {
+      PXC_CUDA(cudaMemcpyAsync(out_ids, dids.p, (size_t)nq * k * sizeof(uint64_t), cudaMemcpyDeviceToHost, s));
+      PXC_CUDA(cudaMemcpyAsync(out_dist, ddist.p, (size_t)nq * k * sizeof(float), cudaMemcpyDeviceToHost, s));
+    }
+    PXC_CUDA(cudaMemcpyAsync(out_len, dlen.p, nq * sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
+    PXC_CUDA(cudaStreamSynchronize(s));
+  });
+}
+
+}  // extern "C"

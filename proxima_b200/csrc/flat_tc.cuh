@@ -1,0 +1,282 @@
+// flat_tc.cuh — K1: exact u8 distance GEMM on tcgen05 tensor cores with a
+// fused per-query top-k, for euclidean stores whose rows and queries are
+// integers in [0,255].
+//
+// Why it is exact: for such data every product and every partial sum of the
+// reference's squared_euclidean (crates/proxima-core/src/distance.rs:267-283)
+// is an integer below 2^24, so the reference's f32 result is the exact
+// integer ||q-x||^2 whatever the summation order. The kernel computes
+// q.x exactly in s32 (kind::i8, u8 x u8), forms r = ||x||^2 - 2 q.x per
+// column, and ranks on r; the distance is r + ||q||^2, converted to f32
+// exactly.
+//
+// Why ranking on r with a strict '<' is exact: columns are database rows in
+// ascending VectorId order ("rank" order), and every thread scans its columns
+// in ascending rank, so a later column that ties the current k-th value has a
+// larger id and loses the (total_cmp, id) comparison
+// (crates/proxima-core/src/topk.rs:63-67).
+//
+// Structure (one CTA per 128 queries x one range of database rows):
+//   warp 0      TMA producer: query tile once, then 256-row database tiles
+//               through a STAGES-deep shared-memory ring (128-byte swizzle,
+//               no multicast);
+//   warp 1      allocates 512 TMEM columns; lane 0 issues tcgen05.mma
+//               (M=128, N=256, K=32 per instruction) into one of two TMEM
+//               accumulators and commits to mbarriers;
+//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time, r = h - 2*dot,
+//               warp-free per-thread top-KT in registers (thread = query row).
+// Every mbarrier wait is bounded by a global-timer limit; on expiry the CTA
+// records DEV_TIMEOUT_* in the status word, drains its own copies and MMAs,
+// frees TMEM and returns.
+#pragma once
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace pxc {
+namespace flat_tc {
+
+constexpr int BM = 128;        // queries per CTA (TMEM lanes)
+constexpr int BN = 256;        // database rows per tile (TMEM columns per accumulator)
+constexpr int KB_BYTES = 128;  // one swizzle atom of K per TMA box
+constexpr int UMMA_K = 32;     // K bytes per tcgen05.mma kind::i8
+constexpr int A_BLOCK = BM * KB_BYTES;  // 16 KiB
+constexpr int B_BLOCK = BN * KB_BYTES;  // 32 KiB
+constexpr int NUM_THREADS = 192;
+constexpr int32_t BIG = 0x3FFFFFFF;     // sentinel: padding columns and empty slots
+constexpr uint32_t R_OFFSET = 0x02000000u;  // makes r non-negative for packing
+
+struct Params {
+  const int32_t* norms;    // ||x||^2 per rank, BIG for padding ranks
+  uint64_t* out_part;      // [nq_pad][nsplit][KT] packed (r+R_OFFSET)<<32 | rank
+  uint32_t* status;        // device error word
+  uint32_t nq;
+  uint32_t kblocks;        // dim_pad / 128
+  uint32_t ntiles;         // nrank_pad / BN
+  uint32_t tiles_per_split;
+  uint32_t nsplit;
+  uint32_t stages;
+  uint64_t wait_ns;
+};
+
+__host__ __device__ inline size_t smem_bytes(uint32_t kblocks, uint32_t stages) {
+  size_t off = (size_t)kblocks * A_BLOCK + (size_t)stages * B_BLOCK;
+  off += (2 * stages + 6) * sizeof(uint64_t) + 16;
+  return off + 1024;  // alignment slack
+}
+
+// Branch-free insertion into an ascending register list; precondition
+// r < lr[K-1]. Elements equal to r stay ahead of it (they have smaller ids).
+template <int K>
+__device__ __forceinline__ void insert_sorted(int32_t (&lr)[K], uint32_t (&lk)[K], int32_t r,
+                                              uint32_t rank) {
+#pragma unroll
+  for (int i = K - 1; i > 0; --i) {
+    bool shift = lr[i - 1] > r;
+    bool here = lr[i] > r;
+    int32_t nr = shift ? lr[i - 1] : (here ? r : lr[i]);
+    uint32_t nk = shift ? lk[i - 1] : (here ? rank : lk[i]);
+    lr[i] = nr;
+    lk[i] = nk;
+  }
+  bool here0 = lr[0] > r;
+  lk[0] = here0 ? rank : lk[0];
+  lr[0] = here0 ? r : lr[0];
+}
+
+__device__ __forceinline__ void record_failure(uint32_t* status, uint32_t code) {
+  if (atomicCAS(status, 0u, code) == 0u) {
+    atomicExch(status + 1, blockIdx.y * gridDim.x + blockIdx.x);
+  }
+}
+
+template <int KT>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    flat_u8_kernel(const __grid_constant__ CUtensorMap tmap_q,
+                   const __grid_constant__ CUtensorMap tmap_x, const Params p) {
+  using namespace sm100;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t kblocks = p.kblocks, stages = p.stages;
+  unsigned char* sA = smem;
+  unsigned char* sB = smem + (size_t)kblocks * A_BLOCK;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + (size_t)stages * B_BLOCK);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + stages;
+  uint64_t* acc_full = bars + 2 * stages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* a_full = acc_empty + 2;
+  uint64_t* mma_done = a_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  __shared__ volatile uint32_t failed;
+
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t qtile = blockIdx.x, split = blockIdx.y;
+  const uint32_t t_begin = split * p.tiles_per_split;
+  const uint32_t t_end = min(t_begin + p.tiles_per_split, p.ntiles);
+  const uint32_t ntile_local = t_end > t_begin ? t_end - t_begin : 0;
+
+  if (warp == 1) {
+    tmem_alloc<512>(tmem_slot);
+    tmem_relinquish();
+  }
+  if (threadIdx.x == 0) {
+    failed = 0;
+    for (uint32_t s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4 * 32);
+    }
+    mbar_init(a_full, 1);
+    mbar_init(mma_done, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmap_q);
+    tma_prefetch_desc(&tmap_x);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- producer ----------------
+      mbar_arrive_expect_tx(a_full, kblocks * A_BLOCK);
+      for (uint32_t kb = 0; kb < kblocks; ++kb)
+        tma_load_2d(sA + (size_t)kb * A_BLOCK, &tmap_q, a_full, kb * KB_BYTES, qtile * BM);
+      uint32_t it = 0;
+      bool ok = true;
+      for (uint32_t t = 0; t < ntile_local && ok; ++t) {
+        for (uint32_t kb = 0; kb < kblocks; ++kb, ++it) {
+          uint32_t s = it % stages, ph = (it / stages) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, p.wait_ns) || failed) {
+            record_failure(p.status, DEV_TIMEOUT_EMPTY);
+            failed = 1;
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], B_BLOCK);
+          tma_load_2d(sB + (size_t)s * B_BLOCK, &tmap_x, &full[s], kb * KB_BYTES,
+                      (t_begin + t) * BN);
+        }
+      }
+      // Drain: every copy this thread issued has landed before the CTA exits.
+      uint32_t first = it > stages ? it - stages : 0;
+      for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % stages], (j / stages) & 1, p.wait_ns);
+      mbar_wait(a_full, 0, p.wait_ns);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      const uint32_t idesc = idesc_u8_s32(BM, BN);
+      bool ok = mbar_wait(a_full, 0, p.wait_ns);
+      if (!ok) {
+        record_failure(p.status, DEV_TIMEOUT_FULL);
+        failed = 1;
+      }
+      tc_fence_after();
+      const uint32_t a_addr = smem_u32(sA), b_addr = smem_u32(sB);
+      uint32_t it = 0;
+      for (uint32_t t = 0; t < ntile_local && ok; ++t) {
+        uint32_t buf = t & 1, use = t >> 1;
+        if (!mbar_wait(&acc_empty[buf], (use & 1) ^ 1, p.wait_ns) || failed) {
+          record_failure(p.status, DEV_TIMEOUT_ACC);
+          failed = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (uint32_t kb = 0; kb < kblocks; ++kb, ++it) {
+          uint32_t s = it % stages, ph = (it / stages) & 1;
+          if (!mbar_wait(&full[s], ph, p.wait_ns) || failed) {
+            record_failure(p.status, DEV_TIMEOUT_FULL);
+            failed = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = smem_desc_k_sw128(a_addr + kb * A_BLOCK);
+          const uint64_t bdesc = smem_desc_k_sw128(b_addr + s * B_BLOCK);
+#pragma unroll
+          for (uint32_t k = 0; k < KB_BYTES / UMMA_K; ++k) {
+            // K advance inside the 128-byte swizzle atom: +32 bytes = +2 in the
+            // 16-byte-unit start-address field.
+            mma_i8(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+          }
+          mma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        mma_commit(&acc_full[buf]);
+      }
+      // All MMAs of this thread complete before TMEM is released.
+      mma_commit(mma_done);
+      mbar_wait(mma_done, 0, p.wait_ns);
+    }
+  } else {
+    // ---------------- epilogue: warps 2..5 ----------------
+    const uint32_t quarter = warp & 3;
+    const uint32_t row = quarter * 32 + lane;
+    int32_t lr[KT];
+    uint32_t lk[KT];
+#pragma unroll
+    for (int i = 0; i < KT; ++i) {
+      lr[i] = BIG;
+      lk[i] = 0xFFFFFFFFu;
+    }
+    for (uint32_t t = 0; t < ntile_local; ++t) {
+      uint32_t buf = t & 1, use = t >> 1;
+      if (!mbar_wait(&acc_full[buf], use & 1, p.wait_ns) || failed) {
+        record_failure(p.status, DEV_TIMEOUT_ACC);
+        failed = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t rank_base = (t_begin + t) * BN;
+      const uint32_t taddr = tmem_base + ((quarter * 32) << 16) + buf * BN;
+#pragma unroll 1
+      for (uint32_t c = 0; c < BN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, v);
+        tmem_ld_wait();
+        const int4* np = reinterpret_cast<const int4*>(p.norms + rank_base + c * 32);
+        int32_t r[32];
+        int32_t rmin = BIG;
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4) {
+          int4 h = __ldg(np + j4);
+          r[4 * j4 + 0] = h.x - 2 * static_cast<int32_t>(v[4 * j4 + 0]);
+          r[4 * j4 + 1] = h.y - 2 * static_cast<int32_t>(v[4 * j4 + 1]);
+          r[4 * j4 + 2] = h.z - 2 * static_cast<int32_t>(v[4 * j4 + 2]);
+          r[4 * j4 + 3] = h.w - 2 * static_cast<int32_t>(v[4 * j4 + 3]);
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) rmin = min(rmin, r[j]);
+        if (rmin < lr[KT - 1]) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (r[j] < lr[KT - 1]) insert_sorted<KT>(lr, lk, r[j], rank_base + c * 32 + j);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+    }
+    const uint32_t q = qtile * BM + row;
+    if (q < p.nq) {
+      uint64_t* dst = p.out_part + ((size_t)q * p.nsplit + split) * KT;
+#pragma unroll
+      for (int i = 0; i < KT; ++i)
+        dst[i] = (static_cast<uint64_t>(static_cast<uint32_t>(lr[i]) + R_OFFSET) << 32) | lk[i];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc<512>(tmem_base);
+}
+
+}  // namespace flat_tc
+}  // namespace pxc

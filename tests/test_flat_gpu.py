@@ -1,0 +1,256 @@
+"""GPU parity of the flat exact search (K1 tensor-core u8 scan and K1g fp32 scan) against the oracle.
+
+The bar is bit-exact: identical ids in identical order and identical f32
+distances, for every query.
+"""
+import ctypes as C
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import pxo
+from proxima_b200 import _native as N
+from proxima_b200 import fixtures
+from proxima_b200.core import Metric, VectorSpace
+from proxima_b200.errors import Configuration, DimensionMismatch, DuplicateId, UnknownId
+
+pytestmark = pytest.mark.gpu
+KAT = json.loads((Path(__file__).parent / "golden" / "reference_kat.json").read_text())
+
+
+def _index(dim, metric, **kw):
+    from proxima_b200.index import FlatIndex
+    return FlatIndex(VectorSpace(dim, metric), **kw)
+
+
+def _assert_same(gpu, ref, nq):
+    gi, gd, gl = gpu
+    ri, rd, rl = ref
+    assert np.array_equal(gl[:nq], rl[:nq]), "lengths differ"
+    for q in range(nq):
+        n = int(rl[q])
+        assert np.array_equal(gi[q, :n], ri[q, :n]), f"query {q}: ids {gi[q, :n]} vs {ri[q, :n]}"
+        assert np.array_equal(gd[q, :n].view(np.uint32), rd[q, :n].view(np.uint32)), f"query {q}: distances"
+
+
+# ---------------- reference golden cases through the VectorIndex mirror ----------------
+
+def test_golden_flat_cases():
+    t = KAT["flat_ties"]
+    idx = _index(2, Metric.EUCLIDEAN)
+    for i in t["insert_ids"]:
+        idx.insert(i, t["vector"])
+    assert [h.id for h in idx.search_all(t["vector"], t["k"])] == t["expected_ids"]
+
+    f = KAT["flat_filter"]
+    idx = _index(1, Metric.EUCLIDEAN)
+    for i in range(f["n"]):
+        idx.insert(i, [float(i)], {"keep": i % f["keep_every"] == 0})
+    hits = idx.search([0.0], f["k"], lambda _id, m: m.get("keep") is True)
+    assert [h.id for h in hits] == f["expected_ids"]
+
+    c = KAT["flat_cosine"]
+    idx = _index(2, Metric.COSINE)
+    idx.insert(1, c["insert"])
+    v = idx.vector(1)
+    assert abs(v[0] - c["stored"][0]) < c["tolerance"] and abs(v[1] - c["stored"][1]) < c["tolerance"]
+    a = idx.search_all([30.0, 40.0], 1)[0].distance
+    b = idx.search_all([0.3, 0.4], 1)[0].distance
+    assert abs(a - b) < 1e-6
+
+    g = KAT["flat_k_larger_than_index"]
+    idx = _index(1, Metric.EUCLIDEAN)
+    for i in range(g["n"]):
+        idx.insert(i, [float(i)])
+    assert len(idx.search_all([0.0], g["k"])) == g["expected_len"]
+    assert idx.search_all([0.0], 0) == []
+
+    tf = KAT["flat_try_from"]
+    from proxima_b200.index import FlatIndex
+    idx = FlatIndex.from_array(VectorSpace(2, Metric.EUCLIDEAN), tf["data"])
+    assert idx.search_all(tf["query"], 1)[0].id == tf["expected_id"]
+
+
+def test_vector_index_contract():
+    idx = _index(3, Metric.EUCLIDEAN)
+    assert idx.search_all([1.0, 2.0, 3.0], 10) == []  # empty index: nothing, no error
+    idx.insert(1, [3.0, 4.0, 0.0])
+    with pytest.raises(DuplicateId):
+        idx.insert(1, [1.0, 1.0, 1.0])
+    with pytest.raises(DimensionMismatch):
+        idx.insert(2, [1.0])
+    with pytest.raises(DimensionMismatch):
+        idx.search_all([1.0, 2.0], 1)
+    with pytest.raises(Configuration):
+        idx.search_all([1.0, 2.0, 3.0], (1 << 24) + 1)
+    assert idx.search_all([3.0, 4.0, 0.0], 1)[0].distance == 0.0
+    idx.upsert(1, [1.0, 1.0, 1.0])
+    assert list(idx.vector(1)) == [1.0, 1.0, 1.0] and idx.len() == 1
+    idx.remove(1)
+    with pytest.raises(UnknownId):
+        idx.remove(1)
+    assert idx.is_empty() and idx.search_all([1.0, 1.0, 1.0], 3) == []
+    # slot churn: removal recycles slots LIFO and results follow the live set
+    for i in range(8):
+        idx.insert(i, [float(i)] * 3)
+    for r in range(50):
+        idx.remove(r % 8)
+        idx.insert(r % 8, [float(r)] * 3)
+    ids = {h.id for h in idx.search_all([0.0, 0.0, 0.0], 8)}
+    assert ids == set(range(8))
+    assert idx.stats().len == 8 and idx.stats().deleted == 0
+
+
+# ---------------- C1: quickstart, cosine, 5000 x 64 ----------------
+
+def test_c1_quickstart_bit_exact():
+    data = fixtures.quickstart()
+    space = VectorSpace(64, Metric.COSINE)
+    from proxima_b200.index import FlatIndex
+    idx = FlatIndex.from_array(space, data)
+    queries = space.prepare_batch(data[::50])
+    got = idx.search_prepared_batch(queries, 10)
+    ref = pxo.flat_search(pxo.prepare(pxo.COSINE, data), queries, 10, pxo.COSINE)
+    assert idx.device_path() == 0
+    _assert_same(got, ref, 100)
+    golden = json.loads((Path(__file__).parent / "golden" / "c1_top10.json").read_text())
+    assert [list(map(int, r)) for r in got[0]] == golden["ids"]
+    assert [[float(x) for x in r] for r in got[1]] == golden["distances"]
+
+
+# ---------------- C2 shape: integer blobs, euclidean ----------------
+
+@pytest.fixture(scope="module")
+def c2_small():
+    db = fixtures.blobs_u8(60_000, 128, 1024, fixtures.C2_CENTRES, fixtures.C2_BASE)
+    q = fixtures.blobs_u8(300, 128, 1024, fixtures.C2_CENTRES, fixtures.C2_QUERIES)
+    return db, q
+
+
+@pytest.mark.parametrize("k", [1, 10, 16, 32])
+def test_c2_tensor_core_path_bit_exact(c2_small, k):
+    db, q = c2_small
+    from proxima_b200.index import FlatIndex
+    idx = FlatIndex.from_array(VectorSpace(128, Metric.EUCLIDEAN), db)
+    assert idx.device_path() == 1
+    got = idx.search_prepared_batch(q, k)
+    ref = pxo.flat_search(db, q, k, pxo.EUCLIDEAN)
+    _assert_same(got, ref, len(q))
+
+
+def test_c2_k100_generic_path_bit_exact(c2_small):
+    db, q = c2_small
+    from proxima_b200.index import FlatIndex
+    idx = FlatIndex.from_array(VectorSpace(128, Metric.EUCLIDEAN), db)
+    got = idx.search_prepared_batch(q, 100)
+    ref = pxo.flat_search(db, q, 100, pxo.EUCLIDEAN)
+    _assert_same(got, ref, len(q))
+
+
+def test_c2_shuffled_ids_removed_slots_and_duplicates(c2_small):
+    db, q = c2_small
+    rng = np.random.default_rng(11)
+    n = 20_000
+    rows = db[:n].copy()
+    rows[5000:5400] = rows[100]  # 400 exact duplicates: distance ties resolved by id
+    ids = rng.permutation(np.arange(10_000_000, 10_000_000 + n)).astype(np.uint64)
+    live = np.ones(n, np.uint8)
+    live[rng.choice(n, 1500, replace=False)] = 0
+    from proxima_b200.index import Context
+    ctx = Context.default()
+    h = N.vp()
+    N.call("pxc_flat_create", ctx.handle, 128, 0, C.byref(h))
+    try:
+        N.call("pxc_flat_sync", h, N.ptr(rows), N.ptr(ids), N.ptr(live), 0, n)
+        assert N.load().pxc_flat_path(h) == 1
+        queries = np.concatenate([q[:200], rows[100:101]])
+        for k in (10, 32):
+            out = (np.zeros((len(queries), k), np.uint64), np.zeros((len(queries), k), np.float32),
+                   np.zeros(len(queries), np.uint32))
+            N.call("pxc_flat_search", h, N.ptr(queries), len(queries), k, None, *map(N.ptr, out))
+            ref = pxo.flat_search(rows, queries, k, pxo.EUCLIDEAN, ids=ids, live=live)
+            _assert_same(out, ref, len(queries))
+    finally:
+        N.load().pxc_flat_destroy(h)
+
+
+def test_c2_filtered_and_non_integer(c2_small):
+    db, q = c2_small
+    n = 30_000
+    rows = db[:n]
+    keep = (np.arange(n) % 7) == 3
+    bitmap = np.packbits(keep, bitorder="little")
+    bitmap = np.concatenate([bitmap, np.zeros(-len(bitmap) % 8, np.uint8)]).view(np.uint64)
+    from proxima_b200.index import FlatIndex
+    idx = FlatIndex.from_array(VectorSpace(128, Metric.EUCLIDEAN), rows)
+    got = idx.search_prepared_batch(q[:64], 10, bitmap)
+    ref = pxo.flat_search(rows, q[:64], 10, pxo.EUCLIDEAN, bitmap=bitmap)
+    _assert_same(got, ref, 64)
+    # non-integer queries on an integer store fall back to the fp32 scan, still exact
+    qf = q[:64] + np.float32(0.25)
+    got = idx.search_prepared_batch(qf, 10)
+    ref = pxo.flat_search(rows, qf, 10, pxo.EUCLIDEAN)
+    _assert_same(got, ref, 64)
+
+
+@pytest.mark.parametrize("metric", [Metric.EUCLIDEAN, Metric.INNER_PRODUCT, Metric.MANHATTAN, Metric.COSINE])
+@pytest.mark.parametrize("dim", [3, 37, 96])
+def test_generic_metrics_bit_exact(metric, dim):
+    rng = np.random.default_rng(dim * 10 + int(metric))
+    rows = (rng.standard_normal((7000, dim)) * 2).astype(np.float32)
+    qs = (rng.standard_normal((45, dim)) * 2).astype(np.float32)
+    space = VectorSpace(dim, metric)
+    from proxima_b200.index import FlatIndex
+    idx = FlatIndex.from_array(space, rows)
+    pq = space.prepare_batch(qs)
+    for k in (1, 17, 300):
+        got = idx.search_prepared_batch(pq, k)
+        ref = pxo.flat_search(pxo.prepare(int(metric), rows), pq, k, int(metric))
+        _assert_same(got, ref, len(qs))
+
+
+def test_large_k_uses_segmented_sort():
+    rng = np.random.default_rng(2)
+    rows = rng.standard_normal((5000, 8)).astype(np.float32)
+    qs = rng.standard_normal((3, 8)).astype(np.float32)
+    from proxima_b200.index import FlatIndex
+    idx = FlatIndex.from_array(VectorSpace(8, Metric.EUCLIDEAN), rows)
+    got = idx.search_prepared_batch(qs, 4500)
+    ref = pxo.flat_search(rows, qs, 4500, pxo.EUCLIDEAN)
+    _assert_same(got, ref, 3)
+
+
+def test_topk_merge_of_shards_equals_single_search(c2_small):
+    """Row shards searched separately (as ranks do) and merged == one search."""
+    db, q = c2_small
+    import torch
+    from proxima_b200.index import Context
+    ctx = Context.default()
+    n, k, parts = 40_000, 10, 4
+    qs = q[:130]
+    ids_all, d_all, l_all = [], [], []
+    for p in range(parts):
+        lo, hi = p * n // parts, (p + 1) * n // parts
+        h = N.vp()
+        N.call("pxc_flat_create", ctx.handle, 128, 0, C.byref(h))
+        gids = np.arange(lo, hi, dtype=np.uint64)
+        N.call("pxc_flat_sync", h, N.ptr(db[lo:hi]), N.ptr(gids), None, 0, hi - lo)
+        out = (np.zeros((len(qs), k), np.uint64), np.zeros((len(qs), k), np.float32), np.zeros(len(qs), np.uint32))
+        N.call("pxc_flat_search", h, N.ptr(qs), len(qs), k, None, *map(N.ptr, out))
+        N.load().pxc_flat_destroy(h)
+        ids_all.append(out[0]); d_all.append(out[1]); l_all.append(out[2])
+    dev = torch.device("cuda:0")
+    t_ids = torch.from_numpy(np.stack(ids_all).view(np.int64)).to(dev)
+    t_d = torch.from_numpy(np.stack(d_all)).to(dev)
+    t_l = torch.from_numpy(np.stack(l_all).view(np.int32)).to(dev)
+    o_ids = torch.zeros((len(qs), k), dtype=torch.int64, device=dev)
+    o_d = torch.zeros((len(qs), k), dtype=torch.float32, device=dev)
+    o_l = torch.zeros(len(qs), dtype=torch.int32, device=dev)
+    N.call("pxc_topk_merge", ctx.handle, t_ids.data_ptr(), t_d.data_ptr(), t_l.data_ptr(), parts, len(qs), k, k,
+           o_ids.data_ptr(), o_d.data_ptr(), o_l.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    got = (o_ids.cpu().numpy().view(np.uint64), o_d.cpu().numpy(), o_l.cpu().numpy().view(np.uint32))
+    ref = pxo.flat_search(db[:n], qs, k, pxo.EUCLIDEAN)
+    _assert_same(got, ref, len(qs))

@@ -1,0 +1,138 @@
+"""Pin the CPU oracle against the reference's own known-answer tests (distance, space, TopK, flat).
+
+The reference is Rust and cannot be built here; tests/golden/reference_kat.json
+transcribes the constants of its unit tests, each with its file:line.
+"""
+import json
+import math
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import pxo
+
+KAT = json.loads((Path(__file__).parent / "golden" / "reference_kat.json").read_text())
+
+
+def test_distance_known_values():
+    k = KAT["distance_known_values"]
+    assert pxo.squared_euclidean(k["a"], k["b"]) == k["squared_euclidean"]
+    assert math.sqrt(pxo.squared_euclidean(k["a"], k["b"])) == k["euclidean"]
+    assert pxo.manhattan(k["a"], k["b"]) == k["manhattan"]
+    assert pxo.dot(k["a"], k["b"]) == k["dot"]
+    assert pxo.space_distance(pxo.INNER_PRODUCT, k["a"], k["b"]) == k["inner_product"]
+
+
+def test_cosine_cases_and_zero_vector():
+    c = KAT["cosine_cases"]
+    for a, b, want in c["cases"]:
+        assert abs(pxo.cosine(a, b) - want) < c["tolerance"]
+    z = KAT["cosine_zero_vector"]
+    assert pxo.cosine(z["a"], z["b"]) == z["value"]
+
+
+def test_cosine_unit_fast_path():
+    c = KAT["cosine_unit_fast_path"]
+    a, b = pxo.normalized(c["a"]), pxo.normalized(c["b"])
+    assert abs(pxo.cosine(a, b) - pxo.cosine_normalized(a, b)) < c["tolerance"]
+
+
+def test_tail_lengths_agree_with_scalar():
+    t = KAT["tail_lengths"]
+    for dim in range(0, t["max_dim"] + 1):
+        a = np.array([i * 0.5 - 3.0 for i in range(dim)], dtype=np.float32)
+        b = np.array([7.0 - i * 0.25 for i in range(dim)], dtype=np.float32)
+        s = pxo.squared_euclidean_scalar(a, b)
+        u = pxo.squared_euclidean(a, b)
+        assert abs(s - u) <= t["rel_tol"] * max(abs(s), 1.0), dim
+
+
+def test_exact_symmetry_of_l2_and_dot():
+    # crates/proxima-core/tests/metric_properties.rs:108-117: symmetry is exact.
+    rng = np.random.default_rng(1)
+    for dim in (1, 7, 8, 33, 128):
+        a, b = rng.standard_normal(dim).astype(np.float32), rng.standard_normal(dim).astype(np.float32)
+        assert pxo.squared_euclidean(a, b) == pxo.squared_euclidean(b, a)
+        assert pxo.dot(a, b) == pxo.dot(b, a)
+        assert pxo.manhattan(a, b) == pxo.manhattan(b, a)
+
+
+def test_normalize_and_prepare():
+    n = KAT["normalize"]
+    v = np.array(n["v"], dtype=np.float32)
+    out = pxo.normalized(v)
+    assert abs(math.sqrt(pxo.dot(out, out)) - 1.0) < 1e-6
+    z = pxo.normalized([0.0, 0.0])
+    assert list(z) == [0.0, 0.0]
+    p = KAT["prepared_cosine_matches_general"]
+    a, b = pxo.prepare(pxo.COSINE, p["a"])[0], pxo.prepare(pxo.COSINE, p["b"])[0]
+    assert abs(pxo.space_distance(pxo.COSINE, a, b) - pxo.cosine(p["a"], p["b"])) < p["tolerance"]
+
+
+def test_host_prepare_matches_oracle_bit_for_bit():
+    """proxima_b200.core.prepare_batch (numpy, the host side) == oracle prepare."""
+    from proxima_b200.core import Metric, VectorSpace
+
+    rng = np.random.default_rng(7)
+    for dim in (5, 8, 64, 100):
+        rows = rng.standard_normal((50, dim)).astype(np.float32) * 3
+        rows[3] = 0.0
+        mine = VectorSpace(dim, Metric.COSINE).prepare_batch(rows)
+        ref = pxo.prepare(pxo.COSINE, rows)
+        assert np.array_equal(mine.view(np.uint32), ref.view(np.uint32))
+
+
+def _flat(rows, ids, queries, k, metric=pxo.EUCLIDEAN, bitmap=None, live=None):
+    return pxo.flat_search(np.asarray(rows, np.float32), np.asarray(queries, np.float32), k, metric,
+                           ids=np.asarray(ids, np.uint64), live=live, bitmap=bitmap)
+
+
+def test_flat_ties_break_on_id():
+    t = KAT["flat_ties"]
+    rows = [t["vector"]] * len(t["insert_ids"])
+    ids, _, lens = _flat(rows, t["insert_ids"], [t["vector"]], t["k"])
+    assert list(ids[0, : lens[0]]) == t["expected_ids"]
+
+
+def test_flat_filter_runs_during_scan():
+    f = KAT["flat_filter"]
+    rows = [[float(i)] for i in range(f["n"])]
+    keep = np.array([i % f["keep_every"] == 0 for i in range(f["n"])])
+    bitmap = np.packbits(keep, bitorder="little")
+    bitmap = np.concatenate([bitmap, np.zeros(-len(bitmap) % 8, np.uint8)]).view(np.uint64)
+    ids, _, lens = _flat(rows, list(range(f["n"])), [[0.0]], f["k"], bitmap=bitmap)
+    assert list(ids[0, : lens[0]]) == f["expected_ids"]
+
+
+def test_flat_k_larger_and_k_zero_and_empty():
+    g = KAT["flat_k_larger_than_index"]
+    rows = [[float(i)] for i in range(g["n"])]
+    _, _, lens = _flat(rows, list(range(g["n"])), [[0.0]], g["k"])
+    assert lens[0] == g["expected_len"]
+    _, _, lens = _flat(rows, list(range(g["n"])), [[0.0]], 0)
+    assert lens[0] == 0
+
+
+def test_flat_try_from():
+    t = KAT["flat_try_from"]
+    rows = np.array(t["data"], np.float32).reshape(-1, 2)
+    ids, _, _ = _flat(rows, list(range(3)), [t["query"]], 1)
+    assert ids[0, 0] == t["expected_id"]
+
+
+def test_total_order_nan_and_negative_zero():
+    # topk.rs:63-67 uses total_cmp: -0.0 < +0.0 and NaN sorts last.
+    rows = np.array([[0.0], [1.0]], np.float32)
+    ids, d, _ = pxo.flat_search(rows, np.array([[0.0]], np.float32), 2, pxo.INNER_PRODUCT,
+                                ids=np.array([5, 3], np.uint64))
+    # dot with 0 query is +0.0 for both; IP = -0.0; tie -> smaller id first
+    assert list(ids[0]) == [3, 5]
+    assert np.signbit(d[0, 0])
+
+
+def test_recall_overlap():
+    e = np.array([1, 2, 3, 4], np.uint64)
+    a = np.array([2, 9, 4], np.uint64)
+    assert pxo.lib().pxo_recall_overlap(e.ctypes.data, 4, a.ctypes.data, 3) == 0.5
+    assert pxo.lib().pxo_recall_overlap(e.ctypes.data, 0, a.ctypes.data, 3) == 1.0
