@@ -469,6 +469,7 @@ struct pxc_flat {
   DBuf<int32_t> q_norm;
   DBuf<int> q_bad;
   DBuf<uint64_t> part;
+  DBuf<int32_t> bound;
   DBuf<float> stage_f;
   DBuf<uint64_t> stage_id;
   DBuf<unsigned long long> bad_idx;
@@ -571,7 +572,7 @@ void rebuild_mirror(pxc_flat* h, cudaStream_t s) {
   PXC_CUDA(cudaStreamSynchronize(s));
   h->all_u8 = (*h->h_flag != 0);
   // 4. u8 operand for the tensor-core path
-  if (h->all_u8 && h->metric == PXC_EUCLIDEAN && h->dim <= 768) {
+  if (h->all_u8 && h->metric == PXC_EUCLIDEAN && h->dim <= (uint32_t)flat_tc::MAX_KBLOCKS * flat_tc::KB_BYTES) {
     h->dp = (h->dim + 127) / 128 * 128;
     h->nrank_pad = (nl + flat_tc::BN - 1) / flat_tc::BN * flat_tc::BN;
     h->op_u8.reserve(h->nrank_pad * h->dp);
@@ -594,7 +595,7 @@ uint32_t choose_splits(uint32_t nqt, uint32_t ntiles, int sms) {
     uint32_t tps = (ntiles + s - 1) / s;
     uint32_t ctas = nqt * ((ntiles + tps - 1) / tps);
     double waves = std::ceil((double)ctas / sms);
-    double cost = waves * (tps + 6.0);  // +6 tiles of fixed per-CTA cost
+    double cost = waves * (tps + 10.0);  // +10 tiles of fixed per-CTA cost
     if (cost < best * 0.995) {
       best = cost;
       best_s = s;
@@ -603,9 +604,16 @@ uint32_t choose_splits(uint32_t nqt, uint32_t ntiles, int sms) {
   return best_s;
 }
 
+template <int KT>
+void launch_tc(const CUtensorMap& tq, const CUtensorMap& tx, const flat_tc::Params& p, dim3 grid,
+               size_t smem, cudaStream_t s) {
+  PXC_CUDA(cudaFuncSetAttribute(flat_tc::flat_u8_kernel<KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  flat_tc::flat_u8_kernel<KT><<<grid, flat_tc::NUM_THREADS, smem, s>>>(tq, tx, p);
+}
+
 void search_tc(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, uint64_t* d_ids,
                float* d_dist, uint32_t* d_len, cudaStream_t s) {
-  const uint32_t KT = k <= 16 ? 16 : 32;
+  const uint32_t KT = k <= 1 ? 1 : k <= 4 ? 4 : k <= 10 ? 10 : k <= 16 ? 16 : 32;
   const uint32_t nq_pad = (nq + flat_tc::BM - 1) / flat_tc::BM * flat_tc::BM;
   const uint32_t nqt = nq_pad / flat_tc::BM;
   const uint32_t ntiles = (uint32_t)(h->nrank_pad / flat_tc::BN);
@@ -613,28 +621,33 @@ void search_tc(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, uint64_t*
   const uint32_t tps = (ntiles + nsplit_req - 1) / nsplit_req;
   const uint32_t nsplit = (ntiles + tps - 1) / tps;
   h->part.reserve((size_t)nq_pad * nsplit * KT);
+  h->bound.reserve(nq_pad);
+  // 0x3F3F3F3F: above every real r (|r| < 2^25) and below the padding sentinel
+  PXC_CUDA(cudaMemsetAsync(h->bound.p, 0x3F, nq_pad * sizeof(int32_t), s));
   flat_tc::Params p;
   p.norms = h->op_norm.p;
+  p.bound = h->bound.p;
   p.out_part = h->part.p;
   p.status = h->ctx->d_status;
   p.nq = nq;
+  p.k = k;
   p.kblocks = h->dp / flat_tc::KB_BYTES;
   p.ntiles = ntiles;
   p.tiles_per_split = tps;
   p.nsplit = nsplit;
-  p.stages = p.kblocks <= 4 ? 4 : 3;
+  p.stages = flat_tc::pick_stages(p.kblocks);
   p.wait_ns = (uint64_t)h->ctx->wait_ms * 1000000ull;
   CUtensorMap tmap_q;
   make_tmap_u8_2d(&tmap_q, h->q_u8.p, h->dp, nq_pad, flat_tc::KB_BYTES, flat_tc::BM);
   size_t smem = flat_tc::smem_bytes(p.kblocks, p.stages);
   dim3 grid(nqt, nsplit);
   ScanTimer timer(h, s);
-  if (KT == 16) {
-    PXC_CUDA(cudaFuncSetAttribute(flat_tc::flat_u8_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    flat_tc::flat_u8_kernel<16><<<grid, flat_tc::NUM_THREADS, smem, s>>>(tmap_q, h->tmap_x, p);
-  } else {
-    PXC_CUDA(cudaFuncSetAttribute(flat_tc::flat_u8_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    flat_tc::flat_u8_kernel<32><<<grid, flat_tc::NUM_THREADS, smem, s>>>(tmap_q, h->tmap_x, p);
+  switch (KT) {
+    case 1: launch_tc<1>(tmap_q, h->tmap_x, p, grid, smem, s); break;
+    case 4: launch_tc<4>(tmap_q, h->tmap_x, p, grid, smem, s); break;
+    case 10: launch_tc<10>(tmap_q, h->tmap_x, p, grid, smem, s); break;
+    case 16: launch_tc<16>(tmap_q, h->tmap_x, p, grid, smem, s); break;
+    default: launch_tc<32>(tmap_q, h->tmap_x, p, grid, smem, s); break;
   }
   PXC_CUDA(cudaGetLastError());
   timer.stop();
@@ -734,7 +747,7 @@ void search_device(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, const
     return;
   }
   bool tc = h->all_u8 && h->metric == PXC_EUCLIDEAN && d_bitmap == nullptr && k <= 32 &&
-            h->dim <= 768 && h->nrank_pad > 0;
+            h->dim <= (uint32_t)flat_tc::MAX_KBLOCKS * flat_tc::KB_BYTES && h->nrank_pad > 0;
   if (tc) {
     const uint32_t nq_pad = (nq + flat_tc::BM - 1) / flat_tc::BM * flat_tc::BM;
     h->q_u8.reserve((size_t)nq_pad * h->dp);
@@ -885,7 +898,7 @@ int32_t pxc_flat_path(const pxc_flat* h) {
       return -1;
     }
   }
-  return (m->all_u8 && m->metric == PXC_EUCLIDEAN && m->dim <= 768 && m->nrank > 0) ? 1 : 0;
+  return (m->all_u8 && m->metric == PXC_EUCLIDEAN && m->dim <= (uint32_t)flat_tc::MAX_KBLOCKS * flat_tc::KB_BYTES && m->nrank > 0) ? 1 : 0;
 }
 
 pxc_status pxc_flat_search_device(pxc_flat* h, const float* d_queries, uint32_t nq, uint32_t k,

@@ -5,10 +5,9 @@
 // Why it is exact: for such data every product and every partial sum of the
 // reference's squared_euclidean (crates/proxima-core/src/distance.rs:267-283)
 // is an integer below 2^24, so the reference's f32 result is the exact
-// integer ||q-x||^2 whatever the summation order. The kernel computes
-// q.x exactly in s32 (kind::i8, u8 x u8), forms r = ||x||^2 - 2 q.x per
-// column, and ranks on r; the distance is r + ||q||^2, converted to f32
-// exactly.
+// integer ||q-x||^2 whatever the summation order. The kernel computes q.x
+// exactly in s32 (kind::i8, u8 x u8), forms r = ||x||^2 - 2 q.x per column
+// and ranks on r; the distance is r + ||q||^2, converted to f32 exactly.
 //
 // Why ranking on r with a strict '<' is exact: columns are database rows in
 // ascending VectorId order ("rank" order), and every thread scans its columns
@@ -16,15 +15,20 @@
 // larger id and loses the (total_cmp, id) comparison
 // (crates/proxima-core/src/topk.rs:63-67).
 //
-// Structure (one CTA per 128 queries x one range of database rows):
-//   warp 0      TMA producer: query tile once, then 256-row database tiles
-//               through a STAGES-deep shared-memory ring (128-byte swizzle,
-//               no multicast);
+// Structure: one CTA per 256 queries x one contiguous range of database
+// rows ("split").
+//   warp 0      TMA producer: the 256-query tile once, then 128-row database
+//               tiles through a STAGES-deep ring (128-byte swizzle, no
+//               multicast);
 //   warp 1      allocates 512 TMEM columns; lane 0 issues tcgen05.mma
-//               (M=128, N=256, K=32 per instruction) into one of two TMEM
-//               accumulators and commits to mbarriers;
-//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time, r = h - 2*dot,
-//               warp-free per-thread top-KT in registers (thread = query row).
+//               (M=128, N=128, K=32 per instruction) for both query halves
+//               into one of two double-buffered TMEM accumulators;
+//   warps 2-9   epilogue, one thread per query row: tcgen05.ld 32 columns at
+//               a time, r = h - 2*dot, running top-KT in registers.
+// The CTAs of one query tile share a per-query bound in global memory: each
+// publishes its current k-th r with atomicMin and prunes with the smallest
+// published bound (a candidate strictly above some CTA's k-th value cannot be
+// in the global top-k), so later splits skip almost every insertion.
 // Every mbarrier wait is bounded by a global-timer limit; on expiry the CTA
 // records DEV_TIMEOUT_* in the status word, drains its own copies and MMAs,
 // frees TMEM and returns.
@@ -35,21 +39,27 @@
 namespace pxc {
 namespace flat_tc {
 
-constexpr int BM = 128;        // queries per CTA (TMEM lanes)
-constexpr int BN = 256;        // database rows per tile (TMEM columns per accumulator)
-constexpr int KB_BYTES = 128;  // one swizzle atom of K per TMA box
+constexpr int BM = 256;        // queries per CTA (two M=128 accumulators)
+constexpr int UM = 128;        // UMMA M
+constexpr int BN = 128;        // database rows per tile = UMMA N
+constexpr int KB_BYTES = 128;  // one 128-byte swizzle atom of K per TMA box
 constexpr int UMMA_K = 32;     // K bytes per tcgen05.mma kind::i8
-constexpr int A_BLOCK = BM * KB_BYTES;  // 16 KiB
-constexpr int B_BLOCK = BN * KB_BYTES;  // 32 KiB
-constexpr int NUM_THREADS = 192;
-constexpr int32_t BIG = 0x3FFFFFFF;     // sentinel: padding columns and empty slots
-constexpr uint32_t R_OFFSET = 0x02000000u;  // makes r non-negative for packing
+constexpr int A_BLOCK = BM * KB_BYTES;  // 32 KiB per K block
+constexpr int B_BLOCK = BN * KB_BYTES;  // 16 KiB per stage
+constexpr int NUM_EPI_WARPS = 8;
+constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;  // 320
+constexpr int MAX_KBLOCKS = 4;                        // dim <= 512
+constexpr int32_t BIG = 0x3FFFFFFF;                   // sentinel: padding columns, empty slots
+constexpr uint32_t R_OFFSET = 0x02000000u;            // makes r non-negative for packing
+constexpr size_t SMEM_LIMIT = 227 * 1024;
 
 struct Params {
   const int32_t* norms;    // ||x||^2 per rank, BIG for padding ranks
+  int32_t* bound;          // [nq_pad] shared pruning bound on r per query
   uint64_t* out_part;      // [nq_pad][nsplit][KT] packed (r+R_OFFSET)<<32 | rank
   uint32_t* status;        // device error word
   uint32_t nq;
+  uint32_t k;              // requested k (<= KT); the k-th value is what is shared
   uint32_t kblocks;        // dim_pad / 128
   uint32_t ntiles;         // nrank_pad / BN
   uint32_t tiles_per_split;
@@ -62,6 +72,12 @@ __host__ __device__ inline size_t smem_bytes(uint32_t kblocks, uint32_t stages) 
   size_t off = (size_t)kblocks * A_BLOCK + (size_t)stages * B_BLOCK;
   off += (2 * stages + 6) * sizeof(uint64_t) + 16;
   return off + 1024;  // alignment slack
+}
+
+__host__ inline uint32_t pick_stages(uint32_t kblocks) {
+  size_t fixed = (size_t)kblocks * A_BLOCK + 1024 + 256;
+  uint32_t s = (uint32_t)((SMEM_LIMIT - fixed) / (B_BLOCK + 16));
+  return s > 8 ? 8 : s;
 }
 
 // Branch-free insertion into an ascending register list; precondition
@@ -84,9 +100,13 @@ __device__ __forceinline__ void insert_sorted(int32_t (&lr)[K], uint32_t (&lk)[K
 }
 
 __device__ __forceinline__ void record_failure(uint32_t* status, uint32_t code) {
-  if (atomicCAS(status, 0u, code) == 0u) {
-    atomicExch(status + 1, blockIdx.y * gridDim.x + blockIdx.x);
-  }
+  if (atomicCAS(status, 0u, code) == 0u) atomicExch(status + 1, blockIdx.y * gridDim.x + blockIdx.x);
+}
+
+__device__ __forceinline__ int32_t load_bound(const int32_t* p) {
+  int32_t v;
+  asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 template <int KT>
@@ -128,7 +148,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4 * 32);
+      mbar_init(&acc_empty[b], NUM_EPI_WARPS * 32);
     }
     mbar_init(a_full, 1);
     mbar_init(mma_done, 1);
@@ -159,8 +179,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[s], B_BLOCK);
-          tma_load_2d(sB + (size_t)s * B_BLOCK, &tmap_x, &full[s], kb * KB_BYTES,
-                      (t_begin + t) * BN);
+          tma_load_2d(sB + (size_t)s * B_BLOCK, &tmap_x, &full[s], kb * KB_BYTES, (t_begin + t) * BN);
         }
       }
       // Drain: every copy this thread issued has landed before the CTA exits.
@@ -171,7 +190,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      const uint32_t idesc = idesc_u8_s32(BM, BN);
+      const uint32_t idesc = idesc_u8_s32(UM, BN);
       bool ok = mbar_wait(a_full, 0, p.wait_ns);
       if (!ok) {
         record_failure(p.status, DEV_TIMEOUT_FULL);
@@ -189,7 +208,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + buf * BN;
         for (uint32_t kb = 0; kb < kblocks; ++kb, ++it) {
           uint32_t s = it % stages, ph = (it / stages) & 1;
           if (!mbar_wait(&full[s], ph, p.wait_ns) || failed) {
@@ -199,13 +217,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint64_t adesc = smem_desc_k_sw128(a_addr + kb * A_BLOCK);
           const uint64_t bdesc = smem_desc_k_sw128(b_addr + s * B_BLOCK);
 #pragma unroll
-          for (uint32_t k = 0; k < KB_BYTES / UMMA_K; ++k) {
-            // K advance inside the 128-byte swizzle atom: +32 bytes = +2 in the
-            // 16-byte-unit start-address field.
-            mma_i8(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+          for (uint32_t m = 0; m < 2; ++m) {
+            const uint64_t adesc = smem_desc_k_sw128(a_addr + kb * A_BLOCK + m * (UM * KB_BYTES));
+            const uint32_t d_tmem = tmem_base + (buf * 2 + m) * BN;
+#pragma unroll
+            for (uint32_t k = 0; k < KB_BYTES / UMMA_K; ++k) {
+              // K advance inside the 128-byte swizzle atom: +32 bytes = +2 in
+              // the 16-byte-unit start-address field.
+              mma_i8(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+            }
           }
           mma_commit(&empty[s]);
         }
@@ -217,9 +239,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_wait(mma_done, 0, p.wait_ns);
     }
   } else {
-    // ---------------- epilogue: warps 2..5 ----------------
+    // ---------------- epilogue: warps 2..9, one thread per query row ----------------
     const uint32_t quarter = warp & 3;
-    const uint32_t row = quarter * 32 + lane;
+    const uint32_t mtile = (warp - 2) >> 2;
+    const uint32_t row = mtile * UM + quarter * 32 + lane;
+    const uint32_t q = qtile * BM + row;
+    int32_t* bound_ptr = p.bound + q;
     int32_t lr[KT];
     uint32_t lk[KT];
 #pragma unroll
@@ -227,6 +252,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       lr[i] = BIG;
       lk[i] = 0xFFFFFFFFu;
     }
+    int32_t shared_bound = load_bound(bound_ptr);  // prune r > shared_bound
+    int32_t published = BIG;
     for (uint32_t t = 0; t < ntile_local; ++t) {
       uint32_t buf = t & 1, use = t >> 1;
       if (!mbar_wait(&acc_full[buf], use & 1, p.wait_ns) || failed) {
@@ -236,35 +263,49 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       tc_fence_after();
       const uint32_t rank_base = (t_begin + t) * BN;
-      const uint32_t taddr = tmem_base + ((quarter * 32) << 16) + buf * BN;
-#pragma unroll 1
+      const uint32_t taddr = tmem_base + ((quarter * 32) << 16) + (buf * 2 + mtile) * BN;
+#pragma unroll
       for (uint32_t c = 0; c < BN / 32; ++c) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(taddr + c * 32, v);
-        tmem_ld_wait();
         const int4* np = reinterpret_cast<const int4*>(p.norms + rank_base + c * 32);
+        int4 h[8];
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4) h[j4] = __ldg(np + j4);
+        tmem_ld_wait();
         int32_t r[32];
-        int32_t rmin = BIG;
 #pragma unroll
         for (int j4 = 0; j4 < 8; ++j4) {
-          int4 h = __ldg(np + j4);
-          r[4 * j4 + 0] = h.x - 2 * static_cast<int32_t>(v[4 * j4 + 0]);
-          r[4 * j4 + 1] = h.y - 2 * static_cast<int32_t>(v[4 * j4 + 1]);
-          r[4 * j4 + 2] = h.z - 2 * static_cast<int32_t>(v[4 * j4 + 2]);
-          r[4 * j4 + 3] = h.w - 2 * static_cast<int32_t>(v[4 * j4 + 3]);
+          r[4 * j4 + 0] = h[j4].x - 2 * static_cast<int32_t>(v[4 * j4 + 0]);
+          r[4 * j4 + 1] = h[j4].y - 2 * static_cast<int32_t>(v[4 * j4 + 1]);
+          r[4 * j4 + 2] = h[j4].z - 2 * static_cast<int32_t>(v[4 * j4 + 2]);
+          r[4 * j4 + 3] = h[j4].w - 2 * static_cast<int32_t>(v[4 * j4 + 3]);
         }
+        int32_t rmin = r[0];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) rmin = min(rmin, r[j]);
-        if (rmin < lr[KT - 1]) {
+        for (int j = 1; j < 32; ++j) rmin = min(rmin, r[j]);
+        // admit r < lr[KT-1] and r <= shared_bound
+        const int32_t thr = min(lr[KT - 1], shared_bound + 1);
+        if (rmin < thr) {
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            if (r[j] < lr[KT - 1]) insert_sorted<KT>(lr, lk, r[j], rank_base + c * 32 + j);
+            if (r[j] < min(lr[KT - 1], shared_bound + 1))
+              insert_sorted<KT>(lr, lk, r[j], rank_base + c * 32 + j);
         }
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
+      // share the bound with the other splits of this query tile: the k-th
+      // value of this split's list (k <= KT, selected without dynamic indexing)
+      int32_t kth = lr[KT - 1];
+#pragma unroll
+      for (int i = 0; i < KT; ++i) kth = (i + 1 == (int)p.k) ? lr[i] : kth;
+      if (kth < published) {
+        published = kth;
+        atomicMin(bound_ptr, published);
+      }
+      shared_bound = min(shared_bound, load_bound(bound_ptr));
     }
-    const uint32_t q = qtile * BM + row;
     if (q < p.nq) {
       uint64_t* dst = p.out_part + ((size_t)q * p.nsplit + split) * KT;
 #pragma unroll
