@@ -24,14 +24,19 @@
 //               (M=128, N=128, K=32 per instruction) for both query halves
 //               into one of two double-buffered TMEM accumulators;
 //   warps 2-9   epilogue, one thread per query row: tcgen05.ld 32 columns at
-//               a time, r = h - 2*dot, running top-KT in registers.
+//               a time (two chunks in flight), r = h - 2*dot, a tree min
+//               against the thread's admission bound; only chunks where some
+//               lane has a candidate take the slow path, which re-reads just
+//               the candidate columns from TMEM and inserts into a sorted
+//               register list of KT entries.
 // The CTAs of one query tile share a per-query bound in global memory: each
 // publishes its current k-th r with atomicMin and prunes with the smallest
 // published bound (a candidate strictly above some CTA's k-th value cannot be
 // in the global top-k), so later splits skip almost every insertion.
 // Every mbarrier wait is bounded by a global-timer limit; on expiry the CTA
 // records DEV_TIMEOUT_* in the status word, drains its own copies and MMAs,
-// frees TMEM and returns.
+// frees TMEM and returns. There is no barrier among the epilogue warps, so a
+// warp that gives up cannot strand another.
 #pragma once
 #include "common.cuh"
 #include "sm100.cuh"
@@ -52,6 +57,7 @@ constexpr int MAX_KBLOCKS = 4;                        // dim <= 512
 constexpr int32_t BIG = 0x3FFFFFFF;                   // sentinel: padding columns, empty slots
 constexpr uint32_t R_OFFSET = 0x02000000u;            // makes r non-negative for packing
 constexpr size_t SMEM_LIMIT = 227 * 1024;
+constexpr size_t NORM_BYTES = (size_t)NUM_EPI_WARPS * 2 * BN * sizeof(int32_t);  // per-warp, 2 tiles
 
 struct Params {
   const int32_t* norms;    // ||x||^2 per rank, BIG for padding ranks
@@ -69,13 +75,13 @@ struct Params {
 };
 
 __host__ __device__ inline size_t smem_bytes(uint32_t kblocks, uint32_t stages) {
-  size_t off = (size_t)kblocks * A_BLOCK + (size_t)stages * B_BLOCK;
+  size_t off = (size_t)kblocks * A_BLOCK + (size_t)stages * B_BLOCK + NORM_BYTES;
   off += (2 * stages + 6) * sizeof(uint64_t) + 16;
   return off + 1024;  // alignment slack
 }
 
 __host__ inline uint32_t pick_stages(uint32_t kblocks) {
-  size_t fixed = (size_t)kblocks * A_BLOCK + 1024 + 256;
+  size_t fixed = (size_t)kblocks * A_BLOCK + NORM_BYTES + 1024 + 256;
   uint32_t s = (uint32_t)((SMEM_LIMIT - fixed) / (B_BLOCK + 16));
   return s > 8 ? 8 : s;
 }
@@ -109,6 +115,49 @@ __device__ __forceinline__ int32_t load_bound(const int32_t* p) {
   return v;
 }
 
+// r = ||x||^2 - 2 q.x for one 32-column chunk; returns the chunk minimum
+// (tree reduction: depth 5 instead of a 31-long dependency chain).
+__device__ __forceinline__ int32_t chunk_r(const uint32_t (&v)[32], const int32_t* nrm, int32_t (&r)[32]) {
+#pragma unroll
+  for (int j4 = 0; j4 < 8; ++j4) {
+    const int4 h = *reinterpret_cast<const int4*>(nrm + 4 * j4);
+    r[4 * j4 + 0] = h.x - 2 * static_cast<int32_t>(v[4 * j4 + 0]);
+    r[4 * j4 + 1] = h.y - 2 * static_cast<int32_t>(v[4 * j4 + 1]);
+    r[4 * j4 + 2] = h.z - 2 * static_cast<int32_t>(v[4 * j4 + 2]);
+    r[4 * j4 + 3] = h.w - 2 * static_cast<int32_t>(v[4 * j4 + 3]);
+  }
+  int32_t m[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) m[j] = min(r[j], r[j + 16]);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) m[j] = min(m[j], m[j + 8]);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) m[j] = min(m[j], m[j + 4]);
+  return min(min(m[0], m[2]), min(m[1], m[3]));
+}
+
+// Slow path of one chunk, entered by the whole warp when some lane has a
+// candidate: build each lane's candidate mask, iterate the union of the masks
+// warp-uniformly, re-read that column from TMEM, insert where admitted.
+template <int KT>
+__device__ __forceinline__ void chunk_insert(const int32_t (&r)[32], int32_t (&lr)[KT], uint32_t (&lk)[KT],
+                                             int32_t shared_bound, uint32_t taddr_chunk,
+                                             const int32_t* nrm, uint32_t rank0) {
+  const int32_t thr = min(lr[KT - 1], shared_bound + 1);
+  uint32_t mask = 0;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) mask |= (r[j] < thr ? 1u : 0u) << j;
+  uint32_t umask = __reduce_or_sync(0xFFFFFFFFu, mask);
+  while (umask) {
+    const int j = __ffs(umask) - 1;
+    umask &= umask - 1;
+    const uint32_t vj = sm100::tmem_ld_32x32b_x1(taddr_chunk + j);
+    sm100::tmem_ld_wait();
+    const int32_t rj = nrm[j] - 2 * static_cast<int32_t>(vj);
+    if (rj < min(lr[KT - 1], shared_bound + 1)) insert_sorted<KT>(lr, lk, rj, rank0 + j);
+  }
+}
+
 template <int KT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     flat_u8_kernel(const __grid_constant__ CUtensorMap tmap_q,
@@ -120,7 +169,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t kblocks = p.kblocks, stages = p.stages;
   unsigned char* sA = smem;
   unsigned char* sB = smem + (size_t)kblocks * A_BLOCK;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + (size_t)stages * B_BLOCK);
+  int32_t* sNorm = reinterpret_cast<int32_t*>(sB + (size_t)stages * B_BLOCK);  // [warp][2][BN]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sNorm + NUM_EPI_WARPS * 2 * BN);
   uint64_t* full = bars;
   uint64_t* empty = bars + stages;
   uint64_t* acc_full = bars + 2 * stages;
@@ -240,11 +290,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else {
     // ---------------- epilogue: warps 2..9, one thread per query row ----------------
+    const uint32_t ew = warp - 2;
     const uint32_t quarter = warp & 3;
-    const uint32_t mtile = (warp - 2) >> 2;
+    const uint32_t mtile = ew >> 2;
     const uint32_t row = mtile * UM + quarter * 32 + lane;
     const uint32_t q = qtile * BM + row;
     int32_t* bound_ptr = p.bound + q;
+    int32_t* wnorm = sNorm + ew * 2 * BN;  // this warp's two tile slots
     int32_t lr[KT];
     uint32_t lk[KT];
 #pragma unroll
@@ -254,9 +306,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     int32_t shared_bound = load_bound(bound_ptr);  // prune r > shared_bound
     int32_t published = BIG;
+    // ||x||^2 of tile t sits in this warp's slot t & 1; tile t+1's is fetched
+    // (4 per lane) while tile t is scanned.
+    int4 next_norm = make_int4(0, 0, 0, 0);
+    if (ntile_local > 0)
+      *reinterpret_cast<int4*>(wnorm + 4 * lane) =
+          __ldg(reinterpret_cast<const int4*>(p.norms + t_begin * BN) + lane);
+    __syncwarp();
     for (uint32_t t = 0; t < ntile_local; ++t) {
-      uint32_t buf = t & 1, use = t >> 1;
-      if (!mbar_wait(&acc_full[buf], use & 1, p.wait_ns) || failed) {
+      const uint32_t buf = t & 1, use = t >> 1;
+      if (t + 1 < ntile_local)
+        next_norm = __ldg(reinterpret_cast<const int4*>(p.norms + (t_begin + t + 1) * BN) + lane);
+      const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&acc_full[buf], use & 1, p.wait_ns) && !failed);
+      if (!ok) {
         record_failure(p.status, DEV_TIMEOUT_ACC);
         failed = 1;
         break;
@@ -264,39 +326,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const uint32_t rank_base = (t_begin + t) * BN;
       const uint32_t taddr = tmem_base + ((quarter * 32) << 16) + (buf * 2 + mtile) * BN;
+      const int32_t* nrm = wnorm + (t & 1) * BN;
+      uint32_t va[32], vb[32];
+      int32_t r[32];
+      tmem_ld_32x32b_x32(taddr, va);
+      tmem_ld_wait();
 #pragma unroll
-      for (uint32_t c = 0; c < BN / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(taddr + c * 32, v);
-        const int4* np = reinterpret_cast<const int4*>(p.norms + rank_base + c * 32);
-        int4 h[8];
-#pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4) h[j4] = __ldg(np + j4);
+      for (uint32_t c = 0; c < BN / 32; c += 2) {
+        // chunk c from va while chunk c+1 loads into vb, then the reverse
+        tmem_ld_32x32b_x32(taddr + (c + 1) * 32, vb);
+        int32_t rmin = chunk_r(va, nrm + c * 32, r);
+        if (__any_sync(0xFFFFFFFFu, rmin < min(lr[KT - 1], shared_bound + 1)))
+          chunk_insert<KT>(r, lr, lk, shared_bound, taddr + c * 32, nrm + c * 32, rank_base + c * 32);
         tmem_ld_wait();
-        int32_t r[32];
-#pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4) {
-          r[4 * j4 + 0] = h[j4].x - 2 * static_cast<int32_t>(v[4 * j4 + 0]);
-          r[4 * j4 + 1] = h[j4].y - 2 * static_cast<int32_t>(v[4 * j4 + 1]);
-          r[4 * j4 + 2] = h[j4].z - 2 * static_cast<int32_t>(v[4 * j4 + 2]);
-          r[4 * j4 + 3] = h[j4].w - 2 * static_cast<int32_t>(v[4 * j4 + 3]);
-        }
-        int32_t rmin = r[0];
-#pragma unroll
-        for (int j = 1; j < 32; ++j) rmin = min(rmin, r[j]);
-        // admit r < lr[KT-1] and r <= shared_bound
-        const int32_t thr = min(lr[KT - 1], shared_bound + 1);
-        if (rmin < thr) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (r[j] < min(lr[KT - 1], shared_bound + 1))
-              insert_sorted<KT>(lr, lk, r[j], rank_base + c * 32 + j);
-        }
+        if (c + 2 < BN / 32) tmem_ld_32x32b_x32(taddr + (c + 2) * 32, va);
+        rmin = chunk_r(vb, nrm + (c + 1) * 32, r);
+        if (__any_sync(0xFFFFFFFFu, rmin < min(lr[KT - 1], shared_bound + 1)))
+          chunk_insert<KT>(r, lr, lk, shared_bound, taddr + (c + 1) * 32, nrm + (c + 1) * 32,
+                           rank_base + (c + 1) * 32);
+        tmem_ld_wait();
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
-      // share the bound with the other splits of this query tile: the k-th
-      // value of this split's list (k <= KT, selected without dynamic indexing)
+      // This warp finished reading slot (t+1)&1 during tile t-1.
+      if (t + 1 < ntile_local) *reinterpret_cast<int4*>(wnorm + ((t + 1) & 1) * BN + 4 * lane) = next_norm;
+      __syncwarp();
+      // Share the bound with the other splits of this query tile: the k-th
+      // value of this split's list (k <= KT, selected without dynamic indexing).
       int32_t kth = lr[KT - 1];
 #pragma unroll
       for (int i = 0; i < KT; ++i) kth = (i + 1 == (int)p.k) ? lr[i] : kth;
