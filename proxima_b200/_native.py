@@ -6,12 +6,14 @@ if the library is missing or no B200 is visible, every call fails loudly.
 from __future__ import annotations
 
 import ctypes as C
+import os
 from pathlib import Path
 
 from .errors import raise_for_status
 
 LIB_DIR = Path(__file__).resolve().parent / "lib"
-LIB_PATH = LIB_DIR / "libproxima_cuda.so"
+# PXC_LIBRARY selects another build of the same ABI (e.g. a packaged copy).
+LIB_PATH = Path(os.environ.get("PXC_LIBRARY", str(LIB_DIR / "libproxima_cuda.so")))
 
 u8p = C.POINTER(C.c_uint8)
 u32p = C.POINTER(C.c_uint32)

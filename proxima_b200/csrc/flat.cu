@@ -397,35 +397,41 @@ __global__ void prep_queries_u8_kernel(const float* __restrict__ Q, uint32_t nq,
 }
 
 // Merge of K1's per-split lists: per query, nsplit*KT packed (r, rank) keys,
-// sort, keep k, distance = r + ||q||^2 (exact integer in f32).
+// sort, drop duplicates (a split may carry entries seeded from an earlier
+// split), keep k, distance = r + ||q||^2 (exact integer in f32).
 __global__ void merge_u8_kernel(const uint64_t* __restrict__ part, uint32_t nsplit, uint32_t KT,
                                 uint32_t cap, uint32_t k, const int32_t* __restrict__ qnorm,
-                                const uint64_t* __restrict__ rank_id, uint64_t* __restrict__ out_ids,
-                                float* __restrict__ out_dist, uint32_t* __restrict__ out_len) {
+                                const uint64_t* __restrict__ rank_id, uint32_t nrank,
+                                uint64_t* __restrict__ out_ids, float* __restrict__ out_dist,
+                                uint32_t* __restrict__ out_len) {
   extern __shared__ uint64_t sl[];
   const uint32_t q = blockIdx.x;
   const uint32_t n = nsplit * KT;
   const uint64_t empty_key = static_cast<uint64_t>(static_cast<uint32_t>(flat_tc::BIG) + flat_tc::R_OFFSET) << 32;
   for (uint32_t i = threadIdx.x; i < cap; i += blockDim.x) {
     uint64_t v = i < n ? part[(size_t)q * n + i] : ~0ull;
-    sl[i] = (v >= empty_key) ? ~0ull : v;
+    // empty slots, and (defensively) any rank outside the mirror, never reach the output
+    sl[i] = (v >= empty_key || static_cast<uint32_t>(v) >= nrank) ? ~0ull : v;
   }
   __syncthreads();
   block_bitonic_sort_u64(sl, cap);
-  __shared__ uint32_t cnt;
-  if (threadIdx.x == 0) cnt = 0;
+  // mark duplicates of the previous key, then compact the unique prefix
+  __shared__ uint32_t flag[2048];
+  for (uint32_t i = threadIdx.x; i < cap; i += blockDim.x)
+    flag[i] = (sl[i] != ~0ull && (i == 0 || sl[i] != sl[i - 1])) ? 1u : 0u;
   __syncthreads();
-  for (uint32_t i = threadIdx.x; i < k && i < cap; i += blockDim.x) {
-    uint64_t v = sl[i];
-    if (v != ~0ull) {
-      int32_t r = static_cast<int32_t>(static_cast<uint32_t>(v >> 32) - flat_tc::R_OFFSET);
-      out_ids[(size_t)q * k + i] = rank_id[static_cast<uint32_t>(v)];
-      out_dist[(size_t)q * k + i] = static_cast<float>(r + qnorm[q]);
-      atomicAdd(&cnt, 1u);
+  if (threadIdx.x == 0) {
+    uint32_t n_out = 0;
+    for (uint32_t i = 0; i < cap && n_out < k; ++i) {
+      if (!flag[i]) continue;
+      const uint64_t v = sl[i];
+      const int32_t r = static_cast<int32_t>(static_cast<uint32_t>(v >> 32) - flat_tc::R_OFFSET);
+      out_ids[(size_t)q * k + n_out] = rank_id[static_cast<uint32_t>(v)];
+      out_dist[(size_t)q * k + n_out] = static_cast<float>(r + qnorm[q]);
+      ++n_out;
     }
+    out_len[q] = n_out;
   }
-  __syncthreads();
-  if (threadIdx.x == 0) out_len[q] = cnt;
 }
 
 __global__ void zero_u32_kernel(uint32_t* p, uint64_t n) {
@@ -470,6 +476,7 @@ struct pxc_flat {
   DBuf<int> q_bad;
   DBuf<uint64_t> part;
   DBuf<int32_t> bound;
+  DBuf<uint32_t> done;  // per query tile: finished-split counter, then the finished split ids
   DBuf<float> stage_f;
   DBuf<uint64_t> stage_id;
   DBuf<unsigned long long> bad_idx;
@@ -587,15 +594,18 @@ void rebuild_mirror(pxc_flat* h, cudaStream_t s) {
 }
 
 // Number of row splits for K1: balance waves of CTAs over the SMs.
-uint32_t choose_splits(uint32_t nqt, uint32_t ntiles, int sms) {
-  uint32_t smax = std::max<uint32_t>(1, std::min<uint32_t>(ntiles / 8, 512));
+// At most 2048 / KT splits, so one query's candidates fit the merge block.
+uint32_t choose_splits(uint32_t nqt, uint32_t ntiles, int sms, uint32_t KT) {
+  uint32_t smax = std::max<uint32_t>(1, std::min<uint32_t>(ntiles / 8, 2048 / KT));
   double best = 1e30;
   uint32_t best_s = 1;
   for (uint32_t s = 1; s <= smax; ++s) {
     uint32_t tps = (ntiles + s - 1) / s;
     uint32_t ctas = nqt * ((ntiles + tps - 1) / tps);
     double waves = std::ceil((double)ctas / sms);
-    double cost = waves * (tps + 10.0);  // +10 tiles of fixed per-CTA cost
+    // +10 tiles of fixed per-CTA cost; the first wave starts without seeds
+    // from finished splits and runs about 1.5x slower, hence the 0.5/waves.
+    double cost = waves * (tps + 10.0) * (1.0 + 0.5 / waves);
     if (cost < best * 0.995) {
       best = cost;
       best_s = s;
@@ -617,16 +627,21 @@ void search_tc(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, uint64_t*
   const uint32_t nq_pad = (nq + flat_tc::BM - 1) / flat_tc::BM * flat_tc::BM;
   const uint32_t nqt = nq_pad / flat_tc::BM;
   const uint32_t ntiles = (uint32_t)(h->nrank_pad / flat_tc::BN);
-  const uint32_t nsplit_req = choose_splits(nqt, ntiles, h->ctx->sm_count);
+  const uint32_t nsplit_req = choose_splits(nqt, ntiles, h->ctx->sm_count, KT);
   const uint32_t tps = (ntiles + nsplit_req - 1) / nsplit_req;
   const uint32_t nsplit = (ntiles + tps - 1) / tps;
   h->part.reserve((size_t)nq_pad * nsplit * KT);
   h->bound.reserve(nq_pad);
+  h->done.reserve(nqt + (size_t)nqt * nsplit);
   // 0x3F3F3F3F: above every real r (|r| < 2^25) and below the padding sentinel
   PXC_CUDA(cudaMemsetAsync(h->bound.p, 0x3F, nq_pad * sizeof(int32_t), s));
+  PXC_CUDA(cudaMemsetAsync(h->done.p, 0, nqt * sizeof(uint32_t), s));
+  PXC_CUDA(cudaMemsetAsync(h->done.p + nqt, 0xFF, (size_t)nqt * nsplit * sizeof(uint32_t), s));
   flat_tc::Params p;
   p.norms = h->op_norm.p;
   p.bound = h->bound.p;
+  p.done_count = h->done.p;
+  p.done_list = h->done.p + nqt;
   p.out_part = h->part.p;
   p.status = h->ctx->d_status;
   p.nq = nq;
@@ -657,7 +672,7 @@ void search_tc(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, uint64_t*
   size_t msmem = cap * sizeof(uint64_t);
   if (msmem > 48 * 1024)
     PXC_CUDA(cudaFuncSetAttribute(merge_u8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msmem));
-  merge_u8_kernel<<<nq, 256, msmem, s>>>(h->part.p, nsplit, KT, cap, k, h->q_norm.p, h->rank_id.p,
+  merge_u8_kernel<<<nq, 256, msmem, s>>>(h->part.p, nsplit, KT, cap, k, h->q_norm.p, h->rank_id.p, (uint32_t)h->nrank,
                                          d_ids, d_dist, d_len);
   PXC_CUDA(cudaGetLastError());
 }

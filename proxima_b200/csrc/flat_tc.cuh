@@ -16,23 +16,29 @@
 // (crates/proxima-core/src/topk.rs:63-67).
 //
 // Structure: one CTA per 256 queries x one contiguous range of database
-// rows ("split").
-//   warp 0      TMA producer: the 256-query tile once, then 128-row database
+// rows ("split"), 256 database rows per tile.
+//   warp 0      TMA producer: the 256-query tile once, then 256-row database
 //               tiles through a STAGES-deep ring (128-byte swizzle, no
 //               multicast);
-//   warp 1      allocates 512 TMEM columns; lane 0 issues tcgen05.mma
-//               (M=128, N=128, K=32 per instruction) for both query halves
-//               into one of two double-buffered TMEM accumulators;
-//   warps 2-9   epilogue, one thread per query row: tcgen05.ld 32 columns at
-//               a time (two chunks in flight), r = h - 2*dot, a tree min
-//               against the thread's admission bound; only chunks where some
-//               lane has a candidate take the slow path, which re-reads just
-//               the candidate columns from TMEM and inserts into a sorted
+//   warp 1      allocates all 512 TMEM columns as two 128 x 256 s32
+//               accumulators, one per query half; lane 0 issues tcgen05.mma
+//               (M=128, N=256, K=32 per instruction). N=256 keeps the
+//               shared-memory operand traffic of each MMA at 96 B/clk, so
+//               the MMAs and the TMA writes fit the SM's shared-memory port
+//               together (with N=128 they serialise and the tile rate halves);
+//   warps 2-9   epilogue, one thread per query row (warps 2-5: first query
+//               half, 6-9: second): tcgen05.ld 32 columns at a time (two
+//               chunks in flight), r = h - 2*dot, a tree min against the
+//               thread's admission bound; only chunks where some lane has a
+//               candidate take the slow path, which re-reads just the
+//               candidate columns from TMEM and inserts into a sorted
 //               register list of KT entries.
-// The CTAs of one query tile share a per-query bound in global memory: each
-// publishes its current k-th r with atomicMin and prunes with the smallest
-// published bound (a candidate strictly above some CTA's k-th value cannot be
-// in the global top-k), so later splits skip almost every insertion.
+// The halves ping-pong: while the tensor core fills one half's accumulator
+// for tile t, the other half's epilogue drains tile t-1 (or t).
+// The CTAs of one query tile share a per-query bound in global memory (each
+// publishes its current k-th r with atomicMin; a candidate strictly above some
+// CTA's k-th value cannot be in the global top-k), and a CTA starts from the
+// final lists of finished earlier splits of its query tile.
 // Every mbarrier wait is bounded by a global-timer limit; on expiry the CTA
 // records DEV_TIMEOUT_* in the status word, drains its own copies and MMAs,
 // frees TMEM and returns. There is no barrier among the epilogue warps, so a
@@ -46,22 +52,28 @@ namespace flat_tc {
 
 constexpr int BM = 256;        // queries per CTA (two M=128 accumulators)
 constexpr int UM = 128;        // UMMA M
-constexpr int BN = 128;        // database rows per tile = UMMA N
+constexpr int BN = 256;        // database rows per tile = UMMA N
 constexpr int KB_BYTES = 128;  // one 128-byte swizzle atom of K per TMA box
 constexpr int UMMA_K = 32;     // K bytes per tcgen05.mma kind::i8
 constexpr int A_BLOCK = BM * KB_BYTES;  // 32 KiB per K block
-constexpr int B_BLOCK = BN * KB_BYTES;  // 16 KiB per stage
+constexpr int B_BLOCK = BN * KB_BYTES;  // 32 KiB per stage
 constexpr int NUM_EPI_WARPS = 8;
 constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;  // 320
-constexpr int MAX_KBLOCKS = 4;                        // dim <= 512
+constexpr int MAX_KBLOCKS = 2;                        // dim <= 256
 constexpr int32_t BIG = 0x3FFFFFFF;                   // sentinel: padding columns, empty slots
 constexpr uint32_t R_OFFSET = 0x02000000u;            // makes r non-negative for packing
 constexpr size_t SMEM_LIMIT = 227 * 1024;
-constexpr size_t NORM_BYTES = (size_t)NUM_EPI_WARPS * 2 * BN * sizeof(int32_t);  // per-warp, 2 tiles
+// per-warp: two tiles of ||x||^2, and a 32 x 32 scratch for the slow path
+constexpr int FIFO_SLOTS = 32;  // deferred-insertion FIFO entries per thread
+constexpr size_t NORM_BYTES =
+    (size_t)NUM_EPI_WARPS * (2 * BN * sizeof(int32_t) + FIFO_SLOTS * 32 * sizeof(uint2));
+constexpr int MAX_SEEDS = 8;  // finished earlier splits merged into a fresh list
 
 struct Params {
   const int32_t* norms;    // ||x||^2 per rank, BIG for padding ranks
   int32_t* bound;          // [nq_pad] shared pruning bound on r per query
+  uint32_t* done_count;    // [nqt] finished splits per query tile
+  uint32_t* done_list;     // [nqt][nsplit] finished split ids in finishing order (~0u = not yet)
   uint64_t* out_part;      // [nq_pad][nsplit][KT] packed (r+R_OFFSET)<<32 | rank
   uint32_t* status;        // device error word
   uint32_t nq;
@@ -80,6 +92,7 @@ __host__ __device__ inline size_t smem_bytes(uint32_t kblocks, uint32_t stages) 
   return off + 1024;  // alignment slack
 }
 
+// Stages in the ring: as many as fit, at most 8, at least two tiles' worth.
 __host__ inline uint32_t pick_stages(uint32_t kblocks) {
   size_t fixed = (size_t)kblocks * A_BLOCK + NORM_BYTES + 1024 + 256;
   uint32_t s = (uint32_t)((SMEM_LIMIT - fixed) / (B_BLOCK + 16));
@@ -114,6 +127,43 @@ __device__ __forceinline__ int32_t load_bound(const int32_t* p) {
   asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ uint32_t load_acquire(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void store_release(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Seed a fresh list with the final lists of up to MAX_SEEDS finished splits
+// of the same query tile that cover SMALLER ranks than this split. Their
+// entries are real candidates, so the list's k-th value is at once a valid
+// and tight admission bound. Exactness is kept: every seeded rank is below
+// every rank this split scans, so a scanned column that ties a seeded value
+// still loses under the strict '<'; and the seeded entries also remain in
+// their own split's list, so the merge (which drops duplicates) sees them.
+template <int KT>
+__device__ __forceinline__ void seed_from_finished(const Params& p, uint32_t qtile, uint32_t split,
+                                                   uint32_t q, int32_t (&lr)[KT], uint32_t (&lk)[KT]) {
+  const uint32_t cnt = min(load_acquire(p.done_count + qtile), p.nsplit);
+  int used = 0;
+  for (uint32_t i = cnt; i > 0 && used < MAX_SEEDS; --i) {
+    const uint32_t s2 = load_acquire(p.done_list + (size_t)qtile * p.nsplit + (i - 1));
+    if (s2 >= split) continue;  // not yet published, or a later split
+    ++used;
+    const unsigned long long* src =
+        reinterpret_cast<const unsigned long long*>(p.out_part + ((size_t)q * p.nsplit + s2) * KT);
+    uint64_t keys[KT];
+#pragma unroll
+    for (int j = 0; j < KT; ++j) keys[j] = __ldcg(src + j);  // all loads in flight at once
+#pragma unroll
+    for (int j = 0; j < KT; ++j) {
+      const int32_t r = static_cast<int32_t>(static_cast<uint32_t>(keys[j] >> 32) - R_OFFSET);
+      if (r < lr[KT - 1]) insert_sorted<KT>(lr, lk, r, static_cast<uint32_t>(keys[j]));
+    }
+  }
+}
 
 // r = ||x||^2 - 2 q.x for one 32-column chunk; returns the chunk minimum
 // (tree reduction: depth 5 instead of a 31-long dependency chain).
@@ -136,25 +186,45 @@ __device__ __forceinline__ int32_t chunk_r(const uint32_t (&v)[32], const int32_
   return min(min(m[0], m[2]), min(m[1], m[3]));
 }
 
-// Slow path of one chunk, entered by the whole warp when some lane has a
-// candidate: build each lane's candidate mask, iterate the union of the masks
-// warp-uniformly, re-read that column from TMEM, insert where admitted.
+// Minimum of r over one 32-column chunk without keeping r (fast path).
+__device__ __forceinline__ int32_t chunk_min(const uint32_t (&v)[32], const int32_t* nrm) {
+  int32_t r[32];
+  return chunk_r(v, nrm, r);
+}
+
+// Deferred insertion. A flagged chunk's admitted (r, rank) pairs are pushed
+// into the thread's FIFO in shared memory ([slot][lane], conflict-free) while
+// the accumulator is held; the FIFO is drained into the register list after
+// the accumulator is released, so insertions overlap the next tile's MMAs
+// instead of stalling them. FIFO order is ascending rank order, so draining
+// with the strict '<' keeps the list exact.
+constexpr int FIFO_CAP = FIFO_SLOTS;  // one full chunk always fits after a drain
+
 template <int KT>
-__device__ __forceinline__ void chunk_insert(const int32_t (&r)[32], int32_t (&lr)[KT], uint32_t (&lk)[KT],
-                                             int32_t shared_bound, uint32_t taddr_chunk,
-                                             const int32_t* nrm, uint32_t rank0) {
-  const int32_t thr = min(lr[KT - 1], shared_bound + 1);
+__device__ __forceinline__ void fifo_drain(const uint2* fifo, uint32_t& cnt, uint32_t lane, int32_t (&lr)[KT],
+                                           uint32_t (&lk)[KT], int32_t shared_bound) {
+  for (uint32_t i = 0; i < cnt; ++i) {
+    const uint2 e = fifo[i * 32 + lane];
+    const int32_t r = static_cast<int32_t>(e.x);
+    if (r < min(lr[KT - 1], shared_bound + 1)) insert_sorted<KT>(lr, lk, r, e.y);
+  }
+  cnt = 0;
+}
+
+template <int KT>
+__device__ __forceinline__ void fifo_push_chunk(const int32_t (&r)[32], int32_t thr, uint32_t rank0, uint2* fifo,
+                                                uint32_t& cnt, uint32_t lane, int32_t (&lr)[KT],
+                                                uint32_t (&lk)[KT], int32_t shared_bound) {
   uint32_t mask = 0;
 #pragma unroll
   for (int j = 0; j < 32; ++j) mask |= (r[j] < thr ? 1u : 0u) << j;
-  uint32_t umask = __reduce_or_sync(0xFFFFFFFFu, mask);
-  while (umask) {
-    const int j = __ffs(umask) - 1;
-    umask &= umask - 1;
-    const uint32_t vj = sm100::tmem_ld_32x32b_x1(taddr_chunk + j);
-    sm100::tmem_ld_wait();
-    const int32_t rj = nrm[j] - 2 * static_cast<int32_t>(vj);
-    if (rj < min(lr[KT - 1], shared_bound + 1)) insert_sorted<KT>(lr, lk, rj, rank0 + j);
+  if (cnt + __popc(mask) > FIFO_CAP) fifo_drain<KT>(fifo, cnt, lane, lr, lk, shared_bound);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (mask & (1u << j)) {
+      fifo[cnt * 32 + lane] = make_uint2(static_cast<uint32_t>(r[j]), rank0 + j);
+      ++cnt;
+    }
   }
 }
 
@@ -170,11 +240,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   unsigned char* sA = smem;
   unsigned char* sB = smem + (size_t)kblocks * A_BLOCK;
   int32_t* sNorm = reinterpret_cast<int32_t*>(sB + (size_t)stages * B_BLOCK);  // [warp][2][BN]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sNorm + NUM_EPI_WARPS * 2 * BN);
+  uint2* sFifo = reinterpret_cast<uint2*>(sNorm + NUM_EPI_WARPS * 2 * BN);    // [warp][slot][lane]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sFifo + NUM_EPI_WARPS * FIFO_SLOTS * 32);
   uint64_t* full = bars;
   uint64_t* empty = bars + stages;
-  uint64_t* acc_full = bars + 2 * stages;
-  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* acc_full = bars + 2 * stages;  // [2]: one per query half
+  uint64_t* acc_empty = acc_full + 2;      // [2]
   uint64_t* a_full = acc_empty + 2;
   uint64_t* mma_done = a_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
@@ -196,9 +267,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], NUM_EPI_WARPS * 32);
+    for (int m = 0; m < 2; ++m) {
+      mbar_init(&acc_full[m], 1);
+      mbar_init(&acc_empty[m], 4 * 32);  // the four epilogue warps of that half
     }
     mbar_init(a_full, 1);
     mbar_init(mma_done, 1);
@@ -211,67 +282,77 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // The producer and MMA roles run as whole, converged warps (every lane
+  // waits, lane 0 issues).
   if (warp == 0) {
+    // ---------------- producer ----------------
     if (lane == 0) {
-      // ---------------- producer ----------------
       mbar_arrive_expect_tx(a_full, kblocks * A_BLOCK);
       for (uint32_t kb = 0; kb < kblocks; ++kb)
         tma_load_2d(sA + (size_t)kb * A_BLOCK, &tmap_q, a_full, kb * KB_BYTES, qtile * BM);
-      uint32_t it = 0;
-      bool ok = true;
-      for (uint32_t t = 0; t < ntile_local && ok; ++t) {
-        for (uint32_t kb = 0; kb < kblocks; ++kb, ++it) {
-          uint32_t s = it % stages, ph = (it / stages) & 1;
-          if (!mbar_wait(&empty[s], ph ^ 1, p.wait_ns) || failed) {
-            record_failure(p.status, DEV_TIMEOUT_EMPTY);
-            failed = 1;
-            ok = false;
-            break;
-          }
+    }
+    __syncwarp();
+    uint32_t it = 0;
+    bool ok = true;
+    for (uint32_t t = 0; t < ntile_local && ok; ++t) {
+      for (uint32_t kb = 0; kb < kblocks; ++kb, ++it) {
+        const uint32_t s = it % stages, ph = (it / stages) & 1;
+        const bool fl = failed;
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&empty[s], ph ^ 1, p.wait_ns) && !fl)) {
+          if (lane == 0) record_failure(p.status, DEV_TIMEOUT_EMPTY);
+          failed = 1;
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
           mbar_arrive_expect_tx(&full[s], B_BLOCK);
           tma_load_2d(sB + (size_t)s * B_BLOCK, &tmap_x, &full[s], kb * KB_BYTES, (t_begin + t) * BN);
         }
+        __syncwarp();
       }
-      // Drain: every copy this thread issued has landed before the CTA exits.
-      uint32_t first = it > stages ? it - stages : 0;
-      for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % stages], (j / stages) & 1, p.wait_ns);
-      mbar_wait(a_full, 0, p.wait_ns);
     }
+    // Drain: every copy this warp issued has landed before the CTA exits.
+    const uint32_t first = it > stages ? it - stages : 0;
+    for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % stages], (j / stages) & 1, p.wait_ns);
+    mbar_wait(a_full, 0, p.wait_ns);
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer ----------------
-      const uint32_t idesc = idesc_u8_s32(UM, BN);
-      bool ok = mbar_wait(a_full, 0, p.wait_ns);
-      if (!ok) {
-        record_failure(p.status, DEV_TIMEOUT_FULL);
-        failed = 1;
-      }
-      tc_fence_after();
-      const uint32_t a_addr = smem_u32(sA), b_addr = smem_u32(sB);
-      uint32_t it = 0;
-      for (uint32_t t = 0; t < ntile_local && ok; ++t) {
-        uint32_t buf = t & 1, use = t >> 1;
-        if (!mbar_wait(&acc_empty[buf], (use & 1) ^ 1, p.wait_ns) || failed) {
-          record_failure(p.status, DEV_TIMEOUT_ACC);
+    // ---------------- MMA issuer ----------------
+    const uint32_t idesc = idesc_u8_s32(UM, BN);
+    bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(a_full, 0, p.wait_ns));
+    if (!ok) {
+      if (lane == 0) record_failure(p.status, DEV_TIMEOUT_FULL);
+      failed = 1;
+    }
+    tc_fence_after();
+    const uint32_t a_addr = smem_u32(sA), b_addr = smem_u32(sB);
+    for (uint32_t t = 0; t < ntile_local && ok; ++t) {
+      const uint32_t it0 = t * kblocks;
+      for (uint32_t m = 0; m < 2 && ok; ++m) {
+        bool fl = failed;
+        // this half's accumulator was drained by its epilogue warps (tile t-1)
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&acc_empty[m], (t & 1) ^ 1, p.wait_ns) && !fl)) {
+          if (lane == 0) record_failure(p.status, DEV_TIMEOUT_ACC);
           failed = 1;
           ok = false;
           break;
         }
         tc_fence_after();
-        for (uint32_t kb = 0; kb < kblocks; ++kb, ++it) {
-          uint32_t s = it % stages, ph = (it / stages) & 1;
-          if (!mbar_wait(&full[s], ph, p.wait_ns) || failed) {
-            record_failure(p.status, DEV_TIMEOUT_FULL);
-            failed = 1;
-            ok = false;
-            break;
+        for (uint32_t kb = 0; kb < kblocks; ++kb) {
+          const uint32_t it = it0 + kb, s = it % stages, ph = (it / stages) & 1;
+          if (m == 0) {
+            fl = failed;
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&full[s], ph, p.wait_ns) && !fl)) {
+              if (lane == 0) record_failure(p.status, DEV_TIMEOUT_FULL);
+              failed = 1;
+              ok = false;
+              break;
+            }
+            tc_fence_after();
           }
-          tc_fence_after();
-          const uint64_t bdesc = smem_desc_k_sw128(b_addr + s * B_BLOCK);
-#pragma unroll
-          for (uint32_t m = 0; m < 2; ++m) {
+          if (lane == 0) {
+            const uint64_t bdesc = smem_desc_k_sw128(b_addr + s * B_BLOCK);
             const uint64_t adesc = smem_desc_k_sw128(a_addr + kb * A_BLOCK + m * (UM * KB_BYTES));
-            const uint32_t d_tmem = tmem_base + (buf * 2 + m) * BN;
+            const uint32_t d_tmem = tmem_base + m * BN;
 #pragma unroll
             for (uint32_t k = 0; k < KB_BYTES / UMMA_K; ++k) {
               // K advance inside the 128-byte swizzle atom: +32 bytes = +2 in
@@ -279,24 +360,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               mma_i8(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
             }
           }
-          mma_commit(&empty[s]);
+          __syncwarp();
         }
         if (!ok) break;
-        mma_commit(&acc_full[buf]);
+        if (lane == 0) mma_commit(&acc_full[m]);
+        __syncwarp();
       }
-      // All MMAs of this thread complete before TMEM is released.
-      mma_commit(mma_done);
-      mbar_wait(mma_done, 0, p.wait_ns);
+      if (!ok) break;
+      // both halves have consumed the tile: release its stages to the producer
+      if (lane == 0)
+        for (uint32_t kb = 0; kb < kblocks; ++kb) mma_commit(&empty[(it0 + kb) % stages]);
+      __syncwarp();
     }
+    // All MMAs of this warp complete before TMEM is released.
+    if (lane == 0) mma_commit(mma_done);
+    __syncwarp();
+    mbar_wait(mma_done, 0, p.wait_ns);
   } else {
     // ---------------- epilogue: warps 2..9, one thread per query row ----------------
     const uint32_t ew = warp - 2;
     const uint32_t quarter = warp & 3;
-    const uint32_t mtile = ew >> 2;
-    const uint32_t row = mtile * UM + quarter * 32 + lane;
+    const uint32_t half = ew >> 2;
+    const uint32_t row = half * UM + quarter * 32 + lane;
     const uint32_t q = qtile * BM + row;
     int32_t* bound_ptr = p.bound + q;
     int32_t* wnorm = sNorm + ew * 2 * BN;  // this warp's two tile slots
+    uint2* wfifo = sFifo + ew * FIFO_SLOTS * 32;  // this warp's deferred-insertion FIFO
+    uint32_t fifo_cnt = 0;
     int32_t lr[KT];
     uint32_t lk[KT];
 #pragma unroll
@@ -304,20 +394,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       lr[i] = BIG;
       lk[i] = 0xFFFFFFFFu;
     }
+    if (q < p.nq) seed_from_finished<KT>(p, qtile, split, q, lr, lk);
     int32_t shared_bound = load_bound(bound_ptr);  // prune r > shared_bound
     int32_t published = BIG;
     // ||x||^2 of tile t sits in this warp's slot t & 1; tile t+1's is fetched
-    // (4 per lane) while tile t is scanned.
-    int4 next_norm = make_int4(0, 0, 0, 0);
-    if (ntile_local > 0)
-      *reinterpret_cast<int4*>(wnorm + 4 * lane) =
-          __ldg(reinterpret_cast<const int4*>(p.norms + t_begin * BN) + lane);
+    // (8 per lane) while tile t is scanned.
+    int4 nx0 = make_int4(0, 0, 0, 0), nx1 = nx0;
+    if (ntile_local > 0) {
+      const int4* src = reinterpret_cast<const int4*>(p.norms + (size_t)t_begin * BN);
+      reinterpret_cast<int4*>(wnorm)[lane] = __ldg(src + lane);
+      reinterpret_cast<int4*>(wnorm)[32 + lane] = __ldg(src + 32 + lane);
+    }
     __syncwarp();
     for (uint32_t t = 0; t < ntile_local; ++t) {
-      const uint32_t buf = t & 1, use = t >> 1;
-      if (t + 1 < ntile_local)
-        next_norm = __ldg(reinterpret_cast<const int4*>(p.norms + (t_begin + t + 1) * BN) + lane);
-      const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&acc_full[buf], use & 1, p.wait_ns) && !failed);
+      if (t + 1 < ntile_local) {
+        const int4* src = reinterpret_cast<const int4*>(p.norms + (size_t)(t_begin + t + 1) * BN);
+        nx0 = __ldg(src + lane);
+        nx1 = __ldg(src + 32 + lane);
+      }
+      const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&acc_full[half], t & 1, p.wait_ns) && !failed);
       if (!ok) {
         record_failure(p.status, DEV_TIMEOUT_ACC);
         failed = 1;
@@ -325,31 +420,51 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       tc_fence_after();
       const uint32_t rank_base = (t_begin + t) * BN;
-      const uint32_t taddr = tmem_base + ((quarter * 32) << 16) + (buf * 2 + mtile) * BN;
+      const uint32_t taddr = tmem_base + ((quarter * 32) << 16) + half * BN;
       const int32_t* nrm = wnorm + (t & 1) * BN;
+      // Fast path, branch-free over the whole tile: per chunk only the minimum
+      // of r, compared with the admission bound taken at the start of the tile
+      // (the list does not change within a tile: insertions are deferred).
+      const int32_t thr = min(lr[KT - 1], shared_bound + 1);
+      // the other splits' bound is read now and folded in after the tile, so
+      // the load's latency hides behind the scan
+      const int32_t fresh_bound = load_bound(bound_ptr);
       uint32_t va[32], vb[32];
-      int32_t r[32];
+      uint32_t hit = 0;  // bit c: chunk c holds a candidate for this lane
       tmem_ld_32x32b_x32(taddr, va);
       tmem_ld_wait();
-#pragma unroll
+#pragma unroll 1
       for (uint32_t c = 0; c < BN / 32; c += 2) {
         // chunk c from va while chunk c+1 loads into vb, then the reverse
         tmem_ld_32x32b_x32(taddr + (c + 1) * 32, vb);
-        int32_t rmin = chunk_r(va, nrm + c * 32, r);
-        if (__any_sync(0xFFFFFFFFu, rmin < min(lr[KT - 1], shared_bound + 1)))
-          chunk_insert<KT>(r, lr, lk, shared_bound, taddr + c * 32, nrm + c * 32, rank_base + c * 32);
+        hit |= static_cast<uint32_t>(chunk_min(va, nrm + c * 32) < thr) << c;
         tmem_ld_wait();
         if (c + 2 < BN / 32) tmem_ld_32x32b_x32(taddr + (c + 2) * 32, va);
-        rmin = chunk_r(vb, nrm + (c + 1) * 32, r);
-        if (__any_sync(0xFFFFFFFFu, rmin < min(lr[KT - 1], shared_bound + 1)))
-          chunk_insert<KT>(r, lr, lk, shared_bound, taddr + (c + 1) * 32, nrm + (c + 1) * 32,
-                           rank_base + (c + 1) * 32);
+        hit |= static_cast<uint32_t>(chunk_min(vb, nrm + (c + 1) * 32) < thr) << (c + 1);
         tmem_ld_wait();
       }
+      // Flagged chunks (one vote per tile) are re-read from TMEM and their
+      // admitted pairs queued; the accumulator is released right after.
+      uint32_t uhit = __reduce_or_sync(0xFFFFFFFFu, hit);
+      while (uhit) {
+        const uint32_t c = __ffs(uhit) - 1;
+        uhit &= uhit - 1;
+        int32_t r[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, va);
+        tmem_ld_wait();
+        chunk_r(va, nrm + c * 32, r);
+        fifo_push_chunk<KT>(r, thr, rank_base + c * 32, wfifo, fifo_cnt, lane, lr, lk, shared_bound);
+      }
       tc_fence_before();
-      mbar_arrive(&acc_empty[buf]);
+      mbar_arrive(&acc_empty[half]);
       // This warp finished reading slot (t+1)&1 during tile t-1.
-      if (t + 1 < ntile_local) *reinterpret_cast<int4*>(wnorm + ((t + 1) & 1) * BN + 4 * lane) = next_norm;
+      if (t + 1 < ntile_local) {
+        int4* dst = reinterpret_cast<int4*>(wnorm + ((t + 1) & 1) * BN);
+        dst[lane] = nx0;
+        dst[32 + lane] = nx1;
+      }
+      // insertions happen while the tensor core fills the next tile
+      if (fifo_cnt) fifo_drain<KT>(wfifo, fifo_cnt, lane, lr, lk, shared_bound);
       __syncwarp();
       // Share the bound with the other splits of this query tile: the k-th
       // value of this split's list (k <= KT, selected without dynamic indexing).
@@ -360,19 +475,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         published = kth;
         atomicMin(bound_ptr, published);
       }
-      shared_bound = min(shared_bound, load_bound(bound_ptr));
+      shared_bound = min(shared_bound, fresh_bound);
     }
     if (q < p.nq) {
       uint64_t* dst = p.out_part + ((size_t)q * p.nsplit + split) * KT;
 #pragma unroll
       for (int i = 0; i < KT; ++i)
         dst[i] = (static_cast<uint64_t>(static_cast<uint32_t>(lr[i]) + R_OFFSET) << 32) | lk[i];
+      __threadfence();  // the list is visible device-wide before this split is announced
     }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc<512>(tmem_base);
+  if (threadIdx.x == 0 && !failed) {
+    // Announce the finished split so later splits of this query tile can seed from it.
+    __threadfence();
+    const uint32_t slot = atomicAdd(p.done_count + qtile, 1u);
+    if (slot < p.nsplit) store_release(p.done_list + (size_t)qtile * p.nsplit + slot, split);
+  }
 }
 
 }  // namespace flat_tc

@@ -140,6 +140,25 @@ def test_c2_tensor_core_path_bit_exact(c2_small, k):
     _assert_same(got, ref, len(q))
 
 
+def test_c2_many_waves_seeding_and_cross_split_ties():
+    """More CTAs than SMs, so later splits seed from finished ones; duplicated rows
+    placed in many different splits make exact distance ties cross split borders."""
+    db = fixtures.blobs_u8(200_000, 128, 1024, fixtures.C2_CENTRES, fixtures.C2_BASE)
+    q = fixtures.blobs_u8(2600, 128, 1024, fixtures.C2_CENTRES, fixtures.C2_QUERIES)
+    rows = db.copy()
+    src = q[:40]  # the first 40 queries each get 6 exact copies of themselves spread over the store
+    for i in range(40):
+        for c in range(6):
+            rows[(i * 4999 + c * 33_331) % len(rows)] = src[i]
+    from proxima_b200.index import FlatIndex
+    idx = FlatIndex.from_array(VectorSpace(128, Metric.EUCLIDEAN), rows)
+    assert idx.device_path() == 1
+    for k in (4, 10):
+        got = idx.search_prepared_batch(q, k)
+        ref = pxo.flat_search(rows, q, k, pxo.EUCLIDEAN)
+        _assert_same(got, ref, len(q))
+
+
 def test_c2_k100_generic_path_bit_exact(c2_small):
     db, q = c2_small
     from proxima_b200.index import FlatIndex
