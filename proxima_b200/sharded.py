@@ -1,0 +1,81 @@
+"""Row-sharded exact search across GPUs (one process per GPU).
+
+Each rank mirrors a contiguous range of database rows with their global
+VectorIds, searches every query on its shard (top-k per query), exchanges the k
+(id, distance) candidates per query with an allgather and merges them on the
+device with ``pxc_topk_merge``. The only data that crosses NVLink is k
+candidates per query per rank.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import _native as N
+
+
+def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous rows [lo, hi) of rank `rank` out of `world` (sizes differ by at most 1)."""
+    return rank * n // world, (rank + 1) * n // world
+
+
+def exchange_candidates(ids: torch.Tensor, dist_: torch.Tensor, lens: torch.Tensor, group=None):
+    """Allgather the per-rank candidate lists.
+
+    ids [nq, k] int64, dist_ [nq, k] float32, lens [nq] int32 -> tensors of shape
+    [world, nq, k], [world, nq, k], [world, nq] in rank order (NCCL for CUDA
+    tensors, gloo for CPU tensors)."""
+    world = dist.get_world_size(group)
+    out_ids = [torch.empty_like(ids) for _ in range(world)]
+    out_d = [torch.empty_like(dist_) for _ in range(world)]
+    out_l = [torch.empty_like(lens) for _ in range(world)]
+    dist.all_gather(out_ids, ids.contiguous(), group=group)
+    dist.all_gather(out_d, dist_.contiguous(), group=group)
+    dist.all_gather(out_l, lens.contiguous(), group=group)
+    return torch.stack(out_ids), torch.stack(out_d), torch.stack(out_l)
+
+
+class ShardedFlat:
+    """One rank's shard of a flat index plus the cross-rank merge."""
+
+    def __init__(self, ctx, dim: int, metric: int, rows: np.ndarray, first_id: int):
+        self.ctx = ctx
+        self.dim = dim
+        self.lib = N.load()
+        h = N.vp()
+        N.call("pxc_flat_create", ctx.handle, dim, metric, C.byref(h))
+        self.handle = h
+        gids = np.arange(first_id, first_id + rows.shape[0], dtype=np.uint64)
+        N.call("pxc_flat_sync", h, N.ptr(np.ascontiguousarray(rows, dtype=np.float32)), N.ptr(gids),
+               None, 0, rows.shape[0])
+
+    def search(self, q_dev: torch.Tensor, k: int, stream_ptr: int):
+        nq = q_dev.shape[0]
+        dev = q_dev.device
+        ids = torch.empty((nq, k), dtype=torch.int64, device=dev)
+        d = torch.empty((nq, k), dtype=torch.float32, device=dev)
+        lens = torch.empty(nq, dtype=torch.int32, device=dev)
+        N.call("pxc_flat_search_device", self.handle, q_dev.data_ptr(), nq, k, None, ids.data_ptr(),
+               d.data_ptr(), lens.data_ptr(), stream_ptr)
+        return ids, d, lens
+
+    def search_global(self, q_dev: torch.Tensor, k: int, stream_ptr: int, group=None):
+        """Local search, allgather, device merge -> global top-k on every rank."""
+        ids, d, lens = self.search(q_dev, k, stream_ptr)
+        g_ids, g_d, g_l = exchange_candidates(ids, d, lens, group)
+        nq = q_dev.shape[0]
+        world = g_ids.shape[0]
+        m_ids = torch.empty((nq, k), dtype=torch.int64, device=q_dev.device)
+        m_d = torch.empty((nq, k), dtype=torch.float32, device=q_dev.device)
+        m_l = torch.empty(nq, dtype=torch.int32, device=q_dev.device)
+        N.call("pxc_topk_merge", self.ctx.handle, g_ids.data_ptr(), g_d.data_ptr(), g_l.data_ptr(), world, nq,
+               k, k, m_ids.data_ptr(), m_d.data_ptr(), m_l.data_ptr(), stream_ptr)
+        return m_ids, m_d, m_l
+
+    def close(self):
+        if self.handle:
+            self.lib.pxc_flat_destroy(self.handle)
+            self.handle = None
