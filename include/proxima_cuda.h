@@ -137,6 +137,22 @@ int32_t pxc_flat_path(const pxc_flat* h);
  * -1 when not recorded. */
 float pxc_flat_last_scan_ms(pxc_flat* h);
 
+/* Allocation-free variant of pxc_flat_search_device. No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory (a host
+ * runtime that has reserved the device for its own pool, or a serving loop
+ * that cannot afford the device-wide synchronisation of cudaMalloc/cudaFree).
+ * Its scratch is one file-scope device array of about 8.6 MiB, held on every
+ * GPU that loads the library. Limits: nq <= 2048, k <= 16, dim <= 256, a
+ * euclidean store of integers in [0,255] (the tensor-core scan), queries of
+ * integers in [0,255], and a device mirror already built by an earlier
+ * pxc_flat_len or search (PXC_CAPACITY / PXC_CONFIGURATION otherwise). The
+ * first call on a device looks up the array's address; make it before any
+ * stream capture. Calls share the array; within a process they are
+ * serialised and each returns after its work has finished. Device buffers. */
+pxc_status pxc_flat_search_noalloc(pxc_flat* h, const float* d_queries, uint32_t nq, uint32_t k,
+                                   uint64_t* d_out_ids, float* d_out_dist, uint32_t* d_out_len,
+                                   void* stream, pxc_error* err);
+
 /* ---- multi-GPU merge ----
  * After each rank searched its own row shard, an allgather leaves `nparts`
  * candidate lists per query on every rank: part p of query q at

@@ -970,3 +970,153 @@ pxc_status pxc_flat_search(pxc_flat* h, const float* queries, uint32_t nq, uint3
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free flat search (no counterpart in the reference).
+//
+// For callers that cannot allocate device memory: a host runtime that has
+// reserved the whole device for its own pool (cudaMalloc would fail), or a
+// latency-bound serving loop that cannot afford the implicit device-wide
+// synchronisation of cudaMalloc/cudaFree. It runs the tensor-core scan (K1)
+// with every per-call scratch buffer carved out of one file-scope device
+// array, so the call allocates nothing: no cudaMalloc, no cudaFree, no
+// allocating library routine.
+//
+// Limits: at most NOALLOC_MAX_QUERIES queries per call, k <= 16, dim <= 256,
+// an integer euclidean store (the K1 conditions), and a device mirror that is
+// already built (call pxc_flat_len or any search once after pxc_flat_sync;
+// building the mirror allocates). The array costs NOALLOC_BYTES of device
+// memory on every GPU that loads the library, until the process exits.
+//
+// The array is shared by every call and keeps the last call's contents; the
+// parts that must start from a known value are reset by each call. Calls whose
+// GPU work overlaps would race on it: within a process this entry point
+// serialises its calls and returns only after its work has finished.
+//
+// Set-up: the first call on a device looks up the array's device address with
+// cudaGetSymbolAddress (with that device current); make that first call
+// before any stream capture.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr uint32_t NOALLOC_MAX_QUERIES = 2048;
+constexpr uint32_t NOALLOC_MAX_SPLITS = 32;
+constexpr uint32_t NOALLOC_MAX_KT = 16;
+constexpr uint32_t NOALLOC_MAX_DIM = 256;
+constexpr size_t NOALLOC_Q_OFF = 0;
+constexpr size_t NOALLOC_PART_OFF = NOALLOC_Q_OFF + (size_t)NOALLOC_MAX_QUERIES * NOALLOC_MAX_DIM;
+constexpr size_t NOALLOC_NORM_OFF =
+    NOALLOC_PART_OFF + (size_t)NOALLOC_MAX_QUERIES * NOALLOC_MAX_SPLITS * NOALLOC_MAX_KT * sizeof(uint64_t);
+constexpr size_t NOALLOC_BOUND_OFF = NOALLOC_NORM_OFF + (size_t)NOALLOC_MAX_QUERIES * sizeof(int32_t);
+constexpr size_t NOALLOC_DONE_OFF = NOALLOC_BOUND_OFF + (size_t)NOALLOC_MAX_QUERIES * sizeof(int32_t);
+constexpr uint32_t NOALLOC_MAX_QTILES = NOALLOC_MAX_QUERIES / flat_tc::BM;
+constexpr size_t NOALLOC_BAD_OFF =
+    NOALLOC_DONE_OFF + ((size_t)NOALLOC_MAX_QTILES * (1 + NOALLOC_MAX_SPLITS) * sizeof(uint32_t) + 255) / 256 * 256;
+constexpr size_t NOALLOC_BYTES = NOALLOC_BAD_OFF + 256;  // ~8.6 MiB
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_BYTES];
+
+namespace {
+std::mutex g_noalloc_mu;        // serialises calls (they share the array)
+void* g_noalloc_addr[256] = {};  // device address of the array, per device ordinal
+
+unsigned char* noalloc_scratch(int device) {
+  if (device < 0 || device >= 256)
+    throw make_failure(PXC_CONFIGURATION, (uint64_t)device, 0, "device", "device ordinal out of range");
+  if (!g_noalloc_addr[device]) {
+    void* p = nullptr;
+    PXC_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    g_noalloc_addr[device] = p;
+  }
+  return static_cast<unsigned char*>(g_noalloc_addr[device]);
+}
+}  // namespace
+
+extern "C" pxc_status pxc_flat_search_noalloc(pxc_flat* h, const float* d_queries, uint32_t nq, uint32_t k,
+                                              uint64_t* d_out_ids, float* d_out_dist, uint32_t* d_out_len,
+                                              void* stream, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(h != nullptr, "handle", 0, "null flat handle");
+    if (nq > NOALLOC_MAX_QUERIES)
+      throw make_failure(PXC_CAPACITY, NOALLOC_MAX_QUERIES, nq, nullptr,
+                         "allocation-free search: at most %u queries per call", NOALLOC_MAX_QUERIES);
+    PXC_CONFIG(k <= NOALLOC_MAX_KT, "k", k, "allocation-free search supports k <= 16");
+    std::lock_guard<std::mutex> global(g_noalloc_mu);
+    std::lock_guard<std::mutex> lock(h->mu);
+    DeviceGuard g(h->ctx->device);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->ctx->stream;
+    PXC_CONFIG(!h->dirty, "mirror", 0,
+               "the device mirror is not built; call pxc_flat_len or a search once after pxc_flat_sync");
+    unsigned char* base = noalloc_scratch(h->ctx->device);
+    if (nq == 0) return;
+    if (k == 0 || h->nrank == 0) {
+      PXC_CUDA(cudaMemsetAsync(d_out_len, 0, nq * sizeof(uint32_t), s));
+      PXC_CUDA(cudaStreamSynchronize(s));
+      return;
+    }
+    PXC_CONFIG(h->all_u8 && h->metric == PXC_EUCLIDEAN && h->dim <= NOALLOC_MAX_DIM && h->nrank_pad > 0, "store",
+               0, "allocation-free search needs a euclidean store of integers in [0,255] with dim <= 256");
+    uint8_t* q_u8 = base + NOALLOC_Q_OFF;
+    uint64_t* part = reinterpret_cast<uint64_t*>(base + NOALLOC_PART_OFF);
+    int32_t* q_norm = reinterpret_cast<int32_t*>(base + NOALLOC_NORM_OFF);
+    int32_t* bound = reinterpret_cast<int32_t*>(base + NOALLOC_BOUND_OFF);
+    uint32_t* done = reinterpret_cast<uint32_t*>(base + NOALLOC_DONE_OFF);
+    int* q_bad = reinterpret_cast<int*>(base + NOALLOC_BAD_OFF);
+
+    const uint32_t nq_pad = (nq + flat_tc::BM - 1) / flat_tc::BM * flat_tc::BM;
+    PXC_CUDA(cudaMemsetAsync(q_bad, 0, sizeof(int), s));
+    prep_queries_u8_kernel<<<nq_pad, 128, 0, s>>>(d_queries, nq, h->dim, h->dp, q_u8, q_norm, q_bad);
+    PXC_CUDA(cudaGetLastError());
+    PXC_CUDA(cudaMemcpyAsync(h->h_flag, q_bad, sizeof(int), cudaMemcpyDeviceToHost, s));
+    PXC_CUDA(cudaStreamSynchronize(s));
+    PXC_CONFIG(*h->h_flag == 0, "queries", 0,
+               "allocation-free search needs query components that are integers in [0,255]");
+
+    const uint32_t KT = k <= 1 ? 1 : k <= 4 ? 4 : k <= 10 ? 10 : 16;
+    const uint32_t nqt = nq_pad / flat_tc::BM;
+    const uint32_t ntiles = (uint32_t)(h->nrank_pad / flat_tc::BN);
+    const uint32_t nsplit_req = std::min(choose_splits(nqt, ntiles, h->ctx->sm_count, KT), NOALLOC_MAX_SPLITS);
+    const uint32_t tps = (ntiles + nsplit_req - 1) / nsplit_req;
+    const uint32_t nsplit = (ntiles + tps - 1) / tps;
+    // reset what must start from a known value
+    PXC_CUDA(cudaMemsetAsync(bound, 0x3F, nq_pad * sizeof(int32_t), s));
+    PXC_CUDA(cudaMemsetAsync(done, 0, nqt * sizeof(uint32_t), s));
+    PXC_CUDA(cudaMemsetAsync(done + nqt, 0xFF, (size_t)nqt * nsplit * sizeof(uint32_t), s));
+    flat_tc::Params p;
+    p.norms = h->op_norm.p;
+    p.bound = bound;
+    p.done_count = done;
+    p.done_list = done + nqt;
+    p.out_part = part;
+    p.status = h->ctx->d_status;
+    p.nq = nq;
+    p.k = k;
+    p.kblocks = h->dp / flat_tc::KB_BYTES;
+    p.ntiles = ntiles;
+    p.tiles_per_split = tps;
+    p.nsplit = nsplit;
+    p.stages = flat_tc::pick_stages(p.kblocks);
+    p.wait_ns = (uint64_t)h->ctx->wait_ms * 1000000ull;
+    CUtensorMap tmap_q;
+    make_tmap_u8_2d(&tmap_q, q_u8, h->dp, nq_pad, flat_tc::KB_BYTES, flat_tc::BM);
+    const size_t smem = flat_tc::smem_bytes(p.kblocks, p.stages);
+    const dim3 grid(nqt, nsplit);
+    switch (KT) {
+      case 1: launch_tc<1>(tmap_q, h->tmap_x, p, grid, smem, s); break;
+      case 4: launch_tc<4>(tmap_q, h->tmap_x, p, grid, smem, s); break;
+      case 10: launch_tc<10>(tmap_q, h->tmap_x, p, grid, smem, s); break;
+      default: launch_tc<16>(tmap_q, h->tmap_x, p, grid, smem, s); break;
+    }
+    PXC_CUDA(cudaGetLastError());
+    uint32_t cap = 32;
+    while (cap < nsplit * KT) cap <<= 1;
+    const size_t msmem = cap * sizeof(uint64_t);
+    if (msmem > 48 * 1024)
+      PXC_CUDA(cudaFuncSetAttribute(merge_u8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msmem));
+    merge_u8_kernel<<<nq, 256, msmem, s>>>(part, nsplit, KT, cap, k, q_norm, h->rank_id.p, (uint32_t)h->nrank,
+                                           d_out_ids, d_out_dist, d_out_len);
+    PXC_CUDA(cudaGetLastError());
+    h->ctx->launches += 3;
+    check_device_status(h->ctx, s, "allocation-free flat search");  // synchronises the stream
+  });
+}
