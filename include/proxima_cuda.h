@@ -164,6 +164,39 @@ pxc_status pxc_topk_merge(pxc_ctx* ctx, const uint64_t* d_ids, const float* d_di
                           uint32_t k, uint64_t* d_out_ids, float* d_out_dist,
                           uint32_t* d_out_len, void* stream, pxc_error* err);
 
+/* ---- k-means ----
+ * Replaces proxima_quantize::kmeans (crates/proxima-quantize/src/kmeans.rs:59-143),
+ * which ProductQuantizer::train (product.rs:247-274) and IvfPqIndex::train
+ * (crates/proxima-index/src/ivfpq.rs:771-777) call. Same algorithm, same
+ * results: k is clamped to max(min(k, n), 1); Lloyd iterations with argmin
+ * ties to the lower centroid index, f64 sums in point order, empty clusters
+ * re-seeded at the farthest point, early stop when no assignment changes
+ * (the stopping pass is counted). */
+typedef struct pxc_kmeans_info {
+  uint32_t k;          /* centroids produced (the clamp above) */
+  uint32_t iterations; /* Clustering::iterations */
+  double inertia;      /* Clustering::inertia (the last assignment pass) */
+  uint32_t path;       /* 0: exact CUDA-core assignment; 1: tensor-core screening + exact re-scoring */
+  uint32_t reseeded;   /* empty clusters re-seeded */
+  uint64_t rescanned;  /* point assignments settled by a full exact scan */
+} pxc_kmeans_info;
+
+/* points: n x dim f32 row-major (HOST). init: NULL for the reference's
+ * k-means++ seeding from ChaCha8Rng::seed_from_u64(seed) (kmeans.rs:146-194),
+ * or k_eff x dim initial centroids (an added option: the reference always
+ * seeds with k-means++). out_centroids: room for k_eff x dim; out_assign
+ * (nullable): n cluster indices. info (nullable). dim <= 512; points must be
+ * finite (PXC_NON_FINITE, a = flat element index). */
+pxc_status pxc_kmeans(pxc_ctx* ctx, const float* points, uint64_t n, uint32_t dim, uint32_t k,
+                      uint32_t max_iterations, const float* init, uint64_t seed,
+                      float* out_centroids, uint32_t* out_assign, pxc_kmeans_info* info,
+                      pxc_error* err);
+/* The same with DEVICE buffers on `stream` (NULL: the context stream). */
+pxc_status pxc_kmeans_device(pxc_ctx* ctx, const float* d_points, uint64_t n, uint32_t dim,
+                             uint32_t k, uint32_t max_iterations, const float* d_init,
+                             uint64_t seed, float* d_out_centroids, uint32_t* d_out_assign,
+                             pxc_kmeans_info* info, void* stream, pxc_error* err);
+
 #ifdef __cplusplus
 }
 #endif

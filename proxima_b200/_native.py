@@ -33,6 +33,17 @@ class PxcError(C.Structure):
     ]
 
 
+class PxcKmeansInfo(C.Structure):
+    _fields_ = [
+        ("k", C.c_uint32),
+        ("iterations", C.c_uint32),
+        ("inertia", C.c_double),
+        ("path", C.c_uint32),
+        ("reseeded", C.c_uint32),
+        ("rescanned", C.c_uint64),
+    ]
+
+
 # name -> (restype, argtypes); every symbol include/proxima_cuda.h declares.
 SIGNATURES: dict[str, tuple] = {
     "pxc_abi_version": (C.c_uint32, []),
@@ -55,6 +66,11 @@ SIGNATURES: dict[str, tuple] = {
     "pxc_ctx_set_profiling": (C.c_int32, [vp, C.c_int32, C.POINTER(PxcError)]),
     "pxc_topk_merge": (C.c_int32, [vp, vp, vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
                                    vp, vp, vp, vp, C.POINTER(PxcError)]),
+    "pxc_kmeans": (C.c_int32, [vp, vp, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, vp, C.c_uint64,
+                               vp, vp, C.POINTER(PxcKmeansInfo), C.POINTER(PxcError)]),
+    "pxc_kmeans_device": (C.c_int32, [vp, vp, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, vp,
+                                      C.c_uint64, vp, vp, C.POINTER(PxcKmeansInfo), vp,
+                                      C.POINTER(PxcError)]),
 }
 
 _lib = None

@@ -30,8 +30,9 @@ NVCC_FLAGS = [
     "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
     f"-I{INCLUDE}", f"-I{CSRC}",
 ]
-CUDA_SOURCES = ["ctx.cu", "flat.cu"]
-HEADERS = ["common.cuh", "sm100.cuh", "flat_tc.cuh", "topk.cuh", "tmap.cuh"]
+CUDA_SOURCES = ["ctx.cu", "flat.cu", "kmeans.cu"]
+HEADERS = ["common.cuh", "sm100.cuh", "flat_tc.cuh", "topk.cuh", "tmap.cuh", "kmeans_tc.cuh",
+           "seqsum.cuh", "rng.h"]
 CXX = os.environ.get("CXX", shutil.which("g++") or "g++")
 
 

@@ -87,3 +87,28 @@ def c2_database(n: int = 1_000_000, dim: int = 128) -> np.ndarray:
 
 def c2_queries(nq: int = 10_000, dim: int = 128) -> np.ndarray:
     return blobs_u8(nq, dim, 1024, C2_CENTRES, C2_QUERIES, 20.0)
+
+
+C3_INIT = 0xC3C30003
+
+
+def c3_points(n: int = 1_000_000, dim: int = 96, nblobs: int = 4096) -> np.ndarray:
+    """Config C3: normalise(centre + N(0, 0.05^2)) around 4,096 unit-sphere centres."""
+    return sphere_blobs(n, dim, nblobs, C3_CENTRES, C3_POINTS, 0.05)
+
+
+def sample_rows(n: int, k: int, seed: int) -> np.ndarray:
+    """k distinct row indices of [0, n): the k smallest splitmix64(seed, i) keys
+    (ties by index), in ascending key order. The seeded random-sample init of C3."""
+    i = np.arange(n, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        z = (np.uint64(seed) + (i + np.uint64(1)) * np.uint64(0x9E3779B97F4A7C15))
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        z = z ^ (z >> np.uint64(31))
+    order = np.lexsort((i, z))
+    return order[:k].astype(np.int64)
+
+
+def c3_init(points: np.ndarray, k: int = 4096, seed: int = C3_INIT) -> np.ndarray:
+    return np.ascontiguousarray(points[sample_rows(len(points), k, seed)])
