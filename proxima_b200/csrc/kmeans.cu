@@ -41,7 +41,8 @@ namespace km {
 constexpr uint32_t INVALID = 0xFFFFFFFFu;
 constexpr int TC = 64;  // centroids per shared-memory tile (tiled exact kernel)
 constexpr uint32_t MAX_DIM = 512;
-constexpr uint32_t SEEDS = 512;              // best-bounded points scanned first when re-seeding
+constexpr uint32_t SEEDS = 32;  // about this many best-bounded points are scanned first when re-seeding
+constexpr uint32_t SCREEN_FALLBACK = 16384;  // more candidates than this: tighten the bounds by screening
 
 // squared (kmeans.rs:234-241): sequential, no fused multiply-add.
 __device__ __forceinline__ float seq_l2(const float* __restrict__ a, const float* __restrict__ b, uint32_t d) {
@@ -55,22 +56,32 @@ __device__ __forceinline__ float seq_l2(const float* __restrict__ a, const float
 }
 
 // Each lane gets seq_l2(A row ia, B row ib): the warp stages its 32 row pairs
-// through shared memory 32 dimensions at a time with coalesced loads, and each
+// through shared memory 32 dimensions at a time with coalesced 16-byte loads
+// (row pitches are multiples of 4 floats, bases 16-byte aligned), and each
 // lane continues its own sequential sum over the staged chunk.
 // sa, sb: 32 x 33 floats each, private to the warp.
 __device__ __forceinline__ float warp_rows_l2(const float* __restrict__ A, uint32_t lda, uint64_t ia,
                                               const float* __restrict__ B, uint32_t ldb, uint64_t ib, uint32_t d,
                                               float* sa, float* sb) {
   const uint32_t lane = threadIdx.x & 31;
+  const uint32_t part = lane & 7;  // which 4 dimensions of the 32-wide chunk
   float s = 0.0f;
   for (uint32_t c0 = 0; c0 < d; c0 += 32) {
-    const bool on = c0 + lane < d;
-#pragma unroll 8
-    for (int r = 0; r < 32; ++r) {
-      const uint64_t ra = __shfl_sync(0xFFFFFFFFu, ia, r);
-      const uint64_t rb = __shfl_sync(0xFFFFFFFFu, ib, r);
-      sa[r * 33 + lane] = on ? __ldg(A + ra * lda + c0 + lane) : 0.0f;
-      sb[r * 33 + lane] = on ? __ldg(B + rb * ldb + c0 + lane) : 0.0f;
+    const bool on = c0 + part * 4 < d;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int row = q * 4 + (int)(lane >> 3);
+      const uint64_t ra = __shfl_sync(0xFFFFFFFFu, ia, row);
+      const uint64_t rb = __shfl_sync(0xFFFFFFFFu, ib, row);
+      float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f), y = x;
+      if (on) {
+        x = __ldg(reinterpret_cast<const float4*>(A + ra * lda + c0) + part);
+        y = __ldg(reinterpret_cast<const float4*>(B + rb * ldb + c0) + part);
+      }
+      float* pa = sa + row * 33 + part * 4;
+      float* pb = sb + row * 33 + part * 4;
+      pa[0] = x.x, pa[1] = x.y, pa[2] = x.z, pa[3] = x.w;
+      pb[0] = y.x, pb[1] = y.y, pb[2] = y.z, pb[3] = y.w;
     }
     __syncwarp();
     const uint32_t cnt = min(32u, d - c0);
@@ -95,7 +106,8 @@ __global__ void __launch_bounds__(128) assign_exact_kernel(
     const float* __restrict__ P, uint32_t ldp, uint64_t n, const uint32_t* __restrict__ list,
     const uint32_t* __restrict__ list_count, const float* __restrict__ C, uint32_t ldc, uint32_t k, uint32_t d,
     uint32_t csplit, unsigned long long* __restrict__ keys, uint32_t* __restrict__ assign,
-    float* __restrict__ bestd, uint32_t* __restrict__ changed, int mode) {
+    float* __restrict__ bestd, uint32_t* __restrict__ changed, int mode, uint32_t* __restrict__ ver,
+    uint32_t ver_val) {
   extern __shared__ __align__(16) float sm[];
   const uint32_t PB = blockDim.x, PBS = PB + 1;
   float* ps = sm;                                        // [d][PBS]
@@ -153,27 +165,26 @@ __global__ void __launch_bounds__(128) assign_exact_kernel(
     atomicMin(keys + pi, ((unsigned long long)__float_as_uint(best) << 32) | bi);
     return;
   }
-  if (mode == 1) {
-    if (assign[pi] != bi) *changed = 1u;
-    assign[pi] = bi;
-  }
+  if (mode == 1 && assign[pi] != bi) *changed = 1u;
+  if (mode >= 1) assign[pi] = bi;
+  if (ver) ver[pi] = ver_val;
   bestd[pi] = best;
 }
 
 // Resolves the (distance, index) keys of a centroid-split exact scan.
 __global__ void resolve_keys_kernel(const uint32_t* __restrict__ list, const uint32_t* __restrict__ count,
                                     unsigned long long* __restrict__ keys, uint32_t* __restrict__ assign,
-                                    float* __restrict__ bestd, uint32_t* __restrict__ changed, int mode) {
+                                    float* __restrict__ bestd, uint32_t* __restrict__ changed, int mode,
+                                    uint32_t* __restrict__ ver, uint32_t ver_val) {
   const uint32_t nl = *count;
   for (uint32_t j = blockIdx.x * blockDim.x + threadIdx.x; j < nl; j += gridDim.x * blockDim.x) {
     const uint32_t pi = list[j];
     const unsigned long long kk = keys[pi];
     keys[pi] = ~0ull;
     const uint32_t bi = (uint32_t)kk;
-    if (mode == 1) {
-      if (assign[pi] != bi) *changed = 1u;
-      assign[pi] = bi;
-    }
+    if (mode == 1 && assign[pi] != bi) *changed = 1u;
+    if (mode >= 1) assign[pi] = bi;
+    if (ver) ver[pi] = ver_val;
     bestd[pi] = __uint_as_float((uint32_t)(kk >> 32));
   }
 }
@@ -382,26 +393,133 @@ __global__ void copy_row_kernel(const float* __restrict__ P, uint32_t ldp, uint3
   for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) dst[i] = P[idx * ldp + i];
 }
 
-// Sort key for choosing re-seed candidates: the larger of the two bounds.
-__global__ void bound_key_kernel(const float* __restrict__ u_cur, const float* __restrict__ u_next, uint64_t n,
-                                 uint32_t* __restrict__ key) {
-  const uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
-  if (i < n) key[i] = __float_as_uint(fmaxf(u_cur[i], u_next[i]));
+// Re-seeding bounds. Each point keeps ub (an upper bound on its nearest
+// distance in the current centroid set), ubc (the centroid row it was measured
+// against) and ube (the empty cluster being processed when it was measured;
+// rows below that index were then in their updated version). When rows
+// [ube, e) have switched to their updated version since, the bound is
+// re-measured against the row as it now stands (for the point's own cluster
+// that distance, u_next, is precomputed).
+constexpr uint32_t UB_SCREENED = 0xFFFFFFFEu;  // ubc of a bound from a screening pass
+
+__device__ __forceinline__ float ub_refresh(const float* __restrict__ P, uint32_t ldp, uint64_t i, uint32_t d,
+                                            const float* __restrict__ next, uint32_t ldc,
+                                            const uint32_t* __restrict__ assign, const float* __restrict__ u_next,
+                                            const float* __restrict__ u_cur, uint32_t e, float* __restrict__ ub,
+                                            uint32_t* __restrict__ ubc, uint32_t* __restrict__ ube) {
+  const uint32_t c = ubc[i];
+  if (c == UB_SCREENED) {  // a screened bound holds for its own set only
+    if (ube[i] == e) return ub[i];
+    const uint32_t a = assign[i];
+    const float v = a < e ? u_next[i] : u_cur[i];
+    ub[i] = v;
+    ubc[i] = a;
+    ube[i] = e;
+    return v;
+  }
+  if (c < ube[i] || c >= e) return ub[i];
+  const float v = c == assign[i] ? u_next[i] : seq_l2(P + i * ldp, next + (size_t)c * ldc, d);
+  ub[i] = v;
+  ube[i] = e;
+  return v;
 }
 
-// Points that can be the farthest against the set next[0,e) + cur[e,k): the
-// nearest distance of point i is at most its exact distance to its own
-// cluster's centroid in that set (u_next if the cluster is below e, else
-// u_cur). Keeps the points whose bound reaches the best exact distance found
-// among the seeds (key: argmax_list_kernel over the seeds).
-__global__ void bound_filter_kernel(const float* __restrict__ u_cur, const float* __restrict__ u_next,
-                                    const uint32_t* __restrict__ assign, uint64_t n, uint32_t e,
-                                    const unsigned long long* __restrict__ key, uint32_t* list, uint32_t* count) {
-  const float lb = __uint_as_float((uint32_t)(*key >> 32));
+// Refreshes the bounds and histograms them for choosing seeds: the points in
+// the top bins of a 2048-bin histogram of the bounds (bits >> 20 of a
+// non-negative float: exponent and three mantissa bits), about `want` of
+// them, at most `cap`.
+__global__ void ub_hist_kernel(const float* __restrict__ P, uint32_t ldp, uint64_t n, uint32_t d,
+                               const float* __restrict__ next, uint32_t ldc, const uint32_t* __restrict__ assign,
+                               const float* __restrict__ u_next, const float* __restrict__ u_cur, uint32_t e,
+                               float* __restrict__ ub,
+                               uint32_t* __restrict__ ubc, uint32_t* __restrict__ ube, uint32_t* __restrict__ hist) {
+  __shared__ uint32_t h[2048];
+  for (uint32_t b = threadIdx.x; b < 2048; b += blockDim.x) h[b] = 0;
+  __syncthreads();
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
-    const float ub = assign[i] < e ? u_next[i] : u_cur[i];
-    if (ub >= lb) list[atomicAdd(count, 1u)] = (uint32_t)i;
+    const float v = ub_refresh(P, ldp, i, d, next, ldc, assign, u_next, u_cur, e, ub, ubc, ube);
+    atomicAdd(&h[__float_as_uint(v) >> 20], 1u);
   }
+  __syncthreads();
+  for (uint32_t b = threadIdx.x; b < 2048; b += blockDim.x)
+    if (h[b]) atomicAdd(hist + b, h[b]);
+}
+// Second level: the bin (of the first histogram) where the top `want`
+// bounds end is histogrammed again on the next 11 bits.
+__global__ void ub_hist2_kernel(const float* __restrict__ ub, uint64_t n, uint32_t* __restrict__ hist, uint32_t want) {
+  __shared__ uint32_t b1, h[2048];
+  if (threadIdx.x == 0) {
+    uint32_t acc = 0, b = 2048;
+    while (b > 0 && acc < want) acc += hist[--b];
+    b1 = b;
+  }
+  for (uint32_t b = threadIdx.x; b < 2048; b += blockDim.x) h[b] = 0;
+  __syncthreads();
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t bits = __float_as_uint(ub[i]);
+    if ((bits >> 20) == b1) atomicAdd(&h[(bits >> 9) & 2047u], 1u);
+  }
+  __syncthreads();
+  for (uint32_t b = threadIdx.x; b < 2048; b += blockDim.x)
+    if (h[b]) atomicAdd(hist + 2048 + b, h[b]);
+}
+
+// Gathers the points whose bound reaches the threshold the two histograms
+// give for the top `want` (ties at the threshold included, at most `cap`).
+__global__ void ub_gather_kernel(const float* __restrict__ ub, uint64_t n, const uint32_t* __restrict__ hist,
+                                 uint32_t want, uint32_t cap, uint32_t* __restrict__ list, uint32_t* count) {
+  __shared__ uint32_t tau;
+  if (threadIdx.x == 0) {
+    uint32_t acc = 0, b = 2048;
+    while (b > 0 && acc < want) acc += hist[--b];
+    const uint32_t b1 = b;
+    acc -= hist[b1];  // bounds strictly above bin b1
+    uint32_t b2 = 2048;
+    while (b2 > 0 && acc < want) acc += hist[2048 + --b2];
+    tau = (b1 << 20) | (b2 << 9);
+  }
+  __syncthreads();
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+    if (__float_as_uint(ub[i]) >= tau) {
+      const uint32_t pos = atomicAdd(count, 1u);
+      if (pos < cap) list[pos] = (uint32_t)i;
+    }
+}
+__global__ void clamp_count_kernel(uint32_t* count, uint32_t cap) {
+  if (*count > cap) *count = cap;
+}
+
+// Tightens the bounds with a screening (MIN) pass over the current set: the
+// nearest exact distance is at most (1+gamma)(||p||^2_hi + m + E), m the
+// smallest screened score (see bound_kernel).
+__global__ void ub_screened_kernel(uint64_t n, uint32_t d, const float* __restrict__ pnorm,
+                                   const uint32_t* __restrict__ cmax_bits, const float* __restrict__ amin, uint32_t e,
+                                   float* __restrict__ ub, uint32_t* __restrict__ ubc, uint32_t* __restrict__ ube) {
+  const uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const double u = 0x1p-24, et = 0x1p-8;
+  const double gam = (d + 4) * u * 1.01, rel = (d + 2) * u * 1.01;
+  const double pn_hi = (double)pnorm[i] * (1.0 + rel);
+  const double cm = (double)__uint_as_float(*cmax_bits) * (1.0 + rel);
+  const double pr = sqrt(pn_hi) * (1.0 + 1e-12), cr = sqrt(cm) * (1.0 + 1e-12);
+  const double E = 2.0 * et * pr * cr + 2.0 * (d + 1) * u * cm + 4.0 * u * (cm + 2.0 * pr * cr) + d * 0x1p-75;
+  double U = (1.0 + gam) * fmax(0.0, pn_hi + (double)amin[i] + E);
+  U += U * 0x1p-40 + 1e-37;
+  const float v = __double2float_ru(U);
+  if (v < ub[i]) {
+    ub[i] = v;
+    ubc[i] = UB_SCREENED;
+    ube[i] = e;
+  }
+}
+
+// Points that can still be the farthest: ub >= the best exact distance found
+// among the seeds (key: argmax_list_kernel over the seeds).
+__global__ void ub_filter_kernel(const float* __restrict__ ub, uint64_t n, const unsigned long long* __restrict__ key,
+                                 uint32_t* list, uint32_t* count) {
+  const float lb = __uint_as_float((uint32_t)(*key >> 32));
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+    if (ub[i] >= lb) list[atomicAdd(count, 1u)] = (uint32_t)i;
 }
 
 // K9 (kmeans.rs:156-159, 182-189): nearest_sq against a new centre, strict '<'.
@@ -479,9 +597,9 @@ struct Runner {
   bool trace = false;
   uint64_t launches = 0;
 
-  DBuf<float> cur, next, part, cnorm, pnorm, bestd, u_next, exact, amin, nearest;
+  DBuf<float> cur, next, part, cnorm, pnorm, bestd, u_next, exact, amin, nearest, ub;
   DBuf<float4> bound;
-  DBuf<uint32_t> assign, cnt, cand, rescan, keys_a, keys_b, iota, sorted, off, words;
+  DBuf<uint32_t> assign, cnt, cand, rescan, keys_a, keys_b, iota, sorted, off, words, ubc, ube, hist;
   DBuf<unsigned long long> key, keys;
   DBuf<unsigned char> sort_tmp;
   size_t sort_tmp_bytes = 0;
@@ -532,8 +650,9 @@ struct Runner {
       PXC_CUDA(cudaMemsetAsync(b->p, 0, (size_t)kpad * ldc * 4, s));
     }
     cnorm.reserve(kpad);
-    for (DBuf<float>* b : {&pnorm, &bestd, &u_next, &exact}) b->reserve(n);
-    for (DBuf<uint32_t>* b : {&assign, &rescan, &keys_a, &keys_b, &iota, &sorted}) b->reserve(n);
+    for (DBuf<float>* b : {&pnorm, &bestd, &u_next, &exact, &ub}) b->reserve(n);
+    for (DBuf<uint32_t>* b : {&assign, &rescan, &keys_a, &keys_b, &iota, &sorted, &ubc, &ube}) b->reserve(n);
+    hist.reserve(4096);
     off.reserve((size_t)k + 1);
     words.reserve(8);
     key.reserve(2);
@@ -575,7 +694,7 @@ struct Runner {
   // device at *dcount, `nl` on the host): the tiled kernel over a 2-D grid of
   // point blocks x centroid ranges, so that short lists still fill the GPU.
   void exact_list(const float* C, const uint32_t* list, const uint32_t* dcount, uint32_t nl, uint32_t* asg,
-                  float* bd, int mode) {
+                  float* bd, int mode, uint32_t* ver = nullptr, uint32_t ver_val = 0) {
     if (nl == 0) return;
     const uint32_t pb = exact_block();
     const uint32_t gx = blocks(nl, pb);
@@ -586,13 +705,13 @@ struct Runner {
     const uint32_t gy = (k + csplit - 1) / csplit;
     if (gy == 1) {
       assign_exact_kernel<<<dim3(gx, 1), pb, exact_smem(pb), s>>>(P, ldp, n, list, dcount, C, ldc, k, d, csplit,
-                                                                 nullptr, asg, bd, words.p + 0, mode);
+                                                                 nullptr, asg, bd, words.p + 0, mode, ver, ver_val);
       ++launches;
     } else {
       assign_exact_kernel<<<dim3(gx, gy), pb, exact_smem(pb), s>>>(P, ldp, n, list, dcount, C, ldc, k, d, csplit,
-                                                                  keys.p, asg, bd, words.p + 0, mode);
+                                                                  keys.p, asg, bd, words.p + 0, mode, nullptr, 0);
       resolve_keys_kernel<<<std::min<uint32_t>(blocks(nl, 256), ctx->sm_count * 8), 256, 0, s>>>(
-          list, dcount, keys.p, asg, bd, words.p + 0, mode);
+          list, dcount, keys.p, asg, bd, words.p + 0, mode, ver, ver_val);
       launches += 2;
     }
     PXC_CUDA(cudaGetLastError());
@@ -604,23 +723,10 @@ struct Runner {
     return h_words[i];
   }
 
-  // Assignment pass against centroids `C` (k rows): writes assign (+ changed
-  // in words[0]) and bestd. `prior`: the current assignment's exact distances
-  // bound the winners (not on the first pass).
-  void nearest_pass(const float* C, bool prior, uint64_t* rescanned) {
-    PXC_CUDA(cudaMemsetAsync(words.p, 0, 8 * sizeof(uint32_t), s));
-    if (!tensor) {
-      const uint32_t pb = exact_block();
-      assign_exact_kernel<<<blocks(n, pb), pb, exact_smem(pb), s>>>(P, ldp, n, nullptr, nullptr, C, ldc, k, d, k,
-                                                                   nullptr, assign.p, bestd.p, words.p + 0, 1);
-      ++launches;
-      PXC_CUDA(cudaGetLastError());
-      return;
-    }
-    const uint64_t kpad = (uint64_t)ntiles * km_tc::BN;
-    sqnorm_kernel<<<blocks(kpad * 32, 256), 256, 0, s>>>(C, ldc, k, d, kpad, cnorm.p, words.p + 4);
-    CUtensorMap tmap_c;
-    make_tmap_f32_2d(&tmap_c, C, d, ldc, k, km_tc::KB_FLOATS, km_tc::BN);
+  // Screening-kernel parameters for centroid set C (norms already in cnorm,
+  // the largest in words[4]).
+  km_tc::Params screen_params(const float* C, CUtensorMap* tmap_c) {
+    make_tmap_f32_2d(tmap_c, C, d, ldc, k, km_tc::KB_FLOATS, km_tc::BN);
     km_tc::Params prm{};
     prm.cnorm = cnorm.p;
     prm.bound = bound.p;
@@ -634,6 +740,37 @@ struct Runner {
     prm.ntiles = ntiles;
     prm.stages = stages;
     prm.wait_ns = (uint64_t)ctx->wait_ms * 1000000ull;
+    return prm;
+  }
+
+  // MIN screening pass against C: amin = smallest screened score per point.
+  void screen(const float* C, bool) {
+    CUtensorMap tmap_c;
+    const km_tc::Params prm = screen_params(C, &tmap_c);
+    km_tc::screen_kernel<true><<<blocks(n, km_tc::BM), km_tc::NUM_THREADS, km_tc::smem_bytes(kblocks, stages), s>>>(
+        tmap_p, tmap_c, prm);
+    ++launches;
+    PXC_CUDA(cudaGetLastError());
+  }
+
+  // Assignment pass against centroids `C` (k rows): writes assign (+ changed
+  // in words[0]) and bestd. `prior`: the current assignment's exact distances
+  // bound the winners (not on the first pass).
+  void nearest_pass(const float* C, bool prior, uint64_t* rescanned) {
+    PXC_CUDA(cudaMemsetAsync(words.p, 0, 8 * sizeof(uint32_t), s));
+    if (!tensor) {
+      const uint32_t pb = exact_block();
+      assign_exact_kernel<<<blocks(n, pb), pb, exact_smem(pb), s>>>(P, ldp, n, nullptr, nullptr, C, ldc, k, d, k,
+                                                                   nullptr, assign.p, bestd.p, words.p + 0, 1,
+                                                                   nullptr, 0);
+      ++launches;
+      PXC_CUDA(cudaGetLastError());
+      return;
+    }
+    const uint64_t kpad = (uint64_t)ntiles * km_tc::BN;
+    sqnorm_kernel<<<blocks(kpad * 32, 256), 256, 0, s>>>(C, ldc, k, d, kpad, cnorm.p, words.p + 4);
+    CUtensorMap tmap_c;
+    const km_tc::Params prm = screen_params(C, &tmap_c);
     const unsigned grid = blocks(n, km_tc::BM);
     const size_t smem = km_tc::smem_bytes(kblocks, stages);
     mark(0);
@@ -651,8 +788,9 @@ struct Runner {
                                                     words.p + 0, rescan.p, words.p + 1, 1);
     launches += 4;
     PXC_CUDA(cudaGetLastError());
-    check_device_status(ctx, s, "k-means screening");
+    PXC_CUDA(cudaMemcpyAsync(ctx->h_status, ctx->d_status, 2 * sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
     const uint32_t nres = read_word(1);
+    if (ctx->h_status[0]) check_device_status(ctx, s, "k-means screening");
     if (trace) {
       DBuf<uint32_t> hist;
       hist.reserve(10);
@@ -753,42 +891,61 @@ struct Runner {
   // at that moment — [0, e) already updated (in next, earlier re-seeds
   // included) and [e, k) not yet (cur).
   //
-  // Exact and pruned: a point's nearest distance in that set is at most its
-  // exact distance to its own cluster's centroid there — u_next (the new
-  // mean) when the cluster is below e, else u_cur (= bestd, the old one). The
-  // SEEDS points with the largest such bound are scanned exactly first; only
-  // points whose bound reaches the best of those can still be the farthest,
-  // and they are scanned exactly too.
+  // Exact and pruned with the bounds above: the points with the largest
+  // bounds are scanned exactly first; only points whose bound reaches the
+  // best of those can still be the farthest, and they are scanned exactly
+  // too. Scanned points keep their exact distance as a tight bound for the
+  // following empty clusters.
   void reseed_empty(Result& r) {
     std::vector<uint32_t> offs(k + 1);
     PXC_CUDA(cudaMemcpyAsync(offs.data(), off.p, (k + 1) * sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
     pair_l2_kernel<<<blocks(n, 128), 128, 0, s>>>(P, ldp, n, d, next.p, ldc, assign.p, u_next.p);
-    bound_key_kernel<<<blocks(n, 256), 256, 0, s>>>(bestd.p, u_next.p, n, keys_a.p);
-    size_t tb = sort_tmp_bytes;
-    PXC_CUDA(cub::DeviceRadixSort::SortPairsDescending(sort_tmp.p, tb, keys_a.p, keys_b.p, iota.p, sorted.p, (int)n, 0,
-                                                       32, s));
-    launches += 4;
+    // bounds: the exact distance to the old centroid of the point's cluster
+    PXC_CUDA(cudaMemcpyAsync(ub.p, bestd.p, n * 4, cudaMemcpyDeviceToDevice, s));
+    PXC_CUDA(cudaMemcpyAsync(ubc.p, assign.p, n * 4, cudaMemcpyDeviceToDevice, s));
+    PXC_CUDA(cudaMemsetAsync(ube.p, 0, n * 4, s));
+    launches += 1;
     PXC_CUDA(cudaStreamSynchronize(s));
-    const uint32_t nseed = (uint32_t)std::min<uint64_t>(SEEDS, n);
-    h_words[3] = nseed;
-    PXC_CUDA(cudaMemcpyAsync(words.p + 3, h_words + 3, sizeof(uint32_t), cudaMemcpyHostToDevice, s));
+    const uint32_t cap = (uint32_t)std::min<uint64_t>(8 * SEEDS, n);
     for (uint32_t e = 0; e < k; ++e) {
       if (offs[e] != offs[e + 1]) continue;
       if (e) PXC_CUDA(cudaMemcpyAsync(part.p, next.p, (size_t)e * ldc * 4, cudaMemcpyDeviceToDevice, s));
       PXC_CUDA(cudaMemcpyAsync(part.p + (size_t)e * ldc, cur.p + (size_t)e * ldc, (size_t)(k - e) * ldc * 4,
                                cudaMemcpyDeviceToDevice, s));
-      PXC_CUDA(cudaMemsetAsync(key.p, 0, 2 * sizeof(unsigned long long), s));
-      PXC_CUDA(cudaMemsetAsync(words.p + 1, 0, sizeof(uint32_t), s));
-      // seeds: exact nearest distance against the set, best one in key[0]
-      exact_list(part.p, sorted.p, words.p + 3, nseed, nullptr, exact.p, 0);
-      argmax_list_kernel<<<4, 256, 0, s>>>(exact.p, sorted.p, nullptr, nseed, key.p);
-      bound_filter_kernel<<<ctx->sm_count * 4, 256, 0, s>>>(bestd.p, u_next.p, assign.p, n, e, key.p, rescan.p,
-                                                            words.p + 1);
-      launches += 3;
-      const uint32_t nl = read_word(1);
-      if (trace) std::fprintf(stderr, "[pxc kmeans] reseed cluster %u: %u points can be the farthest\n", e, nl);
-      exact_list(part.p, rescan.p, words.p + 1, nl, nullptr, exact.p, 0);
-      argmax_list_kernel<<<ctx->sm_count * 4, 256, 0, s>>>(exact.p, rescan.p, words.p + 1, 0, key.p + 1);
+      // seeds: exact distances for the best-bounded points; the best in key[0];
+      // then every point whose bound reaches it
+      auto seed_and_filter = [&]() -> uint32_t {
+        PXC_CUDA(cudaMemsetAsync(key.p, 0, 2 * sizeof(unsigned long long), s));
+        PXC_CUDA(cudaMemsetAsync(words.p + 1, 0, 3 * sizeof(uint32_t), s));
+        PXC_CUDA(cudaMemsetAsync(hist.p, 0, 4096 * sizeof(uint32_t), s));
+        ub_hist_kernel<<<ctx->sm_count * 2, 512, 0, s>>>(P, ldp, n, d, next.p, ldc, assign.p, u_next.p, bestd.p, e,
+                                                          ub.p, ubc.p, ube.p, hist.p);
+        ub_hist2_kernel<<<ctx->sm_count * 2, 512, 0, s>>>(ub.p, n, hist.p, SEEDS);
+        ub_gather_kernel<<<ctx->sm_count * 4, 256, 0, s>>>(ub.p, n, hist.p, SEEDS, cap, sorted.p, words.p + 3);
+        clamp_count_kernel<<<1, 1, 0, s>>>(words.p + 3, cap);
+        exact_list(part.p, sorted.p, words.p + 3, cap, ubc.p, ub.p, 2, ube.p, e);
+        argmax_list_kernel<<<ctx->sm_count, 256, 0, s>>>(ub.p, sorted.p, words.p + 3, 0, key.p);
+        ub_filter_kernel<<<ctx->sm_count * 4, 256, 0, s>>>(ub.p, n, key.p, rescan.p, words.p + 1);
+        launches += 6;
+        return read_word(1);
+      };
+      uint32_t nl = seed_and_filter();
+      const uint32_t nl_cheap = nl;
+      if (nl > SCREEN_FALLBACK && tensor) {
+        // the cheap bounds are loose here: bound every point by a screening pass
+        const uint64_t kpad = (uint64_t)ntiles * km_tc::BN;
+        PXC_CUDA(cudaMemsetAsync(words.p + 4, 0, sizeof(uint32_t), s));
+        sqnorm_kernel<<<blocks(kpad * 32, 256), 256, 0, s>>>(part.p, ldc, k, d, kpad, cnorm.p, words.p + 4);
+        screen(part.p, true);
+        ub_screened_kernel<<<blocks(n, 256), 256, 0, s>>>(n, d, pnorm.p, words.p + 4, amin.p, e, ub.p, ubc.p, ube.p);
+        launches += 2;
+        nl = seed_and_filter();
+      }
+      if (trace)
+        std::fprintf(stderr, "[pxc kmeans] reseed cluster %u: %u points can be the farthest (%u before screening)\n",
+                     e, nl, nl_cheap);
+      exact_list(part.p, rescan.p, words.p + 1, nl, ubc.p, ub.p, 2, ube.p, e);
+      argmax_list_kernel<<<ctx->sm_count * 4, 256, 0, s>>>(ub.p, rescan.p, words.p + 1, 0, key.p + 1);
       copy_row_kernel<<<1, 128, 0, s>>>(P, ldp, d, key.p + 1, next.p + (size_t)e * ldc);
       launches += 2;
       PXC_CUDA(cudaGetLastError());
