@@ -1,6 +1,7 @@
 """Benchmark of the exact flat search hot path (config C2: 1M x 128 euclidean, 10k queries, k=10).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --workload kmeans [...]   # config C3: k-means 1M x 96, k=4096, 20 iterations
 
 One step = one exact top-k search of all queries over the whole database
 (sharded by rows across N GPUs, one process per GPU under torchrun; local
@@ -44,6 +45,7 @@ def parse():
     p.add_argument("--dim", type=int, default=128)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
+    p.add_argument("--workload", choices=["flat", "kmeans"], default="flat")
     return p.parse_args()
 
 
@@ -161,9 +163,134 @@ def run_reference(args):
             "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
+KM_METRIC = "Lloyd iterations/s: k-means 1M×96 k=4096 (proxima_quantize::kmeans, 20 iterations from a seeded sample)"
+KM_CONFIG = {"workload": "C3 k-means: 1,000,000 x 96 f32 (L2-normalised, 4,096 unit-sphere blobs, sigma 0.05), "
+                         "k=4096, 20 Lloyd iterations from 4,096 seeded sample points",
+             "n": 1_000_000, "dim": 96, "k": 4096, "iterations": 20}
+
+
+def kmeans_cpu_baseline(pts: np.ndarray, k: int, seconds: float) -> dict:
+    """One Lloyd iteration of the oracle port on a point sample, on all host cores, scaled to the full set.
+
+    The sample's own first k points are the initial centroids, so no cluster
+    starts empty and the iteration is the assignment plus the update that
+    dominate the reference's cost at full size."""
+    from oracle import pxo
+
+    threads = os.cpu_count() or 1
+    n = len(pts)
+    ns = 4 * k
+    while True:
+        t0 = time.perf_counter()
+        pxo.kmeans(pts[:ns], k, 1, init=pts[:k], nthreads=threads)
+        el = time.perf_counter() - t0
+        if el > seconds / 3 or ns * 2 > n:
+            break
+        ns *= 2
+    per_iter_full = el * n / ns
+    return {"value": 1.0 / per_iter_full, "unit": "iterations/s", "cores": threads, "kind": "port",
+            "sample": f"one Lloyd iteration (assignment + update) of the C++ oracle on the first {ns:,} points, "
+                      f"the first {k:,} of them as the centroids ({el:.2f} s), scaled linearly to {n:,} points"}
+
+
+def run_kmeans(args):
+    """--workload kmeans: one step = one 20-iteration k-means training of C3 with inputs resident on the GPU."""
+    import torch
+
+    from proxima_b200 import _native as N
+    from proxima_b200 import fixtures
+    from proxima_b200.index import Context
+    from proxima_b200.quantize import kmeans
+
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    n, dim, k, iters = 1_000_000, 96, 4096, 20
+    pts = fixtures.c3_points(n, dim)
+    init = fixtures.c3_init(pts, k)
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        cb = kmeans_cpu_baseline(pts, k, args.cpu_seconds)
+        line = {"metric": KM_METRIC, "value": cb["value"], "unit": "iterations/s", "n_gpus": args.gpus,
+                "steps": 1, "warmup": 0, "ms_per_step": 1000.0 / cb["value"] * iters, "higher_is_better": True,
+                "scaling": "replicas", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": dict(KM_CONFIG, parallelism=f"host threads {cb['cores']}"), "impl": "reference",
+                "cpu_baseline": cb,
+                "e2e": {"value": cb["value"], "unit": "iterations/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ctx = Context(local)
+    lib = N.load()
+    N.call("pxc_ctx_set_profiling", ctx.handle, 1)
+    dp = torch.from_numpy(pts).to(dev)
+    di = torch.from_numpy(init).to(dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(3, args.warmup)):
+        kmeans(dp, dim, k, iters, init=di, context=ctx)
+    torch.cuda.synchronize(dev)
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    sampler = ClockSampler(uuid)
+    sampler.start()
+    launches0 = lib.pxc_ctx_launch_count(ctx.handle)
+    ms, screen_ms, screen_passes, res = [], 0.0, 0, None
+    for _ in range(args.steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        res = kmeans(dp, dim, k, iters, init=di, context=ctx)
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        ms.append(a.elapsed_time(b))
+        screen_ms += res.screen_ms
+        screen_passes += res.screen_passes
+    launches = lib.pxc_ctx_launch_count(ctx.handle) - launches0
+    clocks = sampler.stop()
+    ms_per_step = sum(ms) / len(ms)
+    # e2e: the host entry point, points copied in and centroids + assignments copied out each step
+    e2e_steps = max(2, min(args.steps, 3))
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        kmeans(pts, dim, k, iters, init=init, context=ctx, want_assignment=True)
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    if rank == 0:
+        hbm, bf16, src = peaks()
+        tf32 = bf16 / 2.0  # B200 dense TF32 runs at half its dense BF16 rate
+        flops = 2.0 * n * k * dim
+        per_pass = screen_ms / max(1, screen_passes)
+        achieved = flops / (per_pass / 1e3) / 1e12 if per_pass > 0 else None
+        line = {"metric": KM_METRIC, "value": iters / (ms_per_step / 1e3), "unit": "iterations/s",
+                "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms_per_step,
+                "higher_is_better": True, "scaling": "replicas", "vs_baseline": None, "dtype": "tf32+f32",
+                "data": "synthetic",
+                "config": dict(KM_CONFIG, step="one 20-iteration training from the same seeded init",
+                               l2="inputs (384 MB) larger than L2", iterations_run=res.iterations,
+                               reseeded=res.reseeded, rescanned=res.rescanned,
+                               parallelism="single GPU" if world == 1 else f"{world} independent replicas"),
+                "clocks": clocks, "gpu_launches": int(launches),
+                "e2e": {"value": iters / e2e_s, "unit": "iterations/s", "h2d_bytes_per_step": n * dim * 4 + k * dim * 4,
+                        "d2h_bytes_per_step": k * dim * 4 + n * 4},
+                "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf32, "unit": "TFLOP/s",
+                             "frac": achieved / tf32 if achieved else None, "traffic": None,
+                             "kernel": "km_tc::screen_kernel (K7a, CAND pass)", "kernel_ms": per_pass,
+                             "peak_source": f"dense bf16 {src} / 2 = dense tf32 rate",
+                             "algorithmic_flops_per_launch": flops}}
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = kmeans_cpu_baseline(pts, k, args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    ctx.close()
+
 
 def main():
     args = parse()
+    if args.workload == "kmeans":
+        run_kmeans(args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return

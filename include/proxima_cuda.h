@@ -179,6 +179,8 @@ typedef struct pxc_kmeans_info {
   uint32_t path;       /* 0: exact CUDA-core assignment; 1: tensor-core screening + exact re-scoring */
   uint32_t reseeded;   /* empty clusters re-seeded */
   uint64_t rescanned;  /* point assignments settled by a full exact scan */
+  uint32_t screen_passes; /* tensor-core screening launches (CAND passes) */
+  float screen_ms;     /* their summed device time, when profiling is on (pxc_ctx_set_profiling) */
 } pxc_kmeans_info;
 
 /* points: n x dim f32 row-major (HOST). init: NULL for the reference's
@@ -196,6 +198,43 @@ pxc_status pxc_kmeans_device(pxc_ctx* ctx, const float* d_points, uint64_t n, ui
                              uint32_t k, uint32_t max_iterations, const float* d_init,
                              uint64_t seed, float* d_out_centroids, uint32_t* d_out_assign,
                              pxc_kmeans_info* info, void* stream, pxc_error* err);
+
+/* ---- IvfPqIndex ----
+ * The device side of IvfPqIndex (crates/proxima-index/src/ivfpq.rs): coarse
+ * centroids + product-quantizer codebooks, inverted lists of PQ codes in
+ * ascending slot order, and the full-precision store for reranking.
+ * Euclidean and cosine (the metrics whose scoring search_prepared defines). */
+typedef struct pxc_ivfpq pxc_ivfpq;
+/* nlist coarse centroids, m subspaces of 256 centroids (widths as
+ * ProductQuantizer::train lays them out, product.rs:227-238). dim <= 1024, m <= 64. */
+pxc_status pxc_ivfpq_create(pxc_ctx* ctx, uint32_t dim, int32_t metric, uint32_t nlist, uint32_t m,
+                            pxc_ivfpq** out, pxc_error* err);
+void pxc_ivfpq_destroy(pxc_ivfpq* h);
+/* IvfPqIndex::from_parts (ivfpq.rs:481-508): centroids nlist*dim, codebooks
+ * 256*dim (ProductQuantizer::codebooks layout, subspace-major). HOST buffers. */
+pxc_status pxc_ivfpq_set_parts(pxc_ivfpq* h, const float* centroids, const float* codebooks,
+                               pxc_error* err);
+/* The slot store: `vectors` nslots*dim prepared floats (NULL: no reranking,
+ * the retain_vectors=false case), `ids` the VectorId per slot (NULL: id ==
+ * slot), `live` one byte per slot (NULL: all live). HOST buffers. Clears the lists. */
+pxc_status pxc_ivfpq_set_store(pxc_ivfpq* h, const float* vectors, const uint64_t* ids,
+                               const uint8_t* live, uint64_t nslots, pxc_error* err);
+/* The lists from per-slot assignments (list_of, 0xFFFFFFFF = unassigned)
+ * and codes (nslots*m bytes): IvfPqIndex's list_of / codes. HOST buffers. */
+pxc_status pxc_ivfpq_set_codes(pxc_ivfpq* h, const uint32_t* list_of, const uint8_t* codes,
+                               pxc_error* err);
+/* IvfPqIndex::search_with_nprobe (ivfpq.rs:981-1110) for a batch of prepared
+ * queries: nprobe clamped to [1, nlist] (<= 128), shortlist max(rerank, k)
+ * (<= 1024), bitmap over slots or NULL. HOST buffers. */
+pxc_status pxc_ivfpq_search(pxc_ivfpq* h, const float* queries, uint32_t nq, uint32_t k,
+                            uint32_t nprobe, uint32_t rerank, const uint64_t* bitmap,
+                            uint64_t* out_ids, float* out_dist, uint32_t* out_len, pxc_error* err);
+/* Same with DEVICE buffers on `stream` (NULL: the context stream); returns
+ * once enqueued. */
+pxc_status pxc_ivfpq_search_device(pxc_ivfpq* h, const float* d_queries, uint32_t nq, uint32_t k,
+                                   uint32_t nprobe, uint32_t rerank, const uint64_t* d_bitmap,
+                                   uint64_t* d_out_ids, float* d_out_dist, uint32_t* d_out_len,
+                                   void* stream, pxc_error* err);
 
 #ifdef __cplusplus
 }

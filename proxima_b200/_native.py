@@ -41,6 +41,8 @@ class PxcKmeansInfo(C.Structure):
         ("path", C.c_uint32),
         ("reseeded", C.c_uint32),
         ("rescanned", C.c_uint64),
+        ("screen_passes", C.c_uint32),
+        ("screen_ms", C.c_float),
     ]
 
 
@@ -71,6 +73,16 @@ SIGNATURES: dict[str, tuple] = {
     "pxc_kmeans_device": (C.c_int32, [vp, vp, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, vp,
                                       C.c_uint64, vp, vp, C.POINTER(PxcKmeansInfo), vp,
                                       C.POINTER(PxcError)]),
+    "pxc_ivfpq_create": (C.c_int32, [vp, C.c_uint32, C.c_int32, C.c_uint32, C.c_uint32, C.POINTER(vp),
+                                     C.POINTER(PxcError)]),
+    "pxc_ivfpq_destroy": (None, [vp]),
+    "pxc_ivfpq_set_parts": (C.c_int32, [vp, vp, vp, C.POINTER(PxcError)]),
+    "pxc_ivfpq_set_store": (C.c_int32, [vp, vp, vp, vp, C.c_uint64, C.POINTER(PxcError)]),
+    "pxc_ivfpq_set_codes": (C.c_int32, [vp, vp, vp, C.POINTER(PxcError)]),
+    "pxc_ivfpq_search": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, vp, vp, vp, vp,
+                                     C.POINTER(PxcError)]),
+    "pxc_ivfpq_search_device": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, vp, vp,
+                                            vp, vp, vp, C.POINTER(PxcError)]),
 }
 
 _lib = None

@@ -137,6 +137,9 @@ struct pxc_ctx {
   bool profiling = false;
   unsigned long long launches = 0;  // kernels launched by this library on this context
   std::mutex mu;  // serialises use of the context stream from search entry points
+  // k-means scratch kept between calls (grown on demand, freed with the context)
+  void* kmeans_ws = nullptr;
+  void (*kmeans_ws_free)(void*) = nullptr;
 };
 
 namespace pxc {

@@ -110,6 +110,7 @@ void pxc_ctx_destroy(pxc_ctx* ctx) {
   cudaGetDevice(&prev);
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  if (ctx->kmeans_ws && ctx->kmeans_ws_free) ctx->kmeans_ws_free(ctx->kmeans_ws);
   if (ctx->d_status) cudaFree(ctx->d_status);
   if (ctx->h_status) cudaFreeHost(ctx->h_status);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);

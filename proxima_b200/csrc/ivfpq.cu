@@ -1,0 +1,827 @@
+// ivfpq.cu — IvfPqIndex on the device (crates/proxima-index/src/ivfpq.rs),
+// search equal to the reference's search_prepared (:998-1110) on the same
+// parts: the same probed lists, scores, shortlist and reranked top-k.
+//
+// Device layout (HBM):
+//   centroids   nlist x dim f32 (coarse quantizer)
+//   codebooks   256 x dim f32, subspace-major as ProductQuantizer stores them
+//               (subspace s at 256 * offsets[s], entry j at + j * width[s])
+//   lists       CSR over lists: list_off[nlist+1]; list_slot[] the live slots
+//               of each list in ascending slot order; list_codes[] their PQ
+//               codes copied into list order so a list scan reads one
+//               contiguous run (16 bytes per code at m = 16)
+//   store       vectors (slot-major, prepared), ids, and a rank of every live
+//               slot's VectorId, so (score, rank) orders exactly as the
+//               reference's (total_cmp(score), id)
+//
+// Search (per batch of queries):
+//   K4 coarse   every centroid's squared_euclidean in the reference's 8-lane
+//               order (proxima_core::distance, unrolled), top-nprobe by
+//               (distance, list index): per-thread partial lists over centroid
+//               ranges, then a merge.
+//   K5 scan     one CTA per query: for each probed list, the residual table
+//               (q - c) against every codebook entry (sequential sums, as
+//               ProductQuantizer::distance_table) in shared memory, then the
+//               list's codes scored by table lookups (sequential over
+//               subspaces, as DistanceTable::squared_l2), kept in a
+//               thresholded candidate buffer reduced by a block radix-select;
+//   K6 rerank   the shortlist rescored with space.distance on the stored
+//               vectors, top-k.
+// Cosine uses the query's own table once and 1 - q.c + table.inner_product.
+#include <cub/cub.cuh>
+
+#include <algorithm>
+#include <cmath>
+#include <numeric>
+#include <vector>
+
+#include "common.cuh"
+#include "kmeans_api.h"
+#include "rng.h"
+#include "topk.cuh"
+
+namespace pxc {
+namespace ivf {
+
+constexpr uint32_t UNASSIGNED = 0xFFFFFFFFu;
+constexpr uint32_t MAX_NPROBE = 128;
+constexpr uint32_t MAX_SHORTLIST = 1024;
+constexpr uint32_t MAX_M = 64;
+constexpr uint32_t MAX_DIM = 1024;
+constexpr uint32_t SCAN_THREADS = 256;
+constexpr uint32_t CB = 4096;     // candidate buffer per query
+constexpr uint32_t CHUNK = 1024;  // codes scored between buffer checks
+constexpr uint32_t QB = 64;       // queries per coarse block
+constexpr uint32_t TCC = 32;      // centroids per coarse smem tile
+constexpr uint32_t CSPLIT = 8;    // centroid ranges per query (coarse)
+
+// proxima_core::distance::squared_euclidean: eight lane sums over full
+// chunks of 8, reduced ((l0+l1)+(l2+l3))+((l4+l5)+(l6+l7)), plus a
+// sequential tail. `a` may be in shared memory.
+__device__ __forceinline__ float l2_unrolled(const float* a, const float* __restrict__ b, uint32_t dim) {
+  float acc[8];
+#pragma unroll
+  for (int l = 0; l < 8; ++l) acc[l] = 0.0f;
+  const uint32_t full = dim & ~7u;
+  for (uint32_t i = 0; i < full; i += 8) {
+#pragma unroll
+    for (int l = 0; l < 8; ++l) {
+      const float d = __fsub_rn(a[i + l], __ldg(b + i + l));
+      acc[l] = __fadd_rn(acc[l], __fmul_rn(d, d));
+    }
+  }
+  float tail = 0.0f;
+  for (uint32_t i = full; i < dim; ++i) {
+    const float d = __fsub_rn(a[i], __ldg(b + i));
+    tail = __fadd_rn(tail, __fmul_rn(d, d));
+  }
+  const float x = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
+  const float y = __fadd_rn(__fadd_rn(acc[4], acc[5]), __fadd_rn(acc[6], acc[7]));
+  return __fadd_rn(__fadd_rn(x, y), tail);
+}
+__device__ __forceinline__ float dot_unrolled(const float* a, const float* __restrict__ b, uint32_t dim) {
+  float acc[8];
+#pragma unroll
+  for (int l = 0; l < 8; ++l) acc[l] = 0.0f;
+  const uint32_t full = dim & ~7u;
+  for (uint32_t i = 0; i < full; i += 8) {
+#pragma unroll
+    for (int l = 0; l < 8; ++l) acc[l] = __fadd_rn(acc[l], __fmul_rn(a[i + l], __ldg(b + i + l)));
+  }
+  float tail = 0.0f;
+  for (uint32_t i = full; i < dim; ++i) tail = __fadd_rn(tail, __fmul_rn(a[i], __ldg(b + i)));
+  const float x = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
+  const float y = __fadd_rn(__fadd_rn(acc[4], acc[5]), __fadd_rn(acc[6], acc[7]));
+  return __fadd_rn(__fadd_rn(x, y), tail);
+}
+// space.distance for the metrics IVF-PQ reranks with (space.rs:148-156).
+__device__ __forceinline__ float space_distance(int metric, const float* a, const float* __restrict__ b,
+                                                uint32_t dim) {
+  return metric == PXC_COSINE ? __fsub_rn(1.0f, dot_unrolled(a, b, dim)) : l2_unrolled(a, b, dim);
+}
+
+// ---------------------------------------------------------------------------
+// K4: coarse top-nprobe. Block = QB queries (one thread each, the query
+// transposed into shared memory) x one range of centroids (blockIdx.y); each
+// thread keeps its P best (distance, list) keys sorted in shared memory.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(QB) coarse_partial_kernel(const float* __restrict__ Q, uint32_t nq, uint32_t dim,
+                                                            const float* __restrict__ C, uint32_t nlist,
+                                                            uint32_t crange, uint32_t P,
+                                                            uint64_t* __restrict__ partial) {
+  extern __shared__ __align__(16) unsigned char sm_raw[];
+  uint64_t* best = reinterpret_cast<uint64_t*>(sm_raw);                 // [P][QB]
+  float* qs = reinterpret_cast<float*>(best + (size_t)P * QB);          // [dim][QB+1]
+  float* cs = qs + (((size_t)dim * (QB + 1) + 3) & ~size_t(3));         // [TCC][dim]
+  const uint32_t t = threadIdx.x;
+  const uint32_t q0 = blockIdx.x * QB;
+  const uint32_t qi = q0 + t;
+  for (uint32_t e = t; e < QB * dim; e += QB) {
+    const uint32_t r = e / dim, i = e - r * dim;
+    qs[i * (QB + 1) + r] = q0 + r < nq ? Q[(size_t)(q0 + r) * dim + i] : 0.0f;
+  }
+  for (uint32_t j = 0; j < P; ++j) best[j * QB + t] = ~0ull;
+  uint32_t have = 0;
+  const uint32_t cbeg = blockIdx.y * crange, cend = min(nlist, cbeg + crange);
+  for (uint32_t c0 = cbeg; c0 < cend; c0 += TCC) {
+    const uint32_t cnt = min(TCC, cend - c0);
+    __syncthreads();
+    for (uint32_t e = t; e < TCC * dim; e += QB) {
+      const uint32_t j = e / dim, i = e - j * dim;
+      cs[j * dim + i] = j < cnt ? C[(size_t)(c0 + j) * dim + i] : 0.0f;
+    }
+    __syncthreads();
+    if (qi >= nq) continue;
+    for (uint32_t j = 0; j < cnt; ++j) {
+      const float* c = cs + j * dim;
+      float acc[8];
+#pragma unroll
+      for (int l = 0; l < 8; ++l) acc[l] = 0.0f;
+      const uint32_t full = dim & ~7u;
+      const bool vec4 = (dim & 3) == 0;  // rows of the tile 16-byte aligned
+      for (uint32_t i = 0; i < full; i += 8) {
+        float cv[8];
+        if (vec4) {
+          const float4 c0v = *reinterpret_cast<const float4*>(c + i);
+          const float4 c1v = *reinterpret_cast<const float4*>(c + i + 4);
+          cv[0] = c0v.x, cv[1] = c0v.y, cv[2] = c0v.z, cv[3] = c0v.w;
+          cv[4] = c1v.x, cv[5] = c1v.y, cv[6] = c1v.z, cv[7] = c1v.w;
+        } else {
+#pragma unroll
+          for (int l = 0; l < 8; ++l) cv[l] = c[i + l];
+        }
+#pragma unroll
+        for (int l = 0; l < 8; ++l) {
+          const float d = __fsub_rn(qs[(i + l) * (QB + 1) + t], cv[l]);
+          acc[l] = __fadd_rn(acc[l], __fmul_rn(d, d));
+        }
+      }
+      float tail = 0.0f;
+      for (uint32_t i = full; i < dim; ++i) {
+        const float d = __fsub_rn(qs[i * (QB + 1) + t], c[i]);
+        tail = __fadd_rn(tail, __fmul_rn(d, d));
+      }
+      const float x = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
+      const float y = __fadd_rn(__fadd_rn(acc[4], acc[5]), __fadd_rn(acc[6], acc[7]));
+      const float dist = __fadd_rn(__fadd_rn(x, y), tail);
+      const uint64_t key = ((uint64_t)order_key(dist) << 32) | (c0 + j);
+      if (have < P || key < best[(P - 1) * QB + t]) {
+        uint32_t pos = have < P ? have++ : P - 1;
+        while (pos > 0 && best[(pos - 1) * QB + t] > key) {
+          best[pos * QB + t] = best[(pos - 1) * QB + t];
+          --pos;
+        }
+        best[pos * QB + t] = key;
+      }
+    }
+  }
+  if (qi < nq)
+    for (uint32_t j = 0; j < P; ++j) partial[((size_t)qi * gridDim.y + blockIdx.y) * P + j] = best[j * QB + t];
+}
+
+// Merges the partial lists of each query into its nprobe probed lists, in
+// ascending (distance, list) order.
+__global__ void coarse_merge_kernel(const uint64_t* __restrict__ partial, uint32_t nq, uint32_t parts, uint32_t P,
+                                    uint32_t nprobe, uint32_t* __restrict__ probes) {
+  extern __shared__ __align__(16) unsigned char sm_raw[];
+  uint64_t* s = reinterpret_cast<uint64_t*>(sm_raw);
+  const uint32_t q = blockIdx.x;
+  const uint32_t total = parts * P;
+  uint32_t n2 = 1;
+  while (n2 < total) n2 <<= 1;
+  for (uint32_t i = threadIdx.x; i < n2; i += blockDim.x)
+    s[i] = i < total ? partial[(size_t)q * total + i] : ~0ull;
+  block_bitonic_sort_u64(s, n2);
+  for (uint32_t i = threadIdx.x; i < nprobe; i += blockDim.x)
+    probes[(size_t)q * nprobe + i] = s[i] == ~0ull ? UNASSIGNED : (uint32_t)s[i];
+}
+
+// ---------------------------------------------------------------------------
+// Block radix-select: the K-th smallest (1-based) of buf[0, cnt), then keeps
+// exactly the K keys <= it at the front. Keys are unique. Returns the K-th.
+// ---------------------------------------------------------------------------
+__device__ uint64_t select_keep(uint64_t* buf, uint32_t cnt, uint32_t K, uint32_t* hist, uint32_t* sh) {
+  uint64_t prefix = 0, mask = 0;
+  uint32_t k = K;
+  for (int shift = 56; shift >= 0; shift -= 8) {
+    for (uint32_t b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) {
+      const uint64_t key = buf[i];
+      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {  // one warp: prefix sums over the 256 bins
+      const uint32_t lane = threadIdx.x;
+      uint32_t c[8], s = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c[j] = hist[lane * 8 + j];
+        s += c[j];
+      }
+      uint32_t inc = s;
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t v = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+        if (lane >= (uint32_t)o) inc += v;
+      }
+      const uint32_t before = inc - s;
+      if (before < k && inc >= k) {
+        uint32_t acc = before;
+        for (int j = 0; j < 8; ++j) {
+          if (acc + c[j] >= k) {
+            sh[0] = lane * 8 + j;
+            sh[1] = k - acc;
+            break;
+          }
+          acc += c[j];
+        }
+      }
+    }
+    __syncthreads();
+    prefix |= (uint64_t)sh[0] << shift;
+    mask |= 0xFFull << shift;
+    k = sh[1];
+    __syncthreads();
+  }
+  // keep the keys <= prefix (exactly K of them)
+  constexpr uint32_t PER = CB / SCAN_THREADS;
+  uint64_t mine[PER];
+  uint32_t nmine = 0;
+  for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x)
+    if (buf[i] <= prefix) mine[nmine++] = buf[i];
+  if (threadIdx.x == 0) sh[2] = 0;
+  __syncthreads();
+  const uint32_t base = atomicAdd(&sh[2], nmine);
+  for (uint32_t j = 0; j < nmine; ++j) buf[base + j] = mine[j];
+  __syncthreads();
+  return prefix;
+}
+
+struct ScanParams {
+  const float* queries;      // nq x dim (prepared)
+  const uint32_t* probes;    // nq x nprobe list indices
+  const float* centroids;
+  const float* codebooks;
+  const uint32_t* woff;      // [m] widths then [m+1] offsets
+  const uint32_t* list_off;
+  const uint32_t* list_slot;
+  const uint8_t* list_codes;
+  const uint32_t* slot_rank;  // VectorId rank of each slot
+  const uint32_t* rank_slot;
+  const uint64_t* ids;        // VectorId per slot
+  const float* vectors;       // nullable: no rerank
+  const uint64_t* bitmap;     // nullable
+  uint64_t* out_ids;
+  float* out_dist;
+  uint32_t* out_len;
+  uint32_t nq, dim, m, nprobe, k, shortlist;
+  int metric;
+  int rerank;
+};
+
+// K5 + K6: one CTA per query.
+__global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(const ScanParams p) {
+  extern __shared__ __align__(16) unsigned char sm_raw[];
+  uint64_t* buf = reinterpret_cast<uint64_t*>(sm_raw);  // [CB]
+  float* lut = reinterpret_cast<float*>(buf + CB);      // [m][256]
+  float* qs = lut + (size_t)p.m * 256;                  // [dim]
+  float* rs = qs + p.dim;                               // [dim]
+  uint32_t* woff = reinterpret_cast<uint32_t*>(rs + p.dim);  // [2m+1]
+  __shared__ uint32_t hist[256], sh[4], count;
+  __shared__ uint64_t thr;
+  __shared__ float qdc;
+  const uint32_t q = blockIdx.x, t = threadIdx.x;
+  const uint32_t dim = p.dim, m = p.m;
+  const bool cosine = p.metric == PXC_COSINE;
+  for (uint32_t i = t; i < dim; i += blockDim.x) qs[i] = p.queries[(size_t)q * dim + i];
+  for (uint32_t i = t; i < 2 * m + 1; i += blockDim.x) woff[i] = p.woff[i];
+  if (t == 0) {
+    count = 0;
+    thr = ~0ull;
+  }
+  __syncthreads();
+  const uint32_t* widths = woff;
+  const uint32_t* offs = woff + m;
+  // table over a vector v (in shared memory): squared (or dot) per entry
+  auto build_table = [&](const float* v, bool dot) {
+    for (uint32_t s = 0; s < m; ++s) {
+      const uint32_t w = widths[s], o = offs[s];
+      const float* cb = p.codebooks + 256u * o + t * w;
+      float acc = 0.0f;
+      for (uint32_t j = 0; j < w; ++j) {
+        const float c = __ldg(cb + j);
+        if (dot) {
+          acc = __fadd_rn(acc, __fmul_rn(v[o + j], c));
+        } else {
+          const float d = __fsub_rn(v[o + j], c);
+          acc = __fadd_rn(acc, __fmul_rn(d, d));
+        }
+      }
+      lut[s * 256 + t] = acc;
+    }
+  };
+  if (cosine) build_table(qs, true);  // one table per query (the dot products)
+  for (uint32_t pi = 0; pi < p.nprobe; ++pi) {
+    const uint32_t l = p.probes[(size_t)q * p.nprobe + pi];
+    if (l == UNASSIGNED) break;
+    const float* c = p.centroids + (size_t)l * dim;
+    __syncthreads();  // previous list's lookups are done
+    if (!cosine) {
+      for (uint32_t i = t; i < dim; i += blockDim.x) rs[i] = __fsub_rn(qs[i], c[i]);
+      __syncthreads();
+      build_table(rs, false);
+    } else if (t == 0) {
+      qdc = dot_unrolled(qs, c, dim);
+    }
+    __syncthreads();
+    const float one_minus = cosine ? __fsub_rn(1.0f, qdc) : 0.0f;
+    const uint32_t b = p.list_off[l], e = p.list_off[l + 1];
+    for (uint32_t j0 = b; j0 < e; j0 += CHUNK) {
+      if (count > CB - CHUNK) {
+        const uint64_t kth = select_keep(buf, count, p.shortlist, hist, sh);
+        if (t == 0) {
+          count = p.shortlist;
+          thr = kth;
+        }
+        __syncthreads();
+      }
+      const uint64_t th = thr;
+      const uint32_t j1 = min(e, j0 + CHUNK);
+      for (uint32_t j = j0 + t; j < j1; j += blockDim.x) {
+        const uint32_t slot = p.list_slot[j];
+        if (p.bitmap && !((p.bitmap[slot >> 6] >> (slot & 63)) & 1ull)) continue;
+        const uint8_t* code = p.list_codes + (size_t)j * m;
+        float sum = 0.0f;
+        if ((m & 15) == 0) {
+          for (uint32_t s0 = 0; s0 < m; s0 += 16) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(code + s0));
+            const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int u = 0; u < 16; ++u)
+              sum = __fadd_rn(sum, lut[(s0 + u) * 256 + ((w4[u >> 2] >> (8 * (u & 3))) & 255u)]);
+          }
+        } else {
+          for (uint32_t s = 0; s < m; ++s) sum = __fadd_rn(sum, lut[s * 256 + code[s]]);
+        }
+        const float score = cosine ? __fadd_rn(one_minus, -sum) : sum;
+        const uint64_t key = ((uint64_t)order_key(score) << 32) | p.slot_rank[slot];
+        if (key < th) buf[atomicAdd(&count, 1u)] = key;
+      }
+      __syncthreads();
+    }
+  }
+  __syncthreads();
+  uint32_t n = count;
+  if (n > p.shortlist) {
+    select_keep(buf, n, p.shortlist, hist, sh);
+    n = p.shortlist;
+  }
+  uint32_t n2 = 1;
+  while (n2 < n) n2 <<= 1;
+  for (uint32_t i = n + t; i < n2; i += blockDim.x) buf[i] = ~0ull;
+  block_bitonic_sort_u64(buf, n2);
+  uint64_t* outk = buf;
+  if (p.rerank && p.vectors) {
+    // K6: exact distances of the shortlist, top-k of them
+    for (uint32_t i = t; i < n; i += blockDim.x) {
+      const uint32_t rank = (uint32_t)buf[i];
+      const uint32_t slot = p.rank_slot[rank];
+      const float d = space_distance(p.metric, qs, p.vectors + (size_t)slot * dim, dim);
+      buf[CB / 2 + i] = ((uint64_t)order_key(d) << 32) | rank;
+    }
+    for (uint32_t i = n + t; i < n2; i += blockDim.x) buf[CB / 2 + i] = ~0ull;
+    block_bitonic_sort_u64(buf + CB / 2, n2);
+    outk = buf + CB / 2;
+  }
+  const uint32_t take = min(n, p.k);
+  for (uint32_t i = t; i < take; i += blockDim.x) {
+    const uint64_t key = outk[i];
+    const uint32_t slot = p.rank_slot[(uint32_t)key];
+    p.out_ids[(size_t)q * p.k + i] = p.ids[slot];
+    p.out_dist[(size_t)q * p.k + i] = key_to_float((uint32_t)(key >> 32));
+  }
+  if (t == 0) p.out_len[q] = take;
+}
+
+// ---------------------------------------------------------------------------
+// Build side: PQ encoding of residuals (ProductQuantizer::encode_into,
+// product.rs:361-380 with nearest_centroid :529-547: residual x - c per
+// dimension, then the codeword with the smallest sequential squared distance,
+// strict '<' so ties keep the lower index). Block = 128 rows x one subspace;
+// the subspace's codebook in shared memory, each row's residual too.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) pq_encode_kernel(const float* __restrict__ X, uint32_t ldx, uint64_t n,
+                                                        const uint32_t* __restrict__ list_of,
+                                                        const float* __restrict__ centroids, uint32_t dim,
+                                                        const float* __restrict__ codebooks,
+                                                        const uint32_t* __restrict__ woff, uint32_t m,
+                                                        uint8_t* __restrict__ codes) {
+  extern __shared__ __align__(16) float sm[];
+  const uint32_t s = blockIdx.y;
+  const uint32_t w = woff[s], o = woff[m + s];
+  float* book = sm;              // [256][w]
+  float* res = sm + 256 * w;     // [128][w + 1]
+  for (uint32_t e = threadIdx.x; e < 256 * w; e += blockDim.x) book[e] = codebooks[256u * o + e];
+  const uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  const bool valid = i < n && list_of[i] != UNASSIGNED;
+  if (valid) {
+    const float* x = X + i * ldx + o;
+    const float* c = centroids + (size_t)list_of[i] * dim + o;
+    for (uint32_t t = 0; t < w; ++t) res[threadIdx.x * (w + 1) + t] = __fsub_rn(x[t], c[t]);
+  }
+  __syncthreads();
+  if (!valid) {
+    if (i < n) codes[i * m + s] = 0;
+    return;
+  }
+  const float* r = res + threadIdx.x * (w + 1);
+  uint32_t best = 0;
+  float bd = __int_as_float(0x7f800000);
+  for (uint32_t j = 0; j < 256; ++j) {
+    const float* cw = book + j * w;
+    float acc = 0.0f;
+    for (uint32_t t = 0; t < w; ++t) {
+      const float d = __fsub_rn(r[t], cw[t]);
+      acc = __fadd_rn(acc, __fmul_rn(d, d));
+    }
+    if (acc < bd) {
+      bd = acc;
+      best = j;
+    }
+  }
+  codes[i * m + s] = (uint8_t)best;
+}
+
+// Residuals of rows against their lists (ivfpq.rs:788-792): x - c per dimension.
+__global__ void residual_kernel(const float* __restrict__ X, uint32_t ldx, uint64_t n, uint32_t dim,
+                                const uint32_t* __restrict__ list_of, const float* __restrict__ centroids,
+                                float* __restrict__ out) {
+  const uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (e >= n * dim) return;
+  const uint64_t i = e / dim, t = e - i * dim;
+  out[e] = __fsub_rn(X[i * ldx + t], centroids[(size_t)list_of[i] * dim + t]);
+}
+
+// Gathers rows by index into a dense matrix; and one subspace's columns.
+__global__ void gather_rows_kernel(const float* __restrict__ X, uint32_t dim, const uint32_t* __restrict__ rows,
+                                   uint64_t n, float* __restrict__ out) {
+  const uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (e >= n * dim) return;
+  const uint64_t i = e / dim, t = e - i * dim;
+  out[e] = X[(size_t)rows[i] * dim + t];
+}
+__global__ void gather_cols_kernel(const float* __restrict__ X, uint32_t dim, uint64_t n, uint32_t o, uint32_t w,
+                                   uint32_t ldo, float* __restrict__ out) {
+  const uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (e >= n * w) return;
+  const uint64_t i = e / w, t = e - i * w;
+  out[i * ldo + t] = X[i * dim + o + t];
+}
+
+// Dead slots take no list.
+__global__ void mask_dead_kernel(uint32_t* __restrict__ list_of, const uint8_t* __restrict__ live, uint64_t n) {
+  const uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (i < n && !live[i]) list_of[i] = UNASSIGNED;
+}
+__global__ void iota_u32_kernel(uint32_t* out, uint64_t n) {
+  const uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (i < n) out[i] = (uint32_t)i;
+}
+// List boundaries in the (list, slot)-sorted order.
+__global__ void list_bounds_kernel(const uint32_t* __restrict__ keys, uint64_t n, uint32_t nlist,
+                                   uint32_t* __restrict__ off) {
+  const uint32_t l = blockIdx.x * blockDim.x + threadIdx.x;
+  if (l > nlist) return;
+  uint64_t lo = 0, hi = n;
+  while (lo < hi) {
+    const uint64_t mid = (lo + hi) >> 1;
+    if (keys[mid] < l)
+      lo = mid + 1;
+    else
+      hi = mid;
+  }
+  off[l] = (uint32_t)lo;
+}
+__global__ void gather_codes_kernel(const uint8_t* __restrict__ codes, uint32_t m, const uint32_t* __restrict__ slots,
+                                    uint64_t n, uint8_t* __restrict__ out) {
+  const uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (e >= n * m) return;
+  const uint64_t j = e / m, s = e - j * m;
+  out[e] = codes[(size_t)slots[j] * m + s];
+}
+
+}  // namespace ivf
+}  // namespace pxc
+
+// ---------------------------------------------------------------------------
+// Handle
+// ---------------------------------------------------------------------------
+struct pxc_ivfpq {
+  pxc_ctx* ctx = nullptr;
+  uint32_t dim = 0, nlist = 0, m = 0;
+  int32_t metric = 0;
+  std::vector<uint32_t> widths, offsets;
+  pxc::DBuf<uint32_t> woff;
+  pxc::DBuf<float> centroids, codebooks, vectors;
+  bool have_parts = false, have_vectors = false;
+  uint64_t nslots = 0, nlive = 0;
+  std::vector<uint64_t> h_ids;
+  std::vector<uint8_t> h_live;
+  pxc::DBuf<uint64_t> ids;
+  pxc::DBuf<uint32_t> slot_rank, rank_slot;
+  pxc::DBuf<uint32_t> list_off, list_slot, list_of;
+  pxc::DBuf<uint8_t> list_codes, codes, live;
+  bool have_lists = false;
+  pxc::DBuf<float> q_buf;
+  pxc::DBuf<uint32_t> probes;
+  pxc::DBuf<uint64_t> partial, io_ids, bitmap;
+  pxc::DBuf<float> io_dist;
+  pxc::DBuf<uint32_t> io_len;
+  std::mutex mu;
+};
+
+namespace pxc {
+namespace ivf {
+
+void layout(uint32_t dim, uint32_t m, std::vector<uint32_t>& w, std::vector<uint32_t>& o) {
+  // product.rs:227-238 — widths differ by at most one, the remainder leading
+  w.assign(m, dim / m);
+  for (uint32_t s = 0; s < dim % m; ++s) ++w[s];
+  o.assign(m + 1, 0);
+  for (uint32_t s = 0; s < m; ++s) o[s + 1] = o[s] + w[s];
+}
+
+// Builds the list CSR (ascending slots per list) from list_of and the codes.
+void build_lists(pxc_ivfpq* h, const std::vector<uint32_t>& list_of, const uint8_t* codes_host, cudaStream_t s) {
+  std::vector<uint32_t> off(h->nlist + 1, 0);
+  for (uint64_t i = 0; i < h->nslots; ++i)
+    if (h->h_live[i] && list_of[i] != UNASSIGNED) {
+      if (list_of[i] >= h->nlist)
+        throw make_failure(PXC_CORRUPTION, i, list_of[i], "list_of", "slot %llu names list %u of %u",
+                           (unsigned long long)i, list_of[i], h->nlist);
+      ++off[list_of[i] + 1];
+    }
+  for (uint32_t l = 0; l < h->nlist; ++l) off[l + 1] += off[l];
+  const uint64_t total = off[h->nlist];
+  std::vector<uint32_t> slot(total), fill(off.begin(), off.end() - 1);
+  std::vector<uint8_t> lc(std::max<uint64_t>(1, total * h->m));
+  for (uint64_t i = 0; i < h->nslots; ++i)
+    if (h->h_live[i] && list_of[i] != UNASSIGNED) {
+      const uint32_t pos = fill[list_of[i]]++;
+      slot[pos] = (uint32_t)i;
+      std::memcpy(lc.data() + (size_t)pos * h->m, codes_host + i * h->m, h->m);
+    }
+  h->list_off.reserve(h->nlist + 1);
+  h->list_slot.reserve(std::max<uint64_t>(1, total));
+  h->list_codes.reserve(std::max<uint64_t>(16, total * h->m));
+  PXC_CUDA(cudaMemcpyAsync(h->list_off.p, off.data(), off.size() * 4, cudaMemcpyHostToDevice, s));
+  if (total) {
+    PXC_CUDA(cudaMemcpyAsync(h->list_slot.p, slot.data(), total * 4, cudaMemcpyHostToDevice, s));
+    PXC_CUDA(cudaMemcpyAsync(h->list_codes.p, lc.data(), total * h->m, cudaMemcpyHostToDevice, s));
+  }
+  PXC_CUDA(cudaStreamSynchronize(s));
+  h->have_lists = true;
+}
+
+void search_device(pxc_ivfpq* h, const float* d_q, uint32_t nq, uint32_t k, uint32_t nprobe, uint32_t rerank,
+                   const uint64_t* d_bitmap, uint64_t* d_ids, float* d_dist, uint32_t* d_len, cudaStream_t s) {
+  pxc_ctx* ctx = h->ctx;
+  if (nq == 0) return;
+  if (k == 0 || h->nlive == 0 || !h->have_lists) {
+    PXC_CUDA(cudaMemsetAsync(d_len, 0, (size_t)nq * 4, s));
+    return;
+  }
+  PXC_CONFIG(h->have_parts, "codebooks", 0, "the index has no trained parts");
+  nprobe = std::min<uint32_t>(std::max<uint32_t>(nprobe, 1), h->nlist);
+  PXC_CONFIG(nprobe <= MAX_NPROBE, "nprobe", nprobe, "the device search supports nprobe <= 128");
+  const uint32_t shortlist = rerank > 0 ? std::max(rerank, k) : k;
+  PXC_CONFIG(shortlist <= MAX_SHORTLIST, "rerank", shortlist,
+             "the device search keeps at most 1024 candidates per query (max(rerank, k))");
+  const uint32_t dim = h->dim, nlist = h->nlist;
+  // K4: coarse
+  const uint32_t P = nprobe;
+  const uint32_t crange = std::max<uint32_t>(TCC, (nlist + CSPLIT - 1) / CSPLIT);
+  const uint32_t parts = (nlist + crange - 1) / crange;
+  const uint32_t batch = 16384;
+  h->probes.reserve((size_t)std::min(nq, batch) * nprobe);
+  h->partial.reserve((size_t)std::min(nq, batch) * parts * P);
+  const size_t smem_c = (size_t)P * QB * 8 + ((((size_t)dim * (QB + 1) + 3) & ~size_t(3)) + (size_t)TCC * dim) * 4;
+  PXC_CUDA(cudaFuncSetAttribute(coarse_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_c));
+  uint32_t n2 = 1;
+  while (n2 < parts * P) n2 <<= 1;
+  const size_t smem_m = (size_t)n2 * 8;
+  PXC_CUDA(cudaFuncSetAttribute(coarse_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_m));
+  const size_t smem_s = (size_t)CB * 8 + ((size_t)h->m * 256 + 2 * dim) * 4 + (2 * h->m + 1) * 4;
+  PXC_CUDA(cudaFuncSetAttribute(scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_s));
+  for (uint32_t q0 = 0; q0 < nq; q0 += batch) {
+    const uint32_t nb = std::min(batch, nq - q0);
+    const float* qb = d_q + (size_t)q0 * dim;
+    coarse_partial_kernel<<<dim3((nb + QB - 1) / QB, parts), QB, smem_c, s>>>(qb, nb, dim, h->centroids.p, nlist,
+                                                                            crange, P, h->partial.p);
+    coarse_merge_kernel<<<nb, 256, smem_m, s>>>(h->partial.p, nb, parts, P, nprobe, h->probes.p);
+    ScanParams sp{};
+    sp.queries = qb;
+    sp.probes = h->probes.p;
+    sp.centroids = h->centroids.p;
+    sp.codebooks = h->codebooks.p;
+    sp.woff = h->woff.p;
+    sp.list_off = h->list_off.p;
+    sp.list_slot = h->list_slot.p;
+    sp.list_codes = h->list_codes.p;
+    sp.slot_rank = h->slot_rank.p;
+    sp.rank_slot = h->rank_slot.p;
+    sp.ids = h->ids.p;
+    sp.vectors = h->have_vectors ? h->vectors.p : nullptr;
+    sp.bitmap = d_bitmap;
+    sp.out_ids = d_ids + (size_t)q0 * k;
+    sp.out_dist = d_dist + (size_t)q0 * k;
+    sp.out_len = d_len + q0;
+    sp.nq = nb;
+    sp.dim = dim;
+    sp.m = h->m;
+    sp.nprobe = nprobe;
+    sp.k = k;
+    sp.shortlist = shortlist;
+    sp.metric = h->metric;
+    sp.rerank = rerank > 0;
+    scan_kernel<<<nb, SCAN_THREADS, smem_s, s>>>(sp);
+    PXC_CUDA(cudaGetLastError());
+    ctx->launches += 3;
+  }
+}
+
+}  // namespace ivf
+}  // namespace pxc
+
+using namespace pxc;
+
+extern "C" {
+
+pxc_status pxc_ivfpq_create(pxc_ctx* ctx, uint32_t dim, int32_t metric, uint32_t nlist, uint32_t m,
+                            pxc_ivfpq** out, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(ctx != nullptr, "ctx", 0, "null context");
+    PXC_CONFIG(out != nullptr, "out", 0, "output handle pointer is null");
+    PXC_CONFIG(dim >= 1 && dim <= ivf::MAX_DIM, "dim", dim, "the device IVF-PQ supports 1 <= dim <= 1024");
+    PXC_CONFIG(metric == PXC_EUCLIDEAN || metric == PXC_COSINE, "metric", metric,
+               "the device IVF-PQ supports euclidean and cosine");
+    PXC_CONFIG(nlist >= 1, "nlist", nlist, "must be at least 1");
+    PXC_CONFIG(m >= 1 && m <= dim, "subspaces", m, "must be between 1 and the space dimension");
+    PXC_CONFIG(m <= ivf::MAX_M, "subspaces", m, "the device IVF-PQ supports at most 64 subspaces");
+    DeviceGuard g(ctx->device);
+    auto* h = new pxc_ivfpq();
+    h->ctx = ctx;
+    h->dim = dim;
+    h->metric = metric;
+    h->nlist = nlist;
+    h->m = m;
+    ivf::layout(dim, m, h->widths, h->offsets);
+    std::vector<uint32_t> wo(h->widths);
+    wo.insert(wo.end(), h->offsets.begin(), h->offsets.end());
+    try {
+      h->woff.reserve(wo.size());
+      PXC_CUDA(cudaMemcpy(h->woff.p, wo.data(), wo.size() * 4, cudaMemcpyHostToDevice));
+    } catch (...) {
+      delete h;
+      throw;
+    }
+    *out = h;
+  });
+}
+
+void pxc_ivfpq_destroy(pxc_ivfpq* h) {
+  if (!h) return;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(h->ctx->device);
+  delete h;
+  if (prev >= 0) cudaSetDevice(prev);
+}
+
+pxc_status pxc_ivfpq_set_parts(pxc_ivfpq* h, const float* centroids, const float* codebooks, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(h != nullptr && centroids != nullptr && codebooks != nullptr, "parts", 0, "null argument");
+    std::lock_guard<std::mutex> lock(h->mu);
+    DeviceGuard g(h->ctx->device);
+    cudaStream_t s = h->ctx->stream;
+    h->centroids.reserve((size_t)h->nlist * h->dim);
+    h->codebooks.reserve((size_t)256 * h->dim);
+    PXC_CUDA(cudaMemcpyAsync(h->centroids.p, centroids, (size_t)h->nlist * h->dim * 4, cudaMemcpyHostToDevice, s));
+    PXC_CUDA(cudaMemcpyAsync(h->codebooks.p, codebooks, (size_t)256 * h->dim * 4, cudaMemcpyHostToDevice, s));
+    PXC_CUDA(cudaStreamSynchronize(s));
+    h->have_parts = true;
+  });
+}
+
+pxc_status pxc_ivfpq_set_store(pxc_ivfpq* h, const float* vectors, const uint64_t* ids, const uint8_t* live,
+                               uint64_t nslots, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(h != nullptr, "h", 0, "null handle");
+    PXC_CONFIG(nslots < 0xFFFFFFFFull, "nslots", nslots, "the device IVF-PQ supports fewer than 2^32 slots");
+    std::lock_guard<std::mutex> lock(h->mu);
+    DeviceGuard g(h->ctx->device);
+    cudaStream_t s = h->ctx->stream;
+    h->nslots = nslots;
+    h->h_ids.resize(nslots);
+    h->h_live.assign(nslots, 1);
+    for (uint64_t i = 0; i < nslots; ++i) {
+      h->h_ids[i] = ids ? ids[i] : i;
+      if (live) h->h_live[i] = live[i] ? 1 : 0;
+    }
+    if (vectors)
+      for (uint64_t i = 0; i < nslots * h->dim; ++i)
+        if (!std::isfinite(vectors[i]))
+          throw make_failure(PXC_NON_FINITE, i, 0, "vectors", "vector component %llu is not finite",
+                             (unsigned long long)i);
+    // rank of each live slot's VectorId: (score, rank) orders as (score, id)
+    std::vector<uint32_t> order;
+    order.reserve(nslots);
+    for (uint64_t i = 0; i < nslots; ++i)
+      if (h->h_live[i]) order.push_back((uint32_t)i);
+    std::sort(order.begin(), order.end(), [&](uint32_t a, uint32_t b) { return h->h_ids[a] < h->h_ids[b]; });
+    for (size_t r = 1; r < order.size(); ++r)
+      if (h->h_ids[order[r]] == h->h_ids[order[r - 1]])
+        throw make_failure(PXC_DUPLICATE_ID, h->h_ids[order[r]], 0, "ids", "VectorId %llu is live twice",
+                           (unsigned long long)h->h_ids[order[r]]);
+    std::vector<uint32_t> sr(std::max<uint64_t>(1, nslots), 0xFFFFFFFFu);
+    for (size_t r = 0; r < order.size(); ++r) sr[order[r]] = (uint32_t)r;
+    h->nlive = order.size();
+    h->ids.reserve(std::max<uint64_t>(1, nslots));
+    h->slot_rank.reserve(std::max<uint64_t>(1, nslots));
+    h->rank_slot.reserve(std::max<size_t>(1, order.size()));
+    if (nslots) {
+      PXC_CUDA(cudaMemcpyAsync(h->ids.p, h->h_ids.data(), nslots * 8, cudaMemcpyHostToDevice, s));
+      PXC_CUDA(cudaMemcpyAsync(h->slot_rank.p, sr.data(), nslots * 4, cudaMemcpyHostToDevice, s));
+    }
+    if (!order.empty())
+      PXC_CUDA(cudaMemcpyAsync(h->rank_slot.p, order.data(), order.size() * 4, cudaMemcpyHostToDevice, s));
+    h->have_vectors = vectors != nullptr;
+    if (vectors && nslots) {
+      h->vectors.reserve(nslots * h->dim);
+      PXC_CUDA(cudaMemcpyAsync(h->vectors.p, vectors, nslots * h->dim * 4, cudaMemcpyHostToDevice, s));
+    }
+    PXC_CUDA(cudaStreamSynchronize(s));
+    h->have_lists = false;
+  });
+}
+
+pxc_status pxc_ivfpq_set_codes(pxc_ivfpq* h, const uint32_t* list_of, const uint8_t* codes, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(h != nullptr && (h->nslots == 0 || (list_of && codes)), "codes", 0, "null argument");
+    std::lock_guard<std::mutex> lock(h->mu);
+    DeviceGuard g(h->ctx->device);
+    std::vector<uint32_t> lo(list_of, list_of + h->nslots);
+    ivf::build_lists(h, lo, codes, h->ctx->stream);
+  });
+}
+
+pxc_status pxc_ivfpq_search_device(pxc_ivfpq* h, const float* d_queries, uint32_t nq, uint32_t k, uint32_t nprobe,
+                                   uint32_t rerank, const uint64_t* d_bitmap, uint64_t* d_out_ids,
+                                   float* d_out_dist, uint32_t* d_out_len, void* stream, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(h != nullptr, "h", 0, "null handle");
+    PXC_CONFIG(k <= PXC_MAX_K, "k", k, "k exceeds the maximum");
+    std::lock_guard<std::mutex> lock(h->mu);
+    DeviceGuard g(h->ctx->device);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->ctx->stream;
+    ivf::search_device(h, d_queries, nq, k, nprobe, rerank, d_bitmap, d_out_ids, d_out_dist, d_out_len, s);
+  });
+}
+
+pxc_status pxc_ivfpq_search(pxc_ivfpq* h, const float* queries, uint32_t nq, uint32_t k, uint32_t nprobe,
+                            uint32_t rerank, const uint64_t* bitmap, uint64_t* out_ids, float* out_dist,
+                            uint32_t* out_len, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(h != nullptr, "h", 0, "null handle");
+    PXC_CONFIG(k <= PXC_MAX_K, "k", k, "k exceeds the maximum");
+    std::lock_guard<std::mutex> lock(h->mu);
+    DeviceGuard g(h->ctx->device);
+    cudaStream_t s = h->ctx->stream;
+    if (nq == 0) return;
+    for (uint64_t i = 0; i < (uint64_t)nq * h->dim; ++i)
+      if (!std::isfinite(queries[i]))
+        throw make_failure(PXC_NON_FINITE, i, 0, "queries", "query component %llu is not finite",
+                           (unsigned long long)i);
+    h->q_buf.reserve((size_t)nq * h->dim);
+    h->io_ids.reserve((size_t)nq * std::max<uint32_t>(k, 1));
+    h->io_dist.reserve((size_t)nq * std::max<uint32_t>(k, 1));
+    h->io_len.reserve(nq);
+    const uint64_t* db = nullptr;
+    if (bitmap) {
+      const uint64_t words = (h->nslots + 63) / 64;
+      h->bitmap.reserve(std::max<uint64_t>(1, words));
+      if (words) PXC_CUDA(cudaMemcpyAsync(h->bitmap.p, bitmap, words * 8, cudaMemcpyHostToDevice, s));
+      db = h->bitmap.p;
+    }
+    PXC_CUDA(cudaMemcpyAsync(h->q_buf.p, queries, (size_t)nq * h->dim * 4, cudaMemcpyHostToDevice, s));
+    ivf::search_device(h, h->q_buf.p, nq, k, nprobe, rerank, db, h->io_ids.p, h->io_dist.p, h->io_len.p, s);
+    PXC_CUDA(cudaMemcpyAsync(out_len, h->io_len.p, (size_t)nq * 4, cudaMemcpyDeviceToHost, s));
+    if (k) {
+      PXC_CUDA(cudaMemcpyAsync(out_ids, h->io_ids.p, (size_t)nq * k * 8, cudaMemcpyDeviceToHost, s));
+      PXC_CUDA(cudaMemcpyAsync(out_dist, h->io_dist.p, (size_t)nq * k * 4, cudaMemcpyDeviceToHost, s));
+    }
+    PXC_CUDA(cudaStreamSynchronize(s));
+  });
+}
+
+}  // extern "C"

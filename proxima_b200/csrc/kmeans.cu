@@ -30,6 +30,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "kmeans_api.h"
 #include "kmeans_tc.cuh"
 #include "rng.h"
 #include "seqsum.cuh"
@@ -55,17 +56,25 @@ __device__ __forceinline__ float seq_l2(const float* __restrict__ a, const float
   return s;
 }
 
-// Each lane gets seq_l2(A row ia, B row ib): the warp stages its 32 row pairs
-// through shared memory 32 dimensions at a time with coalesced 16-byte loads
-// (row pitches are multiples of 4 floats, bases 16-byte aligned), and each
-// lane continues its own sequential sum over the staged chunk.
+// Each lane gets the distance between A row ia and B row ib: the warp stages
+// its 32 row pairs through shared memory 32 dimensions at a time with
+// coalesced 16-byte loads (row pitches are multiples of 4 floats, bases
+// 16-byte aligned), and each lane continues its own sums over the staged
+// chunk. U8 = false: one sequential sum (kmeans.rs `squared`); U8 = true:
+// eight lane sums over full chunks of 8, reduced pairwise, plus a sequential
+// tail (proxima_core::distance::squared_euclidean).
 // sa, sb: 32 x 33 floats each, private to the warp.
+template <bool U8>
 __device__ __forceinline__ float warp_rows_l2(const float* __restrict__ A, uint32_t lda, uint64_t ia,
                                               const float* __restrict__ B, uint32_t ldb, uint64_t ib, uint32_t d,
                                               float* sa, float* sb) {
   const uint32_t lane = threadIdx.x & 31;
   const uint32_t part = lane & 7;  // which 4 dimensions of the 32-wide chunk
-  float s = 0.0f;
+  const uint32_t full = d & ~7u;
+  float s = 0.0f, tail = 0.0f;
+  float acc[8];
+#pragma unroll
+  for (int l = 0; l < 8; ++l) acc[l] = 0.0f;
   for (uint32_t c0 = 0; c0 < d; c0 += 32) {
     const bool on = c0 + part * 4 < d;
 #pragma unroll
@@ -85,11 +94,31 @@ __device__ __forceinline__ float warp_rows_l2(const float* __restrict__ A, uint3
     }
     __syncwarp();
     const uint32_t cnt = min(32u, d - c0);
-    for (uint32_t j = 0; j < cnt; ++j) {
-      const float t = __fsub_rn(sa[lane * 33 + j], sb[lane * 33 + j]);
-      s = __fadd_rn(s, __fmul_rn(t, t));
+    if (U8) {
+      const uint32_t vfull = c0 + 32 <= full ? 32u : (full > c0 ? full - c0 : 0u);
+      for (uint32_t j = 0; j < vfull; j += 8) {
+#pragma unroll
+        for (int l = 0; l < 8; ++l) {
+          const float t = __fsub_rn(sa[lane * 33 + j + l], sb[lane * 33 + j + l]);
+          acc[l] = __fadd_rn(acc[l], __fmul_rn(t, t));
+        }
+      }
+      for (uint32_t j = vfull; j < cnt; ++j) {
+        const float t = __fsub_rn(sa[lane * 33 + j], sb[lane * 33 + j]);
+        tail = __fadd_rn(tail, __fmul_rn(t, t));
+      }
+    } else {
+      for (uint32_t j = 0; j < cnt; ++j) {
+        const float t = __fsub_rn(sa[lane * 33 + j], sb[lane * 33 + j]);
+        s = __fadd_rn(s, __fmul_rn(t, t));
+      }
     }
     __syncwarp();
+  }
+  if (U8) {
+    const float x = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
+    const float y = __fadd_rn(__fadd_rn(acc[4], acc[5]), __fadd_rn(acc[6], acc[7]));
+    return __fadd_rn(__fadd_rn(x, y), tail);
   }
   return s;
 }
@@ -102,6 +131,7 @@ __device__ __forceinline__ float warp_rows_l2(const float* __restrict__ A, uint3
 // mode 1: write assign (setting *changed when it moves) and bestd;
 // mode 0: write bestd only.
 // ---------------------------------------------------------------------------
+template <bool U8>
 __global__ void __launch_bounds__(128) assign_exact_kernel(
     const float* __restrict__ P, uint32_t ldp, uint64_t n, const uint32_t* __restrict__ list,
     const uint32_t* __restrict__ list_count, const float* __restrict__ C, uint32_t ldc, uint32_t k, uint32_t d,
@@ -136,6 +166,34 @@ __global__ void __launch_bounds__(128) assign_exact_kernel(
       cs[i * TC + j] = j < cnt ? C[(size_t)(c0 + j) * ldc + i] : 0.0f;
     }
     __syncthreads();
+    if (U8) {  // one centroid at a time, eight lane sums
+      const uint32_t full = d & ~7u;
+      for (uint32_t j = 0; j < cnt; ++j) {
+        float acc[8];
+#pragma unroll
+        for (int l = 0; l < 8; ++l) acc[l] = 0.0f;
+        for (uint32_t i = 0; i < full; i += 8) {
+#pragma unroll
+          for (int l = 0; l < 8; ++l) {
+            const float df = __fsub_rn(ps[(i + l) * PBS + t], cs[(i + l) * TC + j]);
+            acc[l] = __fadd_rn(acc[l], __fmul_rn(df, df));
+          }
+        }
+        float tail = 0.0f;
+        for (uint32_t i = full; i < d; ++i) {
+          const float df = __fsub_rn(ps[i * PBS + t], cs[i * TC + j]);
+          tail = __fadd_rn(tail, __fmul_rn(df, df));
+        }
+        const float x = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
+        const float y = __fadd_rn(__fadd_rn(acc[4], acc[5]), __fadd_rn(acc[6], acc[7]));
+        const float D = __fadd_rn(__fadd_rn(x, y), tail);
+        if (D < best) {
+          best = D;
+          bi = c0 + j;
+        }
+      }
+      continue;
+    }
     for (uint32_t g = 0; g < cnt; g += 8) {
       float acc[8];
 #pragma unroll
@@ -212,7 +270,8 @@ __global__ void sqnorm_kernel(const float* __restrict__ X, uint32_t ld, uint64_t
   }
 }
 
-// out[i] = seq_l2(P row i, C row idx[i]) for every point (warp-cooperative).
+// out[i] = distance(P row i, C row idx[i]) for every point (warp-cooperative).
+template <bool U8>
 __global__ void __launch_bounds__(128) pair_l2_kernel(const float* __restrict__ P, uint32_t ldp, uint64_t n, uint32_t d,
                                                       const float* __restrict__ C, uint32_t ldc,
                                                       const uint32_t* __restrict__ idx, float* __restrict__ out) {
@@ -220,7 +279,7 @@ __global__ void __launch_bounds__(128) pair_l2_kernel(const float* __restrict__ 
   const uint32_t w = threadIdx.x >> 5;
   const uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
   const bool valid = i < n;
-  const float s = warp_rows_l2(P, ldp, valid ? i : 0, C, ldc, valid ? idx[i] : 0, d, stage[w][0], stage[w][1]);
+  const float s = warp_rows_l2<U8>(P, ldp, valid ? i : 0, C, ldc, valid ? idx[i] : 0, d, stage[w][0], stage[w][1]);
   if (valid) out[i] = s;
 }
 
@@ -272,6 +331,7 @@ __global__ void bound_kernel(uint64_t n, uint32_t d, const float* __restrict__ p
 // centroid order per point; '<' with the index tie-break keeps the lower
 // index). Inconclusive points (no candidate, or more than CMAX) go to the
 // rescan list.
+template <bool U8>
 __global__ void __launch_bounds__(128) cand_eval_kernel(const float* __restrict__ P, uint32_t ldp, uint64_t n,
                                                         uint32_t d, const float* __restrict__ C, uint32_t ldc, uint32_t k,
                                                         const uint32_t* __restrict__ cnt,
@@ -290,7 +350,7 @@ __global__ void __launch_bounds__(128) cand_eval_kernel(const float* __restrict_
   uint32_t bi = INVALID;
   for (uint32_t j = 0; j < mmax; ++j) {
     const uint32_t c = j < m ? cand[i * km_tc::CMAX + j] : INVALID;
-    const float D = warp_rows_l2(P, ldp, valid ? i : 0, C, ldc, c < k ? c : 0u, d, stage[w][0], stage[w][1]);
+    const float D = warp_rows_l2<U8>(P, ldp, valid ? i : 0, C, ldc, c < k ? c : 0u, d, stage[w][0], stage[w][1]);
     if (c < k && (D < best || (D == best && c < bi))) {
       best = D;
       bi = c;
@@ -444,15 +504,49 @@ __global__ void ub_hist_kernel(const float* __restrict__ P, uint32_t ldp, uint64
   for (uint32_t b = threadIdx.x; b < 2048; b += blockDim.x)
     if (h[b]) atomicAdd(hist + b, h[b]);
 }
-// Second level: the bin (of the first histogram) where the top `want`
-// bounds end is histogrammed again on the next 11 bits.
-__global__ void ub_hist2_kernel(const float* __restrict__ ub, uint64_t n, uint32_t* __restrict__ hist, uint32_t want) {
-  __shared__ uint32_t b1, h[2048];
-  if (threadIdx.x == 0) {
-    uint32_t acc = 0, b = 2048;
-    while (b > 0 && acc < want) acc += hist[--b];
-    b1 = b;
+// The bin, counted from the top of a 2048-bin histogram, where the top
+// `want` entries end: *bin, and the count of entries in bins above it. One
+// block of 256 threads, eight bins each, suffix sums by a block scan.
+__device__ void top_bin(const uint32_t* __restrict__ h, uint32_t want, uint32_t* bin, uint32_t* above) {
+  using Scan = cub::BlockScan<uint32_t, 256>;
+  __shared__ typename Scan::TempStorage tmp;
+  const uint32_t t = threadIdx.x;
+  uint32_t c[8], sum = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {  // thread t owns bins 2047-8t down to 2040-8t
+    c[j] = h[2047 - 8 * t - j];
+    sum += c[j];
   }
+  uint32_t before;  // entries in the bins above this thread's
+  Scan(tmp).ExclusiveSum(sum, before);
+  if (t == 0) {
+    *bin = 0;
+    *above = before;  // overwritten below unless want exceeds everything
+  }
+  __syncthreads();
+  if (before < want && before + sum >= want) {
+    uint32_t acc = before;
+    for (int j = 0; j < 8; ++j) {
+      if (acc + c[j] >= want) {
+        *bin = 2047 - 8 * t - j;
+        *above = acc;
+        break;
+      }
+      acc += c[j];
+    }
+  }
+}
+
+// tau[0] = first-level bin b1, tau[1] = entries above it.
+__global__ void __launch_bounds__(256) ub_level1_kernel(const uint32_t* __restrict__ hist, uint32_t want,
+                                                        uint32_t* tau) {
+  top_bin(hist, want, tau, tau + 1);
+}
+// Second level: bin b1 histogrammed again on the next 11 bits.
+__global__ void ub_hist2_kernel(const float* __restrict__ ub, uint64_t n, uint32_t* __restrict__ hist,
+                                const uint32_t* __restrict__ tau) {
+  __shared__ uint32_t h[2048];
+  const uint32_t b1 = tau[0];
   for (uint32_t b = threadIdx.x; b < 2048; b += blockDim.x) h[b] = 0;
   __syncthreads();
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
@@ -463,24 +557,23 @@ __global__ void ub_hist2_kernel(const float* __restrict__ ub, uint64_t n, uint32
   for (uint32_t b = threadIdx.x; b < 2048; b += blockDim.x)
     if (h[b]) atomicAdd(hist + 2048 + b, h[b]);
 }
-
-// Gathers the points whose bound reaches the threshold the two histograms
-// give for the top `want` (ties at the threshold included, at most `cap`).
-__global__ void ub_gather_kernel(const float* __restrict__ ub, uint64_t n, const uint32_t* __restrict__ hist,
-                                 uint32_t want, uint32_t cap, uint32_t* __restrict__ list, uint32_t* count) {
-  __shared__ uint32_t tau;
-  if (threadIdx.x == 0) {
-    uint32_t acc = 0, b = 2048;
-    while (b > 0 && acc < want) acc += hist[--b];
-    const uint32_t b1 = b;
-    acc -= hist[b1];  // bounds strictly above bin b1
-    uint32_t b2 = 2048;
-    while (b2 > 0 && acc < want) acc += hist[2048 + --b2];
-    tau = (b1 << 20) | (b2 << 9);
-  }
+// tau[2] = the threshold bits for the top `want` bounds.
+__global__ void __launch_bounds__(256) ub_level2_kernel(const uint32_t* __restrict__ hist, uint32_t want,
+                                                        uint32_t* tau) {
+  __shared__ uint32_t b2, above2;
+  const uint32_t left = want > tau[1] ? want - tau[1] : 1u;
+  top_bin(hist + 2048, left, &b2, &above2);
   __syncthreads();
+  if (threadIdx.x == 0) tau[2] = (tau[0] << 20) | (b2 << 9);
+}
+
+// Gathers the points whose bound reaches the threshold (ties included, at
+// most `cap`).
+__global__ void ub_gather_kernel(const float* __restrict__ ub, uint64_t n, const uint32_t* __restrict__ tau,
+                                 uint32_t cap, uint32_t* __restrict__ list, uint32_t* count) {
+  const uint32_t t = tau[2];
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
-    if (__float_as_uint(ub[i]) >= tau) {
+    if (__float_as_uint(ub[i]) >= t) {
       const uint32_t pos = atomicAdd(count, 1u);
       if (pos < cap) list[pos] = (uint32_t)i;
     }
@@ -580,11 +673,42 @@ __global__ void iota_kernel(uint32_t* out, uint64_t n) {
 // ---------------------------------------------------------------------------
 // Host driver
 // ---------------------------------------------------------------------------
-struct Result {
-  uint32_t k = 0, iterations = 0, path = 0, reseeded = 0;
-  uint64_t rescanned = 0;
-  double inertia = 0.0;
+
+// Scratch kept on the context between calls: device buffers only grow, and
+// the pinned host words are allocated once.
+struct Workspace {
+  DBuf<float> cur, next, part, cnorm, pnorm, bestd, u_next, exact, amin, nearest, ub;
+  DBuf<float4> bound;
+  DBuf<uint32_t> assign, cnt, cand, rescan, keys_a, keys_b, iota, sorted, off, words, ubc, ube, hist;
+  DBuf<unsigned long long> key, keys;
+  DBuf<unsigned char> sort_tmp;
+  uint64_t iota_n = 0, keys_n = 0;
+  uint32_t* h_words = nullptr;          // pinned: [0] changed [1] list count [2] empty count
+  double* h_double = nullptr;           // pinned
+  unsigned long long* h_u64 = nullptr;  // pinned: [0] pick, [1..2] validation scratch
+  seqsum::Summer summer;
+  cudaEvent_t prof[2] = {};
+  ~Workspace() {
+    for (cudaEvent_t e : prof)
+      if (e) cudaEventDestroy(e);
+    if (h_words) cudaFreeHost(h_words);
+    if (h_double) cudaFreeHost(h_double);
+    if (h_u64) cudaFreeHost(h_u64);
+  }
+  static void destroy(void* p) { delete static_cast<Workspace*>(p); }
 };
+
+Workspace& workspace(pxc_ctx* ctx) {
+  if (!ctx->kmeans_ws) {
+    ctx->kmeans_ws = new Workspace();
+    ctx->kmeans_ws_free = &Workspace::destroy;
+  }
+  Workspace& w = *static_cast<Workspace*>(ctx->kmeans_ws);
+  if (!w.h_words) PXC_CUDA(cudaMallocHost(&w.h_words, 8 * sizeof(uint32_t)));
+  if (!w.h_double) PXC_CUDA(cudaMallocHost(&w.h_double, 2 * sizeof(double)));
+  if (!w.h_u64) PXC_CUDA(cudaMallocHost(&w.h_u64, 4 * sizeof(unsigned long long)));
+  return w;
+}
 
 struct Runner {
   pxc_ctx* ctx = nullptr;
@@ -595,22 +719,35 @@ struct Runner {
   uint32_t d = 0, k = 0, ldc = 0;
   bool tensor = false;
   bool trace = false;
+  bool unrolled = false;  // exact distances in squared_euclidean's 8-lane order
   uint64_t launches = 0;
 
-  DBuf<float> cur, next, part, cnorm, pnorm, bestd, u_next, exact, amin, nearest, ub;
-  DBuf<float4> bound;
-  DBuf<uint32_t> assign, cnt, cand, rescan, keys_a, keys_b, iota, sorted, off, words, ubc, ube, hist;
-  DBuf<unsigned long long> key, keys;
-  DBuf<unsigned char> sort_tmp;
+  Workspace& w;
+  DBuf<float>&cur, &next, &part, &cnorm, &pnorm, &bestd, &u_next, &exact, &amin, &nearest, &ub;
+  DBuf<float4>& bound;
+  DBuf<uint32_t>&assign, &cnt, &cand, &rescan, &keys_a, &keys_b, &iota, &sorted, &off, &words, &ubc, &ube, &hist;
+  DBuf<unsigned long long>&key, &keys;
+  DBuf<unsigned char>& sort_tmp;
   size_t sort_tmp_bytes = 0;
-  uint32_t* h_words = nullptr;          // pinned: [0] changed [1] list count [2] empty count
-  double* h_double = nullptr;           // pinned
-  unsigned long long* h_u64 = nullptr;  // pinned: [0] pick, [1..2] validation scratch
-  seqsum::Summer summer;
+  uint32_t* h_words;
+  double* h_double;
+  unsigned long long* h_u64;
+  seqsum::Summer& summer;
+  cudaEvent_t* prof;
+
+  explicit Runner(Workspace& ws)
+      : w(ws), cur(ws.cur), next(ws.next), part(ws.part), cnorm(ws.cnorm), pnorm(ws.pnorm), bestd(ws.bestd),
+        u_next(ws.u_next), exact(ws.exact), amin(ws.amin), nearest(ws.nearest), ub(ws.ub), bound(ws.bound),
+        assign(ws.assign), cnt(ws.cnt), cand(ws.cand), rescan(ws.rescan), keys_a(ws.keys_a), keys_b(ws.keys_b),
+        iota(ws.iota), sorted(ws.sorted), off(ws.off), words(ws.words), ubc(ws.ubc), ube(ws.ube), hist(ws.hist),
+        key(ws.key), keys(ws.keys), sort_tmp(ws.sort_tmp), h_words(ws.h_words), h_double(ws.h_double),
+        h_u64(ws.h_u64), summer(ws.summer), prof(ws.prof) {}
   CUtensorMap tmap_p;
   uint32_t kblocks = 0, stages = 0, ntiles = 0;
 
   cudaEvent_t ev[8] = {};
+  uint32_t screen_passes = 0;
+  float screen_ms = 0.0f;
   void mark(int i) {
     if (!trace) return;
     if (!ev[i]) PXC_CUDA(cudaEventCreate(&ev[i]));
@@ -626,15 +763,6 @@ struct Runner {
   ~Runner() {
     for (cudaEvent_t e : ev)
       if (e) cudaEventDestroy(e);
-    if (h_words) cudaFreeHost(h_words);
-    if (h_double) cudaFreeHost(h_double);
-    if (h_u64) cudaFreeHost(h_u64);
-  }
-
-  void pinned() {
-    if (!h_words) PXC_CUDA(cudaMallocHost(&h_words, 8 * sizeof(uint32_t)));
-    if (!h_double) PXC_CUDA(cudaMallocHost(&h_double, 2 * sizeof(double)));
-    if (!h_u64) PXC_CUDA(cudaMallocHost(&h_u64, 4 * sizeof(unsigned long long)));
   }
 
   uint32_t exact_block() const { return d <= 128 ? 128 : (d <= 256 ? 64 : 32); }
@@ -652,12 +780,15 @@ struct Runner {
     cnorm.reserve(kpad);
     for (DBuf<float>* b : {&pnorm, &bestd, &u_next, &exact, &ub}) b->reserve(n);
     for (DBuf<uint32_t>* b : {&assign, &rescan, &keys_a, &keys_b, &iota, &sorted, &ubc, &ube}) b->reserve(n);
-    hist.reserve(4096);
+    hist.reserve(4096 + 4);
     off.reserve((size_t)k + 1);
     words.reserve(8);
     key.reserve(2);
-    keys.reserve(n);
-    PXC_CUDA(cudaMemsetAsync(keys.p, 0xFF, n * 8, s));
+    if (w.keys_n < n) {  // (distance, index) keys start at ~0 and are reset after each use
+      keys.reserve(n);
+      PXC_CUDA(cudaMemsetAsync(keys.p, 0xFF, n * 8, s));
+      w.keys_n = n;
+    }
     PXC_CUDA(cudaMemsetAsync(assign.p, 0, n * 4, s));
     size_t need = 0, need2 = 0;
     PXC_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, need, keys_a.p, keys_b.p, iota.p, sorted.p, (int)n, 0, 32, s));
@@ -665,9 +796,15 @@ struct Runner {
                                                        0, 32, s));
     sort_tmp_bytes = std::max(need, need2);
     sort_tmp.reserve(sort_tmp_bytes);
-    iota_kernel<<<ctx->sm_count * 4, 256, 0, s>>>(iota.p, n);
-    ++launches;
+    if (w.iota_n < n) {
+      iota_kernel<<<ctx->sm_count * 4, 256, 0, s>>>(iota.p, n);
+      ++launches;
+      w.iota_n = n;
+    }
     tensor = want_tensor;
+    if (ctx->profiling)
+      for (int i = 0; i < 2; ++i)
+        if (!prof[i]) PXC_CUDA(cudaEventCreate(&prof[i]));
     if (tensor) {
       kblocks = (d + km_tc::KB_FLOATS - 1) / km_tc::KB_FLOATS;
       stages = km_tc::pick_stages(kblocks);
@@ -684,7 +821,9 @@ struct Runner {
       ++launches;
     }
     const uint32_t pb = exact_block();
-    PXC_CUDA(cudaFuncSetAttribute(assign_exact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    PXC_CUDA(cudaFuncSetAttribute(assign_exact_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)exact_smem(pb)));
+    PXC_CUDA(cudaFuncSetAttribute(assign_exact_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)exact_smem(pb)));
     PXC_CUDA(cudaFuncSetAttribute(kpp_update_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)exact_smem(pb)));
@@ -703,13 +842,14 @@ struct Runner {
     const uint32_t splits = std::min(tiles, want);
     const uint32_t csplit = (tiles + splits - 1) / splits * TC;
     const uint32_t gy = (k + csplit - 1) / csplit;
+    auto kern = unrolled ? assign_exact_kernel<true> : assign_exact_kernel<false>;
     if (gy == 1) {
-      assign_exact_kernel<<<dim3(gx, 1), pb, exact_smem(pb), s>>>(P, ldp, n, list, dcount, C, ldc, k, d, csplit,
-                                                                 nullptr, asg, bd, words.p + 0, mode, ver, ver_val);
+      kern<<<dim3(gx, 1), pb, exact_smem(pb), s>>>(P, ldp, n, list, dcount, C, ldc, k, d, csplit, nullptr, asg, bd,
+                                                   words.p + 0, mode, ver, ver_val);
       ++launches;
     } else {
-      assign_exact_kernel<<<dim3(gx, gy), pb, exact_smem(pb), s>>>(P, ldp, n, list, dcount, C, ldc, k, d, csplit,
-                                                                  keys.p, asg, bd, words.p + 0, mode, nullptr, 0);
+      kern<<<dim3(gx, gy), pb, exact_smem(pb), s>>>(P, ldp, n, list, dcount, C, ldc, k, d, csplit, keys.p, asg, bd,
+                                                    words.p + 0, mode, nullptr, 0);
       resolve_keys_kernel<<<std::min<uint32_t>(blocks(nl, 256), ctx->sm_count * 8), 256, 0, s>>>(
           list, dcount, keys.p, asg, bd, words.p + 0, mode, ver, ver_val);
       launches += 2;
@@ -760,9 +900,9 @@ struct Runner {
     PXC_CUDA(cudaMemsetAsync(words.p, 0, 8 * sizeof(uint32_t), s));
     if (!tensor) {
       const uint32_t pb = exact_block();
-      assign_exact_kernel<<<blocks(n, pb), pb, exact_smem(pb), s>>>(P, ldp, n, nullptr, nullptr, C, ldc, k, d, k,
-                                                                   nullptr, assign.p, bestd.p, words.p + 0, 1,
-                                                                   nullptr, 0);
+      auto kern = unrolled ? assign_exact_kernel<true> : assign_exact_kernel<false>;
+      kern<<<blocks(n, pb), pb, exact_smem(pb), s>>>(P, ldp, n, nullptr, nullptr, C, ldc, k, d, k, nullptr, assign.p,
+                                                     bestd.p, words.p + 0, 1, nullptr, 0);
       ++launches;
       PXC_CUDA(cudaGetLastError());
       return;
@@ -775,22 +915,31 @@ struct Runner {
     const size_t smem = km_tc::smem_bytes(kblocks, stages);
     mark(0);
     if (prior) {
-      pair_l2_kernel<<<blocks(n, 128), 128, 0, s>>>(P, ldp, n, d, C, ldc, assign.p, exact.p);
+      (unrolled ? pair_l2_kernel<true> : pair_l2_kernel<false>)<<<blocks(n, 128), 128, 0, s>>>(P, ldp, n, d, C, ldc,
+                                                                                              assign.p, exact.p);
       bound_kernel<<<blocks(n, 256), 256, 0, s>>>(n, d, pnorm.p, words.p + 4, exact.p, nullptr, bound.p);
     } else {
       km_tc::screen_kernel<true><<<grid, km_tc::NUM_THREADS, smem, s>>>(tmap_p, tmap_c, prm);
       bound_kernel<<<blocks(n, 256), 256, 0, s>>>(n, d, pnorm.p, words.p + 4, nullptr, amin.p, bound.p);
     }
     mark(6);
+    if (ctx->profiling) PXC_CUDA(cudaEventRecord(prof[0], s));
     km_tc::screen_kernel<false><<<grid, km_tc::NUM_THREADS, smem, s>>>(tmap_p, tmap_c, prm);
+    if (ctx->profiling) PXC_CUDA(cudaEventRecord(prof[1], s));
     mark(1);
-    cand_eval_kernel<<<blocks(n, 128), 128, 0, s>>>(P, ldp, n, d, C, ldc, k, cnt.p, cand.p, assign.p, bestd.p,
-                                                    words.p + 0, rescan.p, words.p + 1, 1);
+    (unrolled ? cand_eval_kernel<true> : cand_eval_kernel<false>)<<<blocks(n, 128), 128, 0, s>>>(
+        P, ldp, n, d, C, ldc, k, cnt.p, cand.p, assign.p, bestd.p, words.p + 0, rescan.p, words.p + 1, 1);
     launches += 4;
     PXC_CUDA(cudaGetLastError());
     PXC_CUDA(cudaMemcpyAsync(ctx->h_status, ctx->d_status, 2 * sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
     const uint32_t nres = read_word(1);
     if (ctx->h_status[0]) check_device_status(ctx, s, "k-means screening");
+    ++screen_passes;
+    if (ctx->profiling) {
+      float ms = 0.0f;
+      PXC_CUDA(cudaEventElapsedTime(&ms, prof[0], prof[1]));
+      screen_ms += ms;
+    }
     if (trace) {
       DBuf<uint32_t> hist;
       hist.reserve(10);
@@ -843,16 +992,14 @@ struct Runner {
     }
   }
 
-  Result run(uint32_t max_iter, const float* d_init, uint64_t seed) {
+  Result run(uint32_t max_iter, const float* d_init, ChaCha8* rng) {
     Result r;
     r.k = k;
     r.path = tensor ? 1 : 0;
-    if (d_init) {
+    if (d_init)
       PXC_CUDA(cudaMemcpy2DAsync(cur.p, ldc * 4, d_init, d * 4, d * 4, k, cudaMemcpyDeviceToDevice, s));
-    } else {
-      ChaCha8 rng(seed);
-      seed_kpp(rng);
-    }
+    else
+      seed_kpp(*rng);
     const int sort_bits = std::max(1, 32 - __builtin_clz(std::max<uint32_t>(k - 1, 1)));
     for (uint32_t it = 0; it < max_iter; ++it) {
       r.iterations = it + 1;
@@ -899,7 +1046,7 @@ struct Runner {
   void reseed_empty(Result& r) {
     std::vector<uint32_t> offs(k + 1);
     PXC_CUDA(cudaMemcpyAsync(offs.data(), off.p, (k + 1) * sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
-    pair_l2_kernel<<<blocks(n, 128), 128, 0, s>>>(P, ldp, n, d, next.p, ldc, assign.p, u_next.p);
+    pair_l2_kernel<false><<<blocks(n, 128), 128, 0, s>>>(P, ldp, n, d, next.p, ldc, assign.p, u_next.p);
     // bounds: the exact distance to the old centroid of the point's cluster
     PXC_CUDA(cudaMemcpyAsync(ub.p, bestd.p, n * 4, cudaMemcpyDeviceToDevice, s));
     PXC_CUDA(cudaMemcpyAsync(ubc.p, assign.p, n * 4, cudaMemcpyDeviceToDevice, s));
@@ -920,13 +1067,15 @@ struct Runner {
         PXC_CUDA(cudaMemsetAsync(hist.p, 0, 4096 * sizeof(uint32_t), s));
         ub_hist_kernel<<<ctx->sm_count * 2, 512, 0, s>>>(P, ldp, n, d, next.p, ldc, assign.p, u_next.p, bestd.p, e,
                                                           ub.p, ubc.p, ube.p, hist.p);
-        ub_hist2_kernel<<<ctx->sm_count * 2, 512, 0, s>>>(ub.p, n, hist.p, SEEDS);
-        ub_gather_kernel<<<ctx->sm_count * 4, 256, 0, s>>>(ub.p, n, hist.p, SEEDS, cap, sorted.p, words.p + 3);
+        ub_level1_kernel<<<1, 256, 0, s>>>(hist.p, SEEDS, hist.p + 4096);
+        ub_hist2_kernel<<<ctx->sm_count * 2, 512, 0, s>>>(ub.p, n, hist.p, hist.p + 4096);
+        ub_level2_kernel<<<1, 256, 0, s>>>(hist.p, SEEDS, hist.p + 4096);
+        ub_gather_kernel<<<ctx->sm_count * 4, 256, 0, s>>>(ub.p, n, hist.p + 4096, cap, sorted.p, words.p + 3);
         clamp_count_kernel<<<1, 1, 0, s>>>(words.p + 3, cap);
         exact_list(part.p, sorted.p, words.p + 3, cap, ubc.p, ub.p, 2, ube.p, e);
         argmax_list_kernel<<<ctx->sm_count, 256, 0, s>>>(ub.p, sorted.p, words.p + 3, 0, key.p);
         ub_filter_kernel<<<ctx->sm_count * 4, 256, 0, s>>>(ub.p, n, key.p, rescan.p, words.p + 1);
-        launches += 6;
+        launches += 8;
         return read_word(1);
       };
       uint32_t nl = seed_and_filter();
@@ -956,9 +1105,14 @@ struct Runner {
 
 // `d_pts` has a pitch of `ld` floats. The tensor path needs a 16-byte aligned
 // base and a pitch that is a multiple of 4 floats; other layouts are copied.
-Result kmeans_device(pxc_ctx* ctx, const float* d_pts, uint32_t ld, uint64_t n, uint32_t d, uint32_t k,
-                     uint32_t max_iter, const float* d_init, uint64_t seed, float* d_out_cent,
-                     uint32_t* d_out_assign, cudaStream_t s) {
+// Prepares a Runner over d_pts (pitch ld): validation, layout, workspace.
+// Returns false when there is nothing to cluster (n or d zero).
+static void prepare_runner(Runner& R, pxc_ctx* ctx, const float* d_pts, uint32_t ld, uint64_t n, uint32_t d,
+                           uint32_t k_eff, DBuf<float>& padded, cudaStream_t s, bool allow_tensor);
+
+Result kmeans_impl(pxc_ctx* ctx, const float* d_pts, uint32_t ld, uint64_t n, uint32_t d, uint32_t k,
+                   uint32_t max_iter, const float* d_init, ChaCha8* rng, float* d_out_cent, uint32_t* d_out_assign,
+                   cudaStream_t s) {
   Result r;
   const uint64_t n_eff = d == 0 ? 0 : n;
   const uint32_t k_eff = (uint32_t)std::max<uint64_t>(std::min<uint64_t>(k, n_eff), 1);
@@ -970,15 +1124,29 @@ Result kmeans_device(pxc_ctx* ctx, const float* d_pts, uint32_t ld, uint64_t n, 
   }
   PXC_CONFIG(d <= MAX_DIM, "dim", d, "k-means on the device supports dim <= 512");
   PXC_CONFIG(n <= 0x7FFFFFFFull, "n", n, "k-means on the device supports fewer than 2^31 points");
-  Runner R;
+  Runner R(workspace(ctx));
+  DBuf<float> padded;
+  prepare_runner(R, ctx, d_pts, ld, n, d, k_eff, padded, s, true);
+  r = R.run(max_iter, d_init, rng);
+  r.k = k_eff;
+  r.screen_passes = R.screen_passes;
+  r.screen_ms = R.screen_ms;
+  PXC_CUDA(cudaMemcpy2DAsync(d_out_cent, d * 4, R.cur.p, R.ldc * 4, d * 4, k_eff, cudaMemcpyDeviceToDevice, s));
+  if (d_out_assign) PXC_CUDA(cudaMemcpyAsync(d_out_assign, R.assign.p, n * 4, cudaMemcpyDeviceToDevice, s));
+  PXC_CUDA(cudaStreamSynchronize(s));
+  check_device_status(ctx, s, "k-means");
+  ctx->launches += R.launches;
+  return r;
+}
+
+static void prepare_runner(Runner& R, pxc_ctx* ctx, const float* d_pts, uint32_t ld, uint64_t n, uint32_t d,
+                           uint32_t k_eff, DBuf<float>& padded, cudaStream_t s, bool allow_tensor) {
   R.ctx = ctx;
   R.s = s;
   R.n = n;
   R.d = d;
   R.k = k_eff;
   R.ldc = (d + 3) & ~3u;
-  R.pinned();
-  DBuf<float> padded;
   if ((reinterpret_cast<uintptr_t>(d_pts) & 15) == 0 && (ld & 3) == 0) {
     R.P = d_pts;
     R.ldp = ld;
@@ -1014,15 +1182,35 @@ Result kmeans_device(pxc_ctx* ctx, const float* d_pts, uint32_t ld, uint64_t n, 
   const char* tr = std::getenv("PXC_KMEANS_TRACE");
   R.trace = tr && tr[0] == '1';
 
-  R.setup(want_tensor);
-  r = R.run(max_iter, d_init, seed);
-  r.k = k_eff;
-  PXC_CUDA(cudaMemcpy2DAsync(d_out_cent, d * 4, R.cur.p, R.ldc * 4, d * 4, k_eff, cudaMemcpyDeviceToDevice, s));
-  if (d_out_assign) PXC_CUDA(cudaMemcpyAsync(d_out_assign, R.assign.p, n * 4, cudaMemcpyDeviceToDevice, s));
+  R.setup(want_tensor && allow_tensor);
+}
+
+// kmeans with an explicit seed (k-means++ from ChaCha8Rng::seed_from_u64) or init.
+Result kmeans_device(pxc_ctx* ctx, const float* d_pts, uint32_t ld, uint64_t n, uint32_t d, uint32_t k,
+                     uint32_t max_iter, const float* d_init, uint64_t seed, float* d_out_cent,
+                     uint32_t* d_out_assign, cudaStream_t s) {
+  ChaCha8 rng(seed);
+  return kmeans_impl(ctx, d_pts, ld, n, d, k, max_iter, d_init, d_init ? nullptr : &rng, d_out_cent, d_out_assign, s);
+}
+
+// Exact nearest centroid of every row (ties to the lower index): `unrolled`
+// selects squared_euclidean's 8-lane order (IvfPqIndex's nearest_centroid,
+// ivfpq.rs:1231-1243), else the sequential one. Centroids: k x d, pitch d.
+void nearest_rows(pxc_ctx* ctx, const float* d_pts, uint32_t ld, uint64_t n, uint32_t d, const float* d_cent,
+                  uint32_t k, bool unrolled, uint32_t* d_assign, float* d_dist, cudaStream_t s) {
+  if (n == 0) return;
+  Runner R(workspace(ctx));
+  DBuf<float> padded;
+  R.unrolled = unrolled;
+  prepare_runner(R, ctx, d_pts, ld, n, d, k, padded, s, true);
+  PXC_CUDA(cudaMemcpy2DAsync(R.cur.p, R.ldc * 4, d_cent, d * 4, d * 4, k, cudaMemcpyDeviceToDevice, s));
+  uint64_t rescanned = 0;
+  R.nearest_pass(R.cur.p, false, &rescanned);
+  PXC_CUDA(cudaMemcpyAsync(d_assign, R.assign.p, n * 4, cudaMemcpyDeviceToDevice, s));
+  if (d_dist) PXC_CUDA(cudaMemcpyAsync(d_dist, R.bestd.p, n * 4, cudaMemcpyDeviceToDevice, s));
   PXC_CUDA(cudaStreamSynchronize(s));
-  check_device_status(ctx, s, "k-means");
+  check_device_status(ctx, s, "nearest centroid");
   ctx->launches += R.launches;
-  return r;
 }
 
 void fill_info(pxc_kmeans_info* info, const Result& r) {
@@ -1034,6 +1222,8 @@ void fill_info(pxc_kmeans_info* info, const Result& r) {
   info->path = r.path;
   info->reseeded = r.reseeded;
   info->rescanned = r.rescanned;
+  info->screen_passes = r.screen_passes;
+  info->screen_ms = r.screen_ms;
 }
 
 }  // namespace km

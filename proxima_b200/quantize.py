@@ -28,6 +28,8 @@ class Clustering:
     path: int = 0  # 0 exact CUDA-core assignment, 1 tensor-core screening + exact re-scoring
     reseeded: int = 0
     rescanned: int = 0
+    screen_passes: int = 0
+    screen_ms: float = 0.0
 
 
 def kmeans(points, dim: int, k: int, max_iterations: int, seed: int = 0, init=None,
@@ -61,7 +63,7 @@ def kmeans(points, dim: int, k: int, max_iterations: int, seed: int = 0, init=No
                torch.cuda.current_stream(pts.device).cuda_stream)
         return Clustering(cent.cpu().numpy(), info.inertia, info.iterations,
                           None if assign is None else assign[:n].cpu().numpy().view(np.uint32),
-                          info.path, info.reseeded, info.rescanned)
+                          info.path, info.reseeded, info.rescanned, info.screen_passes, info.screen_ms)
     pts = np.ascontiguousarray(points, dtype=np.float32).reshape(-1)
     n = pts.size // dim if dim else 0
     kk = max(min(k, n), 1)
@@ -76,4 +78,5 @@ def kmeans(points, dim: int, k: int, max_iterations: int, seed: int = 0, init=No
     N.call("pxc_kmeans", ctx.handle, N.ptr(pts), n, dim, k, max_iterations, N.ptr(init_arr), seed,
            N.ptr(cent), N.ptr(assign), C.byref(info))
     return Clustering(cent, info.inertia, info.iterations,
-                      None if assign is None else assign[:n], info.path, info.reseeded, info.rescanned)
+                      None if assign is None else assign[:n], info.path, info.reseeded, info.rescanned,
+                      info.screen_passes, info.screen_ms)

@@ -1,0 +1,102 @@
+"""IVF-PQ search on the GPU (pxc_ivfpq) against the oracle's restatement of
+IvfPqIndex::search_prepared (crates/proxima-index/src/ivfpq.rs:998-1110), on
+the same trained parts: ids, distances and lengths bit for bit, with and
+without reranking, euclidean and cosine, filters, VectorIds that are not the
+slot numbers, dead slots, layouts whose widths are not all equal."""
+import numpy as np
+import pytest
+
+from oracle import pxo
+from proxima_b200 import fixtures
+from proxima_b200.core import Metric
+from proxima_b200.ivfpq import IvfPqIndex
+
+pytestmark = pytest.mark.gpu
+
+
+def _same(got, ref, label):
+    gi, gd, gl = got
+    ri, rd, rl = ref
+    assert np.array_equal(gl, rl), f"{label}: lengths"
+    for q in range(len(rl)):
+        n = int(rl[q])
+        assert np.array_equal(gi[q, :n], ri[q, :n]), f"{label}: ids of query {q}"
+        assert np.array_equal(gd[q, :n].view(np.uint32), rd[q, :n].view(np.uint32)), f"{label}: distances of query {q}"
+
+
+def _build(n, dim, nlist, m, seed, metric=pxo.EUCLIDEAN, nblobs=64):
+    data = fixtures.blobs_u8(n, dim, nblobs, fixtures.C4_CENTRES + seed, fixtures.C4_BASE + seed)
+    if metric == pxo.COSINE:
+        data = data - 127.5
+        data /= np.linalg.norm(data, axis=1, keepdims=True)
+        data = data.astype(np.float32)
+    cent, books, list_of, codes, _ = pxo.ivfpq_train(data, nlist, m, max_iterations=8, training_sample=5000,
+                                                       seed=seed)
+    return data, cent, books, list_of, codes
+
+
+@pytest.mark.parametrize("metric", [pxo.EUCLIDEAN, pxo.COSINE])
+def test_search_matches_oracle(metric):
+    dim, nlist, m = 64, 48, 16
+    data, cent, books, list_of, codes = _build(12000, dim, nlist, m, 1, metric)
+    queries = data[::97][:80] + np.float32(0.25)
+    if metric == pxo.COSINE:
+        queries /= np.linalg.norm(queries, axis=1, keepdims=True)
+    idx = IvfPqIndex(dim, len(cent), m, Metric(metric)).from_parts(cent, books)
+    idx.set_store(data)
+    idx.set_codes(list_of, codes)
+    for nprobe in (1, 4, 16, 100):
+        for rerank in (0, 40):
+            ref = pxo.ivfpq_search(data, cent, books, m, list_of, codes, queries, 10, nprobe, rerank=rerank,
+                                   metric=metric)
+            got = idx.search_batch(queries, 10, nprobe, rerank)
+            _same(got, ref, f"metric {metric} nprobe {nprobe} rerank {rerank}")
+
+
+def test_ids_dead_slots_filter_and_large_k():
+    dim, nlist, m = 64, 32, 8
+    data, cent, books, list_of, codes = _build(9000, dim, nlist, m, 2)
+    rng = np.random.default_rng(5)
+    ids = rng.permutation(np.arange(10**12, 10**12 + 9000, dtype=np.uint64))
+    live = (rng.random(9000) > 0.1).astype(np.uint8)
+    bitmap = np.zeros((9000 + 63) // 64, dtype=np.uint64)
+    keep = np.flatnonzero(rng.random(9000) > 0.3)
+    for s in keep:
+        bitmap[s >> 6] |= np.uint64(1) << np.uint64(s & 63)
+    queries = data[5::151][:40] + np.float32(1.0)
+    idx = IvfPqIndex(dim, nlist, m).from_parts(cent, books)
+    idx.set_store(data, ids=ids, live=live)
+    idx.set_codes(list_of, codes)
+    for k, nprobe, rerank, bm in [(10, 6, 0, None), (10, 6, 30, bitmap), (200, 10, 300, None), (300, 32, 0, bitmap)]:
+        ref = pxo.ivfpq_search(data, cent, books, m, list_of, codes, queries, k, nprobe, rerank=rerank, ids=ids,
+                               live=live, bitmap=bm)
+        got = idx.search_batch(queries, k, nprobe, rerank, bitmap=bm)
+        _same(got, ref, f"k {k} nprobe {nprobe} rerank {rerank} filtered {bm is not None}")
+
+
+def test_uneven_subspace_widths_and_tails():
+    dim, nlist, m = 100, 20, 12  # widths 9 x 4 and 8 x 8; dim % 8 == 4
+    data, cent, books, list_of, codes = _build(5000, dim, nlist, m, 3)
+    queries = data[::123][:30] + np.float32(0.5)
+    idx = IvfPqIndex(dim, nlist, m).from_parts(cent, books)
+    idx.set_store(data)
+    idx.set_codes(list_of, codes)
+    for nprobe, rerank in [(3, 0), (7, 25)]:
+        ref = pxo.ivfpq_search(data, cent, books, m, list_of, codes, queries, 10, nprobe, rerank=rerank)
+        got = idx.search_batch(queries, 10, nprobe, rerank)
+        _same(got, ref, f"nprobe {nprobe} rerank {rerank}")
+
+
+def test_degenerate_calls():
+    dim, nlist, m = 32, 8, 4
+    data, cent, books, list_of, codes = _build(2000, dim, nlist, m, 4)
+    idx = IvfPqIndex(dim, nlist, m).from_parts(cent, books)
+    idx.set_store(data)
+    idx.set_codes(list_of, codes)
+    q = data[:5]
+    _, _, lens = idx.search_batch(q, 0, 4)
+    assert not lens.any()
+    ref = pxo.ivfpq_search(data, cent, books, m, list_of, codes, q, 10, 0)
+    _same(idx.search_batch(q, 10, 0), ref, "nprobe 0 clamps to 1")
+    ref = pxo.ivfpq_search(data, cent, books, m, list_of, codes, q, 10, 99)
+    _same(idx.search_batch(q, 10, 99), ref, "nprobe clamps to nlist")
