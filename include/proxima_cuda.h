@@ -210,7 +210,7 @@ typedef struct pxc_ivfpq pxc_ivfpq;
 pxc_status pxc_ivfpq_create(pxc_ctx* ctx, uint32_t dim, int32_t metric, uint32_t nlist, uint32_t m,
                             pxc_ivfpq** out, pxc_error* err);
 void pxc_ivfpq_destroy(pxc_ivfpq* h);
-/* IvfPqIndex::from_parts (ivfpq.rs:481-508): centroids nlist*dim, codebooks
+/* IvfPqIndex::from_parts (ivfpq.rs:624-717): centroids nlist*dim, codebooks
  * 256*dim (ProductQuantizer::codebooks layout, subspace-major). HOST buffers. */
 pxc_status pxc_ivfpq_set_parts(pxc_ivfpq* h, const float* centroids, const float* codebooks,
                                pxc_error* err);
@@ -223,6 +223,32 @@ pxc_status pxc_ivfpq_set_store(pxc_ivfpq* h, const float* vectors, const uint64_
  * and codes (nslots*m bytes): IvfPqIndex's list_of / codes. HOST buffers. */
 pxc_status pxc_ivfpq_set_codes(pxc_ivfpq* h, const uint32_t* list_of, const uint8_t* codes,
                                pxc_error* err);
+/* encode_all (ivfpq.rs:828-865): every live slot's list (nearest centroid by
+ * squared_euclidean, ties to the lower index) and PQ code of its residual,
+ * lists in ascending slot order. Needs parts and the vectors. */
+pxc_status pxc_ivfpq_encode_all(pxc_ivfpq* h, pxc_error* err);
+/* IvfPqIndex::train (ivfpq.rs:735-825): the stride sample of the live slots
+ * (every ceil(live/training_sample)-th), coarse k-means (k-means++ from
+ * ChaCha8Rng::seed_from_u64(seed)), PQ codebooks on the sample's residuals
+ * with a fresh stream of the same seed advanced across subspaces
+ * (product.rs:198-296), then encode_all. The list count becomes what k-means
+ * produced (nlist clamped to the sample size). */
+typedef struct pxc_ivfpq_report {
+  uint64_t sampled;          /* TrainingReport::sampled */
+  double coarse_inertia;     /* TrainingReport::coarse_inertia */
+  uint64_t coarse_iterations;
+  double residual_inertia;   /* ProductQuantizer::training_inertia */
+  uint64_t populated_lists;
+  uint64_t largest_list;
+  uint64_t produced;         /* lists (centroids) produced */
+  uint64_t pq_iterations;    /* ProductQuantizer::training_iterations */
+} pxc_ivfpq_report;
+pxc_status pxc_ivfpq_train(pxc_ivfpq* h, uint64_t training_sample, uint32_t max_iterations, uint64_t seed,
+                           pxc_ivfpq_report* report, pxc_error* err);
+/* IvfPqIndex::parts (ivfpq.rs:606-617): copies out (each nullable) centroids
+ * nlist*dim, codebooks 256*dim, list_of nslots, codes nslots*m, and nlist. */
+pxc_status pxc_ivfpq_get_parts(pxc_ivfpq* h, float* centroids, float* codebooks, uint32_t* list_of,
+                               uint8_t* codes, uint32_t* out_nlist, pxc_error* err);
 /* IvfPqIndex::search_with_nprobe (ivfpq.rs:981-1110) for a batch of prepared
  * queries: nprobe clamped to [1, nlist] (<= 128), shortlist max(rerank, k)
  * (<= 1024), bitmap over slots or NULL. HOST buffers. */

@@ -46,6 +46,19 @@ class PxcKmeansInfo(C.Structure):
     ]
 
 
+class PxcIvfpqReport(C.Structure):
+    _fields_ = [
+        ("sampled", C.c_uint64),
+        ("coarse_inertia", C.c_double),
+        ("coarse_iterations", C.c_uint64),
+        ("residual_inertia", C.c_double),
+        ("populated_lists", C.c_uint64),
+        ("largest_list", C.c_uint64),
+        ("produced", C.c_uint64),
+        ("pq_iterations", C.c_uint64),
+    ]
+
+
 # name -> (restype, argtypes); every symbol include/proxima_cuda.h declares.
 SIGNATURES: dict[str, tuple] = {
     "pxc_abi_version": (C.c_uint32, []),
@@ -79,6 +92,10 @@ SIGNATURES: dict[str, tuple] = {
     "pxc_ivfpq_set_parts": (C.c_int32, [vp, vp, vp, C.POINTER(PxcError)]),
     "pxc_ivfpq_set_store": (C.c_int32, [vp, vp, vp, vp, C.c_uint64, C.POINTER(PxcError)]),
     "pxc_ivfpq_set_codes": (C.c_int32, [vp, vp, vp, C.POINTER(PxcError)]),
+    "pxc_ivfpq_encode_all": (C.c_int32, [vp, C.POINTER(PxcError)]),
+    "pxc_ivfpq_train": (C.c_int32, [vp, C.c_uint64, C.c_uint32, C.c_uint64, C.POINTER(PxcIvfpqReport),
+                                    C.POINTER(PxcError)]),
+    "pxc_ivfpq_get_parts": (C.c_int32, [vp, vp, vp, vp, vp, C.POINTER(C.c_uint32), C.POINTER(PxcError)]),
     "pxc_ivfpq_search": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, vp, vp, vp, vp,
                                      C.POINTER(PxcError)]),
     "pxc_ivfpq_search_device": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, vp, vp,

@@ -650,6 +650,56 @@ void search_device(pxc_ivfpq* h, const float* d_q, uint32_t nq, uint32_t k, uint
   }
 }
 
+// encode_all (ivfpq.rs:828-865) on the device: list_of = nearest centroid in
+// squared_euclidean's order, codes = PQ code of the residual, lists rebuilt
+// in ascending slot order.
+void encode_all(pxc_ivfpq* h, cudaStream_t s) {
+  pxc_ctx* ctx = h->ctx;
+  const uint64_t n = h->nslots;
+  const uint32_t dim = h->dim, m = h->m;
+  PXC_CONFIG(h->have_parts, "codebooks", 0, "encode needs trained parts");
+  PXC_CONFIG(h->have_vectors, "retain_vectors", 0, "encoding needs the full-precision vectors");
+  h->list_of.reserve(std::max<uint64_t>(1, n));
+  h->codes.reserve(std::max<uint64_t>(16, n * m));
+  if (n) {
+    km::nearest_rows(ctx, h->vectors.p, dim, n, dim, h->centroids.p, h->nlist, true, h->list_of.p, nullptr, s);
+    mask_dead_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(h->list_of.p, h->live.p, n);
+    uint32_t wmax = *std::max_element(h->widths.begin(), h->widths.end());
+    const size_t smem = ((size_t)256 * wmax + 128 * (wmax + 1)) * 4;
+    PXC_CONFIG(smem <= 200 * 1024, "subspaces", m, "subspace too wide for the device encoder");
+    PXC_CUDA(cudaFuncSetAttribute(pq_encode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    pq_encode_kernel<<<dim3((unsigned)((n + 127) / 128), m), 128, smem, s>>>(
+        h->vectors.p, dim, n, h->list_of.p, h->centroids.p, dim, h->codebooks.p, h->woff.p, m, h->codes.p);
+    ctx->launches += 2;
+  }
+  // lists: stable sort of slots by list (unassigned last), boundaries, codes in list order
+  DBuf<uint32_t> slots, keys_out;
+  DBuf<unsigned char> tmp;
+  slots.reserve(std::max<uint64_t>(1, n));
+  keys_out.reserve(std::max<uint64_t>(1, n));
+  h->list_slot.reserve(std::max<uint64_t>(1, n));
+  h->list_off.reserve(h->nlist + 1);
+  h->list_codes.reserve(std::max<uint64_t>(16, n * m));
+  if (n) {
+    iota_u32_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(slots.p, n);
+    size_t tb = 0;
+    PXC_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, tb, h->list_of.p, keys_out.p, slots.p, h->list_slot.p, (int)n, 0,
+                                             32, s));
+    tmp.reserve(tb);
+    PXC_CUDA(cub::DeviceRadixSort::SortPairs(tmp.p, tb, h->list_of.p, keys_out.p, slots.p, h->list_slot.p, (int)n, 0,
+                                             32, s));
+    list_bounds_kernel<<<(h->nlist + 256) / 256, 256, 0, s>>>(keys_out.p, n, h->nlist, h->list_off.p);
+    gather_codes_kernel<<<(unsigned)((n * m + 255) / 256), 256, 0, s>>>(h->codes.p, m, h->list_slot.p, n,
+                                                                       h->list_codes.p);
+    ctx->launches += 4;
+  } else {
+    PXC_CUDA(cudaMemsetAsync(h->list_off.p, 0, (h->nlist + 1) * 4, s));
+  }
+  PXC_CUDA(cudaGetLastError());
+  PXC_CUDA(cudaStreamSynchronize(s));
+  h->have_lists = true;
+}
+
 }  // namespace ivf
 }  // namespace pxc
 
@@ -755,6 +805,8 @@ pxc_status pxc_ivfpq_set_store(pxc_ivfpq* h, const float* vectors, const uint64_
     }
     if (!order.empty())
       PXC_CUDA(cudaMemcpyAsync(h->rank_slot.p, order.data(), order.size() * 4, cudaMemcpyHostToDevice, s));
+    h->live.reserve(std::max<uint64_t>(1, nslots));
+    if (nslots) PXC_CUDA(cudaMemcpyAsync(h->live.p, h->h_live.data(), nslots, cudaMemcpyHostToDevice, s));
     h->have_vectors = vectors != nullptr;
     if (vectors && nslots) {
       h->vectors.reserve(nslots * h->dim);
@@ -772,6 +824,136 @@ pxc_status pxc_ivfpq_set_codes(pxc_ivfpq* h, const uint32_t* list_of, const uint
     DeviceGuard g(h->ctx->device);
     std::vector<uint32_t> lo(list_of, list_of + h->nslots);
     ivf::build_lists(h, lo, codes, h->ctx->stream);
+    h->list_of.reserve(std::max<uint64_t>(1, h->nslots));
+    h->codes.reserve(std::max<uint64_t>(16, h->nslots * h->m));
+    if (h->nslots) {
+      PXC_CUDA(cudaMemcpy(h->list_of.p, list_of, h->nslots * 4, cudaMemcpyHostToDevice));
+      PXC_CUDA(cudaMemcpy(h->codes.p, codes, h->nslots * h->m, cudaMemcpyHostToDevice));
+    }
+  });
+}
+
+pxc_status pxc_ivfpq_encode_all(pxc_ivfpq* h, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(h != nullptr, "h", 0, "null handle");
+    std::lock_guard<std::mutex> lock(h->mu);
+    DeviceGuard g(h->ctx->device);
+    ivf::encode_all(h, h->ctx->stream);
+  });
+}
+
+pxc_status pxc_ivfpq_train(pxc_ivfpq* h, uint64_t training_sample, uint32_t max_iterations, uint64_t seed,
+                           pxc_ivfpq_report* report, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(h != nullptr, "h", 0, "null handle");
+    std::lock_guard<std::mutex> lock(h->mu);
+    DeviceGuard g(h->ctx->device);
+    pxc_ctx* ctx = h->ctx;
+    cudaStream_t s = ctx->stream;
+    const uint32_t dim = h->dim, m = h->m;
+    // ivfpq.rs:736-757
+    PXC_CONFIG(h->have_vectors || h->nlive == 0, "retain_vectors", 0,
+               "training needs the full-precision vectors, which were dropped");
+    std::vector<uint32_t> live;
+    for (uint64_t i = 0; i < h->nslots; ++i)
+      if (h->h_live[i]) live.push_back((uint32_t)i);
+    PXC_CONFIG(!live.empty(), "len", 0, "an empty index has nothing to fit centroids to");
+    PXC_CONFIG(max_iterations >= 1, "max_iterations", max_iterations, "must be at least 1");
+    // the stride sample (ivfpq.rs:762-768): every stride-th live slot
+    const uint64_t stride = std::max<uint64_t>(1, (live.size() + training_sample - 1) / std::max<uint64_t>(1, training_sample));
+    std::vector<uint32_t> pick;
+    for (uint64_t i = 0; i < live.size(); i += stride) pick.push_back(live[i]);
+    const uint64_t ns = pick.size();
+    DBuf<uint32_t> rows;
+    DBuf<float> sample, residuals, cent, proj, book, books;
+    rows.reserve(ns);
+    sample.reserve(ns * dim);
+    PXC_CUDA(cudaMemcpyAsync(rows.p, pick.data(), ns * 4, cudaMemcpyHostToDevice, s));
+    ivf::gather_rows_kernel<<<(unsigned)((ns * dim + 255) / 256), 256, 0, s>>>(h->vectors.p, dim, rows.p, ns, sample.p);
+    // coarse k-means (ivfpq.rs:770-777), ChaCha8 seeded once
+    ChaCha8 rng(seed);
+    const uint32_t produced = (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>(h->nlist, ns));
+    cent.reserve((size_t)produced * dim);
+    km::Result coarse = km::kmeans_impl(ctx, sample.p, dim, ns, dim, h->nlist, max_iterations, nullptr, &rng, cent.p,
+                                        nullptr, s);
+    // residuals of the sample to their nearest centroid (8-lane order)
+    DBuf<uint32_t> near;
+    near.reserve(ns);
+    km::nearest_rows(ctx, sample.p, dim, ns, dim, cent.p, produced, true, near.p, nullptr, s);
+    residuals.reserve(ns * dim);
+    ivf::residual_kernel<<<(unsigned)((ns * dim + 255) / 256), 256, 0, s>>>(sample.p, dim, ns, dim, near.p, cent.p,
+                                                                         residuals.p);
+    // ProductQuantizer::train (product.rs:198-296): one fresh ChaCha8 stream
+    // with the same seed, advanced across subspaces; each codebook padded to
+    // 256 entries by repeating the last centroid
+    ChaCha8 prng(seed);
+    books.reserve((size_t)256 * dim);
+    double residual_inertia = 0.0;
+    uint64_t pq_iterations = 0;
+    for (uint32_t sub = 0; sub < m; ++sub) {
+      const uint32_t w = h->widths[sub], o = h->offsets[sub];
+      const uint32_t ldw = (w + 3) & ~3u;
+      proj.reserve(ns * ldw);
+      ivf::gather_cols_kernel<<<(unsigned)((ns * w + 255) / 256), 256, 0, s>>>(residuals.p, dim, ns, o, w, ldw,
+                                                                             proj.p);
+      book.reserve((size_t)256 * w);
+      km::Result r = km::kmeans_impl(ctx, proj.p, ldw, ns, w, 256, max_iterations, nullptr, &prng, book.p, nullptr, s);
+      residual_inertia += r.inertia;
+      pq_iterations += r.iterations;
+      float* dst = books.p + (size_t)256 * o;
+      PXC_CUDA(cudaMemcpyAsync(dst, book.p, (size_t)r.k * w * 4, cudaMemcpyDeviceToDevice, s));
+      for (uint32_t c = r.k; c < 256; ++c)
+        PXC_CUDA(cudaMemcpyAsync(dst + (size_t)c * w, book.p + (size_t)(r.k - 1) * w, w * 4, cudaMemcpyDeviceToDevice,
+                                 s));
+    }
+    // install the parts (the list count is what k-means produced) and encode
+    h->nlist = produced;
+    h->centroids.reserve((size_t)produced * dim);
+    h->codebooks.reserve((size_t)256 * dim);
+    PXC_CUDA(cudaMemcpyAsync(h->centroids.p, cent.p, (size_t)produced * dim * 4, cudaMemcpyDeviceToDevice, s));
+    PXC_CUDA(cudaMemcpyAsync(h->codebooks.p, books.p, (size_t)256 * dim * 4, cudaMemcpyDeviceToDevice, s));
+    PXC_CUDA(cudaStreamSynchronize(s));
+    h->have_parts = true;
+    ivf::encode_all(h, s);
+    if (report) {
+      std::vector<uint32_t> off(produced + 1);
+      PXC_CUDA(cudaMemcpy(off.data(), h->list_off.p, (produced + 1) * 4, cudaMemcpyDeviceToHost));
+      uint64_t populated = 0, largest = 0;
+      for (uint32_t l = 0; l < produced; ++l) {
+        const uint64_t len = off[l + 1] - off[l];
+        populated += len > 0;
+        largest = std::max(largest, len);
+      }
+      std::memset(report, 0, sizeof(*report));
+      report->sampled = ns;
+      report->coarse_inertia = coarse.inertia;
+      report->coarse_iterations = coarse.iterations;
+      report->residual_inertia = residual_inertia;
+      report->populated_lists = populated;
+      report->largest_list = largest;
+      report->produced = produced;
+      report->pq_iterations = pq_iterations;
+    }
+  });
+}
+
+pxc_status pxc_ivfpq_get_parts(pxc_ivfpq* h, float* centroids, float* codebooks, uint32_t* list_of, uint8_t* codes,
+                               uint32_t* out_nlist, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(h != nullptr, "h", 0, "null handle");
+    std::lock_guard<std::mutex> lock(h->mu);
+    DeviceGuard g(h->ctx->device);
+    cudaStream_t s = h->ctx->stream;
+    if (out_nlist) *out_nlist = h->nlist;
+    if (centroids && h->have_parts)
+      PXC_CUDA(cudaMemcpyAsync(centroids, h->centroids.p, (size_t)h->nlist * h->dim * 4, cudaMemcpyDeviceToHost, s));
+    if (codebooks && h->have_parts)
+      PXC_CUDA(cudaMemcpyAsync(codebooks, h->codebooks.p, (size_t)256 * h->dim * 4, cudaMemcpyDeviceToHost, s));
+    if (list_of && h->nslots && h->list_of.p)
+      PXC_CUDA(cudaMemcpyAsync(list_of, h->list_of.p, h->nslots * 4, cudaMemcpyDeviceToHost, s));
+    if (codes && h->nslots && h->codes.p)
+      PXC_CUDA(cudaMemcpyAsync(codes, h->codes.p, h->nslots * h->m, cudaMemcpyDeviceToHost, s));
+    PXC_CUDA(cudaStreamSynchronize(s));
   });
 }
 

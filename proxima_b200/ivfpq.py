@@ -60,6 +60,26 @@ class IvfPqIndex:
         cd = np.ascontiguousarray(codes, dtype=np.uint8)
         N.call("pxc_ivfpq_set_codes", self.handle, N.ptr(lo), N.ptr(cd))
 
+    def encode_all(self) -> None:
+        N.call("pxc_ivfpq_encode_all", self.handle)
+
+    def train(self, training_sample: int = 100_000, max_iterations: int = 25, seed: int = 0x1FF9C0D):
+        """IvfPqIndex::train on the GPU; returns the TrainingReport fields as a dict."""
+        rep = N.PxcIvfpqReport()
+        N.call("pxc_ivfpq_train", self.handle, training_sample, max_iterations, seed, C.byref(rep))
+        self.nlist = int(rep.produced)
+        return {f: getattr(rep, f) for f, _ in N.PxcIvfpqReport._fields_}
+
+    def parts(self):
+        """(centroids, codebooks, list_of, codes) as the index holds them."""
+        cent = np.zeros((self.nlist, self.dim), dtype=np.float32)
+        books = np.zeros(256 * self.dim, dtype=np.float32)
+        list_of = np.zeros(max(self.nslots, 1), dtype=np.uint32)
+        codes = np.zeros((max(self.nslots, 1), self.m), dtype=np.uint8)
+        nl = C.c_uint32()
+        N.call("pxc_ivfpq_get_parts", self.handle, N.ptr(cent), N.ptr(books), N.ptr(list_of), N.ptr(codes), C.byref(nl))
+        return cent, books, list_of[:self.nslots], codes[:self.nslots]
+
     def search_batch(self, queries, k: int, nprobe: int, rerank: int = 0, bitmap=None):
         q = np.ascontiguousarray(queries, dtype=np.float32).reshape(-1, self.dim)
         nq = len(q)

@@ -100,3 +100,43 @@ def test_degenerate_calls():
     _same(idx.search_batch(q, 10, 0), ref, "nprobe 0 clamps to 1")
     ref = pxo.ivfpq_search(data, cent, books, m, list_of, codes, q, 10, 99)
     _same(idx.search_batch(q, 10, 99), ref, "nprobe clamps to nlist")
+
+
+def test_encode_all_matches_oracle():
+    dim, nlist, m = 64, 300, 16  # nlist >= 256: the coarse assignment takes the tensor-core screen
+    data, cent, books, list_of, codes = _build(20000, dim, nlist, m, 5)
+    rng = np.random.default_rng(2)
+    live = (rng.random(len(data)) > 0.05).astype(np.uint8)
+    idx = IvfPqIndex(dim, len(cent), m).from_parts(cent, books)
+    idx.set_store(data, live=live)
+    idx.encode_all()
+    _, _, g_list, g_codes = idx.parts()
+    r_list = np.zeros(len(data), np.uint32)
+    r_codes = np.zeros((len(data), m), np.uint8)
+    from oracle.pxo import lib, _p
+    lib().pxo_ivfpq_encode_all(_p(data), _p(live), len(data), dim, _p(cent), len(cent), _p(books), m,
+                               _p(r_list), _p(r_codes), 8)
+    assert np.array_equal(g_list, r_list)
+    assert np.array_equal(g_codes[live == 1], r_codes[live == 1])
+    queries = data[::211][:30]
+    ref = pxo.ivfpq_search(data, cent, books, m, r_list, r_codes, queries, 10, 8, rerank=20, live=live)
+    _same(idx.search_batch(queries, 10, 8, 20), ref, "search after a device encode")
+
+
+@pytest.mark.parametrize("nlist", [40, 300])
+def test_train_matches_oracle(nlist):
+    dim, m = 32, 8
+    data = fixtures.blobs_u8(12000, dim, 80, fixtures.C4_CENTRES + 9, fixtures.C4_BASE + 9)
+    cent, books, list_of, codes, rep = pxo.ivfpq_train(data, nlist, m, max_iterations=6, training_sample=3000,
+                                                       seed=0x1FF9C0D)
+    idx = IvfPqIndex(dim, nlist, m)
+    idx.set_store(data)
+    got = idx.train(training_sample=3000, max_iterations=6, seed=0x1FF9C0D)
+    g_cent, g_books, g_list, g_codes = idx.parts()
+    assert got["sampled"] == rep.sampled and got["produced"] == len(cent)
+    assert np.array_equal(g_cent.view(np.uint32), cent.view(np.uint32))
+    assert np.array_equal(g_books.view(np.uint32), books.view(np.uint32))
+    assert np.array_equal(g_list, list_of) and np.array_equal(g_codes, codes)
+    assert got["coarse_iterations"] == rep.coarse_iterations
+    assert got["coarse_inertia"] == rep.coarse_inertia and got["residual_inertia"] == rep.residual_inertia
+    assert got["populated_lists"] == rep.populated_lists and got["largest_list"] == rep.largest_list
