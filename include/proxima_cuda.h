@@ -219,6 +219,14 @@ pxc_status pxc_ivfpq_set_parts(pxc_ivfpq* h, const float* centroids, const float
  * slot), `live` one byte per slot (NULL: all live). HOST buffers. Clears the lists. */
 pxc_status pxc_ivfpq_set_store(pxc_ivfpq* h, const float* vectors, const uint64_t* ids,
                                const uint8_t* live, uint64_t nslots, pxc_error* err);
+/* Same, with the vectors in DEVICE memory (copied); ids and live on the host. */
+pxc_status pxc_ivfpq_set_store_device(pxc_ivfpq* h, const float* d_vectors, const uint64_t* ids,
+                                      const uint8_t* live, uint64_t nslots, pxc_error* err);
+/* Duration of the last search's scan kernel (K5/K6) when it ran as one batch
+ * with profiling on; -1 otherwise. */
+float pxc_ivfpq_last_scan_ms(pxc_ivfpq* h);
+/* PQ codes the last search scored, summed over its queries (synchronising). */
+uint64_t pxc_ivfpq_last_scanned(pxc_ivfpq* h);
 /* The lists from per-slot assignments (list_of, 0xFFFFFFFF = unassigned)
  * and codes (nslots*m bytes): IvfPqIndex's list_of / codes. HOST buffers. */
 pxc_status pxc_ivfpq_set_codes(pxc_ivfpq* h, const uint32_t* list_of, const uint8_t* codes,
@@ -251,7 +259,7 @@ pxc_status pxc_ivfpq_get_parts(pxc_ivfpq* h, float* centroids, float* codebooks,
                                uint8_t* codes, uint32_t* out_nlist, pxc_error* err);
 /* IvfPqIndex::search_with_nprobe (ivfpq.rs:981-1110) for a batch of prepared
  * queries: nprobe clamped to [1, nlist] (<= 128), shortlist max(rerank, k)
- * (<= 1024), bitmap over slots or NULL. HOST buffers. */
+ * (<= 4096), bitmap over slots or NULL. HOST buffers. */
 pxc_status pxc_ivfpq_search(pxc_ivfpq* h, const float* queries, uint32_t nq, uint32_t k,
                             uint32_t nprobe, uint32_t rerank, const uint64_t* bitmap,
                             uint64_t* out_ids, float* out_dist, uint32_t* out_len, pxc_error* err);

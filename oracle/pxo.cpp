@@ -773,9 +773,28 @@ void pxo_ivfpq_search(const float* vectors, const uint64_t* ids, const uint8_t* 
                       const uint64_t* bitmap, uint64_t* out_ids, float* out_dist,
                       uint32_t* out_len, int threads) {
   // lists in ascending slot order (encode_all pushes slots in order)
-  std::vector<std::vector<uint32_t>> lists(nlist);
+  std::vector<uint32_t> off(nlist + 1, 0), slot;
   for (uint64_t s = 0; s < nslots; ++s)
-    if ((!live || live[s]) && list_of[s] != 0xFFFFFFFFu) lists[list_of[s]].push_back(static_cast<uint32_t>(s));
+    if ((!live || live[s]) && list_of[s] != 0xFFFFFFFFu) ++off[list_of[s] + 1];
+  for (uint64_t l = 0; l < nlist; ++l) off[l + 1] += off[l];
+  slot.resize(off[nlist]);
+  std::vector<uint32_t> fill(off.begin(), off.end() - 1);
+  for (uint64_t s = 0; s < nslots; ++s)
+    if ((!live || live[s]) && list_of[s] != 0xFFFFFFFFu) slot[fill[list_of[s]]++] = static_cast<uint32_t>(s);
+  pxo_ivfpq_search_csr(vectors, ids, live, nslots, dim, metric, centroids, nlist, codebooks, m, off.data(),
+                       slot.data(), codes, queries, nq, k, nprobe, rerank, bitmap, out_ids, out_dist, out_len,
+                       threads);
+}
+
+// The same search over lists given as CSR (list_off[nlist+1], list_slot[]
+// ascending within each list), as the index holds them between searches.
+void pxo_ivfpq_search_csr(const float* vectors, const uint64_t* ids, const uint8_t* live,
+                          uint64_t nslots, uint64_t dim, int metric, const float* centroids,
+                          uint64_t nlist, const float* codebooks, uint64_t m,
+                          const uint32_t* list_off, const uint32_t* list_slot, const uint8_t* codes,
+                          const float* queries, uint64_t nq, uint64_t k, uint64_t nprobe, uint64_t rerank,
+                          const uint64_t* bitmap, uint64_t* out_ids, float* out_dist,
+                          uint32_t* out_len, int threads) {
   nprobe = std::min<uint64_t>(std::max<uint64_t>(nprobe, 1), std::max<uint64_t>(nlist, 1));
   std::unordered_map<uint64_t, uint64_t> by_id;
   if (ids && rerank > 0)
@@ -807,7 +826,8 @@ void pxo_ivfpq_search(const float* vectors, const uint64_t* ids, const uint8_t* 
         } else {
           qdc = dot_unrolled(qv, c, dim);
         }
-        for (uint32_t s : lists[l]) {
+        for (uint32_t j = list_off[l]; j < list_off[l + 1]; ++j) {
+          const uint32_t s = list_slot[j];
           if (!bit_set(bitmap, s)) continue;
           const uint8_t* code = codes + static_cast<uint64_t>(s) * m;
           float score = cosine ? (1.0f - qdc) + pxo_pq_adc_inner(table.data(), m, code)

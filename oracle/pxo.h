@@ -138,6 +138,13 @@ void pxo_ivfpq_encode_all(const float* vectors, const uint8_t* live, uint64_t ns
 /* search_prepared (ivfpq.rs:998-1110) for nq prepared queries. Lists are the
  * slots with list_of[s]==l in ascending slot order. vectors may be NULL when
  * rerank==0. metric is PXO_EUCLIDEAN or PXO_COSINE. */
+void pxo_ivfpq_search_csr(const float* vectors, const uint64_t* ids, const uint8_t* live,
+                          uint64_t nslots, uint64_t dim, int metric, const float* centroids,
+                          uint64_t nlist, const float* codebooks, uint64_t m,
+                          const uint32_t* list_off, const uint32_t* list_slot, const uint8_t* codes,
+                          const float* queries, uint64_t nq, uint64_t k, uint64_t nprobe, uint64_t rerank,
+                          const uint64_t* bitmap, uint64_t* out_ids, float* out_dist,
+                          uint32_t* out_len, int threads);
 void pxo_ivfpq_search(const float* vectors, const uint64_t* ids, const uint8_t* live,
                       uint64_t nslots, uint64_t dim, int metric, const float* centroids,
                       uint64_t nlist, const float* codebooks, uint64_t m,

@@ -83,6 +83,8 @@ def lib():
             "pxo_ivfpq_encode_all": (None, [vp, vp, u64, u64, vp, u64, vp, u64, vp, vp, i32]),
             "pxo_ivfpq_search": (None, [vp, vp, vp, u64, u64, i32, vp, u64, vp, u64, vp, vp, vp, u64,
                                         u64, u64, u64, vp, vp, vp, vp, i32]),
+            "pxo_ivfpq_search_csr": (None, [vp, vp, vp, u64, u64, i32, vp, u64, vp, u64, vp, vp, vp, vp, u64,
+                                        u64, u64, u64, vp, vp, vp, vp, i32]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -305,4 +307,24 @@ def ivfpq_search(vectors, centroids, books, m: int, list_of, codes, queries, k: 
     lib().pxo_ivfpq_search(_p(v), _p(ids), _p(live), nslots, dim, metric, _p(cent), cent.shape[0],
                            _p(f32a(books)), m, _p(lo), _p(cd), _p(q), nq, k, nprobe, rerank, _p(bitmap),
                            _p(out_ids), _p(out_d), _p(out_len), nthreads or threads())
+    return out_ids[:, :k], out_d[:, :k], out_len
+
+
+def ivfpq_search_csr(vectors, centroids, books, m: int, list_off, list_slot, codes, queries, k: int, nprobe: int,
+                     rerank: int = 0, metric: int = EUCLIDEAN, nthreads=None):
+    """ivfpq_search over prebuilt lists (CSR), slots as ids, all live."""
+    v = None if vectors is None else f32a(vectors)
+    q = f32a(queries)
+    nq, dim = q.shape
+    cent = f32a(centroids)
+    kk = max(k, 1)
+    out_ids = np.zeros((nq, kk), dtype=np.uint64)
+    out_d = np.zeros((nq, kk), dtype=np.float32)
+    out_len = np.zeros(nq, dtype=np.uint32)
+    lo = np.ascontiguousarray(list_off, dtype=np.uint32)
+    ls = np.ascontiguousarray(list_slot, dtype=np.uint32)
+    cd = np.ascontiguousarray(codes, dtype=np.uint8)
+    lib().pxo_ivfpq_search_csr(_p(v), None, None, len(cd), dim, metric, _p(cent), cent.shape[0], _p(f32a(books)), m,
+                               _p(lo), _p(ls), _p(cd), _p(q), nq, k, nprobe, rerank, None, _p(out_ids), _p(out_d),
+                               _p(out_len), nthreads or threads())
     return out_ids[:, :k], out_d[:, :k], out_len

@@ -91,6 +91,9 @@ SIGNATURES: dict[str, tuple] = {
     "pxc_ivfpq_destroy": (None, [vp]),
     "pxc_ivfpq_set_parts": (C.c_int32, [vp, vp, vp, C.POINTER(PxcError)]),
     "pxc_ivfpq_set_store": (C.c_int32, [vp, vp, vp, vp, C.c_uint64, C.POINTER(PxcError)]),
+    "pxc_ivfpq_set_store_device": (C.c_int32, [vp, vp, vp, vp, C.c_uint64, C.POINTER(PxcError)]),
+    "pxc_ivfpq_last_scan_ms": (C.c_float, [vp]),
+    "pxc_ivfpq_last_scanned": (C.c_uint64, [vp]),
     "pxc_ivfpq_set_codes": (C.c_int32, [vp, vp, vp, C.POINTER(PxcError)]),
     "pxc_ivfpq_encode_all": (C.c_int32, [vp, C.POINTER(PxcError)]),
     "pxc_ivfpq_train": (C.c_int32, [vp, C.c_uint64, C.c_uint32, C.c_uint64, C.POINTER(PxcIvfpqReport),

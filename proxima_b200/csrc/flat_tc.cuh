@@ -160,7 +160,15 @@ __device__ __forceinline__ void seed_from_finished(const Params& p, uint32_t qti
 #pragma unroll
     for (int j = 0; j < KT; ++j) {
       const int32_t r = static_cast<int32_t>(static_cast<uint32_t>(keys[j] >> 32) - R_OFFSET);
-      if (r < lr[KT - 1]) insert_sorted<KT>(lr, lk, r, static_cast<uint32_t>(keys[j]));
+      if (!(r < lr[KT - 1])) continue;
+      // A finished split's list may already hold entries it seeded from a
+      // third split: admit each rank once, or the list (and the bound it
+      // publishes) would rest on fewer than KT distinct candidates.
+      const uint32_t rank = static_cast<uint32_t>(keys[j]);
+      bool dup = false;
+#pragma unroll
+      for (int i = 0; i < KT; ++i) dup |= lk[i] == rank && lr[i] == r;
+      if (!dup) insert_sorted<KT>(lr, lk, r, rank);
     }
   }
 }

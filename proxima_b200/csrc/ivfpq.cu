@@ -45,11 +45,11 @@ namespace ivf {
 
 constexpr uint32_t UNASSIGNED = 0xFFFFFFFFu;
 constexpr uint32_t MAX_NPROBE = 128;
-constexpr uint32_t MAX_SHORTLIST = 1024;
+constexpr uint32_t MAX_SHORTLIST = 4096;
 constexpr uint32_t MAX_M = 64;
 constexpr uint32_t MAX_DIM = 1024;
 constexpr uint32_t SCAN_THREADS = 256;
-constexpr uint32_t CB = 4096;     // candidate buffer per query
+constexpr uint32_t CB_MAX = 8192; // candidate buffer per query (shared memory), largest
 constexpr uint32_t CHUNK = 1024;  // codes scored between buffer checks
 constexpr uint32_t QB = 64;       // queries per coarse block
 constexpr uint32_t TCC = 32;      // centroids per coarse smem tile
@@ -105,6 +105,8 @@ __device__ __forceinline__ float space_distance(int metric, const float* a, cons
 // transposed into shared memory) x one range of centroids (blockIdx.y); each
 // thread keeps its P best (distance, list) keys sorted in shared memory.
 // ---------------------------------------------------------------------------
+constexpr uint32_t TCS = TCC + 4;  // row stride of the transposed centroid tile (16-byte multiple)
+
 __global__ void __launch_bounds__(QB) coarse_partial_kernel(const float* __restrict__ Q, uint32_t nq, uint32_t dim,
                                                             const float* __restrict__ C, uint32_t nlist,
                                                             uint32_t crange, uint32_t P,
@@ -112,7 +114,7 @@ __global__ void __launch_bounds__(QB) coarse_partial_kernel(const float* __restr
   extern __shared__ __align__(16) unsigned char sm_raw[];
   uint64_t* best = reinterpret_cast<uint64_t*>(sm_raw);                 // [P][QB]
   float* qs = reinterpret_cast<float*>(best + (size_t)P * QB);          // [dim][QB+1]
-  float* cs = qs + (((size_t)dim * (QB + 1) + 3) & ~size_t(3));         // [TCC][dim]
+  float* cs = qs + (((size_t)dim * (QB + 1) + 3) & ~size_t(3));         // [dim][TCS]
   const uint32_t t = threadIdx.x;
   const uint32_t q0 = blockIdx.x * QB;
   const uint32_t qi = q0 + t;
@@ -122,56 +124,64 @@ __global__ void __launch_bounds__(QB) coarse_partial_kernel(const float* __restr
   }
   for (uint32_t j = 0; j < P; ++j) best[j * QB + t] = ~0ull;
   uint32_t have = 0;
+  const uint32_t full = dim & ~7u;
+  auto insert = [&](uint64_t key) {
+    if (have < P || key < best[(P - 1) * QB + t]) {
+      uint32_t pos = have < P ? have++ : P - 1;
+      while (pos > 0 && best[(pos - 1) * QB + t] > key) {
+        best[pos * QB + t] = best[(pos - 1) * QB + t];
+        --pos;
+      }
+      best[pos * QB + t] = key;
+    }
+  };
   const uint32_t cbeg = blockIdx.y * crange, cend = min(nlist, cbeg + crange);
   for (uint32_t c0 = cbeg; c0 < cend; c0 += TCC) {
     const uint32_t cnt = min(TCC, cend - c0);
     __syncthreads();
     for (uint32_t e = t; e < TCC * dim; e += QB) {
       const uint32_t j = e / dim, i = e - j * dim;
-      cs[j * dim + i] = j < cnt ? C[(size_t)(c0 + j) * dim + i] : 0.0f;
+      cs[i * TCS + j] = j < cnt ? C[(size_t)(c0 + j) * dim + i] : 0.0f;
     }
     __syncthreads();
     if (qi >= nq) continue;
-    for (uint32_t j = 0; j < cnt; ++j) {
-      const float* c = cs + j * dim;
-      float acc[8];
+    // four centroids at a time: one query load and one 16-byte centroid load per
+    // dimension feed twelve operations; each centroid keeps its own eight lane sums
+    for (uint32_t j0 = 0; j0 < cnt; j0 += 4) {
+      float acc[4][8];
 #pragma unroll
-      for (int l = 0; l < 8; ++l) acc[l] = 0.0f;
-      const uint32_t full = dim & ~7u;
-      const bool vec4 = (dim & 3) == 0;  // rows of the tile 16-byte aligned
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int l = 0; l < 8; ++l) acc[u][l] = 0.0f;
       for (uint32_t i = 0; i < full; i += 8) {
-        float cv[8];
-        if (vec4) {
-          const float4 c0v = *reinterpret_cast<const float4*>(c + i);
-          const float4 c1v = *reinterpret_cast<const float4*>(c + i + 4);
-          cv[0] = c0v.x, cv[1] = c0v.y, cv[2] = c0v.z, cv[3] = c0v.w;
-          cv[4] = c1v.x, cv[5] = c1v.y, cv[6] = c1v.z, cv[7] = c1v.w;
-        } else {
-#pragma unroll
-          for (int l = 0; l < 8; ++l) cv[l] = c[i + l];
-        }
 #pragma unroll
         for (int l = 0; l < 8; ++l) {
-          const float d = __fsub_rn(qs[(i + l) * (QB + 1) + t], cv[l]);
-          acc[l] = __fadd_rn(acc[l], __fmul_rn(d, d));
+          const float qv = qs[(i + l) * (QB + 1) + t];
+          const float4 c4 = *reinterpret_cast<const float4*>(cs + (i + l) * TCS + j0);
+          const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float d = __fsub_rn(qv, cv[u]);
+            acc[u][l] = __fadd_rn(acc[u][l], __fmul_rn(d, d));
+          }
         }
       }
-      float tail = 0.0f;
+      float tail[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       for (uint32_t i = full; i < dim; ++i) {
-        const float d = __fsub_rn(qs[i * (QB + 1) + t], c[i]);
-        tail = __fadd_rn(tail, __fmul_rn(d, d));
-      }
-      const float x = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
-      const float y = __fadd_rn(__fadd_rn(acc[4], acc[5]), __fadd_rn(acc[6], acc[7]));
-      const float dist = __fadd_rn(__fadd_rn(x, y), tail);
-      const uint64_t key = ((uint64_t)order_key(dist) << 32) | (c0 + j);
-      if (have < P || key < best[(P - 1) * QB + t]) {
-        uint32_t pos = have < P ? have++ : P - 1;
-        while (pos > 0 && best[(pos - 1) * QB + t] > key) {
-          best[pos * QB + t] = best[(pos - 1) * QB + t];
-          --pos;
+        const float qv = qs[i * (QB + 1) + t];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float d = __fsub_rn(qv, cs[i * TCS + j0 + u]);
+          tail[u] = __fadd_rn(tail[u], __fmul_rn(d, d));
         }
-        best[pos * QB + t] = key;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (j0 + u >= cnt) break;
+        const float x = __fadd_rn(__fadd_rn(acc[u][0], acc[u][1]), __fadd_rn(acc[u][2], acc[u][3]));
+        const float y = __fadd_rn(__fadd_rn(acc[u][4], acc[u][5]), __fadd_rn(acc[u][6], acc[u][7]));
+        const float dist = __fadd_rn(__fadd_rn(x, y), tail[u]);
+        insert(((uint64_t)order_key(dist) << 32) | (c0 + j0 + u));
       }
     }
   }
@@ -244,7 +254,7 @@ __device__ uint64_t select_keep(uint64_t* buf, uint32_t cnt, uint32_t K, uint32_
     __syncthreads();
   }
   // keep the keys <= prefix (exactly K of them)
-  constexpr uint32_t PER = CB / SCAN_THREADS;
+  constexpr uint32_t PER = CB_MAX / SCAN_THREADS;
   uint64_t mine[PER];
   uint32_t nmine = 0;
   for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x)
@@ -266,7 +276,7 @@ struct ScanParams {
   const uint32_t* list_off;
   const uint32_t* list_slot;
   const uint8_t* list_codes;
-  const uint32_t* slot_rank;  // VectorId rank of each slot
+  const uint32_t* list_rank;  // VectorId rank of each list entry (list order)
   const uint32_t* rank_slot;
   const uint64_t* ids;        // VectorId per slot
   const float* vectors;       // nullable: no rerank
@@ -274,7 +284,9 @@ struct ScanParams {
   uint64_t* out_ids;
   float* out_dist;
   uint32_t* out_len;
+  unsigned long long* scanned;  // codes scored, summed over queries
   uint32_t nq, dim, m, nprobe, k, shortlist;
+  uint32_t cb;  // candidate buffer entries (a power of two >= 2 * shortlist, >= CHUNK + shortlist)
   int metric;
   int rerank;
 };
@@ -282,6 +294,7 @@ struct ScanParams {
 // K5 + K6: one CTA per query.
 __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(const ScanParams p) {
   extern __shared__ __align__(16) unsigned char sm_raw[];
+  const uint32_t CB = p.cb;
   uint64_t* buf = reinterpret_cast<uint64_t*>(sm_raw);  // [CB]
   float* lut = reinterpret_cast<float*>(buf + CB);      // [m][256]
   float* qs = lut + (size_t)p.m * 256;                  // [dim]
@@ -336,6 +349,7 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(const ScanParams p) 
     __syncthreads();
     const float one_minus = cosine ? __fsub_rn(1.0f, qdc) : 0.0f;
     const uint32_t b = p.list_off[l], e = p.list_off[l + 1];
+    if (t == 0 && p.scanned) atomicAdd(p.scanned, (unsigned long long)(e - b));
     for (uint32_t j0 = b; j0 < e; j0 += CHUNK) {
       if (count > CB - CHUNK) {
         const uint64_t kth = select_keep(buf, count, p.shortlist, hist, sh);
@@ -347,24 +361,50 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(const ScanParams p) 
       }
       const uint64_t th = thr;
       const uint32_t j1 = min(e, j0 + CHUNK);
-      for (uint32_t j = j0 + t; j < j1; j += blockDim.x) {
-        const uint32_t slot = p.list_slot[j];
-        if (p.bitmap && !((p.bitmap[slot >> 6] >> (slot & 63)) & 1ull)) continue;
-        const uint8_t* code = p.list_codes + (size_t)j * m;
-        float sum = 0.0f;
-        if ((m & 15) == 0) {
-          for (uint32_t s0 = 0; s0 < m; s0 += 16) {
-            const uint4 v = __ldg(reinterpret_cast<const uint4*>(code + s0));
-            const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+      // four codes per thread at once: four independent lookup chains
+      constexpr int U = CHUNK / SCAN_THREADS;
+      uint32_t jj[U];
+      bool on[U];
+      float sum[U];
 #pragma unroll
-            for (int u = 0; u < 16; ++u)
-              sum = __fadd_rn(sum, lut[(s0 + u) * 256 + ((w4[u >> 2] >> (8 * (u & 3))) & 255u)]);
-          }
-        } else {
-          for (uint32_t s = 0; s < m; ++s) sum = __fadd_rn(sum, lut[s * 256 + code[s]]);
+      for (int u = 0; u < U; ++u) {
+        jj[u] = j0 + t + u * SCAN_THREADS;
+        on[u] = jj[u] < j1;
+        sum[u] = 0.0f;
+        if (on[u] && p.bitmap) {
+          const uint32_t slot = p.list_slot[jj[u]];
+          on[u] = (p.bitmap[slot >> 6] >> (slot & 63)) & 1ull;
         }
-        const float score = cosine ? __fadd_rn(one_minus, -sum) : sum;
-        const uint64_t key = ((uint64_t)order_key(score) << 32) | p.slot_rank[slot];
+      }
+      if ((m & 15) == 0) {
+        for (uint32_t s0 = 0; s0 < m; s0 += 16) {
+          uint32_t w4[U][4];
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (on[u]) v = __ldg(reinterpret_cast<const uint4*>(p.list_codes + (size_t)jj[u] * m + s0));
+            w4[u][0] = v.x, w4[u][1] = v.y, w4[u][2] = v.z, w4[u][3] = v.w;
+          }
+#pragma unroll
+          for (int b = 0; b < 16; ++b) {
+            const float* row = lut + (s0 + b) * 256;
+#pragma unroll
+            for (int u = 0; u < U; ++u) sum[u] = __fadd_rn(sum[u], row[(w4[u][b >> 2] >> (8 * (b & 3))) & 255u]);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (on[u]) {
+            const uint8_t* code = p.list_codes + (size_t)jj[u] * m;
+            for (uint32_t s2 = 0; s2 < m; ++s2) sum[u] = __fadd_rn(sum[u], lut[s2 * 256 + code[s2]]);
+          }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (!on[u]) continue;
+        const float score = cosine ? __fadd_rn(one_minus, -sum[u]) : sum[u];
+        const uint64_t key = ((uint64_t)order_key(score) << 32) | p.list_rank[jj[u]];
         if (key < th) buf[atomicAdd(&count, 1u)] = key;
       }
       __syncthreads();
@@ -478,6 +518,13 @@ __global__ void gather_cols_kernel(const float* __restrict__ X, uint32_t dim, ui
   out[i * ldo + t] = X[i * dim + o + t];
 }
 
+// Id rank of each list entry, in list order.
+__global__ void list_rank_kernel(const uint32_t* __restrict__ list_slot, const uint32_t* __restrict__ slot_rank,
+                                 uint64_t n, uint32_t* __restrict__ out) {
+  const uint64_t j = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (j < n) out[j] = slot_rank[list_slot[j]];
+}
+
 // Dead slots take no list.
 __global__ void mask_dead_kernel(uint32_t* __restrict__ list_of, const uint8_t* __restrict__ live, uint64_t n) {
   const uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
@@ -529,7 +576,9 @@ struct pxc_ivfpq {
   std::vector<uint8_t> h_live;
   pxc::DBuf<uint64_t> ids;
   pxc::DBuf<uint32_t> slot_rank, rank_slot;
-  pxc::DBuf<uint32_t> list_off, list_slot, list_of;
+  pxc::DBuf<uint32_t> list_off, list_slot, list_of, list_rank;
+  pxc::DBuf<unsigned long long> scanned;
+  unsigned long long* h_scanned = nullptr;  // pinned
   pxc::DBuf<uint8_t> list_codes, codes, live;
   bool have_lists = false;
   pxc::DBuf<float> q_buf;
@@ -537,7 +586,14 @@ struct pxc_ivfpq {
   pxc::DBuf<uint64_t> partial, io_ids, bitmap;
   pxc::DBuf<float> io_dist;
   pxc::DBuf<uint32_t> io_len;
+  cudaEvent_t ev_begin = nullptr, ev_end = nullptr;  // scan timing when the context profiles
+  bool timed = false;
   std::mutex mu;
+  ~pxc_ivfpq() {
+    if (h_scanned) cudaFreeHost(h_scanned);
+    if (ev_begin) cudaEventDestroy(ev_begin);
+    if (ev_end) cudaEventDestroy(ev_end);
+  }
 };
 
 namespace pxc {
@@ -579,6 +635,10 @@ void build_lists(pxc_ivfpq* h, const std::vector<uint32_t>& list_of, const uint8
     PXC_CUDA(cudaMemcpyAsync(h->list_slot.p, slot.data(), total * 4, cudaMemcpyHostToDevice, s));
     PXC_CUDA(cudaMemcpyAsync(h->list_codes.p, lc.data(), total * h->m, cudaMemcpyHostToDevice, s));
   }
+  h->list_rank.reserve(std::max<uint64_t>(1, total));
+  if (total)
+    list_rank_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(h->list_slot.p, h->slot_rank.p, total,
+                                                                      h->list_rank.p);
   PXC_CUDA(cudaStreamSynchronize(s));
   h->have_lists = true;
 }
@@ -596,7 +656,7 @@ void search_device(pxc_ivfpq* h, const float* d_q, uint32_t nq, uint32_t k, uint
   PXC_CONFIG(nprobe <= MAX_NPROBE, "nprobe", nprobe, "the device search supports nprobe <= 128");
   const uint32_t shortlist = rerank > 0 ? std::max(rerank, k) : k;
   PXC_CONFIG(shortlist <= MAX_SHORTLIST, "rerank", shortlist,
-             "the device search keeps at most 1024 candidates per query (max(rerank, k))");
+             "the device search keeps at most 4096 candidates per query (max(rerank, k))");
   const uint32_t dim = h->dim, nlist = h->nlist;
   // K4: coarse
   const uint32_t P = nprobe;
@@ -605,14 +665,23 @@ void search_device(pxc_ivfpq* h, const float* d_q, uint32_t nq, uint32_t k, uint
   const uint32_t batch = 16384;
   h->probes.reserve((size_t)std::min(nq, batch) * nprobe);
   h->partial.reserve((size_t)std::min(nq, batch) * parts * P);
-  const size_t smem_c = (size_t)P * QB * 8 + ((((size_t)dim * (QB + 1) + 3) & ~size_t(3)) + (size_t)TCC * dim) * 4;
+  const size_t smem_c = (size_t)P * QB * 8 + ((((size_t)dim * (QB + 1) + 3) & ~size_t(3)) + (size_t)TCS * dim) * 4;
   PXC_CUDA(cudaFuncSetAttribute(coarse_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_c));
   uint32_t n2 = 1;
   while (n2 < parts * P) n2 <<= 1;
   const size_t smem_m = (size_t)n2 * 8;
   PXC_CUDA(cudaFuncSetAttribute(coarse_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_m));
-  const size_t smem_s = (size_t)CB * 8 + ((size_t)h->m * 256 + 2 * dim) * 4 + (2 * h->m + 1) * 4;
+  uint32_t cb = 4096;
+  while (cb < 2 * shortlist || cb < CHUNK + shortlist) cb <<= 1;
+  const size_t smem_s = (size_t)cb * 8 + ((size_t)h->m * 256 + 2 * dim) * 4 + (2 * h->m + 1) * 4;
   PXC_CUDA(cudaFuncSetAttribute(scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_s));
+  if (ctx->profiling) {
+    if (!h->ev_begin) PXC_CUDA(cudaEventCreate(&h->ev_begin));
+    if (!h->ev_end) PXC_CUDA(cudaEventCreate(&h->ev_end));
+  }
+  h->timed = false;
+  h->scanned.reserve(1);
+  PXC_CUDA(cudaMemsetAsync(h->scanned.p, 0, sizeof(unsigned long long), s));
   for (uint32_t q0 = 0; q0 < nq; q0 += batch) {
     const uint32_t nb = std::min(batch, nq - q0);
     const float* qb = d_q + (size_t)q0 * dim;
@@ -628,7 +697,8 @@ void search_device(pxc_ivfpq* h, const float* d_q, uint32_t nq, uint32_t k, uint
     sp.list_off = h->list_off.p;
     sp.list_slot = h->list_slot.p;
     sp.list_codes = h->list_codes.p;
-    sp.slot_rank = h->slot_rank.p;
+    sp.list_rank = h->list_rank.p;
+    sp.scanned = h->scanned.p;
     sp.rank_slot = h->rank_slot.p;
     sp.ids = h->ids.p;
     sp.vectors = h->have_vectors ? h->vectors.p : nullptr;
@@ -642,9 +712,16 @@ void search_device(pxc_ivfpq* h, const float* d_q, uint32_t nq, uint32_t k, uint
     sp.nprobe = nprobe;
     sp.k = k;
     sp.shortlist = shortlist;
+    sp.cb = cb;
     sp.metric = h->metric;
     sp.rerank = rerank > 0;
+    const bool time_it = ctx->profiling && q0 == 0 && nb == nq;  // one batch: time its scan
+    if (time_it) PXC_CUDA(cudaEventRecord(h->ev_begin, s));
     scan_kernel<<<nb, SCAN_THREADS, smem_s, s>>>(sp);
+    if (time_it) {
+      PXC_CUDA(cudaEventRecord(h->ev_end, s));
+      h->timed = true;
+    }
     PXC_CUDA(cudaGetLastError());
     ctx->launches += 3;
   }
@@ -691,7 +768,9 @@ void encode_all(pxc_ivfpq* h, cudaStream_t s) {
     list_bounds_kernel<<<(h->nlist + 256) / 256, 256, 0, s>>>(keys_out.p, n, h->nlist, h->list_off.p);
     gather_codes_kernel<<<(unsigned)((n * m + 255) / 256), 256, 0, s>>>(h->codes.p, m, h->list_slot.p, n,
                                                                        h->list_codes.p);
-    ctx->launches += 4;
+    h->list_rank.reserve(n);
+    list_rank_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(h->list_slot.p, h->slot_rank.p, n, h->list_rank.p);
+    ctx->launches += 5;
   } else {
     PXC_CUDA(cudaMemsetAsync(h->list_off.p, 0, (h->nlist + 1) * 4, s));
   }
@@ -815,6 +894,44 @@ pxc_status pxc_ivfpq_set_store(pxc_ivfpq* h, const float* vectors, const uint64_
     PXC_CUDA(cudaStreamSynchronize(s));
     h->have_lists = false;
   });
+}
+
+pxc_status pxc_ivfpq_set_store_device(pxc_ivfpq* h, const float* d_vectors, const uint64_t* ids,
+                                      const uint8_t* live, uint64_t nslots, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(h != nullptr, "h", 0, "null handle");
+    PXC_CONFIG(nslots < 0xFFFFFFFFull, "nslots", nslots, "the device IVF-PQ supports fewer than 2^32 slots");
+    {
+      // ids and live flags (host) as in pxc_ivfpq_set_store, no vectors yet
+      pxc_error e2{};
+      pxc_status st = pxc_ivfpq_set_store(h, nullptr, ids, live, nslots, &e2);
+      if (st != PXC_OK) throw make_failure(st, e2.a, e2.b, e2.parameter, "%s", e2.detail);
+    }
+    std::lock_guard<std::mutex> lock(h->mu);
+    DeviceGuard g(h->ctx->device);
+    cudaStream_t s = h->ctx->stream;
+    if (d_vectors && nslots) {
+      h->vectors.reserve(nslots * h->dim);
+      PXC_CUDA(cudaMemcpyAsync(h->vectors.p, d_vectors, nslots * h->dim * 4, cudaMemcpyDeviceToDevice, s));
+      PXC_CUDA(cudaStreamSynchronize(s));
+      h->have_vectors = true;
+    }
+  });
+}
+
+uint64_t pxc_ivfpq_last_scanned(pxc_ivfpq* h) {
+  if (!h || !h->scanned.p) return 0;
+  unsigned long long v = 0;
+  if (cudaMemcpy(&v, h->scanned.p, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return 0;
+  return v;
+}
+
+float pxc_ivfpq_last_scan_ms(pxc_ivfpq* h) {
+  if (!h || !h->timed) return -1.0f;
+  float ms = -1.0f;
+  if (cudaEventSynchronize(h->ev_end) != cudaSuccess) return -1.0f;
+  if (cudaEventElapsedTime(&ms, h->ev_begin, h->ev_end) != cudaSuccess) return -1.0f;
+  return ms;
 }
 
 pxc_status pxc_ivfpq_set_codes(pxc_ivfpq* h, const uint32_t* list_of, const uint8_t* codes, pxc_error* err) {

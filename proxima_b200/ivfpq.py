@@ -55,6 +55,14 @@ class IvfPqIndex:
         N.call("pxc_ivfpq_set_store", self.handle, N.ptr(v), N.ptr(i), N.ptr(lv), n)
         self.nslots = n
 
+    def set_store_device(self, vectors, ids=None, live=None) -> None:
+        """The store with the vectors already on the GPU (a CUDA torch tensor, n x dim)."""
+        n = vectors.shape[0]
+        i = None if ids is None else np.ascontiguousarray(ids, dtype=np.uint64)
+        lv = None if live is None else np.ascontiguousarray(live, dtype=np.uint8)
+        N.call("pxc_ivfpq_set_store_device", self.handle, vectors.contiguous().data_ptr(), N.ptr(i), N.ptr(lv), n)
+        self.nslots = n
+
     def set_codes(self, list_of, codes) -> None:
         lo = np.ascontiguousarray(list_of, dtype=np.uint32)
         cd = np.ascontiguousarray(codes, dtype=np.uint8)
@@ -91,3 +99,16 @@ class IvfPqIndex:
         N.call("pxc_ivfpq_search", self.handle, N.ptr(q), nq, k, nprobe, rerank, N.ptr(bm), N.ptr(ids),
                N.ptr(dist), N.ptr(lens))
         return ids[:, :k], dist[:, :k], lens
+
+    def search_device(self, d_queries, k: int, nprobe: int, rerank: int, d_ids, d_dist, d_lens, stream: int,
+                      d_bitmap=None) -> None:
+        """Device-buffer search (torch tensors), enqueued on `stream`."""
+        N.call("pxc_ivfpq_search_device", self.handle, d_queries.data_ptr(), d_queries.shape[0], k, nprobe, rerank,
+               None if d_bitmap is None else d_bitmap.data_ptr(), d_ids.data_ptr(), d_dist.data_ptr(),
+               d_lens.data_ptr(), stream)
+
+    def last_scan_ms(self) -> float:
+        return N.load().pxc_ivfpq_last_scan_ms(self.handle)
+
+    def last_scanned(self) -> int:
+        return N.load().pxc_ivfpq_last_scanned(self.handle)

@@ -273,3 +273,43 @@ def test_topk_merge_of_shards_equals_single_search(c2_small):
     got = (o_ids.cpu().numpy().view(np.uint64), o_d.cpu().numpy(), o_l.cpu().numpy().view(np.uint32))
     ref = pxo.flat_search(db[:n], qs, k, pxo.EUCLIDEAN)
     _assert_same(got, ref, len(qs))
+
+
+def test_c2_many_query_tiles_match_brute_force():
+    """Thousands of queries: the scan runs in several waves, later splits seed
+    their lists from finished ones (including lists that were seeded
+    themselves). Checked against a brute-force scan in exact integer
+    arithmetic, ties by id."""
+    import torch
+
+    from proxima_b200 import _native as N
+    from proxima_b200 import fixtures
+
+    n, dim, nq, k = 300_000, 128, 4096, 10
+    db = fixtures.blobs_u8(n, dim, 512, fixtures.C2_CENTRES, fixtures.C2_BASE)
+    q = fixtures.blobs_u8(nq, dim, 512, fixtures.C2_CENTRES, fixtures.C2_QUERIES)
+    from proxima_b200.index import Context
+    import ctypes as C
+
+    ctx = Context.default()
+    h = N.vp()
+    N.call("pxc_flat_create", ctx.handle, dim, 0, C.byref(h))
+    try:
+        N.call("pxc_flat_sync", h, N.ptr(db), None, None, 0, n)
+        assert N.load().pxc_flat_path(h) == 1
+        ids = np.zeros((nq, k), np.uint64)
+        dist = np.zeros((nq, k), np.float32)
+        lens = np.zeros(nq, np.uint32)
+        N.call("pxc_flat_search", h, N.ptr(q), nq, k, None, N.ptr(ids), N.ptr(dist), N.ptr(lens))
+        dbt = torch.from_numpy(db).cuda().to(torch.int64)
+        qt = torch.from_numpy(q).cuda().to(torch.int64)
+        for i in list(range(0, nq, 97)) + [nq - 1]:
+            d = ((dbt - qt[i]) ** 2).sum(1)
+            kth = torch.topk(d, k, largest=False).values.max()
+            cand = torch.nonzero(d <= kth).flatten()
+            order = sorted(zip(d[cand].tolist(), cand.tolist()))[:k]
+            assert lens[i] == k
+            assert ids[i].tolist() == [c for _, c in order], f"query {i}: ids"
+            assert dist[i].tolist() == [float(v) for v, _ in order], f"query {i}: distances"
+    finally:
+        N.load().pxc_flat_destroy(h)
