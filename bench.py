@@ -115,21 +115,28 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(rows)}
 
 
-def cpu_baseline(db: np.ndarray, queries: np.ndarray, k: int, seconds: float) -> dict:
-    """The oracle port of FlatIndex::search on all host cores, on a bounded query sample."""
+def cpu_baseline(db: np.ndarray, queries: np.ndarray, k: int, seconds: float, gpu_ids=None) -> dict:
+    """The oracle port of FlatIndex::search on all host cores, on a bounded query sample; its answers for
+    the sample are also compared with the GPU's (gpu_ids: the GPU's ids for every query)."""
     from oracle import pxo
 
     threads = os.cpu_count() or 1
     batch = max(threads, 8)
     pxo.flat_search(db, queries[:batch], k, pxo.EUCLIDEAN, nthreads=threads)  # warm
-    done, t0 = 0, time.perf_counter()
+    done, t0, same = 0, time.perf_counter(), 0
     while time.perf_counter() - t0 < seconds and done + batch <= len(queries):
-        pxo.flat_search(db, queries[done:done + batch], k, pxo.EUCLIDEAN, nthreads=threads)
+        ref_ids, _, ref_len = pxo.flat_search(db, queries[done:done + batch], k, pxo.EUCLIDEAN, nthreads=threads)
+        if gpu_ids is not None:
+            for i in range(batch):
+                same += int(np.array_equal(gpu_ids[done + i, :ref_len[i]], ref_ids[i, :ref_len[i]]))
         done += batch
     el = time.perf_counter() - t0
-    return {"value": done / el, "unit": "queries/s", "cores": threads, "kind": "port",
-            "sample": f"{done} of the {len(queries)} queries against the full {db.shape[0]:,}-row database "
-                      f"({el:.1f} s, C++ oracle restating FlatIndex::search, one query per thread at a time)"}
+    out = {"value": done / el, "unit": "queries/s", "cores": threads, "kind": "port",
+           "sample": f"{done} of the {len(queries)} queries against the full {db.shape[0]:,}-row database "
+                     f"({el:.1f} s, C++ oracle restating FlatIndex::search, one query per thread at a time)"}
+    if gpu_ids is not None:
+        out["parity"] = {"queries": done, "identical_ids": same}
+    return out
 
 
 def run_reference(args):
@@ -684,7 +691,8 @@ def main():
                 "roofline": roofline}
         if world == 1 and not args.no_cpu_baseline:
             db = shard
-            line["cpu_baseline"] = cpu_baseline(db, queries, k, args.cpu_seconds)
+            gpu_ids = ids.cpu().numpy().view(np.uint64)
+            line["cpu_baseline"] = cpu_baseline(db, queries, k, args.cpu_seconds, gpu_ids)
         print(json.dumps(line), flush=True)
     lib.pxc_flat_destroy(h)
     ctx.close()
