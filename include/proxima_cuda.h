@@ -270,6 +270,118 @@ pxc_status pxc_ivfpq_search_device(pxc_ivfpq* h, const float* d_queries, uint32_
                                    uint64_t* d_out_ids, float* d_out_dist, uint32_t* d_out_len,
                                    void* stream, pxc_error* err);
 
+/* ---- ScalarQuantizer ----
+ * crates/proxima-quantize/src/scalar.rs. Range modes and code types in the
+ * declaration order of RangeMode / CodeType. */
+#define PXC_RANGE_GLOBAL 0
+#define PXC_RANGE_PER_DIMENSION 1
+#define PXC_CODE_U8 0
+#define PXC_CODE_I8 1
+/* ScalarQuantizer::train (scalar.rs:141-195) on n x dim HOST training rows:
+ * per group (1 under Global, dim under PerDimension) the observed min, scale
+ * = (max - min) / 255 and inverse_scale = scale > 0 ? 1 / scale : 0.
+ * Bit-identical to the reference's sequential fold, including the sign of a
+ * zero bound. n == 0 is PXC_CONFIGURATION ("training"); a non-finite value is
+ * PXC_NON_FINITE with a = its index within the vector. */
+pxc_status pxc_sq_train(pxc_ctx* ctx, const float* training, uint64_t n, uint32_t dim, int32_t mode,
+                        float* out_min, float* out_scale, float* out_inv_scale, pxc_error* err);
+/* Same with DEVICE training rows (outputs on the host), on `stream`. */
+pxc_status pxc_sq_train_device(pxc_ctx* ctx, const float* d_training, uint64_t n, uint32_t dim,
+                               int32_t mode, float* out_min, float* out_scale, float* out_inv_scale,
+                               void* stream, pxc_error* err);
+/* The observed (min, max) per group of DEVICE training rows, before the
+ * scale is formed: what a trainer sharded over ranks combines. Folding the
+ * ranks' values in rank order with `v < min` / `v > max` reproduces the
+ * single-pass result exactly. Outputs on the host. */
+pxc_status pxc_sq_ranges_device(pxc_ctx* ctx, const float* d_training, uint64_t n, uint32_t dim,
+                                int32_t mode, float* out_min, float* out_max, void* stream,
+                                pxc_error* err);
+/* ScalarQuantizer::encode_into (scalar.rs:246-268) for n vectors: HOST
+ * buffers, out_codes n x dim bytes (U8 levels or I8 level - 128). */
+pxc_status pxc_sq_encode(pxc_ctx* ctx, const float* min, const float* inv_scale, uint32_t dim,
+                         int32_t mode, int32_t code_type, const float* vectors, uint64_t n,
+                         uint8_t* out_codes, pxc_error* err);
+/* Same with DEVICE vectors and codes (the range table on the host). */
+pxc_status pxc_sq_encode_device(pxc_ctx* ctx, const float* min, const float* inv_scale, uint32_t dim,
+                                int32_t mode, int32_t code_type, const float* d_vectors, uint64_t n,
+                                uint8_t* d_out_codes, void* stream, pxc_error* err);
+/* ScalarQuantizer::decode (scalar.rs:270-296): min + level * scale. HOST buffers. */
+pxc_status pxc_sq_decode(pxc_ctx* ctx, const float* min, const float* scale, uint32_t dim, int32_t mode,
+                         int32_t code_type, const uint8_t* codes, uint64_t n, float* out,
+                         pxc_error* err);
+
+/* ---- SQ filtered search ----
+ * No counterpart index in the reference: its SQ path is train -> encode ->
+ * asymmetric scoring (crates/proxima-quantize/tests/recall.rs:139-148,
+ * scalar.rs:298-319). The device index holds the prepared rows (the re-rank
+ * store), their I8 codes, the VectorIds and integer metadata columns, and
+ * answers "top-k by the metric among the rows the filter accepts" as an int8
+ * over-fetch followed by an exact re-rank: the query in code space is
+ * quantized to s8 (one step per query, max |q_c * scale_c| / 127), the
+ * `overfetch` rows with the largest s8 . code score (ties to the lower id)
+ * are re-scored with VectorSpace::distance (cosine 1 - dot_unrolled, inner
+ * product -dot_unrolled) and the k smallest by (total_cmp, id) returned.
+ * Cosine and inner product; dim <= 1024. */
+typedef struct pxc_sq pxc_sq;
+/* A metadata condition lo <= value <= hi on an integer column (set with
+ * pxc_sq_set_column); a slot without the field fails it. The typed form of
+ * an Int filter (crates/proxima-server/src/filter.rs:58-75); e.g.
+ * year >= 2027 is {column, 0, 2027, INT64_MAX}. */
+typedef struct pxc_int_range {
+  uint32_t column;
+  uint32_t reserved;
+  int64_t lo;
+  int64_t hi;
+} pxc_int_range;
+pxc_status pxc_sq_create(pxc_ctx* ctx, uint32_t dim, int32_t metric, pxc_sq** out, pxc_error* err);
+void pxc_sq_destroy(pxc_sq* h);
+/* ScalarQuantizer::from_parts-style: a trained range table (groups entries
+ * each). Re-encodes the store when one is set. HOST buffers. */
+pxc_status pxc_sq_set_quantizer(pxc_sq* h, int32_t mode, const float* min, const float* scale,
+                                const float* inv_scale, pxc_error* err);
+pxc_status pxc_sq_get_quantizer(pxc_sq* h, int32_t* mode, float* min, float* scale, float* inv_scale,
+                                pxc_error* err);
+/* ScalarQuantizer::train over the live stored rows (slot order), then encode. */
+pxc_status pxc_sq_train_store(pxc_sq* h, int32_t mode, pxc_error* err);
+/* The slot store: nslots*dim prepared floats, VectorId per slot (NULL: id ==
+ * slot), live byte per slot (NULL: all live). Clears the metadata columns and
+ * re-encodes when a quantizer is set. HOST buffers. */
+pxc_status pxc_sq_set_store(pxc_sq* h, const float* vectors, const uint64_t* ids, const uint8_t* live,
+                            uint64_t nslots, pxc_error* err);
+/* Same with the vectors in DEVICE memory (copied); ids and live on the host. */
+pxc_status pxc_sq_set_store_device(pxc_sq* h, const float* d_vectors, const uint64_t* ids,
+                                   const uint8_t* live, uint64_t nslots, pxc_error* err);
+/* Integer metadata column `column`: one value per slot, `present` one byte
+ * per slot (NULL: every slot has the field). HOST buffers. */
+pxc_status pxc_sq_set_column(pxc_sq* h, uint32_t column, const int64_t* values, const uint8_t* present,
+                             pxc_error* err);
+/* Live rows in the store. */
+uint64_t pxc_sq_len(const pxc_sq* h);
+/* The stored I8 codes per slot (nslots x dim; dead slots zero). HOST buffer. */
+pxc_status pxc_sq_get_codes(pxc_sq* h, uint8_t* out_codes, pxc_error* err);
+/* Batched filtered search with HOST buffers: `queries` nq*dim prepared
+ * floats, `bitmap` over slots or NULL, `ranges` nranges (<= 8) conditions
+ * ANDed with it; max(overfetch, k) <= 2048. Outputs nq*k ids/distances and
+ * nq lengths. */
+pxc_status pxc_sq_search(pxc_sq* h, const float* queries, uint32_t nq, uint32_t k, uint32_t overfetch,
+                         const uint64_t* bitmap, const pxc_int_range* ranges, uint32_t nranges,
+                         uint64_t* out_ids, float* out_dist, uint32_t* out_len, pxc_error* err);
+/* Same with DEVICE queries, bitmap and outputs (`ranges` stays a host array),
+ * ordered on `stream` (NULL: the context stream). Returns after the work has
+ * finished: the accepted-row count sizes the scan. */
+pxc_status pxc_sq_search_device(pxc_sq* h, const float* d_queries, uint32_t nq, uint32_t k,
+                                uint32_t overfetch, const uint64_t* d_bitmap, const pxc_int_range* ranges,
+                                uint32_t nranges, uint64_t* d_out_ids, float* d_out_dist,
+                                uint32_t* d_out_len, void* stream, pxc_error* err);
+/* Device time of the last search's scan (K12 passes and selection) when it
+ * ran as one batch with profiling on; -1 otherwise. */
+float pxc_sq_last_scan_ms(pxc_sq* h);
+/* Rows the last search's filter accepted. */
+uint64_t pxc_sq_last_accepted(const pxc_sq* h);
+/* Queries of the last search whose candidates overflowed the over-fetch
+ * buffer and were answered by the exact chunked fallback. */
+uint32_t pxc_sq_last_fallback(const pxc_sq* h);
+
 #ifdef __cplusplus
 }
 #endif

@@ -631,7 +631,8 @@ void pxo_sq_encode(const float* min, const float* inv_scale, uint64_t dim, int m
     for (uint64_t c = 0; c < dim; ++c) {
       uint64_t g = mode == PXO_RANGE_GLOBAL ? 0 : c;
       float x = std::round((vectors[i * dim + c] - min[g]) * inv_scale[g]);
-      x = x < 0.0f ? 0.0f : (x > 255.0f ? 255.0f : x);
+      // clamp(0, 255) then `as u8`, which saturates and maps NaN to 0
+      x = !(x >= 0.0f) ? 0.0f : (x > 255.0f ? 255.0f : x);
       uint8_t level = static_cast<uint8_t>(x);
       out_codes[i * dim + c] = code_type == PXO_CODE_I8 ? static_cast<uint8_t>(level - 128) : level;
     }
@@ -668,6 +669,76 @@ float pxo_sq_asymmetric_inner_product(const float* min, const float* scale, uint
   for (uint64_t c = 0; c < dim; ++c)
     sum += query[c] * sq_reconstruct(min, scale, mode, code_type, c, code[c]);
   return -sum;
+}
+
+// ---------------------------------------------------------------------------
+// Scalar-quantized filtered search (the SQ composition: the reference has no
+// SQ index; its SQ path is train -> encode -> asymmetric scoring,
+// crates/proxima-quantize/tests/recall.rs:139-148). Steps, per query:
+//  1. the query in code space: w_c = q_c * scale_g, quantized to s8 with one
+//     step per query, amax / 127: q8_c = clamp(round(w_c * (127 / amax)), -127, 127)
+//     (all zero when amax == 0);
+//  2. integer score S = sum_c q8_c * code_c over the I8 codes (level - 128) of
+//     every accepted row. S ranks rows as the asymmetric inner product
+//     (scalar.rs:298-319) does, up to the query's quantization: the per-query
+//     terms sum_c q_c min_c and 128 * sum_c w_c do not depend on the row;
+//  3. the `overfetch` rows of largest S, ties to the lower rank;
+//  4. their exact distances (cosine 1 - dot_unrolled, inner product
+//     -dot_unrolled: distance.rs:317-331, 400-402, 291-293) and the k
+//     smallest by (total_cmp, id), as TopK orders them (topk.rs:63-67).
+// Rows are given in rank order (ascending VectorId).
+// ---------------------------------------------------------------------------
+void pxo_sq_query_s8(const float* scale, uint64_t dim, int mode, const float* query, int8_t* out) {
+  std::vector<float> w(dim);
+  float amax = 0.0f;
+  for (uint64_t c = 0; c < dim; ++c) {
+    w[c] = query[c] * scale[mode == PXO_RANGE_GLOBAL ? 0 : c];
+    float a = std::fabs(w[c]);
+    amax = a > amax ? a : amax;
+  }
+  float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+  for (uint64_t c = 0; c < dim; ++c) {
+    float x = std::round(w[c] * inv);
+    x = x < -127.0f ? -127.0f : (x > 127.0f ? 127.0f : x);
+    out[c] = static_cast<int8_t>(x);
+  }
+}
+
+void pxo_sq_search(const float* scale, uint64_t dim, int mode, const int8_t* codes,
+                   const float* rows, const uint64_t* ids, const uint8_t* accepted, uint64_t nrank,
+                   int metric, const float* queries, uint64_t nq, uint64_t k, uint64_t overfetch,
+                   uint64_t* out_ids, float* out_dist, uint32_t* out_len, int threads) {
+  const uint64_t f = std::max(overfetch, k);
+  parallel_for(nq, threads, [&](uint64_t qb, uint64_t qe) {
+    std::vector<int8_t> q8(dim);
+    std::vector<std::pair<int32_t, uint64_t>> cand;  // (-S, rank): ascending = best first
+    for (uint64_t q = qb; q < qe; ++q) {
+      const float* qv = queries + q * dim;
+      pxo_sq_query_s8(scale, dim, mode, qv, q8.data());
+      cand.clear();
+      for (uint64_t r = 0; r < nrank; ++r) {
+        if (accepted && !accepted[r]) continue;
+        const int8_t* code = codes + r * dim;
+        int32_t sum = 0;
+        for (uint64_t c = 0; c < dim; ++c) sum += static_cast<int32_t>(q8[c]) * code[c];
+        cand.emplace_back(-sum, r);
+      }
+      const uint64_t keep = std::min<uint64_t>(f, cand.size());
+      std::partial_sort(cand.begin(), cand.begin() + keep, cand.end());
+      TopK top(k);
+      for (uint64_t i = 0; i < keep; ++i) {
+        const uint64_t r = cand[i].second;
+        const float dot = dot_unrolled(qv, rows + r * dim, dim);
+        top.push(r, metric == PXO_COSINE ? 1.0f - dot : -dot);
+      }
+      auto v = top.sorted();
+      for (size_t i = 0; i < v.size(); ++i) {
+        out_ids[q * k + i] = ids ? ids[v[i].id] : v[i].id;
+        out_dist[q * k + i] = v[i].dist;
+      }
+      out_len[q] = static_cast<uint32_t>(v.size());
+    }
+  });
 }
 
 // ivfpq.rs:1231-1243

@@ -111,6 +111,14 @@ float pxo_sq_asymmetric_inner_product(const float* min, const float* scale, uint
                                       int mode, int code_type, const float* query,
                                       const uint8_t* code);
 
+/* SQ composition (no reference index): query quantization to s8 and the
+ * over-fetch + exact re-rank search over I8 codes in rank order. */
+void pxo_sq_query_s8(const float* scale, uint64_t dim, int mode, const float* query, int8_t* out);
+void pxo_sq_search(const float* scale, uint64_t dim, int mode, const int8_t* codes,
+                   const float* rows, const uint64_t* ids, const uint8_t* accepted, uint64_t nrank,
+                   int metric, const float* queries, uint64_t nq, uint64_t k, uint64_t overfetch,
+                   uint64_t* out_ids, float* out_dist, uint32_t* out_len, int threads);
+
 /* ---- ivfpq.rs ---- */
 /* nearest_centroid with 8-lane L2 (ivfpq.rs:1231-1243) */
 uint32_t pxo_ivf_nearest_centroid(const float* v, const float* centroids, uint64_t dim,

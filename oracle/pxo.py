@@ -77,6 +77,8 @@ def lib():
             "pxo_sq_decode": (None, [vp, vp, u64, i32, i32, vp, u64, vp]),
             "pxo_sq_asymmetric_squared_l2": (f32, [vp, vp, u64, i32, i32, vp, vp]),
             "pxo_sq_asymmetric_inner_product": (f32, [vp, vp, u64, i32, i32, vp, vp]),
+            "pxo_sq_query_s8": (None, [vp, u64, i32, vp, vp]),
+            "pxo_sq_search": (None, [vp, u64, i32, vp, vp, vp, vp, u64, i32, vp, u64, u64, u64, vp, vp, vp, i32]),
             "pxo_ivf_nearest_centroid": (C.c_uint32, [vp, vp, u64, u64]),
             "pxo_ivfpq_train": (u64, [vp, vp, u64, u64, u64, u64, u64, u64, u64, vp, vp, vp, vp, vp,
                                       vp, vp, i32]),
@@ -270,6 +272,35 @@ def sq_asym_l2(mn, sc, dim: int, mode: int, code_type: int, query, code) -> floa
 
 
 # ---- ivfpq.rs ----
+def sq_query_s8(scale, dim: int, mode: int, query) -> np.ndarray:
+    """The query in code space as s8 (the SQ search's step 1)."""
+    sc = f32a(scale)
+    q = f32a(query)
+    out = np.zeros(dim, np.int8)
+    lib().pxo_sq_query_s8(_p(sc), dim, mode, _p(q), _p(out))
+    return out
+
+
+def sq_search(scale, mode: int, codes, rows, queries, k: int, overfetch: int, metric: int,
+              ids=None, accepted=None, nthreads=None):
+    """Over-fetch on s8 scores, exact re-rank to k. ``codes`` (n, dim) I8 codes
+    and ``rows`` (n, dim) prepared vectors in rank order; ``ids`` the VectorId of
+    each rank (ascending), ``accepted`` one byte per rank or None."""
+    c = np.ascontiguousarray(codes).view(np.int8)
+    r = f32a(rows).reshape(c.shape)
+    n, dim = c.shape
+    q = f32a(queries).reshape(-1, dim)
+    nq = q.shape[0]
+    oid = np.zeros((nq, max(k, 1)), np.uint64)
+    od = np.zeros((nq, max(k, 1)), np.float32)
+    ol = np.zeros(nq, np.uint32)
+    idv = None if ids is None else np.ascontiguousarray(ids, np.uint64)
+    acc = None if accepted is None else np.ascontiguousarray(accepted, np.uint8)
+    lib().pxo_sq_search(_p(f32a(scale)), dim, mode, _p(c), _p(r), _p(idv), _p(acc), n, metric, _p(q), nq,
+                        k, overfetch, _p(oid), _p(od), _p(ol), nthreads or threads())
+    return oid[:, :k], od[:, :k], ol
+
+
 def ivfpq_train(vectors, nlist: int, m: int, max_iterations: int = 25, training_sample: int = 100_000,
                 seed: int = 0x1FF9C0D, live=None, coarse_init=None, pq_init=None, nthreads=None):
     v = f32a(vectors)

@@ -59,6 +59,17 @@ class PxcIvfpqReport(C.Structure):
     ]
 
 
+class PxcIntRange(C.Structure):
+    """pxc_int_range: lo <= value <= hi on an integer metadata column."""
+
+    _fields_ = [
+        ("column", C.c_uint32),
+        ("reserved", C.c_uint32),
+        ("lo", C.c_int64),
+        ("hi", C.c_int64),
+    ]
+
+
 # name -> (restype, argtypes); every symbol include/proxima_cuda.h declares.
 SIGNATURES: dict[str, tuple] = {
     "pxc_abi_version": (C.c_uint32, []),
@@ -103,6 +114,34 @@ SIGNATURES: dict[str, tuple] = {
                                      C.POINTER(PxcError)]),
     "pxc_ivfpq_search_device": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, vp, vp,
                                             vp, vp, vp, C.POINTER(PxcError)]),
+    "pxc_sq_train": (C.c_int32, [vp, vp, C.c_uint64, C.c_uint32, C.c_int32, vp, vp, vp, C.POINTER(PxcError)]),
+    "pxc_sq_train_device": (C.c_int32, [vp, vp, C.c_uint64, C.c_uint32, C.c_int32, vp, vp, vp, vp,
+                                        C.POINTER(PxcError)]),
+    "pxc_sq_ranges_device": (C.c_int32, [vp, vp, C.c_uint64, C.c_uint32, C.c_int32, vp, vp, vp,
+                                         C.POINTER(PxcError)]),
+    "pxc_sq_encode": (C.c_int32, [vp, vp, vp, C.c_uint32, C.c_int32, C.c_int32, vp, C.c_uint64, vp,
+                                  C.POINTER(PxcError)]),
+    "pxc_sq_encode_device": (C.c_int32, [vp, vp, vp, C.c_uint32, C.c_int32, C.c_int32, vp, C.c_uint64, vp, vp,
+                                         C.POINTER(PxcError)]),
+    "pxc_sq_decode": (C.c_int32, [vp, vp, vp, C.c_uint32, C.c_int32, C.c_int32, vp, C.c_uint64, vp,
+                                  C.POINTER(PxcError)]),
+    "pxc_sq_create": (C.c_int32, [vp, C.c_uint32, C.c_int32, C.POINTER(vp), C.POINTER(PxcError)]),
+    "pxc_sq_destroy": (None, [vp]),
+    "pxc_sq_set_quantizer": (C.c_int32, [vp, C.c_int32, vp, vp, vp, C.POINTER(PxcError)]),
+    "pxc_sq_get_quantizer": (C.c_int32, [vp, C.POINTER(C.c_int32), vp, vp, vp, C.POINTER(PxcError)]),
+    "pxc_sq_train_store": (C.c_int32, [vp, C.c_int32, C.POINTER(PxcError)]),
+    "pxc_sq_set_store": (C.c_int32, [vp, vp, vp, vp, C.c_uint64, C.POINTER(PxcError)]),
+    "pxc_sq_set_store_device": (C.c_int32, [vp, vp, vp, vp, C.c_uint64, C.POINTER(PxcError)]),
+    "pxc_sq_set_column": (C.c_int32, [vp, C.c_uint32, vp, vp, C.POINTER(PxcError)]),
+    "pxc_sq_len": (C.c_uint64, [vp]),
+    "pxc_sq_get_codes": (C.c_int32, [vp, vp, C.POINTER(PxcError)]),
+    "pxc_sq_search": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, vp, vp, C.c_uint32, vp, vp, vp,
+                                  C.POINTER(PxcError)]),
+    "pxc_sq_search_device": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, vp, vp, C.c_uint32, vp, vp,
+                                         vp, vp, C.POINTER(PxcError)]),
+    "pxc_sq_last_scan_ms": (C.c_float, [vp]),
+    "pxc_sq_last_accepted": (C.c_uint64, [vp]),
+    "pxc_sq_last_fallback": (C.c_uint32, [vp]),
 }
 
 _lib = None

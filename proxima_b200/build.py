@@ -30,9 +30,9 @@ NVCC_FLAGS = [
     "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
     f"-I{INCLUDE}", f"-I{CSRC}",
 ]
-CUDA_SOURCES = ["ctx.cu", "flat.cu", "kmeans.cu", "ivfpq.cu"]
+CUDA_SOURCES = ["ctx.cu", "flat.cu", "kmeans.cu", "ivfpq.cu", "sq.cu"]
 HEADERS = ["common.cuh", "sm100.cuh", "flat_tc.cuh", "topk.cuh", "tmap.cuh", "kmeans_tc.cuh",
-           "seqsum.cuh", "rng.h", "kmeans_api.h"]
+           "seqsum.cuh", "rng.h", "kmeans_api.h", "select.cuh", "refdist.cuh", "sq_tc.cuh"]
 CXX = os.environ.get("CXX", shutil.which("g++") or "g++")
 
 

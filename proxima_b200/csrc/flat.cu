@@ -23,12 +23,11 @@
 
 #include "common.cuh"
 #include "flat_tc.cuh"
+#include "select.cuh"
 #include "tmap.cuh"
 #include "topk.cuh"
 
 namespace pxc {
-
-constexpr uint32_t SENTINEL = 0xFFFFFFFFu;  // excluded candidate (filtered / padding)
 
 // ---------------------------------------------------------------------------
 // Reference-order distance (crates/proxima-core/src/distance.rs). All float
@@ -141,123 +140,6 @@ __global__ void __launch_bounds__(256) dist_chunk_kernel(
       D[(size_t)q * C + (r - c0)] = key;
     }
   }
-}
-
-// Selection step of K1g, one block per query. L_in holds the running top-k of
-// ranks below c0 as (key << 32 | rank) in ascending RANK order; the chunk adds
-// ranks c0.. . The new list is the k smallest of the union under
-// (key, rank), written in ascending rank order again, so equal keys resolve
-// to the smaller rank. Found with a 4-pass radix select on the key and a
-// stable block-wide compaction.
-constexpr int SEL_THREADS = 256;
-__global__ void __launch_bounds__(SEL_THREADS) select_chunk_kernel(
-    const uint64_t* __restrict__ L_in, const uint32_t* __restrict__ len_in,
-    uint64_t* __restrict__ L_out, uint32_t* __restrict__ len_out, const uint32_t* __restrict__ D,
-    uint32_t C, uint64_t c0, uint32_t cvalid, uint32_t k, uint32_t q_base) {
-  using Scan = cub::BlockScan<uint32_t, SEL_THREADS>;
-  using Reduce = cub::BlockReduce<uint32_t, SEL_THREADS>;
-  __shared__ typename Scan::TempStorage scan_tmp;
-  __shared__ typename Reduce::TempStorage red_tmp;
-  __shared__ uint32_t hist[256];
-  __shared__ uint32_t s_prefix, s_mask, s_remaining, s_take_all, s_thr, s_survivors;
-  const uint32_t q = q_base + blockIdx.x;
-  const uint64_t* Lq = L_in + (size_t)blockIdx.x * k;
-  uint64_t* Oq = L_out + (size_t)blockIdx.x * k;
-  const uint32_t* Dq = D + (size_t)q * C;
-  const uint32_t lin = len_in[blockIdx.x];
-  const uint32_t n = lin + cvalid;
-
-  // Fast path: a full list rejects every chunk key that is not strictly below
-  // its worst key (a chunk rank is larger than every listed rank).
-  if (lin == k) {
-    uint32_t worst = 0;
-    for (uint32_t i = threadIdx.x; i < lin; i += SEL_THREADS)
-      worst = max(worst, static_cast<uint32_t>(Lq[i] >> 32));
-    uint32_t w = Reduce(red_tmp).Reduce(worst, cub::Max());
-    if (threadIdx.x == 0) s_thr = w;
-    __syncthreads();
-    uint32_t cnt = 0;
-    for (uint32_t i = threadIdx.x; i < cvalid; i += SEL_THREADS) cnt += Dq[i] < s_thr;
-    uint32_t total = Reduce(red_tmp).Sum(cnt);
-    if (threadIdx.x == 0) s_survivors = total;
-    __syncthreads();
-    if (s_survivors == 0) {
-      for (uint32_t i = threadIdx.x; i < lin; i += SEL_THREADS) Oq[i] = Lq[i];
-      if (threadIdx.x == 0) len_out[blockIdx.x] = lin;
-      return;
-    }
-  }
-
-  auto key_at = [&](uint32_t i) -> uint32_t {
-    return i < lin ? static_cast<uint32_t>(Lq[i] >> 32) : Dq[i - lin];
-  };
-  if (threadIdx.x == 0) {
-    s_prefix = 0;
-    s_mask = 0;
-    s_remaining = k;
-    s_take_all = 0;
-  }
-  for (int pass = 0; pass < 4; ++pass) {
-    const int shift = 24 - 8 * pass;
-    for (uint32_t i = threadIdx.x; i < 256; i += SEL_THREADS) hist[i] = 0;
-    __syncthreads();
-    if (s_take_all) break;
-    const uint32_t prefix = s_prefix, mask = s_mask;
-    for (uint32_t i = threadIdx.x; i < n; i += SEL_THREADS) {
-      uint32_t key = key_at(i);
-      if (key != SENTINEL && (key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      uint32_t need = s_remaining, cum = 0, digit = 256;
-      for (uint32_t b = 0; b < 256; ++b) {
-        if (cum + hist[b] >= need) {
-          digit = b;
-          break;
-        }
-        cum += hist[b];
-      }
-      if (digit == 256) {
-        s_take_all = 1;  // fewer than `need` candidates share the prefix: all of them fit
-      } else {
-        s_prefix = prefix | (digit << shift);
-        s_mask = mask | (255u << shift);
-        s_remaining = need - cum;
-      }
-    }
-    __syncthreads();
-  }
-  const bool take_all = s_take_all != 0;
-  const uint32_t thr = s_prefix, quota_eq = s_remaining;
-  // Stable compaction in (list, chunk) = ascending rank order.
-  uint32_t out_base = 0, eq_base = 0;
-  for (uint32_t base = 0; base < n; base += SEL_THREADS) {
-    const uint32_t i = base + threadIdx.x;
-    uint32_t key = SENTINEL;
-    uint64_t packed = 0;
-    if (i < n) {
-      if (i < lin) {
-        packed = Lq[i];
-        key = static_cast<uint32_t>(packed >> 32);
-      } else {
-        key = Dq[i - lin];
-        packed = (static_cast<uint64_t>(key) << 32) | static_cast<uint32_t>(c0 + (i - lin));
-      }
-    }
-    const bool valid = key != SENTINEL;
-    uint32_t is_eq = (!take_all && valid && key == thr) ? 1u : 0u;
-    uint32_t eq_before, eq_total;
-    Scan(scan_tmp).ExclusiveSum(is_eq, eq_before, eq_total);
-    __syncthreads();
-    bool sel = valid && (take_all || key < thr || (is_eq && eq_base + eq_before < quota_eq));
-    uint32_t pos, sel_total;
-    Scan(scan_tmp).ExclusiveSum(sel ? 1u : 0u, pos, sel_total);
-    __syncthreads();
-    if (sel) Oq[out_base + pos] = packed;
-    out_base += sel_total;
-    eq_base += eq_total;
-  }
-  if (threadIdx.x == 0) len_out[blockIdx.x] = out_base;
 }
 
 // Final ordering of a K1g list (k <= 2048): sort by (key, rank), map rank to id.

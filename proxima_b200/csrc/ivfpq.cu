@@ -38,6 +38,8 @@
 #include "common.cuh"
 #include "kmeans_api.h"
 #include "rng.h"
+#include "refdist.cuh"
+#include "select.cuh"
 #include "topk.cuh"
 
 namespace pxc {
@@ -55,46 +57,8 @@ constexpr uint32_t QB = 64;       // queries per coarse block
 constexpr uint32_t TCC = 32;      // centroids per coarse smem tile
 constexpr uint32_t CSPLIT = 8;    // centroid ranges per query (coarse)
 
-// proxima_core::distance::squared_euclidean: eight lane sums over full
-// chunks of 8, reduced ((l0+l1)+(l2+l3))+((l4+l5)+(l6+l7)), plus a
-// sequential tail. `a` may be in shared memory.
-__device__ __forceinline__ float l2_unrolled(const float* a, const float* __restrict__ b, uint32_t dim) {
-  float acc[8];
-#pragma unroll
-  for (int l = 0; l < 8; ++l) acc[l] = 0.0f;
-  const uint32_t full = dim & ~7u;
-  for (uint32_t i = 0; i < full; i += 8) {
-#pragma unroll
-    for (int l = 0; l < 8; ++l) {
-      const float d = __fsub_rn(a[i + l], __ldg(b + i + l));
-      acc[l] = __fadd_rn(acc[l], __fmul_rn(d, d));
-    }
-  }
-  float tail = 0.0f;
-  for (uint32_t i = full; i < dim; ++i) {
-    const float d = __fsub_rn(a[i], __ldg(b + i));
-    tail = __fadd_rn(tail, __fmul_rn(d, d));
-  }
-  const float x = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
-  const float y = __fadd_rn(__fadd_rn(acc[4], acc[5]), __fadd_rn(acc[6], acc[7]));
-  return __fadd_rn(__fadd_rn(x, y), tail);
-}
-__device__ __forceinline__ float dot_unrolled(const float* a, const float* __restrict__ b, uint32_t dim) {
-  float acc[8];
-#pragma unroll
-  for (int l = 0; l < 8; ++l) acc[l] = 0.0f;
-  const uint32_t full = dim & ~7u;
-  for (uint32_t i = 0; i < full; i += 8) {
-#pragma unroll
-    for (int l = 0; l < 8; ++l) acc[l] = __fadd_rn(acc[l], __fmul_rn(a[i + l], __ldg(b + i + l)));
-  }
-  float tail = 0.0f;
-  for (uint32_t i = full; i < dim; ++i) tail = __fadd_rn(tail, __fmul_rn(a[i], __ldg(b + i)));
-  const float x = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
-  const float y = __fadd_rn(__fadd_rn(acc[4], acc[5]), __fadd_rn(acc[6], acc[7]));
-  return __fadd_rn(__fadd_rn(x, y), tail);
-}
-// space.distance for the metrics IVF-PQ reranks with (space.rs:148-156).
+// VectorSpace::distance for the two metrics search_prepared scores:
+// cosine = 1 - dot_unrolled, euclidean = squared_euclidean.
 __device__ __forceinline__ float space_distance(int metric, const float* a, const float* __restrict__ b,
                                                 uint32_t dim) {
   return metric == PXC_COSINE ? __fsub_rn(1.0f, dot_unrolled(a, b, dim)) : l2_unrolled(a, b, dim);
@@ -206,67 +170,6 @@ __global__ void coarse_merge_kernel(const uint64_t* __restrict__ partial, uint32
     probes[(size_t)q * nprobe + i] = s[i] == ~0ull ? UNASSIGNED : (uint32_t)s[i];
 }
 
-// ---------------------------------------------------------------------------
-// Block radix-select: the K-th smallest (1-based) of buf[0, cnt), then keeps
-// exactly the K keys <= it at the front. Keys are unique. Returns the K-th.
-// ---------------------------------------------------------------------------
-__device__ uint64_t select_keep(uint64_t* buf, uint32_t cnt, uint32_t K, uint32_t* hist, uint32_t* sh) {
-  uint64_t prefix = 0, mask = 0;
-  uint32_t k = K;
-  for (int shift = 56; shift >= 0; shift -= 8) {
-    for (uint32_t b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
-    __syncthreads();
-    for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) {
-      const uint64_t key = buf[i];
-      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
-    }
-    __syncthreads();
-    if (threadIdx.x < 32) {  // one warp: prefix sums over the 256 bins
-      const uint32_t lane = threadIdx.x;
-      uint32_t c[8], s = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        c[j] = hist[lane * 8 + j];
-        s += c[j];
-      }
-      uint32_t inc = s;
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t v = __shfl_up_sync(0xFFFFFFFFu, inc, o);
-        if (lane >= (uint32_t)o) inc += v;
-      }
-      const uint32_t before = inc - s;
-      if (before < k && inc >= k) {
-        uint32_t acc = before;
-        for (int j = 0; j < 8; ++j) {
-          if (acc + c[j] >= k) {
-            sh[0] = lane * 8 + j;
-            sh[1] = k - acc;
-            break;
-          }
-          acc += c[j];
-        }
-      }
-    }
-    __syncthreads();
-    prefix |= (uint64_t)sh[0] << shift;
-    mask |= 0xFFull << shift;
-    k = sh[1];
-    __syncthreads();
-  }
-  // keep the keys <= prefix (exactly K of them)
-  constexpr uint32_t PER = CB_MAX / SCAN_THREADS;
-  uint64_t mine[PER];
-  uint32_t nmine = 0;
-  for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x)
-    if (buf[i] <= prefix) mine[nmine++] = buf[i];
-  if (threadIdx.x == 0) sh[2] = 0;
-  __syncthreads();
-  const uint32_t base = atomicAdd(&sh[2], nmine);
-  for (uint32_t j = 0; j < nmine; ++j) buf[base + j] = mine[j];
-  __syncthreads();
-  return prefix;
-}
-
 struct ScanParams {
   const float* queries;      // nq x dim (prepared)
   const uint32_t* probes;    // nq x nprobe list indices
@@ -352,7 +255,7 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(const ScanParams p) 
     if (t == 0 && p.scanned) atomicAdd(p.scanned, (unsigned long long)(e - b));
     for (uint32_t j0 = b; j0 < e; j0 += CHUNK) {
       if (count > CB - CHUNK) {
-        const uint64_t kth = select_keep(buf, count, p.shortlist, hist, sh);
+        const uint64_t kth = select_keep<CB_MAX / SCAN_THREADS>(buf, count, p.shortlist, hist, sh);
         if (t == 0) {
           count = p.shortlist;
           thr = kth;
@@ -413,7 +316,7 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(const ScanParams p) 
   __syncthreads();
   uint32_t n = count;
   if (n > p.shortlist) {
-    select_keep(buf, n, p.shortlist, hist, sh);
+    select_keep<CB_MAX / SCAN_THREADS>(buf, n, p.shortlist, hist, sh);
     n = p.shortlist;
   }
   uint32_t n2 = 1;
