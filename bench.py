@@ -3,6 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     python bench.py --workload kmeans [...]   # config C3: k-means 1M x 96, k=4096, 20 iterations
     python bench.py --workload ivfpq [...]    # config C4: IVF-PQ 20M x 128, nlist 16384, m=16, recall@10 >= 0.9
+    python bench.py --workload sq [...]       # config C5: SQ int8 filtered scan, 6.25M x 768 per GPU, 4,096 queries
 
 One step = one exact top-k search of all queries over the whole database
 (sharded by rows across N GPUs, one process per GPU under torchrun; local
@@ -46,7 +47,8 @@ def parse():
     p.add_argument("--dim", type=int, default=128)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
-    p.add_argument("--workload", choices=["flat", "kmeans", "ivfpq"], default="flat")
+    p.add_argument("--workload", choices=["flat", "kmeans", "ivfpq", "sq"], default="flat")
+    p.add_argument("--sq-n", type=int, default=6_250_000, help="rows per GPU (C5: 50M over 8 GPUs)")
     p.add_argument("--ivf-n", type=int, default=20_000_000)
     p.add_argument("--ivf-nlist", type=int, default=16384)
     return p.parse_args()
@@ -522,8 +524,241 @@ def ivfpq_cpu_baseline(idx, d_vec, queries, nprobe, rerank, seconds):
                       "per thread)"}
 
 
+SQ_METRIC = "queries/s: SQ int8 filtered scan (768-d cosine, year >= 2027, over-fetch 100 on int8, exact top-10)"
+
+
+def run_sq(args):
+    """--workload sq: C5 per GPU. Each GPU holds one 6.25M-row shard of the 50M x 768 corpus (the 8-way
+    split of C5), its I8 codes under a per-dimension quantizer trained over every shard, and the year
+    column. One step = the 4,096-query batch: filter compaction, int8 over-fetch of 100 on the tensor cores,
+    exact fp32 re-rank to 10 on the shard; with N GPUs an NCCL allgather of the 10 per query and the
+    (total_cmp, id) merge."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    from proxima_b200 import _native as N
+    from proxima_b200 import fixtures
+    from proxima_b200.core import Metric
+    from proxima_b200.index import Context
+    from proxima_b200.sq import CodeType, IntRange, RangeMode, ScalarQuantizer, SqIndex, combine_ranges, ranges_device
+
+    per, dim, nq, k, F = args.sq_n, 768, 4096, 10, 100
+    lo = rank * per
+    ctx = Context(local)
+    lib = N.load()
+    keep_host = world == 1 and rank == 0
+    t0 = time.perf_counter()
+    d_vec = torch.empty((per, dim), dtype=torch.float32, device=dev)
+    host = np.empty((per, dim), dtype=np.float32) if keep_host else None
+    chunk = 500_000
+    for b in range(0, per, chunk):
+        e = min(per, b + chunk)
+        part = fixtures.sphere_blobs(e - b, dim, 10_000, fixtures.C5_CENTRES, fixtures.C5_BASE, 0.03, row_begin=lo + b)
+        d_vec[b:e].copy_(torch.from_numpy(part))
+        if host is not None:
+            host[b:e] = part
+    years = fixtures.uniform_int(per, fixtures.C5_YEARS, 2000, 30, row_begin=lo)
+    queries = fixtures.sphere_blobs(nq, dim, 10_000, fixtures.C5_CENTRES, fixtures.C5_QUERIES, 0.03)
+    t_gen = time.perf_counter() - t0
+
+    t0 = time.perf_counter()
+    # quantizer over all shards: per-shard ranges folded in rank order (== one pass over the corpus)
+    rlo, rhi = ranges_device(d_vec, dim, RangeMode.PER_DIMENSION, ctx)
+    if world > 1:
+        t = torch.from_numpy(np.stack([rlo, rhi])).to(dev)
+        g = torch.empty((world, 2, dim), dtype=torch.float32, device=dev)
+        dist.all_gather_into_tensor(g, t)
+        g = g.cpu().numpy()
+        lows, highs = [g[r, 0] for r in range(world)], [g[r, 1] for r in range(world)]
+    else:
+        lows, highs = [rlo], [rhi]
+    mn, sc, inv = combine_ranges(lows, highs)
+    idx = SqIndex(dim, Metric.COSINE, ctx)
+    idx.set_store(d_vec, ids=np.arange(lo, lo + per, dtype=np.uint64))
+    idx.set_quantizer(ScalarQuantizer(dim, RangeMode.PER_DIMENSION, CodeType.I8, mn, sc, inv, ctx))
+    idx.set_column(0, years)
+    del d_vec
+    torch.cuda.empty_cache()
+    torch.cuda.synchronize(dev)
+    t_build = time.perf_counter() - t0
+    flt = [IntRange(0, lo=2027)]
+
+    stream = torch.cuda.Stream(dev)  # an explicit stream: the library's work and the events share it
+    torch.cuda.set_stream(stream)
+    sp = stream.cuda_stream
+    q_host = torch.from_numpy(queries).pin_memory()
+    q_dev = q_host.to(dev)
+    ids = torch.empty((nq, k), dtype=torch.int64, device=dev)
+    dists = torch.empty((nq, k), dtype=torch.float32, device=dev)
+    lens = torch.empty(nq, dtype=torch.int32, device=dev)
+    if world > 1:
+        g_ids = torch.empty((world, nq, k), dtype=torch.int64, device=dev)
+        g_d = torch.empty((world, nq, k), dtype=torch.float32, device=dev)
+        g_l = torch.empty((world, nq), dtype=torch.int32, device=dev)
+        m_ids = torch.empty((nq, k), dtype=torch.int64, device=dev)
+        m_d = torch.empty((nq, k), dtype=torch.float32, device=dev)
+        m_l = torch.empty(nq, dtype=torch.int32, device=dev)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MiB > 126 MB L2
+
+    def step(q_ptr):
+        N.call("pxc_sq_search_device", idx.handle, q_ptr, nq, k, F, None, *idx._ranges(flt), ids.data_ptr(),
+               dists.data_ptr(), lens.data_ptr(), sp)
+        if world > 1:
+            dist.all_gather_into_tensor(g_ids, ids)
+            dist.all_gather_into_tensor(g_d, dists)
+            dist.all_gather_into_tensor(g_l, lens)
+            N.call("pxc_topk_merge", ctx.handle, g_ids.data_ptr(), g_d.data_ptr(), g_l.data_ptr(), world, nq, k, k,
+                   m_ids.data_ptr(), m_d.data_ptr(), m_l.data_ptr(), sp)
+
+    N.call("pxc_ctx_set_profiling", ctx.handle, 1)
+    for _ in range(max(3, args.warmup)):
+        step(q_dev.data_ptr())
+    torch.cuda.synchronize(dev)
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    sampler = ClockSampler(uuid)
+    sampler.start()
+    launches0 = lib.pxc_ctx_launch_count(ctx.handle)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    scan_ms = []
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    for i in range(args.steps):
+        flush.zero_()  # evict L2 between timed steps (not timed)
+        ev[i][0].record(stream)
+        step(q_dev.data_ptr())
+        ev[i][1].record(stream)
+        scan_ms.append(idx.last_scan_ms())
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    launches = lib.pxc_ctx_launch_count(ctx.handle) - launches0
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    total_ms = torch.tensor([sum(step_ms)], dtype=torch.float64, device=dev)
+    scan_mean = torch.tensor([sum(scan_ms) / len(scan_ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
+        dist.all_reduce(scan_mean, op=dist.ReduceOp.MAX)
+    ms_per_step = total_ms.item() / args.steps
+    clocks = sampler.stop()
+    accepted = idx.last_accepted()
+    fallback = idx.last_fallback()
+    retried = idx.last_retried()
+    res_ids = (m_ids if world > 1 else ids).cpu().numpy().view(np.uint64)
+
+    # ---- e2e: host queries in, host results out, every step ----
+    out_ids = torch.empty((nq, k), dtype=torch.int64).pin_memory()
+    out_d = torch.empty((nq, k), dtype=torch.float32).pin_memory()
+    out_l = torch.empty(nq, dtype=torch.int32).pin_memory()
+    e2e_steps = max(3, min(args.steps, 20))
+
+    def e2e_step():
+        if world == 1:
+            rr, nr = idx._ranges(flt)
+            N.call("pxc_sq_search", idx.handle, q_host.data_ptr(), nq, k, F, None, rr, nr, out_ids.data_ptr(),
+                   out_d.data_ptr(), out_l.data_ptr())
+        else:
+            qd = q_host.to(dev, non_blocking=True)
+            step(qd.data_ptr())
+            out_ids.copy_(m_ids, non_blocking=True)
+            out_d.copy_(m_d, non_blocking=True)
+            out_l.copy_(m_l, non_blocking=True)
+            torch.cuda.synchronize(dev)
+
+    for _ in range(2):
+        e2e_step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    e2e_s = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
+    e2e_qps = nq * e2e_steps / e2e_s.item()
+
+    if rank == 0:
+        hbm, bf16, src = peaks()
+        peak_tops = 2.0 * bf16
+        ops = 2.0 * accepted * dim * nq  # int8 multiply-adds of one step on the accepted rows of this shard
+        achieved = ops / (scan_mean.item() / 1e3) / 1e12 if scan_mean.item() > 0 else None
+        line = {"metric": SQ_METRIC, "value": nq / (ms_per_step / 1e3), "unit": "queries/s", "n_gpus": world,
+                "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms_per_step,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "s8 x s8 -> s32, f32 re-rank",
+                "data": "synthetic",
+                "config": {"workload": f"C5 per GPU: {per:,} x 768 f32 rows of the 50M-row corpus (10,000 unit-sphere "
+                                       "blobs, sigma 0.03, L2-normalised), per-dimension I8 SQ trained over all "
+                                       "shards, year uniform in [2000, 2029], filter year >= 2027, 4,096 queries, "
+                                       "over-fetch 100 on int8, exact cosine re-rank to k=10",
+                           "rows_per_gpu": per, "accepted_rows_per_gpu": accepted, "retried_queries": retried,
+                           "fallback_queries": fallback,
+                           "l2": "flushed (256 MiB write) between timed steps; codes 4.8 GB per GPU",
+                           "generate_s": round(t_gen, 2), "build_s": round(t_build, 2),
+                           "parallelism": "single GPU" if world == 1 else f"row shards x{world} + NCCL allgather"},
+                "clocks": clocks, "gpu_launches": int(launches),
+                "e2e": {"value": e2e_qps, "unit": "queries/s", "h2d_bytes_per_step": nq * dim * 4,
+                        "d2h_bytes_per_step": nq * k * 12 + nq * 4},
+                "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tops, "unit": "TOPS",
+                             "frac": achieved / peak_tops if achieved else None, "traffic": None,
+                             "kernel": "sq_scan_kernel (K12, DENSE prefix + THRESH) with the over-fetch selection",
+                             "kernel_ms": scan_mean.item(), "peak_source": f"2 x dense bf16 {src} = dense int8 rate",
+                             "algorithmic_ops_per_launch": ops}}
+        if keep_host and not args.no_cpu_baseline:
+            line["cpu_baseline"] = sq_cpu_baseline(host, years, queries, res_ids, k, args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    idx.close()
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def sq_cpu_baseline(host, years, queries, gpu_ids, k, seconds):
+    """The reference's CPU answer to the same query: FlatIndex::search with the filter (the oracle port,
+    one query per thread), on a bounded query sample over the full shard; its ids are compared with the
+    GPU's, which must be identical (the re-rank is exact)."""
+    from oracle import pxo
+
+    threads = os.cpu_count() or 1
+    acc = years >= 2027
+    words = np.zeros((len(acc) + 63) // 64, dtype=np.uint64)
+    idx = np.nonzero(acc)[0].astype(np.uint64)
+    np.bitwise_or.at(words, (idx >> np.uint64(6)).astype(np.int64), np.left_shift(np.uint64(1), idx & np.uint64(63)))
+    batch = max(threads, 8)
+    done, same, t0 = 0, 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds and done + batch <= len(queries):
+        ref_ids, _, ref_len = pxo.flat_search(host, queries[done:done + batch], k, pxo.COSINE, bitmap=words,
+                                              nthreads=threads)
+        for i in range(batch):
+            same += int(np.array_equal(gpu_ids[done + i, :ref_len[i]], ref_ids[i, :ref_len[i]]))
+        done += batch
+    el = time.perf_counter() - t0
+    return {"value": done / el if el > 0 else None, "unit": "queries/s", "cores": threads, "kind": "port",
+            "sample": f"{done} of the 4,096 queries, exact filtered FlatIndex::search (cosine, year >= 2027) over the "
+                      f"full {host.shape[0]:,}-row shard ({el:.1f} s, C++ oracle, one query per thread)",
+            "parity": {"queries": done, "identical_ids": same}}
+
+
 def main():
     args = parse()
+    if args.workload == "sq":
+        run_sq(args)
+        return
     if args.workload == "ivfpq":
         run_ivfpq(args)
         return

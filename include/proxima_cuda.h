@@ -378,6 +378,9 @@ pxc_status pxc_sq_search_device(pxc_sq* h, const float* d_queries, uint32_t nq, 
 float pxc_sq_last_scan_ms(pxc_sq* h);
 /* Rows the last search's filter accepted. */
 uint64_t pxc_sq_last_accepted(const pxc_sq* h);
+/* Queries of the last search whose speculative admission key admitted too
+ * few rows and that were scanned again with the safe key. */
+uint32_t pxc_sq_last_retried(const pxc_sq* h);
 /* Queries of the last search whose candidates overflowed the over-fetch
  * buffer and were answered by the exact chunked fallback. */
 uint32_t pxc_sq_last_fallback(const pxc_sq* h);

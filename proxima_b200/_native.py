@@ -142,6 +142,7 @@ SIGNATURES: dict[str, tuple] = {
     "pxc_sq_last_scan_ms": (C.c_float, [vp]),
     "pxc_sq_last_accepted": (C.c_uint64, [vp]),
     "pxc_sq_last_fallback": (C.c_uint32, [vp]),
+    "pxc_sq_last_retried": (C.c_uint32, [vp]),
 }
 
 _lib = None

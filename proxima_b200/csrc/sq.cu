@@ -21,11 +21,17 @@
 //      their I8 codes gathered contiguously;
 //   2. each query is taken to code space, w_c = q_c * scale_g, and quantized
 //      to s8 with one step per query (amax / 127);
-//   3. K12 (sq_tc.cuh): S = q8 . code on tcgen05 s8 MMA; the top `overfetch`
-//      columns by (S desc, rank asc): a DENSE pass over a prefix of the
-//      columns gives each query an admission key, a THRESH pass over the rest
-//      appends only columns at or above it, and a block radix select keeps
-//      the best `overfetch`;
+//   3. K12 (sq_tc.cuh): S = q8 . code on tcgen05 s8 MMA; the top
+//      F = max(overfetch, k) columns by (S desc, rank asc). A DENSE pass over
+//      a prefix of the columns gives each query its prefix top-F; a THRESH
+//      pass over the rest appends only the columns whose key is at or below
+//      an admission key, and a block radix select keeps the best F of the
+//      union. The admission key is speculative, the r-th prefix key with r
+//      sized so that about 4F columns are expected to pass; the result is
+//      exact whenever F keys of the union are at or below it, which the
+//      merge verifies. Queries that fail are scanned again with the F-th
+//      prefix key (always exact), and a query whose candidate buffer still
+//      overflows is answered by DENSE passes over all columns;
 //   4. exact re-rank of those rows with the reference's distance
 //      (cosine 1 - dot_unrolled, inner product -dot_unrolled) and the k
 //      smallest by (total_cmp, id).
@@ -52,7 +58,8 @@
 namespace pxc {
 namespace sq {
 
-constexpr uint32_t PREFIX = 16384;        // columns of the DENSE prefix pass
+constexpr uint32_t PREFIX = 8192;         // columns of the DENSE prefix pass
+constexpr uint64_t SPEC_MARGIN = 4;       // expected admitted columns / F under the speculative key
 constexpr uint32_t QBATCH = 4096;         // queries per scan batch
 constexpr uint32_t CB = 8192;             // merge buffer (keys) per query
 constexpr uint32_t MAX_OVERFETCH = 2048;  // max(overfetch, k)
@@ -273,54 +280,94 @@ __global__ void __launch_bounds__(256) query_s8_kernel(const float* __restrict__
   }
 }
 
-// Admission key per query from its prefix list (the over-fetch-th key, or
-// everything when the prefix held fewer); resets the candidate counts.
-__global__ void tau_kernel(const uint64_t* __restrict__ L, const uint32_t* __restrict__ len, uint32_t nq,
-                           uint32_t F, uint32_t* __restrict__ tau, uint32_t* __restrict__ cnt) {
-  const uint32_t q = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-  const uint32_t lane = threadIdx.x & 31;
-  if (q >= nq) return;
+// Admission keys per query from its prefix list (sorted here): the r-th key
+// (speculative) and the F-th key (safe: F prefix columns are at or below it).
+// A prefix list shorter than F admits everything. One block per query.
+__global__ void __launch_bounds__(128) prefix_taus_kernel(const uint64_t* __restrict__ L, const uint32_t* __restrict__ len,
+                                                          uint32_t F, uint32_t r, uint32_t* __restrict__ tau_spec,
+                                                          uint32_t* __restrict__ tau_safe) {
+  extern __shared__ __align__(16) uint64_t keys[];
+  const uint32_t q = blockIdx.x;
   const uint32_t n = len[q];
-  uint32_t m = 0;
-  for (uint32_t i = lane; i < n; i += 32) m = max(m, static_cast<uint32_t>(L[(size_t)q * F + i] >> 32));
-  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-  if (lane == 0) {
-    tau[q] = n >= F ? m : SENTINEL;
-    cnt[q] = 0;
+  uint32_t n2 = 1;
+  while (n2 < n) n2 <<= 1;
+  for (uint32_t i = threadIdx.x; i < n2; i += blockDim.x) keys[i] = i < n ? L[(size_t)q * F + i] : ~0ull;
+  block_bitonic_sort_u64(keys, n2);
+  if (threadIdx.x == 0) {
+    const bool full = n >= F;
+    tau_spec[q] = full ? static_cast<uint32_t>(keys[r - 1] >> 32) : SENTINEL;
+    tau_safe[q] = full ? static_cast<uint32_t>(keys[F - 1] >> 32) : SENTINEL;
   }
 }
 
+__global__ void gather_u32_kernel(const uint32_t* __restrict__ src, const uint32_t* __restrict__ idx, uint32_t n,
+                                  uint32_t* __restrict__ dst) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) dst[i] = src[idx[i]];
+}
+
 // Per query: the union of its prefix list and its THRESH candidates, cut to
-// the best F. A query whose candidates overflowed the buffer is listed for
-// the exact fallback instead.
+// the best F (candidates taken CB - F at a time, the kept F carried over).
+// The query is listed in `fail` instead when its candidates overflowed the
+// buffer, or (with `verify`) when fewer than F of the union are at or below
+// the admission key it was scanned with: only then is the union's top F
+// certainly the exact top F. A failed query's `next_tau` is a key with at
+// least F columns at or below it (the F-th of the union, or `safe_tau` after
+// an overflow), a valid admission key for its next scan.
 __global__ void __launch_bounds__(256) merge_kernel(const uint64_t* __restrict__ L0, const uint32_t* __restrict__ len0,
                                                     const uint64_t* __restrict__ cand, const uint32_t* __restrict__ cnt,
-                                                    uint32_t cap, uint32_t F, uint64_t* __restrict__ Lf,
-                                                    uint32_t* __restrict__ lenf, uint32_t* __restrict__ ovf,
-                                                    uint32_t* __restrict__ n_ovf) {
+                                                    uint32_t cap, uint32_t F, const uint32_t* __restrict__ verify,
+                                                    const uint32_t* __restrict__ safe_tau, uint64_t* __restrict__ Lf,
+                                                    uint32_t* __restrict__ lenf, uint32_t* __restrict__ next_tau,
+                                                    uint32_t* __restrict__ fail, uint32_t* __restrict__ n_fail) {
   extern __shared__ __align__(16) uint64_t buf[];
   __shared__ uint32_t hist[256], sh[4];
+  __shared__ unsigned long long s_max;
   const uint32_t q = blockIdx.x;
   const uint32_t c = cnt[q];
-  if (c > cap) {
+  const uint32_t l0 = len0[q];
+  if (c > cap || (verify && l0 + c < F)) {
     if (threadIdx.x == 0) {
       lenf[q] = 0;
-      ovf[atomicAdd(n_ovf, 1u)] = q;
+      if (next_tau) next_tau[q] = safe_tau ? safe_tau[q] : SENTINEL;
+      fail[atomicAdd(n_fail, 1u)] = q;
     }
     return;
   }
-  const uint32_t l0 = len0[q];
-  const uint32_t n = l0 + c;
   for (uint32_t i = threadIdx.x; i < l0; i += blockDim.x) buf[i] = L0[(size_t)q * F + i];
-  for (uint32_t i = threadIdx.x; i < c; i += blockDim.x) buf[l0 + i] = cand[(size_t)q * cap + i];
-  __syncthreads();
-  uint32_t keep = n;
-  if (n > F) {
-    select_keep<CB / 256>(buf, n, F, hist, sh);
-    keep = F;
+  uint32_t n = l0;
+  bool selected = false;
+  uint64_t kth = 0;
+  for (uint32_t off = 0; off < c; off += CB - F) {
+    const uint32_t m = min(CB - F, c - off);
+    for (uint32_t i = threadIdx.x; i < m; i += blockDim.x) buf[n + i] = cand[(size_t)q * cap + off + i];
+    n += m;
+    __syncthreads();
+    if (n > F) {
+      kth = select_keep<CB / 256>(buf, n, F, hist, sh);
+      n = F;
+      selected = true;
+    }
   }
-  for (uint32_t i = threadIdx.x; i < keep; i += blockDim.x) Lf[(size_t)q * F + i] = buf[i];
-  if (threadIdx.x == 0) lenf[q] = keep;
+  if (!selected) {
+    if (threadIdx.x == 0) s_max = 0;
+    __syncthreads();
+    unsigned long long mx = 0;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) mx = max(mx, (unsigned long long)buf[i]);
+    atomicMax(&s_max, mx);
+    __syncthreads();
+    kth = s_max;
+  }
+  if (verify && static_cast<uint32_t>(kth >> 32) > verify[q]) {
+    if (threadIdx.x == 0) {
+      lenf[q] = 0;
+      if (next_tau) next_tau[q] = static_cast<uint32_t>(kth >> 32);
+      fail[atomicAdd(n_fail, 1u)] = q;
+    }
+    return;
+  }
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) Lf[(size_t)q * F + i] = buf[i];
+  if (threadIdx.x == 0) lenf[q] = n;
 }
 
 __global__ void gather_lists_kernel(const uint64_t* __restrict__ L, const uint32_t* __restrict__ len,
@@ -423,7 +470,8 @@ struct pxc_sq {
   // search scratch (grown on demand)
   DBuf<uint8_t> flags, codes_c, q8, q8s, sel_tmp;
   DBuf<uint32_t> acc, d_nacc, D, lenz, len0, lenf, lens, lens2, tau, cnt, ovf, n_ovf;
-  DBuf<uint64_t> L0, Lf, Ls, Ls2, cand;
+  DBuf<uint64_t> L0, Lf, Ls, Ls2, L1, L2, cand;
+  DBuf<uint32_t> len1, len2;
   DBuf<float> q_dev;
   DBuf<uint64_t> o_ids;
   DBuf<float> o_dist;
@@ -434,6 +482,7 @@ struct pxc_sq {
   bool timed = false;
   uint64_t last_accepted = 0;
   uint32_t last_fallback = 0;
+  uint32_t last_retried = 0;
   std::mutex mu;
   ~pxc_sq() {
     for (auto& c : columns) {
@@ -599,23 +648,32 @@ uint32_t read_word(pxc_sq* h, const uint32_t* d, cudaStream_t s) {
   return *h->h_word;
 }
 
-// The exact fallback for the queries in `ovf` (device list of n entries):
-// DENSE passes over every column after the prefix, merged chunk by chunk
-// into the query's prefix list, which then replaces its final list.
-void fallback(pxc_sq* h, const int8_t* q8, uint32_t n, const uint8_t* d_codes, uint64_t nacc, uint32_t p0, uint32_t F,
-              cudaStream_t s) {
+// q8 rows idx[0..n) of the batch into q8s (zero-padded to whole query tiles).
+const int8_t* gather_queries(pxc_sq* h, const int8_t* q8, const uint32_t* idx, uint32_t n, cudaStream_t s) {
   const uint32_t pitch = h->pitch;
   const uint32_t n_pad = (uint32_t)round_up(n, sq_tc::BM);
   h->q8s.reserve((size_t)n_pad * pitch);
   PXC_CUDA(cudaMemsetAsync(h->q8s.p, 0, (size_t)n_pad * pitch, s));
   gather_rows16_kernel<<<std::max<uint32_t>(1, std::min<uint32_t>(4096, (n * (pitch / 16) + 255) / 256)), 256, 0, s>>>(
-      reinterpret_cast<const uint8_t*>(q8), h->ovf.p, nullptr, n, pitch, h->q8s.p);
+      reinterpret_cast<const uint8_t*>(q8), idx, nullptr, n, pitch, h->q8s.p);
+  PXC_CUDA(cudaGetLastError());
+  h->ctx->launches += 1;
+  return reinterpret_cast<const int8_t*>(h->q8s.p);
+}
+
+// The exact fallback for the batch queries in `list` (device, n entries):
+// DENSE passes over every column after the prefix, merged chunk by chunk
+// into the query's prefix list, which then replaces its final list.
+void fallback(pxc_sq* h, const int8_t* q8, const uint32_t* list, uint32_t n, const uint8_t* d_codes, uint64_t nacc,
+              uint32_t p0, uint32_t F, cudaStream_t s) {
+  const uint32_t n_pad = (uint32_t)round_up(n, sq_tc::BM);
+  const int8_t* q8s = gather_queries(h, q8, list, n, s);
   h->Ls.reserve((size_t)n * F);
   h->Ls2.reserve((size_t)n * F);
   h->lens.reserve(n);
   h->lens2.reserve(n);
-  gather_lists_kernel<<<n, 256, 0, s>>>(h->L0.p, h->len0.p, h->ovf.p, F, h->Ls.p, h->lens.p);
-  h->ctx->launches += 2;
+  gather_lists_kernel<<<n, 256, 0, s>>>(h->L0.p, h->len0.p, list, F, h->Ls.p, h->lens.p);
+  h->ctx->launches += 1;
   const uint64_t dcap = (uint64_t)sq::QBATCH * PREFIX;
   const uint32_t chunk = (uint32_t)std::max<uint64_t>(sq_tc::BN, dcap / n_pad / sq_tc::BN * sq_tc::BN);
   uint64_t* La = h->Ls.p;
@@ -625,14 +683,31 @@ void fallback(pxc_sq* h, const int8_t* q8, uint32_t n, const uint8_t* d_codes, u
   for (uint64_t c0 = p0; c0 < nacc; c0 += chunk) {
     const uint32_t c1 = (uint32_t)std::min<uint64_t>(nacc, c0 + chunk);
     const uint64_t ld = round_up(c1 - c0, sq_tc::BN);
-    scan_pass<sq_tc::MODE_DENSE>(h, reinterpret_cast<const int8_t*>(h->q8s.p), n, d_codes, nacc, (uint32_t)c0, c1,
+    scan_pass<sq_tc::MODE_DENSE>(h, q8s, n, d_codes, nacc, (uint32_t)c0, c1,
                                  h->D.p, ld, nullptr, nullptr, nullptr, 0, s);
     select_chunk_kernel<<<n, SEL_THREADS, 0, s>>>(La, la, Lb, lb, h->D.p, (uint32_t)ld, c0, c1 - (uint32_t)c0, F, 0);
     h->ctx->launches += 1;
     std::swap(La, Lb);
     std::swap(la, lb);
   }
-  scatter_lists_kernel<<<n, 256, 0, s>>>(La, la, h->ovf.p, F, h->Lf.p, h->lenf.p);
+  scatter_lists_kernel<<<n, 256, 0, s>>>(La, la, list, F, h->Lf.p, h->lenf.p);
+  PXC_CUDA(cudaGetLastError());
+  h->ctx->launches += 1;
+}
+
+// One THRESH pass over columns [p0, nacc) for nb query rows, admitting keys
+// <= tau[q], then the merge with the prefix lists; failures (overflow, or a
+// verification miss when `verify` is given) are listed in fail / n_fail.
+void thresh_round(pxc_sq* h, const int8_t* q8, uint32_t nb, const uint8_t* d_codes, uint64_t nacc, uint32_t p0,
+                  uint32_t F, uint32_t cap, const uint64_t* L0, const uint32_t* len0, const uint32_t* tau,
+                  const uint32_t* verify, const uint32_t* safe_tau, uint64_t* Lout, uint32_t* lenout,
+                  uint32_t* next_tau, uint32_t* fail, uint32_t* n_fail, cudaStream_t s) {
+  PXC_CUDA(cudaMemsetAsync(h->cnt.p, 0, (size_t)nb * 4, s));
+  PXC_CUDA(cudaMemsetAsync(n_fail, 0, 4, s));
+  scan_pass<sq_tc::MODE_THRESH>(h, q8, nb, d_codes, nacc, p0, (uint32_t)nacc, nullptr, 0, tau, h->cand.p, h->cnt.p,
+                                cap, s);
+  merge_kernel<<<nb, 256, CB * 8, s>>>(L0, len0, h->cand.p, h->cnt.p, cap, F, verify, safe_tau, Lout, lenout,
+                                       next_tau, fail, n_fail);
   PXC_CUDA(cudaGetLastError());
   h->ctx->launches += 1;
 }
@@ -648,6 +723,7 @@ void search_device(pxc_sq* h, const float* d_q, uint32_t nq, uint32_t k, uint32_
   if (nq == 0) return;
   h->timed = false;
   h->last_fallback = 0;
+  h->last_retried = 0;
   if (k == 0 || h->nrank == 0) {
     PXC_CUDA(cudaMemsetAsync(d_len, 0, (size_t)nq * 4, s));
     h->last_accepted = 0;
@@ -710,18 +786,23 @@ void search_device(pxc_sq* h, const float* d_q, uint32_t nq, uint32_t k, uint32_
   h->lenf.reserve(qb_max);
   h->L0.reserve((size_t)qb_max * F);
   h->Lf.reserve((size_t)qb_max * F);
-  h->tau.reserve(qb_max);
+  h->tau.reserve(4 * (size_t)qb_max);  // speculative, safe, gathered next, next
   h->cnt.reserve(qb_max);
-  h->ovf.reserve(qb_max);
-  h->n_ovf.reserve(1);
+  h->ovf.reserve(3 * (size_t)qb_max);  // round-1 failures, round-2 failures, fallback list
+  h->n_ovf.reserve(2);
+  h->L1.reserve((size_t)qb_max * F);
+  h->L2.reserve((size_t)qb_max * F);
+  h->len1.reserve(qb_max);
+  h->len2.reserve(qb_max);
   if (nacc > p0) h->cand.reserve((size_t)qb_max * cap);
   PXC_CUDA(cudaMemsetAsync(h->lenz.p, 0, QBATCH * 4, s));
   PXC_CUDA(cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(CB * 8)));
   PXC_CUDA(cudaFuncSetAttribute(rerank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)(MAX_OVERFETCH * 8 + MAX_DIM * 4)));
-  if (const char* e = std::getenv("PXC_SQ_CAP")) {  // diagnostic: shrink the THRESH buffer to force the fallback
+  uint32_t cap_limit = 0xFFFFFFFFu;
+  if (const char* e = std::getenv("PXC_SQ_CAP")) {  // diagnostic: shrink the THRESH buffers to force the fallback
     const long v = std::strtol(e, nullptr, 10);
-    if (v >= 0 && (uint32_t)v < cap) cap = (uint32_t)v;
+    if (v >= 0 && (uint32_t)v < cap) cap = cap_limit = (uint32_t)v;
   }
   if (h->ctx->profiling) {
     if (!h->ev_begin) {
@@ -729,7 +810,14 @@ void search_device(pxc_sq* h, const float* d_q, uint32_t nq, uint32_t k, uint32_
       PXC_CUDA(cudaEventCreate(&h->ev_end));
     }
   }
-  uint32_t fallback_total = 0;
+  uint32_t fallback_total = 0, retried_total = 0;
+  // speculative admission rank: about SPEC_MARGIN * F of the whole set are expected at or below the
+  // r-th key of a p0-column prefix
+  uint32_t r_spec = (uint32_t)std::min<uint64_t>(F, std::max<uint64_t>(1, (SPEC_MARGIN * (uint64_t)F * p0 + nacc - 1) / nacc));
+  if (const char* e = std::getenv("PXC_SQ_SPEC_R")) {  // diagnostic: force the speculative rank
+    const long v = std::strtol(e, nullptr, 10);
+    if (v >= 1 && (uint32_t)v <= F) r_spec = (uint32_t)v;
+  }
   for (uint32_t qb = 0; qb < nq; qb += QBATCH) {
     const uint32_t nb = std::min(QBATCH, nq - qb);
     const uint32_t nb_pad = (uint32_t)round_up(nb, sq_tc::BM);
@@ -750,19 +838,45 @@ void search_device(pxc_sq* h, const float* d_q, uint32_t nq, uint32_t k, uint32_
     const uint64_t* Lfin = h->L0.p;
     const uint32_t* lfin = h->len0.p;
     if (nacc > p0) {
-      // 3b. THRESH over the rest, then the merge
-      tau_kernel<<<(nb + 7) / 8, 256, 0, s>>>(h->L0.p, h->len0.p, nb, F, h->tau.p, h->cnt.p);
-      PXC_CUDA(cudaMemsetAsync(h->n_ovf.p, 0, 4, s));
+      // 3b. THRESH over the rest with a speculative admission key (the r-th
+      // of the prefix), verified by the merge: a query whose union holds F
+      // keys at or below it is exact.
+      uint32_t* tau_spec = h->tau.p;
+      uint32_t* tau_safe = h->tau.p + qb_max;
+      uint32_t* tau_sub = h->tau.p + 2 * (size_t)qb_max;
+      uint32_t* tau_next = h->tau.p + 3 * (size_t)qb_max;
+      uint32_t* fail1 = h->ovf.p;
+      uint32_t* fail2 = h->ovf.p + qb_max;
+      uint32_t* fb_list = h->ovf.p + 2 * (size_t)qb_max;
+      uint32_t n2p = 1;
+      while (n2p < F) n2p <<= 1;
+      prefix_taus_kernel<<<nb, 128, n2p * 8, s>>>(h->L0.p, h->len0.p, F, r_spec, tau_spec, tau_safe);
       h->ctx->launches += 1;
-      scan_pass<sq_tc::MODE_THRESH>(h, q8, nb, d_codes, nacc, p0, (uint32_t)nacc, nullptr, 0, h->tau.p, h->cand.p,
-                                    h->cnt.p, cap, s);
-      merge_kernel<<<nb, 256, CB * 8, s>>>(h->L0.p, h->len0.p, h->cand.p, h->cnt.p, cap, F, h->Lf.p, h->lenf.p,
-                                           h->ovf.p, h->n_ovf.p);
-      PXC_CUDA(cudaGetLastError());
-      h->ctx->launches += 1;
-      const uint32_t n_ovf = read_word(h, h->n_ovf.p, s);
-      if (n_ovf > 0) fallback(h, q8, n_ovf, d_codes, nacc, p0, F, s);
-      fallback_total += n_ovf;
+      thresh_round(h, q8, nb, d_codes, nacc, p0, F, cap, h->L0.p, h->len0.p, tau_spec, r_spec < F ? tau_spec : nullptr,
+                   tau_safe, h->Lf.p, h->lenf.p, tau_next, fail1, h->n_ovf.p, s);
+      const uint32_t n1 = read_word(h, h->n_ovf.p, s);
+      retried_total += n1;
+      if (n1 > 0) {
+        // 3c. the failed queries again with a safe key (F columns are known at or below it), each
+        // with the whole candidate buffer shared among them
+        const int8_t* q8s = gather_queries(h, q8, fail1, n1, s);
+        gather_lists_kernel<<<n1, 256, 0, s>>>(h->L0.p, h->len0.p, fail1, F, h->L1.p, h->len1.p);
+        gather_u32_kernel<<<(n1 + 255) / 256, 256, 0, s>>>(tau_next, fail1, n1, tau_sub);
+        h->ctx->launches += 2;
+        const uint32_t cap2 = (uint32_t)std::min<uint64_t>(0x7FFFFFFFull, (uint64_t)qb_max * (CB - F) / n1);
+        thresh_round(h, q8s, n1, d_codes, nacc, p0, F, std::max(cap, std::min<uint32_t>(cap2, cap_limit)), h->L1.p,
+                     h->len1.p, tau_sub, nullptr, nullptr, h->L2.p, h->len2.p, nullptr, fail2, h->n_ovf.p + 1, s);
+        scatter_lists_kernel<<<n1, 256, 0, s>>>(h->L2.p, h->len2.p, fail1, F, h->Lf.p, h->lenf.p);
+        h->ctx->launches += 1;
+        const uint32_t n2 = read_word(h, h->n_ovf.p + 1, s);
+        if (n2 > 0) {
+          // 3d. overflowing buffers: the exact chunked fallback
+          gather_u32_kernel<<<(n2 + 255) / 256, 256, 0, s>>>(fail1, fail2, n2, fb_list);
+          h->ctx->launches += 1;
+          fallback(h, q8, fb_list, n2, d_codes, nacc, p0, F, s);
+          fallback_total += n2;
+        }
+      }
       Lfin = h->Lf.p;
       lfin = h->lenf.p;
     }
@@ -778,6 +892,7 @@ void search_device(pxc_sq* h, const float* d_q, uint32_t nq, uint32_t k, uint32_
     h->ctx->launches += 1;
   }
   h->last_fallback = fallback_total;
+  h->last_retried = retried_total;
   check_device_status(h->ctx, s, "SQ search (tensor-core scan)");
 }
 
@@ -1187,5 +1302,6 @@ float pxc_sq_last_scan_ms(pxc_sq* h) {
 
 uint64_t pxc_sq_last_accepted(const pxc_sq* h) { return h ? h->last_accepted : 0; }
 uint32_t pxc_sq_last_fallback(const pxc_sq* h) { return h ? h->last_fallback : 0; }
+uint32_t pxc_sq_last_retried(const pxc_sq* h) { return h ? h->last_retried : 0; }
 
 }  // extern "C"

@@ -15,11 +15,11 @@
 //   DENSE   writes every key of columns [c_begin, c_end) to a query-major
 //           matrix (the prefix pass, and the exact fallback);
 //   THRESH  appends only the columns whose key is <= the query's admission
-//           key tau (the over-fetch-th key of the prefix), to a per-query
-//           candidate buffer. Any column above tau is beaten by `overfetch`
-//           prefix columns, so the buffer plus the prefix list holds the
-//           exact top-overfetch. A query whose buffer overflows is reported
-//           through its count and redone with DENSE passes by the host.
+//           key tau to a per-query candidate buffer (one reservation per
+//           lane per tile). The host derives tau from the prefix pass and
+//           checks afterwards that enough columns passed for the result to
+//           be exact; a query whose buffer overflows (its count exceeds the
+//           capacity) is redone by the host.
 //
 // Structure: one CTA per 128 queries x one contiguous range of tiles.
 //   warp 0      TMA producer: the query tile once (kblocks boxes of 128 B x
@@ -53,6 +53,7 @@ constexpr int MAX_KBLOCKS = 8;                        // dim <= 1024
 constexpr size_t SMEM_LIMIT = 227 * 1024;
 constexpr int MODE_DENSE = 0;
 constexpr int MODE_THRESH = 1;
+constexpr uint32_t HIT_BUF = 8;  // THRESH: admitted columns buffered per thread before a flush
 
 struct Params {
   uint32_t* dense;        // DENSE: [nq_rows][dense_ld] keys of columns c_begin..
@@ -91,16 +92,19 @@ __device__ __forceinline__ void record_failure(uint32_t* status, uint32_t code) 
   if (atomicCAS(status, 0u, code) == 0u) atomicExch(status + 1, blockIdx.y * gridDim.x + blockIdx.x);
 }
 
-// Largest of 32 scores (tree: depth 5).
-__device__ __forceinline__ int32_t max32(const uint32_t (&v)[32]) {
-  int32_t m[16];
+// v[j] for a lane-varying j without dynamic register indexing (which would
+// move v to local memory): a five-level select tree.
+__device__ __forceinline__ uint32_t pick32(const uint32_t (&v)[32], uint32_t j) {
+  uint32_t a[16];
 #pragma unroll
-  for (int j = 0; j < 16; ++j) m[j] = max(static_cast<int32_t>(v[j]), static_cast<int32_t>(v[j + 16]));
+  for (int i = 0; i < 16; ++i) a[i] = (j & 16) ? v[i + 16] : v[i];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) m[j] = max(m[j], m[j + 8]);
+  for (int i = 0; i < 8; ++i) a[i] = (j & 8) ? a[i + 8] : a[i];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) m[j] = max(m[j], m[j + 4]);
-  return max(max(m[0], m[2]), max(m[1], m[3]));
+  for (int i = 0; i < 4; ++i) a[i] = (j & 4) ? a[i + 4] : a[i];
+  a[0] = (j & 2) ? a[2] : a[0];
+  a[1] = (j & 2) ? a[3] : a[1];
+  return (j & 1) ? a[1] : a[0];
 }
 
 template <int MODE>
@@ -257,6 +261,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int64_t t = (int64_t)0x80000000ll - (int64_t)p.tau[q];
       sthr = t > 0x7FFFFFFFll ? 0x7FFFFFFF : static_cast<int32_t>(t);
     }
+    // THRESH: admitted (key << 32 | column) pairs wait in a small register
+    // buffer; a full buffer (and the CTA's end) reserves room with one atomic
+    // and stores them, so the epilogue rarely waits on a global atomic.
+    uint64_t hb[HIT_BUF];
+    uint32_t hn = 0;
+    auto flush = [&]() {
+      if (hn == 0) return;
+      const uint32_t pos = atomicAdd(p.cand_cnt + q, hn);
+      uint64_t* dst = p.cand + (size_t)q * p.cap;
+#pragma unroll
+      for (uint32_t i = 0; i < HIT_BUF; ++i)
+        if (i < hn && pos + i < p.cap) dst[pos + i] = hb[i];
+      hn = 0;
+    };
     for (uint32_t t = 0; t < ntile_local; ++t) {
       const uint32_t b = t & 1, use = t >> 1;
       const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&acc_full[b], use & 1, p.wait_ns) && !failed);
@@ -268,50 +286,49 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const uint32_t col_tile = p.c_begin + (t_begin + t) * BN + colhalf * 128;
       const uint32_t taddr = tmem_base + ((quarter * 32) << 16) + b * BN + colhalf * 128;
-      uint32_t v[32];
-      if (MODE == MODE_DENSE) {
+      // two 32-column chunks in flight per wait
 #pragma unroll 1
-        for (uint32_t c = 0; c < 4; ++c) {
-          tmem_ld_32x32b_x32(taddr + c * 32, v);
-          tmem_ld_wait();
-          const uint32_t col0 = col_tile + c * 32;
-          if (qvalid) {
-            uint4* dst = reinterpret_cast<uint4*>(p.dense + (size_t)q * p.dense_ld + (col0 - p.c_begin));
+      for (uint32_t c = 0; c < 4; c += 2) {
+        uint32_t v[2][32];
+        tmem_ld_32x32b_x32(taddr + c * 32, v[0]);
+        tmem_ld_32x32b_x32(taddr + (c + 1) * 32, v[1]);
+        tmem_ld_wait();
 #pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4) {
-              uint32_t k4[4];
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t col0 = col_tile + (c + h) * 32;
+          if (MODE == MODE_DENSE) {
+            if (qvalid) {
+              uint4* dst = reinterpret_cast<uint4*>(p.dense + (size_t)q * p.dense_ld + (col0 - p.c_begin));
 #pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                const uint32_t col = col0 + 4 * j4 + u;
-                k4[u] = col < p.c_end ? score_key(static_cast<int32_t>(v[4 * j4 + u])) : SENTINEL;
+              for (int j4 = 0; j4 < 8; ++j4) {
+                uint32_t k4[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  const uint32_t col = col0 + 4 * j4 + u;
+                  k4[u] = col < p.c_end ? score_key(static_cast<int32_t>(v[h][4 * j4 + u])) : SENTINEL;
+                }
+                dst[j4] = make_uint4(k4[0], k4[1], k4[2], k4[3]);
               }
-              dst[j4] = make_uint4(k4[0], k4[1], k4[2], k4[3]);
             }
-          }
-        }
-      } else {
-        uint32_t hit = 0;
-#pragma unroll 1
-        for (uint32_t c = 0; c < 4; ++c) {
-          tmem_ld_32x32b_x32(taddr + c * 32, v);
-          tmem_ld_wait();
-          hit |= static_cast<uint32_t>(max32(v) >= sthr) << c;
-        }
-        uint32_t uhit = __reduce_or_sync(0xFFFFFFFFu, hit);
-        while (uhit) {  // rare: re-read the flagged chunk and append its admitted columns
-          const uint32_t c = __ffs(uhit) - 1;
-          uhit &= uhit - 1;
-          tmem_ld_32x32b_x32(taddr + c * 32, v);
-          tmem_ld_wait();
-          if (qvalid && ((hit >> c) & 1)) {
-            const uint32_t col0 = col_tile + c * 32;
+          } else {
+            uint32_t m = 0;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int32_t s = static_cast<int32_t>(v[j]);
-              if (s >= sthr && col0 + j < p.c_end) {
-                const uint32_t pos = atomicAdd(p.cand_cnt + q, 1u);
-                if (pos < p.cap)
-                  p.cand[(size_t)q * p.cap + pos] = (static_cast<uint64_t>(score_key(s)) << 32) | (col0 + j);
+            for (int j = 0; j < 32; ++j) m |= static_cast<uint32_t>(static_cast<int32_t>(v[h][j]) >= sthr) << j;
+            const uint32_t lim = p.c_end > col0 ? min(32u, p.c_end - col0) : 0u;
+            if (lim < 32) m &= (1u << lim) - 1u;
+            if (!qvalid) m = 0;
+            // one admitted column per lane per round, rounds while any lane has one left
+            while (__any_sync(0xFFFFFFFFu, m != 0)) {
+              if (m) {
+                const uint32_t j = __ffs(m) - 1;
+                m &= m - 1;
+                const uint64_t key = (static_cast<uint64_t>(score_key(static_cast<int32_t>(pick32(v[h], j)))) << 32) |
+                                     (col0 + j);
+                if (hn == HIT_BUF) flush();
+#pragma unroll
+                for (uint32_t i = HIT_BUF - 1; i > 0; --i) hb[i] = hb[i - 1];
+                hb[0] = key;
+                ++hn;
               }
             }
           }
@@ -320,6 +337,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_before();
       mbar_arrive(&acc_empty[b]);
     }
+    if (MODE == MODE_THRESH) flush();
   }
   tc_fence_before();
   __syncthreads();

@@ -273,3 +273,6 @@ class SqIndex:
 
     def last_fallback(self) -> int:
         return int(N.load().pxc_sq_last_fallback(self.handle))
+
+    def last_retried(self) -> int:
+        return int(N.load().pxc_sq_last_retried(self.handle))

@@ -227,6 +227,27 @@ def test_search_forced_fallback_is_identical(monkeypatch):
     _same(forced, base, "fallback")
 
 
+def test_search_failed_speculation_is_retried_exactly(monkeypatch):
+    """With the speculative admission key forced to the best prefix key, most
+    queries admit fewer than F rows, fail verification and are scanned again
+    with the safe key; the answers do not change."""
+    dim, n = 64, 40000
+    data, years = _corpus(n, dim, 100, 17)
+    queries = fixtures.sphere_blobs(200, dim, 100, fixtures.C5_CENTRES + 17, fixtures.C5_QUERIES + 5, 0.03)
+    idx = SqIndex(dim, Metric.COSINE)
+    idx.set_store(data)
+    sq = idx.train()
+    idx.set_column(0, years)
+    base = idx.search_batch(queries, 10, 100, ranges=[IntRange(0, lo=2001)])
+    monkeypatch.setenv("PXC_SQ_SPEC_R", "1")
+    forced = idx.search_batch(queries, 10, 100, ranges=[IntRange(0, lo=2001)])
+    assert idx.last_retried() > len(queries) // 2
+    _same(forced, base, "retried")
+    acc = years >= 2001
+    _same(forced, _oracle_search(sq, data, np.arange(n, dtype=np.uint64), None, acc, queries, 10, 100, pxo.COSINE),
+          "retried vs oracle")
+
+
 def test_ties_empty_and_edges():
     dim = 32
     base = fixtures.sphere_blobs(50, dim, 5, 77, 78, 0.03)
