@@ -40,6 +40,7 @@
 // -> slot map and per-slot VectorIds, metadata columns as int64 per slot.
 #include <cub/device/device_select.cuh>
 #include <cub/iterator/counting_input_iterator.cuh>
+#include <cuda_pipeline.h>
 
 #include <algorithm>
 #include <cmath>
@@ -280,23 +281,122 @@ __global__ void __launch_bounds__(256) query_s8_kernel(const float* __restrict__
   }
 }
 
-// Admission keys per query from its prefix list (sorted here): the r-th key
-// (speculative) and the F-th key (safe: F prefix columns are at or below it).
-// A prefix list shorter than F admits everything. One block per query.
-__global__ void __launch_bounds__(128) prefix_taus_kernel(const uint64_t* __restrict__ L, const uint32_t* __restrict__ len,
-                                                          uint32_t F, uint32_t r, uint32_t* __restrict__ tau_spec,
-                                                          uint32_t* __restrict__ tau_safe) {
-  extern __shared__ __align__(16) uint64_t keys[];
-  const uint32_t q = blockIdx.x;
-  const uint32_t n = len[q];
+// Top F of the prefix pass per query (block of PSEL_THREADS threads), in
+// place of a general chunk selection: the keys of columns [0, p0) are read
+// from the DENSE matrix into registers; one histogram over their observed
+// range (256 bins, warp-private counters) finds the bin holding the F-th key;
+// only keys in that bin or below survive into shared memory as
+// (key << 32 | column), an exact radix select keeps F of them, and they are
+// sorted. Writes L0 (ascending), len0, and the admission keys tau_spec (the
+// r-th) and tau_safe (the F-th); both are SENTINEL when fewer than F columns
+// exist.
+constexpr uint32_t PSEL_THREADS = 256;
+constexpr uint32_t PSEL_PER = PREFIX / PSEL_THREADS;
+__global__ void __launch_bounds__(PSEL_THREADS) prefix_select_kernel(const uint32_t* __restrict__ D, uint64_t ld,
+                                                                     uint32_t p0, uint32_t F, uint32_t r,
+                                                                     uint64_t* __restrict__ L0, uint32_t* __restrict__ len0,
+                                                                     uint32_t* __restrict__ tau_spec,
+                                                                     uint32_t* __restrict__ tau_safe) {
+  extern __shared__ __align__(16) uint64_t buf[];  // CB entries
+  __shared__ uint32_t hist[PSEL_THREADS / 32][256];
+  __shared__ uint32_t tot[256], hsel[256], sh[4];
+  __shared__ uint32_t s_min, s_max, s_bin, s_cnt;
+  const uint32_t q = blockIdx.x, t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const uint32_t* Dq = D + (size_t)q * ld;
+  uint32_t k[PSEL_PER];
+  uint32_t mn = 0xFFFFFFFFu, mx = 0;
+#pragma unroll
+  for (uint32_t i = 0; i < PSEL_PER; ++i) {
+    const uint32_t c = t + i * PSEL_THREADS;
+    k[i] = c < p0 ? Dq[c] : SENTINEL;
+    if (k[i] != SENTINEL) {
+      mn = min(mn, k[i]);
+      mx = max(mx, k[i]);
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    mn = min(mn, __shfl_xor_sync(0xFFFFFFFFu, mn, o));
+    mx = max(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+  }
+  if (t == 0) {
+    s_min = 0xFFFFFFFFu;
+    s_max = 0;
+    s_cnt = 0;
+  }
+  for (uint32_t b = t; b < 256 * (PSEL_THREADS / 32); b += PSEL_THREADS) (&hist[0][0])[b] = 0;
+  __syncthreads();
+  if (lane == 0) {
+    atomicMin(&s_min, mn);
+    atomicMax(&s_max, mx);
+  }
+  __syncthreads();
+  const uint32_t kmin = s_min, span = s_max - s_min;
+  const uint32_t shift = (s_max < s_min || span < 256) ? 0u : (32u - __clz(span)) - 8u;
+  // lanes of a warp that fall into the same bin add once (the keys crowd a few bins)
+#pragma unroll
+  for (uint32_t i = 0; i < PSEL_PER; ++i) {
+    const bool valid = k[i] != SENTINEL;
+    const uint32_t bin = valid ? (k[i] - kmin) >> shift : 256u;
+    const uint32_t peers = __match_any_sync(0xFFFFFFFFu, bin);
+    if (valid && lane == static_cast<uint32_t>(__ffs(peers) - 1)) atomicAdd(&hist[warp][bin], __popc(peers));
+  }
+  __syncthreads();
+  {
+    uint32_t sum = 0;
+    for (uint32_t w = 0; w < PSEL_THREADS / 32; ++w) sum += hist[w][t & 255];
+    if (t < 256) tot[t] = sum;
+  }
+  __syncthreads();
+  if (warp == 0) {  // prefix sums over the 256 bins: the bin holding the F-th key
+    uint32_t c[8], ssum = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      c[j] = tot[lane * 8 + j];
+      ssum += c[j];
+    }
+    uint32_t inc = ssum;
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t v = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+      if (lane >= (uint32_t)o) inc += v;
+    }
+    const uint32_t total = __shfl_sync(0xFFFFFFFFu, inc, 31);
+    if (lane == 0 && total < F) s_bin = 255;  // fewer than F keys: every one survives
+    uint32_t before = inc - ssum;
+    if (total >= F && before < F && inc >= F) {
+      uint32_t acc = before;
+      for (int j = 0; j < 8; ++j) {
+        acc += c[j];
+        if (acc >= F) {
+          s_bin = lane * 8 + j;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const uint32_t bstar = s_bin;
+#pragma unroll
+  for (uint32_t i = 0; i < PSEL_PER; ++i) {
+    if (k[i] != SENTINEL && ((k[i] - kmin) >> shift) <= bstar)
+      buf[atomicAdd(&s_cnt, 1u)] = (static_cast<uint64_t>(k[i]) << 32) | (t + i * PSEL_THREADS);
+  }
+  __syncthreads();
+  const uint32_t n = s_cnt;
+  uint32_t keep = n;
+  if (n > F) {
+    select_keep<CB / PSEL_THREADS>(buf, n, F, hsel, sh);
+    keep = F;
+  }
   uint32_t n2 = 1;
-  while (n2 < n) n2 <<= 1;
-  for (uint32_t i = threadIdx.x; i < n2; i += blockDim.x) keys[i] = i < n ? L[(size_t)q * F + i] : ~0ull;
-  block_bitonic_sort_u64(keys, n2);
-  if (threadIdx.x == 0) {
-    const bool full = n >= F;
-    tau_spec[q] = full ? static_cast<uint32_t>(keys[r - 1] >> 32) : SENTINEL;
-    tau_safe[q] = full ? static_cast<uint32_t>(keys[F - 1] >> 32) : SENTINEL;
+  while (n2 < keep) n2 <<= 1;
+  for (uint32_t i = keep + t; i < n2; i += PSEL_THREADS) buf[i] = ~0ull;
+  block_bitonic_sort_u64(buf, n2);
+  for (uint32_t i = t; i < keep; i += PSEL_THREADS) L0[(size_t)q * F + i] = buf[i];
+  if (t == 0) {
+    len0[q] = keep;
+    const bool full = keep >= F;
+    tau_spec[q] = full ? static_cast<uint32_t>(buf[r - 1] >> 32) : SENTINEL;
+    tau_safe[q] = full ? static_cast<uint32_t>(buf[F - 1] >> 32) : SENTINEL;
   }
 }
 
@@ -387,43 +487,66 @@ __global__ void scatter_lists_kernel(const uint64_t* __restrict__ Ls, const uint
   if (threadIdx.x == 0) len[q] = n;
 }
 
-// K2 for SQ: exact distances of a query's <= F candidates (eight threads per
-// candidate, thread l running lane l of dot_unrolled, the lanes combined by
-// the same pairwise tree, then the tail), the k smallest by (key, rank).
-__global__ void __launch_bounds__(256) rerank_kernel(const float* __restrict__ Q, uint32_t dim,
-                                                     const uint64_t* __restrict__ Lf, const uint32_t* __restrict__ lenf,
-                                                     uint32_t F, const uint32_t* __restrict__ acc,
-                                                     const uint32_t* __restrict__ rank_slot, const float* __restrict__ rows,
-                                                     const uint64_t* __restrict__ ids, int metric, uint32_t k,
-                                                     uint64_t* __restrict__ out_ids, float* __restrict__ out_dist,
-                                                     uint32_t* __restrict__ out_len) {
+// K2 for SQ: exact distances of a query's <= F candidates and the k
+// smallest by (key, rank). Groups of eight threads take one candidate at a
+// time: the row is first copied into the group's shared-memory slot with
+// asynchronous 16-byte copies (all in flight at once), then thread l runs
+// lane l of dot_unrolled over it, the lanes are combined by the same
+// pairwise tree and the tail is added.
+constexpr uint32_t RR_THREADS = 128;
+constexpr uint32_t RR_GROUPS = RR_THREADS / 8;
+__host__ __device__ inline uint32_t rr_stride(uint32_t dim) { return (dim + 3) / 4 * 4 + 8; }
+__host__ inline size_t rr_smem(uint32_t dim) {
+  return (size_t)MAX_OVERFETCH * 8 + (size_t)rr_stride(dim) * 4 * (RR_GROUPS + 1);
+}
+__global__ void __launch_bounds__(RR_THREADS) rerank_kernel(const float* __restrict__ Q, uint32_t dim,
+                                                            const uint64_t* __restrict__ Lf, const uint32_t* __restrict__ lenf,
+                                                            uint32_t F, const uint32_t* __restrict__ acc,
+                                                            const uint32_t* __restrict__ rank_slot, const float* __restrict__ rows,
+                                                            const uint64_t* __restrict__ ids, int metric, uint32_t k,
+                                                            uint64_t* __restrict__ out_ids, float* __restrict__ out_dist,
+                                                            uint32_t* __restrict__ out_len) {
   extern __shared__ __align__(16) unsigned char smem[];
-  uint64_t* keys = reinterpret_cast<uint64_t*>(smem);  // [n2]
+  uint64_t* keys = reinterpret_cast<uint64_t*>(smem);  // [MAX_OVERFETCH]
+  const uint32_t stride = rr_stride(dim);
+  float* qs = reinterpret_cast<float*>(keys + MAX_OVERFETCH);
+  float* slots = qs + stride;
   const uint32_t q = blockIdx.x;
   const uint32_t n = lenf[q];
   uint32_t n2 = 1;
   while (n2 < n) n2 <<= 1;
-  float* qs = reinterpret_cast<float*>(keys + n2);
   for (uint32_t c = threadIdx.x; c < dim; c += blockDim.x) qs[c] = Q[(size_t)q * dim + c];
   for (uint32_t i = n + threadIdx.x; i < n2; i += blockDim.x) keys[i] = ~0ull;
   __syncthreads();
-  const uint32_t l = threadIdx.x & 7, grp = threadIdx.x >> 3, ngrp = blockDim.x >> 3;
+  const uint32_t l = threadIdx.x & 7, grp = threadIdx.x >> 3;
+  float* slot = slots + (size_t)grp * stride;
   const uint32_t full = dim & ~7u;
-  for (uint32_t base = 0; base < n; base += ngrp) {
+  const bool vec = (dim & 3) == 0;
+  for (uint32_t base = 0; base < n; base += RR_GROUPS) {
     const uint32_t i = base + grp;
     const bool on = i < n;
     uint32_t rank = 0;
-    float a = 0.0f, tail = 0.0f;
     if (on) {
       const uint32_t col = static_cast<uint32_t>(Lf[(size_t)q * F + i]);
       rank = acc ? acc[col] : col;
       const float* x = rows + (size_t)rank_slot[rank] * dim;
-      for (uint32_t e = l; e < full; e += 8) a = __fadd_rn(a, __fmul_rn(qs[e], __ldg(x + e)));
+      if (vec) {
+        for (uint32_t e = 4 * l; e < dim; e += 32) __pipeline_memcpy_async(slot + e, x + e, 16);
+        __pipeline_commit();
+        __pipeline_wait_prior(0);
+      } else {
+        for (uint32_t e = l; e < dim; e += 8) slot[e] = __ldg(x + e);
+      }
+    }
+    __syncwarp();
+    float a = 0.0f, tail = 0.0f;
+    if (on) {
+      for (uint32_t e = l; e < full; e += 8) a = __fadd_rn(a, __fmul_rn(qs[e], slot[e]));
       if (l == 0)
-        for (uint32_t e = full; e < dim; ++e) tail = __fadd_rn(tail, __fmul_rn(qs[e], __ldg(x + e)));
+        for (uint32_t e = full; e < dim; ++e) tail = __fadd_rn(tail, __fmul_rn(qs[e], slot[e]));
     }
     // ((l0+l1)+(l2+l3))+((l4+l5)+(l6+l7)): IEEE addition is commutative, so
-    // the xor-butterfly forms exactly these sums.
+    // the xor-butterfly within the group of eight forms exactly these sums.
     a = __fadd_rn(a, __shfl_xor_sync(0xFFFFFFFFu, a, 1));
     a = __fadd_rn(a, __shfl_xor_sync(0xFFFFFFFFu, a, 2));
     a = __fadd_rn(a, __shfl_xor_sync(0xFFFFFFFFu, a, 4));
@@ -432,6 +555,7 @@ __global__ void __launch_bounds__(256) rerank_kernel(const float* __restrict__ Q
       const float d = metric == PXC_COSINE ? __fsub_rn(1.0f, dot) : -dot;
       keys[i] = (static_cast<uint64_t>(order_key(d)) << 32) | rank;
     }
+    __syncwarp();  // the slot is read before the next copy overwrites it
   }
   block_bitonic_sort_u64(keys, n2);
   const uint32_t take = min(n, k);
@@ -469,7 +593,7 @@ struct pxc_sq {
   std::map<uint32_t, std::pair<DBuf<int64_t>*, DBuf<uint8_t>*>> columns;
   // search scratch (grown on demand)
   DBuf<uint8_t> flags, codes_c, q8, q8s, sel_tmp;
-  DBuf<uint32_t> acc, d_nacc, D, lenz, len0, lenf, lens, lens2, tau, cnt, ovf, n_ovf;
+  DBuf<uint32_t> acc, d_nacc, D, len0, lenf, lens, lens2, tau, cnt, ovf, n_ovf;
   DBuf<uint64_t> L0, Lf, Ls, Ls2, L1, L2, cand;
   DBuf<uint32_t> len1, len2;
   DBuf<float> q_dev;
@@ -781,7 +905,6 @@ void search_device(pxc_sq* h, const float* d_q, uint32_t nq, uint32_t k, uint32_
   const uint32_t qb_pad = (uint32_t)round_up(qb_max, sq_tc::BM);
   h->q8.reserve((size_t)qb_pad * pitch);
   h->D.reserve((size_t)QBATCH * PREFIX);
-  h->lenz.reserve(QBATCH);
   h->len0.reserve(qb_max);
   h->lenf.reserve(qb_max);
   h->L0.reserve((size_t)qb_max * F);
@@ -795,10 +918,9 @@ void search_device(pxc_sq* h, const float* d_q, uint32_t nq, uint32_t k, uint32_
   h->len1.reserve(qb_max);
   h->len2.reserve(qb_max);
   if (nacc > p0) h->cand.reserve((size_t)qb_max * cap);
-  PXC_CUDA(cudaMemsetAsync(h->lenz.p, 0, QBATCH * 4, s));
   PXC_CUDA(cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(CB * 8)));
-  PXC_CUDA(cudaFuncSetAttribute(rerank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)(MAX_OVERFETCH * 8 + MAX_DIM * 4)));
+  PXC_CUDA(cudaFuncSetAttribute(rerank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rr_smem(h->dim)));
+  PXC_CUDA(cudaFuncSetAttribute(prefix_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(CB * 8)));
   uint32_t cap_limit = 0xFFFFFFFFu;
   if (const char* e = std::getenv("PXC_SQ_CAP")) {  // diagnostic: shrink the THRESH buffers to force the fallback
     const long v = std::strtol(e, nullptr, 10);
@@ -831,9 +953,8 @@ void search_device(pxc_sq* h, const float* d_q, uint32_t nq, uint32_t k, uint32_
     // 3a. DENSE prefix and its top-F
     const uint64_t ld0 = round_up(p0, sq_tc::BN);
     scan_pass<sq_tc::MODE_DENSE>(h, q8, nb, d_codes, nacc, 0, p0, h->D.p, ld0, nullptr, nullptr, nullptr, 0, s);
-    // (an empty input list: lenz is zero, so Lf is never read)
-    select_chunk_kernel<<<nb, SEL_THREADS, 0, s>>>(h->Lf.p, h->lenz.p, h->L0.p, h->len0.p, h->D.p, (uint32_t)ld0, 0,
-                                                   p0, F, 0);
+    prefix_select_kernel<<<nb, PSEL_THREADS, CB * 8, s>>>(h->D.p, ld0, p0, F, r_spec, h->L0.p, h->len0.p,
+                                                          h->tau.p, h->tau.p + qb_max);
     h->ctx->launches += 1;
     const uint64_t* Lfin = h->L0.p;
     const uint32_t* lfin = h->len0.p;
@@ -848,10 +969,6 @@ void search_device(pxc_sq* h, const float* d_q, uint32_t nq, uint32_t k, uint32_
       uint32_t* fail1 = h->ovf.p;
       uint32_t* fail2 = h->ovf.p + qb_max;
       uint32_t* fb_list = h->ovf.p + 2 * (size_t)qb_max;
-      uint32_t n2p = 1;
-      while (n2p < F) n2p <<= 1;
-      prefix_taus_kernel<<<nb, 128, n2p * 8, s>>>(h->L0.p, h->len0.p, F, r_spec, tau_spec, tau_safe);
-      h->ctx->launches += 1;
       thresh_round(h, q8, nb, d_codes, nacc, p0, F, cap, h->L0.p, h->len0.p, tau_spec, r_spec < F ? tau_spec : nullptr,
                    tau_safe, h->Lf.p, h->lenf.p, tau_next, fail1, h->n_ovf.p, s);
       const uint32_t n1 = read_word(h, h->n_ovf.p, s);
@@ -885,8 +1002,7 @@ void search_device(pxc_sq* h, const float* d_q, uint32_t nq, uint32_t k, uint32_
       h->timed = true;
     }
     // 4. exact re-rank to k
-    const size_t rsmem = (size_t)MAX_OVERFETCH * 8 + (size_t)h->dim * 4;
-    rerank_kernel<<<nb, 256, rsmem, s>>>(Qb, h->dim, Lfin, lfin, F, acc, h->rank_slot.p, h->rows.p, h->ids.p,
+    rerank_kernel<<<nb, RR_THREADS, rr_smem(h->dim), s>>>(Qb, h->dim, Lfin, lfin, F, acc, h->rank_slot.p, h->rows.p, h->ids.p,
                                          h->metric, k, d_ids + (size_t)qb * k, d_dist + (size_t)qb * k, d_len + qb);
     PXC_CUDA(cudaGetLastError());
     h->ctx->launches += 1;
