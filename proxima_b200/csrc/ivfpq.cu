@@ -224,6 +224,22 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(const ScanParams p) 
       const uint32_t w = widths[s], o = offs[s];
       const float* cb = p.codebooks + 256u * o + t * w;
       float acc = 0.0f;
+      if (w == 8) {  // the common layout: the codeword in two 16-byte loads, the sum in order
+        const float4 c0 = __ldg(reinterpret_cast<const float4*>(cb));
+        const float4 c1 = __ldg(reinterpret_cast<const float4*>(cb) + 1);
+        const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+        for (uint32_t j = 0; j < 8; ++j) {
+          if (dot) {
+            acc = __fadd_rn(acc, __fmul_rn(v[o + j], c[j]));
+          } else {
+            const float d = __fsub_rn(v[o + j], c[j]);
+            acc = __fadd_rn(acc, __fmul_rn(d, d));
+          }
+        }
+        lut[s * 256 + t] = acc;
+        continue;
+      }
       for (uint32_t j = 0; j < w; ++j) {
         const float c = __ldg(cb + j);
         if (dot) {
@@ -288,11 +304,15 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(const ScanParams p) 
             if (on[u]) v = __ldg(reinterpret_cast<const uint4*>(p.list_codes + (size_t)jj[u] * m + s0));
             w4[u][0] = v.x, w4[u][1] = v.y, w4[u][2] = v.z, w4[u][3] = v.w;
           }
+          const float* rows = lut + s0 * 256;
 #pragma unroll
           for (int b = 0; b < 16; ++b) {
-            const float* row = lut + (s0 + b) * 256;
 #pragma unroll
-            for (int u = 0; u < U; ++u) sum[u] = __fadd_rn(sum[u], row[(w4[u][b >> 2] >> (8 * (b & 3))) & 255u]);
+            for (int u = 0; u < U; ++u) {
+              // byte b & 3 of the word, zero-extended (one PRMT)
+              const uint32_t idx = __byte_perm(w4[u][b >> 2], 0u, 0x4440u + (b & 3));
+              sum[u] = __fadd_rn(sum[u], rows[b * 256 + idx]);
+            }
           }
         }
       } else {
