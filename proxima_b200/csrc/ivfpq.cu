@@ -352,12 +352,29 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(const ScanParams p) 
             for (uint32_t s2 = 0; s2 < m; ++s2) sum[u] = __fadd_rn(sum[u], lut[s2 * 256 + code[s2]]);
           }
       }
+      // Admission: the score's order key decides alone unless it ties the
+      // threshold's, so the rank is loaded only for codes that may enter; one
+      // shared-memory reservation per warp and code slot.
+      const uint32_t th_hi = static_cast<uint32_t>(th >> 32);
+      const uint32_t lane = t & 31;
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        if (!on[u]) continue;
         const float score = cosine ? __fadd_rn(one_minus, -sum[u]) : sum[u];
-        const uint64_t key = ((uint64_t)order_key(score) << 32) | p.list_rank[jj[u]];
-        if (key < th) buf[atomicAdd(&count, 1u)] = key;
+        const uint32_t ok = order_key(score);
+        bool want = on[u] && ok <= th_hi;
+        uint64_t key = 0;
+        if (want) {
+          key = ((uint64_t)ok << 32) | p.list_rank[jj[u]];
+          want = key < th;
+        }
+        const uint32_t mask = __ballot_sync(0xFFFFFFFFu, want);
+        if (mask) {
+          const uint32_t leader = __ffs(mask) - 1;
+          uint32_t base = 0;
+          if (lane == leader) base = atomicAdd(&count, static_cast<uint32_t>(__popc(mask)));
+          base = __shfl_sync(0xFFFFFFFFu, base, leader);
+          if (want) buf[base + __popc(mask & ((1u << lane) - 1u))] = key;
+        }
       }
       __syncthreads();
     }
