@@ -64,33 +64,46 @@ __device__ __forceinline__ float space_distance(int metric, const float* a, cons
   return metric == PXC_COSINE ? __fsub_rn(1.0f, dot_unrolled(a, b, dim)) : l2_unrolled(a, b, dim);
 }
 
-// The same sums for dim % 8 == 0 with the row read as two 16-byte loads per
-// group of eight elements (the operation order is unchanged: lane l still
-// takes elements l, l+8, ...).
-__device__ __forceinline__ float space_distance_vec8(int metric, const float* a, const float* __restrict__ b,
-                                                     uint32_t dim) {
-  float acc[8];
+// The same sums for dim % 8 == 0, two rows at once, each row read as two
+// 16-byte loads per group of eight elements (the operation order is
+// unchanged: lane l still takes elements l, l+8, ...; the tail of an
+// 8-multiple is exactly 0.0 and is still added).
+__device__ __forceinline__ void space_distance_vec8x2(int metric, const float* a, const float* __restrict__ b0,
+                                                      const float* __restrict__ b1, uint32_t dim, float& d0,
+                                                      float& d1) {
+  float acc0[8], acc1[8];
 #pragma unroll
-  for (int l = 0; l < 8; ++l) acc[l] = 0.0f;
-  const float4* b4 = reinterpret_cast<const float4*>(b);
+  for (int l = 0; l < 8; ++l) acc0[l] = acc1[l] = 0.0f;
+  const float4* p0 = reinterpret_cast<const float4*>(b0);
+  const float4* p1 = reinterpret_cast<const float4*>(b1);
   const bool cosine = metric == PXC_COSINE;
+#pragma unroll 2
   for (uint32_t i = 0; i < dim; i += 8) {
-    const float4 u = __ldg(b4 + i / 4), w = __ldg(b4 + i / 4 + 1);
-    const float x[8] = {u.x, u.y, u.z, u.w, w.x, w.y, w.z, w.w};
+    const float4 u0 = __ldg(p0 + i / 4), w0 = __ldg(p0 + i / 4 + 1);
+    const float4 u1 = __ldg(p1 + i / 4), w1 = __ldg(p1 + i / 4 + 1);
+    const float x0[8] = {u0.x, u0.y, u0.z, u0.w, w0.x, w0.y, w0.z, w0.w};
+    const float x1[8] = {u1.x, u1.y, u1.z, u1.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
     for (int l = 0; l < 8; ++l) {
+      const float q = a[i + l];
       if (cosine) {
-        acc[l] = __fadd_rn(acc[l], __fmul_rn(a[i + l], x[l]));
+        acc0[l] = __fadd_rn(acc0[l], __fmul_rn(q, x0[l]));
+        acc1[l] = __fadd_rn(acc1[l], __fmul_rn(q, x1[l]));
       } else {
-        const float d = __fsub_rn(a[i + l], x[l]);
-        acc[l] = __fadd_rn(acc[l], __fmul_rn(d, d));
+        const float e0 = __fsub_rn(q, x0[l]), e1 = __fsub_rn(q, x1[l]);
+        acc0[l] = __fadd_rn(acc0[l], __fmul_rn(e0, e0));
+        acc1[l] = __fadd_rn(acc1[l], __fmul_rn(e1, e1));
       }
     }
   }
-  const float s0 = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
-  const float s1 = __fadd_rn(__fadd_rn(acc[4], acc[5]), __fadd_rn(acc[6], acc[7]));
-  const float sum = __fadd_rn(__fadd_rn(s0, s1), 0.0f);  // the tail of an 8-multiple is exactly 0.0
-  return cosine ? __fsub_rn(1.0f, sum) : sum;
+  auto fin = [&](const float (&acc)[8]) {
+    const float s0 = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
+    const float s1 = __fadd_rn(__fadd_rn(acc[4], acc[5]), __fadd_rn(acc[6], acc[7]));
+    const float sum = __fadd_rn(__fadd_rn(s0, s1), 0.0f);
+    return cosine ? __fsub_rn(1.0f, sum) : sum;
+  };
+  d0 = fin(acc0);
+  d1 = fin(acc1);
 }
 
 // ---------------------------------------------------------------------------
@@ -392,12 +405,24 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(const ScanParams p) 
   uint64_t* outk = buf;
   if (p.rerank && p.vectors) {
     // K6: exact distances of the shortlist, top-k of them
-    for (uint32_t i = t; i < n; i += blockDim.x) {
-      const uint32_t rank = (uint32_t)buf[i];
-      const uint32_t slot = p.rank_slot[rank];
-      const float* x = p.vectors + (size_t)slot * dim;
-      const float d = (dim & 7) == 0 ? space_distance_vec8(p.metric, qs, x, dim) : space_distance(p.metric, qs, x, dim);
-      buf[CB / 2 + i] = ((uint64_t)order_key(d) << 32) | rank;
+    if ((dim & 7) == 0) {
+      // two rows per thread at a time: twice the loads in flight
+      for (uint32_t i = t; i < n; i += 2 * blockDim.x) {
+        const uint32_t i1 = i + blockDim.x;
+        const uint32_t r0 = (uint32_t)buf[i];
+        const uint32_t r1 = i1 < n ? (uint32_t)buf[i1] : r0;
+        float d0, d1;
+        space_distance_vec8x2(p.metric, qs, p.vectors + (size_t)p.rank_slot[r0] * dim,
+                              p.vectors + (size_t)p.rank_slot[r1] * dim, dim, d0, d1);
+        buf[CB / 2 + i] = ((uint64_t)order_key(d0) << 32) | r0;
+        if (i1 < n) buf[CB / 2 + i1] = ((uint64_t)order_key(d1) << 32) | r1;
+      }
+    } else {
+      for (uint32_t i = t; i < n; i += blockDim.x) {
+        const uint32_t rank = (uint32_t)buf[i];
+        const float d = space_distance(p.metric, qs, p.vectors + (size_t)p.rank_slot[rank] * dim, dim);
+        buf[CB / 2 + i] = ((uint64_t)order_key(d) << 32) | rank;
+      }
     }
     for (uint32_t i = n + t; i < n2; i += blockDim.x) buf[CB / 2 + i] = ~0ull;
     block_bitonic_sort_u64(buf + CB / 2, n2);
