@@ -16,9 +16,9 @@
 //
 // Search (per batch of queries):
 //   K4 coarse   every centroid's squared_euclidean in the reference's 8-lane
-//               order (proxima_core::distance, unrolled), top-nprobe by
-//               (distance, list index): per-thread partial lists over centroid
-//               ranges, then a merge.
+//               order (proxima_core::distance, unrolled) from the tiled fp32
+//               distance kernel, top-nprobe by (distance, list index) with a
+//               block radix select per query.
 //   K5 scan     one CTA per query: for each probed list, the residual table
 //               (q - c) against every codebook entry (sequential sums, as
 //               ProductQuantizer::distance_table) in shared memory, then the
@@ -40,6 +40,7 @@
 #include "rng.h"
 #include "refdist.cuh"
 #include "select.cuh"
+#include "fp32scan.cuh"
 #include "topk.cuh"
 
 namespace pxc {
@@ -53,9 +54,6 @@ constexpr uint32_t MAX_DIM = 1024;
 constexpr uint32_t SCAN_THREADS = 256;
 constexpr uint32_t CB_MAX = 8192; // candidate buffer per query (shared memory), largest
 constexpr uint32_t CHUNK = 1024;  // codes scored between buffer checks
-constexpr uint32_t QB = 64;       // queries per coarse block
-constexpr uint32_t TCC = 32;      // centroids per coarse smem tile
-constexpr uint32_t CSPLIT = 8;    // centroid ranges per query (coarse)
 
 // VectorSpace::distance for the two metrics search_prepared scores:
 // cosine = 1 - dot_unrolled, euclidean = squared_euclidean.
@@ -107,109 +105,24 @@ __device__ __forceinline__ void space_distance_vec8x2(int metric, const float* a
 }
 
 // ---------------------------------------------------------------------------
-// K4: coarse top-nprobe. Block = QB queries (one thread each, the query
-// transposed into shared memory) x one range of centroids (blockIdx.y); each
-// thread keeps its P best (distance, list) keys sorted in shared memory.
+// K4: coarse top-nprobe. The exact 8-lane squared_euclidean of every (query,
+// centroid) pair (nearest_centroid's order, ivfpq.rs:1231-1249) comes from the
+// tiled fp32 distance kernel as order keys, one row per query; a block-wide
+// radix select keeps the nprobe smallest (key, list) per query and this kernel
+// sorts them ascending into the probe list (UNASSIGNED past the end).
 // ---------------------------------------------------------------------------
-constexpr uint32_t TCS = TCC + 4;  // row stride of the transposed centroid tile (16-byte multiple)
-
-__global__ void __launch_bounds__(QB) coarse_partial_kernel(const float* __restrict__ Q, uint32_t nq, uint32_t dim,
-                                                            const float* __restrict__ C, uint32_t nlist,
-                                                            uint32_t crange, uint32_t P,
-                                                            uint64_t* __restrict__ partial) {
-  extern __shared__ __align__(16) unsigned char sm_raw[];
-  uint64_t* best = reinterpret_cast<uint64_t*>(sm_raw);                 // [P][QB]
-  float* qs = reinterpret_cast<float*>(best + (size_t)P * QB);          // [dim][QB+1]
-  float* cs = qs + (((size_t)dim * (QB + 1) + 3) & ~size_t(3));         // [dim][TCS]
-  const uint32_t t = threadIdx.x;
-  const uint32_t q0 = blockIdx.x * QB;
-  const uint32_t qi = q0 + t;
-  for (uint32_t e = t; e < QB * dim; e += QB) {
-    const uint32_t r = e / dim, i = e - r * dim;
-    qs[i * (QB + 1) + r] = q0 + r < nq ? Q[(size_t)(q0 + r) * dim + i] : 0.0f;
-  }
-  for (uint32_t j = 0; j < P; ++j) best[j * QB + t] = ~0ull;
-  uint32_t have = 0;
-  const uint32_t full = dim & ~7u;
-  auto insert = [&](uint64_t key) {
-    if (have < P || key < best[(P - 1) * QB + t]) {
-      uint32_t pos = have < P ? have++ : P - 1;
-      while (pos > 0 && best[(pos - 1) * QB + t] > key) {
-        best[pos * QB + t] = best[(pos - 1) * QB + t];
-        --pos;
-      }
-      best[pos * QB + t] = key;
-    }
-  };
-  const uint32_t cbeg = blockIdx.y * crange, cend = min(nlist, cbeg + crange);
-  for (uint32_t c0 = cbeg; c0 < cend; c0 += TCC) {
-    const uint32_t cnt = min(TCC, cend - c0);
-    __syncthreads();
-    for (uint32_t e = t; e < TCC * dim; e += QB) {
-      const uint32_t j = e / dim, i = e - j * dim;
-      cs[i * TCS + j] = j < cnt ? C[(size_t)(c0 + j) * dim + i] : 0.0f;
-    }
-    __syncthreads();
-    if (qi >= nq) continue;
-    // four centroids at a time: one query load and one 16-byte centroid load per
-    // dimension feed twelve operations; each centroid keeps its own eight lane sums
-    for (uint32_t j0 = 0; j0 < cnt; j0 += 4) {
-      float acc[4][8];
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-#pragma unroll
-        for (int l = 0; l < 8; ++l) acc[u][l] = 0.0f;
-      for (uint32_t i = 0; i < full; i += 8) {
-#pragma unroll
-        for (int l = 0; l < 8; ++l) {
-          const float qv = qs[(i + l) * (QB + 1) + t];
-          const float4 c4 = *reinterpret_cast<const float4*>(cs + (i + l) * TCS + j0);
-          const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float d = __fsub_rn(qv, cv[u]);
-            acc[u][l] = __fadd_rn(acc[u][l], __fmul_rn(d, d));
-          }
-        }
-      }
-      float tail[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      for (uint32_t i = full; i < dim; ++i) {
-        const float qv = qs[i * (QB + 1) + t];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float d = __fsub_rn(qv, cs[i * TCS + j0 + u]);
-          tail[u] = __fadd_rn(tail[u], __fmul_rn(d, d));
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (j0 + u >= cnt) break;
-        const float x = __fadd_rn(__fadd_rn(acc[u][0], acc[u][1]), __fadd_rn(acc[u][2], acc[u][3]));
-        const float y = __fadd_rn(__fadd_rn(acc[u][4], acc[u][5]), __fadd_rn(acc[u][6], acc[u][7]));
-        const float dist = __fadd_rn(__fadd_rn(x, y), tail[u]);
-        insert(((uint64_t)order_key(dist) << 32) | (c0 + j0 + u));
-      }
-    }
-  }
-  if (qi < nq)
-    for (uint32_t j = 0; j < P; ++j) partial[((size_t)qi * gridDim.y + blockIdx.y) * P + j] = best[j * QB + t];
-}
-
-// Merges the partial lists of each query into its nprobe probed lists, in
-// ascending (distance, list) order.
-__global__ void coarse_merge_kernel(const uint64_t* __restrict__ partial, uint32_t nq, uint32_t parts, uint32_t P,
-                                    uint32_t nprobe, uint32_t* __restrict__ probes) {
-  extern __shared__ __align__(16) unsigned char sm_raw[];
-  uint64_t* s = reinterpret_cast<uint64_t*>(sm_raw);
+__global__ void __launch_bounds__(128) probes_from_lists_kernel(const uint64_t* __restrict__ L,
+                                                                const uint32_t* __restrict__ len, uint32_t P,
+                                                                uint32_t nprobe, uint32_t* __restrict__ probes) {
+  __shared__ uint64_t keys[MAX_NPROBE];
   const uint32_t q = blockIdx.x;
-  const uint32_t total = parts * P;
+  const uint32_t n = min(len[q], P);
   uint32_t n2 = 1;
-  while (n2 < total) n2 <<= 1;
-  for (uint32_t i = threadIdx.x; i < n2; i += blockDim.x)
-    s[i] = i < total ? partial[(size_t)q * total + i] : ~0ull;
-  block_bitonic_sort_u64(s, n2);
+  while (n2 < n) n2 <<= 1;
+  for (uint32_t i = threadIdx.x; i < n2; i += blockDim.x) keys[i] = i < n ? L[(size_t)q * P + i] : ~0ull;
+  block_bitonic_sort_u64(keys, n2);
   for (uint32_t i = threadIdx.x; i < nprobe; i += blockDim.x)
-    probes[(size_t)q * nprobe + i] = s[i] == ~0ull ? UNASSIGNED : (uint32_t)s[i];
+    probes[(size_t)q * nprobe + i] = i < n ? static_cast<uint32_t>(keys[i]) : UNASSIGNED;
 }
 
 struct ScanParams {
@@ -577,8 +490,8 @@ struct pxc_ivfpq {
   pxc::DBuf<uint8_t> list_codes, codes, live;
   bool have_lists = false;
   pxc::DBuf<float> q_buf;
-  pxc::DBuf<uint32_t> probes;
-  pxc::DBuf<uint64_t> partial, io_ids, bitmap;
+  pxc::DBuf<uint32_t> probes, coarse_d, coarse_len, coarse_zero;
+  pxc::DBuf<uint64_t> coarse_l, io_ids, bitmap;
   pxc::DBuf<float> io_dist;
   pxc::DBuf<uint32_t> io_len;
   cudaEvent_t ev_begin = nullptr, ev_end = nullptr;  // scan timing when the context profiles
@@ -655,17 +568,15 @@ void search_device(pxc_ivfpq* h, const float* d_q, uint32_t nq, uint32_t k, uint
   const uint32_t dim = h->dim, nlist = h->nlist;
   // K4: coarse
   const uint32_t P = nprobe;
-  const uint32_t crange = std::max<uint32_t>(TCC, (nlist + CSPLIT - 1) / CSPLIT);
-  const uint32_t parts = (nlist + crange - 1) / crange;
   const uint32_t batch = 16384;
-  h->probes.reserve((size_t)std::min(nq, batch) * nprobe);
-  h->partial.reserve((size_t)std::min(nq, batch) * parts * P);
-  const size_t smem_c = (size_t)P * QB * 8 + ((((size_t)dim * (QB + 1) + 3) & ~size_t(3)) + (size_t)TCS * dim) * 4;
-  PXC_CUDA(cudaFuncSetAttribute(coarse_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_c));
-  uint32_t n2 = 1;
-  while (n2 < parts * P) n2 <<= 1;
-  const size_t smem_m = (size_t)n2 * 8;
-  PXC_CUDA(cudaFuncSetAttribute(coarse_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_m));
+  const uint32_t cpad = (nlist + 63) / 64 * 64;  // distance-matrix row stride (whole 64-column tiles)
+  const uint32_t nbmax = std::min(nq, batch);
+  h->probes.reserve((size_t)nbmax * nprobe);
+  h->coarse_d.reserve((size_t)nbmax * cpad);
+  h->coarse_l.reserve((size_t)nbmax * P);
+  h->coarse_len.reserve(nbmax);
+  h->coarse_zero.reserve(nbmax);
+  PXC_CUDA(cudaMemsetAsync(h->coarse_zero.p, 0, (size_t)nbmax * 4, s));
   uint32_t cb = 4096;
   while (cb < 2 * shortlist || cb < CHUNK + shortlist) cb <<= 1;
   const size_t smem_s = (size_t)cb * 8 + ((size_t)h->m * 256 + 2 * dim) * 4 + (2 * h->m + 1) * 4;
@@ -680,9 +591,12 @@ void search_device(pxc_ivfpq* h, const float* d_q, uint32_t nq, uint32_t k, uint
   for (uint32_t q0 = 0; q0 < nq; q0 += batch) {
     const uint32_t nb = std::min(batch, nq - q0);
     const float* qb = d_q + (size_t)q0 * dim;
-    coarse_partial_kernel<<<dim3((nb + QB - 1) / QB, parts), QB, smem_c, s>>>(qb, nb, dim, h->centroids.p, nlist,
-                                                                            crange, P, h->partial.p);
-    coarse_merge_kernel<<<nb, 256, smem_m, s>>>(h->partial.p, nb, parts, P, nprobe, h->probes.p);
+    dist_chunk_kernel<PXC_EUCLIDEAN><<<dim3(cpad / 64, (nb + 31) / 32), 256, 0, s>>>(
+        qb, nb, h->centroids.p, nlist, dim, 0, cpad, nullptr, nullptr, h->coarse_d.p);
+    // (an empty input list: coarse_zero holds zero lengths, so coarse_l is not read before it is written)
+    select_chunk_kernel<<<nb, SEL_THREADS, 0, s>>>(h->coarse_l.p, h->coarse_zero.p, h->coarse_l.p, h->coarse_len.p,
+                                                   h->coarse_d.p, cpad, 0, nlist, P, 0);
+    probes_from_lists_kernel<<<nb, 128, 0, s>>>(h->coarse_l.p, h->coarse_len.p, P, nprobe, h->probes.p);
     ScanParams sp{};
     sp.queries = qb;
     sp.probes = h->probes.p;
@@ -718,7 +632,7 @@ void search_device(pxc_ivfpq* h, const float* d_q, uint32_t nq, uint32_t k, uint
       h->timed = true;
     }
     PXC_CUDA(cudaGetLastError());
-    ctx->launches += 3;
+    ctx->launches += 4;
   }
 }
 
