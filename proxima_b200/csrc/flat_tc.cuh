@@ -18,8 +18,7 @@
 // Structure: one CTA per 256 queries x one contiguous range of database
 // rows ("split"), 256 database rows per tile.
 //   warp 0      TMA producer: the 256-query tile once, then 256-row database
-//               tiles through a STAGES-deep ring (128-byte swizzle, no
-//               multicast);
+//               tiles through a STAGES-deep ring (128-byte swizzle);
 //   warp 1      allocates all 512 TMEM columns as two 128 x 256 s32
 //               accumulators, one per query half; lane 0 issues tcgen05.mma
 //               (M=128, N=256, K=32 per instruction). N=256 keeps the

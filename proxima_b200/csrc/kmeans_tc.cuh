@@ -15,7 +15,7 @@
 //              to an exact rescan.
 //
 // Structure: one CTA per 256 points and all centroids.
-//   warp 0    TMA producer (128-byte swizzle, no multicast): the point tile
+//   warp 0    TMA producer (128-byte swizzle): the point tile
 //             once, then 256-centroid tiles through a ring of K-block stages;
 //   warp 1    TMEM allocator and MMA issuer: M=128, N=256, K=8 per
 //             tcgen05.mma kind::tf32, one 256-column accumulator per point half;

@@ -1,10 +1,10 @@
 // sm100.cuh — thin inline-PTX wrappers for the Blackwell (sm_100a) features
-// the scan kernels use: mbarriers with bounded waits, non-multicast TMA tile
+// the scan kernels use: mbarriers with bounded waits, TMA tile
 // loads, and the tcgen05 tensor-core family (TMEM alloc, MMA, commit, load).
 //
 // Descriptor bit layouts follow the PTX ISA's "shared memory descriptor" and
 // "instruction descriptor" tables for tcgen05.mma (also mirrored in CUTLASS's
-// cute/arch/mma_sm100_desc.hpp). No TMA multicast is used anywhere.
+// cute/arch/mma_sm100_desc.hpp). Every TMA load fills only the issuing CTA's shared memory.
 #pragma once
 
 #include <cuda.h>
@@ -63,7 +63,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   }
 }
 
-// ---- TMA (tiled, non-multicast) ----
+// ---- TMA (tiled, into the issuing CTA's shared memory) ----
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

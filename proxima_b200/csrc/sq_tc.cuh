@@ -24,7 +24,7 @@
 // Structure: one CTA per 128 queries x one contiguous range of tiles.
 //   warp 0      TMA producer: the query tile once (kblocks boxes of 128 B x
 //               128 rows), then code tiles (128 B x 256 rows per stage)
-//               through a STAGES-deep ring; 128-byte swizzle, no multicast;
+//               through a STAGES-deep ring; 128-byte swizzle;
 //   warp 1      allocates 512 TMEM columns = two 128 x 256 s32 accumulators
 //               and issues tcgen05.mma (M=128, N=256, K=32), alternating
 //               accumulators per tile so the epilogue of tile t overlaps the
