@@ -14,6 +14,7 @@
 #include <cub/device/device_radix_sort.cuh>
 #include <cub/device/device_segmented_radix_sort.cuh>
 #include <cub/device/device_select.cuh>
+#include <cub/iterator/counting_input_iterator.cuh>
 
 #include <algorithm>
 #include <cmath>
@@ -138,6 +139,32 @@ __global__ void build_u8_operand_kernel(const float* __restrict__ rank_rows, uin
   if (threadIdx.x == 0) norms[r] = r < nrank ? acc : flat_tc::BIG;
 }
 
+// Filtered K1: one flag per rank (the filter bitmap is over slots).
+__global__ void rank_flags_kernel(const uint32_t* __restrict__ rank_slot, uint64_t nrank,
+                                  const uint64_t* __restrict__ bitmap, uint8_t* __restrict__ flags) {
+  for (uint64_t r = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; r < nrank; r += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t slot = rank_slot[r];
+    flags[r] = static_cast<uint8_t>((bitmap[slot >> 6] >> (slot & 63)) & 1ull);
+  }
+}
+
+// Filtered K1 operand: row i (of npad) = u8 row acc[i] (zero past nacc), its
+// ||x||^2 (BIG past nacc: never selected) and VectorId. The accepted ranks are
+// in ascending rank order, so the compacted index orders as the id does.
+__global__ void gather_operand_kernel(const uint8_t* __restrict__ op, const int32_t* __restrict__ norms,
+                                      const uint64_t* __restrict__ rank_id, const uint32_t* __restrict__ acc,
+                                      uint64_t nacc, uint32_t dp, uint8_t* __restrict__ out_op,
+                                      int32_t* __restrict__ out_norm, uint64_t* __restrict__ out_id) {
+  const uint64_t i = blockIdx.x;
+  const uint4* src = i < nacc ? reinterpret_cast<const uint4*>(op + (uint64_t)acc[i] * dp) : nullptr;
+  uint4* dst = reinterpret_cast<uint4*>(out_op + i * dp);
+  for (uint32_t w = threadIdx.x; w < dp / 16; w += blockDim.x) dst[w] = src ? __ldg(src + w) : make_uint4(0, 0, 0, 0);
+  if (threadIdx.x == 0) {
+    out_norm[i] = i < nacc ? norms[acc[i]] : flat_tc::BIG;
+    if (i < nacc) out_id[i] = rank_id[acc[i]];
+  }
+}
+
 // Queries for K1: u8 tile [nq_pad][dp], ||q||^2, and a flag if any query
 // component is not an integer in [0,255] (then K1 does not apply).
 __global__ void prep_queries_u8_kernel(const float* __restrict__ Q, uint32_t nq, uint32_t dim,
@@ -236,6 +263,11 @@ struct pxc_flat {
   DBuf<uint8_t> op_u8;
   DBuf<int32_t> op_norm;
   CUtensorMap tmap_x;
+  // filtered K1: the operand of the accepted ranks only (rebuilt per search)
+  DBuf<uint8_t> f_flags, f_op;
+  DBuf<uint32_t> f_acc, f_count;
+  DBuf<int32_t> f_norm;
+  DBuf<uint64_t> f_id;
   // scratch
   DBuf<unsigned char> tmp;
   DBuf<uint32_t> dchunk;
@@ -391,12 +423,21 @@ void launch_tc(const CUtensorMap& tq, const CUtensorMap& tx, const flat_tc::Para
   flat_tc::flat_u8_kernel<KT><<<grid, flat_tc::NUM_THREADS, smem, s>>>(tq, tx, p);
 }
 
-void search_tc(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, uint64_t* d_ids,
+// The database side of one K1 search: the full mirror, or the accepted ranks of a filter.
+struct TcOperand {
+  const CUtensorMap* tmap_x;
+  const int32_t* norms;
+  uint64_t nrank_pad;
+  const uint64_t* rank_id;
+  uint64_t nrank;
+};
+
+void search_tc(pxc_flat* h, const TcOperand& op, const float* d_q, uint32_t nq, uint32_t k, uint64_t* d_ids,
                float* d_dist, uint32_t* d_len, cudaStream_t s) {
   const uint32_t KT = k <= 1 ? 1 : k <= 4 ? 4 : k <= 10 ? 10 : k <= 16 ? 16 : 32;
   const uint32_t nq_pad = (nq + flat_tc::BM - 1) / flat_tc::BM * flat_tc::BM;
   const uint32_t nqt = nq_pad / flat_tc::BM;
-  const uint32_t ntiles = (uint32_t)(h->nrank_pad / flat_tc::BN);
+  const uint32_t ntiles = (uint32_t)(op.nrank_pad / flat_tc::BN);
   const uint32_t nsplit_req = choose_splits(nqt, ntiles, h->ctx->sm_count, KT);
   const uint32_t tps = (ntiles + nsplit_req - 1) / nsplit_req;
   const uint32_t nsplit = (ntiles + tps - 1) / tps;
@@ -408,7 +449,7 @@ void search_tc(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, uint64_t*
   PXC_CUDA(cudaMemsetAsync(h->done.p, 0, nqt * sizeof(uint32_t), s));
   PXC_CUDA(cudaMemsetAsync(h->done.p + nqt, 0xFF, (size_t)nqt * nsplit * sizeof(uint32_t), s));
   flat_tc::Params p;
-  p.norms = h->op_norm.p;
+  p.norms = op.norms;
   p.bound = h->bound.p;
   p.done_count = h->done.p;
   p.done_list = h->done.p + nqt;
@@ -428,11 +469,11 @@ void search_tc(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, uint64_t*
   dim3 grid(nqt, nsplit);
   ScanTimer timer(h, s);
   switch (KT) {
-    case 1: launch_tc<1>(tmap_q, h->tmap_x, p, grid, smem, s); break;
-    case 4: launch_tc<4>(tmap_q, h->tmap_x, p, grid, smem, s); break;
-    case 10: launch_tc<10>(tmap_q, h->tmap_x, p, grid, smem, s); break;
-    case 16: launch_tc<16>(tmap_q, h->tmap_x, p, grid, smem, s); break;
-    default: launch_tc<32>(tmap_q, h->tmap_x, p, grid, smem, s); break;
+    case 1: launch_tc<1>(tmap_q, *op.tmap_x, p, grid, smem, s); break;
+    case 4: launch_tc<4>(tmap_q, *op.tmap_x, p, grid, smem, s); break;
+    case 10: launch_tc<10>(tmap_q, *op.tmap_x, p, grid, smem, s); break;
+    case 16: launch_tc<16>(tmap_q, *op.tmap_x, p, grid, smem, s); break;
+    default: launch_tc<32>(tmap_q, *op.tmap_x, p, grid, smem, s); break;
   }
   PXC_CUDA(cudaGetLastError());
   timer.stop();
@@ -442,7 +483,7 @@ void search_tc(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, uint64_t*
   size_t msmem = cap * sizeof(uint64_t);
   if (msmem > 48 * 1024)
     PXC_CUDA(cudaFuncSetAttribute(merge_u8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msmem));
-  merge_u8_kernel<<<nq, 256, msmem, s>>>(h->part.p, nsplit, KT, cap, k, h->q_norm.p, h->rank_id.p, (uint32_t)h->nrank,
+  merge_u8_kernel<<<nq, 256, msmem, s>>>(h->part.p, nsplit, KT, cap, k, h->q_norm.p, op.rank_id, (uint32_t)op.nrank,
                                          d_ids, d_dist, d_len);
   PXC_CUDA(cudaGetLastError());
 }
@@ -531,7 +572,7 @@ void search_device(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, const
     PXC_CUDA(cudaMemsetAsync(d_len, 0, nq * sizeof(uint32_t), s));
     return;
   }
-  bool tc = h->all_u8 && h->metric == PXC_EUCLIDEAN && d_bitmap == nullptr && k <= 32 &&
+  bool tc = h->all_u8 && h->metric == PXC_EUCLIDEAN && k <= 32 &&
             h->dim <= (uint32_t)flat_tc::MAX_KBLOCKS * flat_tc::KB_BYTES && h->nrank_pad > 0;
   if (tc) {
     const uint32_t nq_pad = (nq + flat_tc::BM - 1) / flat_tc::BM * flat_tc::BM;
@@ -547,7 +588,39 @@ void search_device(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, const
     tc = (*h->h_flag == 0);
   }
   if (tc) {
-    search_tc(h, d_q, nq, k, d_ids, d_dist, d_len, s);
+    TcOperand op{&h->tmap_x, h->op_norm.p, h->nrank_pad, h->rank_id.p, h->nrank};
+    CUtensorMap tmap_f;
+    if (d_bitmap) {
+      // the filter's accepted ranks, compacted in rank order, as K1's database
+      h->f_flags.reserve(h->nrank);
+      h->f_acc.reserve(h->nrank);
+      h->f_count.reserve(1);
+      rank_flags_kernel<<<grid1d(h->nrank, 256), 256, 0, s>>>(h->rank_slot.p, h->nrank, d_bitmap, h->f_flags.p);
+      size_t tb = 0;
+      cub::CountingInputIterator<uint32_t> it(0);
+      PXC_CUDA(cub::DeviceSelect::Flagged(nullptr, tb, it, h->f_flags.p, h->f_acc.p, h->f_count.p, (int64_t)h->nrank, s));
+      h->tmp.reserve(std::max<size_t>(tb, 1));
+      PXC_CUDA(cub::DeviceSelect::Flagged(h->tmp.p, tb, it, h->f_flags.p, h->f_acc.p, h->f_count.p, (int64_t)h->nrank, s));
+      PXC_CUDA(cudaMemcpyAsync(h->h_flag, h->f_count.p, sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
+      PXC_CUDA(cudaStreamSynchronize(s));
+      const uint64_t nacc = static_cast<uint32_t>(*h->h_flag);
+      h->ctx->launches += 3;
+      if (nacc == 0) {
+        PXC_CUDA(cudaMemsetAsync(d_len, 0, nq * sizeof(uint32_t), s));
+        return;
+      }
+      const uint64_t npad = (nacc + flat_tc::BN - 1) / flat_tc::BN * flat_tc::BN;
+      h->f_op.reserve(npad * h->dp);
+      h->f_norm.reserve(npad);
+      h->f_id.reserve(npad);
+      gather_operand_kernel<<<(unsigned)npad, 64, 0, s>>>(h->op_u8.p, h->op_norm.p, h->rank_id.p, h->f_acc.p, nacc,
+                                                         h->dp, h->f_op.p, h->f_norm.p, h->f_id.p);
+      PXC_CUDA(cudaGetLastError());
+      h->ctx->launches += 1;
+      make_tmap_u8_2d(&tmap_f, h->f_op.p, h->dp, npad, flat_tc::KB_BYTES, flat_tc::BN);
+      op = TcOperand{&tmap_f, h->f_norm.p, npad, h->f_id.p, nacc};
+    }
+    search_tc(h, op, d_q, nq, k, d_ids, d_dist, d_len, s);
     check_device_status(h->ctx, s, "flat search (tensor-core scan)");
   } else {
     search_generic(h, d_q, nq, k, d_bitmap, d_ids, d_dist, d_len, s);

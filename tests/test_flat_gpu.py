@@ -214,6 +214,40 @@ def test_c2_filtered_and_non_integer(c2_small):
     _assert_same(got, ref, 64)
 
 
+def _bitmap(keep):
+    bm = np.packbits(keep, bitorder="little")
+    return np.concatenate([bm, np.zeros(-len(bm) % 8, np.uint8)]).view(np.uint64)
+
+
+@pytest.mark.parametrize("k", [1, 10, 32])
+def test_c2_filtered_tensor_core_path_bit_exact(c2_small, k):
+    """A filter on an integer euclidean store runs on the tensor-core scan over
+    the accepted rows; ids not in slot order and dead slots included."""
+    db, q = c2_small
+    n = 60_000
+    rows = db[:n]
+    rng = np.random.default_rng(k)
+    ids = rng.permutation(n).astype(np.uint64) * 5 + 3
+    live = (rng.random(n) > 0.1).astype(np.uint8)
+    h = N.vp()
+    from proxima_b200.index import Context
+    ctx = Context.default()
+    N.call("pxc_flat_create", ctx.handle, 128, 0, C.byref(h))
+    N.call("pxc_flat_sync", h, N.ptr(rows), N.ptr(ids), N.ptr(live), 0, n)
+    nq = 300
+    for keep in ((rng.random(n) < 0.1), (np.arange(n) % 2 == 0), np.zeros(n, bool), np.ones(n, bool),
+                 (np.arange(n) < 5)):
+        bm = _bitmap(keep)
+        oid = np.zeros((nq, k), np.uint64)
+        od = np.zeros((nq, k), np.float32)
+        ol = np.zeros(nq, np.uint32)
+        N.call("pxc_flat_search", h, N.ptr(q[:nq]), nq, k, N.ptr(bm), N.ptr(oid), N.ptr(od), N.ptr(ol))
+        assert N.load().pxc_flat_path(h) == 1
+        ref = pxo.flat_search(rows, q[:nq], k, pxo.EUCLIDEAN, ids=ids, live=live, bitmap=bm)
+        _assert_same((oid, od, ol), ref, nq)
+    N.load().pxc_flat_destroy(h)
+
+
 @pytest.mark.parametrize("metric", [Metric.EUCLIDEAN, Metric.INNER_PRODUCT, Metric.MANHATTAN, Metric.COSINE])
 @pytest.mark.parametrize("dim", [3, 37, 96])
 def test_generic_metrics_bit_exact(metric, dim):
