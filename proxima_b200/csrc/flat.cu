@@ -14,7 +14,7 @@
 #include <cub/device/device_radix_sort.cuh>
 #include <cub/device/device_segmented_radix_sort.cuh>
 #include <cub/device/device_select.cuh>
-#include <cub/iterator/counting_input_iterator.cuh>
+#include <thrust/iterator/counting_iterator.h>
 
 #include <algorithm>
 #include <cmath>
@@ -597,7 +597,7 @@ void search_device(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, const
       h->f_count.reserve(1);
       rank_flags_kernel<<<grid1d(h->nrank, 256), 256, 0, s>>>(h->rank_slot.p, h->nrank, d_bitmap, h->f_flags.p);
       size_t tb = 0;
-      cub::CountingInputIterator<uint32_t> it(0);
+      thrust::counting_iterator<uint32_t> it(0);
       PXC_CUDA(cub::DeviceSelect::Flagged(nullptr, tb, it, h->f_flags.p, h->f_acc.p, h->f_count.p, (int64_t)h->nrank, s));
       h->tmp.reserve(std::max<size_t>(tb, 1));
       PXC_CUDA(cub::DeviceSelect::Flagged(h->tmp.p, tb, it, h->f_flags.p, h->f_acc.p, h->f_count.p, (int64_t)h->nrank, s));

@@ -39,7 +39,7 @@
 // codes in rank order with a 128-byte-multiple pitch (zero padded), the rank
 // -> slot map and per-slot VectorIds, metadata columns as int64 per slot.
 #include <cub/device/device_select.cuh>
-#include <cub/iterator/counting_input_iterator.cuh>
+#include <thrust/iterator/counting_iterator.h>
 #include <cuda_pipeline.h>
 
 #include <algorithm>
@@ -130,6 +130,94 @@ __global__ void __launch_bounds__(256) range_kernel(const float* __restrict__ X,
     atomicMax(o.kmax + g, kmax);
     if (zn != ~0ull) atomicMin(o.zneg + g, zn);
     if (zp != ~0ull) atomicMin(o.zpos + g, zp);
+  }
+}
+
+// The same for dim % 4 == 0: each lane folds four adjacent columns read as one
+// 16-byte load, four rows in flight; a warp covers 128 columns.
+__global__ void __launch_bounds__(256) range4_kernel(const float* __restrict__ X, uint64_t ld,
+                                                    const uint32_t* __restrict__ row_map, uint64_t n,
+                                                    uint32_t dim, int global, uint64_t rows_per_block,
+                                                    RangeOut o) {
+  __shared__ uint32_t s_min[8][128], s_max[8][128];
+  __shared__ unsigned long long s_zn[8][128], s_zp[8][128];
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t c0 = blockIdx.y * 128 + lane * 4;
+  const uint64_t r0 = blockIdx.x * rows_per_block;
+  const uint64_t r1 = min(n, r0 + rows_per_block);
+  uint32_t kmin[4], kmax[4];
+  unsigned long long zn[4], zp[4], bad = ~0ull;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    kmin[u] = 0xFFFFFFFFu;
+    kmax[u] = 0;
+    zn[u] = zp[u] = ~0ull;
+  }
+  auto fold = [&](float v, uint64_t r, int u) {
+    const unsigned long long idx = r * dim + c0 + u;
+    if (!isfinite(v)) {
+      bad = min(bad, idx);
+      return;
+    }
+    const uint32_t k = class_key(v);
+    kmin[u] = min(kmin[u], k);
+    kmax[u] = max(kmax[u], k);
+    if (v == 0.0f) {
+      if (signbit(v)) zn[u] = min(zn[u], idx);
+      else zp[u] = min(zp[u], idx);
+    }
+  };
+  if (c0 < dim) {
+    uint64_t r = r0 + warp;
+    for (; r + 24 < r1; r += 32) {  // four rows of this warp in flight, folded in row order
+      float4 v[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint64_t rr = r + 8 * j;
+        v[j] = __ldg(reinterpret_cast<const float4*>(X + (row_map ? (uint64_t)row_map[rr] : rr) * ld + c0));
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        fold(v[j].x, r + 8 * j, 0);
+        fold(v[j].y, r + 8 * j, 1);
+        fold(v[j].z, r + 8 * j, 2);
+        fold(v[j].w, r + 8 * j, 3);
+      }
+    }
+    for (; r < r1; r += 8) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(X + (row_map ? (uint64_t)row_map[r] : r) * ld + c0));
+      fold(v.x, r, 0);
+      fold(v.y, r, 1);
+      fold(v.z, r, 2);
+      fold(v.w, r, 3);
+    }
+  }
+  if (bad != ~0ull) atomicMin(o.bad, bad);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    s_min[warp][lane * 4 + u] = kmin[u];
+    s_max[warp][lane * 4 + u] = kmax[u];
+    s_zn[warp][lane * 4 + u] = zn[u];
+    s_zp[warp][lane * 4 + u] = zp[u];
+  }
+  __syncthreads();
+  if (threadIdx.x < 128) {
+    const uint32_t cc = threadIdx.x, c = blockIdx.y * 128 + cc;
+    if (c < dim) {
+      uint32_t mn = s_min[0][cc], mx = s_max[0][cc];
+      unsigned long long a = s_zn[0][cc], b = s_zp[0][cc];
+      for (int w = 1; w < 8; ++w) {
+        mn = min(mn, s_min[w][cc]);
+        mx = max(mx, s_max[w][cc]);
+        a = min(a, s_zn[w][cc]);
+        b = min(b, s_zp[w][cc]);
+      }
+      const uint32_t g = global ? 0 : c;
+      atomicMin(o.kmin + g, mn);
+      atomicMax(o.kmax + g, mx);
+      if (a != ~0ull) atomicMin(o.zneg + g, a);
+      if (b != ~0ull) atomicMin(o.zpos + g, b);
+    }
   }
 }
 
@@ -332,14 +420,9 @@ __global__ void __launch_bounds__(PSEL_THREADS) prefix_select_kernel(const uint3
   __syncthreads();
   const uint32_t kmin = s_min, span = s_max - s_min;
   const uint32_t shift = (s_max < s_min || span < 256) ? 0u : (32u - __clz(span)) - 8u;
-  // lanes of a warp that fall into the same bin add once (the keys crowd a few bins)
 #pragma unroll
-  for (uint32_t i = 0; i < PSEL_PER; ++i) {
-    const bool valid = k[i] != SENTINEL;
-    const uint32_t bin = valid ? (k[i] - kmin) >> shift : 256u;
-    const uint32_t peers = __match_any_sync(0xFFFFFFFFu, bin);
-    if (valid && lane == static_cast<uint32_t>(__ffs(peers) - 1)) atomicAdd(&hist[warp][bin], __popc(peers));
-  }
+  for (uint32_t i = 0; i < PSEL_PER; ++i)
+    if (k[i] != SENTINEL) atomicAdd(&hist[warp][(k[i] - kmin) >> shift], 1u);
   __syncthreads();
   {
     uint32_t sum = 0;
@@ -646,13 +729,18 @@ void ranges_device(pxc_ctx* ctx, const float* d_x, const uint32_t* d_row_map, ui
   PXC_CUDA(cudaMemsetAsync(o.kmin, 0xFF, groups * 4, s));
   PXC_CUDA(cudaMemsetAsync(o.kmax, 0, groups * 4, s));
   PXC_CUDA(cudaMemsetAsync(o.zneg, 0xFF, (size_t)groups * 16 + 8, s));
-  const uint32_t cgroups = (dim + 31) / 32;
+  const bool vec = dim % 4 == 0 && (reinterpret_cast<uintptr_t>(d_x) & 15) == 0;
+  const uint32_t cgroups = vec ? (dim + 127) / 128 : (dim + 31) / 32;
   const uint64_t target_blocks = (uint64_t)ctx->sm_count * 8;
   uint64_t rblocks = std::max<uint64_t>(1, target_blocks / cgroups);
   const uint64_t rows_per_block = std::max<uint64_t>(64, (n + rblocks - 1) / rblocks);
   rblocks = (n + rows_per_block - 1) / rows_per_block;
-  range_kernel<<<dim3((unsigned)rblocks, cgroups), 256, 0, s>>>(d_x, dim, d_row_map, n, dim,
-                                                                 mode == PXC_RANGE_GLOBAL, rows_per_block, o);
+  if (vec)
+    range4_kernel<<<dim3((unsigned)rblocks, cgroups), 256, 0, s>>>(d_x, dim, d_row_map, n, dim,
+                                                                    mode == PXC_RANGE_GLOBAL, rows_per_block, o);
+  else
+    range_kernel<<<dim3((unsigned)rblocks, cgroups), 256, 0, s>>>(d_x, dim, d_row_map, n, dim,
+                                                                   mode == PXC_RANGE_GLOBAL, rows_per_block, o);
   PXC_CUDA(cudaGetLastError());
   ctx->launches += 1;
   std::vector<uint8_t> h(bytes);
@@ -875,7 +963,7 @@ void search_device(pxc_sq* h, const float* d_q, uint32_t nq, uint32_t k, uint32_
     const unsigned g = (unsigned)std::min<uint64_t>((h->nrank + 255) / 256, (uint64_t)h->ctx->sm_count * 16);
     accept_kernel<<<g, 256, 0, s>>>(h->rank_slot.p, h->nrank, d_bitmap, f, h->flags.p);
     size_t tmp = 0;
-    cub::CountingInputIterator<uint32_t> it(0);
+    thrust::counting_iterator<uint32_t> it(0);
     PXC_CUDA(cub::DeviceSelect::Flagged(nullptr, tmp, it, h->flags.p, h->acc.p, h->d_nacc.p, (int64_t)h->nrank, s));
     h->sel_tmp.reserve(std::max<size_t>(tmp, 1));
     PXC_CUDA(cub::DeviceSelect::Flagged(h->sel_tmp.p, tmp, it, h->flags.p, h->acc.p, h->d_nacc.p, (int64_t)h->nrank, s));
