@@ -59,7 +59,7 @@
 namespace pxc {
 namespace sq {
 
-constexpr uint32_t PREFIX = 8192;         // columns of the DENSE prefix pass
+constexpr uint32_t PREFIX = 4096;         // columns of the DENSE prefix pass
 constexpr uint64_t SPEC_MARGIN = 4;       // expected admitted columns / F under the speculative key
 constexpr uint32_t QBATCH = 4096;         // queries per scan batch
 constexpr uint32_t CB = 8192;             // merge buffer (keys) per query

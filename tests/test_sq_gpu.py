@@ -301,3 +301,72 @@ def test_top10_equals_exact_filtered_flat():
     assert np.array_equal(gl, rl)
     assert np.array_equal(gi, ri)
     assert np.array_equal(_bits(gd), _bits(rd))
+
+
+def test_row_shards_merge_like_the_per_shard_composition():
+    """The C5 multi-GPU form on one GPU: two row shards with global VectorIds, one
+    quantizer from the shards' ranges folded in shard order, each shard's exact
+    top-k merged on the device (pxc_topk_merge) — equal to the oracle run per
+    shard and merged by (total_cmp, id)."""
+    import torch
+
+    from proxima_b200 import _native as N
+    from proxima_b200.sq import ranges_device
+
+    dim, n, k, F = 64, 30000, 10, 100
+    data, years = _corpus(n, dim, 120, 41)
+    queries = fixtures.sphere_blobs(120, dim, 120, fixtures.C5_CENTRES + 41, fixtures.C5_QUERIES + 6, 0.03)
+    cut = 13000
+    parts = [(0, cut), (cut, n)]
+    lows, highs = [], []
+    for a, b in parts:
+        lo, hi = ranges_device(torch.from_numpy(data[a:b]).cuda(), dim)
+        lows.append(lo)
+        highs.append(hi)
+    mn, sc, inv = combine_ranges(lows, highs)
+    quant = ScalarQuantizer(dim, RangeMode.PER_DIMENSION, CodeType.I8, mn, sc, inv)
+    ref_m, ref_sc, ref_inv = pxo.sq_train(data, pxo.RANGE_PER_DIMENSION)
+    assert np.array_equal(_bits(mn), _bits(ref_m)) and np.array_equal(_bits(inv), _bits(ref_inv))
+    nq = len(queries)
+    g_ids = torch.zeros((2, nq, k), dtype=torch.int64, device="cuda")
+    g_d = torch.zeros((2, nq, k), dtype=torch.float32, device="cuda")
+    g_l = torch.zeros((2, nq), dtype=torch.int32, device="cuda")
+    oracle_parts = []
+    for r, (a, b) in enumerate(parts):
+        idx = SqIndex(dim, Metric.COSINE)
+        ids = np.arange(a, b, dtype=np.uint64)
+        idx.set_store(data[a:b], ids=ids)
+        idx.set_quantizer(quant)
+        idx.set_column(0, years[a:b])
+        gi, gd, gl = idx.search_batch(queries, k, F, ranges=[IntRange(0, lo=2025)])
+        g_ids[r] = torch.from_numpy(gi.view(np.int64)).cuda()
+        g_d[r] = torch.from_numpy(gd).cuda()
+        g_l[r] = torch.from_numpy(gl.view(np.int32)).cuda()
+        oracle_parts.append(_oracle_search(quant, data[a:b], ids, None, years[a:b] >= 2025, queries, k, F, pxo.COSINE))
+        idx.close()
+    m_ids = torch.zeros((nq, k), dtype=torch.int64, device="cuda")
+    m_d = torch.zeros((nq, k), dtype=torch.float32, device="cuda")
+    m_l = torch.zeros(nq, dtype=torch.int32, device="cuda")
+    from proxima_b200.index import Context
+
+    ctx = Context.default()
+    N.call("pxc_topk_merge", ctx.handle, g_ids.data_ptr(), g_d.data_ptr(), g_l.data_ptr(), 2, nq, k, k,
+           m_ids.data_ptr(), m_d.data_ptr(), m_l.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    got = (m_ids.cpu().numpy().view(np.uint64), m_d.cpu().numpy(), m_l.cpu().numpy().view(np.uint32))
+    # the oracle's per-shard answers merged by (total_cmp(distance), id)
+    ri = np.zeros((nq, k), np.uint64)
+    rd = np.zeros((nq, k), np.float32)
+    rl = np.zeros(nq, np.uint32)
+    def total_key(x):  # f32::total_cmp as a signed integer order
+        v = int(np.float32(x).view(np.int32))
+        return v ^ ((v >> 31) & 0x7FFFFFFF)
+
+    for q in range(nq):
+        cands = [(total_key(pd[q, j]), int(pi[q, j]), pd[q, j]) for pi, pd, pl in oracle_parts
+                 for j in range(int(pl[q]))]
+        cands.sort(key=lambda c: (c[0], c[1]))
+        for j, c in enumerate(cands[:k]):
+            ri[q, j], rd[q, j] = c[1], c[2]
+        rl[q] = min(k, len(cands))
+    _same(got, (ri, rd, rl), "merged shards")
