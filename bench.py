@@ -289,7 +289,7 @@ def run_kmeans(args):
                         "d2h_bytes_per_step": k * dim * 4 + n * 4},
                 "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf32, "unit": "TFLOP/s",
                              "frac": achieved / tf32 if achieved else None, "traffic": None,
-                             "kernel": "km_tc::screen_kernel (K7a; MIN and CAND screening passes, mean per launch)",
+                             "kernel": "km_tc::screen_kernel (K7a, CAND pass: the assignment screen of every iteration)",
                              "kernel_ms": per_pass,
                              "peak_source": f"dense bf16 {src} / 2 = dense tf32 rate",
                              "algorithmic_flops_per_launch": flops}}
