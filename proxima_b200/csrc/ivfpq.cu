@@ -144,7 +144,7 @@ struct ScanParams {
   uint32_t* out_len;
   unsigned long long* scanned;  // codes scored, summed over queries
   uint32_t nq, dim, m, nprobe, k, shortlist;
-  uint32_t cb;  // candidate buffer entries (a power of two >= 2 * shortlist, >= CHUNK + shortlist)
+  uint32_t cb;  // candidate buffer entries (>= shortlist + 2 * CHUNK, >= 4096, <= CB_MAX)
   int metric;
   int rerank;
 };
@@ -314,9 +314,10 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(const ScanParams p) 
   uint32_t n2 = 1;
   while (n2 < n) n2 <<= 1;
   for (uint32_t i = n + t; i < n2; i += blockDim.x) buf[i] = ~0ull;
-  block_bitonic_sort_u64(buf, n2);
+  if (!(p.rerank && p.vectors)) block_bitonic_sort_u64(buf, n2);
   uint64_t* outk = buf;
   if (p.rerank && p.vectors) {
+    // (in place: the thread that reads entry i writes its new key to entry i)
     // K6: exact distances of the shortlist, top-k of them
     if ((dim & 7) == 0) {
       // two rows per thread at a time: twice the loads in flight
@@ -327,19 +328,17 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(const ScanParams p) 
         float d0, d1;
         space_distance_vec8x2(p.metric, qs, p.vectors + (size_t)p.rank_slot[r0] * dim,
                               p.vectors + (size_t)p.rank_slot[r1] * dim, dim, d0, d1);
-        buf[CB / 2 + i] = ((uint64_t)order_key(d0) << 32) | r0;
-        if (i1 < n) buf[CB / 2 + i1] = ((uint64_t)order_key(d1) << 32) | r1;
+        buf[i] = ((uint64_t)order_key(d0) << 32) | r0;
+        if (i1 < n) buf[i1] = ((uint64_t)order_key(d1) << 32) | r1;
       }
     } else {
       for (uint32_t i = t; i < n; i += blockDim.x) {
         const uint32_t rank = (uint32_t)buf[i];
         const float d = space_distance(p.metric, qs, p.vectors + (size_t)p.rank_slot[rank] * dim, dim);
-        buf[CB / 2 + i] = ((uint64_t)order_key(d) << 32) | rank;
+        buf[i] = ((uint64_t)order_key(d) << 32) | rank;
       }
     }
-    for (uint32_t i = n + t; i < n2; i += blockDim.x) buf[CB / 2 + i] = ~0ull;
-    block_bitonic_sort_u64(buf + CB / 2, n2);
-    outk = buf + CB / 2;
+    block_bitonic_sort_u64(buf, n2);
   }
   const uint32_t take = min(n, p.k);
   for (uint32_t i = t; i < take; i += blockDim.x) {
@@ -577,8 +576,9 @@ void search_device(pxc_ivfpq* h, const float* d_q, uint32_t nq, uint32_t k, uint
   h->coarse_len.reserve(nbmax);
   h->coarse_zero.reserve(nbmax);
   PXC_CUDA(cudaMemsetAsync(h->coarse_zero.p, 0, (size_t)nbmax * 4, s));
-  uint32_t cb = 4096;
-  while (cb < 2 * shortlist || cb < CHUNK + shortlist) cb <<= 1;
+  // candidate buffer: the shortlist, two chunks of room and the final sort's
+  // power of two (at least 4096 entries)
+  const uint32_t cb = std::max<uint32_t>(4096, (shortlist + 2 * CHUNK + 1023) / 1024 * 1024);
   const size_t smem_s = (size_t)cb * 8 + ((size_t)h->m * 256 + 2 * dim) * 4 + (2 * h->m + 1) * 4;
   PXC_CUDA(cudaFuncSetAttribute(scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_s));
   if (ctx->profiling) {
