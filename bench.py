@@ -48,6 +48,9 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
     p.add_argument("--workload", choices=["flat", "kmeans", "ivfpq", "sq"], default="flat")
+    p.add_argument("--flat-scaling", choices=["weak", "strong"], default="weak",
+                   help="flat at N>1: weak = N x --nq queries per step over the row-sharded database (each GPU "
+                        "scans the equivalent of --nq queries x --n rows); strong = --nq queries split N ways")
     p.add_argument("--sq-n", type=int, default=6_250_000, help="rows per GPU (C5: 50M over 8 GPUs)")
     p.add_argument("--ivf-n", type=int, default=20_000_000)
     p.add_argument("--ivf-nlist", type=int, default=16384)
@@ -167,7 +170,8 @@ def run_reference(args):
     qps = args.steps * per_step / el
     line = {"metric": METRIC, "value": qps, "unit": "queries/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": el * 1000 / args.steps, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "weak" if args.gpus > 1 and args.flat_scaling == "weak" else "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": dict(CONFIG, parallelism=f"host threads {threads}"), "impl": "reference",
             "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": threads, "kind": "port",
                              "sample": f"each step = {per_step} queries over the full {args.n:,}-row database "
@@ -786,7 +790,11 @@ def main():
     from proxima_b200 import fixtures
     from proxima_b200.index import Context
 
-    n, dim, nq, k = args.n, args.dim, args.nq, args.k
+    n, dim, k = args.n, args.dim, args.k
+    # Weak scaling keeps each GPU's scan at (--nq queries x --n rows): the rows are split N ways and the
+    # query batch grows N-fold (the first N x --nq queries of the same seeded stream).
+    weak = world > 1 and args.flat_scaling == "weak"
+    nq = args.nq * world if weak else args.nq
     lo, hi = rank * n // world, (rank + 1) * n // world
     shard = fixtures.blobs_u8(hi - lo, dim, 1024, fixtures.C2_CENTRES, fixtures.C2_BASE, row_begin=lo)
     queries = fixtures.c2_queries(nq, dim)
@@ -917,10 +925,14 @@ def main():
                     "algorithmic_ops_per_launch": ops}
         line = {"metric": METRIC, "value": nq / (ms_per_step / 1e3), "unit": "queries/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-                "scaling": "strong", "vs_baseline": None, "dtype": "u8" if path == 1 else "f32",
+                "scaling": "weak" if weak else "strong", "vs_baseline": None,
+                "dtype": "u8" if path == 1 else "f32",
                 "data": "synthetic",
-                "config": dict(CONFIG, l2="flushed (256 MiB write) between timed steps",
-                               parallelism=f"row shards x{world}" if world > 1 else "single GPU",
+                "config": dict(CONFIG, queries=nq, l2="flushed (256 MiB write) between timed steps",
+                               parallelism=(f"row shards x{world} + NCCL allgather of k candidates per query"
+                                            + (f"; {args.nq:,} queries per GPU per step, so each GPU scans "
+                                               f"{args.nq:,} x {n:,} query-row pairs as on one GPU" if weak else ""))
+                               if world > 1 else "single GPU",
                                scan_path="tensor-core u8 (exact)" if path == 1 else "fp32 reference order"),
                 "clocks": clocks, "gpu_launches": int(launches),
                 "e2e": {"value": e2e_qps, "unit": "queries/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
