@@ -923,17 +923,20 @@ def main():
                     "kernel_ms": scan_mean.item(),
                     "peak_source": f"2 x dense bf16 {src} = dense int8 rate",
                     "algorithmic_ops_per_launch": ops}
-        line = {"metric": METRIC, "value": nq / (ms_per_step / 1e3), "unit": "queries/s", "n_gpus": world,
+        line = {"metric": METRIC.replace("k=10", f"k={k}"), "value": nq / (ms_per_step / 1e3), "unit": "queries/s",
+                "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
                 "scaling": "weak" if weak else "strong", "vs_baseline": None,
                 "dtype": "u8" if path == 1 else "f32",
                 "data": "synthetic",
-                "config": dict(CONFIG, queries=nq, l2="flushed (256 MiB write) between timed steps",
+                "config": dict(CONFIG, queries=nq, k=k, l2="flushed (256 MiB write) between timed steps",
                                parallelism=(f"row shards x{world} + NCCL allgather of k candidates per query"
                                             + (f"; {args.nq:,} queries per GPU per step, so each GPU scans "
                                                f"{args.nq:,} x {n:,} query-row pairs as on one GPU" if weak else ""))
                                if world > 1 else "single GPU",
-                               scan_path="tensor-core u8 (exact)" if path == 1 else "fp32 reference order"),
+                               scan_path=("fp32 reference order" if path != 1 else "tensor-core u8 (exact)"
+                                          if k <= 32 else "tensor-core u8 over row groups, merged and proven exact"
+                                          if k <= 128 else "fp32 reference order")),
                 "clocks": clocks, "gpu_launches": int(launches),
                 "e2e": {"value": e2e_qps, "unit": "queries/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
                 "roofline": roofline}

@@ -136,6 +136,10 @@ int32_t pxc_flat_path(const pxc_flat* h);
 /* Duration of the last search's scan kernel (K1 or K1g), with profiling on;
  * -1 when not recorded. */
 float pxc_flat_last_scan_ms(pxc_flat* h);
+/* Queries of the last search with 32 < k <= 128 on the tensor-core path whose
+ * grouped answer could not be proven exact (32 or more of their top k in one
+ * row group) and that were searched again on the fp32 scan; 0 otherwise. */
+uint32_t pxc_flat_last_redone(const pxc_flat* h);
 
 /* Allocation-free variant of pxc_flat_search_device. No counterpart in the
  * reference: it exists for callers that cannot allocate device memory (a host

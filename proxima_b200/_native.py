@@ -88,6 +88,7 @@ SIGNATURES: dict[str, tuple] = {
     "pxc_flat_search_noalloc": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, vp, vp, vp, vp,
                                             C.POINTER(PxcError)]),
     "pxc_flat_last_scan_ms": (C.c_float, [vp]),
+    "pxc_flat_last_redone": (C.c_uint32, [vp]),
     "pxc_ctx_launch_count": (C.c_uint64, [vp]),
     "pxc_ctx_set_profiling": (C.c_int32, [vp, C.c_int32, C.POINTER(PxcError)]),
     "pxc_topk_merge": (C.c_int32, [vp, vp, vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,

@@ -238,6 +238,65 @@ __global__ void zero_u32_kernel(uint32_t* p, uint64_t n) {
 
 inline unsigned grid1d(uint64_t n, unsigned block) { return (unsigned)((n + block - 1) / block); }
 
+// K1 keeps at most TC_MAX_K entries per query row; k up to GROUPED_MAX_K runs
+// as GROUP_K searches over disjoint rank groups (search_tc_grouped).
+constexpr uint32_t TC_MAX_K = 32;
+constexpr uint32_t GROUP_K = 32;
+constexpr uint32_t GROUPED_MAX_K = 128;
+
+// Exactness of a grouped search, per query. Each group list is that group's
+// own top GROUP_K, so every row missing from the union of the lists lies
+// behind the last entry of its group's list. When every full group list ends
+// at or behind the merged k-th entry (by (total_cmp(distance), id)), no missing
+// row can be among the first k and the merged list is the exact answer.
+// Otherwise (32 or more of the query's top k in one group, or fewer than k
+// merged entries while a group list is full) the query is flagged for K1g.
+__global__ void group_check_kernel(const uint64_t* __restrict__ gids, const float* __restrict__ gdist,
+                                   const uint32_t* __restrict__ glen, uint32_t ngroups, uint32_t nq,
+                                   const uint64_t* __restrict__ ids, const float* __restrict__ dist,
+                                   const uint32_t* __restrict__ len, uint32_t k, uint8_t* __restrict__ redo) {
+  const uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= nq) return;
+  const bool have_k = len[q] >= k;
+  const uint32_t kth_key = have_k ? order_key(dist[(size_t)q * k + k - 1]) : 0u;
+  const uint64_t kth_id = have_k ? ids[(size_t)q * k + k - 1] : 0ull;
+  uint8_t bad = 0;
+  for (uint32_t g = 0; g < ngroups && !bad; ++g) {
+    const size_t row = (size_t)g * nq + q;
+    if (glen[row] < GROUP_K) continue;  // the whole group is in the union
+    if (!have_k) {
+      bad = 1;
+      break;
+    }
+    const uint32_t key = order_key(gdist[row * GROUP_K + GROUP_K - 1]);
+    const uint64_t id = gids[row * GROUP_K + GROUP_K - 1];
+    if (key < kth_key || (key == kth_key && id < kth_id)) bad = 1;
+  }
+  redo[q] = bad;
+}
+
+// Row i of out = query idx[i].
+__global__ void gather_queries_kernel(const float* __restrict__ q, const uint32_t* __restrict__ idx,
+                                      uint32_t dim, float* __restrict__ out) {
+  const size_t src = (size_t)idx[blockIdx.x] * dim;
+  const size_t dst = (size_t)blockIdx.x * dim;
+  for (uint32_t d = threadIdx.x; d < dim; d += blockDim.x) out[dst + d] = q[src + d];
+}
+
+// Result row i replaces the result of query idx[i].
+__global__ void scatter_results_kernel(const uint64_t* __restrict__ ids, const float* __restrict__ dist,
+                                       const uint32_t* __restrict__ len, const uint32_t* __restrict__ idx,
+                                       uint32_t k, uint64_t* __restrict__ out_ids, float* __restrict__ out_dist,
+                                       uint32_t* __restrict__ out_len) {
+  const uint32_t q = idx[blockIdx.x];
+  const uint32_t n = len[blockIdx.x];
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+    out_ids[(size_t)q * k + i] = ids[(size_t)blockIdx.x * k + i];
+    out_dist[(size_t)q * k + i] = dist[(size_t)blockIdx.x * k + i];
+  }
+  if (threadIdx.x == 0) out_len[q] = n;
+}
+
 }  // namespace pxc
 
 using namespace pxc;
@@ -282,6 +341,11 @@ struct pxc_flat {
   DBuf<float> stage_f;
   DBuf<uint64_t> stage_id;
   DBuf<unsigned long long> bad_idx;
+  // grouped K1 (32 < k <= 128): per-group lists, the queries searched again on K1g
+  DBuf<uint64_t> g_ids, g_redo_ids;
+  DBuf<float> g_dist, g_redo_q, g_redo_dist;
+  DBuf<uint32_t> g_len, g_redo_idx, g_redo_len;
+  DBuf<uint8_t> g_redo;
   // buffers of the host-pointer entry point, kept across calls
   DBuf<float> io_q;
   DBuf<uint64_t> io_bm, io_ids;
@@ -291,6 +355,7 @@ struct pxc_flat {
   cudaEvent_t ev_begin = nullptr, ev_end = nullptr;
   bool ev_recorded = false;
   int* h_flag = nullptr;  // pinned
+  uint32_t last_redo = 0;  // queries of the last grouped search redone on K1g
   std::mutex mu;
 };
 
@@ -301,7 +366,7 @@ struct ScanTimer {
   pxc_flat* h;
   cudaStream_t s;
   bool on;
-  ScanTimer(pxc_flat* h_, cudaStream_t s_) : h(h_), s(s_), on(h_->ctx->profiling) {
+  ScanTimer(pxc_flat* h_, cudaStream_t s_, bool enable = true) : h(h_), s(s_), on(enable && h_->ctx->profiling) {
     if (!on) return;
     if (!h->ev_begin) {
       PXC_CUDA(cudaEventCreate(&h->ev_begin));
@@ -430,10 +495,11 @@ struct TcOperand {
   uint64_t nrank_pad;
   const uint64_t* rank_id;
   uint64_t nrank;
+  const uint8_t* rows;  // [nrank_pad][dp] u8, the memory tmap_x describes
 };
 
 void search_tc(pxc_flat* h, const TcOperand& op, const float* d_q, uint32_t nq, uint32_t k, uint64_t* d_ids,
-               float* d_dist, uint32_t* d_len, cudaStream_t s) {
+               float* d_dist, uint32_t* d_len, cudaStream_t s, bool timed = true) {
   const uint32_t KT = k <= 1 ? 1 : k <= 4 ? 4 : k <= 10 ? 10 : k <= 16 ? 16 : 32;
   const uint32_t nq_pad = (nq + flat_tc::BM - 1) / flat_tc::BM * flat_tc::BM;
   const uint32_t nqt = nq_pad / flat_tc::BM;
@@ -467,7 +533,7 @@ void search_tc(pxc_flat* h, const TcOperand& op, const float* d_q, uint32_t nq, 
   make_tmap_u8_2d(&tmap_q, h->q_u8.p, h->dp, nq_pad, flat_tc::KB_BYTES, flat_tc::BM);
   size_t smem = flat_tc::smem_bytes(p.kblocks, p.stages);
   dim3 grid(nqt, nsplit);
-  ScanTimer timer(h, s);
+  ScanTimer timer(h, s, timed);
   switch (KT) {
     case 1: launch_tc<1>(tmap_q, *op.tmap_x, p, grid, smem, s); break;
     case 4: launch_tc<4>(tmap_q, *op.tmap_x, p, grid, smem, s); break;
@@ -563,16 +629,87 @@ void search_generic(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, cons
   timer.stop();
 }
 
+// 32 < k <= 128 on the tensor cores: the operand is cut into groups of whole
+// 256-row tiles, K1 returns each group's top GROUP_K, the group lists are
+// merged by (distance, id), and group_check_kernel proves the merged top k
+// exact per query; the few queries it cannot prove are searched again on K1g.
+// Groups: ceil(0.08 k), so a group holds 1/12.5 of a query's top k on
+// average and reaching GROUP_K in one group is rare unless rows that are near
+// one another are also near in id order.
+void search_tc_grouped(pxc_flat* h, const TcOperand& op, const float* d_q, uint32_t nq, uint32_t k,
+                       const uint64_t* d_bitmap, uint64_t* d_ids, float* d_dist, uint32_t* d_len, cudaStream_t s) {
+  const uint64_t ntiles = op.nrank_pad / flat_tc::BN;
+  const uint32_t want = std::max<uint32_t>(2, (k * 2 + 24) / 25);
+  if (ntiles < want) {  // too few rows to split: the fp32 scan
+    search_generic(h, d_q, nq, k, d_bitmap, d_ids, d_dist, d_len, s);
+    return;
+  }
+  const uint64_t tpg = (ntiles + want - 1) / want;
+  const uint32_t ng = (uint32_t)((ntiles + tpg - 1) / tpg);
+  h->g_ids.reserve((size_t)ng * nq * GROUP_K);
+  h->g_dist.reserve((size_t)ng * nq * GROUP_K);
+  h->g_len.reserve((size_t)ng * nq);
+  h->g_redo.reserve(nq);
+  h->g_redo_idx.reserve(nq);
+  h->g_redo_len.reserve(1);  // the count first; resized below if queries need K1g
+  ScanTimer timer(h, s);
+  for (uint32_t g = 0; g < ng; ++g) {
+    const uint64_t t0 = (uint64_t)g * tpg;
+    const uint64_t t1 = std::min<uint64_t>(ntiles, t0 + tpg);
+    const uint64_t r0 = t0 * flat_tc::BN;
+    const uint64_t rows_pad = (t1 - t0) * flat_tc::BN;
+    // r0 < nrank: the last tile of the operand holds at least one real row
+    const uint64_t nreal = std::min<uint64_t>(op.nrank, t1 * flat_tc::BN) - r0;
+    CUtensorMap tm;
+    make_tmap_u8_2d(&tm, op.rows + r0 * h->dp, h->dp, rows_pad, flat_tc::KB_BYTES, flat_tc::BN);
+    TcOperand gop{&tm, op.norms + r0, rows_pad, op.rank_id + r0, nreal, op.rows + r0 * h->dp};
+    const size_t off = (size_t)g * nq;
+    search_tc(h, gop, d_q, nq, GROUP_K, h->g_ids.p + off * GROUP_K, h->g_dist.p + off * GROUP_K,
+              h->g_len.p + off, s, false);
+  }
+  pxc_error err{};
+  if (pxc_topk_merge(h->ctx, h->g_ids.p, h->g_dist.p, h->g_len.p, ng, nq, GROUP_K, k, d_ids, d_dist, d_len, s,
+                     &err) != PXC_OK)
+    throw make_failure((pxc_status)err.code, err.a, err.b, nullptr, "group merge: %s", err.detail);
+  timer.stop();
+  group_check_kernel<<<grid1d(nq, 256), 256, 0, s>>>(h->g_ids.p, h->g_dist.p, h->g_len.p, ng, nq, d_ids, d_dist,
+                                                      d_len, k, h->g_redo.p);
+  PXC_CUDA(cudaGetLastError());
+  size_t tb = 0;
+  thrust::counting_iterator<uint32_t> it(0);
+  PXC_CUDA(cub::DeviceSelect::Flagged(nullptr, tb, it, h->g_redo.p, h->g_redo_idx.p, h->g_redo_len.p, (int64_t)nq, s));
+  h->tmp.reserve(std::max<size_t>(tb, 1));
+  PXC_CUDA(cub::DeviceSelect::Flagged(h->tmp.p, tb, it, h->g_redo.p, h->g_redo_idx.p, h->g_redo_len.p, (int64_t)nq, s));
+  PXC_CUDA(cudaMemcpyAsync(h->h_flag, h->g_redo_len.p, sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
+  PXC_CUDA(cudaStreamSynchronize(s));
+  const uint32_t nredo = static_cast<uint32_t>(*h->h_flag);
+  h->last_redo = nredo;
+  h->ctx->launches += 3;  // check + two select passes
+  if (nredo == 0) return;
+  h->g_redo_q.reserve((size_t)nredo * h->dim);
+  h->g_redo_ids.reserve((size_t)nredo * k);
+  h->g_redo_dist.reserve((size_t)nredo * k);
+  h->g_redo_len.reserve(nredo);
+  gather_queries_kernel<<<nredo, 128, 0, s>>>(d_q, h->g_redo_idx.p, h->dim, h->g_redo_q.p);
+  PXC_CUDA(cudaGetLastError());
+  search_generic(h, h->g_redo_q.p, nredo, k, d_bitmap, h->g_redo_ids.p, h->g_redo_dist.p, h->g_redo_len.p, s);
+  scatter_results_kernel<<<nredo, 128, 0, s>>>(h->g_redo_ids.p, h->g_redo_dist.p, h->g_redo_len.p,
+                                               h->g_redo_idx.p, k, d_ids, d_dist, d_len);
+  PXC_CUDA(cudaGetLastError());
+  h->ctx->launches += 2;
+}
+
 void search_device(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, const uint64_t* d_bitmap,
                    uint64_t* d_ids, float* d_dist, uint32_t* d_len, cudaStream_t s) {
   PXC_CONFIG(k <= PXC_MAX_K, "k", k, "exceeds the 16777216 result ceiling");
+  h->last_redo = 0;
   if (h->dirty) rebuild_mirror(h, s);
   if (nq == 0) return;
   if (k == 0 || h->nrank == 0) {
     PXC_CUDA(cudaMemsetAsync(d_len, 0, nq * sizeof(uint32_t), s));
     return;
   }
-  bool tc = h->all_u8 && h->metric == PXC_EUCLIDEAN && k <= 32 &&
+  bool tc = h->all_u8 && h->metric == PXC_EUCLIDEAN && k <= GROUPED_MAX_K &&
             h->dim <= (uint32_t)flat_tc::MAX_KBLOCKS * flat_tc::KB_BYTES && h->nrank_pad > 0;
   if (tc) {
     const uint32_t nq_pad = (nq + flat_tc::BM - 1) / flat_tc::BM * flat_tc::BM;
@@ -588,7 +725,7 @@ void search_device(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, const
     tc = (*h->h_flag == 0);
   }
   if (tc) {
-    TcOperand op{&h->tmap_x, h->op_norm.p, h->nrank_pad, h->rank_id.p, h->nrank};
+    TcOperand op{&h->tmap_x, h->op_norm.p, h->nrank_pad, h->rank_id.p, h->nrank, h->op_u8.p};
     CUtensorMap tmap_f;
     if (d_bitmap) {
       // the filter's accepted ranks, compacted in rank order, as K1's database
@@ -618,9 +755,12 @@ void search_device(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, const
       PXC_CUDA(cudaGetLastError());
       h->ctx->launches += 1;
       make_tmap_u8_2d(&tmap_f, h->f_op.p, h->dp, npad, flat_tc::KB_BYTES, flat_tc::BN);
-      op = TcOperand{&tmap_f, h->f_norm.p, npad, h->f_id.p, nacc};
+      op = TcOperand{&tmap_f, h->f_norm.p, npad, h->f_id.p, nacc, h->f_op.p};
     }
-    search_tc(h, op, d_q, nq, k, d_ids, d_dist, d_len, s);
+    if (k <= TC_MAX_K)
+      search_tc(h, op, d_q, nq, k, d_ids, d_dist, d_len, s);
+    else
+      search_tc_grouped(h, op, d_q, nq, k, d_bitmap, d_ids, d_dist, d_len, s);
     check_device_status(h->ctx, s, "flat search (tensor-core scan)");
   } else {
     search_generic(h, d_q, nq, k, d_bitmap, d_ids, d_dist, d_len, s);
@@ -743,6 +883,8 @@ float pxc_flat_last_scan_ms(pxc_flat* h) {
   if (cudaEventElapsedTime(&ms, h->ev_begin, h->ev_end) != cudaSuccess) return -1.0f;
   return ms;
 }
+
+uint32_t pxc_flat_last_redone(const pxc_flat* h) { return h ? h->last_redo : 0u; }
 
 int32_t pxc_flat_path(const pxc_flat* h) {
   if (!h) return -1;

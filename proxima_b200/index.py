@@ -319,6 +319,11 @@ class FlatIndex:
         self._sync()
         return int(self._lib.pxc_flat_path(self.handle))
 
+    def last_redone(self) -> int:
+        """Queries of the last search (32 < k <= 128, tensor-core path) whose grouped answer was
+        searched again on the fp32 scan because it could not be proven exact."""
+        return int(self._lib.pxc_flat_last_redone(self.handle))
+
 
 @dataclass
 class RecallReport:

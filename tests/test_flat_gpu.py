@@ -159,13 +159,37 @@ def test_c2_many_waves_seeding_and_cross_split_ties():
         _assert_same(got, ref, len(q))
 
 
-def test_c2_k100_generic_path_bit_exact(c2_small):
+@pytest.mark.parametrize("k", [33, 64, 100, 128])
+def test_c2_grouped_tensor_core_path_bit_exact(c2_small, k):
+    """32 < k <= 128: K1 over disjoint row groups, merged, proven exact per query."""
     db, q = c2_small
     from proxima_b200.index import FlatIndex
     idx = FlatIndex.from_array(VectorSpace(128, Metric.EUCLIDEAN), db)
-    got = idx.search_prepared_batch(q, 100)
-    ref = pxo.flat_search(db, q, 100, pxo.EUCLIDEAN)
+    assert idx.device_path() == 1
+    got = idx.search_prepared_batch(q, k)
+    ref = pxo.flat_search(db, q, k, pxo.EUCLIDEAN)
     _assert_same(got, ref, len(q))
+    assert idx.last_redone() <= 3  # blob rows are spread over the groups: nearly every query is proven
+
+
+def test_c2_grouped_redo_when_neighbours_share_a_group(c2_small):
+    """Queries whose top 100 crowd into one row group (40 exact copies in consecutive
+    ids) fail the grouped proof and are answered by the fp32 scan; all stay exact."""
+    db, q = c2_small
+    rows = db[:40_000].copy()
+    for i in range(24):
+        rows[1000 + i * 1200:1000 + i * 1200 + 40] = q[i]
+    from proxima_b200.index import FlatIndex
+    idx = FlatIndex.from_array(VectorSpace(128, Metric.EUCLIDEAN), rows)
+    got = idx.search_prepared_batch(q[:200], 100)
+    ref = pxo.flat_search(rows, q[:200], 100, pxo.EUCLIDEAN)
+    _assert_same(got, ref, 200)
+    assert idx.last_redone() >= 24
+    # small stores (fewer tiles than groups) take the fp32 scan directly
+    small = FlatIndex.from_array(VectorSpace(128, Metric.EUCLIDEAN), db[:700])
+    got = small.search_prepared_batch(q[:50], 128)
+    ref = pxo.flat_search(db[:700], q[:50], 128, pxo.EUCLIDEAN)
+    _assert_same(got, ref, 50)
 
 
 def test_c2_shuffled_ids_removed_slots_and_duplicates(c2_small):
@@ -219,7 +243,7 @@ def _bitmap(keep):
     return np.concatenate([bm, np.zeros(-len(bm) % 8, np.uint8)]).view(np.uint64)
 
 
-@pytest.mark.parametrize("k", [1, 10, 32])
+@pytest.mark.parametrize("k", [1, 10, 32, 100])
 def test_c2_filtered_tensor_core_path_bit_exact(c2_small, k):
     """A filter on an integer euclidean store runs on the tensor-core scan over
     the accepted rows; ids not in slot order and dead slots included."""
