@@ -196,7 +196,8 @@ __global__ void prep_queries_u8_kernel(const float* __restrict__ Q, uint32_t nq,
 // Merge of K1's per-split lists: per query, nsplit*KT packed (r, rank) keys,
 // sort, drop duplicates (a split may carry entries seeded from an earlier
 // split), keep k, distance = r + ||q||^2 (exact integer in f32).
-__global__ void merge_u8_kernel(const uint64_t* __restrict__ part, uint32_t nsplit, uint32_t KT,
+// Launched with 256 threads per block (one block per query).
+__global__ void __launch_bounds__(256) merge_u8_kernel(const uint64_t* __restrict__ part, uint32_t nsplit, uint32_t KT,
                                 uint32_t cap, uint32_t k, const int32_t* __restrict__ qnorm,
                                 const uint64_t* __restrict__ rank_id, uint32_t nrank,
                                 uint64_t* __restrict__ out_ids, float* __restrict__ out_dist,
@@ -217,18 +218,28 @@ __global__ void merge_u8_kernel(const uint64_t* __restrict__ part, uint32_t nspl
   for (uint32_t i = threadIdx.x; i < cap; i += blockDim.x)
     flag[i] = (sl[i] != ~0ull && (i == 0 || sl[i] != sl[i - 1])) ? 1u : 0u;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    uint32_t n_out = 0;
-    for (uint32_t i = 0; i < cap && n_out < k; ++i) {
-      if (!flag[i]) continue;
-      const uint64_t v = sl[i];
-      const int32_t r = static_cast<int32_t>(static_cast<uint32_t>(v >> 32) - flat_tc::R_OFFSET);
-      out_ids[(size_t)q * k + n_out] = rank_id[static_cast<uint32_t>(v)];
-      out_dist[(size_t)q * k + n_out] = static_cast<float>(r + qnorm[q]);
-      ++n_out;
-    }
-    out_len[q] = n_out;
+  // Each thread takes a contiguous run of the sorted keys; an exclusive scan of
+  // the per-run unique counts gives each run its first output position, so the
+  // id lookups of one query's k results are issued in parallel.
+  using Scan = cub::BlockScan<uint32_t, 256>;
+  __shared__ typename Scan::TempStorage scan_tmp;
+  const uint32_t per = (cap + 255) / 256;
+  const uint32_t b = threadIdx.x * per;
+  const uint32_t e = min(b + per, cap);
+  uint32_t cnt = 0;
+  for (uint32_t i = b; i < e; ++i) cnt += flag[i];
+  uint32_t pos = 0, total = 0;
+  Scan(scan_tmp).ExclusiveSum(cnt, pos, total);
+  const int32_t qn = qnorm[q];
+  for (uint32_t i = b; i < e && pos < k; ++i) {
+    if (!flag[i]) continue;
+    const uint64_t v = sl[i];
+    const int32_t r = static_cast<int32_t>(static_cast<uint32_t>(v >> 32) - flat_tc::R_OFFSET);
+    out_ids[(size_t)q * k + pos] = rank_id[static_cast<uint32_t>(v)];
+    out_dist[(size_t)q * k + pos] = static_cast<float>(r + qn);
+    ++pos;
   }
+  if (threadIdx.x == 0) out_len[q] = min(total, k);
 }
 
 __global__ void zero_u32_kernel(uint32_t* p, uint64_t n) {
