@@ -125,6 +125,24 @@ __global__ void __launch_bounds__(128) probes_from_lists_kernel(const uint64_t* 
     probes[(size_t)q * nprobe + i] = i < n ? static_cast<uint32_t>(keys[i]) : UNASSIGNED;
 }
 
+// Re-rank on u8 rows. When the metric is euclidean, dim <= 256 and the query
+// and every live row are integers in [0,255], each term (q - x)^2 <= 65025 and
+// every partial sum <= 256 * 65025 < 2^24 is an integer, so the reference's
+// f32 squared_euclidean is exact in any order and equals the integer sum
+// below (|q - x| per byte, then a 4-way dot product of the differences).
+constexpr uint32_t U8_MAX_DIM = 256;
+
+__device__ __forceinline__ uint32_t sqdiff_u8x16(const uint4 a, const uint4 b, uint32_t acc) {
+  uint32_t d = __vabsdiffu4(a.x, b.x);
+  acc = __dp4a(d, d, acc);
+  d = __vabsdiffu4(a.y, b.y);
+  acc = __dp4a(d, d, acc);
+  d = __vabsdiffu4(a.z, b.z);
+  acc = __dp4a(d, d, acc);
+  d = __vabsdiffu4(a.w, b.w);
+  return __dp4a(d, d, acc);
+}
+
 struct ScanParams {
   const float* queries;      // nq x dim (prepared)
   const uint32_t* probes;    // nq x nprobe list indices
@@ -138,6 +156,7 @@ struct ScanParams {
   const uint32_t* rank_slot;
   const uint64_t* ids;        // VectorId per slot
   const float* vectors;       // nullable: no rerank
+  const uint8_t* vec_u8;      // nullable: rank-major u8 copy of the live rows (see build_u8_rows)
   const uint64_t* bitmap;     // nullable
   uint64_t* out_ids;
   float* out_dist;
@@ -148,6 +167,22 @@ struct ScanParams {
   int metric;
   int rerank;
 };
+
+// u8 copy of the live rows in rank order for the u8 re-rank; clears *all_int
+// when a component is not an integer in [0,255] (the copy is then unused).
+__global__ void build_u8_rows_kernel(const float* __restrict__ vectors, const uint32_t* __restrict__ rank_slot,
+                                     uint64_t nrank, uint32_t dim, uint8_t* __restrict__ out,
+                                     int* __restrict__ all_int) {
+  const uint64_t r = blockIdx.x;
+  if (r >= nrank) return;
+  const float* row = vectors + (size_t)rank_slot[r] * dim;
+  for (uint32_t d = threadIdx.x; d < dim; d += blockDim.x) {
+    const float v = row[d];
+    const bool ok = v >= 0.0f && v <= 255.0f && v == floorf(v);
+    if (!ok) *all_int = 0;
+    out[r * dim + d] = ok ? static_cast<uint8_t>(v) : 0;
+  }
+}
 
 // K5 + K6: one CTA per query.
 __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(const ScanParams p) {
@@ -161,16 +196,25 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(const ScanParams p) 
   __shared__ uint32_t hist[256], sh[4], count;
   __shared__ uint64_t thr;
   __shared__ float qdc;
+  __shared__ __align__(16) uint8_t qu8[U8_MAX_DIM];  // the query as u8 (u8 re-rank)
   const uint32_t q = blockIdx.x, t = threadIdx.x;
   const uint32_t dim = p.dim, m = p.m;
   const bool cosine = p.metric == PXC_COSINE;
-  for (uint32_t i = t; i < dim; i += blockDim.x) qs[i] = p.queries[(size_t)q * dim + i];
+  int q_int = 1;
+  for (uint32_t i = t; i < dim; i += blockDim.x) {
+    const float v = p.queries[(size_t)q * dim + i];
+    qs[i] = v;
+    const bool ok = v >= 0.0f && v <= 255.0f && v == floorf(v);
+    q_int &= ok ? 1 : 0;
+    if (i < U8_MAX_DIM) qu8[i] = ok ? static_cast<uint8_t>(v) : 0;
+  }
   for (uint32_t i = t; i < 2 * m + 1; i += blockDim.x) woff[i] = p.woff[i];
   if (t == 0) {
     count = 0;
     thr = ~0ull;
   }
-  __syncthreads();
+  // the host sets vec_u8 only for euclidean stores of integer rows with dim <= 256, dim % 16 == 0
+  const bool rerank_u8 = __syncthreads_and(q_int) && p.vec_u8 != nullptr;
   const uint32_t* widths = woff;
   const uint32_t* offs = woff + m;
   // table over a vector v (in shared memory): squared (or dot) per entry
@@ -319,7 +363,28 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(const ScanParams p) 
   if (p.rerank && p.vectors) {
     // (in place: the thread that reads entry i writes its new key to entry i)
     // K6: exact distances of the shortlist, top-k of them
-    if ((dim & 7) == 0) {
+    if (rerank_u8) {
+      // 128-byte rows for C4's dim 128: a quarter of the f32 rows' traffic
+      const uint32_t nv = dim / 16;
+      const uint4* q4 = reinterpret_cast<const uint4*>(qu8);
+      for (uint32_t i = t; i < n; i += 2 * blockDim.x) {
+        const uint32_t i1 = i + blockDim.x;
+        const uint32_t r0 = (uint32_t)buf[i];
+        const uint32_t r1 = i1 < n ? (uint32_t)buf[i1] : r0;
+        const uint4* x0 = reinterpret_cast<const uint4*>(p.vec_u8 + (size_t)r0 * dim);
+        const uint4* x1 = reinterpret_cast<const uint4*>(p.vec_u8 + (size_t)r1 * dim);
+        uint32_t a0 = 0, a1 = 0;
+#pragma unroll 8
+        for (uint32_t j = 0; j < nv; ++j) {
+          const uint4 u = __ldg(x0 + j), w = __ldg(x1 + j);
+          const uint4 qv = q4[j];
+          a0 = sqdiff_u8x16(qv, u, a0);
+          a1 = sqdiff_u8x16(qv, w, a1);
+        }
+        buf[i] = ((uint64_t)order_key(static_cast<float>(a0)) << 32) | r0;
+        if (i1 < n) buf[i1] = ((uint64_t)order_key(static_cast<float>(a1)) << 32) | r1;
+      }
+    } else if ((dim & 7) == 0) {
       // two rows per thread at a time: twice the loads in flight
       for (uint32_t i = t; i < n; i += 2 * blockDim.x) {
         const uint32_t i1 = i + blockDim.x;
@@ -478,6 +543,11 @@ struct pxc_ivfpq {
   pxc::DBuf<uint32_t> woff;
   pxc::DBuf<float> centroids, codebooks, vectors;
   bool have_parts = false, have_vectors = false;
+  // u8 re-rank rows: 0 = not built since the store changed, 1 = built, 2 = not applicable
+  int u8_state = 0;
+  pxc::DBuf<uint8_t> vec_u8;
+  pxc::DBuf<int> u8_flag;
+  int* h_u8_flag = nullptr;  // pinned
   uint64_t nslots = 0, nlive = 0;
   std::vector<uint64_t> h_ids;
   std::vector<uint8_t> h_live;
@@ -498,6 +568,7 @@ struct pxc_ivfpq {
   std::mutex mu;
   ~pxc_ivfpq() {
     if (h_scanned) cudaFreeHost(h_scanned);
+    if (h_u8_flag) cudaFreeHost(h_u8_flag);
     if (ev_begin) cudaEventDestroy(ev_begin);
     if (ev_end) cudaEventDestroy(ev_end);
   }
@@ -565,6 +636,23 @@ void search_device(pxc_ivfpq* h, const float* d_q, uint32_t nq, uint32_t k, uint
   PXC_CONFIG(shortlist <= MAX_SHORTLIST, "rerank", shortlist,
              "the device search keeps at most 4096 candidates per query (max(rerank, k))");
   const uint32_t dim = h->dim, nlist = h->nlist;
+  if (rerank > 0 && h->have_vectors && h->u8_state == 0) {
+    h->u8_state = 2;
+    if (h->metric == PXC_EUCLIDEAN && dim <= U8_MAX_DIM && dim % 16 == 0 && h->nlive < (1ull << 31)) {
+      h->vec_u8.reserve(h->nlive * dim);
+      h->u8_flag.reserve(1);
+      if (!h->h_u8_flag) PXC_CUDA(cudaMallocHost(&h->h_u8_flag, sizeof(int)));
+      const int one = 1;
+      PXC_CUDA(cudaMemcpyAsync(h->u8_flag.p, &one, sizeof(int), cudaMemcpyHostToDevice, s));
+      build_u8_rows_kernel<<<(unsigned)h->nlive, 128, 0, s>>>(h->vectors.p, h->rank_slot.p, h->nlive, dim,
+                                                              h->vec_u8.p, h->u8_flag.p);
+      PXC_CUDA(cudaGetLastError());
+      PXC_CUDA(cudaMemcpyAsync(h->h_u8_flag, h->u8_flag.p, sizeof(int), cudaMemcpyDeviceToHost, s));
+      PXC_CUDA(cudaStreamSynchronize(s));
+      ctx->launches += 1;
+      if (*h->h_u8_flag) h->u8_state = 1;
+    }
+  }
   // K4: coarse
   const uint32_t P = nprobe;
   const uint32_t batch = 16384;
@@ -611,6 +699,7 @@ void search_device(pxc_ivfpq* h, const float* d_q, uint32_t nq, uint32_t k, uint
     sp.rank_slot = h->rank_slot.p;
     sp.ids = h->ids.p;
     sp.vectors = h->have_vectors ? h->vectors.p : nullptr;
+    sp.vec_u8 = (h->have_vectors && h->u8_state == 1) ? h->vec_u8.p : nullptr;
     sp.bitmap = d_bitmap;
     sp.out_ids = d_ids + (size_t)q0 * k;
     sp.out_dist = d_dist + (size_t)q0 * k;
@@ -802,6 +891,7 @@ pxc_status pxc_ivfpq_set_store(pxc_ivfpq* h, const float* vectors, const uint64_
     }
     PXC_CUDA(cudaStreamSynchronize(s));
     h->have_lists = false;
+    h->u8_state = 0;
   });
 }
 
@@ -825,6 +915,7 @@ pxc_status pxc_ivfpq_set_store_device(pxc_ivfpq* h, const float* d_vectors, cons
       PXC_CUDA(cudaStreamSynchronize(s));
       h->have_vectors = true;
     }
+    h->u8_state = 0;
   });
 }
 

@@ -102,6 +102,32 @@ def test_degenerate_calls():
     _same(idx.search_batch(q, 10, 99), ref, "nprobe clamps to nlist")
 
 
+def test_u8_rerank_integer_rows_and_mixed_queries():
+    """Integer rows in [0,255]: the re-rank reads u8 rows for integer queries and f32 rows for the
+    others (one batch holds both); a store with one non-integer row re-ranks in f32 throughout."""
+    dim, nlist, m = 128, 40, 16
+    data, cent, books, list_of, codes = _build(15000, dim, nlist, m, 7)
+    queries = np.concatenate([data[3::301][:40],
+                              fixtures.blobs_u8(40, dim, 64, fixtures.C4_CENTRES + 7, fixtures.C4_QUERIES),
+                              data[7::409][:20] + np.float32(0.5)])
+    queries[5, 17] = 256.0  # an integer outside [0,255]
+    rng = np.random.default_rng(8)
+    ids = rng.permutation(np.arange(5, 5 + 15000, dtype=np.uint64) * 3)
+    live = (rng.random(15000) > 0.08).astype(np.uint8)
+    bitmap = np.zeros((15000 + 63) // 64, dtype=np.uint64)
+    for s_ in np.flatnonzero(rng.random(15000) > 0.4):
+        bitmap[s_ >> 6] |= np.uint64(1) << np.uint64(s_ & 63)
+    for rows in (data, np.where(np.arange(15000)[:, None] == 77, data + np.float32(0.5), data)):
+        idx = IvfPqIndex(dim, nlist, m).from_parts(cent, books)
+        idx.set_store(rows, ids=ids, live=live)
+        idx.set_codes(list_of, codes)
+        for k, nprobe, rerank, bm in [(10, 8, 200, None), (10, 40, 1000, bitmap), (50, 5, 60, None)]:
+            ref = pxo.ivfpq_search(rows, cent, books, m, list_of, codes, queries, k, nprobe, rerank=rerank, ids=ids,
+                                   live=live, bitmap=bm)
+            got = idx.search_batch(queries, k, nprobe, rerank, bitmap=bm)
+            _same(got, ref, f"k {k} nprobe {nprobe} rerank {rerank} filtered {bm is not None}")
+
+
 def test_encode_all_matches_oracle():
     dim, nlist, m = 64, 300, 16  # nlist >= 256: the coarse assignment takes the tensor-core screen
     data, cent, books, list_of, codes = _build(20000, dim, nlist, m, 5)
