@@ -136,3 +136,51 @@ def test_recall_overlap():
     a = np.array([2, 9, 4], np.uint64)
     assert pxo.lib().pxo_recall_overlap(e.ctypes.data, 4, a.ctypes.data, 3) == 0.5
     assert pxo.lib().pxo_recall_overlap(e.ctypes.data, 0, a.ctypes.data, 3) == 1.0
+
+
+def _grouped_search(data, ids, queries, k, ngroups, group_k=32):
+    """The decomposition the device uses for 32 < k <= 128, restated on the oracle: each
+    contiguous group's own top group_k, merged by (distance, id), and the per-query check
+    that every full group list ends at or behind the merged k-th entry."""
+    bounds = np.linspace(0, len(data), ngroups + 1).astype(int)
+    lists = [pxo.flat_search(data[a:b], queries, group_k, pxo.EUCLIDEAN, ids=ids[a:b])
+             for a, b in zip(bounds[:-1], bounds[1:])]
+    merged, proven = [], []
+    for q in range(len(queries)):
+        cand = []
+        for gi, gd, gl in lists:
+            cand += [(float(gd[q, i]), int(gi[q, i])) for i in range(int(gl[q]))]
+        cand.sort()
+        top = cand[:k]
+        ok = True
+        for gi, gd, gl in lists:
+            if int(gl[q]) < group_k:
+                continue
+            last = (float(gd[q, group_k - 1]), int(gi[q, group_k - 1]))
+            if len(top) < k or last < top[-1]:
+                ok = False
+        merged.append(top)
+        proven.append(ok)
+    return merged, proven
+
+
+def test_grouped_top_k_is_exact_whenever_the_check_passes():
+    rng = np.random.default_rng(21)
+    centres = rng.integers(0, 256, (40, 16))
+    rows = np.clip(np.rint(centres[np.arange(6000) % 40] + rng.normal(0, 12, (6000, 16))), 0, 255)
+    rows = rows.astype(np.float32)
+    rows[3000:3045] = rows[10]  # 45 copies in one group: the queries near row 10 cannot be proven
+    ids = rng.permutation(np.arange(100, 6100, dtype=np.uint64))
+    queries = np.concatenate([rows[10:11], rows[::97][:60] + 1.0]).astype(np.float32)
+    k = 100
+    merged, proven = _grouped_search(rows, ids, queries, k, 8)
+    full_i, full_d, full_l = pxo.flat_search(rows, queries, k, pxo.EUCLIDEAN, ids=ids)
+    assert not proven[0]
+    assert sum(proven) >= 50
+    for q in range(len(queries)):
+        exact = [(float(full_d[q, i]), int(full_i[q, i])) for i in range(int(full_l[q]))]
+        if proven[q]:
+            assert merged[q] == exact
+    # the failing query really differs: the group kept only 32 of the 45 copies
+    exact0 = [(float(full_d[0, i]), int(full_i[0, i])) for i in range(int(full_l[0]))]
+    assert merged[0] != exact0
