@@ -123,15 +123,18 @@ pxc_status pxc_flat_search(pxc_flat* h, const float* queries, uint32_t nq, uint3
                            const uint64_t* bitmap, uint64_t* out_ids, float* out_dist,
                            uint32_t* out_len, pxc_error* err);
 /* Same, with DEVICE buffers on the context's device, ordered on `stream`
- * (a cudaStream_t; NULL = the context's stream). Returns after the work is
- * enqueued; the caller synchronises the stream. */
+ * (a cudaStream_t; NULL = the context's stream). The call waits on the
+ * stream for small host decisions (whether the queries are integers in
+ * [0,255]; with 32 < k <= 128, which queries the grouped scan proved exact)
+ * and returns with the result kernels enqueued; the caller synchronises the
+ * stream before reading the outputs. */
 pxc_status pxc_flat_search_device(pxc_flat* h, const float* d_queries, uint32_t nq,
                                   uint32_t k, const uint64_t* d_bitmap, uint64_t* d_out_ids,
                                   float* d_out_dist, uint32_t* d_out_len, void* stream,
                                   pxc_error* err);
 /* Which scan kernel the next search will use: 1 = tensor-core u8 (every live
  * row and the queries are integers in [0,255] under euclidean, so the u8
- * product is exact), 0 = fp32 reference-order scan. Diagnostic only. */
+ * product is exact; k <= 128), 0 = fp32 reference-order scan. Diagnostic only. */
 int32_t pxc_flat_path(const pxc_flat* h);
 /* Duration of the last search's scan kernel (K1 or K1g), with profiling on;
  * -1 when not recorded. */
