@@ -184,3 +184,19 @@ def test_grouped_top_k_is_exact_whenever_the_check_passes():
     # the failing query really differs: the group kept only 32 of the 45 copies
     exact0 = [(float(full_d[0, i]), int(full_i[0, i])) for i in range(int(full_l[0]))]
     assert merged[0] != exact0
+
+
+@pytest.mark.parametrize("dim", [1, 7, 16, 100, 128, 255, 256])
+def test_integer_vectors_have_exact_f32_squared_euclidean(dim):
+    """The premise of the u8 scans (flat K1, the IVF-PQ u8 re-rank): for integer components in
+    [0,255] and dim <= 256 the reference's 8-lane f32 squared_euclidean equals the exact integer
+    sum, the extreme pair (all 0 against all 255) included."""
+    rng = np.random.default_rng(dim)
+    pairs = [(np.zeros(dim), np.full(dim, 255.0)), (np.full(dim, 255.0), np.zeros(dim))]
+    pairs += [(rng.integers(0, 256, dim).astype(np.float64), rng.integers(0, 256, dim).astype(np.float64))
+              for _ in range(200)]
+    for a, b in pairs:
+        exact = int(((a.astype(np.int64) - b.astype(np.int64)) ** 2).sum())
+        assert exact < 2 ** 24
+        got = pxo.squared_euclidean(a.astype(np.float32), b.astype(np.float32))
+        assert got == float(exact)
