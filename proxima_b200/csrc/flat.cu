@@ -367,6 +367,7 @@ struct pxc_flat {
   bool ev_recorded = false;
   int* h_flag = nullptr;  // pinned
   uint32_t last_redo = 0;  // queries of the last grouped search redone on K1g
+  cudaEvent_t ev_done = nullptr;  // end of the last search's work (handoff of the scratch)
   std::mutex mu;
 };
 
@@ -391,6 +392,22 @@ struct ScanTimer {
     h->ev_recorded = true;
   }
 };
+
+// The handle's device scratch and mirror pass from one call to the next in
+// stream order. A search may return before its kernels finish (the fp32 scan
+// does), and concurrent searches may run on different streams, so each search
+// makes its stream wait (on the GPU) for the previous search's work, and
+// records the end of its own; calls that rewrite the mirror wait on the host.
+void handoff_wait(pxc_flat* h, cudaStream_t s) {
+  if (h->ev_done) PXC_CUDA(cudaStreamWaitEvent(s, h->ev_done, 0));
+}
+void handoff_done(pxc_flat* h, cudaStream_t s) {
+  if (!h->ev_done) PXC_CUDA(cudaEventCreateWithFlags(&h->ev_done, cudaEventDisableTiming));
+  PXC_CUDA(cudaEventRecord(h->ev_done, s));
+}
+void handoff_drain(pxc_flat* h) {
+  if (h->ev_done) PXC_CUDA(cudaEventSynchronize(h->ev_done));
+}
 
 void ensure_capacity(pxc_flat* h, uint64_t want, cudaStream_t s) {
   uint64_t cap = h->ids.n;
@@ -810,6 +827,10 @@ void pxc_flat_destroy(pxc_flat* h) {
   cudaGetDevice(&prev);
   cudaSetDevice(h->ctx->device);
   cudaStreamSynchronize(h->ctx->stream);
+  if (h->ev_done) {
+    cudaEventSynchronize(h->ev_done);  // a search on another stream may still be running
+    cudaEventDestroy(h->ev_done);
+  }
   if (h->ev_begin) cudaEventDestroy(h->ev_begin);
   if (h->ev_end) cudaEventDestroy(h->ev_end);
   if (h->h_flag) cudaFreeHost(h->h_flag);
@@ -828,6 +849,7 @@ pxc_status pxc_flat_sync(pxc_flat* h, const float* rows, const uint64_t* ids, co
     std::lock_guard<std::mutex> lock(h->mu);
     DeviceGuard g(h->ctx->device);
     cudaStream_t s = h->ctx->stream;
+    handoff_drain(h);
     const uint64_t dim = h->dim;
     // stage + validate before touching the mirror
     h->stage_f.reserve(nslots * dim);
@@ -867,6 +889,8 @@ pxc_status pxc_flat_truncate(pxc_flat* h, uint64_t nslots, pxc_error* err) {
     PXC_CONFIG(h != nullptr, "handle", 0, "null flat handle");
     std::lock_guard<std::mutex> lock(h->mu);
     PXC_CONFIG(nslots <= h->nslots, "nslots", nslots, "truncate cannot grow the mirror");
+    DeviceGuard g(h->ctx->device);
+    handoff_drain(h);  // the next search rebuilds the mirror that earlier searches may still read
     h->nslots = nslots;
     h->dirty = true;
   });
@@ -920,7 +944,9 @@ pxc_status pxc_flat_search_device(pxc_flat* h, const float* d_queries, uint32_t 
     std::lock_guard<std::mutex> lock(h->mu);
     DeviceGuard g(h->ctx->device);
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->ctx->stream;
+    handoff_wait(h, s);
     search_device(h, d_queries, nq, k, d_bitmap, d_out_ids, d_out_dist, d_out_len, s);
+    handoff_done(h, s);
   });
 }
 
@@ -934,6 +960,7 @@ pxc_status pxc_flat_search(pxc_flat* h, const float* queries, uint32_t nq, uint3
     std::lock_guard<std::mutex> lock(h->mu);
     DeviceGuard g(h->ctx->device);
     cudaStream_t s = h->ctx->stream;
+    handoff_wait(h, s);
     const uint64_t dim = h->dim;
     DBuf<float>& dq = h->io_q;
     DBuf<uint64_t>& dbm = h->io_bm;
@@ -961,6 +988,7 @@ pxc_status pxc_flat_search(pxc_flat* h, const float* queries, uint32_t nq, uint3
       PXC_CUDA(cudaMemcpyAsync(out_dist, ddist.p, (size_t)nq * k * sizeof(float), cudaMemcpyDeviceToHost, s));
     }
     PXC_CUDA(cudaMemcpyAsync(out_len, dlen.p, nq * sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
+    handoff_done(h, s);
     PXC_CUDA(cudaStreamSynchronize(s));
   });
 }

@@ -565,8 +565,13 @@ struct pxc_ivfpq {
   pxc::DBuf<uint32_t> io_len;
   cudaEvent_t ev_begin = nullptr, ev_end = nullptr;  // scan timing when the context profiles
   bool timed = false;
+  cudaEvent_t ev_done = nullptr;  // end of the last search's work (handoff of the scratch)
   std::mutex mu;
   ~pxc_ivfpq() {
+    if (ev_done) {
+      cudaEventSynchronize(ev_done);  // a search on another stream may still be running
+      cudaEventDestroy(ev_done);
+    }
     if (h_scanned) cudaFreeHost(h_scanned);
     if (h_u8_flag) cudaFreeHost(h_u8_flag);
     if (ev_begin) cudaEventDestroy(ev_begin);
@@ -576,6 +581,22 @@ struct pxc_ivfpq {
 
 namespace pxc {
 namespace ivf {
+
+// The handle's device scratch and index pass from one call to the next in
+// stream order. A device search returns once its kernels are enqueued and
+// concurrent searches may run on different streams, so each search makes its
+// stream wait (on the GPU) for the previous search's work and records the end
+// of its own; calls that rewrite the index wait on the host.
+void handoff_wait(pxc_ivfpq* h, cudaStream_t s) {
+  if (h->ev_done) PXC_CUDA(cudaStreamWaitEvent(s, h->ev_done, 0));
+}
+void handoff_done(pxc_ivfpq* h, cudaStream_t s) {
+  if (!h->ev_done) PXC_CUDA(cudaEventCreateWithFlags(&h->ev_done, cudaEventDisableTiming));
+  PXC_CUDA(cudaEventRecord(h->ev_done, s));
+}
+void handoff_drain(pxc_ivfpq* h) {
+  if (h->ev_done) PXC_CUDA(cudaEventSynchronize(h->ev_done));
+}
 
 void layout(uint32_t dim, uint32_t m, std::vector<uint32_t>& w, std::vector<uint32_t>& o) {
   // product.rs:227-238 — widths differ by at most one, the remainder leading
@@ -831,6 +852,7 @@ pxc_status pxc_ivfpq_set_parts(pxc_ivfpq* h, const float* centroids, const float
     std::lock_guard<std::mutex> lock(h->mu);
     DeviceGuard g(h->ctx->device);
     cudaStream_t s = h->ctx->stream;
+    ivf::handoff_drain(h);
     h->centroids.reserve((size_t)h->nlist * h->dim);
     h->codebooks.reserve((size_t)256 * h->dim);
     PXC_CUDA(cudaMemcpyAsync(h->centroids.p, centroids, (size_t)h->nlist * h->dim * 4, cudaMemcpyHostToDevice, s));
@@ -848,6 +870,7 @@ pxc_status pxc_ivfpq_set_store(pxc_ivfpq* h, const float* vectors, const uint64_
     std::lock_guard<std::mutex> lock(h->mu);
     DeviceGuard g(h->ctx->device);
     cudaStream_t s = h->ctx->stream;
+    ivf::handoff_drain(h);
     h->nslots = nslots;
     h->h_ids.resize(nslots);
     h->h_live.assign(nslots, 1);
@@ -909,6 +932,7 @@ pxc_status pxc_ivfpq_set_store_device(pxc_ivfpq* h, const float* d_vectors, cons
     std::lock_guard<std::mutex> lock(h->mu);
     DeviceGuard g(h->ctx->device);
     cudaStream_t s = h->ctx->stream;
+    ivf::handoff_drain(h);
     if (d_vectors && nslots) {
       h->vectors.reserve(nslots * h->dim);
       PXC_CUDA(cudaMemcpyAsync(h->vectors.p, d_vectors, nslots * h->dim * 4, cudaMemcpyDeviceToDevice, s));
@@ -939,6 +963,7 @@ pxc_status pxc_ivfpq_set_codes(pxc_ivfpq* h, const uint32_t* list_of, const uint
     PXC_CONFIG(h != nullptr && (h->nslots == 0 || (list_of && codes)), "codes", 0, "null argument");
     std::lock_guard<std::mutex> lock(h->mu);
     DeviceGuard g(h->ctx->device);
+    ivf::handoff_drain(h);
     std::vector<uint32_t> lo(list_of, list_of + h->nslots);
     ivf::build_lists(h, lo, codes, h->ctx->stream);
     h->list_of.reserve(std::max<uint64_t>(1, h->nslots));
@@ -955,6 +980,7 @@ pxc_status pxc_ivfpq_encode_all(pxc_ivfpq* h, pxc_error* err) {
     PXC_CONFIG(h != nullptr, "h", 0, "null handle");
     std::lock_guard<std::mutex> lock(h->mu);
     DeviceGuard g(h->ctx->device);
+    ivf::handoff_drain(h);
     ivf::encode_all(h, h->ctx->stream);
   });
 }
@@ -965,6 +991,7 @@ pxc_status pxc_ivfpq_train(pxc_ivfpq* h, uint64_t training_sample, uint32_t max_
     PXC_CONFIG(h != nullptr, "h", 0, "null handle");
     std::lock_guard<std::mutex> lock(h->mu);
     DeviceGuard g(h->ctx->device);
+    ivf::handoff_drain(h);
     pxc_ctx* ctx = h->ctx;
     cudaStream_t s = ctx->stream;
     const uint32_t dim = h->dim, m = h->m;
@@ -1083,7 +1110,9 @@ pxc_status pxc_ivfpq_search_device(pxc_ivfpq* h, const float* d_queries, uint32_
     std::lock_guard<std::mutex> lock(h->mu);
     DeviceGuard g(h->ctx->device);
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->ctx->stream;
+    ivf::handoff_wait(h, s);
     ivf::search_device(h, d_queries, nq, k, nprobe, rerank, d_bitmap, d_out_ids, d_out_dist, d_out_len, s);
+    ivf::handoff_done(h, s);
   });
 }
 
@@ -1105,6 +1134,7 @@ pxc_status pxc_ivfpq_search(pxc_ivfpq* h, const float* queries, uint32_t nq, uin
     h->io_ids.reserve((size_t)nq * std::max<uint32_t>(k, 1));
     h->io_dist.reserve((size_t)nq * std::max<uint32_t>(k, 1));
     h->io_len.reserve(nq);
+    ivf::handoff_wait(h, s);
     const uint64_t* db = nullptr;
     if (bitmap) {
       const uint64_t words = (h->nslots + 63) / 64;
@@ -1119,6 +1149,7 @@ pxc_status pxc_ivfpq_search(pxc_ivfpq* h, const float* queries, uint32_t nq, uin
       PXC_CUDA(cudaMemcpyAsync(out_ids, h->io_ids.p, (size_t)nq * k * 8, cudaMemcpyDeviceToHost, s));
       PXC_CUDA(cudaMemcpyAsync(out_dist, h->io_dist.p, (size_t)nq * k * 4, cudaMemcpyDeviceToHost, s));
     }
+    ivf::handoff_done(h, s);
     PXC_CUDA(cudaStreamSynchronize(s));
   });
 }
