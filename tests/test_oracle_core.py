@@ -200,3 +200,38 @@ def test_integer_vectors_have_exact_f32_squared_euclidean(dim):
         assert exact < 2 ** 24
         got = pxo.squared_euclidean(a.astype(np.float32), b.astype(np.float32))
         assert got == float(exact)
+
+
+def _two_squares(d: float) -> list[float]:
+    """An integer point (a, b) with a^2 + b^2 == d: its squared distance to the origin is d exactly."""
+    n = int(d)
+    for a in range(int(math.isqrt(n)) + 1):
+        b = math.isqrt(n - a * a)
+        if a * a + b * b == n:
+            return [float(a), float(b)]
+    raise ValueError(d)
+
+
+def test_topk_known_answers_through_the_flat_scan():
+    """TopK's own tests (topk.rs:215-265), replayed as slots of a flat scan from the origin."""
+    t = KAT["topk_best_k"]
+    ids = [i for i, _ in t["pushes"]]
+    rows = [_two_squares(d) for _, d in t["pushes"]]
+    got, dist, lens = _flat(rows, ids, [[0.0, 0.0]], t["k"])
+    assert list(got[0, : lens[0]]) == t["expected_ids"]
+    assert list(dist[0, : lens[0]]) == sorted(d for _, d in t["pushes"])[: t["k"]]
+    # ties break on id whatever the slot (arrival) order
+    t = KAT["topk_ties"]
+    answers = []
+    for order in t["orders"]:
+        rows = [_two_squares(t["distance"])] * len(order)
+        got, _, lens = _flat(rows, order, [[0.0, 0.0]], t["k"])
+        answers.append(list(got[0, : lens[0]]))
+    assert answers[0] == answers[1] == sorted(t["orders"][0])[: t["k"]]
+    # k = 0 returns nothing; fewer candidates than k is not an error
+    t = KAT["topk_k_zero_and_short"]
+    _, _, lens = _flat([[1.0, 0.0]], [1], [[0.0, 0.0]], 0)
+    assert int(lens[0]) == t["k_zero_len"]
+    _, _, lens = _flat([[1.0, 0.0]] * t["short_pushes"], list(range(1, t["short_pushes"] + 1)), [[0.0, 0.0]],
+                       t["short_k"])
+    assert int(lens[0]) == t["short_len"]
