@@ -8,7 +8,8 @@
  *
  * Each entry point names the reference interface (Liona-orph/proxima, Rust)
  * it replaces. The Rust side keeps its types and calls these through a thin
- * FFI crate (`proxima-cuda`); see INTEGRATION.md for the binding.
+ * FFI crate (`proxima-cuda`) that declares these functions and owns the
+ * handles.
  *
  * Conventions shared by all entry points:
  *  - Host pointers are borrowed for the duration of the call and copied; no
@@ -93,6 +94,14 @@ uint64_t pxc_ctx_launch_count(const pxc_ctx* ctx);
  * on the launching stream; pxc_flat_last_scan_ms reads the last duration
  * (milliseconds, synchronising on the end event). Off by default. */
 pxc_status pxc_ctx_set_profiling(pxc_ctx* ctx, int32_t on, pxc_error* err);
+/* Diagnostic switches for tests, off by default; no production caller sets
+ * them. "sq_candidate_cap" (>= 0) shrinks the SQ threshold pass's candidate
+ * buffers so that its exact fallback runs; "sq_spec_rank" (>= 1) forces the SQ
+ * speculative admission rank; "kmeans_exact" (0/1) assigns k-means points
+ * without the tensor-core screen; "kmeans_trace" (0/1) prints per-iteration
+ * counters to stderr. A negative cap or rank restores the default. Unknown
+ * names are PXC_CONFIGURATION. */
+pxc_status pxc_ctx_set_option(pxc_ctx* ctx, const char* name, int64_t value, pxc_error* err);
 
 /* ---- FlatIndex: exact filtered top-k ----
  * Replaces the scan loop of FlatIndex::search
@@ -154,8 +163,10 @@ uint32_t pxc_flat_last_redone(const pxc_flat* h);
  * integers in [0,255], and a device mirror already built by an earlier
  * pxc_flat_len or search (PXC_CAPACITY / PXC_CONFIGURATION otherwise). The
  * first call on a device looks up the array's address; make it before any
- * stream capture. Calls share the array; within a process they are
- * serialised and each returns after its work has finished. Device buffers. */
+ * stream capture. Each call synchronises `stream` twice (after checking that
+ * the queries are integers, and at the end) and returns after its work has
+ * finished. Calls share the array; within a process they are serialised.
+ * Device buffers. */
 pxc_status pxc_flat_search_noalloc(pxc_flat* h, const float* d_queries, uint32_t nq, uint32_t k,
                                    uint64_t* d_out_ids, float* d_out_dist, uint32_t* d_out_len,
                                    void* stream, pxc_error* err);
@@ -170,6 +181,38 @@ pxc_status pxc_topk_merge(pxc_ctx* ctx, const uint64_t* d_ids, const float* d_di
                           const uint32_t* d_lens, uint32_t nparts, uint32_t nq, uint32_t k_in,
                           uint32_t k, uint64_t* d_out_ids, float* d_out_dist,
                           uint32_t* d_out_len, void* stream, pxc_error* err);
+
+/* ---- ChaCha8Rng ----
+ * The generator the reference's training draws from: rand_chacha 0.3.1's
+ * ChaCha8Rng (crates/proxima-quantize/src/kmeans.rs:150,167,169,
+ * product.rs:247, crates/proxima-index/src/ivfpq.rs:770), carried across the
+ * boundary as the three values rand_chacha exposes: get_seed() (32 bytes),
+ * get_stream() and get_word_pos() (a u128 count of u32 words, below 2^68).
+ * A Rust caller passes its generator with
+ *   pxc_rng { seed: rng.get_seed(), stream: rng.get_stream(),
+ *             word_pos_lo: pos as u64, word_pos_hi: (pos >> 64) as u64 }
+ * and afterwards restores it with set_stream + set_word_pos. These run on the
+ * host (no device work). */
+typedef struct pxc_rng {
+  uint8_t seed[32];
+  uint64_t stream;
+  uint64_t word_pos_lo;
+  uint64_t word_pos_hi;
+} pxc_rng;
+/* ChaCha8Rng::seed_from_u64(state) (rand_core 0.6.4: PCG32 expansion of the
+ * u64 into the 32-byte seed), stream 0, word position 0. */
+pxc_status pxc_rng_seed_from_u64(uint64_t state, pxc_rng* out, pxc_error* err);
+/* n successive RngCore::next_u32 draws; advances `rng`. */
+pxc_status pxc_rng_next_u32(pxc_rng* rng, uint32_t* out, uint64_t n, pxc_error* err);
+/* Rng::gen_range(0..bound) for usize (rand 0.8); bound >= 1. Advances `rng`. */
+pxc_status pxc_rng_gen_index(pxc_rng* rng, uint64_t bound, uint64_t* out, pxc_error* err);
+/* Rng::gen_range(low..high) for f64 (rand 0.8); low < high, finite span. */
+pxc_status pxc_rng_gen_f64(pxc_rng* rng, double low, double high, double* out, pxc_error* err);
+/* The ChaCha block function with `rounds` rounds (8 is ChaCha8Rng's; 20 is
+ * RFC 8439's): 16 words for (key, 64-bit block counter, 64-bit stream).
+ * Exposed so the generator can be checked against published known answers. */
+pxc_status pxc_chacha_block(const uint32_t key[8], uint64_t counter, uint64_t stream, uint32_t rounds,
+                            uint32_t out[16], pxc_error* err);
 
 /* ---- k-means ----
  * Replaces proxima_quantize::kmeans (crates/proxima-quantize/src/kmeans.rs:59-143),
@@ -191,20 +234,70 @@ typedef struct pxc_kmeans_info {
 } pxc_kmeans_info;
 
 /* points: n x dim f32 row-major (HOST). init: NULL for the reference's
- * k-means++ seeding from ChaCha8Rng::seed_from_u64(seed) (kmeans.rs:146-194),
- * or k_eff x dim initial centroids (an added option: the reference always
- * seeds with k-means++). out_centroids: room for k_eff x dim; out_assign
- * (nullable): n cluster indices. info (nullable). dim <= 512; points must be
- * finite (PXC_NON_FINITE, a = flat element index). */
+ * k-means++ seeding (kmeans.rs:146-194) drawn from `rng`, the caller's
+ * ChaCha8Rng state, which is advanced in place exactly as the reference's
+ * `&mut ChaCha8Rng` is (kmeans.rs:59-65); or k_eff x dim initial centroids
+ * (an added option: the reference always seeds with k-means++), in which case
+ * `rng` is neither read nor advanced and may be NULL. out_centroids: room for
+ * k_eff x dim; out_assign (nullable): n cluster indices. info (nullable).
+ * dim <= 512; points must be finite (PXC_NON_FINITE, a = flat element index).
+ * n == 0 returns k_eff zero centroids without drawing. */
 pxc_status pxc_kmeans(pxc_ctx* ctx, const float* points, uint64_t n, uint32_t dim, uint32_t k,
-                      uint32_t max_iterations, const float* init, uint64_t seed,
+                      uint32_t max_iterations, const float* init, pxc_rng* rng,
                       float* out_centroids, uint32_t* out_assign, pxc_kmeans_info* info,
                       pxc_error* err);
 /* The same with DEVICE buffers on `stream` (NULL: the context stream). */
 pxc_status pxc_kmeans_device(pxc_ctx* ctx, const float* d_points, uint64_t n, uint32_t dim,
                              uint32_t k, uint32_t max_iterations, const float* d_init,
-                             uint64_t seed, float* d_out_centroids, uint32_t* d_out_assign,
+                             pxc_rng* rng, float* d_out_centroids, uint32_t* d_out_assign,
                              pxc_kmeans_info* info, void* stream, pxc_error* err);
+
+/* ---- ProductQuantizer ----
+ * crates/proxima-quantize/src/product.rs. Codebooks are 256 x dim floats in
+ * ProductQuantizer::codebooks' layout: subspace-major, subspace s holding 256
+ * codewords of width[s] floats at 256 * offset[s], widths dim / m with the
+ * remainder spread over the leading subspaces (product.rs:227-238).
+ * 1 <= m <= dim <= 1024 (PXC_CONFIGURATION "subspaces" otherwise). */
+/* ProductQuantizer::train (product.rs:198-296) on n x dim HOST training rows:
+ * one ChaCha8Rng::seed_from_u64(seed) stream advanced across subspaces,
+ * kmeans(projection, width, 256, max_iterations, rng) per subspace (on the
+ * device, as pxc_kmeans), codebooks padded to 256 entries by repeating the
+ * last centroid. out_inertia / out_iterations (nullable) are
+ * training_inertia / training_iterations. n == 0 is PXC_CONFIGURATION
+ * ("training"); a non-finite component is PXC_NON_FINITE (a = its index
+ * within the vector). */
+pxc_status pxc_pq_train(pxc_ctx* ctx, const float* training, uint64_t n, uint32_t dim, uint32_t m,
+                        uint32_t max_iterations, uint64_t seed, float* out_codebooks, double* out_inertia,
+                        uint64_t* out_iterations, pxc_error* err);
+/* Same with DEVICE training rows and codebook output, on `stream`. */
+pxc_status pxc_pq_train_device(pxc_ctx* ctx, const float* d_training, uint64_t n, uint32_t dim, uint32_t m,
+                               uint32_t max_iterations, uint64_t seed, float* d_out_codebooks, double* out_inertia,
+                               uint64_t* out_iterations, void* stream, pxc_error* err);
+/* ProductQuantizer::encode_into (product.rs:361-380) for n vectors: per
+ * subspace the codeword with the smallest sequential squared distance, ties
+ * to the lower index (nearest_centroid, :529-547). HOST buffers; out_codes
+ * n x m bytes. */
+pxc_status pxc_pq_encode(pxc_ctx* ctx, const float* codebooks, uint32_t dim, uint32_t m, const float* vectors,
+                         uint64_t n, uint8_t* out_codes, pxc_error* err);
+/* Same with DEVICE codebooks, vectors and codes, on `stream`. */
+pxc_status pxc_pq_encode_device(pxc_ctx* ctx, const float* d_codebooks, uint32_t dim, uint32_t m,
+                                const float* d_vectors, uint64_t n, uint8_t* d_out_codes, void* stream,
+                                pxc_error* err);
+/* ProductQuantizer::decode (product.rs:387-398): the chosen codewords
+ * concatenated, n x dim floats. HOST buffers. */
+pxc_status pxc_pq_decode(pxc_ctx* ctx, const float* codebooks, uint32_t dim, uint32_t m, const uint8_t* codes,
+                         uint64_t n, float* out, pxc_error* err);
+/* ProductQuantizer::distance_table (product.rs:407-439) for nq queries:
+ * out_squared / out_dot are nq x m x 256 floats, entry (q, s, c) at
+ * (q * m + s) * 256 + c, each the sequential sum over the subspace width of
+ * (q - c)^2 or q * c. DistanceTable::squared_l2 / inner_product
+ * (product.rs:580-601) are then m lookups per code. HOST buffers. */
+pxc_status pxc_pq_tables(pxc_ctx* ctx, const float* codebooks, uint32_t dim, uint32_t m, const float* queries,
+                         uint32_t nq, float* out_squared, float* out_dot, pxc_error* err);
+/* Same with DEVICE buffers, on `stream`. */
+pxc_status pxc_pq_tables_device(pxc_ctx* ctx, const float* d_codebooks, uint32_t dim, uint32_t m,
+                                const float* d_queries, uint32_t nq, float* d_out_squared, float* d_out_dot,
+                                void* stream, pxc_error* err);
 
 /* ---- IvfPqIndex ----
  * The device side of IvfPqIndex (crates/proxima-index/src/ivfpq.rs): coarse
@@ -316,6 +409,20 @@ pxc_status pxc_sq_encode_device(pxc_ctx* ctx, const float* min, const float* inv
 pxc_status pxc_sq_decode(pxc_ctx* ctx, const float* min, const float* scale, uint32_t dim, int32_t mode,
                          int32_t code_type, const uint8_t* codes, uint64_t n, float* out,
                          pxc_error* err);
+
+/* ScalarQuantizer::asymmetric_squared_l2 (metric PXC_EUCLIDEAN) or
+ * asymmetric_inner_product (PXC_INNER_PRODUCT, and PXC_COSINE on prepared
+ * vectors) (scalar.rs:298-327) for every pair of nq HOST queries and n HOST
+ * codes: out[q * n + i], the reference's sequential sum over components with
+ * reconstruct = min + level * scale, bit for bit. nq <= 524280. */
+pxc_status pxc_sq_asymmetric(pxc_ctx* ctx, const float* min, const float* scale, uint32_t dim, int32_t mode,
+                             int32_t code_type, int32_t metric, const float* queries, uint32_t nq,
+                             const uint8_t* codes, uint64_t n, float* out, pxc_error* err);
+/* Same with DEVICE queries, codes and output (the range table on the host),
+ * on `stream`. */
+pxc_status pxc_sq_asymmetric_device(pxc_ctx* ctx, const float* min, const float* scale, uint32_t dim, int32_t mode,
+                                    int32_t code_type, int32_t metric, const float* d_queries, uint32_t nq,
+                                    const uint8_t* d_codes, uint64_t n, float* d_out, void* stream, pxc_error* err);
 
 /* ---- SQ filtered search ----
  * No counterpart index in the reference: its SQ path is train -> encode ->

@@ -155,18 +155,22 @@ void parallel_for(uint64_t n, int threads, const std::function<void(uint64_t, ui
 
 // ---------------------------------------------------------------------------
 // rand restatement. ChaCha (D. J. Bernstein, "ChaCha, a variant of Salsa20")
-// with 8 rounds, 64-bit block counter in words 12-13 and a zero 64-bit stream
-// id in words 14-15, blocks emitted four at a time into a 64-word buffer;
-// seed_from_u64 expands the u64 with PCG32 (XSH-RR, O'Neill 2014) into the
-// 32-byte key; ranges follow rand 0.8's documented widening-multiply
-// rejection (integers) and [1,2)-mantissa method (floats). PARITY UNPINNED.
+// with 8 rounds, 64-bit block counter in words 12-13 and a 64-bit stream id
+// in words 14-15 (zero for the generator), blocks emitted four at a time into
+// a 64-word buffer; seed_from_u64 expands the u64 with PCG32 (XSH-RR, O'Neill
+// 2014) into the 32-byte key; ranges follow rand 0.8's documented
+// widening-multiply rejection (integers) and [1,2)-mantissa method (floats).
+// The block function is pinned by RFC 8439's and the 8-round zero-key known
+// answers (tests/test_rng_kat.py); the draws of the Rust crates themselves are
+// not (no golden draw exists in the reference).
 // ---------------------------------------------------------------------------
 inline uint32_t rotl32(uint32_t x, int r) { return (x << r) | (x >> (32 - r)); }
 
-void chacha_block(const uint32_t key[8], uint64_t counter, uint32_t out[16], int rounds) {
+void chacha_block(const uint32_t key[8], uint64_t counter, uint64_t stream, uint32_t out[16], int rounds) {
   uint32_t s[16] = {0x61707865u, 0x3320646eu, 0x79622d32u, 0x6b206574u,
                     key[0], key[1], key[2], key[3], key[4], key[5], key[6], key[7],
-                    static_cast<uint32_t>(counter), static_cast<uint32_t>(counter >> 32), 0u, 0u};
+                    static_cast<uint32_t>(counter), static_cast<uint32_t>(counter >> 32),
+                    static_cast<uint32_t>(stream), static_cast<uint32_t>(stream >> 32)};
   uint32_t x[16];
   std::memcpy(x, s, sizeof(x));
   auto qr = [&](int a, int b, int c, int d) {
@@ -183,7 +187,7 @@ void chacha_block(const uint32_t key[8], uint64_t counter, uint32_t out[16], int
 }
 
 void rng_refill(pxo_rng* r) {
-  for (int b = 0; b < 4; ++b) chacha_block(r->key, r->counter + b, r->buf + 16 * b, 8);
+  for (int b = 0; b < 4; ++b) chacha_block(r->key, r->counter + b, 0, r->buf + 16 * b, 8);
   r->counter += 4;
   r->index = 0;
 }
@@ -191,6 +195,10 @@ void rng_refill(pxo_rng* r) {
 }  // namespace
 
 extern "C" {
+
+void pxo_chacha_block(const uint32_t key[8], uint64_t counter, uint64_t stream, int rounds, uint32_t out[16]) {
+  chacha_block(key, counter, stream, out, rounds);
+}
 
 float pxo_squared_euclidean(const float* a, const float* b, uint64_t dim) { return l2_unrolled(a, b, dim); }
 float pxo_squared_euclidean_scalar(const float* a, const float* b, uint64_t dim) { return l2_sequential(a, b, dim); }

@@ -63,6 +63,8 @@ float pxo_recall_overlap(const uint64_t* exact, uint32_t exact_len,
 
 /* ---- rand restatement (ChaCha8 + PCG32 seed expansion + rand 0.8 ranges) ---- */
 typedef struct pxo_rng { uint32_t key[8]; uint64_t counter; uint32_t buf[64]; uint32_t index; } pxo_rng;
+/* the ChaCha block function: key, 64-bit counter (words 12-13), 64-bit stream (14-15), rounds */
+void pxo_chacha_block(const uint32_t key[8], uint64_t counter, uint64_t stream, int rounds, uint32_t out[16]);
 void pxo_rng_seed_from_u64(pxo_rng* r, uint64_t seed);
 uint32_t pxo_rng_next_u32(pxo_rng* r);
 uint64_t pxo_rng_next_u64(pxo_rng* r);

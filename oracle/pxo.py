@@ -58,6 +58,7 @@ def lib():
             "pxo_prepare": (i64, [i32, vp, u64, u64]),
             "pxo_flat_search": (None, [vp, vp, vp, u64, u64, i32, vp, u64, u64, vp, vp, vp, vp, i32]),
             "pxo_recall_overlap": (f32, [vp, C.c_uint32, vp, C.c_uint32]),
+            "pxo_chacha_block": (None, [vp, u64, u64, C.c_int, vp]),
             "pxo_rng_seed_from_u64": (None, [vp, u64]),
             "pxo_rng_next_u32": (C.c_uint32, [vp]),
             "pxo_rng_next_u64": (u64, [vp]),

@@ -59,6 +59,17 @@ class PxcIvfpqReport(C.Structure):
     ]
 
 
+class PxcRng(C.Structure):
+    """pxc_rng: a ChaCha8Rng as rand_chacha exposes it (seed, stream, word position)."""
+
+    _fields_ = [
+        ("seed", C.c_uint8 * 32),
+        ("stream", C.c_uint64),
+        ("word_pos_lo", C.c_uint64),
+        ("word_pos_hi", C.c_uint64),
+    ]
+
+
 class PxcIntRange(C.Structure):
     """pxc_int_range: lo <= value <= hi on an integer metadata column."""
 
@@ -93,11 +104,33 @@ SIGNATURES: dict[str, tuple] = {
     "pxc_ctx_set_profiling": (C.c_int32, [vp, C.c_int32, C.POINTER(PxcError)]),
     "pxc_topk_merge": (C.c_int32, [vp, vp, vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
                                    vp, vp, vp, vp, C.POINTER(PxcError)]),
-    "pxc_kmeans": (C.c_int32, [vp, vp, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, vp, C.c_uint64,
+    "pxc_ctx_set_option": (C.c_int32, [vp, C.c_char_p, C.c_int64, C.POINTER(PxcError)]),
+    "pxc_rng_seed_from_u64": (C.c_int32, [C.c_uint64, C.POINTER(PxcRng), C.POINTER(PxcError)]),
+    "pxc_rng_next_u32": (C.c_int32, [C.POINTER(PxcRng), vp, C.c_uint64, C.POINTER(PxcError)]),
+    "pxc_rng_gen_index": (C.c_int32, [C.POINTER(PxcRng), C.c_uint64, C.POINTER(C.c_uint64), C.POINTER(PxcError)]),
+    "pxc_rng_gen_f64": (C.c_int32, [C.POINTER(PxcRng), C.c_double, C.c_double, C.POINTER(C.c_double),
+                                    C.POINTER(PxcError)]),
+    "pxc_chacha_block": (C.c_int32, [vp, C.c_uint64, C.c_uint64, C.c_uint32, vp, C.POINTER(PxcError)]),
+    "pxc_kmeans": (C.c_int32, [vp, vp, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, vp, C.POINTER(PxcRng),
                                vp, vp, C.POINTER(PxcKmeansInfo), C.POINTER(PxcError)]),
     "pxc_kmeans_device": (C.c_int32, [vp, vp, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, vp,
-                                      C.c_uint64, vp, vp, C.POINTER(PxcKmeansInfo), vp,
+                                      C.POINTER(PxcRng), vp, vp, C.POINTER(PxcKmeansInfo), vp,
                                       C.POINTER(PxcError)]),
+    "pxc_pq_train": (C.c_int32, [vp, vp, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint64, vp,
+                                 C.POINTER(C.c_double), C.POINTER(C.c_uint64), C.POINTER(PxcError)]),
+    "pxc_pq_train_device": (C.c_int32, [vp, vp, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint64, vp,
+                                        C.POINTER(C.c_double), C.POINTER(C.c_uint64), vp, C.POINTER(PxcError)]),
+    "pxc_pq_encode": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, vp, C.c_uint64, vp, C.POINTER(PxcError)]),
+    "pxc_pq_encode_device": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, vp, C.c_uint64, vp, vp,
+                                         C.POINTER(PxcError)]),
+    "pxc_pq_decode": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, vp, C.c_uint64, vp, C.POINTER(PxcError)]),
+    "pxc_pq_tables": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, vp, C.c_uint32, vp, vp, C.POINTER(PxcError)]),
+    "pxc_pq_tables_device": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, vp, C.c_uint32, vp, vp, vp,
+                                         C.POINTER(PxcError)]),
+    "pxc_sq_asymmetric": (C.c_int32, [vp, vp, vp, C.c_uint32, C.c_int32, C.c_int32, C.c_int32, vp, C.c_uint32,
+                                      vp, C.c_uint64, vp, C.POINTER(PxcError)]),
+    "pxc_sq_asymmetric_device": (C.c_int32, [vp, vp, vp, C.c_uint32, C.c_int32, C.c_int32, C.c_int32, vp,
+                                             C.c_uint32, vp, C.c_uint64, vp, vp, C.POINTER(PxcError)]),
     "pxc_ivfpq_create": (C.c_int32, [vp, C.c_uint32, C.c_int32, C.c_uint32, C.c_uint32, C.POINTER(vp),
                                      C.POINTER(PxcError)]),
     "pxc_ivfpq_destroy": (None, [vp]),

@@ -136,7 +136,12 @@ struct pxc_ctx {
   int sm_count = 0;
   bool profiling = false;
   unsigned long long launches = 0;  // kernels launched by this library on this context
-  std::mutex mu;  // serialises use of the context stream from search entry points
+  std::mutex mu;  // serialises use of the context stream and d_status (k-means, SQ)
+  // Diagnostic knobs set through pxc_ctx_set_option (tests only; all off by default).
+  int64_t opt_sq_candidate_cap = -1;  // >= 0: shrink the SQ threshold-pass buffers (forces the fallback)
+  int64_t opt_sq_spec_rank = -1;      // >= 1: force the SQ speculative admission rank
+  bool opt_kmeans_exact = false;      // k-means assignment without the tensor-core screen
+  bool opt_kmeans_trace = false;      // k-means prints per-iteration counters to stderr
   // k-means scratch kept between calls (grown on demand, freed with the context)
   void* kmeans_ws = nullptr;
   void (*kmeans_ws_free)(void*) = nullptr;
@@ -193,4 +198,6 @@ struct DBuf {
 // Reads the device error word after a kernel with bounded waits and turns it
 // into a Failure. Synchronises the stream.
 void check_device_status(pxc_ctx* ctx, cudaStream_t s, const char* where);
+// Same for an error word owned by a handle (d_status device, h_status pinned).
+void check_status_word(uint32_t* d_status, uint32_t* h_status, cudaStream_t s, const char* where);
 }  // namespace pxc

@@ -8,13 +8,16 @@
 namespace pxc {
 
 void check_device_status(pxc_ctx* ctx, cudaStream_t s, const char* where) {
-  PXC_CUDA(cudaMemcpyAsync(ctx->h_status, ctx->d_status, 2 * sizeof(uint32_t),
-                           cudaMemcpyDeviceToHost, s));
+  check_status_word(ctx->d_status, ctx->h_status, s, where);
+}
+
+void check_status_word(uint32_t* d_status, uint32_t* h_status, cudaStream_t s, const char* where) {
+  PXC_CUDA(cudaMemcpyAsync(h_status, d_status, 2 * sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
   PXC_CUDA(cudaStreamSynchronize(s));
-  uint32_t code = ctx->h_status[0];
+  uint32_t code = h_status[0];
   if (code != DEV_OK) {
-    uint32_t aux = ctx->h_status[1];
-    PXC_CUDA(cudaMemsetAsync(ctx->d_status, 0, 2 * sizeof(uint32_t), s));
+    uint32_t aux = h_status[1];
+    PXC_CUDA(cudaMemsetAsync(d_status, 0, 2 * sizeof(uint32_t), s));
     PXC_CUDA(cudaStreamSynchronize(s));
     if (code == DEV_BAD_SHAPE)
       throw make_failure(PXC_INTERNAL, code, aux, nullptr, "%s: kernel rejected its launch shape",
@@ -128,6 +131,25 @@ pxc_status pxc_ctx_set_wait_limit(pxc_ctx* ctx, uint32_t milliseconds, pxc_error
 }
 
 uint64_t pxc_ctx_launch_count(const pxc_ctx* ctx) { return ctx ? ctx->launches : 0; }
+
+pxc_status pxc_ctx_set_option(pxc_ctx* ctx, const char* name, int64_t value, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(ctx != nullptr, "ctx", 0, "null context");
+    PXC_CONFIG(name != nullptr, "name", 0, "null option name");
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (std::strcmp(name, "sq_candidate_cap") == 0) {
+      ctx->opt_sq_candidate_cap = value < 0 ? -1 : value;
+    } else if (std::strcmp(name, "sq_spec_rank") == 0) {
+      ctx->opt_sq_spec_rank = value < 1 ? -1 : value;
+    } else if (std::strcmp(name, "kmeans_exact") == 0) {
+      ctx->opt_kmeans_exact = value != 0;
+    } else if (std::strcmp(name, "kmeans_trace") == 0) {
+      ctx->opt_kmeans_trace = value != 0;
+    } else {
+      throw make_failure(PXC_CONFIGURATION, 0, 0, "name", "unknown diagnostic option '%.64s'", name);
+    }
+  });
+}
 
 pxc_status pxc_ctx_set_profiling(pxc_ctx* ctx, int32_t on, pxc_error* err) {
   return guarded(err, [&] {

@@ -366,6 +366,11 @@ struct pxc_flat {
   cudaEvent_t ev_begin = nullptr, ev_end = nullptr;
   bool ev_recorded = false;
   int* h_flag = nullptr;  // pinned
+  // This handle's device error word for K1's bounded waits ([0] code, [1] block)
+  // and its pinned mirror: handles on one context search concurrently, so each
+  // reads back only the failures of its own kernels.
+  uint32_t* d_status = nullptr;
+  uint32_t* h_status = nullptr;
   uint32_t last_redo = 0;  // queries of the last grouped search redone on K1g
   cudaEvent_t ev_done = nullptr;  // end of the last search's work (handoff of the scratch)
   std::mutex mu;
@@ -548,7 +553,7 @@ void search_tc(pxc_flat* h, const TcOperand& op, const float* d_q, uint32_t nq, 
   p.done_count = h->done.p;
   p.done_list = h->done.p + nqt;
   p.out_part = h->part.p;
-  p.status = h->ctx->d_status;
+  p.status = h->d_status;
   p.nq = nq;
   p.k = k;
   p.kblocks = h->dp / flat_tc::KB_BYTES;
@@ -789,7 +794,7 @@ void search_device(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, const
       search_tc(h, op, d_q, nq, k, d_ids, d_dist, d_len, s);
     else
       search_tc_grouped(h, op, d_q, nq, k, d_bitmap, d_ids, d_dist, d_len, s);
-    check_device_status(h->ctx, s, "flat search (tensor-core scan)");
+    check_status_word(h->d_status, h->h_status, s, "flat search (tensor-core scan)");
   } else {
     search_generic(h, d_q, nq, k, d_bitmap, d_ids, d_dist, d_len, s);
   }
@@ -813,8 +818,11 @@ pxc_status pxc_flat_create(pxc_ctx* ctx, uint32_t dim, int32_t metric, pxc_flat*
     h->dim = dim;
     h->metric = metric;
     cudaError_t e = cudaMallocHost(&h->h_flag, sizeof(int));
+    if (e == cudaSuccess) e = cudaMallocHost(&h->h_status, 2 * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&h->d_status, 2 * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(h->d_status, 0, 2 * sizeof(uint32_t));
     if (e != cudaSuccess) {
-      delete h;
+      pxc_flat_destroy(h);
       PXC_CUDA(e);
     }
     *out = h;
@@ -834,6 +842,8 @@ void pxc_flat_destroy(pxc_flat* h) {
   if (h->ev_begin) cudaEventDestroy(h->ev_begin);
   if (h->ev_end) cudaEventDestroy(h->ev_end);
   if (h->h_flag) cudaFreeHost(h->h_flag);
+  if (h->h_status) cudaFreeHost(h->h_status);
+  if (h->d_status) cudaFree(h->d_status);
   delete h;
   if (prev >= 0) cudaSetDevice(prev);
 }
@@ -1019,7 +1029,8 @@ pxc_status pxc_flat_search(pxc_flat* h, const float* queries, uint32_t nq, uint3
 //
 // Set-up: the first call on a device looks up the array's device address with
 // cudaGetSymbolAddress (with that device current); make that first call
-// before any stream capture.
+// before any stream capture. Every call synchronises its stream (after the
+// query check and at the end), so it returns with its work finished.
 // ---------------------------------------------------------------------------
 namespace {
 constexpr uint32_t NOALLOC_MAX_QUERIES = 2048;
@@ -1112,7 +1123,7 @@ extern "C" pxc_status pxc_flat_search_noalloc(pxc_flat* h, const float* d_querie
     p.done_count = done;
     p.done_list = done + nqt;
     p.out_part = part;
-    p.status = h->ctx->d_status;
+    p.status = h->d_status;
     p.nq = nq;
     p.k = k;
     p.kblocks = h->dp / flat_tc::KB_BYTES;
@@ -1141,6 +1152,6 @@ extern "C" pxc_status pxc_flat_search_noalloc(pxc_flat* h, const float* d_querie
                                            d_out_ids, d_out_dist, d_out_len);
     PXC_CUDA(cudaGetLastError());
     h->ctx->launches += 3;
-    check_device_status(h->ctx, s, "allocation-free flat search");  // synchronises the stream
+    check_status_word(h->d_status, h->h_status, s, "allocation-free flat search");  // synchronises the stream
   });
 }

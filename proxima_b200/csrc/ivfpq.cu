@@ -435,11 +435,16 @@ __global__ void __launch_bounds__(128) pq_encode_kernel(const float* __restrict_
   float* res = sm + 256 * w;     // [128][w + 1]
   for (uint32_t e = threadIdx.x; e < 256 * w; e += blockDim.x) book[e] = codebooks[256u * o + e];
   const uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
-  const bool valid = i < n && list_of[i] != UNASSIGNED;
+  // list_of == nullptr: plain ProductQuantizer::encode_into, the row itself
+  const bool valid = i < n && (list_of == nullptr || list_of[i] != UNASSIGNED);
   if (valid) {
     const float* x = X + i * ldx + o;
-    const float* c = centroids + (size_t)list_of[i] * dim + o;
-    for (uint32_t t = 0; t < w; ++t) res[threadIdx.x * (w + 1) + t] = __fsub_rn(x[t], c[t]);
+    if (list_of) {
+      const float* c = centroids + (size_t)list_of[i] * dim + o;
+      for (uint32_t t = 0; t < w; ++t) res[threadIdx.x * (w + 1) + t] = __fsub_rn(x[t], c[t]);
+    } else {
+      for (uint32_t t = 0; t < w; ++t) res[threadIdx.x * (w + 1) + t] = x[t];
+    }
   }
   __syncthreads();
   if (!valid) {
@@ -462,6 +467,51 @@ __global__ void __launch_bounds__(128) pq_encode_kernel(const float* __restrict_
     }
   }
   codes[i * m + s] = (uint8_t)best;
+}
+
+// ProductQuantizer::distance_table (product.rs:407-439): for every (query,
+// subspace, codeword) the sequential sums l2 += d*d, ip += q*c over the
+// subspace width, from 0.0, without contraction. Block = one (query,
+// subspace), thread = codeword; out[(q*m + s)*256 + c].
+__global__ void __launch_bounds__(256) pq_tables_kernel(const float* __restrict__ Q, uint32_t dim,
+                                                        const float* __restrict__ codebooks,
+                                                        const uint32_t* __restrict__ woff, uint32_t m,
+                                                        float* __restrict__ sq, float* __restrict__ dot) {
+  const uint32_t q = blockIdx.x, s = blockIdx.y, c = threadIdx.x;
+  const uint32_t w = woff[s], o = woff[m + s];
+  const float* qs = Q + (size_t)q * dim + o;
+  const float* cw = codebooks + 256ull * o + (size_t)c * w;
+  float l2 = 0.0f, ip = 0.0f;
+  for (uint32_t t = 0; t < w; ++t) {
+    const float qv = __ldg(qs + t), cv = __ldg(cw + t);
+    const float d = __fsub_rn(qv, cv);
+    l2 = __fadd_rn(l2, __fmul_rn(d, d));
+    ip = __fadd_rn(ip, __fmul_rn(qv, cv));
+  }
+  const size_t e = ((size_t)q * m + s) * 256 + c;
+  sq[e] = l2;
+  dot[e] = ip;
+}
+
+// ProductQuantizer::decode (product.rs:387-398): the chosen codewords, concatenated.
+__global__ void pq_decode_kernel(const uint8_t* __restrict__ codes, uint64_t n, uint32_t dim, uint32_t m,
+                                 const float* __restrict__ codebooks, const uint32_t* __restrict__ woff,
+                                 float* __restrict__ out) {
+  const uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (e >= n * m) return;
+  const uint64_t i = e / m;
+  const uint32_t s = (uint32_t)(e - i * m);
+  const uint32_t w = woff[s], o = woff[m + s];
+  const float* src = codebooks + 256ull * o + (size_t)codes[e] * w;
+  for (uint32_t t = 0; t < w; ++t) out[i * dim + o + t] = src[t];
+}
+
+// First non-finite element of n x dim rows (flat index), ~0 if none.
+__global__ void first_nonfinite_kernel(const float* __restrict__ X, uint64_t count,
+                                       unsigned long long* __restrict__ first) {
+  for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < count;
+       e += (uint64_t)gridDim.x * blockDim.x)
+    if (!isfinite(X[e])) atomicMin(first, (unsigned long long)e);
 }
 
 // Residuals of rows against their lists (ivfpq.rs:788-792): x - c per dimension.
@@ -749,6 +799,76 @@ void search_device(pxc_ivfpq* h, const float* d_q, uint32_t nq, uint32_t k, uint
 // encode_all (ivfpq.rs:828-865) on the device: list_of = nearest centroid in
 // squared_euclidean's order, codes = PQ code of the residual, lists rebuilt
 // in ascending slot order.
+// ProductQuantizer::train's per-subspace loop (product.rs:242-284) on n dense
+// device rows of `dim` floats: one ChaCha8 stream seeded once and advanced
+// across subspaces, kmeans(projection, width, 256, max_iter, rng) per
+// subspace, each codebook padded to 256 entries by repeating its last
+// centroid, inertia and iterations summed in subspace order. The caller holds
+// ctx->mu (k-means uses the context's workspace).
+void pq_train(pxc_ctx* ctx, const float* d_x, uint64_t n, uint32_t dim, const std::vector<uint32_t>& widths,
+              const std::vector<uint32_t>& offsets, uint32_t max_iter, uint64_t seed, float* d_books,
+              double* inertia, uint64_t* iterations, cudaStream_t s) {
+  ChaCha8 prng(seed);
+  DBuf<float> proj, book;
+  double total = 0.0;
+  uint64_t its = 0;
+  for (uint32_t sub = 0; sub < (uint32_t)widths.size(); ++sub) {
+    const uint32_t w = widths[sub], o = offsets[sub];
+    const uint32_t ldw = (w + 3) & ~3u;
+    proj.reserve(n * ldw);
+    gather_cols_kernel<<<(unsigned)((n * w + 255) / 256), 256, 0, s>>>(d_x, dim, n, o, w, ldw, proj.p);
+    book.reserve((size_t)256 * w);
+    km::Result r = km::kmeans_impl(ctx, proj.p, ldw, n, w, 256, max_iter, nullptr, &prng, book.p, nullptr, s);
+    total += r.inertia;
+    its += r.iterations;
+    float* dst = d_books + (size_t)256 * o;
+    PXC_CUDA(cudaMemcpyAsync(dst, book.p, (size_t)r.k * w * 4, cudaMemcpyDeviceToDevice, s));
+    for (uint32_t c = r.k; c < 256; ++c)
+      PXC_CUDA(cudaMemcpyAsync(dst + (size_t)c * w, book.p + (size_t)(r.k - 1) * w, w * 4, cudaMemcpyDeviceToDevice,
+                               s));
+    ctx->launches += 1;
+  }
+  PXC_CUDA(cudaStreamSynchronize(s));
+  *inertia = total;
+  *iterations = its;
+}
+
+// The (widths, offsets) table of a quantizer as the device kernels read it:
+// woff[s] = width, woff[m + s] = offset.
+void upload_layout(uint32_t dim, uint32_t m, std::vector<uint32_t>& w, std::vector<uint32_t>& o, DBuf<uint32_t>& woff,
+                   cudaStream_t s) {
+  layout(dim, m, w, o);
+  std::vector<uint32_t> host(2 * m);
+  for (uint32_t i = 0; i < m; ++i) {
+    host[i] = w[i];
+    host[m + i] = o[i];
+  }
+  woff.reserve(2 * m);
+  PXC_CUDA(cudaMemcpyAsync(woff.p, host.data(), 2 * m * 4, cudaMemcpyHostToDevice, s));
+}
+
+// Validation shared by the ProductQuantizer entry points (product.rs:199-213).
+void check_pq_shape(uint32_t dim, uint32_t m) {
+  PXC_CONFIG(dim >= 1 && dim <= MAX_DIM, "dim", dim, "the device quantizer supports 1 <= dim <= 1024");
+  PXC_CONFIG(m >= 1 && m <= dim, "subspaces", m, "must be between 1 and the space dimension");
+}
+
+// Throws NonFinite{index within its vector} for the first non-finite element.
+void check_finite(const float* d_x, uint64_t n, uint32_t dim, cudaStream_t s) {
+  if (n == 0) return;
+  DBuf<unsigned long long> first;
+  first.reserve(1);
+  PXC_CUDA(cudaMemsetAsync(first.p, 0xFF, 8, s));
+  first_nonfinite_kernel<<<1184, 256, 0, s>>>(d_x, n * dim, first.p);
+  PXC_CUDA(cudaGetLastError());
+  unsigned long long h = 0;
+  PXC_CUDA(cudaMemcpyAsync(&h, first.p, 8, cudaMemcpyDeviceToHost, s));
+  PXC_CUDA(cudaStreamSynchronize(s));
+  if (h != ~0ull)
+    throw make_failure(PXC_NON_FINITE, h % dim, 0, "training", "component %llu of vector %llu is not finite",
+                       h % dim, h / dim);
+}
+
 void encode_all(pxc_ivfpq* h, cudaStream_t s) {
   pxc_ctx* ctx = h->ctx;
   const uint64_t n = h->nslots;
@@ -979,6 +1099,7 @@ pxc_status pxc_ivfpq_encode_all(pxc_ivfpq* h, pxc_error* err) {
   return guarded(err, [&] {
     PXC_CONFIG(h != nullptr, "h", 0, "null handle");
     std::lock_guard<std::mutex> lock(h->mu);
+    std::lock_guard<std::mutex> ctx_lock(h->ctx->mu);  // nearest centroid uses the context's workspace
     DeviceGuard g(h->ctx->device);
     ivf::handoff_drain(h);
     ivf::encode_all(h, h->ctx->stream);
@@ -990,6 +1111,7 @@ pxc_status pxc_ivfpq_train(pxc_ivfpq* h, uint64_t training_sample, uint32_t max_
   return guarded(err, [&] {
     PXC_CONFIG(h != nullptr, "h", 0, "null handle");
     std::lock_guard<std::mutex> lock(h->mu);
+    std::lock_guard<std::mutex> ctx_lock(h->ctx->mu);  // k-means uses the context's workspace
     DeviceGuard g(h->ctx->device);
     ivf::handoff_drain(h);
     pxc_ctx* ctx = h->ctx;
@@ -1009,7 +1131,7 @@ pxc_status pxc_ivfpq_train(pxc_ivfpq* h, uint64_t training_sample, uint32_t max_
     for (uint64_t i = 0; i < live.size(); i += stride) pick.push_back(live[i]);
     const uint64_t ns = pick.size();
     DBuf<uint32_t> rows;
-    DBuf<float> sample, residuals, cent, proj, book, books;
+    DBuf<float> sample, residuals, cent, books;
     rows.reserve(ns);
     sample.reserve(ns * dim);
     PXC_CUDA(cudaMemcpyAsync(rows.p, pick.data(), ns * 4, cudaMemcpyHostToDevice, s));
@@ -1027,29 +1149,13 @@ pxc_status pxc_ivfpq_train(pxc_ivfpq* h, uint64_t training_sample, uint32_t max_
     residuals.reserve(ns * dim);
     ivf::residual_kernel<<<(unsigned)((ns * dim + 255) / 256), 256, 0, s>>>(sample.p, dim, ns, dim, near.p, cent.p,
                                                                          residuals.p);
-    // ProductQuantizer::train (product.rs:198-296): one fresh ChaCha8 stream
-    // with the same seed, advanced across subspaces; each codebook padded to
-    // 256 entries by repeating the last centroid
-    ChaCha8 prng(seed);
+    // ProductQuantizer::train (product.rs:198-296) on the residuals, with a
+    // fresh ChaCha8 stream of the same seed (ivfpq.rs:794-800)
     books.reserve((size_t)256 * dim);
     double residual_inertia = 0.0;
     uint64_t pq_iterations = 0;
-    for (uint32_t sub = 0; sub < m; ++sub) {
-      const uint32_t w = h->widths[sub], o = h->offsets[sub];
-      const uint32_t ldw = (w + 3) & ~3u;
-      proj.reserve(ns * ldw);
-      ivf::gather_cols_kernel<<<(unsigned)((ns * w + 255) / 256), 256, 0, s>>>(residuals.p, dim, ns, o, w, ldw,
-                                                                             proj.p);
-      book.reserve((size_t)256 * w);
-      km::Result r = km::kmeans_impl(ctx, proj.p, ldw, ns, w, 256, max_iterations, nullptr, &prng, book.p, nullptr, s);
-      residual_inertia += r.inertia;
-      pq_iterations += r.iterations;
-      float* dst = books.p + (size_t)256 * o;
-      PXC_CUDA(cudaMemcpyAsync(dst, book.p, (size_t)r.k * w * 4, cudaMemcpyDeviceToDevice, s));
-      for (uint32_t c = r.k; c < 256; ++c)
-        PXC_CUDA(cudaMemcpyAsync(dst + (size_t)c * w, book.p + (size_t)(r.k - 1) * w, w * 4, cudaMemcpyDeviceToDevice,
-                                 s));
-    }
+    ivf::pq_train(ctx, residuals.p, ns, dim, h->widths, h->offsets, max_iterations, seed, books.p, &residual_inertia,
+                  &pq_iterations, s);
     // install the parts (the list count is what k-means produced) and encode
     h->nlist = produced;
     h->centroids.reserve((size_t)produced * dim);
@@ -1150,6 +1256,187 @@ pxc_status pxc_ivfpq_search(pxc_ivfpq* h, const float* queries, uint32_t nq, uin
       PXC_CUDA(cudaMemcpyAsync(out_dist, h->io_dist.p, (size_t)nq * k * 4, cudaMemcpyDeviceToHost, s));
     }
     ivf::handoff_done(h, s);
+    PXC_CUDA(cudaStreamSynchronize(s));
+  });
+}
+
+// ---------------------------------------------------------------------------
+// ProductQuantizer on its own (crates/proxima-quantize/src/product.rs)
+// ---------------------------------------------------------------------------
+pxc_status pxc_pq_train_device(pxc_ctx* ctx, const float* d_training, uint64_t n, uint32_t dim, uint32_t m,
+                               uint32_t max_iterations, uint64_t seed, float* d_out_codebooks, double* out_inertia,
+                               uint64_t* out_iterations, void* stream, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(ctx != nullptr, "ctx", 0, "null context");
+    ivf::check_pq_shape(dim, m);
+    PXC_CONFIG(max_iterations >= 1, "max_iterations", max_iterations, "must be at least 1");
+    PXC_CONFIG(n >= 1 && d_training != nullptr, "training", n, "must be a non-empty multiple of the space dimension");
+    PXC_CONFIG(n <= 0x7FFFFFFFull, "training", n, "the device quantizer trains on fewer than 2^31 vectors");
+    PXC_CONFIG(d_out_codebooks != nullptr, "out_codebooks", 0, "null output buffer");
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    DeviceGuard g(ctx->device);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    ivf::check_finite(d_training, n, dim, s);
+    std::vector<uint32_t> w, o;
+    ivf::layout(dim, m, w, o);
+    double inertia = 0.0;
+    uint64_t its = 0;
+    ivf::pq_train(ctx, d_training, n, dim, w, o, max_iterations, seed, d_out_codebooks, &inertia, &its, s);
+    if (out_inertia) *out_inertia = inertia;
+    if (out_iterations) *out_iterations = its;
+  });
+}
+
+pxc_status pxc_pq_train(pxc_ctx* ctx, const float* training, uint64_t n, uint32_t dim, uint32_t m,
+                        uint32_t max_iterations, uint64_t seed, float* out_codebooks, double* out_inertia,
+                        uint64_t* out_iterations, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(ctx != nullptr, "ctx", 0, "null context");
+    ivf::check_pq_shape(dim, m);
+    PXC_CONFIG(max_iterations >= 1, "max_iterations", max_iterations, "must be at least 1");
+    PXC_CONFIG(n >= 1 && training != nullptr, "training", n, "must be a non-empty multiple of the space dimension");
+    PXC_CONFIG(out_codebooks != nullptr, "out_codebooks", 0, "null output buffer");
+    DBuf<float> dx, books;
+    {
+      DeviceGuard g(ctx->device);
+      dx.reserve(n * dim);
+      books.reserve((size_t)256 * dim);
+      // on the context stream, which the device entry point below also uses
+      PXC_CUDA(cudaMemcpyAsync(dx.p, training, n * dim * 4, cudaMemcpyHostToDevice, ctx->stream));
+    }
+    pxc_error e2{};
+    if (pxc_pq_train_device(ctx, dx.p, n, dim, m, max_iterations, seed, books.p, out_inertia, out_iterations, nullptr,
+                            &e2) != PXC_OK)
+      throw make_failure((pxc_status)e2.code, e2.a, e2.b, e2.parameter, "%s", e2.detail);
+    DeviceGuard g(ctx->device);
+    PXC_CUDA(cudaMemcpy(out_codebooks, books.p, (size_t)256 * dim * 4, cudaMemcpyDeviceToHost));
+  });
+}
+
+pxc_status pxc_pq_encode_device(pxc_ctx* ctx, const float* d_codebooks, uint32_t dim, uint32_t m,
+                                const float* d_vectors, uint64_t n, uint8_t* d_out_codes, void* stream,
+                                pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(ctx != nullptr, "ctx", 0, "null context");
+    ivf::check_pq_shape(dim, m);
+    if (n == 0) return;
+    PXC_CONFIG(d_codebooks && d_vectors && d_out_codes, "buffers", 0, "null buffer");
+    DeviceGuard g(ctx->device);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    std::vector<uint32_t> w, o;
+    DBuf<uint32_t> woff;
+    ivf::upload_layout(dim, m, w, o, woff, s);
+    const uint32_t wmax = *std::max_element(w.begin(), w.end());
+    const size_t smem = ((size_t)256 * wmax + 128 * (wmax + 1)) * 4;
+    PXC_CONFIG(smem <= 200 * 1024, "subspaces", m, "subspace too wide for the device encoder");
+    PXC_CUDA(cudaFuncSetAttribute(ivf::pq_encode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    for (uint64_t b = 0; b < n; b += (1ull << 30)) {  // grid.x stays below 2^31 / 128 blocks per launch
+      const uint64_t nb = std::min<uint64_t>(n - b, 1ull << 30);
+      ivf::pq_encode_kernel<<<dim3((unsigned)((nb + 127) / 128), m), 128, smem, s>>>(
+          d_vectors + b * dim, dim, nb, nullptr, nullptr, dim, d_codebooks, woff.p, m, d_out_codes + b * m);
+      PXC_CUDA(cudaGetLastError());
+      ctx->launches += 1;
+    }
+    PXC_CUDA(cudaStreamSynchronize(s));  // woff is freed on return
+  });
+}
+
+pxc_status pxc_pq_encode(pxc_ctx* ctx, const float* codebooks, uint32_t dim, uint32_t m, const float* vectors,
+                         uint64_t n, uint8_t* out_codes, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(ctx != nullptr, "ctx", 0, "null context");
+    ivf::check_pq_shape(dim, m);
+    if (n == 0) return;
+    PXC_CONFIG(codebooks && vectors && out_codes, "buffers", 0, "null buffer");
+    DeviceGuard g(ctx->device);
+    cudaStream_t s = ctx->stream;
+    std::lock_guard<std::mutex> lock(ctx->mu);  // the context stream
+    DBuf<float> db, dv;
+    DBuf<uint8_t> dc;
+    db.reserve((size_t)256 * dim);
+    dv.reserve(n * dim);
+    dc.reserve(n * m);
+    PXC_CUDA(cudaMemcpyAsync(db.p, codebooks, (size_t)256 * dim * 4, cudaMemcpyHostToDevice, s));
+    PXC_CUDA(cudaMemcpyAsync(dv.p, vectors, n * dim * 4, cudaMemcpyHostToDevice, s));
+    pxc_error e2{};
+    if (pxc_pq_encode_device(ctx, db.p, dim, m, dv.p, n, dc.p, s, &e2) != PXC_OK)
+      throw make_failure((pxc_status)e2.code, e2.a, e2.b, e2.parameter, "%s", e2.detail);
+    PXC_CUDA(cudaMemcpyAsync(out_codes, dc.p, n * m, cudaMemcpyDeviceToHost, s));
+    PXC_CUDA(cudaStreamSynchronize(s));
+  });
+}
+
+pxc_status pxc_pq_decode(pxc_ctx* ctx, const float* codebooks, uint32_t dim, uint32_t m, const uint8_t* codes,
+                         uint64_t n, float* out, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(ctx != nullptr, "ctx", 0, "null context");
+    ivf::check_pq_shape(dim, m);
+    if (n == 0) return;
+    PXC_CONFIG(codebooks && codes && out, "buffers", 0, "null buffer");
+    DeviceGuard g(ctx->device);
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    cudaStream_t s = ctx->stream;
+    std::vector<uint32_t> w, o;
+    DBuf<uint32_t> woff;
+    ivf::upload_layout(dim, m, w, o, woff, s);
+    DBuf<float> db, dout;
+    DBuf<uint8_t> dc;
+    db.reserve((size_t)256 * dim);
+    dc.reserve(n * m);
+    dout.reserve(n * dim);
+    PXC_CUDA(cudaMemcpyAsync(db.p, codebooks, (size_t)256 * dim * 4, cudaMemcpyHostToDevice, s));
+    PXC_CUDA(cudaMemcpyAsync(dc.p, codes, n * m, cudaMemcpyHostToDevice, s));
+    ivf::pq_decode_kernel<<<(unsigned)((n * m + 255) / 256), 256, 0, s>>>(dc.p, n, dim, m, db.p, woff.p, dout.p);
+    PXC_CUDA(cudaGetLastError());
+    ctx->launches += 1;
+    PXC_CUDA(cudaMemcpyAsync(out, dout.p, n * dim * 4, cudaMemcpyDeviceToHost, s));
+    PXC_CUDA(cudaStreamSynchronize(s));
+  });
+}
+
+pxc_status pxc_pq_tables_device(pxc_ctx* ctx, const float* d_codebooks, uint32_t dim, uint32_t m,
+                                const float* d_queries, uint32_t nq, float* d_out_squared, float* d_out_dot,
+                                void* stream, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(ctx != nullptr, "ctx", 0, "null context");
+    ivf::check_pq_shape(dim, m);
+    if (nq == 0) return;
+    PXC_CONFIG(d_codebooks && d_queries && d_out_squared && d_out_dot, "buffers", 0, "null buffer");
+    DeviceGuard g(ctx->device);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    std::vector<uint32_t> w, o;
+    DBuf<uint32_t> woff;
+    ivf::upload_layout(dim, m, w, o, woff, s);
+    ivf::pq_tables_kernel<<<dim3(nq, m), 256, 0, s>>>(d_queries, dim, d_codebooks, woff.p, m, d_out_squared,
+                                                      d_out_dot);
+    PXC_CUDA(cudaGetLastError());
+    ctx->launches += 1;
+    PXC_CUDA(cudaStreamSynchronize(s));  // woff is freed on return
+  });
+}
+
+pxc_status pxc_pq_tables(pxc_ctx* ctx, const float* codebooks, uint32_t dim, uint32_t m, const float* queries,
+                         uint32_t nq, float* out_squared, float* out_dot, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(ctx != nullptr, "ctx", 0, "null context");
+    ivf::check_pq_shape(dim, m);
+    if (nq == 0) return;
+    PXC_CONFIG(codebooks && queries && out_squared && out_dot, "buffers", 0, "null buffer");
+    DeviceGuard g(ctx->device);
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    cudaStream_t s = ctx->stream;
+    DBuf<float> db, dq, dsq, ddot;
+    db.reserve((size_t)256 * dim);
+    dq.reserve((size_t)nq * dim);
+    dsq.reserve((size_t)nq * m * 256);
+    ddot.reserve((size_t)nq * m * 256);
+    PXC_CUDA(cudaMemcpyAsync(db.p, codebooks, (size_t)256 * dim * 4, cudaMemcpyHostToDevice, s));
+    PXC_CUDA(cudaMemcpyAsync(dq.p, queries, (size_t)nq * dim * 4, cudaMemcpyHostToDevice, s));
+    pxc_error e2{};
+    if (pxc_pq_tables_device(ctx, db.p, dim, m, dq.p, nq, dsq.p, ddot.p, s, &e2) != PXC_OK)
+      throw make_failure((pxc_status)e2.code, e2.a, e2.b, e2.parameter, "%s", e2.detail);
+    PXC_CUDA(cudaMemcpyAsync(out_squared, dsq.p, (size_t)nq * m * 256 * 4, cudaMemcpyDeviceToHost, s));
+    PXC_CUDA(cudaMemcpyAsync(out_dot, ddot.p, (size_t)nq * m * 256 * 4, cudaMemcpyDeviceToHost, s));
     PXC_CUDA(cudaStreamSynchronize(s));
   });
 }

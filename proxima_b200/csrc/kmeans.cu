@@ -1176,21 +1176,31 @@ static void prepare_runner(Runner& R, pxc_ctx* ctx, const float* d_pts, uint32_t
   if (hb != ~0ull) throw make_failure(PXC_NON_FINITE, hb, 0, "points", "point element %llu is not finite", hb);
   float maxabs;
   std::memcpy(&maxabs, &hm, 4);
-  const char* force = std::getenv("PXC_KMEANS_EXACT");
-  const bool want_tensor = !(force && force[0] == '1') && d >= 16 && d <= 32u * km_tc::MAX_KBLOCKS &&
+  const bool want_tensor = !ctx->opt_kmeans_exact && d >= 16 && d <= 32u * km_tc::MAX_KBLOCKS &&
                            k_eff >= 256 && n >= 256 && maxabs <= 0x1p40f;
-  const char* tr = std::getenv("PXC_KMEANS_TRACE");
-  R.trace = tr && tr[0] == '1';
+  R.trace = ctx->opt_kmeans_trace;
 
   R.setup(want_tensor && allow_tensor);
 }
 
-// kmeans with an explicit seed (k-means++ from ChaCha8Rng::seed_from_u64) or init.
+// The caller's ChaCha8Rng state (pxc_rng) as a generator, and back.
+ChaCha8 rng_from_abi(const pxc_rng* r) {
+  PXC_CONFIG(r->word_pos_hi < 16, "word_pos", r->word_pos_hi, "ChaCha8Rng word positions are below 2^68");
+  return ChaCha8(r->seed, r->stream, r->word_pos_lo, r->word_pos_hi);
+}
+void rng_to_abi(const ChaCha8& g, pxc_rng* r) { g.state(r->seed, &r->stream, &r->word_pos_lo, &r->word_pos_hi); }
+
+// kmeans drawing k-means++ from the caller's generator (advanced in place), or from an init.
 Result kmeans_device(pxc_ctx* ctx, const float* d_pts, uint32_t ld, uint64_t n, uint32_t d, uint32_t k,
-                     uint32_t max_iter, const float* d_init, uint64_t seed, float* d_out_cent,
+                     uint32_t max_iter, const float* d_init, pxc_rng* rng, float* d_out_cent,
                      uint32_t* d_out_assign, cudaStream_t s) {
-  ChaCha8 rng(seed);
-  return kmeans_impl(ctx, d_pts, ld, n, d, k, max_iter, d_init, d_init ? nullptr : &rng, d_out_cent, d_out_assign, s);
+  const bool draws = d_init == nullptr && n > 0 && d > 0;
+  PXC_CONFIG(!draws || rng != nullptr, "rng", 0, "k-means++ seeding needs the caller's generator (rng is null)");
+  if (!draws) return kmeans_impl(ctx, d_pts, ld, n, d, k, max_iter, d_init, nullptr, d_out_cent, d_out_assign, s);
+  ChaCha8 g = rng_from_abi(rng);
+  Result r = kmeans_impl(ctx, d_pts, ld, n, d, k, max_iter, d_init, &g, d_out_cent, d_out_assign, s);
+  rng_to_abi(g, rng);
+  return r;
 }
 
 // Exact nearest centroid of every row (ties to the lower index): `unrolled`
@@ -1234,7 +1244,7 @@ using namespace pxc;
 extern "C" {
 
 pxc_status pxc_kmeans_device(pxc_ctx* ctx, const float* points, uint64_t n, uint32_t dim, uint32_t k,
-                             uint32_t max_iterations, const float* init, uint64_t seed, float* out_centroids,
+                             uint32_t max_iterations, const float* init, pxc_rng* rng, float* out_centroids,
                              uint32_t* out_assign, pxc_kmeans_info* info, void* stream, pxc_error* err) {
   return guarded(err, [&] {
     PXC_CONFIG(ctx != nullptr, "ctx", 0, "null context");
@@ -1243,14 +1253,14 @@ pxc_status pxc_kmeans_device(pxc_ctx* ctx, const float* points, uint64_t n, uint
     std::lock_guard<std::mutex> lock(ctx->mu);
     DeviceGuard g(ctx->device);
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
-    km::Result r = km::kmeans_device(ctx, points, dim, n, dim, k, max_iterations, init, seed, out_centroids,
+    km::Result r = km::kmeans_device(ctx, points, dim, n, dim, k, max_iterations, init, rng, out_centroids,
                                      out_assign, s);
     km::fill_info(info, r);
   });
 }
 
 pxc_status pxc_kmeans(pxc_ctx* ctx, const float* points, uint64_t n, uint32_t dim, uint32_t k,
-                      uint32_t max_iterations, const float* init, uint64_t seed, float* out_centroids,
+                      uint32_t max_iterations, const float* init, pxc_rng* rng, float* out_centroids,
                       uint32_t* out_assign, pxc_kmeans_info* info, pxc_error* err) {
   return guarded(err, [&] {
     PXC_CONFIG(ctx != nullptr, "ctx", 0, "null context");
@@ -1276,13 +1286,59 @@ pxc_status pxc_kmeans(pxc_ctx* ctx, const float* points, uint64_t n, uint32_t di
       PXC_CUDA(cudaMemcpyAsync(dinit.p, init, (size_t)k_eff * dim * 4, cudaMemcpyHostToDevice, s));
     }
     if (out_assign && n_eff) dassign.reserve(n_eff);
-    km::Result r = km::kmeans_device(ctx, dp.p, ld, n_eff, dim, k, max_iterations, init ? dinit.p : nullptr, seed,
+    km::Result r = km::kmeans_device(ctx, dp.p, ld, n_eff, dim, k, max_iterations, init ? dinit.p : nullptr, rng,
                                      dcent.p, out_assign ? dassign.p : nullptr, s);
     if (dim) PXC_CUDA(cudaMemcpyAsync(out_centroids, dcent.p, (size_t)r.k * dim * 4, cudaMemcpyDeviceToHost, s));
     if (out_assign && n_eff)
       PXC_CUDA(cudaMemcpyAsync(out_assign, dassign.p, n_eff * 4, cudaMemcpyDeviceToHost, s));
     PXC_CUDA(cudaStreamSynchronize(s));
     km::fill_info(info, r);
+  });
+}
+
+pxc_status pxc_rng_seed_from_u64(uint64_t state, pxc_rng* out, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(out != nullptr, "out", 0, "null generator");
+    km::rng_to_abi(ChaCha8(state), out);
+  });
+}
+
+pxc_status pxc_rng_next_u32(pxc_rng* rng, uint32_t* out, uint64_t n, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(rng != nullptr, "rng", 0, "null generator");
+    PXC_CONFIG(out != nullptr || n == 0, "out", 0, "null output buffer");
+    ChaCha8 g = km::rng_from_abi(rng);
+    for (uint64_t i = 0; i < n; ++i) out[i] = g.next_u32();
+    km::rng_to_abi(g, rng);
+  });
+}
+
+pxc_status pxc_rng_gen_index(pxc_rng* rng, uint64_t bound, uint64_t* out, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(rng != nullptr && out != nullptr, "rng", 0, "null generator or output");
+    PXC_CONFIG(bound >= 1, "bound", bound, "gen_range(0..bound) needs bound >= 1");
+    ChaCha8 g = km::rng_from_abi(rng);
+    *out = g.gen_index(bound);
+    km::rng_to_abi(g, rng);
+  });
+}
+
+pxc_status pxc_rng_gen_f64(pxc_rng* rng, double low, double high, double* out, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(rng != nullptr && out != nullptr, "rng", 0, "null generator or output");
+    PXC_CONFIG(low < high && std::isfinite(high - low), "high", 0, "gen_range(low..high) needs low < high, finite span");
+    ChaCha8 g = km::rng_from_abi(rng);
+    *out = g.gen_f64(low, high);
+    km::rng_to_abi(g, rng);
+  });
+}
+
+pxc_status pxc_chacha_block(const uint32_t key[8], uint64_t counter, uint64_t stream, uint32_t rounds,
+                            uint32_t out[16], pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(key != nullptr && out != nullptr, "key", 0, "null key or output");
+    PXC_CONFIG(rounds >= 2 && rounds <= 64 && rounds % 2 == 0, "rounds", rounds, "must be even, 2..64");
+    chacha_block(key, counter, stream, (int)rounds, out);
   });
 }
 

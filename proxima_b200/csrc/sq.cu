@@ -295,6 +295,64 @@ __global__ void __launch_bounds__(256) decode_kernel(const uint8_t* __restrict__
   }
 }
 
+// ScalarQuantizer::asymmetric_squared_l2 / asymmetric_inner_product
+// (scalar.rs:298-327) for every (query, code) pair: the sequential sum over
+// components of d * d with d = q - reconstruct, or of q * reconstruct then
+// negated, where reconstruct = min + f32(level) * scale; every step rounded
+// on its own (no contraction), as the reference computes it. Block = 128
+// codes (one per thread) x ASYM_Q queries; each 64-component slab of the
+// codes and queries is staged in shared memory, so one reconstruct serves
+// ASYM_Q queries. out[q * n + row].
+constexpr uint32_t ASYM_Q = 8;
+constexpr uint32_t ASYM_SLAB = 64;
+__global__ void __launch_bounds__(128) asymmetric_kernel(const float* __restrict__ Q, uint32_t nq,
+                                                         const uint8_t* __restrict__ codes, uint64_t n,
+                                                         uint32_t dim, const float* __restrict__ mn,
+                                                         const float* __restrict__ sc, int global, int i8,
+                                                         int inner, float* __restrict__ out) {
+  __shared__ uint8_t s_codes[128][ASYM_SLAB + 4];  // 68-byte rows: a warp's reads of one column hit distinct banks
+  __shared__ float s_q[ASYM_Q][ASYM_SLAB];
+  const uint64_t row0 = (uint64_t)blockIdx.x * 128;
+  const uint32_t q0 = blockIdx.y * ASYM_Q;
+  const uint32_t nqb = min(ASYM_Q, nq - q0);
+  float sum[ASYM_Q];
+#pragma unroll
+  for (int j = 0; j < (int)ASYM_Q; ++j) sum[j] = 0.0f;
+  for (uint32_t c0 = 0; c0 < dim; c0 += ASYM_SLAB) {
+    const uint32_t w = min(ASYM_SLAB, dim - c0);
+    __syncthreads();
+    for (uint32_t e = threadIdx.x; e < 128 * w; e += 128) {
+      const uint32_t r = e / w, t = e - r * w;
+      const uint64_t gr = row0 + r;
+      s_codes[r][t] = gr < n ? codes[gr * dim + c0 + t] : 0;
+    }
+    for (uint32_t e = threadIdx.x; e < ASYM_Q * w; e += 128) {
+      const uint32_t j = e / w, t = e - j * w;
+      s_q[j][t] = j < nqb ? Q[(size_t)(q0 + j) * dim + c0 + t] : 0.0f;
+    }
+    __syncthreads();
+    for (uint32_t t = 0; t < w; ++t) {
+      const uint32_t c = c0 + t, g = global ? 0 : c;
+      const uint8_t b = s_codes[threadIdx.x][t];
+      const uint8_t level = i8 ? static_cast<uint8_t>(b ^ 0x80u) : b;
+      const float r = __fadd_rn(__ldg(mn + g), __fmul_rn(static_cast<float>(level), __ldg(sc + g)));
+#pragma unroll
+      for (int j = 0; j < (int)ASYM_Q; ++j) {
+        const float qv = s_q[j][t];
+        if (inner) {
+          sum[j] = __fadd_rn(sum[j], __fmul_rn(qv, r));
+        } else {
+          const float d = __fsub_rn(qv, r);
+          sum[j] = __fadd_rn(sum[j], __fmul_rn(d, d));
+        }
+      }
+    }
+  }
+  const uint64_t row = row0 + threadIdx.x;
+  if (row >= n) return;
+  for (uint32_t j = 0; j < nqb; ++j) out[(size_t)(q0 + j) * n + row] = inner ? -sum[j] : sum[j];
+}
+
 // ---------------------------------------------------------------------------
 // search: acceptance, compaction, query preparation
 // ---------------------------------------------------------------------------
@@ -1010,9 +1068,9 @@ void search_device(pxc_sq* h, const float* d_q, uint32_t nq, uint32_t k, uint32_
   PXC_CUDA(cudaFuncSetAttribute(rerank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rr_smem(h->dim)));
   PXC_CUDA(cudaFuncSetAttribute(prefix_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(CB * 8)));
   uint32_t cap_limit = 0xFFFFFFFFu;
-  if (const char* e = std::getenv("PXC_SQ_CAP")) {  // diagnostic: shrink the THRESH buffers to force the fallback
-    const long v = std::strtol(e, nullptr, 10);
-    if (v >= 0 && (uint32_t)v < cap) cap = cap_limit = (uint32_t)v;
+  {  // diagnostic (pxc_ctx_set_option "sq_candidate_cap"): shrink the THRESH buffers to force the fallback
+    const int64_t v = h->ctx->opt_sq_candidate_cap;
+    if (v >= 0 && (uint64_t)v < cap) cap = cap_limit = (uint32_t)v;
   }
   if (h->ctx->profiling) {
     if (!h->ev_begin) {
@@ -1024,9 +1082,9 @@ void search_device(pxc_sq* h, const float* d_q, uint32_t nq, uint32_t k, uint32_
   // speculative admission rank: about SPEC_MARGIN * F of the whole set are expected at or below the
   // r-th key of a p0-column prefix
   uint32_t r_spec = (uint32_t)std::min<uint64_t>(F, std::max<uint64_t>(1, (SPEC_MARGIN * (uint64_t)F * p0 + nacc - 1) / nacc));
-  if (const char* e = std::getenv("PXC_SQ_SPEC_R")) {  // diagnostic: force the speculative rank
-    const long v = std::strtol(e, nullptr, 10);
-    if (v >= 1 && (uint32_t)v <= F) r_spec = (uint32_t)v;
+  {  // diagnostic (pxc_ctx_set_option "sq_spec_rank"): force the speculative rank
+    const int64_t v = h->ctx->opt_sq_spec_rank;
+    if (v >= 1 && (uint64_t)v <= F) r_spec = (uint32_t)v;
   }
   for (uint32_t qb = 0; qb < nq; qb += QBATCH) {
     const uint32_t nb = std::min(QBATCH, nq - qb);
@@ -1273,6 +1331,62 @@ pxc_status pxc_sq_decode(pxc_ctx* ctx, const float* min, const float* scale, uin
     PXC_CUDA(cudaGetLastError());
     ctx->launches += 1;
     PXC_CUDA(cudaMemcpyAsync(out, x.p, n * dim * 4, cudaMemcpyDeviceToHost, s));
+    PXC_CUDA(cudaStreamSynchronize(s));
+  });
+}
+
+pxc_status pxc_sq_asymmetric_device(pxc_ctx* ctx, const float* min, const float* scale, uint32_t dim, int32_t mode,
+                                    int32_t code_type, int32_t metric, const float* d_queries, uint32_t nq,
+                                    const uint8_t* d_codes, uint64_t n, float* d_out, void* stream, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(ctx != nullptr, "ctx", 0, "null context");
+    sq::check_quantizer_args(dim, mode, code_type);
+    PXC_CONFIG(min && scale, "quantizer", 0, "null range table");
+    PXC_CONFIG(metric == PXC_EUCLIDEAN || metric == PXC_INNER_PRODUCT || metric == PXC_COSINE, "metric", metric,
+               "asymmetric scoring is squared L2 (euclidean) or the negated dot (inner product, cosine)");
+    PXC_CONFIG(nq <= 65535u * sq::ASYM_Q, "nq", nq, "at most 524280 queries per call");
+    if (nq == 0 || n == 0) return;
+    PXC_CONFIG(d_queries && d_codes && d_out, "buffers", 0, "null buffer");
+    DeviceGuard g(ctx->device);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    const uint32_t groups = mode == PXC_RANGE_GLOBAL ? 1 : dim;
+    DBuf<float> t;
+    t.reserve(2 * groups);
+    PXC_CUDA(cudaMemcpyAsync(t.p, min, groups * 4, cudaMemcpyHostToDevice, s));
+    PXC_CUDA(cudaMemcpyAsync(t.p + groups, scale, groups * 4, cudaMemcpyHostToDevice, s));
+    const dim3 grid((unsigned)((n + 127) / 128), (nq + sq::ASYM_Q - 1) / sq::ASYM_Q);
+    sq::asymmetric_kernel<<<grid, 128, 0, s>>>(d_queries, nq, d_codes, n, dim, t.p, t.p + groups,
+                                               mode == PXC_RANGE_GLOBAL, code_type == PXC_CODE_I8,
+                                               metric != PXC_EUCLIDEAN, d_out);
+    PXC_CUDA(cudaGetLastError());
+    ctx->launches += 1;
+    PXC_CUDA(cudaStreamSynchronize(s));  // the range table is freed on return
+  });
+}
+
+pxc_status pxc_sq_asymmetric(pxc_ctx* ctx, const float* min, const float* scale, uint32_t dim, int32_t mode,
+                             int32_t code_type, int32_t metric, const float* queries, uint32_t nq,
+                             const uint8_t* codes, uint64_t n, float* out, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(ctx != nullptr, "ctx", 0, "null context");
+    sq::check_quantizer_args(dim, mode, code_type);
+    if (nq == 0 || n == 0) return;
+    PXC_CONFIG(queries && codes && out, "buffers", 0, "null buffer");
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    DeviceGuard g(ctx->device);
+    cudaStream_t s = ctx->stream;
+    DBuf<float> dq, dout;
+    DBuf<uint8_t> dc;
+    dq.reserve((size_t)nq * dim);
+    dc.reserve(n * dim);
+    dout.reserve((size_t)nq * n);
+    PXC_CUDA(cudaMemcpyAsync(dq.p, queries, (size_t)nq * dim * 4, cudaMemcpyHostToDevice, s));
+    PXC_CUDA(cudaMemcpyAsync(dc.p, codes, n * dim, cudaMemcpyHostToDevice, s));
+    pxc_error e2{};
+    if (pxc_sq_asymmetric_device(ctx, min, scale, dim, mode, code_type, metric, dq.p, nq, dc.p, n, dout.p, s, &e2) !=
+        PXC_OK)
+      throw make_failure((pxc_status)e2.code, e2.a, e2.b, e2.parameter, "%s", e2.detail);
+    PXC_CUDA(cudaMemcpyAsync(out, dout.p, (size_t)nq * n * 4, cudaMemcpyDeviceToHost, s));
     PXC_CUDA(cudaStreamSynchronize(s));
   });
 }

@@ -65,6 +65,10 @@ class Context:
     def set_wait_limit(self, ms: int) -> None:
         N.call("pxc_ctx_set_wait_limit", self.handle, ms)
 
+    def set_option(self, name: str, value: int) -> None:
+        """A diagnostic switch of the native library (tests only; see pxc_ctx_set_option)."""
+        N.call("pxc_ctx_set_option", self.handle, name.encode(), int(value))
+
     def close(self) -> None:
         if getattr(self, "handle", None):
             self._lib.pxc_ctx_destroy(self.handle)
@@ -356,7 +360,7 @@ def recall_at_k(candidate, truth: FlatIndex, queries, k: int, filter=AcceptAll) 
     """recall_at_k[_filtered] (crates/proxima-index/src/recall.rs:108-169), batched on the GPU."""
     dim = truth.space.dim
     q = np.asarray(queries, dtype=np.float32).reshape(-1)
-    if q.size % dim != 0:
+    if dim == 0 or q.size % dim != 0:  # recall.rs:131-137
         raise Configuration("queries", q.size, "must be a multiple of the index dimension")
     if q.size == 0:
         return RecallReport(0, k, 0.0, 0.0, [], 0)
@@ -367,7 +371,10 @@ def recall_at_k(candidate, truth: FlatIndex, queries, k: int, filter=AcceptAll) 
         if len(a) < len(e):
             short += 1
         per_query.append(_overlap([h.id for h in e], a))
-    mean = float(np.float32(np.sum(np.asarray(per_query, dtype=np.float32), dtype=np.float32)) /
-                 np.float32(len(per_query)))
+    # recall.rs:155: Iterator::sum over f32 is a sequential fold, then one division
+    total = np.float32(0.0)
+    for r in per_query:
+        total = np.float32(total + np.float32(r))
+    mean = float(total / np.float32(len(per_query)))
     mn = min(per_query)
     return RecallReport(len(per_query), k, mean, mn, per_query, short)

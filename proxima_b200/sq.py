@@ -119,6 +119,25 @@ class ScalarQuantizer:
                int(self.mode), int(self.code_type), N.ptr(v), v.shape[0], N.ptr(out))
         return out
 
+    def asymmetric(self, queries, codes, metric: Metric = Metric.EUCLIDEAN) -> np.ndarray:
+        """asymmetric_squared_l2 (EUCLIDEAN) or asymmetric_inner_product (INNER_PRODUCT, COSINE on
+        prepared vectors), scalar.rs:298-327, for every (query, code) pair: an (nq, n) float32 array."""
+        q = np.ascontiguousarray(queries, np.float32).reshape(-1, self.dim)
+        c = np.ascontiguousarray(codes, np.uint8).reshape(-1, self.dim)
+        out = np.zeros((q.shape[0], c.shape[0]), np.float32)
+        N.call("pxc_sq_asymmetric", self.ctx.handle, N.ptr(self.min), N.ptr(self.scale), self.dim,
+               int(self.mode), int(self.code_type), int(metric), N.ptr(q), q.shape[0], N.ptr(c), c.shape[0],
+               N.ptr(out))
+        return out
+
+    def asymmetric_squared_l2(self, query, code) -> float:
+        """scalar.rs:298-305 for one query and one code."""
+        return float(self.asymmetric(query, code, Metric.EUCLIDEAN)[0, 0])
+
+    def asymmetric_inner_product(self, query, code) -> float:
+        """scalar.rs:313-319 for one query and one code."""
+        return float(self.asymmetric(query, code, Metric.INNER_PRODUCT)[0, 0])
+
     def decode(self, codes) -> np.ndarray:
         """decode (scalar.rs:270-296): min + level * scale per component."""
         c = np.ascontiguousarray(codes, np.uint8).reshape(-1, self.dim)

@@ -5,13 +5,13 @@ tensor-core screening + exact re-scoring), with k-means++ and injected seeds,
 empty-cluster re-seeding, duplicate centroids (ties, screening overflow),
 the k clamp and the degenerate shapes the reference handles.
 """
-import os
 
 import numpy as np
 import pytest
 
 from oracle import pxo
 from proxima_b200 import fixtures
+from proxima_b200.index import Context
 from proxima_b200.quantize import kmeans
 
 pytestmark = pytest.mark.gpu
@@ -66,11 +66,12 @@ def test_tensor_path_equals_forced_exact_path():
     pts = _blobs(8192, 96, 300, 4)
     init = fixtures.c3_init(pts, 300, seed=3)
     a = kmeans(pts, 96, 300, 5, init=init, want_assignment=True)
-    os.environ["PXC_KMEANS_EXACT"] = "1"
+    ctx = Context.default()
+    ctx.set_option("kmeans_exact", 1)
     try:
         b = kmeans(pts, 96, 300, 5, init=init, want_assignment=True)
     finally:
-        del os.environ["PXC_KMEANS_EXACT"]
+        ctx.set_option("kmeans_exact", 0)
     assert a.path == 1 and b.path == 0
     assert np.array_equal(a.centroids.view(np.uint32), b.centroids.view(np.uint32))
     assert np.array_equal(a.assignment, b.assignment)

@@ -221,8 +221,11 @@ def test_search_forced_fallback_is_identical(monkeypatch):
     idx.set_column(0, years)
     base = idx.search_batch(queries, 10, 100, ranges=[IntRange(0, lo=2003)])
     assert idx.last_fallback() == 0
-    monkeypatch.setenv("PXC_SQ_CAP", "0")
-    forced = idx.search_batch(queries, 10, 100, ranges=[IntRange(0, lo=2003)])
+    idx.ctx.set_option("sq_candidate_cap", 0)
+    try:
+        forced = idx.search_batch(queries, 10, 100, ranges=[IntRange(0, lo=2003)])
+    finally:
+        idx.ctx.set_option("sq_candidate_cap", -1)
     assert 0 < idx.last_fallback() <= len(queries)
     _same(forced, base, "fallback")
 
@@ -239,8 +242,11 @@ def test_search_failed_speculation_is_retried_exactly(monkeypatch):
     sq = idx.train()
     idx.set_column(0, years)
     base = idx.search_batch(queries, 10, 100, ranges=[IntRange(0, lo=2001)])
-    monkeypatch.setenv("PXC_SQ_SPEC_R", "1")
-    forced = idx.search_batch(queries, 10, 100, ranges=[IntRange(0, lo=2001)])
+    idx.ctx.set_option("sq_spec_rank", 1)
+    try:
+        forced = idx.search_batch(queries, 10, 100, ranges=[IntRange(0, lo=2001)])
+    finally:
+        idx.ctx.set_option("sq_spec_rank", -1)
     assert idx.last_retried() > len(queries) // 2
     _same(forced, base, "retried")
     acc = years >= 2001

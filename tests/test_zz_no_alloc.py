@@ -59,3 +59,37 @@ def test_noalloc_search_matches_the_regular_entry_point_on_two_calls():
             _search("pxc_flat_search_noalloc", h, big[:4], 17, torch)
     finally:
         N.load().pxc_flat_destroy(h)
+
+
+@pytest.mark.parametrize("k", [1, 4])
+def test_noalloc_search_at_its_limits_matches_the_oracle(k):
+    """At the entry point's limits — 2,048 queries, dim 256 (two K blocks), a
+    120k-row store, so the split count is clamped to the array's 32 — the ids
+    and distance bits equal the oracle's exact search and the regular entry
+    point's, on two calls in a row."""
+    import torch
+    from oracle import pxo
+    from proxima_b200 import _native as N
+    from proxima_b200 import fixtures
+    from proxima_b200.index import Context
+
+    dim, n, nq = 256, 120_000, 2048
+    db = fixtures.blobs_u8(n, dim, 512, fixtures.C2_CENTRES + 3, fixtures.C2_BASE + 3)
+    ctx = Context.default()
+    h = N.vp()
+    N.call("pxc_flat_create", ctx.handle, dim, 0, C.byref(h))
+    try:
+        N.call("pxc_flat_sync", h, N.ptr(db), None, None, 0, n)
+        assert N.load().pxc_flat_len(h) == n
+        for call in range(2):
+            qh = fixtures.blobs_u8(nq, dim, 512, fixtures.C2_CENTRES + 3, fixtures.C2_QUERIES + 11 + call)
+            q = torch.from_numpy(qh).cuda()
+            got = _search("pxc_flat_search_noalloc", h, q, k, torch)
+            ref = _search("pxc_flat_search_device", h, q, k, torch)
+            ri, rd, rl = pxo.flat_search(db, qh, k, pxo.EUCLIDEAN)
+            assert np.array_equal(got[2], rl) and np.array_equal(ref[2], rl), f"call {call}: lengths"
+            assert np.array_equal(got[0], ri.astype(np.int64)), f"call {call}: ids"
+            assert np.array_equal(got[1].view(np.uint32), rd.view(np.uint32)), f"call {call}: distances"
+            assert np.array_equal(got[0], ref[0]) and np.array_equal(got[1].view(np.uint32), ref[1].view(np.uint32))
+    finally:
+        N.load().pxc_flat_destroy(h)
