@@ -143,14 +143,20 @@ pxc_status pxc_flat_search_device(pxc_flat* h, const float* d_queries, uint32_t 
                                   pxc_error* err);
 /* Which scan kernel the next search will use: 1 = tensor-core u8 (every live
  * row and the queries are integers in [0,255] under euclidean, so the u8
- * product is exact; k <= 128), 0 = fp32 reference-order scan. Diagnostic only. */
+ * product is exact; k <= 128); 2 = tensor-core f16 screen of K2_KT = 32
+ * candidates per query, re-ranked with the exact f32 distance and proven per
+ * query (any other store under euclidean, cosine or inner product with
+ * dim <= 128, for unfiltered searches with k <= 24; unproven queries run on the
+ * fp32 scan); 0 = fp32 reference-order scan. Diagnostic only. */
 int32_t pxc_flat_path(const pxc_flat* h);
 /* Duration of the last search's scan kernel (K1 or K1g), with profiling on;
  * -1 when not recorded. */
 float pxc_flat_last_scan_ms(pxc_flat* h);
-/* Queries of the last search with 32 < k <= 128 on the tensor-core path whose
- * grouped answer could not be proven exact (32 or more of their top k in one
- * row group) and that were searched again on the fp32 scan; 0 otherwise. */
+/* Queries of the last search that a tensor-core path could not prove exact
+ * and that were searched again on the fp32 scan: with 32 < k <= 128 on the u8
+ * path, those with 32 or more of their top k in one row group; on the f16
+ * screen, those whose candidates' k-th exact distance was not provably ahead
+ * of every row the screen left out; 0 otherwise. */
 uint32_t pxc_flat_last_redone(const pxc_flat* h);
 
 /* Allocation-free variant of pxc_flat_search_device. No counterpart in the

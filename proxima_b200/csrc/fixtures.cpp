@@ -129,6 +129,23 @@ void pxf_blobs_u8(uint64_t row_begin, uint64_t n, uint64_t dim, uint64_t nblobs,
   });
 }
 
+// The same blobs without rounding or clipping: real-valued rows (the
+// non-integer counterpart of C2 for the f16 tensor-core screen).
+void pxf_blobs_f32(uint64_t row_begin, uint64_t n, uint64_t dim, uint64_t nblobs,
+                   uint64_t centre_seed, uint64_t noise_seed, double sigma, float* out,
+                   int threads) {
+  parallel_rows(n, threads, [&](uint64_t b, uint64_t e) {
+    for (uint64_t r = b; r < e; ++r) {
+      uint64_t i = row_begin + r;
+      uint64_t blob = i % nblobs;
+      for (uint64_t d = 0; d < dim; ++d) {
+        double c = 255.0 * unit53(stream_at(centre_seed, blob * dim + d));
+        out[r * dim + d] = static_cast<float>(c + sigma * normal4(noise_seed, i * dim + d));
+      }
+    }
+  });
+}
+
 // Unit-sphere blobs: centre = normalize(N(0,1)^dim) from `centre_seed`; row i
 // of blob i % nblobs is normalize(centre + sigma * N(0,1)) from `noise_seed`.
 void pxf_sphere_blobs(uint64_t row_begin, uint64_t n, uint64_t dim, uint64_t nblobs,

@@ -22,8 +22,11 @@
 #include <new>
 #include <vector>
 
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 #include "flat_tc.cuh"
+#include "refdist.cuh"
 #include "fp32scan.cuh"
 #include "select.cuh"
 #include "tmap.cuh"
@@ -308,6 +311,280 @@ __global__ void scatter_results_kernel(const uint64_t* __restrict__ ids, const f
   if (threadIdx.x == 0) out_len[q] = n;
 }
 
+// ---------------------------------------------------------------------------
+// K2: the tensor-core path for non-integer data (euclidean, cosine, inner
+// product). A screen on kind::f16 tensor cores (flat_tc.cuh, F16Scan) keeps
+// each query's K2_KT best rows by an approximate score d~; the candidates are
+// re-scored with the reference's exact f32 distance (8-lane order) and sorted
+// by (total_cmp, id); a query's answer is proven exact when every row the
+// screen did not keep is provably behind the k-th exact distance:
+//   d_ref(x) >= d~(x) - E_s - E_ref >= d~_KT - E_s - E_ref > d_k,
+// with E_s a rigorous bound on |d~ - d| (the f16 rounding of both operands,
+// the tensor core's f32 accumulation, the centring and the f32 epilogue) and
+// E_ref the reference's own rounding. Queries that cannot be proven are
+// searched again on K1g. The screen works on rows and queries centred on the
+// rows' mean (which shrinks the operands, and with them the bound) and
+// scaled by powers of two so that the f16 values use the full range.
+// ---------------------------------------------------------------------------
+constexpr uint32_t K2_KT = 32;         // candidates the screen keeps per query
+constexpr uint32_t K2_MAX_K = 24;      // largest k served (the rest of the list is the proof's margin)
+constexpr uint32_t K2_MAX_DIM = 128;   // two 128-byte K blocks of f16
+constexpr uint32_t K2_MEAN_CHUNKS = 64;
+
+// Partial column sums (f64) of the rank-ordered rows: block (32 columns x 8
+// row lanes) per (column group, row chunk); column_mean_kernel folds the
+// chunks in order, so the mean does not depend on scheduling.
+__global__ void column_partial_kernel(const float* __restrict__ rows, uint64_t n, uint32_t dim,
+                                      double* __restrict__ part) {
+  const uint32_t col = blockIdx.x * 32 + threadIdx.x;
+  const uint64_t per = (n + gridDim.y - 1) / gridDim.y;
+  const uint64_t r0 = (uint64_t)blockIdx.y * per, r1 = min(n, r0 + per);
+  double acc = 0.0;
+  if (col < dim)
+    for (uint64_t r = r0 + threadIdx.y; r < r1; r += 8) acc += (double)rows[r * dim + col];
+  __shared__ double red[8][33];
+  red[threadIdx.y][threadIdx.x] = acc;
+  __syncthreads();
+  if (threadIdx.y == 0 && col < dim) {
+    double t = 0.0;
+    for (int i = 0; i < 8; ++i) t += red[i][threadIdx.x];
+    part[(size_t)blockIdx.y * dim + col] = t;
+  }
+}
+__global__ void column_mean_kernel(const double* __restrict__ part, uint32_t chunks, uint32_t dim, uint64_t n,
+                                   float* __restrict__ mu) {
+  const uint32_t col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= dim) return;
+  double t = 0.0;
+  for (uint32_t c = 0; c < chunks; ++c) t += part[(size_t)c * dim + col];
+  mu[col] = (float)(t / (double)n);
+}
+
+// Ranges the screen's scale and bound need, over the centred rows:
+// [0] max |x'_i|, [1] max ||x'||, [2] max ||x|| (uncentred), [3] max |h_x|,
+// each as the bits of a non-negative float rounded up (atomicMax on bits).
+__device__ __forceinline__ float round_up_f32(double v) {
+  float f = (float)v;
+  return ((double)f < v) ? nextafterf(f, INFINITY) : f;
+}
+__global__ void k2_row_stats_kernel(const float* __restrict__ rows, uint64_t n, uint32_t dim,
+                                    const float* __restrict__ mu, int metric, float* __restrict__ h_out,
+                                    uint32_t* __restrict__ stats) {
+  const uint64_t r = blockIdx.x;
+  double c2 = 0.0, u2 = 0.0, mx = 0.0;
+  float amax = 0.0f;
+  for (uint32_t d = threadIdx.x; d < dim; d += blockDim.x) {
+    const float x = rows[r * dim + d];
+    const float xc = __fsub_rn(x, mu[d]);
+    c2 += (double)xc * xc;
+    u2 += (double)x * x;
+    mx += (double)mu[d] * xc;
+    amax = fmaxf(amax, fabsf(xc));
+  }
+  using Red = cub::BlockReduce<double, 128>;
+  __shared__ typename Red::TempStorage t1, t2, t3;
+  __shared__ float s_amax;
+  if (threadIdx.x == 0) s_amax = 0.0f;
+  __syncthreads();
+  atomicMax(reinterpret_cast<unsigned*>(&s_amax), __float_as_uint(amax));
+  const double C2 = Red(t1).Sum(c2);
+  const double U2 = Red(t2).Sum(u2);
+  const double MX = Red(t3).Sum(mx);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const double h = metric == PXC_EUCLIDEAN ? C2 : -MX;
+    h_out[r] = (float)h;
+    atomicMax(stats + 0, __float_as_uint(s_amax));
+    atomicMax(stats + 1, __float_as_uint(round_up_f32(sqrt(C2))));
+    atomicMax(stats + 2, __float_as_uint(round_up_f32(sqrt(U2))));
+    atomicMax(stats + 3, __float_as_uint(round_up_f32(fabs(h))));
+  }
+}
+
+// f16 operand: row r = fl16((x_r - mu) * 2^ax) (rank order; zero padding),
+// padding rows' term = F16Scan::big().
+__global__ void k2_operand_kernel(const float* __restrict__ rows, uint64_t n, uint32_t dim, uint32_t dp,
+                                  const float* __restrict__ mu, int ax, __half* __restrict__ op,
+                                  float* __restrict__ h) {
+  const uint64_t r = blockIdx.x;
+  for (uint32_t d = threadIdx.x; d < dp; d += blockDim.x) {
+    float v = 0.0f;
+    if (r < n && d < dim) v = ldexpf(__fsub_rn(rows[r * dim + d], mu[d]), ax);
+    op[r * dp + d] = __float2half_rn(v);
+  }
+  if (threadIdx.x == 0 && r >= n) h[r] = flat_tc::F16Scan::big();
+}
+
+// Per query: the f16 operand row, the factor c_q, the constant that turns
+// the screen's r into d~, and the two error terms of the proof.
+struct K2Query {
+  float coef;      // c_q
+  float cst;       // d~ = r + cst
+  double eps;      // E_s: |d~ - d_real| <= eps for every row
+  double eref;     // cosine / IP: |d_ref - d_real| <= eref; euclidean: relative factor gamma
+};
+__global__ void k2_prep_queries_kernel(const float* __restrict__ Q, uint32_t nq, uint32_t dim, uint32_t dp,
+                                       const float* __restrict__ mu, int metric, int ax, const float* __restrict__ xst,
+                                       __half* __restrict__ qop, K2Query* __restrict__ meta) {
+  const uint32_t q = blockIdx.x;
+  double c2 = 0.0, u2 = 0.0, qm = 0.0;
+  float amax = 0.0f;
+  if (q < nq) {
+    for (uint32_t d = threadIdx.x; d < dim; d += blockDim.x) {
+      const float x = Q[(size_t)q * dim + d];
+      const float xc = __fsub_rn(x, mu[d]);
+      c2 += (double)xc * xc;
+      u2 += (double)x * x;
+      qm += (double)x * mu[d];
+      amax = fmaxf(amax, fabsf(xc));
+    }
+  }
+  using Red = cub::BlockReduce<double, 128>;
+  __shared__ typename Red::TempStorage t1, t2, t3;
+  __shared__ float s_amax;
+  __shared__ int s_aq;
+  if (threadIdx.x == 0) s_amax = 0.0f;
+  __syncthreads();
+  atomicMax(reinterpret_cast<unsigned*>(&s_amax), __float_as_uint(amax));
+  const double C2 = Red(t1).Sum(c2);
+  const double U2 = Red(t2).Sum(u2);
+  const double QM = Red(t3).Sum(qm);
+  __syncthreads();
+  if (threadIdx.x == 0) s_aq = s_amax > 0.0f ? 14 - ilogbf(s_amax) : 0;
+  __syncthreads();
+  const int aq = s_aq;
+  for (uint32_t d = threadIdx.x; d < dp; d += blockDim.x) {
+    float v = 0.0f;
+    if (q < nq && d < dim) v = ldexpf(__fsub_rn(Q[(size_t)q * dim + d], mu[d]), aq);
+    qop[(size_t)q * dp + d] = __float2half_rn(v);
+  }
+  if (threadIdx.x != 0) return;
+  K2Query m;
+  const double k = metric == PXC_EUCLIDEAN ? 2.0 : 1.0;
+  m.coef = (float)(-k * ldexp(1.0, -(aq + ax)));
+  m.cst = (float)(metric == PXC_EUCLIDEAN ? C2 : (metric == PXC_COSINE ? 1.0 - QM : -QM));
+  const double Qn = sqrt(C2) * (1.0 + 1e-12), Qu = sqrt(U2) * (1.0 + 1e-12);
+  const double M = xst[1], Mu = xst[2], Hmax = xst[3];
+  const double D = (double)dim, u = ldexp(1.0, -11);
+  const double A = ldexp(Qn, aq), B = ldexp(M, ax), sub = ldexp(1.0, -25) * sqrt(D);
+  const double e_f16 = (2.0 * u + u * u) * A * B + ldexp(1.0, -25) * (1.0 + u) * sqrt(D) * (A + B) +
+                       D * ldexp(1.0, -50);
+  const double e_acc = D * ldexp(1.0, -23) * (A * (1.0 + u) + sub) * (B * (1.0 + u) + sub);
+  const double scale = k * ldexp(1.0, -(aq + ax));
+  const double e_dot = (e_f16 + e_acc) * scale;
+  const double qmn = k * Qn * M * 1.01;
+  const double e_center = metric == PXC_EUCLIDEAN ? ldexp(1.0, -23) * (Qn + M) * (Qn + M) * 1.01
+                                                  : ldexp(1.0, -24) * M * (Qu + Qn) * 1.01;
+  const double e_round = ldexp(1.0, -22) * (Hmax + qmn + fabs((double)m.cst) + 1.0);
+  m.eps = 1.02 * (e_dot + e_center + e_round) + 1e-30;
+  const double gamma = (D / 8.0 + 8.0) * ldexp(1.0, -24) * 1.1;
+  m.eref = metric == PXC_EUCLIDEAN ? gamma : gamma * Qu * Mu + ldexp(1.0, -24) * (1.0 + Qu * Mu);
+  // a query whose factors leave the f32 range cannot be screened; it is proven never
+  if (!(isfinite(m.coef) && isfinite(m.cst) && isfinite(m.eps)) || q >= nq) m.eps = INFINITY;
+  meta[q] = m;
+}
+
+__global__ void copy_coef_kernel(const K2Query* __restrict__ meta, uint32_t n, float* __restrict__ coef) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) coef[i] = meta[i].coef;
+}
+
+// space.distance on prepared operands (crates/proxima-core/src/space.rs:148-156).
+__device__ __forceinline__ float k2_ref_distance(int metric, const float* q, const float* __restrict__ x,
+                                                 uint32_t dim) {
+  if (metric == PXC_EUCLIDEAN) return l2_unrolled(q, x, dim);
+  const float s = dot_unrolled(q, x, dim);
+  return metric == PXC_COSINE ? __fsub_rn(1.0f, s) : -s;
+}
+
+// Per query: the union of the screen's split lists (sorted, duplicates
+// dropped), its first K2_KT entries re-scored exactly and sorted by
+// (total_cmp, id), the first k written out, and the proof. 128 threads.
+__global__ void __launch_bounds__(128) k2_rerank_kernel(const uint64_t* __restrict__ part, uint32_t nsplit, uint32_t cap,
+                                                        const K2Query* __restrict__ meta, const float* __restrict__ Q,
+                                                        uint32_t dim, int metric, const float* __restrict__ rank_rows,
+                                                        const uint64_t* __restrict__ rank_id, uint32_t nrank, uint32_t k,
+                                                        uint64_t* __restrict__ out_ids, float* __restrict__ out_dist,
+                                                        uint32_t* __restrict__ out_len, uint8_t* __restrict__ redo) {
+  extern __shared__ uint64_t sl[];  // [cap]
+  __shared__ uint32_t flag[2048];
+  __shared__ uint64_t cand[K2_KT];
+  __shared__ uint32_t ncand;
+  const uint32_t q = blockIdx.x;
+  const uint32_t n = nsplit * K2_KT;
+  const uint32_t empty = flat_tc::F16Scan::pack(flat_tc::F16Scan::big());
+  for (uint32_t i = threadIdx.x; i < cap; i += blockDim.x) {
+    const uint64_t v = i < n ? part[(size_t)q * n + i] : ~0ull;
+    sl[i] = (static_cast<uint32_t>(v >> 32) >= empty || static_cast<uint32_t>(v) >= nrank) ? ~0ull : v;
+  }
+  __syncthreads();
+  block_bitonic_sort_u64(sl, cap);
+  for (uint32_t i = threadIdx.x; i < cap; i += blockDim.x)
+    flag[i] = (sl[i] != ~0ull && (i == 0 || sl[i] != sl[i - 1])) ? 1u : 0u;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t c = 0;
+    for (uint32_t i = 0; i < cap && c < K2_KT + 1; ++i) {
+      if (!flag[i]) continue;
+      if (c < K2_KT) cand[c] = sl[i];
+      ++c;
+    }
+    ncand = c;  // K2_KT + 1 means: more rows were seen than the list keeps
+  }
+  __syncthreads();
+  const uint32_t nc = min(ncand, K2_KT);
+  // exact distances of the candidates (one thread each), keyed by (distance, rank)
+  __shared__ uint64_t ex[K2_KT];
+  const float* qrow = Q + (size_t)q * dim;
+  if (threadIdx.x < K2_KT) {
+    uint64_t key = ~0ull;
+    if (threadIdx.x < nc) {
+      const uint32_t rank = static_cast<uint32_t>(cand[threadIdx.x]);
+      const float d = k2_ref_distance(metric, qrow, rank_rows + (size_t)rank * dim, dim);
+      key = (static_cast<uint64_t>(order_key(d)) << 32) | rank;
+    }
+    ex[threadIdx.x] = key;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {  // warp bitonic sort of the 32 keys
+    uint64_t v = ex[threadIdx.x];
+    for (uint32_t size = 2; size <= 32; size <<= 1)
+      for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+        const uint64_t o = __shfl_xor_sync(0xFFFFFFFFu, v, stride);
+        const bool up = (threadIdx.x & size) == 0;
+        const bool lower = (threadIdx.x & stride) == 0;
+        v = (lower == up) ? (v < o ? v : o) : (v < o ? o : v);
+      }
+    ex[threadIdx.x] = v;
+  }
+  __syncthreads();
+  const uint32_t take = min(nc, k);
+  for (uint32_t i = threadIdx.x; i < take; i += blockDim.x) {
+    const uint64_t v = ex[i];
+    out_ids[(size_t)q * k + i] = rank_id[static_cast<uint32_t>(v)];
+    out_dist[(size_t)q * k + i] = key_to_float(static_cast<uint32_t>(v >> 32));
+  }
+  if (threadIdx.x == 0) {
+    out_len[q] = take;
+    uint8_t bad = 0;
+    if (nrank > K2_KT) {
+      // Every row outside the first K2_KT of the union has d~ at or behind the
+      // K2_KT-th entry: it was behind it in the union, or a full split list or
+      // the shared bound (a full list's last entry) turned it away.
+      const K2Query m = meta[q];
+      const double T = (double)flat_tc::F16Scan::unpack(static_cast<uint32_t>(cand[K2_KT - 1] >> 32)) + (double)m.cst;
+      double lower = T - m.eps;
+      if (metric == PXC_EUCLIDEAN)
+        lower = lower > 0.0 ? lower * (1.0 - m.eref) : lower * (1.0 + m.eref);
+      else
+        lower -= m.eref;
+      const double dk = take ? (double)key_to_float(static_cast<uint32_t>(ex[take - 1] >> 32)) : INFINITY;
+      bad = (ncand < K2_KT || take < k || !(lower > dk)) ? 1 : 0;
+    }
+    redo[q] = bad;
+  }
+}
+
 }  // namespace pxc
 
 using namespace pxc;
@@ -371,6 +648,17 @@ struct pxc_flat {
   // reads back only the failures of its own kernels.
   uint32_t* d_status = nullptr;
   uint32_t* h_status = nullptr;
+  // K2 operand (built on the first non-integer search after the mirror changed)
+  int k2_state = 0;  // 0: not built, 1: built, 2: not applicable to this store
+  uint32_t k2_dp = 0;           // f16 elements per operand row (dim rounded up to 64)
+  uint64_t k2_nrank_pad = 0;
+  int k2_ax = 0;                // rows are scaled by 2^k2_ax
+  DBuf<__half> k2_op, k2_q;
+  DBuf<float> k2_h, k2_mu, k2_coef;
+  DBuf<double> k2_part;
+  DBuf<uint32_t> k2_stats;      // max |x'_i|, max ||x'||, max ||x||, max |h_x| (float bits)
+  DBuf<K2Query> k2_meta;
+  CUtensorMap k2_tmap_x;
   uint32_t last_redo = 0;  // queries of the last grouped search redone on K1g
   cudaEvent_t ev_done = nullptr;  // end of the last search's work (handoff of the scratch)
   std::mutex mu;
@@ -429,6 +717,7 @@ void rebuild_mirror(pxc_flat* h, cudaStream_t s) {
   const uint64_t n = h->nslots;
   h->nrank = 0;
   h->all_u8 = false;
+  h->k2_state = 0;
   if (n == 0) {
     h->dirty = false;
     return;
@@ -514,11 +803,12 @@ uint32_t choose_splits(uint32_t nqt, uint32_t ntiles, int sms, uint32_t KT) {
   return best_s;
 }
 
-template <int KT>
+template <int KT, class P = flat_tc::U8Scan>
 void launch_tc(const CUtensorMap& tq, const CUtensorMap& tx, const flat_tc::Params& p, dim3 grid,
                size_t smem, cudaStream_t s) {
-  PXC_CUDA(cudaFuncSetAttribute(flat_tc::flat_u8_kernel<KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  flat_tc::flat_u8_kernel<KT><<<grid, flat_tc::NUM_THREADS, smem, s>>>(tq, tx, p);
+  PXC_CUDA(cudaFuncSetAttribute(flat_tc::flat_scan_kernel<KT, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)smem));
+  flat_tc::flat_scan_kernel<KT, P><<<grid, flat_tc::NUM_THREADS, smem, s>>>(tq, tx, p);
 }
 
 // The database side of one K1 search: the full mirror, or the accepted ranks of a filter.
@@ -549,7 +839,8 @@ void search_tc(pxc_flat* h, const TcOperand& op, const float* d_q, uint32_t nq, 
   PXC_CUDA(cudaMemsetAsync(h->done.p + nqt, 0xFF, (size_t)nqt * nsplit * sizeof(uint32_t), s));
   flat_tc::Params p;
   p.norms = op.norms;
-  p.bound = h->bound.p;
+  p.qcoef = nullptr;
+  p.bound = reinterpret_cast<uint32_t*>(h->bound.p);
   p.done_count = h->done.p;
   p.done_list = h->done.p + nqt;
   p.out_part = h->part.p;
@@ -560,11 +851,11 @@ void search_tc(pxc_flat* h, const TcOperand& op, const float* d_q, uint32_t nq, 
   p.ntiles = ntiles;
   p.tiles_per_split = tps;
   p.nsplit = nsplit;
-  p.stages = flat_tc::pick_stages(p.kblocks);
+  p.stages = flat_tc::pick_stages<flat_tc::U8Scan>(p.kblocks);
   p.wait_ns = (uint64_t)h->ctx->wait_ms * 1000000ull;
   CUtensorMap tmap_q;
   make_tmap_u8_2d(&tmap_q, h->q_u8.p, h->dp, nq_pad, flat_tc::KB_BYTES, flat_tc::BM);
-  size_t smem = flat_tc::smem_bytes(p.kblocks, p.stages);
+  size_t smem = flat_tc::smem_bytes<flat_tc::U8Scan>(p.kblocks, p.stages);
   dim3 grid(nqt, nsplit);
   ScanTimer timer(h, s, timed);
   switch (KT) {
@@ -732,6 +1023,148 @@ void search_tc_grouped(pxc_flat* h, const TcOperand& op, const float* d_q, uint3
   h->ctx->launches += 2;
 }
 
+// The K2 operand of the current mirror: centre, ranges, scale, f16 rows and
+// row terms. Leaves k2_state = 2 when the store does not suit the screen
+// (dim > 128, manhattan, or magnitudes whose squares leave the f32 range).
+void build_k2(pxc_flat* h, cudaStream_t s) {
+  h->k2_state = 2;
+  const uint64_t n = h->nrank;
+  const uint32_t dim = h->dim;
+  if (n == 0 || dim > K2_MAX_DIM || h->metric == PXC_MANHATTAN) return;
+  h->k2_mu.reserve(dim);
+  h->k2_part.reserve((size_t)K2_MEAN_CHUNKS * dim);
+  column_partial_kernel<<<dim3((dim + 31) / 32, K2_MEAN_CHUNKS), dim3(32, 8), 0, s>>>(h->rank_rows.p, n, dim,
+                                                                                      h->k2_part.p);
+  column_mean_kernel<<<(dim + 127) / 128, 128, 0, s>>>(h->k2_part.p, K2_MEAN_CHUNKS, dim, n, h->k2_mu.p);
+  h->k2_dp = (dim + 63) / 64 * 64;
+  h->k2_nrank_pad = (n + flat_tc::BN - 1) / flat_tc::BN * flat_tc::BN;
+  h->k2_h.reserve(h->k2_nrank_pad);
+  h->k2_stats.reserve(4);
+  PXC_CUDA(cudaMemsetAsync(h->k2_stats.p, 0, 4 * sizeof(uint32_t), s));
+  k2_row_stats_kernel<<<(unsigned)n, 128, 0, s>>>(h->rank_rows.p, n, dim, h->k2_mu.p, h->metric, h->k2_h.p,
+                                                 h->k2_stats.p);
+  PXC_CUDA(cudaGetLastError());
+  uint32_t st[4];
+  PXC_CUDA(cudaMemcpyAsync(st, h->k2_stats.p, sizeof(st), cudaMemcpyDeviceToHost, s));
+  PXC_CUDA(cudaStreamSynchronize(s));
+  h->ctx->launches += 3;
+  float f[4];
+  std::memcpy(f, st, sizeof(f));
+  for (float v : f)
+    if (!std::isfinite(v) || v > 1e30f) return;
+  if ((double)f[1] * f[1] > 1e36 || (double)f[2] * f[2] > 1e36) return;
+  h->k2_ax = f[0] > 0.0f ? 14 - std::ilogb(f[0]) : 0;
+  h->k2_op.reserve(h->k2_nrank_pad * h->k2_dp);
+  k2_operand_kernel<<<(unsigned)h->k2_nrank_pad, 128, 0, s>>>(h->rank_rows.p, n, dim, h->k2_dp, h->k2_mu.p,
+                                                             h->k2_ax, h->k2_op.p, h->k2_h.p);
+  PXC_CUDA(cudaGetLastError());
+  h->ctx->launches += 1;
+  make_tmap_u8_2d(&h->k2_tmap_x, h->k2_op.p, (uint64_t)h->k2_dp * 2, h->k2_nrank_pad, flat_tc::KB_BYTES,
+                  flat_tc::BN);
+  PXC_CUDA(cudaStreamSynchronize(s));
+  h->k2_state = 1;
+}
+
+// Searches K2 serves: no filter (the screen's operand is the whole mirror),
+// k small enough for the over-fetch to carry a proof, a metric with a
+// product form, and a store that fits the f16 operand.
+bool k2_applicable(const pxc_flat* h, uint32_t k, const uint64_t* d_bitmap) {
+  return d_bitmap == nullptr && k >= 1 && k <= K2_MAX_K && h->metric != PXC_MANHATTAN && h->dim <= K2_MAX_DIM &&
+         h->nrank > 0;
+}
+
+// Queries flagged in h->g_redo (their screen could not prove them) are
+// searched again on K1g and their rows replaced. Synchronises the stream.
+void redo_flagged(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, const uint64_t* d_bitmap, uint64_t* d_ids,
+                  float* d_dist, uint32_t* d_len, cudaStream_t s) {
+  size_t tb = 0;
+  thrust::counting_iterator<uint32_t> it(0);
+  PXC_CUDA(cub::DeviceSelect::Flagged(nullptr, tb, it, h->g_redo.p, h->g_redo_idx.p, h->g_redo_len.p, (int64_t)nq, s));
+  h->tmp.reserve(std::max<size_t>(tb, 1));
+  PXC_CUDA(cub::DeviceSelect::Flagged(h->tmp.p, tb, it, h->g_redo.p, h->g_redo_idx.p, h->g_redo_len.p, (int64_t)nq, s));
+  PXC_CUDA(cudaMemcpyAsync(h->h_flag, h->g_redo_len.p, sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
+  PXC_CUDA(cudaStreamSynchronize(s));
+  const uint32_t nredo = static_cast<uint32_t>(*h->h_flag);
+  h->last_redo = nredo;
+  h->ctx->launches += 2;
+  if (nredo == 0) return;
+  h->g_redo_q.reserve((size_t)nredo * h->dim);
+  h->g_redo_ids.reserve((size_t)nredo * k);
+  h->g_redo_dist.reserve((size_t)nredo * k);
+  h->g_redo_len.reserve(nredo);
+  gather_queries_kernel<<<nredo, 128, 0, s>>>(d_q, h->g_redo_idx.p, h->dim, h->g_redo_q.p);
+  PXC_CUDA(cudaGetLastError());
+  search_generic(h, h->g_redo_q.p, nredo, k, d_bitmap, h->g_redo_ids.p, h->g_redo_dist.p, h->g_redo_len.p, s);
+  scatter_results_kernel<<<nredo, 128, 0, s>>>(h->g_redo_ids.p, h->g_redo_dist.p, h->g_redo_len.p,
+                                               h->g_redo_idx.p, k, d_ids, d_dist, d_len);
+  PXC_CUDA(cudaGetLastError());
+  h->ctx->launches += 2;
+}
+
+// K2: the f16 screen (flat_scan_kernel<K2_KT, F16Scan>), the exact re-rank
+// with its per-query proof, and K1g for the queries left unproven.
+void search_k2(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, uint64_t* d_ids, float* d_dist,
+               uint32_t* d_len, cudaStream_t s) {
+  const uint32_t nq_pad = (nq + flat_tc::BM - 1) / flat_tc::BM * flat_tc::BM;
+  const uint32_t nqt = nq_pad / flat_tc::BM;
+  const uint32_t dp = h->k2_dp;
+  h->k2_q.reserve((size_t)nq_pad * dp);
+  h->k2_meta.reserve(nq_pad);
+  h->k2_coef.reserve(nq_pad);
+  k2_prep_queries_kernel<<<nq_pad, 128, 0, s>>>(d_q, nq, h->dim, dp, h->k2_mu.p, h->metric, h->k2_ax,
+                                                reinterpret_cast<const float*>(h->k2_stats.p), h->k2_q.p,
+                                                h->k2_meta.p);
+  PXC_CUDA(cudaGetLastError());
+  copy_coef_kernel<<<grid1d(nq_pad, 256), 256, 0, s>>>(h->k2_meta.p, nq_pad, h->k2_coef.p);
+  const uint32_t ntiles = (uint32_t)(h->k2_nrank_pad / flat_tc::BN);
+  const uint32_t nsplit_req = choose_splits(nqt, ntiles, h->ctx->sm_count, K2_KT);
+  const uint32_t tps = (ntiles + nsplit_req - 1) / nsplit_req;
+  const uint32_t nsplit = (ntiles + tps - 1) / tps;
+  h->part.reserve((size_t)nq_pad * nsplit * K2_KT);
+  h->bound.reserve(nq_pad);
+  h->done.reserve(nqt + (size_t)nqt * nsplit);
+  PXC_CUDA(cudaMemsetAsync(h->bound.p, 0xFF, nq_pad * sizeof(uint32_t), s));  // reads as "no bound yet"
+  PXC_CUDA(cudaMemsetAsync(h->done.p, 0, nqt * sizeof(uint32_t), s));
+  PXC_CUDA(cudaMemsetAsync(h->done.p + nqt, 0xFF, (size_t)nqt * nsplit * sizeof(uint32_t), s));
+  flat_tc::Params p;
+  p.norms = h->k2_h.p;
+  p.qcoef = h->k2_coef.p;
+  p.bound = reinterpret_cast<uint32_t*>(h->bound.p);
+  p.done_count = h->done.p;
+  p.done_list = h->done.p + nqt;
+  p.out_part = h->part.p;
+  p.status = h->d_status;
+  p.nq = nq;
+  p.k = K2_KT;  // rows behind a full list's last entry cannot enter the union's first K2_KT
+  p.kblocks = dp * 2 / flat_tc::KB_BYTES;
+  p.ntiles = ntiles;
+  p.tiles_per_split = tps;
+  p.nsplit = nsplit;
+  p.stages = flat_tc::pick_stages<flat_tc::F16Scan>(p.kblocks);
+  p.wait_ns = (uint64_t)h->ctx->wait_ms * 1000000ull;
+  CUtensorMap tmap_q;
+  make_tmap_u8_2d(&tmap_q, h->k2_q.p, (uint64_t)dp * 2, nq_pad, flat_tc::KB_BYTES, flat_tc::BM);
+  const size_t smem = flat_tc::smem_bytes<flat_tc::F16Scan>(p.kblocks, p.stages);
+  {
+    ScanTimer timer(h, s);
+    launch_tc<K2_KT, flat_tc::F16Scan>(tmap_q, h->k2_tmap_x, p, dim3(nqt, nsplit), smem, s);
+    PXC_CUDA(cudaGetLastError());
+    timer.stop();
+  }
+  uint32_t cap = 32;
+  while (cap < nsplit * K2_KT) cap <<= 1;
+  h->g_redo.reserve(nq);
+  h->g_redo_idx.reserve(nq);
+  h->g_redo_len.reserve(1);
+  k2_rerank_kernel<<<nq, 128, cap * sizeof(uint64_t), s>>>(h->part.p, nsplit, cap, h->k2_meta.p, d_q, h->dim,
+                                                           h->metric, h->rank_rows.p, h->rank_id.p,
+                                                           (uint32_t)h->nrank, k, d_ids, d_dist, d_len, h->g_redo.p);
+  PXC_CUDA(cudaGetLastError());
+  h->ctx->launches += 4;
+  check_status_word(h->d_status, h->h_status, s, "flat search (tensor-core screen)");
+  redo_flagged(h, d_q, nq, k, nullptr, d_ids, d_dist, d_len, s);
+}
+
 void search_device(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, const uint64_t* d_bitmap,
                    uint64_t* d_ids, float* d_dist, uint32_t* d_len, cudaStream_t s) {
   PXC_CONFIG(k <= PXC_MAX_K, "k", k, "exceeds the 16777216 result ceiling");
@@ -795,9 +1228,16 @@ void search_device(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, const
     else
       search_tc_grouped(h, op, d_q, nq, k, d_bitmap, d_ids, d_dist, d_len, s);
     check_status_word(h->d_status, h->h_status, s, "flat search (tensor-core scan)");
-  } else {
-    search_generic(h, d_q, nq, k, d_bitmap, d_ids, d_dist, d_len, s);
+    return;
   }
+  if (k2_applicable(h, k, d_bitmap)) {
+    if (h->k2_state == 0) build_k2(h, s);
+    if (h->k2_state == 1) {
+      search_k2(h, d_q, nq, k, d_ids, d_dist, d_len, s);
+      return;
+    }
+  }
+  search_generic(h, d_q, nq, k, d_bitmap, d_ids, d_dist, d_len, s);
 }
 
 }  // namespace
@@ -943,7 +1383,20 @@ int32_t pxc_flat_path(const pxc_flat* h) {
       return -1;
     }
   }
-  return (m->all_u8 && m->metric == PXC_EUCLIDEAN && m->dim <= (uint32_t)flat_tc::MAX_KBLOCKS * flat_tc::KB_BYTES && m->nrank > 0) ? 1 : 0;
+  if (m->all_u8 && m->metric == PXC_EUCLIDEAN && m->dim <= (uint32_t)flat_tc::MAX_KBLOCKS * flat_tc::KB_BYTES &&
+      m->nrank > 0)
+    return 1;
+  if (!k2_applicable(m, 1, nullptr)) return 0;
+  if (m->k2_state == 0) {
+    try {
+      DeviceGuard g(m->ctx->device);
+      handoff_drain(m);
+      build_k2(m, m->ctx->stream);
+    } catch (...) {
+      return -1;
+    }
+  }
+  return m->k2_state == 1 ? 2 : 0;
 }
 
 pxc_status pxc_flat_search_device(pxc_flat* h, const float* d_queries, uint32_t nq, uint32_t k,
@@ -1119,7 +1572,8 @@ extern "C" pxc_status pxc_flat_search_noalloc(pxc_flat* h, const float* d_querie
     PXC_CUDA(cudaMemsetAsync(done + nqt, 0xFF, (size_t)nqt * nsplit * sizeof(uint32_t), s));
     flat_tc::Params p;
     p.norms = h->op_norm.p;
-    p.bound = bound;
+    p.qcoef = nullptr;
+    p.bound = reinterpret_cast<uint32_t*>(bound);
     p.done_count = done;
     p.done_list = done + nqt;
     p.out_part = part;
@@ -1130,11 +1584,11 @@ extern "C" pxc_status pxc_flat_search_noalloc(pxc_flat* h, const float* d_querie
     p.ntiles = ntiles;
     p.tiles_per_split = tps;
     p.nsplit = nsplit;
-    p.stages = flat_tc::pick_stages(p.kblocks);
+    p.stages = flat_tc::pick_stages<flat_tc::U8Scan>(p.kblocks);
     p.wait_ns = (uint64_t)h->ctx->wait_ms * 1000000ull;
     CUtensorMap tmap_q;
     make_tmap_u8_2d(&tmap_q, q_u8, h->dp, nq_pad, flat_tc::KB_BYTES, flat_tc::BM);
-    const size_t smem = flat_tc::smem_bytes(p.kblocks, p.stages);
+    const size_t smem = flat_tc::smem_bytes<flat_tc::U8Scan>(p.kblocks, p.stages);
     const dim3 grid(nqt, nsplit);
     switch (KT) {
       case 1: launch_tc<1>(tmap_q, h->tmap_x, p, grid, smem, s); break;

@@ -42,6 +42,15 @@
 // records DEV_TIMEOUT_* in the status word, drains its own copies and MMAs,
 // frees TMEM and returns. There is no barrier among the epilogue warps, so a
 // warp that gives up cannot strand another.
+//
+// The same kernel, instantiated with the F16Scan policy, is K2: the screen of
+// the tensor-core path for non-integer data and every metric. There the
+// operands are f16 copies of the centred rows and queries, each scaled by a
+// power of two (exact), the MMA is kind::f16 with f32 accumulation, and the
+// epilogue ranks on r = h_x + c_q * (q^ . x^) in f32 (h_x a per-row term, c_q a
+// per-query factor that undoes the scales). The lists it returns are screened
+// candidates, not answers: the caller re-ranks them exactly and proves each
+// query's answer with an error bound on the screen (flat.cu).
 #pragma once
 #include "common.cuh"
 #include "sm100.cuh"
@@ -58,26 +67,77 @@ constexpr int A_BLOCK = BM * KB_BYTES;  // 32 KiB per K block
 constexpr int B_BLOCK = BN * KB_BYTES;  // 32 KiB per stage
 constexpr int NUM_EPI_WARPS = 8;
 constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;  // 320
-constexpr int MAX_KBLOCKS = 2;                        // dim <= 256
+constexpr int MAX_KBLOCKS = 2;                        // 256 bytes of K: dim <= 256 (u8), <= 128 (f16)
 constexpr int32_t BIG = 0x3FFFFFFF;                   // sentinel: padding columns, empty slots
 constexpr uint32_t R_OFFSET = 0x02000000u;            // makes r non-negative for packing
 constexpr size_t SMEM_LIMIT = 227 * 1024;
-// per-warp: two tiles of ||x||^2, and a 32 x 32 scratch for the slow path
-constexpr int FIFO_SLOTS = 32;  // deferred-insertion FIFO entries per thread
-constexpr size_t NORM_BYTES =
-    (size_t)NUM_EPI_WARPS * (2 * BN * sizeof(int32_t) + FIFO_SLOTS * 32 * sizeof(uint2));
 constexpr int MAX_SEEDS = 8;  // finished earlier splits merged into a fresh list
 
+// Instruction descriptor for kind::f16: f16 x f16 -> f32, both K-major
+// (PTX ISA instruction-descriptor table).
+__host__ __device__ constexpr uint32_t idesc_f16_f32(uint32_t m, uint32_t n) {
+  return (1u << 4)     // D format: f32
+         | (0u << 7)   // A: f16
+         | (0u << 10)  // B: f16
+         | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// K1: u8 operands, exact s32 products; ranks on r = ||x||^2 - 2 q.x.
+struct U8Scan {
+  using T = int32_t;
+  static constexpr int FIFO_SLOTS = 32;  // deferred-insertion FIFO entries per thread
+  __host__ __device__ static constexpr T big() { return BIG; }
+  __host__ __device__ static uint32_t pack(T r) { return static_cast<uint32_t>(r) + R_OFFSET; }
+  __host__ __device__ static T unpack(uint32_t key) { return static_cast<int32_t>(key - R_OFFSET); }
+  __device__ static T next_up(T r) { return r + 1; }
+  __device__ static T value(uint32_t acc, T h, float) { return h - 2 * static_cast<int32_t>(acc); }
+  __device__ static uint32_t idesc() { return sm100::idesc_u8_s32(UM, BN); }
+  __device__ static void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+    sm100::mma_i8(d, a, b, id, acc);
+  }
+};
+
+// K2: f16 operands, f32 accumulation; ranks on r = h_x + c_q * (q^ . x^).
+struct F16Scan {
+  using T = float;
+  static constexpr int FIFO_SLOTS = 16;
+  __host__ __device__ static constexpr T big() { return 3.0e38f; }
+  __host__ __device__ static uint32_t pack(T r) { return order_key(r); }
+  __host__ __device__ static T unpack(uint32_t key) { return key_to_float(key); }
+  __device__ static T next_up(T r) { return key_to_float(order_key(r) + 1u); }
+  __device__ static T value(uint32_t acc, T h, float c) { return fmaf(__uint_as_float(acc), c, h); }
+  __device__ static uint32_t idesc() { return idesc_f16_f32(UM, BN); }
+  __device__ static void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+    mma_f16(d, a, b, id, acc);
+  }
+};
+
+// per-warp: two tiles of the per-row term, and the deferred-insertion FIFO
+template <class P>
+__host__ __device__ constexpr size_t norm_bytes() {
+  return (size_t)NUM_EPI_WARPS * (2 * BN * 4 + P::FIFO_SLOTS * 32 * sizeof(uint2));
+}
+
 struct Params {
-  const int32_t* norms;    // ||x||^2 per rank, BIG for padding ranks
-  int32_t* bound;          // [nq_pad] shared pruning bound on r per query
+  const void* norms;       // per-rank row term (P::T): ||x||^2 for K1; padding ranks hold P::big()
+  const float* qcoef;      // K2: per-query factor c_q (nullptr for K1)
+  uint32_t* bound;         // [nq_pad] shared pruning bound per query, as a packed key (P::pack)
   uint32_t* done_count;    // [nqt] finished splits per query tile
   uint32_t* done_list;     // [nqt][nsplit] finished split ids in finishing order (~0u = not yet)
-  uint64_t* out_part;      // [nq_pad][nsplit][KT] packed (r+R_OFFSET)<<32 | rank
+  uint64_t* out_part;      // [nq_pad][nsplit][KT] packed P::pack(r)<<32 | rank
   uint32_t* status;        // device error word
   uint32_t nq;
-  uint32_t k;              // requested k (<= KT); the k-th value is what is shared
-  uint32_t kblocks;        // dim_pad / 128
+  uint32_t k;              // the list position whose value is shared as the pruning bound (<= KT)
+  uint32_t kblocks;        // K bytes / 128
   uint32_t ntiles;         // nrank_pad / BN
   uint32_t tiles_per_split;
   uint32_t nsplit;
@@ -85,29 +145,30 @@ struct Params {
   uint64_t wait_ns;
 };
 
+template <class P>
 __host__ __device__ inline size_t smem_bytes(uint32_t kblocks, uint32_t stages) {
-  size_t off = (size_t)kblocks * A_BLOCK + (size_t)stages * B_BLOCK + NORM_BYTES;
+  size_t off = (size_t)kblocks * A_BLOCK + (size_t)stages * B_BLOCK + norm_bytes<P>();
   off += (2 * stages + 6) * sizeof(uint64_t) + 16;
   return off + 1024;  // alignment slack
 }
 
-// Stages in the ring: as many as fit, at most 8, at least two tiles' worth.
+// Stages in the ring: as many as fit, at most 8.
+template <class P>
 __host__ inline uint32_t pick_stages(uint32_t kblocks) {
-  size_t fixed = (size_t)kblocks * A_BLOCK + NORM_BYTES + 1024 + 256;
+  size_t fixed = (size_t)kblocks * A_BLOCK + norm_bytes<P>() + 1024 + 256;
   uint32_t s = (uint32_t)((SMEM_LIMIT - fixed) / (B_BLOCK + 16));
   return s > 8 ? 8 : s;
 }
 
 // Branch-free insertion into an ascending register list; precondition
 // r < lr[K-1]. Elements equal to r stay ahead of it (they have smaller ids).
-template <int K>
-__device__ __forceinline__ void insert_sorted(int32_t (&lr)[K], uint32_t (&lk)[K], int32_t r,
-                                              uint32_t rank) {
+template <int K, class T>
+__device__ __forceinline__ void insert_sorted(T (&lr)[K], uint32_t (&lk)[K], T r, uint32_t rank) {
 #pragma unroll
   for (int i = K - 1; i > 0; --i) {
     bool shift = lr[i - 1] > r;
     bool here = lr[i] > r;
-    int32_t nr = shift ? lr[i - 1] : (here ? r : lr[i]);
+    T nr = shift ? lr[i - 1] : (here ? r : lr[i]);
     uint32_t nk = shift ? lk[i - 1] : (here ? rank : lk[i]);
     lr[i] = nr;
     lk[i] = nk;
@@ -121,10 +182,13 @@ __device__ __forceinline__ void record_failure(uint32_t* status, uint32_t code) 
   if (atomicCAS(status, 0u, code) == 0u) atomicExch(status + 1, blockIdx.y * gridDim.x + blockIdx.x);
 }
 
-__device__ __forceinline__ int32_t load_bound(const int32_t* p) {
-  int32_t v;
-  asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+// The shared bound as a value; keys above the sentinel's (the 0xFF.. fill)
+// read as the sentinel.
+template <class P>
+__device__ __forceinline__ typename P::T load_bound(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return P::unpack(min(v, P::pack(P::big())));
 }
 __device__ __forceinline__ uint32_t load_acquire(const uint32_t* p) {
   uint32_t v;
@@ -142,9 +206,10 @@ __device__ __forceinline__ void store_release(uint32_t* p, uint32_t v) {
 // every rank this split scans, so a scanned column that ties a seeded value
 // still loses under the strict '<'; and the seeded entries also remain in
 // their own split's list, so the merge (which drops duplicates) sees them.
-template <int KT>
-__device__ __forceinline__ void seed_from_finished(const Params& p, uint32_t qtile, uint32_t split,
-                                                   uint32_t q, int32_t (&lr)[KT], uint32_t (&lk)[KT]) {
+template <int KT, class P>
+__device__ __forceinline__ void seed_from_finished(const Params& p, uint32_t qtile, uint32_t split, uint32_t q,
+                                                   typename P::T (&lr)[KT], uint32_t (&lk)[KT]) {
+  using T = typename P::T;
   const uint32_t cnt = min(load_acquire(p.done_count + qtile), p.nsplit);
   int used = 0;
   for (uint32_t i = cnt; i > 0 && used < MAX_SEEDS; --i) {
@@ -158,7 +223,7 @@ __device__ __forceinline__ void seed_from_finished(const Params& p, uint32_t qti
     for (int j = 0; j < KT; ++j) keys[j] = __ldcg(src + j);  // all loads in flight at once
 #pragma unroll
     for (int j = 0; j < KT; ++j) {
-      const int32_t r = static_cast<int32_t>(static_cast<uint32_t>(keys[j] >> 32) - R_OFFSET);
+      const T r = P::unpack(static_cast<uint32_t>(keys[j] >> 32));
       if (!(r < lr[KT - 1])) continue;
       // A finished split's list may already hold entries it seeded from a
       // third split: admit each rank once, or the list (and the bound it
@@ -167,23 +232,27 @@ __device__ __forceinline__ void seed_from_finished(const Params& p, uint32_t qti
       bool dup = false;
 #pragma unroll
       for (int i = 0; i < KT; ++i) dup |= lk[i] == rank && lr[i] == r;
-      if (!dup) insert_sorted<KT>(lr, lk, r, rank);
+      if (!dup) insert_sorted<KT, T>(lr, lk, r, rank);
     }
   }
 }
 
-// r = ||x||^2 - 2 q.x for one 32-column chunk; returns the chunk minimum
-// (tree reduction: depth 5 instead of a 31-long dependency chain).
-__device__ __forceinline__ int32_t chunk_r(const uint32_t (&v)[32], const int32_t* nrm, int32_t (&r)[32]) {
+// r of one 32-column chunk (P::value of the accumulator and the row term);
+// returns the chunk minimum (tree reduction: depth 5 instead of a 31-long
+// dependency chain).
+template <class P>
+__device__ __forceinline__ typename P::T chunk_r(const uint32_t (&v)[32], const typename P::T* nrm, float c,
+                                                 typename P::T (&r)[32]) {
+  using T = typename P::T;
 #pragma unroll
   for (int j4 = 0; j4 < 8; ++j4) {
-    const int4 h = *reinterpret_cast<const int4*>(nrm + 4 * j4);
-    r[4 * j4 + 0] = h.x - 2 * static_cast<int32_t>(v[4 * j4 + 0]);
-    r[4 * j4 + 1] = h.y - 2 * static_cast<int32_t>(v[4 * j4 + 1]);
-    r[4 * j4 + 2] = h.z - 2 * static_cast<int32_t>(v[4 * j4 + 2]);
-    r[4 * j4 + 3] = h.w - 2 * static_cast<int32_t>(v[4 * j4 + 3]);
+    const int4 hb = *reinterpret_cast<const int4*>(nrm + 4 * j4);
+    const T h[4] = {*reinterpret_cast<const T*>(&hb.x), *reinterpret_cast<const T*>(&hb.y),
+                    *reinterpret_cast<const T*>(&hb.z), *reinterpret_cast<const T*>(&hb.w)};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) r[4 * j4 + j] = P::value(v[4 * j4 + j], h[j], c);
   }
-  int32_t m[16];
+  T m[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) m[j] = min(r[j], r[j + 16]);
 #pragma unroll
@@ -194,9 +263,10 @@ __device__ __forceinline__ int32_t chunk_r(const uint32_t (&v)[32], const int32_
 }
 
 // Minimum of r over one 32-column chunk without keeping r (fast path).
-__device__ __forceinline__ int32_t chunk_min(const uint32_t (&v)[32], const int32_t* nrm) {
-  int32_t r[32];
-  return chunk_r(v, nrm, r);
+template <class P>
+__device__ __forceinline__ typename P::T chunk_min(const uint32_t (&v)[32], const typename P::T* nrm, float c) {
+  typename P::T r[32];
+  return chunk_r<P>(v, nrm, c, r);
 }
 
 // Deferred insertion. A flagged chunk's admitted (r, rank) pairs are pushed
@@ -205,50 +275,54 @@ __device__ __forceinline__ int32_t chunk_min(const uint32_t (&v)[32], const int3
 // the accumulator is released, so insertions overlap the next tile's MMAs
 // instead of stalling them. FIFO order is ascending rank order, so draining
 // with the strict '<' keeps the list exact.
-constexpr int FIFO_CAP = FIFO_SLOTS;  // one full chunk always fits after a drain
-
-template <int KT>
-__device__ __forceinline__ void fifo_drain(const uint2* fifo, uint32_t& cnt, uint32_t lane, int32_t (&lr)[KT],
-                                           uint32_t (&lk)[KT], int32_t shared_bound) {
+// One FIFO holds at most one flagged chunk's 32 entries beyond what a drain
+// leaves (the K2 FIFO of 16 drains mid-chunk, see fifo_push_chunk).
+template <int KT, class P>
+__device__ __forceinline__ void fifo_drain(const uint2* fifo, uint32_t& cnt, uint32_t lane,
+                                           typename P::T (&lr)[KT], uint32_t (&lk)[KT],
+                                           typename P::T shared_bound) {
+  using T = typename P::T;
+  const T above = P::next_up(shared_bound);  // admit r <= shared_bound
   for (uint32_t i = 0; i < cnt; ++i) {
     const uint2 e = fifo[i * 32 + lane];
-    const int32_t r = static_cast<int32_t>(e.x);
-    if (r < min(lr[KT - 1], shared_bound + 1)) insert_sorted<KT>(lr, lk, r, e.y);
+    const T r = *reinterpret_cast<const T*>(&e.x);
+    if (r < min(lr[KT - 1], above)) insert_sorted<KT, T>(lr, lk, r, e.y);
   }
   cnt = 0;
 }
 
-template <int KT>
-__device__ __forceinline__ void fifo_push_chunk(const int32_t (&r)[32], int32_t thr, uint32_t rank0, uint2* fifo,
-                                                uint32_t& cnt, uint32_t lane, int32_t (&lr)[KT],
-                                                uint32_t (&lk)[KT], int32_t shared_bound) {
+template <int KT, class P>
+__device__ __forceinline__ void fifo_push_chunk(const typename P::T (&r)[32], typename P::T thr, uint32_t rank0,
+                                                uint2* fifo, uint32_t& cnt, uint32_t lane, typename P::T (&lr)[KT],
+                                                uint32_t (&lk)[KT], typename P::T shared_bound) {
   uint32_t mask = 0;
 #pragma unroll
   for (int j = 0; j < 32; ++j) mask |= (r[j] < thr ? 1u : 0u) << j;
-  if (cnt + __popc(mask) > FIFO_CAP) fifo_drain<KT>(fifo, cnt, lane, lr, lk, shared_bound);
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     if (mask & (1u << j)) {
-      fifo[cnt * 32 + lane] = make_uint2(static_cast<uint32_t>(r[j]), rank0 + j);
+      if (cnt == (uint32_t)P::FIFO_SLOTS) fifo_drain<KT, P>(fifo, cnt, lane, lr, lk, shared_bound);
+      fifo[cnt * 32 + lane] = make_uint2(*reinterpret_cast<const uint32_t*>(&r[j]), rank0 + j);
       ++cnt;
     }
   }
 }
 
-template <int KT>
+template <int KT, class P>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    flat_u8_kernel(const __grid_constant__ CUtensorMap tmap_q,
-                   const __grid_constant__ CUtensorMap tmap_x, const Params p) {
+    flat_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
+                     const __grid_constant__ CUtensorMap tmap_x, const Params p) {
   using namespace sm100;
+  using T = typename P::T;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t kblocks = p.kblocks, stages = p.stages;
   unsigned char* sA = smem;
   unsigned char* sB = smem + (size_t)kblocks * A_BLOCK;
-  int32_t* sNorm = reinterpret_cast<int32_t*>(sB + (size_t)stages * B_BLOCK);  // [warp][2][BN]
+  T* sNorm = reinterpret_cast<T*>(sB + (size_t)stages * B_BLOCK);             // [warp][2][BN]
   uint2* sFifo = reinterpret_cast<uint2*>(sNorm + NUM_EPI_WARPS * 2 * BN);    // [warp][slot][lane]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sFifo + NUM_EPI_WARPS * FIFO_SLOTS * 32);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sFifo + NUM_EPI_WARPS * P::FIFO_SLOTS * 32);
   uint64_t* full = bars;
   uint64_t* empty = bars + stages;
   uint64_t* acc_full = bars + 2 * stages;  // [2]: one per query half
@@ -324,7 +398,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     mbar_wait(a_full, 0, p.wait_ns);
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    const uint32_t idesc = idesc_u8_s32(UM, BN);
+    const uint32_t idesc = P::idesc();
     bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(a_full, 0, p.wait_ns));
     if (!ok) {
       if (lane == 0) record_failure(p.status, DEV_TIMEOUT_FULL);
@@ -364,7 +438,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (uint32_t k = 0; k < KB_BYTES / UMMA_K; ++k) {
               // K advance inside the 128-byte swizzle atom: +32 bytes = +2 in
               // the 16-byte-unit start-address field.
-              mma_i8(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+              P::mma(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
             }
           }
           __syncwarp();
@@ -390,32 +464,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t half = ew >> 2;
     const uint32_t row = half * UM + quarter * 32 + lane;
     const uint32_t q = qtile * BM + row;
-    int32_t* bound_ptr = p.bound + q;
-    int32_t* wnorm = sNorm + ew * 2 * BN;  // this warp's two tile slots
-    uint2* wfifo = sFifo + ew * FIFO_SLOTS * 32;  // this warp's deferred-insertion FIFO
+    uint32_t* bound_ptr = p.bound + q;
+    T* wnorm = sNorm + ew * 2 * BN;  // this warp's two tile slots
+    uint2* wfifo = sFifo + ew * P::FIFO_SLOTS * 32;  // this warp's deferred-insertion FIFO
     uint32_t fifo_cnt = 0;
-    int32_t lr[KT];
+    const float coef = (p.qcoef != nullptr && q < p.nq) ? p.qcoef[q] : 0.0f;
+    T lr[KT];
     uint32_t lk[KT];
 #pragma unroll
     for (int i = 0; i < KT; ++i) {
-      lr[i] = BIG;
+      lr[i] = P::big();
       lk[i] = 0xFFFFFFFFu;
     }
-    if (q < p.nq) seed_from_finished<KT>(p, qtile, split, q, lr, lk);
-    int32_t shared_bound = load_bound(bound_ptr);  // prune r > shared_bound
-    int32_t published = BIG;
+    if (q < p.nq) seed_from_finished<KT, P>(p, qtile, split, q, lr, lk);
+    T shared_bound = load_bound<P>(bound_ptr);  // prune r > shared_bound
+    T published = P::big();
     // ||x||^2 of tile t sits in this warp's slot t & 1; tile t+1's is fetched
     // (8 per lane) while tile t is scanned.
     int4 nx0 = make_int4(0, 0, 0, 0), nx1 = nx0;
     if (ntile_local > 0) {
-      const int4* src = reinterpret_cast<const int4*>(p.norms + (size_t)t_begin * BN);
+      const int4* src = reinterpret_cast<const int4*>(static_cast<const T*>(p.norms) + (size_t)t_begin * BN);
       reinterpret_cast<int4*>(wnorm)[lane] = __ldg(src + lane);
       reinterpret_cast<int4*>(wnorm)[32 + lane] = __ldg(src + 32 + lane);
     }
     __syncwarp();
     for (uint32_t t = 0; t < ntile_local; ++t) {
       if (t + 1 < ntile_local) {
-        const int4* src = reinterpret_cast<const int4*>(p.norms + (size_t)(t_begin + t + 1) * BN);
+        const int4* src = reinterpret_cast<const int4*>(static_cast<const T*>(p.norms) + (size_t)(t_begin + t + 1) * BN);
         nx0 = __ldg(src + lane);
         nx1 = __ldg(src + 32 + lane);
       }
@@ -428,14 +503,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const uint32_t rank_base = (t_begin + t) * BN;
       const uint32_t taddr = tmem_base + ((quarter * 32) << 16) + half * BN;
-      const int32_t* nrm = wnorm + (t & 1) * BN;
+      const T* nrm = wnorm + (t & 1) * BN;
       // Fast path, branch-free over the whole tile: per chunk only the minimum
       // of r, compared with the admission bound taken at the start of the tile
       // (the list does not change within a tile: insertions are deferred).
-      const int32_t thr = min(lr[KT - 1], shared_bound + 1);
+      const T thr = min(lr[KT - 1], P::next_up(shared_bound));
       // the other splits' bound is read now and folded in after the tile, so
       // the load's latency hides behind the scan
-      const int32_t fresh_bound = load_bound(bound_ptr);
+      const T fresh_bound = load_bound<P>(bound_ptr);
       uint32_t va[32], vb[32];
       uint32_t hit = 0;  // bit c: chunk c holds a candidate for this lane
       tmem_ld_32x32b_x32(taddr, va);
@@ -444,10 +519,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (uint32_t c = 0; c < BN / 32; c += 2) {
         // chunk c from va while chunk c+1 loads into vb, then the reverse
         tmem_ld_32x32b_x32(taddr + (c + 1) * 32, vb);
-        hit |= static_cast<uint32_t>(chunk_min(va, nrm + c * 32) < thr) << c;
+        hit |= static_cast<uint32_t>(chunk_min<P>(va, nrm + c * 32, coef) < thr) << c;
         tmem_ld_wait();
         if (c + 2 < BN / 32) tmem_ld_32x32b_x32(taddr + (c + 2) * 32, va);
-        hit |= static_cast<uint32_t>(chunk_min(vb, nrm + (c + 1) * 32) < thr) << (c + 1);
+        hit |= static_cast<uint32_t>(chunk_min<P>(vb, nrm + (c + 1) * 32, coef) < thr) << (c + 1);
         tmem_ld_wait();
       }
       // Flagged chunks (one vote per tile) are re-read from TMEM and their
@@ -456,11 +531,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       while (uhit) {
         const uint32_t c = __ffs(uhit) - 1;
         uhit &= uhit - 1;
-        int32_t r[32];
+        T r[32];
         tmem_ld_32x32b_x32(taddr + c * 32, va);
         tmem_ld_wait();
-        chunk_r(va, nrm + c * 32, r);
-        fifo_push_chunk<KT>(r, thr, rank_base + c * 32, wfifo, fifo_cnt, lane, lr, lk, shared_bound);
+        chunk_r<P>(va, nrm + c * 32, coef, r);
+        fifo_push_chunk<KT, P>(r, thr, rank_base + c * 32, wfifo, fifo_cnt, lane, lr, lk, shared_bound);
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[half]);
@@ -471,16 +546,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         dst[32 + lane] = nx1;
       }
       // insertions happen while the tensor core fills the next tile
-      if (fifo_cnt) fifo_drain<KT>(wfifo, fifo_cnt, lane, lr, lk, shared_bound);
+      if (fifo_cnt) fifo_drain<KT, P>(wfifo, fifo_cnt, lane, lr, lk, shared_bound);
       __syncwarp();
       // Share the bound with the other splits of this query tile: the k-th
       // value of this split's list (k <= KT, selected without dynamic indexing).
-      int32_t kth = lr[KT - 1];
+      T kth = lr[KT - 1];
 #pragma unroll
       for (int i = 0; i < KT; ++i) kth = (i + 1 == (int)p.k) ? lr[i] : kth;
       if (kth < published) {
         published = kth;
-        atomicMin(bound_ptr, published);
+        atomicMin(bound_ptr, P::pack(published));
       }
       shared_bound = min(shared_bound, fresh_bound);
     }
@@ -488,7 +563,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint64_t* dst = p.out_part + ((size_t)q * p.nsplit + split) * KT;
 #pragma unroll
       for (int i = 0; i < KT; ++i)
-        dst[i] = (static_cast<uint64_t>(static_cast<uint32_t>(lr[i]) + R_OFFSET) << 32) | lk[i];
+        dst[i] = (static_cast<uint64_t>(P::pack(lr[i])) << 32) | lk[i];
       __threadfence();  // the list is visible device-wide before this split is announced
     }
   }
