@@ -330,6 +330,7 @@ constexpr uint32_t K2_KT = 32;         // candidates the screen keeps per query
 constexpr uint32_t K2_MAX_K = 24;      // largest k served (the rest of the list is the proof's margin)
 constexpr uint32_t K2_MAX_DIM = 128;   // two 128-byte K blocks of f16
 constexpr uint32_t K2_MEAN_CHUNKS = 64;
+constexpr uint32_t K2_RANGE_BATCH = 256;  // redo queries per range pass (256 x 32 KiB of collection)
 
 // Partial column sums (f64) of the rank-ordered rows: block (32 columns x 8
 // row lanes) per (column group, row chunk); column_mean_kernel folds the
@@ -422,6 +423,7 @@ struct K2Query {
   float cst;       // d~ = r + cst
   double eps;      // E_s: |d~ - d_real| <= eps for every row
   double eref;     // cosine / IP: |d_ref - d_real| <= eref; euclidean: relative factor gamma
+  float delta;     // margin of the shared bound over the k-th screened value (> 2 E_s + E_ref)
 };
 __global__ void k2_prep_queries_kernel(const float* __restrict__ Q, uint32_t nq, uint32_t dim, uint32_t dp,
                                        const float* __restrict__ mu, int metric, int ax, const float* __restrict__ xst,
@@ -481,12 +483,21 @@ __global__ void k2_prep_queries_kernel(const float* __restrict__ Q, uint32_t nq,
   m.eref = metric == PXC_EUCLIDEAN ? gamma : gamma * Qu * Mu + ldexp(1.0, -24) * (1.0 + Qu * Mu);
   // a query whose factors leave the f32 range cannot be screened; it is proven never
   if (!(isfinite(m.coef) && isfinite(m.cst) && isfinite(m.eps)) || q >= nq) m.eps = INFINITY;
+  // A row whose screened value is behind the k-th by more than 2 E_s + E_ref
+  // (plus the reference's relative error at that size) is provably behind the
+  // k-th exact distance; sharing kth + delta lets the screen drop it.
+  const double ref_part = metric == PXC_EUCLIDEAN ? m.eref * (fabs((double)m.cst) + Hmax + qmn) * 2.0 : m.eref;
+  m.delta = round_up_f32(1.25 * (2.0 * m.eps + ref_part) + 1e-30);
   meta[q] = m;
 }
 
-__global__ void copy_coef_kernel(const K2Query* __restrict__ meta, uint32_t n, float* __restrict__ coef) {
+__global__ void copy_coef_kernel(const K2Query* __restrict__ meta, uint32_t n, float* __restrict__ coef,
+                                 float* __restrict__ delta) {
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) coef[i] = meta[i].coef;
+  if (i < n) {
+    coef[i] = meta[i].coef;
+    delta[i] = meta[i].delta;
+  }
 }
 
 // space.distance on prepared operands (crates/proxima-core/src/space.rs:148-156).
@@ -501,11 +512,13 @@ __device__ __forceinline__ float k2_ref_distance(int metric, const float* q, con
 // dropped), its first K2_KT entries re-scored exactly and sorted by
 // (total_cmp, id), the first k written out, and the proof. 128 threads.
 __global__ void __launch_bounds__(128) k2_rerank_kernel(const uint64_t* __restrict__ part, uint32_t nsplit, uint32_t cap,
+                                                        const uint32_t* __restrict__ bound,
                                                         const K2Query* __restrict__ meta, const float* __restrict__ Q,
                                                         uint32_t dim, int metric, const float* __restrict__ rank_rows,
                                                         const uint64_t* __restrict__ rank_id, uint32_t nrank, uint32_t k,
                                                         uint64_t* __restrict__ out_ids, float* __restrict__ out_dist,
-                                                        uint32_t* __restrict__ out_len, uint8_t* __restrict__ redo) {
+                                                        uint32_t* __restrict__ out_len, uint8_t* __restrict__ redo,
+                                                        float* __restrict__ kth_out) {
   extern __shared__ uint64_t sl[];  // [cap]
   __shared__ uint32_t flag[2048];
   __shared__ uint64_t cand[K2_KT];
@@ -566,23 +579,97 @@ __global__ void __launch_bounds__(128) k2_rerank_kernel(const uint64_t* __restri
   }
   if (threadIdx.x == 0) {
     out_len[q] = take;
+    // Every row the candidates leave out has r >= T: the shared bound turned
+    // it away (r > the final bound), or a full split list did (r >= that
+    // list's last entry >= the union's K2_KT-th), or it is behind the union's
+    // K2_KT-th entry. T = big: no row was left out.
+    using F = flat_tc::F16Scan;
+    float T = F::unpack(min(bound[q], F::pack(F::big())));
+    if (ncand >= K2_KT) T = fminf(T, F::unpack(static_cast<uint32_t>(cand[K2_KT - 1] >> 32)));
     uint8_t bad = 0;
-    if (nrank > K2_KT) {
-      // Every row outside the first K2_KT of the union has d~ at or behind the
-      // K2_KT-th entry: it was behind it in the union, or a full split list or
-      // the shared bound (a full list's last entry) turned it away.
+    if (T < F::big()) {
       const K2Query m = meta[q];
-      const double T = (double)flat_tc::F16Scan::unpack(static_cast<uint32_t>(cand[K2_KT - 1] >> 32)) + (double)m.cst;
-      double lower = T - m.eps;
+      double lower = (double)T + (double)m.cst - m.eps;
       if (metric == PXC_EUCLIDEAN)
         lower = lower > 0.0 ? lower * (1.0 - m.eref) : lower * (1.0 + m.eref);
       else
         lower -= m.eref;
       const double dk = take ? (double)key_to_float(static_cast<uint32_t>(ex[take - 1] >> 32)) : INFINITY;
-      bad = (ncand < K2_KT || take < k || !(lower > dk)) ? 1 : 0;
+      bad = (take < k || !(lower > dk)) ? 1 : 0;
     }
     redo[q] = bad;
+    // the candidates' k-th exact distance bounds the true k-th from above
+    kth_out[q] = take == k ? key_to_float(static_cast<uint32_t>(ex[take - 1] >> 32)) : INFINITY;
   }
+}
+
+// The screen's fallback for the queries it could not prove: every row's
+// exact distance, and the rows at or ahead of the candidates' k-th exact
+// distance t (an upper bound of the true k-th) collected per query. The true
+// top k is among them. Block = 128 rows x K2_RANGE_Q redo queries (held in
+// shared memory); a query whose collection overflows K2_RANGE_CAP is left to
+// the fp32 scan.
+constexpr uint32_t K2_RANGE_Q = 4;
+constexpr uint32_t K2_RANGE_CAP = 4096;
+__global__ void __launch_bounds__(128) k2_range_kernel(const float* __restrict__ Qr, const float* __restrict__ thr,
+                                                       uint32_t nredo, const float* __restrict__ rank_rows,
+                                                       uint32_t nrank, uint32_t dim, int metric,
+                                                       uint64_t* __restrict__ buf, uint32_t* __restrict__ cnt) {
+  __shared__ float sq[K2_RANGE_Q][K2_MAX_DIM];
+  const uint32_t q0 = blockIdx.y * K2_RANGE_Q;
+  const uint32_t nqb = min(K2_RANGE_Q, nredo - q0);
+  for (uint32_t e = threadIdx.x; e < nqb * dim; e += blockDim.x) sq[e / dim][e % dim] = Qr[(size_t)(q0 + e / dim) * dim + e % dim];
+  __syncthreads();
+  const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= nrank) return;
+  const float* x = rank_rows + (size_t)r * dim;
+  for (uint32_t j = 0; j < nqb; ++j) {
+    const float d = k2_ref_distance(metric, sq[j], x, dim);
+    const uint32_t key = order_key(d);
+    if (key <= order_key(thr[q0 + j])) {
+      const uint32_t pos = atomicAdd(cnt + q0 + j, 1u);
+      if (pos < K2_RANGE_CAP) buf[(size_t)(q0 + j) * K2_RANGE_CAP + pos] = (static_cast<uint64_t>(key) << 32) | r;
+    }
+  }
+}
+
+// Per redo query: sort the collected (distance, rank) keys and write the first
+// k to the query's result row; flag an overflow. 256 threads.
+__global__ void __launch_bounds__(256) k2_range_finish_kernel(const uint64_t* __restrict__ buf,
+                                                              const uint32_t* __restrict__ cnt,
+                                                              const uint32_t* __restrict__ idx, uint32_t k,
+                                                              const uint64_t* __restrict__ rank_id,
+                                                              uint64_t* __restrict__ out_ids,
+                                                              float* __restrict__ out_dist, uint32_t* __restrict__ out_len,
+                                                              uint8_t* __restrict__ overflow) {
+  extern __shared__ uint64_t sb[];  // [K2_RANGE_CAP]
+  const uint32_t i = blockIdx.x;
+  const uint32_t n = cnt[i];
+  if (n > K2_RANGE_CAP) {
+    if (threadIdx.x == 0) overflow[i] = 1;
+    return;
+  }
+  uint32_t cap = 32;
+  while (cap < n) cap <<= 1;
+  for (uint32_t e = threadIdx.x; e < cap; e += blockDim.x) sb[e] = e < n ? buf[(size_t)i * K2_RANGE_CAP + e] : ~0ull;
+  __syncthreads();
+  block_bitonic_sort_u64(sb, cap);
+  const uint32_t q = idx[i];
+  const uint32_t take = min(n, k);
+  for (uint32_t e = threadIdx.x; e < take; e += blockDim.x) {
+    out_ids[(size_t)q * k + e] = rank_id[static_cast<uint32_t>(sb[e])];
+    out_dist[(size_t)q * k + e] = key_to_float(static_cast<uint32_t>(sb[e] >> 32));
+  }
+  if (threadIdx.x == 0) {
+    out_len[q] = take;
+    overflow[i] = 0;
+  }
+}
+
+__global__ void gather_f32_kernel(const float* __restrict__ src, const uint32_t* __restrict__ idx, uint32_t n,
+                                  float* __restrict__ out) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = src[idx[i]];
 }
 
 }  // namespace pxc
@@ -659,6 +746,10 @@ struct pxc_flat {
   DBuf<uint32_t> k2_stats;      // max |x'_i|, max ||x'||, max ||x||, max |h_x| (float bits)
   DBuf<K2Query> k2_meta;
   CUtensorMap k2_tmap_x;
+  DBuf<float> k2_kth, k2_thr;     // per query: the candidates' k-th exact distance; gathered for redo queries
+  DBuf<uint64_t> k2_range;        // [nredo][K2_RANGE_CAP] collected (distance, rank) keys
+  DBuf<uint32_t> k2_range_cnt, k2_ovf_idx, k2_ovf_len;
+  DBuf<uint8_t> k2_ovf;
   uint32_t last_redo = 0;  // queries of the last grouped search redone on K1g
   cudaEvent_t ev_done = nullptr;  // end of the last search's work (handoff of the scratch)
   std::mutex mu;
@@ -840,6 +931,7 @@ void search_tc(pxc_flat* h, const TcOperand& op, const float* d_q, uint32_t nq, 
   flat_tc::Params p;
   p.norms = op.norms;
   p.qcoef = nullptr;
+  p.qdelta = nullptr;
   p.bound = reinterpret_cast<uint32_t*>(h->bound.p);
   p.done_count = h->done.p;
   p.done_list = h->done.p + nqt;
@@ -1073,36 +1165,9 @@ bool k2_applicable(const pxc_flat* h, uint32_t k, const uint64_t* d_bitmap) {
          h->nrank > 0;
 }
 
-// Queries flagged in h->g_redo (their screen could not prove them) are
-// searched again on K1g and their rows replaced. Synchronises the stream.
-void redo_flagged(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, const uint64_t* d_bitmap, uint64_t* d_ids,
-                  float* d_dist, uint32_t* d_len, cudaStream_t s) {
-  size_t tb = 0;
-  thrust::counting_iterator<uint32_t> it(0);
-  PXC_CUDA(cub::DeviceSelect::Flagged(nullptr, tb, it, h->g_redo.p, h->g_redo_idx.p, h->g_redo_len.p, (int64_t)nq, s));
-  h->tmp.reserve(std::max<size_t>(tb, 1));
-  PXC_CUDA(cub::DeviceSelect::Flagged(h->tmp.p, tb, it, h->g_redo.p, h->g_redo_idx.p, h->g_redo_len.p, (int64_t)nq, s));
-  PXC_CUDA(cudaMemcpyAsync(h->h_flag, h->g_redo_len.p, sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
-  PXC_CUDA(cudaStreamSynchronize(s));
-  const uint32_t nredo = static_cast<uint32_t>(*h->h_flag);
-  h->last_redo = nredo;
-  h->ctx->launches += 2;
-  if (nredo == 0) return;
-  h->g_redo_q.reserve((size_t)nredo * h->dim);
-  h->g_redo_ids.reserve((size_t)nredo * k);
-  h->g_redo_dist.reserve((size_t)nredo * k);
-  h->g_redo_len.reserve(nredo);
-  gather_queries_kernel<<<nredo, 128, 0, s>>>(d_q, h->g_redo_idx.p, h->dim, h->g_redo_q.p);
-  PXC_CUDA(cudaGetLastError());
-  search_generic(h, h->g_redo_q.p, nredo, k, d_bitmap, h->g_redo_ids.p, h->g_redo_dist.p, h->g_redo_len.p, s);
-  scatter_results_kernel<<<nredo, 128, 0, s>>>(h->g_redo_ids.p, h->g_redo_dist.p, h->g_redo_len.p,
-                                               h->g_redo_idx.p, k, d_ids, d_dist, d_len);
-  PXC_CUDA(cudaGetLastError());
-  h->ctx->launches += 2;
-}
-
 // K2: the f16 screen (flat_scan_kernel<K2_KT, F16Scan>), the exact re-rank
-// with its per-query proof, and K1g for the queries left unproven.
+// with its per-query proof, and for the queries left unproven an exact range
+// scan (K1g for the few whose range overflows).
 void search_k2(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, uint64_t* d_ids, float* d_dist,
                uint32_t* d_len, cudaStream_t s) {
   const uint32_t nq_pad = (nq + flat_tc::BM - 1) / flat_tc::BM * flat_tc::BM;
@@ -1110,12 +1175,13 @@ void search_k2(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, uint64_t*
   const uint32_t dp = h->k2_dp;
   h->k2_q.reserve((size_t)nq_pad * dp);
   h->k2_meta.reserve(nq_pad);
-  h->k2_coef.reserve(nq_pad);
+  h->k2_coef.reserve(2 * (size_t)nq_pad);  // c_q, then delta_q
   k2_prep_queries_kernel<<<nq_pad, 128, 0, s>>>(d_q, nq, h->dim, dp, h->k2_mu.p, h->metric, h->k2_ax,
                                                 reinterpret_cast<const float*>(h->k2_stats.p), h->k2_q.p,
                                                 h->k2_meta.p);
   PXC_CUDA(cudaGetLastError());
-  copy_coef_kernel<<<grid1d(nq_pad, 256), 256, 0, s>>>(h->k2_meta.p, nq_pad, h->k2_coef.p);
+  copy_coef_kernel<<<grid1d(nq_pad, 256), 256, 0, s>>>(h->k2_meta.p, nq_pad, h->k2_coef.p,
+                                                       h->k2_coef.p + nq_pad);
   const uint32_t ntiles = (uint32_t)(h->k2_nrank_pad / flat_tc::BN);
   const uint32_t nsplit_req = choose_splits(nqt, ntiles, h->ctx->sm_count, K2_KT);
   const uint32_t tps = (ntiles + nsplit_req - 1) / nsplit_req;
@@ -1129,13 +1195,14 @@ void search_k2(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, uint64_t*
   flat_tc::Params p;
   p.norms = h->k2_h.p;
   p.qcoef = h->k2_coef.p;
+  p.qdelta = h->k2_coef.p + nq_pad;
   p.bound = reinterpret_cast<uint32_t*>(h->bound.p);
   p.done_count = h->done.p;
   p.done_list = h->done.p + nqt;
   p.out_part = h->part.p;
   p.status = h->d_status;
   p.nq = nq;
-  p.k = K2_KT;  // rows behind a full list's last entry cannot enter the union's first K2_KT
+  p.k = k;  // the shared bound is min(last entry, k-th + delta_q): F16Scan::publish
   p.kblocks = dp * 2 / flat_tc::KB_BYTES;
   p.ntiles = ntiles;
   p.tiles_per_split = tps;
@@ -1156,13 +1223,72 @@ void search_k2(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, uint64_t*
   h->g_redo.reserve(nq);
   h->g_redo_idx.reserve(nq);
   h->g_redo_len.reserve(1);
-  k2_rerank_kernel<<<nq, 128, cap * sizeof(uint64_t), s>>>(h->part.p, nsplit, cap, h->k2_meta.p, d_q, h->dim,
+  h->k2_kth.reserve(nq);
+  k2_rerank_kernel<<<nq, 128, cap * sizeof(uint64_t), s>>>(h->part.p, nsplit, cap,
+                                                           reinterpret_cast<const uint32_t*>(h->bound.p),
+                                                           h->k2_meta.p, d_q, h->dim,
                                                            h->metric, h->rank_rows.p, h->rank_id.p,
-                                                           (uint32_t)h->nrank, k, d_ids, d_dist, d_len, h->g_redo.p);
+                                                           (uint32_t)h->nrank, k, d_ids, d_dist, d_len, h->g_redo.p,
+                                                           h->k2_kth.p);
   PXC_CUDA(cudaGetLastError());
   h->ctx->launches += 4;
   check_status_word(h->d_status, h->h_status, s, "flat search (tensor-core screen)");
-  redo_flagged(h, d_q, nq, k, nullptr, d_ids, d_dist, d_len, s);
+  // the unproven queries: the exact range scan, then (on overflow) K1g
+  size_t tb = 0;
+  thrust::counting_iterator<uint32_t> it(0);
+  PXC_CUDA(cub::DeviceSelect::Flagged(nullptr, tb, it, h->g_redo.p, h->g_redo_idx.p, h->g_redo_len.p, (int64_t)nq, s));
+  h->tmp.reserve(std::max<size_t>(tb, 1));
+  PXC_CUDA(cub::DeviceSelect::Flagged(h->tmp.p, tb, it, h->g_redo.p, h->g_redo_idx.p, h->g_redo_len.p, (int64_t)nq, s));
+  PXC_CUDA(cudaMemcpyAsync(h->h_flag, h->g_redo_len.p, sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
+  PXC_CUDA(cudaStreamSynchronize(s));
+  const uint32_t nredo = static_cast<uint32_t>(*h->h_flag);
+  h->last_redo = nredo;
+  h->ctx->launches += 2;
+  if (nredo == 0) return;
+  for (uint32_t b = 0; b < nredo; b += K2_RANGE_BATCH) {
+    const uint32_t nb = std::min(K2_RANGE_BATCH, nredo - b);
+    const uint32_t* idx = h->g_redo_idx.p + b;
+    h->g_redo_q.reserve((size_t)nb * h->dim);
+    h->k2_thr.reserve(nb);
+    h->k2_range.reserve((size_t)nb * K2_RANGE_CAP);
+    h->k2_range_cnt.reserve(nb);
+    h->k2_ovf.reserve(nb);
+    gather_queries_kernel<<<nb, 128, 0, s>>>(d_q, idx, h->dim, h->g_redo_q.p);
+    gather_f32_kernel<<<grid1d(nb, 256), 256, 0, s>>>(h->k2_kth.p, idx, nb, h->k2_thr.p);
+    PXC_CUDA(cudaMemsetAsync(h->k2_range_cnt.p, 0, nb * sizeof(uint32_t), s));
+    k2_range_kernel<<<dim3(grid1d(h->nrank, 128), (nb + K2_RANGE_Q - 1) / K2_RANGE_Q), 128, 0, s>>>(
+        h->g_redo_q.p, h->k2_thr.p, nb, h->rank_rows.p, (uint32_t)h->nrank, h->dim, h->metric, h->k2_range.p,
+        h->k2_range_cnt.p);
+    PXC_CUDA(cudaFuncSetAttribute(k2_range_finish_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)(K2_RANGE_CAP * sizeof(uint64_t))));
+    k2_range_finish_kernel<<<nb, 256, K2_RANGE_CAP * sizeof(uint64_t), s>>>(
+        h->k2_range.p, h->k2_range_cnt.p, idx, k, h->rank_id.p, d_ids, d_dist, d_len, h->k2_ovf.p);
+    PXC_CUDA(cudaGetLastError());
+    h->ctx->launches += 4;
+    // overflowing queries (ties or near-ties beyond the collection's capacity): K1g
+    h->k2_ovf_idx.reserve(nb);
+    h->k2_ovf_len.reserve(1);
+    tb = 0;
+    PXC_CUDA(cub::DeviceSelect::Flagged(nullptr, tb, idx, h->k2_ovf.p, h->k2_ovf_idx.p, h->k2_ovf_len.p, (int64_t)nb, s));
+    h->tmp.reserve(std::max<size_t>(tb, 1));
+    PXC_CUDA(cub::DeviceSelect::Flagged(h->tmp.p, tb, idx, h->k2_ovf.p, h->k2_ovf_idx.p, h->k2_ovf_len.p, (int64_t)nb, s));
+    PXC_CUDA(cudaMemcpyAsync(h->h_flag, h->k2_ovf_len.p, sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
+    PXC_CUDA(cudaStreamSynchronize(s));
+    const uint32_t novf = static_cast<uint32_t>(*h->h_flag);
+    h->ctx->launches += 2;
+    if (novf == 0) continue;
+    h->g_redo_q.reserve((size_t)novf * h->dim);
+    h->g_redo_ids.reserve((size_t)novf * k);
+    h->g_redo_dist.reserve((size_t)novf * k);
+    h->g_redo_len.reserve(novf);
+    gather_queries_kernel<<<novf, 128, 0, s>>>(d_q, h->k2_ovf_idx.p, h->dim, h->g_redo_q.p);
+    PXC_CUDA(cudaGetLastError());
+    search_generic(h, h->g_redo_q.p, novf, k, nullptr, h->g_redo_ids.p, h->g_redo_dist.p, h->g_redo_len.p, s);
+    scatter_results_kernel<<<novf, 128, 0, s>>>(h->g_redo_ids.p, h->g_redo_dist.p, h->g_redo_len.p,
+                                                h->k2_ovf_idx.p, k, d_ids, d_dist, d_len);
+    PXC_CUDA(cudaGetLastError());
+    h->ctx->launches += 2;
+  }
 }
 
 void search_device(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, const uint64_t* d_bitmap,
@@ -1573,6 +1699,7 @@ extern "C" pxc_status pxc_flat_search_noalloc(pxc_flat* h, const float* d_querie
     flat_tc::Params p;
     p.norms = h->op_norm.p;
     p.qcoef = nullptr;
+    p.qdelta = nullptr;
     p.bound = reinterpret_cast<uint32_t*>(bound);
     p.done_count = done;
     p.done_list = done + nqt;

@@ -100,6 +100,8 @@ struct U8Scan {
   __host__ __device__ static T unpack(uint32_t key) { return static_cast<int32_t>(key - R_OFFSET); }
   __device__ static T next_up(T r) { return r + 1; }
   __device__ static T value(uint32_t acc, T h, float) { return h - 2 * static_cast<int32_t>(acc); }
+  // the value shared as the pruning bound: the list's k-th
+  __device__ static T publish(T kth, T, float) { return kth; }
   __device__ static uint32_t idesc() { return sm100::idesc_u8_s32(UM, BN); }
   __device__ static void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
     sm100::mma_i8(d, a, b, id, acc);
@@ -115,6 +117,10 @@ struct F16Scan {
   __host__ __device__ static T unpack(uint32_t key) { return key_to_float(key); }
   __device__ static T next_up(T r) { return key_to_float(order_key(r) + 1u); }
   __device__ static T value(uint32_t acc, T h, float c) { return fmaf(__uint_as_float(acc), c, h); }
+  // the value shared as the pruning bound: the list's last entry, or its k-th
+  // plus the query's margin when that is smaller (rows behind it cannot
+  // change a provable answer)
+  __device__ static T publish(T kth, T last, float delta) { return fminf(last, kth + delta); }
   __device__ static uint32_t idesc() { return idesc_f16_f32(UM, BN); }
   __device__ static void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
     mma_f16(d, a, b, id, acc);
@@ -130,13 +136,14 @@ __host__ __device__ constexpr size_t norm_bytes() {
 struct Params {
   const void* norms;       // per-rank row term (P::T): ||x||^2 for K1; padding ranks hold P::big()
   const float* qcoef;      // K2: per-query factor c_q (nullptr for K1)
+  const float* qdelta;     // K2: per-query margin added to the k-th value before it is shared (nullptr: 0)
   uint32_t* bound;         // [nq_pad] shared pruning bound per query, as a packed key (P::pack)
   uint32_t* done_count;    // [nqt] finished splits per query tile
   uint32_t* done_list;     // [nqt][nsplit] finished split ids in finishing order (~0u = not yet)
   uint64_t* out_part;      // [nq_pad][nsplit][KT] packed P::pack(r)<<32 | rank
   uint32_t* status;        // device error word
   uint32_t nq;
-  uint32_t k;              // the list position whose value is shared as the pruning bound (<= KT)
+  uint32_t k;              // the list position whose value is shared as the pruning bound (<= KT, see P::publish)
   uint32_t kblocks;        // K bytes / 128
   uint32_t ntiles;         // nrank_pad / BN
   uint32_t tiles_per_split;
@@ -469,6 +476,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint2* wfifo = sFifo + ew * P::FIFO_SLOTS * 32;  // this warp's deferred-insertion FIFO
     uint32_t fifo_cnt = 0;
     const float coef = (p.qcoef != nullptr && q < p.nq) ? p.qcoef[q] : 0.0f;
+    const float delta = (p.qdelta != nullptr && q < p.nq) ? p.qdelta[q] : 0.0f;
     T lr[KT];
     uint32_t lk[KT];
 #pragma unroll
@@ -553,8 +561,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       T kth = lr[KT - 1];
 #pragma unroll
       for (int i = 0; i < KT; ++i) kth = (i + 1 == (int)p.k) ? lr[i] : kth;
-      if (kth < published) {
-        published = kth;
+      const T pub = P::publish(kth, lr[KT - 1], delta);
+      if (pub < published) {
+        published = pub;
         atomicMin(bound_ptr, P::pack(published));
       }
       shared_bound = min(shared_bound, fresh_bound);

@@ -6,7 +6,7 @@ failures of its own kernels.
 
 * two flat handles on one context searched from two host threads on the
   tensor-core scan (each handle owns its device error word);
-* one flat handle (fp32 scan, which returns before its kernels finish) and one
+* one flat handle (fp32 scan, k = 30, which returns before its kernels finish) and one
   IVF-PQ handle searched on two CUDA streams with interleaved calls: each
   handle passes its scratch from one search to the next in stream order.
 """
@@ -94,13 +94,13 @@ def test_interleaved_searches_on_two_streams_equal_serial():
     data = fixtures.sphere_blobs(n, dim, 64, 31, 32, 0.1)  # not integers: the fp32 flat scan
     batches = [fixtures.sphere_blobs(300 + 37 * i, dim, 64, 31, 40 + i, 0.1) for i in range(6)]
     flat = FlatIndex.from_array(VectorSpace(dim, Metric.EUCLIDEAN), data)
-    assert flat.device_path() == 0
+    kf = 30  # beyond the f16 screen's k: the fp32 scan, which returns before its kernels finish
     cent, books, list_of, codes, _ = pxo.ivfpq_train(data, 64, 8, 4, 8000, 0x31)
     ivf = IvfPqIndex(dim, 64, 8, Metric.EUCLIDEAN)
     ivf.from_parts(cent, books)
     ivf.set_store(data)
     ivf.set_codes(list_of, codes)
-    serial_flat = [flat.search_prepared_batch(b, 10) for b in batches]
+    serial_flat = [flat.search_prepared_batch(b, kf) for b in batches]
     serial_ivf = [ivf.search_batch(b, 10, 8, 200) for b in batches]
     streams = [torch.cuda.Stream(), torch.cuda.Stream()]
     dqs = [torch.from_numpy(b).cuda() for b in batches]
@@ -108,7 +108,7 @@ def test_interleaved_searches_on_two_streams_equal_serial():
     out_flat, out_ivf = [], []
     for i, dq in enumerate(dqs):  # consecutive searches alternate between the two streams
         s = streams[i % 2]
-        out_flat.append(_flat_device(flat, dq, 10, s, torch))
+        out_flat.append(_flat_device(flat, dq, kf, s, torch))
         out_ivf.append(_ivf_device(ivf, dq, 10, 8, 200, streams[(i + 1) % 2], torch))
     torch.cuda.synchronize()
     for i in range(len(batches)):

@@ -113,7 +113,7 @@ def test_c1_quickstart_bit_exact():
     queries = space.prepare_batch(data[::50])
     got = idx.search_prepared_batch(queries, 10)
     ref = pxo.flat_search(pxo.prepare(pxo.COSINE, data), queries, 10, pxo.COSINE)
-    assert idx.device_path() == 0
+    assert idx.device_path() == 2  # the f16 screen; unproven queries run on the fp32 scan
     _assert_same(got, ref, 100)
     golden = json.loads((Path(__file__).parent / "golden" / "c1_top10.json").read_text())
     assert [list(map(int, r)) for r in got[0]] == golden["ids"]
