@@ -51,6 +51,15 @@ def parse():
     p.add_argument("--flat-scaling", choices=["weak", "strong"], default="weak",
                    help="flat at N>1: weak = N x --nq queries per step over the row-sharded database (each GPU "
                         "scans the equivalent of --nq queries x --n rows); strong = --nq queries split N ways")
+    p.add_argument("--data", choices=["u8", "real"], default="u8",
+                   help="flat: C2's integer rows (u8, the exact u8 tensor-core scan) or the same blobs unrounded "
+                        "(real, the f16 tensor-core screen + exact re-rank)")
+    p.add_argument("--metric", choices=["euclidean", "cosine"], default="euclidean")
+    p.add_argument("--no-extras", action="store_true",
+                   help="flat at N=1: skip the sub-records of the other configurations (C2 k=100, real-valued "
+                        "C2, C3, C4, C5), each measured by its own bench.py run")
+    p.add_argument("--extras-steps", type=int, default=5)
+    p.add_argument("--parity-queries", type=int, default=96, help="N>1: queries checked against the oracle")
     p.add_argument("--sq-n", type=int, default=6_250_000, help="rows per GPU (C5: 50M over 8 GPUs)")
     p.add_argument("--ivf-n", type=int, default=20_000_000)
     p.add_argument("--ivf-nlist", type=int, default=16384)
@@ -120,27 +129,31 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(rows)}
 
 
-def cpu_baseline(db: np.ndarray, queries: np.ndarray, k: int, seconds: float, gpu_ids=None) -> dict:
+def cpu_baseline(db: np.ndarray, queries: np.ndarray, k: int, seconds: float, gpu_ids=None, gpu_dist=None,
+                 metric: int = 0) -> dict:
     """The oracle port of FlatIndex::search on all host cores, on a bounded query sample; its answers for
-    the sample are also compared with the GPU's (gpu_ids: the GPU's ids for every query)."""
+    the sample are also compared with the GPU's, ids and f32 distance bits (gpu_ids / gpu_dist: the GPU's
+    answer for every query). `db` and `queries` are prepared (cosine: normalised)."""
     from oracle import pxo
 
     threads = os.cpu_count() or 1
     batch = max(threads, 8)
-    pxo.flat_search(db, queries[:batch], k, pxo.EUCLIDEAN, nthreads=threads)  # warm
+    pxo.flat_search(db, queries[:batch], k, metric, nthreads=threads)  # warm
     done, t0, same = 0, time.perf_counter(), 0
     while time.perf_counter() - t0 < seconds and done + batch <= len(queries):
-        ref_ids, _, ref_len = pxo.flat_search(db, queries[done:done + batch], k, pxo.EUCLIDEAN, nthreads=threads)
+        ref_ids, ref_d, ref_len = pxo.flat_search(db, queries[done:done + batch], k, metric, nthreads=threads)
         if gpu_ids is not None:
             for i in range(batch):
-                same += int(np.array_equal(gpu_ids[done + i, :ref_len[i]], ref_ids[i, :ref_len[i]]))
+                n_ = ref_len[i]
+                same += int(np.array_equal(gpu_ids[done + i, :n_], ref_ids[i, :n_]) and
+                            np.array_equal(gpu_dist[done + i, :n_].view(np.uint32), ref_d[i, :n_].view(np.uint32)))
         done += batch
     el = time.perf_counter() - t0
     out = {"value": done / el, "unit": "queries/s", "cores": threads, "kind": "port",
            "sample": f"{done} of the {len(queries)} queries against the full {db.shape[0]:,}-row database "
                      f"({el:.1f} s, C++ oracle restating FlatIndex::search, one query per thread at a time)"}
     if gpu_ids is not None:
-        out["parity"] = {"queries": done, "identical_ids": same}
+        out["parity"] = {"queries": done, "identical_ids_and_distance_bits": same}
     return out
 
 
@@ -610,9 +623,9 @@ def run_sq(args):
     dists = torch.empty((nq, k), dtype=torch.float32, device=dev)
     lens = torch.empty(nq, dtype=torch.int32, device=dev)
     if world > 1:
-        g_ids = torch.empty((world, nq, k), dtype=torch.int64, device=dev)
-        g_d = torch.empty((world, nq, k), dtype=torch.float32, device=dev)
-        g_l = torch.empty((world, nq), dtype=torch.int32, device=dev)
+        from proxima_b200.sharded import init_comm
+
+        init_comm(ctx, timeout_ms=120_000)
         m_ids = torch.empty((nq, k), dtype=torch.int64, device=dev)
         m_d = torch.empty((nq, k), dtype=torch.float32, device=dev)
         m_l = torch.empty(nq, dtype=torch.int32, device=dev)
@@ -621,11 +634,8 @@ def run_sq(args):
     def step(q_ptr):
         N.call("pxc_sq_search_device", idx.handle, q_ptr, nq, k, F, None, *idx._ranges(flt), ids.data_ptr(),
                dists.data_ptr(), lens.data_ptr(), sp)
-        if world > 1:
-            dist.all_gather_into_tensor(g_ids, ids)
-            dist.all_gather_into_tensor(g_d, dists)
-            dist.all_gather_into_tensor(g_l, lens)
-            N.call("pxc_topk_merge", ctx.handle, g_ids.data_ptr(), g_d.data_ptr(), g_l.data_ptr(), world, nq, k, k,
+        if world > 1:  # one packed allgather over the library's communicator, then the merge
+            N.call("pxc_topk_exchange", ctx.handle, ids.data_ptr(), dists.data_ptr(), lens.data_ptr(), nq, k, k,
                    m_ids.data_ptr(), m_d.data_ptr(), m_l.data_ptr(), sp)
 
     N.call("pxc_ctx_set_profiling", ctx.handle, 1)
@@ -718,7 +728,8 @@ def run_sq(args):
                            "fallback_queries": fallback,
                            "l2": "flushed (256 MiB write) between timed steps; codes 4.8 GB per GPU",
                            "generate_s": round(t_gen, 2), "build_s": round(t_build, 2),
-                           "parallelism": "single GPU" if world == 1 else f"row shards x{world} + NCCL allgather"},
+                           "parallelism": "single GPU" if world == 1 else
+                           f"row shards x{world}; the library's NCCL communicator: one packed allgather, merge"},
                 "clocks": clocks, "gpu_launches": int(launches),
                 "e2e": {"value": e2e_qps, "unit": "queries/s", "h2d_bytes_per_step": nq * dim * 4,
                         "d2h_bytes_per_step": nq * k * 12 + nq * 4},
@@ -762,6 +773,53 @@ def sq_cpu_baseline(host, years, queries, gpu_ids, k, seconds):
             "parity": {"queries": done, "identical_ids": same}}
 
 
+def flat_rows(args, lo: int, hi: int) -> np.ndarray:
+    from proxima_b200 import fixtures
+
+    gen = fixtures.blobs_u8 if args.data == "u8" else fixtures.blobs_f32
+    return gen(hi - lo, args.dim, 1024, fixtures.C2_CENTRES, fixtures.C2_BASE, row_begin=lo)
+
+
+def flat_queries(args, nq: int) -> np.ndarray:
+    from proxima_b200 import fixtures
+
+    gen = fixtures.blobs_u8 if args.data == "u8" else fixtures.blobs_f32
+    return gen(nq, args.dim, 1024, fixtures.C2_CENTRES, fixtures.C2_QUERIES)
+
+
+def run_extras(args) -> dict:
+    """Sub-records of the other configurations, each from its own bench.py run (fresh process, the same GPU):
+    C2 at k=100, real-valued C2 (euclidean and cosine: the f16 tensor-core screen), C3, C4 and C5."""
+    runs = {
+        "c2_k100": ["--workload", "flat", "--k", "100"],
+        "c2_real_euclidean": ["--workload", "flat", "--data", "real"],
+        "c2_real_cosine": ["--workload", "flat", "--data", "real", "--metric", "cosine"],
+        "c3_kmeans": ["--workload", "kmeans"],
+        "c4_ivfpq": ["--workload", "ivfpq"],
+        "c5_sq": ["--workload", "sq"],
+    }
+    out = {}
+    for name, extra in runs.items():
+        cmd = [sys.executable, str(ROOT / "bench.py"), "--gpus", "1", "--steps", str(args.extras_steps),
+               "--warmup", "3", "--no-extras", "--cpu-seconds", "6", *extra]
+        t0 = time.perf_counter()
+        try:
+            proc = subprocess.run(cmd, capture_output=True, text=True, timeout=900,
+                                  env=dict(os.environ, RANK="0", LOCAL_RANK=os.environ.get("LOCAL_RANK", "0"),
+                                           WORLD_SIZE="1"))
+            line = None
+            for ln in proc.stdout.splitlines():
+                if ln.startswith("{"):
+                    line = json.loads(ln)
+            if line is None:
+                line = {"error": f"exit {proc.returncode}: {proc.stderr.strip().splitlines()[-1:]}"}
+        except subprocess.TimeoutExpired:
+            line = {"error": "timed out after 900 s"}
+        line["wall_s"] = round(time.perf_counter() - t0, 1)
+        out[name] = line
+    return out
+
+
 def main():
     args = parse()
     if args.workload == "sq":
@@ -790,22 +848,27 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
 
     from proxima_b200 import _native as N
-    from proxima_b200 import fixtures
+    from proxima_b200.core import Metric, VectorSpace
     from proxima_b200.index import Context
+    from proxima_b200.sharded import init_comm
 
     n, dim, k = args.n, args.dim, args.k
+    metric = Metric.COSINE if args.metric == "cosine" else Metric.EUCLIDEAN
+    space = VectorSpace(dim, metric)
     # Weak scaling keeps each GPU's scan at (--nq queries x --n rows): the rows are split N ways and the
     # query batch grows N-fold (the first N x --nq queries of the same seeded stream).
     weak = world > 1 and args.flat_scaling == "weak"
     nq = args.nq * world if weak else args.nq
     lo, hi = rank * n // world, (rank + 1) * n // world
-    shard = fixtures.blobs_u8(hi - lo, dim, 1024, fixtures.C2_CENTRES, fixtures.C2_BASE, row_begin=lo)
-    queries = fixtures.c2_queries(nq, dim)
+    shard = space.prepare_batch(flat_rows(args, lo, hi))
+    queries = space.prepare_batch(flat_queries(args, nq))
 
     ctx = Context(local)
     lib = N.load()
+    if world > 1:
+        init_comm(ctx, timeout_ms=120_000)  # the library's NCCL communicator over the ranks
     h = N.vp()
-    N.call("pxc_flat_create", ctx.handle, dim, 0, C.byref(h))
+    N.call("pxc_flat_create", ctx.handle, dim, int(metric), C.byref(h))
     gids = np.arange(lo, hi, dtype=np.uint64)
     N.call("pxc_flat_sync", h, N.ptr(shard), N.ptr(gids), None, 0, hi - lo)
     path = lib.pxc_flat_path(h)
@@ -818,24 +881,12 @@ def main():
     ids = torch.empty((nq, k), dtype=torch.int64, device=dev)
     dists = torch.empty((nq, k), dtype=torch.float32, device=dev)
     lens = torch.empty(nq, dtype=torch.int32, device=dev)
-    if world > 1:
-        g_ids = torch.empty((world, nq, k), dtype=torch.int64, device=dev)
-        g_d = torch.empty((world, nq, k), dtype=torch.float32, device=dev)
-        g_l = torch.empty((world, nq), dtype=torch.int32, device=dev)
-        m_ids = torch.empty((nq, k), dtype=torch.int64, device=dev)
-        m_d = torch.empty((nq, k), dtype=torch.float32, device=dev)
-        m_l = torch.empty(nq, dtype=torch.int32, device=dev)
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MiB > 126 MB L2
+    entry = "pxc_flat_search_sharded" if world > 1 else "pxc_flat_search_device"
 
     def step(q_ptr):
-        N.call("pxc_flat_search_device", h, q_ptr, nq, k, None, ids.data_ptr(), dists.data_ptr(),
-               lens.data_ptr(), sp)
-        if world > 1:
-            dist.all_gather_into_tensor(g_ids, ids)
-            dist.all_gather_into_tensor(g_d, dists)
-            dist.all_gather_into_tensor(g_l, lens)
-            N.call("pxc_topk_merge", ctx.handle, g_ids.data_ptr(), g_d.data_ptr(), g_l.data_ptr(), world, nq, k, k,
-                   m_ids.data_ptr(), m_d.data_ptr(), m_l.data_ptr(), sp)
+        # N > 1: local search, one packed NCCL allgather, merge (inside the library)
+        N.call(entry, h, q_ptr, nq, k, None, ids.data_ptr(), dists.data_ptr(), lens.data_ptr(), sp)
 
     N.call("pxc_ctx_set_profiling", ctx.handle, 1)
     for _ in range(max(3, args.warmup)):
@@ -851,7 +902,7 @@ def main():
     sampler.start()
     launches0 = lib.pxc_ctx_launch_count(ctx.handle)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    scan_ms = []
+    scan_ms, redone = [], 0
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
@@ -861,6 +912,7 @@ def main():
         step(q_dev.data_ptr())
         ev[i][1].record(stream)
         scan_ms.append(lib.pxc_flat_last_scan_ms(h))
+        redone += lib.pxc_flat_last_redone(h)
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
@@ -873,6 +925,8 @@ def main():
         dist.all_reduce(scan_mean, op=dist.ReduceOp.MAX)
     ms_per_step = total_ms.item() / args.steps
     clocks = sampler.stop()
+    res_ids = ids.cpu().numpy().view(np.uint64)
+    res_d = dists.cpu().numpy()
 
     # ---- e2e: host buffers in, host results out, every step ----
     out_ids = torch.empty((nq, k), dtype=torch.int64).pin_memory()
@@ -889,9 +943,9 @@ def main():
         else:
             qd = q_host.to(dev, non_blocking=True)
             step(qd.data_ptr())
-            out_ids.copy_(m_ids, non_blocking=True)
-            out_d.copy_(m_d, non_blocking=True)
-            out_l.copy_(m_l, non_blocking=True)
+            out_ids.copy_(ids, non_blocking=True)
+            out_d.copy_(dists, non_blocking=True)
+            out_l.copy_(lens, non_blocking=True)
             torch.cuda.synchronize(dev)
 
     for _ in range(2):
@@ -907,51 +961,77 @@ def main():
     if world > 1:
         dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
     e2e_qps = nq * e2e_steps / e2e_s.item()
-
-    if rank == 0:
-        hbm, bf16, src = peaks()
-        # K1 is u8 x u8 -> s32 on tcgen05 (kind::i8); B200's dense int8 rate is twice its dense bf16 rate.
-        peak_tops = 2.0 * bf16 if path == 1 else None
-        ops = 2.0 * (hi - lo) * dim * nq  # per launch of the scan kernel on this rank
-        achieved = ops / (scan_mean.item() / 1e3) / 1e12 if scan_mean.item() > 0 else None
-        traffic = None
-        tf = ROOT / "profiles" / "traffic.json"
-        if tf.exists():
-            t = json.loads(tf.read_text()).get("flat_u8_kernel_c2_bytes_per_launch")
-            if t and world == 1:
-                traffic = t
-        roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_tops, "unit": "TOPS",
-                    "frac": (achieved / peak_tops) if (achieved and peak_tops) else None, "traffic": traffic,
-                    "kernel": "flat_u8_kernel (K1)" if path == 1 else "dist_chunk_kernel + select (K1g)",
-                    "kernel_ms": scan_mean.item(),
-                    "peak_source": f"2 x dense bf16 {src} = dense int8 rate",
-                    "algorithmic_ops_per_launch": ops}
-        line = {"metric": METRIC.replace("k=10", f"k={k}"), "value": nq / (ms_per_step / 1e3), "unit": "queries/s",
-                "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-                "scaling": "weak" if weak else "strong", "vs_baseline": None,
-                "dtype": "u8" if path == 1 else "f32",
-                "data": "synthetic",
-                "config": dict(CONFIG, queries=nq, k=k, l2="flushed (256 MiB write) between timed steps",
-                               parallelism=(f"row shards x{world} + NCCL allgather of k candidates per query"
-                                            + (f"; {args.nq:,} queries per GPU per step, so each GPU scans "
-                                               f"{args.nq:,} x {n:,} query-row pairs as on one GPU" if weak else ""))
-                               if world > 1 else "single GPU",
-                               scan_path=("fp32 reference order" if path != 1 else "tensor-core u8 (exact)"
-                                          if k <= 32 else "tensor-core u8 over row groups, merged and proven exact"
-                                          if k <= 128 else "fp32 reference order")),
-                "clocks": clocks, "gpu_launches": int(launches),
-                "e2e": {"value": e2e_qps, "unit": "queries/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-                "roofline": roofline}
-        if world == 1 and not args.no_cpu_baseline:
-            db = shard
-            gpu_ids = ids.cpu().numpy().view(np.uint64)
-            line["cpu_baseline"] = cpu_baseline(db, queries, k, args.cpu_seconds, gpu_ids)
-        print(json.dumps(line), flush=True)
     lib.pxc_flat_destroy(h)
     ctx.close()
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
+
+    if rank != 0:
+        return
+    hbm, bf16, src = peaks()
+    # K1 is u8 x u8 -> s32 on tcgen05 (kind::i8): dense int8 = 2 x dense bf16. K2's screen is
+    # f16 x f16 -> f32 (kind::f16): the dense bf16/f16 rate.
+    peak = 2.0 * bf16 if path == 1 else bf16 if path == 2 else None
+    ops = 2.0 * (hi - lo) * dim * nq  # per launch of the scan kernel on this rank
+    achieved = ops / (scan_mean.item() / 1e3) / 1e12 if scan_mean.item() > 0 else None
+    traffic, traffic_src = None, None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists() and world == 1 and path == 1 and k <= 32 and n == 1_000_000 and nq == 10_000:
+        t = json.loads(tf.read_text()).get("flat_u8_kernel_c2_bytes_per_launch")
+        if t:
+            traffic, traffic_src = t, "ncu dram__bytes_read.sum + dram__bytes_write.sum of this launch shape " \
+                                      "(profiles/flat_u8_kernel_c2.md)"
+    kernel = {1: "flat_scan_kernel<KT, U8Scan> (K1)", 2: "flat_scan_kernel<32, F16Scan> (K2 screen)"}.get(
+        path, "dist_chunk_kernel + select (K1g)")
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peak,
+                "unit": "TOPS" if path == 1 else "TFLOP/s",
+                "frac": (achieved / peak) if (achieved and peak) else None, "traffic": traffic,
+                "traffic_source": traffic_src, "kernel": kernel, "kernel_ms": scan_mean.item(),
+                "peak_source": (f"2 x dense bf16 {src} = dense int8 rate" if path == 1 else
+                                f"dense bf16 {src} = dense f16 rate"),
+                "algorithmic_ops_per_launch": ops}
+    data_desc = ("integers in [0,255], 1,024 blobs, sigma 20" if args.data == "u8"
+                 else "real-valued: the same 1,024 blobs, sigma 20, unrounded")
+    workload = (f"C2 exact flat search: {n:,} x {dim} f32 ({data_desc}), {nq:,} queries, k={k}, {args.metric}")
+    scan_path = {1: ("tensor-core u8 (exact)" if k <= 32 else "tensor-core u8 over row groups, merged and proven exact"),
+                 2: "tensor-core f16 screen of 32 per query, exact f32 re-rank, proven per query"}.get(
+        path, "fp32 reference order")
+    line = {"metric": METRIC.replace("k=10", f"k={k}").replace("euclidean", args.metric) +
+            ("" if args.data == "u8" else ", real-valued rows"),
+            "value": nq / (ms_per_step / 1e3), "unit": "queries/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak" if weak else "strong", "vs_baseline": None,
+            "dtype": {1: "u8", 2: "f16 screen + f32 re-rank"}.get(path, "f32"),
+            "data": "synthetic",
+            "config": dict(CONFIG, workload=workload, n=n, queries=nq, k=k, metric=args.metric, rows=args.data,
+                           l2="flushed (256 MiB write) between timed steps",
+                           parallelism=(f"row shards x{world}; the library's NCCL communicator: one packed "
+                                        f"allgather of k candidates per query, device merge"
+                                        + (f"; {args.nq:,} queries per GPU per step, so each GPU scans "
+                                           f"{args.nq:,} x {n:,} query-row pairs as on one GPU" if weak else ""))
+                           if world > 1 else "single GPU",
+                           scan_path=scan_path, unproven_queries_rescanned=redone),
+            "clocks": clocks, "gpu_launches": int(launches),
+            "e2e": {"value": e2e_qps, "unit": "queries/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "roofline": roofline}
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(shard, queries, k, args.cpu_seconds, res_ids, res_d, int(metric))
+    elif world > 1:
+        # the merged answer of the sampled queries against the oracle over the whole database
+        from oracle import pxo
+
+        full = space.prepare_batch(flat_rows(args, 0, n))
+        samp = np.linspace(0, nq - 1, num=min(args.parity_queries, nq)).astype(np.int64)
+        ri, rd, rl = pxo.flat_search(full, queries[samp], k, int(metric))
+        same = sum(int(np.array_equal(res_ids[q, :rl[i]], ri[i, :rl[i]]) and
+                       np.array_equal(res_d[q, :rl[i]].view(np.uint32), rd[i, :rl[i]].view(np.uint32)))
+                   for i, q in enumerate(samp))
+        line["config"]["parity_sample"] = {"queries": len(samp), "identical_ids_and_distance_bits": same,
+                                           "against": f"oracle FlatIndex::search over all {n:,} rows"}
+    if world == 1 and not args.no_extras:
+        line["extras"] = run_extras(args)
+    print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

@@ -78,7 +78,8 @@ uint32_t pxc_abi_version(void);
  * Replaces nothing in the reference (which is single-threaded CPU code); it
  * owns the device state every handle below is created on. Exactly one device
  * per context: multi-GPU runs use one process (and one context) per GPU and
- * exchange candidates with NCCL (see pxc_topk_merge). */
+ * exchange candidates over the context's NCCL communicator
+ * (pxc_ctx_init_comm, pxc_flat_search_sharded, pxc_topk_exchange). */
 typedef struct pxc_ctx pxc_ctx;
 pxc_status pxc_ctx_create(const int* devices, int n_devices, pxc_ctx** out, pxc_error* err);
 void pxc_ctx_destroy(pxc_ctx* ctx);
@@ -176,6 +177,44 @@ uint32_t pxc_flat_last_redone(const pxc_flat* h);
 pxc_status pxc_flat_search_noalloc(pxc_flat* h, const float* d_queries, uint32_t nq, uint32_t k,
                                    uint64_t* d_out_ids, float* d_out_dist, uint32_t* d_out_len,
                                    void* stream, pxc_error* err);
+
+/* ---- multi-GPU: the context's communicator and the candidate exchange ----
+ * The reference is single-process; this is the data-parallel form of its
+ * search: every rank holds a shard of the rows (with their global
+ * VectorIds), searches all queries on it, and one NCCL allgather over NVLink
+ * carries the k candidates per query to every rank, where they are merged by
+ * (total_cmp(distance), id) (TopK::push over the union,
+ * crates/proxima-core/src/topk.rs:119-138). NCCL is loaded at run time
+ * (libnccl.so.2); without it these entry points return PXC_CONFIGURATION. */
+#define PXC_COMM_ID_BYTES 128
+/* A fresh communicator id (ncclGetUniqueId). Rank 0 creates it and hands the
+ * 128 bytes to every rank by the job's own means (MPI, a TCP store, ...). */
+pxc_status pxc_comm_unique_id(uint8_t out[PXC_COMM_ID_BYTES], pxc_error* err);
+/* Joins the context to the job's communicator (ncclCommInitRank; collective
+ * over the ranks). nranks == 1 needs no id traffic and makes the exchanges
+ * below local merges. timeout_ms bounds every later wait on the exchange: on
+ * expiry, or an asynchronous NCCL error, the communicator is aborted and the
+ * call returns PXC_TIMEOUT / PXC_DEVICE. Every rank must issue the exchanges
+ * in the same order. */
+pxc_status pxc_ctx_init_comm(pxc_ctx* ctx, const uint8_t id[PXC_COMM_ID_BYTES], int32_t nranks, int32_t rank,
+                             uint32_t timeout_ms, pxc_error* err);
+int32_t pxc_ctx_comm_size(const pxc_ctx* ctx);
+int32_t pxc_ctx_comm_rank(const pxc_ctx* ctx);
+/* FlatIndex::search over a row-sharded store: this rank's handle holds its
+ * shard (global VectorIds as ids); every rank passes the same prepared
+ * queries. Local exact search, one packed allgather (ids, distances, lengths
+ * of k candidates per query in a single buffer), merge: every rank receives
+ * the global top-k, equal to one unsharded search. DEVICE buffers; returns
+ * after the exchange has finished. nranks * k <= 8192. */
+pxc_status pxc_flat_search_sharded(pxc_flat* h, const float* d_queries, uint32_t nq, uint32_t k,
+                                   const uint64_t* d_bitmap, uint64_t* d_out_ids, float* d_out_dist,
+                                   uint32_t* d_out_len, void* stream, pxc_error* err);
+/* The same exchange for any local top-k_in lists (nq x k_in ids and
+ * distances, nq lengths; DEVICE buffers), e.g. an SQ or IVF-PQ shard's answer:
+ * allgather over the communicator and merge into the global top-k. */
+pxc_status pxc_topk_exchange(pxc_ctx* ctx, const uint64_t* d_ids, const float* d_dist, const uint32_t* d_lens,
+                             uint32_t nq, uint32_t k_in, uint32_t k, uint64_t* d_out_ids, float* d_out_dist,
+                             uint32_t* d_out_len, void* stream, pxc_error* err);
 
 /* ---- multi-GPU merge ----
  * After each rank searched its own row shard, an allgather leaves `nparts`

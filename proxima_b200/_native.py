@@ -105,6 +105,14 @@ SIGNATURES: dict[str, tuple] = {
     "pxc_topk_merge": (C.c_int32, [vp, vp, vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
                                    vp, vp, vp, vp, C.POINTER(PxcError)]),
     "pxc_ctx_set_option": (C.c_int32, [vp, C.c_char_p, C.c_int64, C.POINTER(PxcError)]),
+    "pxc_comm_unique_id": (C.c_int32, [vp, C.POINTER(PxcError)]),
+    "pxc_ctx_init_comm": (C.c_int32, [vp, vp, C.c_int32, C.c_int32, C.c_uint32, C.POINTER(PxcError)]),
+    "pxc_ctx_comm_size": (C.c_int32, [vp]),
+    "pxc_ctx_comm_rank": (C.c_int32, [vp]),
+    "pxc_flat_search_sharded": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, vp, vp, vp, vp, vp,
+                                            C.POINTER(PxcError)]),
+    "pxc_topk_exchange": (C.c_int32, [vp, vp, vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, vp, vp, vp, vp,
+                                      C.POINTER(PxcError)]),
     "pxc_rng_seed_from_u64": (C.c_int32, [C.c_uint64, C.POINTER(PxcRng), C.POINTER(PxcError)]),
     "pxc_rng_next_u32": (C.c_int32, [C.POINTER(PxcRng), vp, C.c_uint64, C.POINTER(PxcError)]),
     "pxc_rng_gen_index": (C.c_int32, [C.POINTER(PxcRng), C.c_uint64, C.POINTER(C.c_uint64), C.POINTER(PxcError)]),

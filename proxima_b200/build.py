@@ -67,7 +67,7 @@ def build_cuda(verbose: bool = False) -> Path:
             list(ex.map(_run, jobs))
     out = LIB / "libproxima_cuda.so"
     if _newer(out, objs):
-        _run([NVCC, *ARCH, "-shared", "-o", str(out), *map(str, objs), "-cudart", "static"])
+        _run([NVCC, *ARCH, "-shared", "-o", str(out), *map(str, objs), "-cudart", "static", "-ldl"])
     return out
 
 

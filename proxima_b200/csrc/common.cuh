@@ -145,6 +145,15 @@ struct pxc_ctx {
   // k-means scratch kept between calls (grown on demand, freed with the context)
   void* kmeans_ws = nullptr;
   void (*kmeans_ws_free)(void*) = nullptr;
+  // The NCCL communicator over the ranks of one job (one context per rank;
+  // pxc_ctx_init_comm). Collectives are issued in call order under comm_mu.
+  void* comm = nullptr;  // ncclComm_t
+  int nranks = 1, rank = 0;
+  uint32_t comm_timeout_ms = 60000;
+  std::mutex comm_mu;
+  unsigned char* x_send = nullptr;  // exchange buffers (device), grown on demand
+  unsigned char* x_recv = nullptr;
+  size_t x_send_bytes = 0, x_recv_bytes = 0;
 };
 
 namespace pxc {
@@ -200,4 +209,15 @@ struct DBuf {
 void check_device_status(pxc_ctx* ctx, cudaStream_t s, const char* where);
 // Same for an error word owned by a handle (d_status device, h_status pinned).
 void check_status_word(uint32_t* d_status, uint32_t* h_status, cudaStream_t s, const char* where);
+
+// Candidate exchange over the context's communicator: `send` holds this
+// rank's segment (ids [nq][k_in] u64 | distances [nq][k_in] f32 | lengths [nq]
+// u32, seg_bytes long, 16-byte multiple); one NCCL allgather of the segments,
+// then the (total_cmp, id) merge of every rank's lists into the outputs. Waits
+// (bounded by the context's communicator timeout) for the work to finish.
+size_t exchange_segment_bytes(uint32_t nq, uint32_t k_in);
+void exchange_and_merge(pxc_ctx* ctx, const unsigned char* send, uint32_t nq, uint32_t k_in, uint32_t k,
+                        uint64_t* d_out_ids, float* d_out_dist, uint32_t* d_out_len, cudaStream_t s);
+// The context's send buffer, grown to at least `bytes` (callers hold comm_mu).
+unsigned char* exchange_send_buffer(pxc_ctx* ctx, size_t bytes);
 }  // namespace pxc

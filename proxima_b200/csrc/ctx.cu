@@ -1,11 +1,123 @@
-// ctx.cu — device context and the multi-GPU candidate merge.
+// ctx.cu — device context, the NCCL communicator and the multi-GPU
+// candidate exchange + merge.
+#include <dlfcn.h>
+#include <nccl.h>
+
 #include <algorithm>
+#include <chrono>
 #include <new>
+#include <string>
+#include <thread>
 
 #include "common.cuh"
 #include "topk.cuh"
 
 namespace pxc {
+
+// NCCL is resolved at run time (dlopen of libnccl.so.2, the copy a process
+// such as PyTorch has already loaded, else the system's), so the library
+// loads, and single-GPU use works, without it.
+struct NcclApi {
+  bool ok = false;
+  std::string why;
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
+  ncclResult_t (*comm_async_error)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+static NcclApi load_nccl() {
+  NcclApi a;
+  void* lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+  if (!lib) lib = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+  if (!lib) {
+    a.why = "libnccl.so.2 not found";
+    return a;
+  }
+  auto sym = [&](const char* name) {
+    void* p = dlsym(lib, name);
+    if (!p && a.why.empty()) a.why = std::string("libnccl lacks ") + name;
+    return p;
+  };
+  a.get_unique_id = reinterpret_cast<decltype(a.get_unique_id)>(sym("ncclGetUniqueId"));
+  a.comm_init_rank = reinterpret_cast<decltype(a.comm_init_rank)>(sym("ncclCommInitRank"));
+  a.comm_destroy = reinterpret_cast<decltype(a.comm_destroy)>(sym("ncclCommDestroy"));
+  a.comm_abort = reinterpret_cast<decltype(a.comm_abort)>(sym("ncclCommAbort"));
+  a.comm_async_error = reinterpret_cast<decltype(a.comm_async_error)>(sym("ncclCommGetAsyncError"));
+  a.all_gather = reinterpret_cast<decltype(a.all_gather)>(sym("ncclAllGather"));
+  a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(sym("ncclAllReduce"));
+  a.error_string = reinterpret_cast<decltype(a.error_string)>(sym("ncclGetErrorString"));
+  a.ok = a.why.empty();
+  return a;
+}
+
+static const NcclApi& nccl_api() {
+  static const NcclApi api = load_nccl();
+  return api;
+}
+
+static const NcclApi& nccl() {
+  const NcclApi& api = nccl_api();
+  if (!api.ok) throw make_failure(PXC_CONFIGURATION, 0, 0, "nccl", "NCCL is unavailable: %s", api.why.c_str());
+  return api;
+}
+
+#define PXC_NCCL(expr)                                                                           \
+  do {                                                                                           \
+    ncclResult_t r__ = (expr);                                                                   \
+    if (r__ != ncclSuccess)                                                                      \
+      throw ::pxc::make_failure(PXC_DEVICE, (uint64_t)r__, 0, "nccl", "%s: %s", #expr,          \
+                                ::pxc::nccl().error_string(r__));                              \
+  } while (0)
+
+// Waits for the stream with the communicator's timeout; on expiry or an
+// asynchronous NCCL error the communicator is aborted (later collectives on
+// it fail at once) and PXC_TIMEOUT / PXC_DEVICE is raised.
+static void wait_comm(pxc_ctx* ctx, cudaStream_t s, const char* where) {
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t q = cudaStreamQuery(s);
+    if (q == cudaSuccess) return;
+    if (q != cudaErrorNotReady) PXC_CUDA(q);
+    ncclResult_t ae = ncclSuccess;
+    if (ctx->comm) nccl().comm_async_error(static_cast<ncclComm_t>(ctx->comm), &ae);
+    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
+    if (ae != ncclSuccess || ms > (long long)ctx->comm_timeout_ms) {
+      if (ctx->comm) nccl().comm_abort(static_cast<ncclComm_t>(ctx->comm));
+      ctx->comm = nullptr;
+      ctx->nranks = 1;
+      ctx->rank = 0;
+      if (ae != ncclSuccess)
+        throw make_failure(PXC_DEVICE, (uint64_t)ae, 0, "nccl", "%s: %s (communicator aborted)", where,
+                           nccl().error_string(ae));
+      throw make_failure(PXC_TIMEOUT, ctx->comm_timeout_ms, 0, "nccl",
+                         "%s: the exchange did not finish within %u ms (communicator aborted)", where,
+                         ctx->comm_timeout_ms);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
+
+size_t exchange_segment_bytes(uint32_t nq, uint32_t k_in) {
+  const size_t raw = (size_t)nq * k_in * 12 + (size_t)nq * 4;
+  return (raw + 15) / 16 * 16;
+}
+
+unsigned char* exchange_send_buffer(pxc_ctx* ctx, size_t bytes) {
+  if (bytes > ctx->x_send_bytes) {
+    if (ctx->x_send) cudaFree(ctx->x_send);
+    ctx->x_send = nullptr;
+    ctx->x_send_bytes = 0;
+    PXC_CUDA(cudaMalloc(&ctx->x_send, bytes));
+    ctx->x_send_bytes = bytes;
+  }
+  return ctx->x_send;
+}
 
 void check_device_status(pxc_ctx* ctx, cudaStream_t s, const char* where) {
   check_status_word(ctx->d_status, ctx->h_status, s, where);
@@ -28,12 +140,13 @@ void check_status_word(uint32_t* d_status, uint32_t* h_status, cudaStream_t s, c
 }
 
 // One warp-free block per query: gather the union of the parts, sort by
-// (total_cmp(distance), id), keep k.
+// (total_cmp(distance), id), keep k. Part p's lists start at ids + p *
+// part_stride64 (and dist / lens + p * part_stride32), entry (q, i) at q * k_in + i.
 __global__ void merge_parts_kernel(const uint64_t* __restrict__ ids, const float* __restrict__ dist,
                                    const uint32_t* __restrict__ lens, uint32_t nparts, uint32_t nq,
-                                   uint32_t k_in, uint32_t k, uint32_t cap,
-                                   uint64_t* __restrict__ out_ids, float* __restrict__ out_dist,
-                                   uint32_t* __restrict__ out_len) {
+                                   uint32_t k_in, uint32_t k, uint32_t cap, size_t part_stride64,
+                                   size_t part_stride32, uint64_t* __restrict__ out_ids,
+                                   float* __restrict__ out_dist, uint32_t* __restrict__ out_len) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   uint32_t* skey = reinterpret_cast<uint32_t*>(smem_raw);
   uint64_t* sid = reinterpret_cast<uint64_t*>(smem_raw + cap * sizeof(uint32_t) +
@@ -44,12 +157,12 @@ __global__ void merge_parts_kernel(const uint64_t* __restrict__ ids, const float
   if (threadIdx.x == 0) count = 0;
   __syncthreads();
   for (uint32_t p = 0; p < nparts; ++p) {
-    uint32_t len = min(lens[(size_t)p * nq + q], k_in);
+    uint32_t len = min(lens[p * part_stride32 + q], k_in);
     for (uint32_t i = threadIdx.x; i < len; i += blockDim.x) {
       uint32_t pos = atomicAdd(&count, 1u);
-      size_t src = ((size_t)p * nq + q) * k_in + i;
-      skey[pos] = order_key(dist[src]);
-      sid[pos] = ids[src];
+      const size_t e = (size_t)q * k_in + i;
+      skey[pos] = order_key(dist[p * part_stride32 + e]);
+      sid[pos] = ids[p * part_stride64 + e];
     }
   }
   __syncthreads();
@@ -66,6 +179,46 @@ __global__ void merge_parts_kernel(const uint64_t* __restrict__ ids, const float
     out_dist[(size_t)q * k + i] = key_to_float(skey[i]);
   }
   if (threadIdx.x == 0) out_len[q] = take;
+}
+
+// Shared-memory size and launch of the merge for `total` candidates per query.
+static void launch_merge(const uint64_t* ids, const float* dist, const uint32_t* lens, uint32_t nparts, uint32_t nq,
+                         uint32_t k_in, uint32_t k, size_t stride64, size_t stride32, uint64_t* out_ids,
+                         float* out_dist, uint32_t* out_len, cudaStream_t s) {
+  const uint64_t total = (uint64_t)nparts * k_in;
+  uint32_t cap = 1;
+  while (cap < total) cap <<= 1;
+  if (cap < 32) cap = 32;
+  size_t smem = cap * sizeof(uint32_t) + ((cap * sizeof(uint32_t)) & 4) + cap * sizeof(uint64_t);
+  if (smem > 48 * 1024)
+    PXC_CUDA(cudaFuncSetAttribute(merge_parts_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  merge_parts_kernel<<<nq, 256, smem, s>>>(ids, dist, lens, nparts, nq, k_in, k, cap, stride64, stride32, out_ids,
+                                           out_dist, out_len);
+  PXC_CUDA(cudaGetLastError());
+}
+
+void exchange_and_merge(pxc_ctx* ctx, const unsigned char* send, uint32_t nq, uint32_t k_in, uint32_t k,
+                        uint64_t* d_out_ids, float* d_out_dist, uint32_t* d_out_len, cudaStream_t s) {
+  const size_t seg = exchange_segment_bytes(nq, k_in);
+  const uint32_t nranks = (uint32_t)ctx->nranks;
+  const unsigned char* all = send;
+  if (nranks > 1) {
+    if ((size_t)nranks * seg > ctx->x_recv_bytes) {
+      if (ctx->x_recv) cudaFree(ctx->x_recv);
+      ctx->x_recv = nullptr;
+      ctx->x_recv_bytes = 0;
+      PXC_CUDA(cudaMalloc(&ctx->x_recv, (size_t)nranks * seg));
+      ctx->x_recv_bytes = (size_t)nranks * seg;
+    }
+    PXC_NCCL(nccl().all_gather(send, ctx->x_recv, seg, ncclUint8, static_cast<ncclComm_t>(ctx->comm), s));
+    all = ctx->x_recv;
+  }
+  const uint64_t* ids = reinterpret_cast<const uint64_t*>(all);
+  const float* dist = reinterpret_cast<const float*>(all + (size_t)nq * k_in * 8);
+  const uint32_t* lens = reinterpret_cast<const uint32_t*>(all + (size_t)nq * k_in * 12);
+  launch_merge(ids, dist, lens, nranks, nq, k_in, k, seg / 8, seg / 4, d_out_ids, d_out_dist, d_out_len, s);
+  ctx->launches += 1;
+  wait_comm(ctx, s, "candidate exchange");
 }
 
 }  // namespace pxc
@@ -114,6 +267,9 @@ void pxc_ctx_destroy(pxc_ctx* ctx) {
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   if (ctx->kmeans_ws && ctx->kmeans_ws_free) ctx->kmeans_ws_free(ctx->kmeans_ws);
+  if (ctx->comm && nccl_api().ok) nccl_api().comm_destroy(static_cast<ncclComm_t>(ctx->comm));
+  if (ctx->x_send) cudaFree(ctx->x_send);
+  if (ctx->x_recv) cudaFree(ctx->x_recv);
   if (ctx->d_status) cudaFree(ctx->d_status);
   if (ctx->h_status) cudaFreeHost(ctx->h_status);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
@@ -158,6 +314,65 @@ pxc_status pxc_ctx_set_profiling(pxc_ctx* ctx, int32_t on, pxc_error* err) {
   });
 }
 
+pxc_status pxc_comm_unique_id(uint8_t out[128], pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(out != nullptr, "out", 0, "null output");
+    ncclUniqueId id;
+    PXC_NCCL(nccl().get_unique_id(&id));
+    std::memcpy(out, id.internal, sizeof(id.internal));
+  });
+}
+
+pxc_status pxc_ctx_init_comm(pxc_ctx* ctx, const uint8_t id[128], int32_t nranks, int32_t rank, uint32_t timeout_ms,
+                             pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(ctx != nullptr && id != nullptr, "ctx", 0, "null argument");
+    PXC_CONFIG(nranks >= 1 && nranks <= 4096, "nranks", nranks, "must be between 1 and 4096");
+    PXC_CONFIG(rank >= 0 && rank < nranks, "rank", rank, "must be in [0, nranks)");
+    PXC_CONFIG(timeout_ms >= 100, "timeout_ms", timeout_ms, "must be at least 100");
+    std::lock_guard<std::mutex> lock(ctx->comm_mu);
+    PXC_CONFIG(ctx->comm == nullptr, "comm", 0, "the context already has a communicator");
+    ctx->comm_timeout_ms = timeout_ms;
+    if (nranks == 1) {
+      ctx->nranks = 1;
+      ctx->rank = 0;
+      return;
+    }
+    DeviceGuard g(ctx->device);
+    ncclUniqueId uid;
+    std::memcpy(uid.internal, id, sizeof(uid.internal));
+    ncclComm_t comm = nullptr;
+    PXC_NCCL(nccl().comm_init_rank(&comm, nranks, uid, rank));
+    ctx->comm = comm;
+    ctx->nranks = nranks;
+    ctx->rank = rank;
+  });
+}
+
+int32_t pxc_ctx_comm_size(const pxc_ctx* ctx) { return ctx ? ctx->nranks : 0; }
+int32_t pxc_ctx_comm_rank(const pxc_ctx* ctx) { return ctx ? ctx->rank : -1; }
+
+pxc_status pxc_topk_exchange(pxc_ctx* ctx, const uint64_t* d_ids, const float* d_dist, const uint32_t* d_lens,
+                             uint32_t nq, uint32_t k_in, uint32_t k, uint64_t* d_out_ids, float* d_out_dist,
+                             uint32_t* d_out_len, void* stream, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(ctx != nullptr, "ctx", 0, "null context");
+    PXC_CONFIG(k <= PXC_MAX_K, "k", k, "exceeds the 16777216 result ceiling");
+    PXC_CONFIG((uint64_t)ctx->nranks * k_in <= 8192, "nranks*k_in", (uint64_t)ctx->nranks * k_in,
+               "the merge holds at most 8192 candidates per query");
+    if (nq == 0) return;
+    DeviceGuard g(ctx->device);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    std::lock_guard<std::mutex> lock(ctx->comm_mu);
+    unsigned char* send = exchange_send_buffer(ctx, exchange_segment_bytes(nq, k_in));
+    const size_t n = (size_t)nq * k_in;
+    PXC_CUDA(cudaMemcpyAsync(send, d_ids, n * 8, cudaMemcpyDeviceToDevice, s));
+    PXC_CUDA(cudaMemcpyAsync(send + n * 8, d_dist, n * 4, cudaMemcpyDeviceToDevice, s));
+    PXC_CUDA(cudaMemcpyAsync(send + n * 12, d_lens, (size_t)nq * 4, cudaMemcpyDeviceToDevice, s));
+    exchange_and_merge(ctx, send, nq, k_in, k, d_out_ids, d_out_dist, d_out_len, s);
+  });
+}
+
 pxc_status pxc_topk_merge(pxc_ctx* ctx, const uint64_t* d_ids, const float* d_dist,
                           const uint32_t* d_lens, uint32_t nparts, uint32_t nq, uint32_t k_in,
                           uint32_t k, uint64_t* d_out_ids, float* d_out_dist,
@@ -172,16 +387,8 @@ pxc_status pxc_topk_merge(pxc_ctx* ctx, const uint64_t* d_ids, const float* d_di
     if (nq == 0) return;
     DeviceGuard g(ctx->device);
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
-    uint32_t cap = 1;
-    while (cap < total) cap <<= 1;
-    if (cap < 32) cap = 32;
-    size_t smem = cap * sizeof(uint32_t) + ((cap * sizeof(uint32_t)) & 4) + cap * sizeof(uint64_t);
-    if (smem > 48 * 1024)
-      PXC_CUDA(cudaFuncSetAttribute(merge_parts_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)smem));
-    merge_parts_kernel<<<nq, 256, smem, s>>>(d_ids, d_dist, d_lens, nparts, nq, k_in, k, cap,
-                                             d_out_ids, d_out_dist, d_out_len);
-    PXC_CUDA(cudaGetLastError());
+    launch_merge(d_ids, d_dist, d_lens, nparts, nq, k_in, k, (size_t)nq * k_in, nq, d_out_ids, d_out_dist,
+                 d_out_len, s);
     ctx->launches += 1;
   });
 }

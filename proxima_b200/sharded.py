@@ -1,10 +1,12 @@
 """Row-sharded exact search across GPUs (one process per GPU).
 
 Each rank mirrors a contiguous range of database rows with their global
-VectorIds, searches every query on its shard (top-k per query), exchanges the k
-(id, distance) candidates per query with an allgather and merges them on the
-device with ``pxc_topk_merge``. The only data that crosses NVLink is k
-candidates per query per rank.
+VectorIds and joins the job's NCCL communicator, which the native library owns
+(``pxc_ctx_init_comm``). ``pxc_flat_search_sharded`` searches every query on the
+rank's shard, carries the k (id, distance) candidates per query to every rank in
+one packed allgather and merges them on the device. The only data that crosses
+NVLink is k candidates per query per rank. ``torch.distributed`` is used only
+to hand rank 0's 128-byte communicator id to the other ranks.
 """
 from __future__ import annotations
 
@@ -22,8 +24,34 @@ def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
     return rank * n // world, (rank + 1) * n // world
 
 
+def broadcast_comm_id(group=None) -> bytes:
+    """Rank 0's fresh communicator id (pxc_comm_unique_id), broadcast to every
+    rank of `group` (gloo: CPU tensor; nccl: CUDA tensor)."""
+    lib = N.load()
+    buf = (C.c_uint8 * 128)()
+    if dist.get_rank(group) == 0:
+        N.call("pxc_comm_unique_id", buf)
+    backend = dist.get_backend(group)
+    dev = torch.device("cuda", torch.cuda.current_device()) if backend == "nccl" else torch.device("cpu")
+    t = torch.tensor(list(bytes(buf)), dtype=torch.uint8, device=dev)
+    dist.broadcast(t, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+    del lib
+    return bytes(t.cpu().tolist())
+
+
+def init_comm(ctx, group=None, timeout_ms: int = 60_000) -> None:
+    """Join the context to the communicator of the ranks of `group` (collective)."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    cid = broadcast_comm_id(group)
+    idbuf = (C.c_uint8 * 128).from_buffer_copy(cid)
+    N.call("pxc_ctx_init_comm", ctx.handle, idbuf, world, rank, timeout_ms)
+
+
 def exchange_candidates(ids: torch.Tensor, dist_: torch.Tensor, lens: torch.Tensor, group=None):
-    """Allgather the per-rank candidate lists.
+    """Allgather the per-rank candidate lists through torch.distributed (the host-side
+    restatement the CPU tests check the merge semantics with; the GPU path uses
+    the library's own exchange).
 
     ids [nq, k] int64, dist_ [nq, k] float32, lens [nq] int32 -> tensors of shape
     [world, nq, k], [world, nq, k], [world, nq] in rank order (NCCL for CUDA
@@ -62,17 +90,15 @@ class ShardedFlat:
                d.data_ptr(), lens.data_ptr(), stream_ptr)
         return ids, d, lens
 
-    def search_global(self, q_dev: torch.Tensor, k: int, stream_ptr: int, group=None):
-        """Local search, allgather, device merge -> global top-k on every rank."""
-        ids, d, lens = self.search(q_dev, k, stream_ptr)
-        g_ids, g_d, g_l = exchange_candidates(ids, d, lens, group)
+    def search_global(self, q_dev: torch.Tensor, k: int, stream_ptr: int):
+        """Local search, one packed NCCL allgather, device merge -> global top-k on every rank
+        (the context must have joined the communicator: init_comm)."""
         nq = q_dev.shape[0]
-        world = g_ids.shape[0]
         m_ids = torch.empty((nq, k), dtype=torch.int64, device=q_dev.device)
         m_d = torch.empty((nq, k), dtype=torch.float32, device=q_dev.device)
         m_l = torch.empty(nq, dtype=torch.int32, device=q_dev.device)
-        N.call("pxc_topk_merge", self.ctx.handle, g_ids.data_ptr(), g_d.data_ptr(), g_l.data_ptr(), world, nq,
-               k, k, m_ids.data_ptr(), m_d.data_ptr(), m_l.data_ptr(), stream_ptr)
+        N.call("pxc_flat_search_sharded", self.handle, q_dev.data_ptr(), nq, k, None, m_ids.data_ptr(),
+               m_d.data_ptr(), m_l.data_ptr(), stream_ptr)
         return m_ids, m_d, m_l
 
     def close(self):

@@ -122,3 +122,17 @@ def test_filtered_and_manhattan_searches_stay_on_the_fp32_scan():
     ri, rd, rl = pxo.flat_search(data, data[7:8], 5, pxo.EUCLIDEAN, bitmap=bitmap)
     assert [h.id for h in hits] == [int(x) for x in ri[0, :rl[0]]]
     idx.close()
+
+
+def test_unproven_queries_take_the_range_scan_and_its_overflow():
+    """5,000 copies of one row: a query equal to it ties with all of them, the
+    screen cannot prove it, and the exact range scan collects more rows than
+    its capacity (4,096), so the query ends on the fp32 scan; a query at a
+    small offset is proven or range-scanned. Answers order the ties by id."""
+    rng = np.random.default_rng(17)
+    dup = rng.standard_normal(16).astype(np.float32)
+    data = np.concatenate([np.tile(dup, (5000, 1)), rng.standard_normal((3000, 16)).astype(np.float32)])
+    ids = rng.permutation(len(data)).astype(np.uint64)
+    queries = np.stack([dup, dup + np.float32(0.01), rng.standard_normal(16).astype(np.float32)])
+    redo = _check(data, queries, 10, Metric.EUCLIDEAN, ids=ids)
+    assert redo >= 1
