@@ -141,11 +141,12 @@ void check_status_word(uint32_t* d_status, uint32_t* h_status, cudaStream_t s, c
 
 // One warp-free block per query: gather the union of the parts, sort by
 // (total_cmp(distance), id), keep k. Part p's lists start at ids + p *
-// part_stride64 (and dist / lens + p * part_stride32), entry (q, i) at q * k_in + i.
+// stride_ids, dist + p * stride_dist and lens + p * stride_len (elements);
+// entry (q, i) at q * k_in + i, the length of q at q.
 __global__ void merge_parts_kernel(const uint64_t* __restrict__ ids, const float* __restrict__ dist,
                                    const uint32_t* __restrict__ lens, uint32_t nparts, uint32_t nq,
-                                   uint32_t k_in, uint32_t k, uint32_t cap, size_t part_stride64,
-                                   size_t part_stride32, uint64_t* __restrict__ out_ids,
+                                   uint32_t k_in, uint32_t k, uint32_t cap, size_t stride_ids,
+                                   size_t stride_dist, size_t stride_len, uint64_t* __restrict__ out_ids,
                                    float* __restrict__ out_dist, uint32_t* __restrict__ out_len) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   uint32_t* skey = reinterpret_cast<uint32_t*>(smem_raw);
@@ -157,12 +158,12 @@ __global__ void merge_parts_kernel(const uint64_t* __restrict__ ids, const float
   if (threadIdx.x == 0) count = 0;
   __syncthreads();
   for (uint32_t p = 0; p < nparts; ++p) {
-    uint32_t len = min(lens[p * part_stride32 + q], k_in);
+    uint32_t len = min(lens[p * stride_len + q], k_in);
     for (uint32_t i = threadIdx.x; i < len; i += blockDim.x) {
       uint32_t pos = atomicAdd(&count, 1u);
       const size_t e = (size_t)q * k_in + i;
-      skey[pos] = order_key(dist[p * part_stride32 + e]);
-      sid[pos] = ids[p * part_stride64 + e];
+      skey[pos] = order_key(dist[p * stride_dist + e]);
+      sid[pos] = ids[p * stride_ids + e];
     }
   }
   __syncthreads();
@@ -183,8 +184,8 @@ __global__ void merge_parts_kernel(const uint64_t* __restrict__ ids, const float
 
 // Shared-memory size and launch of the merge for `total` candidates per query.
 static void launch_merge(const uint64_t* ids, const float* dist, const uint32_t* lens, uint32_t nparts, uint32_t nq,
-                         uint32_t k_in, uint32_t k, size_t stride64, size_t stride32, uint64_t* out_ids,
-                         float* out_dist, uint32_t* out_len, cudaStream_t s) {
+                         uint32_t k_in, uint32_t k, size_t stride_ids, size_t stride_dist, size_t stride_len,
+                         uint64_t* out_ids, float* out_dist, uint32_t* out_len, cudaStream_t s) {
   const uint64_t total = (uint64_t)nparts * k_in;
   uint32_t cap = 1;
   while (cap < total) cap <<= 1;
@@ -192,8 +193,8 @@ static void launch_merge(const uint64_t* ids, const float* dist, const uint32_t*
   size_t smem = cap * sizeof(uint32_t) + ((cap * sizeof(uint32_t)) & 4) + cap * sizeof(uint64_t);
   if (smem > 48 * 1024)
     PXC_CUDA(cudaFuncSetAttribute(merge_parts_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  merge_parts_kernel<<<nq, 256, smem, s>>>(ids, dist, lens, nparts, nq, k_in, k, cap, stride64, stride32, out_ids,
-                                           out_dist, out_len);
+  merge_parts_kernel<<<nq, 256, smem, s>>>(ids, dist, lens, nparts, nq, k_in, k, cap, stride_ids, stride_dist,
+                                           stride_len, out_ids, out_dist, out_len);
   PXC_CUDA(cudaGetLastError());
 }
 
@@ -216,7 +217,7 @@ void exchange_and_merge(pxc_ctx* ctx, const unsigned char* send, uint32_t nq, ui
   const uint64_t* ids = reinterpret_cast<const uint64_t*>(all);
   const float* dist = reinterpret_cast<const float*>(all + (size_t)nq * k_in * 8);
   const uint32_t* lens = reinterpret_cast<const uint32_t*>(all + (size_t)nq * k_in * 12);
-  launch_merge(ids, dist, lens, nranks, nq, k_in, k, seg / 8, seg / 4, d_out_ids, d_out_dist, d_out_len, s);
+  launch_merge(ids, dist, lens, nranks, nq, k_in, k, seg / 8, seg / 4, seg / 4, d_out_ids, d_out_dist, d_out_len, s);
   ctx->launches += 1;
   wait_comm(ctx, s, "candidate exchange");
 }
@@ -387,8 +388,8 @@ pxc_status pxc_topk_merge(pxc_ctx* ctx, const uint64_t* d_ids, const float* d_di
     if (nq == 0) return;
     DeviceGuard g(ctx->device);
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
-    launch_merge(d_ids, d_dist, d_lens, nparts, nq, k_in, k, (size_t)nq * k_in, nq, d_out_ids, d_out_dist,
-                 d_out_len, s);
+    launch_merge(d_ids, d_dist, d_lens, nparts, nq, k_in, k, (size_t)nq * k_in, (size_t)nq * k_in, nq, d_out_ids,
+                 d_out_dist, d_out_len, s);
     ctx->launches += 1;
   });
 }

@@ -282,8 +282,8 @@ __device__ __forceinline__ typename P::T chunk_min(const uint32_t (&v)[32], cons
 // the accumulator is released, so insertions overlap the next tile's MMAs
 // instead of stalling them. FIFO order is ascending rank order, so draining
 // with the strict '<' keeps the list exact.
-// One FIFO holds at most one flagged chunk's 32 entries beyond what a drain
-// leaves (the K2 FIFO of 16 drains mid-chunk, see fifo_push_chunk).
+// A FIFO takes a flagged chunk in pieces of P::FIFO_SLOTS columns or fewer,
+// draining first when the piece's entries would not fit.
 template <int KT, class P>
 __device__ __forceinline__ void fifo_drain(const uint2* fifo, uint32_t& cnt, uint32_t lane,
                                            typename P::T (&lr)[KT], uint32_t (&lk)[KT],
@@ -302,15 +302,20 @@ template <int KT, class P>
 __device__ __forceinline__ void fifo_push_chunk(const typename P::T (&r)[32], typename P::T thr, uint32_t rank0,
                                                 uint2* fifo, uint32_t& cnt, uint32_t lane, typename P::T (&lr)[KT],
                                                 uint32_t (&lk)[KT], typename P::T shared_bound) {
-  uint32_t mask = 0;
+  constexpr int PIECE = P::FIFO_SLOTS < 32 ? P::FIFO_SLOTS : 32;
+  static_assert(32 % PIECE == 0, "FIFO pieces must tile the chunk");
 #pragma unroll
-  for (int j = 0; j < 32; ++j) mask |= (r[j] < thr ? 1u : 0u) << j;
+  for (int j0 = 0; j0 < 32; j0 += PIECE) {
+    uint32_t mask = 0;
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    if (mask & (1u << j)) {
-      if (cnt == (uint32_t)P::FIFO_SLOTS) fifo_drain<KT, P>(fifo, cnt, lane, lr, lk, shared_bound);
-      fifo[cnt * 32 + lane] = make_uint2(*reinterpret_cast<const uint32_t*>(&r[j]), rank0 + j);
-      ++cnt;
+    for (int j = 0; j < PIECE; ++j) mask |= (r[j0 + j] < thr ? 1u : 0u) << j;
+    if (cnt + __popc(mask) > (uint32_t)P::FIFO_SLOTS) fifo_drain<KT, P>(fifo, cnt, lane, lr, lk, shared_bound);
+#pragma unroll
+    for (int j = 0; j < PIECE; ++j) {
+      if (mask & (1u << j)) {
+        fifo[cnt * 32 + lane] = make_uint2(*reinterpret_cast<const uint32_t*>(&r[j0 + j]), rank0 + j0 + j);
+        ++cnt;
+      }
     }
   }
 }
