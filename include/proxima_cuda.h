@@ -344,6 +344,23 @@ pxc_status pxc_pq_tables_device(pxc_ctx* ctx, const float* d_codebooks, uint32_t
                                 const float* d_queries, uint32_t nq, float* d_out_squared, float* d_out_dot,
                                 void* stream, pxc_error* err);
 
+/* kmeans over points sharded across the ranks of the context's communicator
+ * (pxc_ctx_init_comm): this rank's n points (DEVICE, n x dim) are its
+ * consecutive range of the global point order, rank by rank. Every rank
+ * passes the same k x dim DEVICE init (the injected-init mode of pxc_kmeans;
+ * the sharded form has no k-means++ seeding) and receives the same
+ * centroids; out_assign (nullable) gets its own points' clusters. Each
+ * iteration exchanges, over the communicator, the inertia and changed flag
+ * of the assignment pass and the per-cluster f64 sums and counts (folded in
+ * rank order), and for every empty cluster the ranks' farthest points (the
+ * global one wins, ties to the lower global index), so the iteration count,
+ * assignments and re-seeding follow kmeans.rs:59-143 over the whole set;
+ * centroids equal the unsharded run's whenever the per-cluster sums are exact
+ * and otherwise agree within rounding. Every rank needs n >= 1. */
+pxc_status pxc_kmeans_sharded(pxc_ctx* ctx, const float* d_points, uint64_t n, uint32_t dim, uint32_t k,
+                              uint32_t max_iterations, const float* d_init, float* d_out_centroids,
+                              uint32_t* d_out_assign, pxc_kmeans_info* info, void* stream, pxc_error* err);
+
 /* ---- IvfPqIndex ----
  * The device side of IvfPqIndex (crates/proxima-index/src/ivfpq.rs): coarse
  * centroids + product-quantizer codebooks, inverted lists of PQ codes in
@@ -414,6 +431,17 @@ pxc_status pxc_ivfpq_search_device(pxc_ivfpq* h, const float* d_queries, uint32_
                                    uint32_t nprobe, uint32_t rerank, const uint64_t* d_bitmap,
                                    uint64_t* d_out_ids, float* d_out_dist, uint32_t* d_out_len,
                                    void* stream, pxc_error* err);
+
+/* search_with_nprobe over an index whose rows are sharded across the ranks of
+ * the context's communicator: every rank holds the same parts (centroids,
+ * codebooks) and the lists of its own rows (global VectorIds as ids), probes
+ * the same nprobe lists on its shard, re-ranks its own shortlist of
+ * max(rerank, k), and one packed allgather + merge gives every rank the
+ * global top-k: the union of the ranks' answers ordered by (total_cmp, id).
+ * DEVICE buffers; returns after the exchange has finished. */
+pxc_status pxc_ivfpq_search_sharded(pxc_ivfpq* h, const float* d_queries, uint32_t nq, uint32_t k, uint32_t nprobe,
+                                    uint32_t rerank, const uint64_t* d_bitmap, uint64_t* d_out_ids, float* d_out_dist,
+                                    uint32_t* d_out_len, void* stream, pxc_error* err);
 
 /* ---- ScalarQuantizer ----
  * crates/proxima-quantize/src/scalar.rs. Range modes and code types in the

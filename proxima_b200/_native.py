@@ -124,6 +124,8 @@ SIGNATURES: dict[str, tuple] = {
     "pxc_kmeans_device": (C.c_int32, [vp, vp, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, vp,
                                       C.POINTER(PxcRng), vp, vp, C.POINTER(PxcKmeansInfo), vp,
                                       C.POINTER(PxcError)]),
+    "pxc_kmeans_sharded": (C.c_int32, [vp, vp, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, vp, vp, vp,
+                                       C.POINTER(PxcKmeansInfo), vp, C.POINTER(PxcError)]),
     "pxc_pq_train": (C.c_int32, [vp, vp, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint64, vp,
                                  C.POINTER(C.c_double), C.POINTER(C.c_uint64), C.POINTER(PxcError)]),
     "pxc_pq_train_device": (C.c_int32, [vp, vp, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint64, vp,
@@ -154,6 +156,8 @@ SIGNATURES: dict[str, tuple] = {
     "pxc_ivfpq_get_parts": (C.c_int32, [vp, vp, vp, vp, vp, C.POINTER(C.c_uint32), C.POINTER(PxcError)]),
     "pxc_ivfpq_search": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, vp, vp, vp, vp,
                                      C.POINTER(PxcError)]),
+    "pxc_ivfpq_search_sharded": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, vp, vp,
+                                             vp, vp, vp, C.POINTER(PxcError)]),
     "pxc_ivfpq_search_device": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, vp, vp,
                                             vp, vp, vp, C.POINTER(PxcError)]),
     "pxc_sq_train": (C.c_int32, [vp, vp, C.c_uint64, C.c_uint32, C.c_int32, vp, vp, vp, C.POINTER(PxcError)]),

@@ -220,4 +220,8 @@ void exchange_and_merge(pxc_ctx* ctx, const unsigned char* send, uint32_t nq, ui
                         uint64_t* d_out_ids, float* d_out_dist, uint32_t* d_out_len, cudaStream_t s);
 // The context's send buffer, grown to at least `bytes` (callers hold comm_mu).
 unsigned char* exchange_send_buffer(pxc_ctx* ctx, size_t bytes);
+// ncclAllGather of `bytes` per rank over the context's communicator (recv:
+// nranks * bytes, rank order), then the bounded wait of the exchange. With one
+// rank, a device copy. Callers hold comm_mu.
+void comm_allgather(pxc_ctx* ctx, const void* send, void* recv, size_t bytes, cudaStream_t s, const char* where);
 }  // namespace pxc

@@ -103,6 +103,16 @@ static void wait_comm(pxc_ctx* ctx, cudaStream_t s, const char* where) {
   }
 }
 
+void comm_allgather(pxc_ctx* ctx, const void* send, void* recv, size_t bytes, cudaStream_t s, const char* where) {
+  if (ctx->nranks <= 1 || ctx->comm == nullptr) {
+    PXC_CUDA(cudaMemcpyAsync(recv, send, bytes, cudaMemcpyDeviceToDevice, s));
+    PXC_CUDA(cudaStreamSynchronize(s));
+    return;
+  }
+  PXC_NCCL(nccl().all_gather(send, recv, bytes, ncclUint8, static_cast<ncclComm_t>(ctx->comm), s));
+  wait_comm(ctx, s, where);
+}
+
 size_t exchange_segment_bytes(uint32_t nq, uint32_t k_in) {
   const size_t raw = (size_t)nq * k_in * 12 + (size_t)nq * 4;
   return (raw + 15) / 16 * 16;

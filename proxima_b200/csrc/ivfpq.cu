@@ -1222,6 +1222,30 @@ pxc_status pxc_ivfpq_search_device(pxc_ivfpq* h, const float* d_queries, uint32_
   });
 }
 
+pxc_status pxc_ivfpq_search_sharded(pxc_ivfpq* h, const float* d_queries, uint32_t nq, uint32_t k, uint32_t nprobe,
+                                    uint32_t rerank, const uint64_t* d_bitmap, uint64_t* d_out_ids, float* d_out_dist,
+                                    uint32_t* d_out_len, void* stream, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(h != nullptr, "h", 0, "null handle");
+    PXC_CONFIG(k <= PXC_MAX_K, "k", k, "k exceeds the maximum");
+    pxc_ctx* ctx = h->ctx;
+    PXC_CONFIG((uint64_t)ctx->nranks * k <= 8192, "nranks*k", (uint64_t)ctx->nranks * k,
+               "the merge holds at most 8192 candidates per query");
+    if (nq == 0) return;
+    std::lock_guard<std::mutex> lock(h->mu);
+    DeviceGuard g(ctx->device);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    std::lock_guard<std::mutex> comm_lock(ctx->comm_mu);
+    unsigned char* send = exchange_send_buffer(ctx, exchange_segment_bytes(nq, k));
+    const size_t n = (size_t)nq * k;
+    ivf::handoff_wait(h, s);
+    ivf::search_device(h, d_queries, nq, k, nprobe, rerank, d_bitmap, reinterpret_cast<uint64_t*>(send),
+                       reinterpret_cast<float*>(send + n * 8), reinterpret_cast<uint32_t*>(send + n * 12), s);
+    exchange_and_merge(ctx, send, nq, k, k, d_out_ids, d_out_dist, d_out_len, s);
+    ivf::handoff_done(h, s);
+  });
+}
+
 pxc_status pxc_ivfpq_search(pxc_ivfpq* h, const float* queries, uint32_t nq, uint32_t k, uint32_t nprobe,
                             uint32_t rerank, const uint64_t* bitmap, uint64_t* out_ids, float* out_dist,
                             uint32_t* out_len, pxc_error* err) {

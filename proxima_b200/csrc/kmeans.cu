@@ -427,6 +427,95 @@ __global__ void cluster_mean_kernel(const float* __restrict__ P, uint32_t ldp, u
   if (on) out[(size_t)c * ldc + dim] = __double2float_rn(__dmul_rn(s, 1.0 / (double)(e - b)));
 }
 
+// Point-sharded update, this rank's half: per cluster the f64 sums of the
+// rank's members in point order (the chains of cluster_mean_kernel) and the
+// member count; empty clusters write zeros.
+__global__ void cluster_sum_kernel(const float* __restrict__ P, uint32_t ldp, uint32_t d, uint32_t groups,
+                                   const uint32_t* __restrict__ sorted, const uint32_t* __restrict__ off, uint32_t k,
+                                   double* __restrict__ sums, uint32_t* __restrict__ counts) {
+  const uint32_t w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t c = w / groups, g = w - c * groups;
+  if (c >= k) return;
+  const uint32_t b = off[c], e = off[c + 1];
+  const uint32_t dim = g * 32 + lane;
+  const bool on = dim < d;
+  if (lane == 0 && g == 0) counts[c] = e - b;
+  const float* base = P + dim;
+  double s = 0.0;
+  for (uint32_t m0 = b; m0 < e; m0 += 32) {
+    const uint32_t cntm = min(32u, e - m0);
+    const uint32_t mine = lane < cntm ? sorted[m0 + lane] : 0u;
+    for (uint32_t j = 0; j < cntm; ++j) {
+      const uint32_t pt = __shfl_sync(0xFFFFFFFFu, mine, j);
+      const float v = on ? __ldg(base + (size_t)pt * ldp) : 0.0f;
+      s = __dadd_rn(s, (double)v);
+    }
+  }
+  if (on) sums[(size_t)c * d + dim] = s;
+}
+
+// The other half: every rank's sums folded in rank order (the ranks hold
+// consecutive ranges of the point order), the counts added, and
+// c = (sum * (1.0/count)) as f32 (kmeans.rs:127-135). Segment of rank r at
+// all + r * seg: sums [k][d] f64, then counts [k] u32. gcount: the global counts.
+__global__ void fold_means_kernel(const unsigned char* __restrict__ all, size_t seg, uint32_t nranks, uint32_t k,
+                                  uint32_t d, float* __restrict__ next, uint32_t ldc, uint32_t* __restrict__ gcount,
+                                  uint32_t* __restrict__ empty_count) {
+  const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= (uint64_t)k * d) return;
+  const uint32_t c = (uint32_t)(t / d), j = (uint32_t)(t - (uint64_t)c * d);
+  double S = 0.0;
+  uint32_t N = 0;
+  for (uint32_t r = 0; r < nranks; ++r) {
+    const double* sums = reinterpret_cast<const double*>(all + r * seg);
+    const uint32_t* cnt = reinterpret_cast<const uint32_t*>(all + r * seg + (size_t)k * d * 8);
+    S = __dadd_rn(S, sums[(size_t)c * d + j]);
+    N += cnt[c];
+  }
+  if (j == 0) gcount[c] = N;
+  if (N == 0) {
+    if (j == 0) atomicAdd(empty_count, 1u);
+    return;
+  }
+  next[(size_t)c * ldc + j] = __double2float_rn(__dmul_rn(S, 1.0 / (double)N));
+}
+
+// Sharded re-seeding: this rank's farthest point (a key of argmax_list_kernel)
+// as a segment [key u64, global index u64, the point's d floats].
+__global__ void farthest_candidate_kernel(const float* __restrict__ P, uint32_t ldp, uint32_t d,
+                                          const unsigned long long* __restrict__ key, uint64_t global_first,
+                                          unsigned char* __restrict__ seg) {
+  const unsigned long long kk = *key;
+  const uint64_t idx = 0xFFFFFFFFull - (kk & 0xFFFFFFFFull);
+  if (threadIdx.x == 0) {
+    reinterpret_cast<unsigned long long*>(seg)[0] = kk;
+    reinterpret_cast<unsigned long long*>(seg)[1] = global_first + idx;
+  }
+  float* row = reinterpret_cast<float*>(seg + 16);
+  for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) row[i] = P[idx * ldp + i];
+}
+// The global farthest point among the ranks' candidates: the largest
+// distance, ties to the lowest global index (farthest_point's strict '>'
+// over the whole point order), copied into the centroid row.
+__global__ void farthest_pick_kernel(const unsigned char* __restrict__ all, size_t seg, uint32_t nranks, uint32_t d,
+                                     float* __restrict__ dst) {
+  __shared__ uint32_t best;
+  if (threadIdx.x == 0) {
+    uint32_t b = 0;
+    for (uint32_t r = 1; r < nranks; ++r) {
+      const unsigned long long* kr = reinterpret_cast<const unsigned long long*>(all + r * seg);
+      const unsigned long long* kb = reinterpret_cast<const unsigned long long*>(all + b * seg);
+      const uint32_t dr = (uint32_t)(kr[0] >> 32), db = (uint32_t)(kb[0] >> 32);
+      if (dr > db || (dr == db && kr[1] < kb[1])) b = r;
+    }
+    best = b;
+  }
+  __syncthreads();
+  const float* row = reinterpret_cast<const float*>(all + best * seg + 16);
+  for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) dst[i] = row[i];
+}
+
 // farthest_point (kmeans.rs:215-226) helpers: largest distance, first index on
 // ties, as one u64 key (distance bits, then the complemented index).
 __global__ void argmax_list_kernel(const float* __restrict__ v, const uint32_t* __restrict__ list,
@@ -744,6 +833,14 @@ struct Runner {
         h_u64(ws.h_u64), summer(ws.summer), prof(ws.prof) {}
   CUtensorMap tmap_p;
   uint32_t kblocks = 0, stages = 0, ntiles = 0;
+  // Point-sharded mode (pxc_kmeans_sharded): this rank holds points
+  // [global_first, global_first + n) of the global order; the per-iteration
+  // state is exchanged over the context's communicator.
+  bool sharded = false;
+  uint64_t global_first = 0;
+  DBuf<unsigned char> xs, xr;
+  DBuf<uint32_t> gcount;
+  std::vector<uint32_t> h_gcount;
 
   cudaEvent_t ev[8] = {};
   uint32_t screen_passes = 0;
@@ -1008,8 +1105,17 @@ struct Runner {
       mark(3);
       PXC_CUDA(cudaMemcpyAsync(h_words + 4, words.p, sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
       r.inertia = seq_sum(bestd.p, false);  // synchronises
-      const bool changed = h_words[4] != 0;
+      bool changed = h_words[4] != 0;
+      if (sharded) exchange_progress(r.inertia, changed);
       if (!changed && it > 0) break;
+      if (sharded) {
+        sharded_update(sort_bits);
+        mark(4);
+        if (read_word(2)) reseed_empty(r);
+        mark(5);
+        std::swap(cur.p, next.p);
+        continue;
+      }
       // update: stable sort by cluster, per-cluster sums in point order
       size_t tb = sort_tmp_bytes;
       PXC_CUDA(cub::DeviceRadixSort::SortPairs(sort_tmp.p, tb, assign.p, keys_b.p, iota.p, sorted.p, (int)n, 0,
@@ -1033,6 +1139,69 @@ struct Runner {
     return r;
   }
 
+  // Sharded: the ranks' inertia (f64 partial sums, added in rank order) and
+  // `changed` flags (any) of the assignment pass.
+  void exchange_progress(double& inertia, bool& changed) {
+    struct alignas(16) Progress {
+      double inertia;
+      uint32_t changed, pad;
+    };
+    const int nr = ctx->nranks;
+    xs.reserve(sizeof(Progress));
+    xr.reserve(sizeof(Progress) * nr);
+    Progress mine{inertia, changed ? 1u : 0u, 0u};
+    PXC_CUDA(cudaMemcpyAsync(xs.p, &mine, sizeof(mine), cudaMemcpyHostToDevice, s));
+    comm_allgather(ctx, xs.p, xr.p, sizeof(Progress), s, "k-means progress exchange");
+    std::vector<Progress> all(nr);
+    PXC_CUDA(cudaMemcpy(all.data(), xr.p, sizeof(Progress) * nr, cudaMemcpyDeviceToHost));
+    double total = 0.0;
+    bool any = false;
+    for (const Progress& p : all) {
+      total += p.inertia;
+      any |= p.changed != 0;
+    }
+    inertia = total;
+    changed = any;
+  }
+
+  // Sharded update: local per-cluster sums and counts, one allgather, the
+  // rank-ordered fold into next; words[2] counts the globally empty clusters.
+  void sharded_update(int sort_bits) {
+    size_t tb = sort_tmp_bytes;
+    PXC_CUDA(cub::DeviceRadixSort::SortPairs(sort_tmp.p, tb, assign.p, keys_b.p, iota.p, sorted.p, (int)n, 0,
+                                             sort_bits, s));
+    offsets_kernel<<<blocks(k + 1, 256), 256, 0, s>>>(keys_b.p, n, k, off.p);
+    const size_t seg = ((size_t)k * d * 8 + (size_t)k * 4 + 15) / 16 * 16;
+    xs.reserve(seg);
+    xr.reserve(seg * ctx->nranks);
+    const uint32_t groups = (d + 31) / 32;
+    cluster_sum_kernel<<<blocks((uint64_t)k * groups * 32, 256), 256, 0, s>>>(
+        P, ldp, d, groups, sorted.p, off.p, k, reinterpret_cast<double*>(xs.p),
+        reinterpret_cast<uint32_t*>(xs.p + (size_t)k * d * 8));
+    PXC_CUDA(cudaGetLastError());
+    launches += 3;
+    comm_allgather(ctx, xs.p, xr.p, seg, s, "k-means update exchange");
+    gcount.reserve(k);
+    PXC_CUDA(cudaMemsetAsync(words.p + 2, 0, sizeof(uint32_t), s));
+    fold_means_kernel<<<blocks((uint64_t)k * d, 256), 256, 0, s>>>(xr.p, seg, ctx->nranks, k, d, next.p, ldc,
+                                                                   gcount.p, words.p + 2);
+    PXC_CUDA(cudaGetLastError());
+    launches += 1;
+  }
+
+  // Sharded re-seeding of cluster e: the ranks' farthest points exchanged,
+  // the global one copied into next[e] on every rank.
+  void sharded_farthest(uint32_t e, const unsigned long long* local_key) {
+    const size_t seg = (16 + (size_t)d * 4 + 15) / 16 * 16;
+    xs.reserve(seg);
+    xr.reserve(seg * ctx->nranks);
+    farthest_candidate_kernel<<<1, 128, 0, s>>>(P, ldp, d, local_key, global_first, xs.p);
+    comm_allgather(ctx, xs.p, xr.p, seg, s, "k-means re-seed exchange");
+    farthest_pick_kernel<<<1, 128, 0, s>>>(xr.p, seg, ctx->nranks, d, next.p + (size_t)e * ldc);
+    PXC_CUDA(cudaGetLastError());
+    launches += 2;
+  }
+
   // Empty clusters, in index order (kmeans.rs:118-126): each takes the
   // farthest point (kmeans.rs:215-226) against the centroids as they stand
   // at that moment — [0, e) already updated (in next, earlier re-seeds
@@ -1046,6 +1215,10 @@ struct Runner {
   void reseed_empty(Result& r) {
     std::vector<uint32_t> offs(k + 1);
     PXC_CUDA(cudaMemcpyAsync(offs.data(), off.p, (k + 1) * sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
+    if (sharded) {  // emptiness is global: the folded counts
+      h_gcount.resize(k);
+      PXC_CUDA(cudaMemcpyAsync(h_gcount.data(), gcount.p, k * sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
+    }
     pair_l2_kernel<false><<<blocks(n, 128), 128, 0, s>>>(P, ldp, n, d, next.p, ldc, assign.p, u_next.p);
     // bounds: the exact distance to the old centroid of the point's cluster
     PXC_CUDA(cudaMemcpyAsync(ub.p, bestd.p, n * 4, cudaMemcpyDeviceToDevice, s));
@@ -1055,7 +1228,7 @@ struct Runner {
     PXC_CUDA(cudaStreamSynchronize(s));
     const uint32_t cap = (uint32_t)std::min<uint64_t>(8 * SEEDS, n);
     for (uint32_t e = 0; e < k; ++e) {
-      if (offs[e] != offs[e + 1]) continue;
+      if (sharded ? h_gcount[e] != 0 : offs[e] != offs[e + 1]) continue;
       if (e) PXC_CUDA(cudaMemcpyAsync(part.p, next.p, (size_t)e * ldc * 4, cudaMemcpyDeviceToDevice, s));
       PXC_CUDA(cudaMemcpyAsync(part.p + (size_t)e * ldc, cur.p + (size_t)e * ldc, (size_t)(k - e) * ldc * 4,
                                cudaMemcpyDeviceToDevice, s));
@@ -1095,7 +1268,10 @@ struct Runner {
                      e, nl, nl_cheap);
       exact_list(part.p, rescan.p, words.p + 1, nl, ubc.p, ub.p, 2, ube.p, e);
       argmax_list_kernel<<<ctx->sm_count * 4, 256, 0, s>>>(ub.p, rescan.p, words.p + 1, 0, key.p + 1);
-      copy_row_kernel<<<1, 128, 0, s>>>(P, ldp, d, key.p + 1, next.p + (size_t)e * ldc);
+      if (sharded)
+        sharded_farthest(e, key.p + 1);
+      else
+        copy_row_kernel<<<1, 128, 0, s>>>(P, ldp, d, key.p + 1, next.p + (size_t)e * ldc);
       launches += 2;
       PXC_CUDA(cudaGetLastError());
       ++r.reseeded;
@@ -1128,6 +1304,51 @@ Result kmeans_impl(pxc_ctx* ctx, const float* d_pts, uint32_t ld, uint64_t n, ui
   DBuf<float> padded;
   prepare_runner(R, ctx, d_pts, ld, n, d, k_eff, padded, s, true);
   r = R.run(max_iter, d_init, rng);
+  r.k = k_eff;
+  r.screen_passes = R.screen_passes;
+  r.screen_ms = R.screen_ms;
+  PXC_CUDA(cudaMemcpy2DAsync(d_out_cent, d * 4, R.cur.p, R.ldc * 4, d * 4, k_eff, cudaMemcpyDeviceToDevice, s));
+  if (d_out_assign) PXC_CUDA(cudaMemcpyAsync(d_out_assign, R.assign.p, n * 4, cudaMemcpyDeviceToDevice, s));
+  PXC_CUDA(cudaStreamSynchronize(s));
+  check_device_status(ctx, s, "k-means");
+  ctx->launches += R.launches;
+  return r;
+}
+
+// proxima_quantize::kmeans over points sharded across the ranks of the
+// context's communicator, from an injected init (identical on every rank).
+// Assignments are exact per point; the per-cluster f64 sums are folded in
+// rank order, so centroids equal a single run's whenever those sums are
+// exact, and are within rounding of it otherwise.
+Result kmeans_sharded_impl(pxc_ctx* ctx, const float* d_pts, uint32_t ld, uint64_t n, uint32_t d, uint32_t k,
+                           uint32_t max_iter, const float* d_init, float* d_out_cent, uint32_t* d_out_assign,
+                           cudaStream_t s) {
+  PXC_CONFIG(d >= 1 && d <= MAX_DIM, "dim", d, "k-means on the device supports 1 <= dim <= 512");
+  PXC_CONFIG(n >= 1 && n <= 0x7FFFFFFFull, "n", n, "every rank holds between 1 and 2^31 - 1 points");
+  PXC_CONFIG(d_init != nullptr, "init", 0, "the sharded k-means starts from an injected init");
+  std::lock_guard<std::mutex> comm_lock(ctx->comm_mu);
+  // the global point order: ranks hold consecutive ranges
+  const int nr = ctx->nranks;
+  DBuf<uint64_t> cnt_s, cnt_r;
+  cnt_s.reserve(2);
+  cnt_r.reserve(2 * (size_t)nr);
+  const uint64_t mine[2] = {n, 0};
+  PXC_CUDA(cudaMemcpyAsync(cnt_s.p, mine, sizeof(mine), cudaMemcpyHostToDevice, s));
+  comm_allgather(ctx, cnt_s.p, cnt_r.p, sizeof(mine), s, "k-means point counts");
+  std::vector<uint64_t> counts(2 * (size_t)nr);
+  PXC_CUDA(cudaMemcpy(counts.data(), cnt_r.p, counts.size() * 8, cudaMemcpyDeviceToHost));
+  uint64_t n_global = 0, first = 0;
+  for (int r = 0; r < nr; ++r) {
+    if (r == ctx->rank) first = n_global;
+    n_global += counts[2 * r];
+  }
+  const uint32_t k_eff = (uint32_t)std::max<uint64_t>(std::min<uint64_t>(k, n_global), 1);
+  Runner R(workspace(ctx));
+  DBuf<float> padded;
+  prepare_runner(R, ctx, d_pts, ld, n, d, k_eff, padded, s, true);
+  R.sharded = true;
+  R.global_first = first;
+  Result r = R.run(max_iter, d_init, nullptr);
   r.k = k_eff;
   r.screen_passes = R.screen_passes;
   r.screen_ms = R.screen_ms;
@@ -1292,6 +1513,21 @@ pxc_status pxc_kmeans(pxc_ctx* ctx, const float* points, uint64_t n, uint32_t di
     if (out_assign && n_eff)
       PXC_CUDA(cudaMemcpyAsync(out_assign, dassign.p, n_eff * 4, cudaMemcpyDeviceToHost, s));
     PXC_CUDA(cudaStreamSynchronize(s));
+    km::fill_info(info, r);
+  });
+}
+
+pxc_status pxc_kmeans_sharded(pxc_ctx* ctx, const float* d_points, uint64_t n, uint32_t dim, uint32_t k,
+                              uint32_t max_iterations, const float* d_init, float* d_out_centroids,
+                              uint32_t* d_out_assign, pxc_kmeans_info* info, void* stream, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(ctx != nullptr, "ctx", 0, "null context");
+    PXC_CONFIG(d_out_centroids != nullptr && d_points != nullptr, "points", 0, "null buffer");
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    DeviceGuard g(ctx->device);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    km::Result r = km::kmeans_sharded_impl(ctx, d_points, dim, n, dim, k, max_iterations, d_init, d_out_centroids,
+                                           d_out_assign, s);
     km::fill_info(info, r);
   });
 }

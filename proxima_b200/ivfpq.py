@@ -107,6 +107,14 @@ class IvfPqIndex:
                None if d_bitmap is None else d_bitmap.data_ptr(), d_ids.data_ptr(), d_dist.data_ptr(),
                d_lens.data_ptr(), stream)
 
+    def search_sharded_device(self, d_queries, k: int, nprobe: int, rerank: int, d_ids, d_dist, d_lens, stream: int,
+                              d_bitmap=None) -> None:
+        """The row-sharded search (pxc_ivfpq_search_sharded): this rank's shard, the library's exchange,
+        the global top-k on every rank. The context must have joined the communicator."""
+        N.call("pxc_ivfpq_search_sharded", self.handle, d_queries.data_ptr(), d_queries.shape[0], k, nprobe,
+               rerank, None if d_bitmap is None else d_bitmap.data_ptr(), d_ids.data_ptr(), d_dist.data_ptr(),
+               d_lens.data_ptr(), stream)
+
     def last_scan_ms(self) -> float:
         return N.load().pxc_ivfpq_last_scan_ms(self.handle)
 

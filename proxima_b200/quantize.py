@@ -162,6 +162,27 @@ def kmeans(points, dim: int, k: int, max_iterations: int, rng: ChaCha8Rng | None
                       info.screen_passes, info.screen_ms)
 
 
+def kmeans_sharded(points, dim: int, k: int, max_iterations: int, init, context) -> Clustering:
+    """k-means over points sharded across the ranks of `context`'s communicator
+    (pxc_kmeans_sharded): `points` is this rank's CUDA tensor (its consecutive range
+    of the global point order), `init` the k x dim start shared by every rank.
+    Returns the global centroids and this rank's assignment."""
+    import torch
+
+    pts = points.contiguous().view(-1)
+    n = pts.numel() // dim
+    d_init = torch.as_tensor(init, dtype=torch.float32, device=pts.device).contiguous().view(-1)
+    kk = d_init.numel() // dim
+    cent = torch.empty((kk, dim), dtype=torch.float32, device=pts.device)
+    assign = torch.empty((n,), dtype=torch.int32, device=pts.device)
+    info = N.PxcKmeansInfo()
+    N.call("pxc_kmeans_sharded", context.handle, pts.data_ptr(), n, dim, k, max_iterations, d_init.data_ptr(),
+           cent.data_ptr(), assign.data_ptr(), C.byref(info), torch.cuda.current_stream(pts.device).cuda_stream)
+    return Clustering(cent[:info.k].cpu().numpy(), info.inertia, info.iterations,
+                      assign.cpu().numpy().view(np.uint32), info.path, info.reseeded, info.rescanned,
+                      info.screen_passes, info.screen_ms)
+
+
 CENTROIDS_PER_SUBSPACE = 256
 
 

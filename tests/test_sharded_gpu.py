@@ -147,3 +147,220 @@ def test_two_rank_sharded_flat_equals_unsharded():
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     res = q.get(timeout=10)
     assert res == {"u8": True, "real cosine": True}, res
+
+
+def _merge_by_total_order(parts, k):
+    """Union of per-shard (ids, dist, len) answers ordered by (total_cmp(distance), id), first k."""
+    nq = parts[0][0].shape[0]
+    ids = np.zeros((nq, k), np.uint64)
+    dist = np.zeros((nq, k), np.float32)
+    lens = np.zeros(nq, np.uint32)
+    for q in range(nq):
+        cand = []
+        for pi, pd, pl in parts:
+            for j in range(int(pl[q])):
+                b = int(pd[q, j:j + 1].view(np.int32)[0])
+                key = b ^ 0x7FFFFFFF if b < 0 else b
+                cand.append((key, int(pi[q, j]), pd[q, j]))
+        cand.sort(key=lambda c: (c[0], c[1]))
+        cand = cand[:k]
+        lens[q] = len(cand)
+        for j, c in enumerate(cand):
+            ids[q, j], dist[q, j] = c[1], c[2]
+    return ids, dist, lens
+
+
+def _ivf_shard_answer(data, lo, hi, cent, books, m, queries, k, nprobe, rerank):
+    from oracle import pxo
+
+    rows = data[lo:hi]
+    list_of = np.zeros(len(rows), np.uint32)
+    codes = np.zeros((len(rows), m), np.uint8)
+    pxo.lib().pxo_ivfpq_encode_all(rows.ctypes.data, None, len(rows), rows.shape[1], cent.ctypes.data, len(cent),
+                                   books.ctypes.data, m, list_of.ctypes.data, codes.ctypes.data, pxo.threads())
+    return pxo.ivfpq_search(rows, cent, books, m, list_of, codes, queries, k, nprobe, rerank,
+                            ids=np.arange(lo, hi, dtype=np.uint64))
+
+
+def test_single_rank_ivfpq_sharded_equals_search():
+    from oracle import pxo
+    from proxima_b200 import _native as N
+    from proxima_b200 import fixtures
+    from proxima_b200.index import Context
+    from proxima_b200.ivfpq import IvfPqIndex
+
+    ctx = Context(0)
+    N.call("pxc_ctx_init_comm", ctx.handle, (C.c_uint8 * 128)(), 1, 0, 5000)
+    data = fixtures.blobs_u8(20_000, 32, 64, 3, 4) + np.float32(0.25)
+    queries = fixtures.blobs_u8(200, 32, 64, 3, 5)
+    cent, books, _, _, _ = pxo.ivfpq_train(data, 64, 8, 4, 10_000, 0x77)
+    idx = IvfPqIndex(32, 64, 8, context=ctx)
+    idx.from_parts(cent, books)
+    idx.set_store(data, ids=np.arange(500, 500 + len(data), dtype=np.uint64))
+    idx.encode_all()
+    q = torch.from_numpy(queries).cuda()
+    out = [torch.empty((200, 10), dtype=torch.int64, device="cuda"), torch.empty((200, 10), device="cuda"),
+           torch.empty(200, dtype=torch.int32, device="cuda")]
+    idx.search_sharded_device(q, 10, 6, 50, *out, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    ref = _ivf_shard_answer(data, 0, len(data), cent, books, 8, queries, 10, 6, 50)
+    ref = (ref[0] + np.uint64(500), ref[1], ref[2])
+    _same((out[0].cpu().numpy().view(np.uint64), out[1].cpu().numpy(), out[2].cpu().numpy().view(np.uint32)), ref,
+          "ivf-pq sharded, one rank")
+    idx.close()
+    ctx.close()
+
+
+def _ivf_rank(rank, world, port, out):
+    import sys
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from oracle import pxo
+    from proxima_b200 import fixtures
+    from proxima_b200.index import Context
+    from proxima_b200.ivfpq import IvfPqIndex
+    from proxima_b200.sharded import init_comm, shard_range
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        ctx = Context(rank)
+        init_comm(ctx, timeout_ms=30_000)
+        data = fixtures.blobs_u8(40_000, 32, 64, 3, 4)
+        queries = fixtures.blobs_u8(300, 32, 64, 3, 5)
+        cent, books, _, _, _ = pxo.ivfpq_train(data, 64, 8, 4, 10_000, 0x77)  # replicated parts
+        lo, hi = shard_range(len(data), rank, world)
+        idx = IvfPqIndex(32, 64, 8, context=ctx)
+        idx.from_parts(cent, books)
+        idx.set_store(data[lo:hi], ids=np.arange(lo, hi, dtype=np.uint64))
+        idx.encode_all()
+        q = torch.from_numpy(queries).cuda()
+        res = [torch.empty((300, 10), dtype=torch.int64, device="cuda"), torch.empty((300, 10), device="cuda"),
+               torch.empty(300, dtype=torch.int32, device="cuda")]
+        idx.search_sharded_device(q, 10, 8, 100, *res, torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        if rank == 0:
+            parts = [_ivf_shard_answer(data, *shard_range(len(data), r, world), cent, books, 8, queries, 10, 8, 100)
+                     for r in range(world)]
+            ri, rd, rl = _merge_by_total_order(parts, 10)
+            gi = res[0].cpu().numpy().view(np.uint64)
+            gd = res[1].cpu().numpy()
+            gl = res[2].cpu().numpy().view(np.uint32)
+            out.put(bool(np.array_equal(gl, rl) and np.array_equal(gi, ri) and
+                         np.array_equal(gd.view(np.uint32), rd.view(np.uint32))))
+        idx.close()
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_two_rank_sharded_ivfpq_equals_the_oracle_composition():
+    """Lists split by rows over two ranks, each probing the same lists on its
+    shard with its own shortlist, then the exchange: equal to the oracle's
+    per-shard search_prepared merged by (total_cmp, id)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    mctx = mp.get_context("spawn")
+    q = mctx.Queue()
+    port = _free_port()
+    procs = [mctx.Process(target=_ivf_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(240)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert q.get(timeout=10) is True
+
+
+def test_single_rank_sharded_kmeans_equals_kmeans():
+    """One rank: the sharded k-means (exchanges included) is the unsharded run
+    bit for bit, empty-cluster re-seeding included (duplicated init rows)."""
+    from proxima_b200 import _native as N
+    from proxima_b200 import fixtures
+    from proxima_b200.index import Context
+    from proxima_b200.quantize import kmeans, kmeans_sharded
+
+    ctx = Context(0)
+    N.call("pxc_ctx_init_comm", ctx.handle, (C.c_uint8 * 128)(), 1, 0, 5000)
+    pts = fixtures.sphere_blobs(20_000, 48, 60, 21, 22, 0.05)
+    init = pts[:300].copy()
+    init[150:200] = init[100:150]  # duplicates: the higher copies end empty and are re-seeded
+    d = torch.from_numpy(pts).cuda()
+    a = kmeans(d, 48, 300, 8, init=init, context=ctx, want_assignment=True)
+    b = kmeans_sharded(d, 48, 300, 8, init, ctx)
+    assert b.reseeded > 0 and a.reseeded == b.reseeded
+    assert a.iterations == b.iterations and a.inertia == b.inertia
+    assert np.array_equal(a.centroids.view(np.uint32), b.centroids.view(np.uint32))
+    assert np.array_equal(a.assignment, b.assignment)
+    ctx.close()
+
+
+def _km_rank(rank, world, port, out):
+    import sys
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from oracle import pxo
+    from proxima_b200 import fixtures
+    from proxima_b200.index import Context
+    from proxima_b200.quantize import kmeans_sharded
+    from proxima_b200.sharded import init_comm, shard_range
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        ctx = Context(rank)
+        init_comm(ctx, timeout_ms=30_000)
+        pts = fixtures.sphere_blobs(60_000, 64, 200, 31, 32, 0.05)
+        init = pts[:512].copy()
+        init[300:340] = init[200:240]  # empty clusters to re-seed across the ranks
+        lo, hi = shard_range(len(pts), rank, world)
+        got = kmeans_sharded(torch.from_numpy(pts[lo:hi]).cuda(), 64, 512, 10, init, ctx)
+        assigns = [torch.empty(shard_range(len(pts), r, world)[1] - shard_range(len(pts), r, world)[0],
+                               dtype=torch.int32, device="cuda") for r in range(world)]
+        dist.all_gather(assigns, torch.from_numpy(got.assignment.view(np.int32)).cuda())
+        if rank == 0:
+            cent, assign, inertia, iters = pxo.kmeans(pts, 512, 10, init=init)
+            ga = np.concatenate([a.cpu().numpy().view(np.uint32) for a in assigns])
+            rel = np.abs(got.centroids - cent).max() / max(np.abs(cent).max(), 1e-30)
+            out.put({"iterations": got.iterations == iters, "reseeded": got.reseeded > 0,
+                     "assign_diff": int((ga != assign).sum()), "centroid_rel": float(rel),
+                     "inertia_rel": abs(got.inertia - inertia) / inertia})
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_two_rank_sharded_kmeans_matches_the_oracle():
+    """Points split over two ranks: the same iterations, re-seeds and
+    assignments as the oracle's kmeans over all points, centroids within 1e-3
+    relative (the per-cluster f64 sums are folded in rank order)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    mctx = mp.get_context("spawn")
+    q = mctx.Queue()
+    port = _free_port()
+    procs = [mctx.Process(target=_km_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(240)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = q.get(timeout=10)
+    assert res["iterations"] and res["reseeded"], res
+    assert res["assign_diff"] <= 60 and res["centroid_rel"] < 1e-3 and res["inertia_rel"] < 1e-6, res
