@@ -129,6 +129,16 @@ void pxf_blobs_u8(uint64_t row_begin, uint64_t n, uint64_t dim, uint64_t nblobs,
   });
 }
 
+// Rows row_first, row_first + stride, ... (n of them) of pxf_blobs_u8's
+// stream: a stride sample without generating the rows in between.
+void pxf_blobs_u8_strided(uint64_t row_first, uint64_t stride, uint64_t n, uint64_t dim, uint64_t nblobs,
+                          uint64_t centre_seed, uint64_t noise_seed, double sigma, float* out, int threads) {
+  parallel_rows(n, threads, [&](uint64_t b, uint64_t e) {
+    for (uint64_t r = b; r < e; ++r) pxf_blobs_u8(row_first + r * stride, 1, dim, nblobs, centre_seed, noise_seed,
+                                                   sigma, out + r * dim, 1);
+  });
+}
+
 // The same blobs without rounding or clipping: real-valued rows (the
 // non-integer counterpart of C2 for the f16 tensor-core screen).
 void pxf_blobs_f32(uint64_t row_begin, uint64_t n, uint64_t dim, uint64_t nblobs,

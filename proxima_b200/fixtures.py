@@ -31,9 +31,11 @@ def _load():
         lib.pxf_splitmix_corpus.argtypes = [u64, u64, u64, vp]
         lib.pxf_blobs_u8.argtypes = [u64, u64, u64, u64, u64, u64, f64, vp, i32]
         lib.pxf_blobs_f32.argtypes = [u64, u64, u64, u64, u64, u64, f64, vp, i32]
+        lib.pxf_blobs_u8_strided.argtypes = [u64, u64, u64, u64, u64, u64, u64, f64, vp, i32]
         lib.pxf_sphere_blobs.argtypes = [u64, u64, u64, u64, u64, u64, f64, vp, i32]
         lib.pxf_uniform_int.argtypes = [u64, u64, u64, C.c_int64, u64, vp]
         for f in (lib.pxf_quickstart, lib.pxf_splitmix_corpus, lib.pxf_blobs_u8, lib.pxf_blobs_f32,
+                  lib.pxf_blobs_u8_strided,
                   lib.pxf_sphere_blobs, lib.pxf_uniform_int):
             f.restype = None
         _lib = lib
@@ -64,6 +66,15 @@ def blobs_u8(n: int, dim: int, nblobs: int, centre_seed: int, noise_seed: int,
     out = np.empty((n, dim), dtype=np.float32)
     _load().pxf_blobs_u8(row_begin, n, dim, nblobs, centre_seed, noise_seed, sigma,
                          out.ctypes.data, _threads())
+    return out
+
+
+def blobs_u8_strided(n: int, stride: int, dim: int, nblobs: int, centre_seed: int, noise_seed: int,
+                     sigma: float = 20.0, row_first: int = 0) -> np.ndarray:
+    """Rows row_first + i * stride (i < n) of blobs_u8's stream: a stride sample."""
+    out = np.empty((n, dim), dtype=np.float32)
+    _load().pxf_blobs_u8_strided(row_first, stride, n, dim, nblobs, centre_seed, noise_seed, sigma,
+                                 out.ctypes.data, _threads())
     return out
 
 
