@@ -590,7 +590,8 @@ def run_ivfpq_sharded(args):
     for b in range(0, hi - lo, chunk):
         e = min(hi - lo, b + chunk)
         rows = d_vec[b:e].cpu().numpy()
-        N.call("pxc_flat_sync", fh, N.ptr(rows), N.ptr(np.arange(lo + b, lo + e, dtype=np.uint64)), None, b, e - b)
+        row_ids = np.arange(lo + b, lo + e, dtype=np.uint64)  # kept alive across the call
+        N.call("pxc_flat_sync", fh, N.ptr(rows), N.ptr(row_ids), None, b, e - b)
     stream = torch.cuda.Stream(dev)
     torch.cuda.set_stream(stream)
     sp = stream.cuda_stream

@@ -210,7 +210,8 @@ pxc_status pxc_flat_search_sharded(pxc_flat* h, const float* d_queries, uint32_t
                                    const uint64_t* d_bitmap, uint64_t* d_out_ids, float* d_out_dist,
                                    uint32_t* d_out_len, void* stream, pxc_error* err);
 /* The same exchange for any local top-k_in lists (nq x k_in ids and
- * distances, nq lengths; DEVICE buffers), e.g. an SQ or IVF-PQ shard's answer:
+ * distances, nq lengths; DEVICE buffers), each sorted by (total_cmp, id) as
+ * every search here returns them, e.g. an SQ or IVF-PQ shard's answer:
  * allgather over the communicator and merge into the global top-k. */
 pxc_status pxc_topk_exchange(pxc_ctx* ctx, const uint64_t* d_ids, const float* d_dist, const uint32_t* d_lens,
                              uint32_t nq, uint32_t k_in, uint32_t k, uint64_t* d_out_ids, float* d_out_dist,

@@ -221,7 +221,8 @@ def call(name: str, *args) -> None:
 
 
 def ptr(arr) -> int | None:
-    """Address of a numpy array or torch tensor (None passes through)."""
+    """Address of a numpy array or torch tensor (None passes through). The caller
+    keeps `arr` alive until the call that uses the address returns."""
     if arr is None:
         return None
     if hasattr(arr, "data_ptr"):

@@ -192,6 +192,59 @@ __global__ void merge_parts_kernel(const uint64_t* __restrict__ ids, const float
   if (threadIdx.x == 0) out_len[q] = take;
 }
 
+// Merge of part lists that are each sorted by (total_cmp(distance), id), as
+// every search of this library returns them: one warp per query; each
+// candidate's output position is its index in its own list plus, per other
+// list, the number of entries ahead of it (binary search; an equal entry of a
+// lower part counts as ahead), so positions are distinct and no sort is needed.
+__device__ __forceinline__ bool entry_before(uint32_t ka, uint64_t ia, uint32_t kb, uint64_t ib) {
+  return ka < kb || (ka == kb && ia < ib);
+}
+__global__ void __launch_bounds__(128) merge_sorted_kernel(const uint64_t* __restrict__ ids,
+                                                           const float* __restrict__ dist,
+                                                           const uint32_t* __restrict__ lens, uint32_t nparts,
+                                                           uint32_t nq, uint32_t k_in, uint32_t k, size_t stride_ids,
+                                                           size_t stride_dist, size_t stride_len,
+                                                           uint64_t* __restrict__ out_ids, float* __restrict__ out_dist,
+                                                           uint32_t* __restrict__ out_len) {
+  const uint32_t q = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const uint32_t lane = threadIdx.x & 31;
+  if (q >= nq) return;
+  const size_t row = (size_t)q * k_in;
+  uint32_t total = 0;
+  for (uint32_t p = 0; p < nparts; ++p) total += min(lens[p * stride_len + q], k_in);
+  for (uint32_t c = lane; c < nparts * k_in; c += 32) {
+    const uint32_t p = c / k_in, i = c - p * k_in;
+    const uint32_t len = min(lens[p * stride_len + q], k_in);
+    if (i >= len) continue;
+    const uint32_t key = order_key(dist[p * stride_dist + row + i]);
+    const uint64_t id = ids[p * stride_ids + row + i];
+    uint32_t pos = i;
+    for (uint32_t o = 0; o < nparts && pos < k; ++o) {
+      if (o == p) continue;
+      const uint32_t lo_len = min(lens[o * stride_len + q], k_in);
+      // entries of list o ahead of (key, id): strictly before, or equal when o < p
+      uint32_t a = 0, b = lo_len;
+      while (a < b) {
+        const uint32_t mid = (a + b) >> 1;
+        const uint32_t km = order_key(dist[o * stride_dist + row + mid]);
+        const uint64_t im = ids[o * stride_ids + row + mid];
+        const bool ahead = entry_before(km, im, key, id) || (o < p && km == key && im == id);
+        if (ahead)
+          a = mid + 1;
+        else
+          b = mid;
+      }
+      pos += a;
+    }
+    if (pos < k) {
+      out_ids[(size_t)q * k + pos] = id;
+      out_dist[(size_t)q * k + pos] = dist[p * stride_dist + row + i];
+    }
+  }
+  if (lane == 0) out_len[q] = min(total, k);
+}
+
 // Shared-memory size and launch of the merge for `total` candidates per query.
 static void launch_merge(const uint64_t* ids, const float* dist, const uint32_t* lens, uint32_t nparts, uint32_t nq,
                          uint32_t k_in, uint32_t k, size_t stride_ids, size_t stride_dist, size_t stride_len,
@@ -227,7 +280,10 @@ void exchange_and_merge(pxc_ctx* ctx, const unsigned char* send, uint32_t nq, ui
   const uint64_t* ids = reinterpret_cast<const uint64_t*>(all);
   const float* dist = reinterpret_cast<const float*>(all + (size_t)nq * k_in * 8);
   const uint32_t* lens = reinterpret_cast<const uint32_t*>(all + (size_t)nq * k_in * 12);
-  launch_merge(ids, dist, lens, nranks, nq, k_in, k, seg / 8, seg / 4, seg / 4, d_out_ids, d_out_dist, d_out_len, s);
+  // every rank's lists come sorted from its search
+  merge_sorted_kernel<<<(nq + 3) / 4, 128, 0, s>>>(ids, dist, lens, nranks, nq, k_in, k, seg / 8, seg / 4, seg / 4,
+                                                   d_out_ids, d_out_dist, d_out_len);
+  PXC_CUDA(cudaGetLastError());
   ctx->launches += 1;
   wait_comm(ctx, s, "candidate exchange");
 }

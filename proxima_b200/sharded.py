@@ -77,7 +77,8 @@ class ShardedFlat:
         N.call("pxc_flat_create", ctx.handle, dim, metric, C.byref(h))
         self.handle = h
         gids = np.arange(first_id, first_id + rows.shape[0], dtype=np.uint64)
-        N.call("pxc_flat_sync", h, N.ptr(np.ascontiguousarray(rows, dtype=np.float32)), N.ptr(gids),
+        rows = np.ascontiguousarray(rows, dtype=np.float32)  # a reference held across the call
+        N.call("pxc_flat_sync", h, N.ptr(rows), N.ptr(gids),
                None, 0, rows.shape[0])
 
     def search(self, q_dev: torch.Tensor, k: int, stream_ptr: int):
