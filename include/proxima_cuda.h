@@ -132,6 +132,16 @@ uint64_t pxc_flat_len(const pxc_flat* h);
 pxc_status pxc_flat_search(pxc_flat* h, const float* queries, uint32_t nq, uint32_t k,
                            const uint64_t* bitmap, uint64_t* out_ids, float* out_dist,
                            uint32_t* out_len, pxc_error* err);
+/* The same search with the filter given as MetadataFilter conditions
+ * (see pxc_columns below) over `cols`, the handle's metadata columns indexed by
+ * slot: the accepted set is computed on the device, no bitmap crosses the
+ * boundary. HOST queries and outputs. */
+typedef struct pxc_columns pxc_columns;
+typedef struct pxc_condition pxc_condition;
+typedef struct pxc_operand pxc_operand;
+pxc_status pxc_flat_search_where(pxc_flat* h, pxc_columns* cols, const pxc_condition* conds, uint32_t ncond,
+                                 const pxc_operand* operands, uint32_t noperands, const float* queries, uint32_t nq,
+                                 uint32_t k, uint64_t* out_ids, float* out_dist, uint32_t* out_len, pxc_error* err);
 /* Same, with DEVICE buffers on the context's device, ordered on `stream`
  * (a cudaStream_t; NULL = the context's stream). The call waits on the
  * stream for small host decisions (whether the queries are integers in
@@ -177,6 +187,61 @@ uint32_t pxc_flat_last_redone(const pxc_flat* h);
 pxc_status pxc_flat_search_noalloc(pxc_flat* h, const float* d_queries, uint32_t nq, uint32_t k,
                                    uint64_t* d_out_ids, float* d_out_dist, uint32_t* d_out_len,
                                    void* stream, pxc_error* err);
+
+/* ---- typed metadata filters on the device ----
+ * MetadataFilter (crates/proxima-server/src/filter.rs:58-75, 216-256)
+ * compiled to conditions over typed device columns and evaluated by one
+ * thread per slot into the bitmap over slots that every search entry point
+ * takes (pxc_flat_search_device, pxc_ivfpq_search_device, pxc_sq_search_device
+ * and the sharded forms): the per-slot host closure pass is gone. A column
+ * holds one MetadataValue per slot as a type tag and a 64-bit payload: Int
+ * the i64, Float the f64 bits, Bool 0/1, Text a code the caller assigns per
+ * distinct string (equal strings, equal codes). Tags follow MetadataValue's
+ * declaration order (crates/proxima-core/src/metadata.rs:21-31). */
+#define PXC_VALUE_ABSENT 0
+#define PXC_VALUE_TEXT 1
+#define PXC_VALUE_INT 2
+#define PXC_VALUE_FLOAT 3
+#define PXC_VALUE_BOOL 4
+/* Condition operators, in the order of filter.rs's Condition enum. */
+#define PXC_COND_EQ 0
+#define PXC_COND_NE 1
+#define PXC_COND_GT 2
+#define PXC_COND_GE 3
+#define PXC_COND_LT 4
+#define PXC_COND_LE 5
+#define PXC_COND_IN 6
+#define PXC_COND_EXISTS 7
+/* One condition on one column. eq / ne: (tag, value) is the operand; gt, gte,
+ * lt, lte: a numeric bound (tag INT or FLOAT); in: `count` operands starting at
+ * operands[value]; exists: value != 0 means exists:true. All conditions must
+ * hold; an absent field fails all but exists:false. */
+struct pxc_condition {
+  uint32_t column;
+  uint32_t op;
+  uint32_t tag;
+  uint32_t count;
+  int64_t value;
+};
+struct pxc_operand {
+  uint32_t tag;
+  uint32_t reserved;
+  int64_t value;
+};
+pxc_status pxc_columns_create(pxc_ctx* ctx, pxc_columns** out, pxc_error* err);
+void pxc_columns_destroy(pxc_columns* cols);
+/* Slots [slot_begin, slot_begin + nslots) of column `column` (< 4096): HOST
+ * tags and payloads. Slots never written read as absent. */
+pxc_status pxc_columns_set(pxc_columns* cols, uint32_t column, const uint8_t* tags, const int64_t* values,
+                           uint64_t slot_begin, uint64_t nslots, pxc_error* err);
+/* Forget every slot at or beyond nslots (after the store shrank). */
+pxc_status pxc_columns_truncate(pxc_columns* cols, uint64_t nslots, pxc_error* err);
+/* The accepted slots among [0, nslots) as a DEVICE bitmap of ceil(nslots/64)
+ * words (bit s & 63 of word s/64), ordered on `stream`; conditions and operands
+ * are HOST arrays. Returns after the bitmap is written. */
+pxc_status pxc_columns_eval(pxc_columns* cols, uint64_t nslots, const pxc_condition* conds, uint32_t ncond,
+                            const pxc_operand* operands, uint32_t noperands, uint64_t* d_bitmap, void* stream,
+                            pxc_error* err);
 
 /* ---- multi-GPU: the context's communicator and the candidate exchange ----
  * The reference is single-process; this is the data-parallel form of its
@@ -426,6 +491,13 @@ pxc_status pxc_ivfpq_get_parts(pxc_ivfpq* h, float* centroids, float* codebooks,
 pxc_status pxc_ivfpq_search(pxc_ivfpq* h, const float* queries, uint32_t nq, uint32_t k,
                             uint32_t nprobe, uint32_t rerank, const uint64_t* bitmap,
                             uint64_t* out_ids, float* out_dist, uint32_t* out_len, pxc_error* err);
+/* The same search with the filter given as MetadataFilter conditions over
+ * the handle's metadata columns (pxc_columns), evaluated on the device. HOST
+ * queries and outputs. */
+pxc_status pxc_ivfpq_search_where(pxc_ivfpq* h, pxc_columns* cols, const pxc_condition* conds, uint32_t ncond,
+                                  const pxc_operand* operands, uint32_t noperands, const float* queries, uint32_t nq,
+                                  uint32_t k, uint32_t nprobe, uint32_t rerank, uint64_t* out_ids, float* out_dist,
+                                  uint32_t* out_len, pxc_error* err);
 /* Same with DEVICE buffers on `stream` (NULL: the context stream); returns
  * once enqueued. */
 pxc_status pxc_ivfpq_search_device(pxc_ivfpq* h, const float* d_queries, uint32_t nq, uint32_t k,

@@ -360,3 +360,95 @@ def ivfpq_search_csr(vectors, centroids, books, m: int, list_off, list_slot, cod
                                _p(lo), _p(ls), _p(cd), _p(q), nq, k, nprobe, rerank, None, _p(out_ids), _p(out_d),
                                _p(out_len), nthreads or threads())
     return out_ids[:, :k], out_d[:, :k], out_len
+
+
+# ---- crates/proxima-server/src/filter.rs (the checker for the device filter) ----
+def _filter_scalar(v):
+    """scalar_value (filter.rs:171-183): (variant, payload)."""
+    if isinstance(v, bool):
+        return ("Bool", v)
+    if isinstance(v, str):
+        return ("Text", v)
+    if isinstance(v, (int, float, np.integer, np.floating)):
+        f = float(v)
+        if f == f and abs(f) != float("inf") and f == int(f) and abs(f) < 9.007e15:
+            return ("Int", int(f))
+        return ("Float", f)
+    raise ValueError("filter needs a string, number or boolean")
+
+
+def _meta_value(v):
+    """MetadataValue of a Python value (crates/proxima-core/src/metadata.rs:21-31), no coercion."""
+    if v is None:
+        return None
+    if isinstance(v, bool):
+        return ("Bool", v)
+    if isinstance(v, (int, np.integer)):
+        return ("Int", int(v))
+    if isinstance(v, (float, np.floating)):
+        return ("Float", float(v))
+    return ("Text", v)
+
+
+def _f64_total_key(f):
+    import struct
+    b = struct.unpack("<q", struct.pack("<d", f))[0]
+    return b ^ ((b >> 63) & 0x7FFFFFFFFFFFFFFF)
+
+
+def _number_compare(bound, value):
+    """Number::compare (filter.rs:81-97)."""
+    if bound[0] == "Int" and value[0] == "Int":
+        return (value[1] > bound[1]) - (value[1] < bound[1])
+    if value[0] == "Float" and bound[0] in ("Float", "Int"):
+        a, b = _f64_total_key(value[1]), _f64_total_key(float(bound[1]))
+        return (a > b) - (a < b)
+    return None
+
+
+def metadata_filter_accepts(filter_obj: dict, metadata: dict) -> bool:
+    """MetadataFilter::parse (filter.rs:122-200) then Filter::accepts (:216-256), restated."""
+    conds = []
+    for field, cond in filter_obj.items():
+        if isinstance(cond, dict):
+            for op, operand in cond.items():
+                if op == "in":
+                    conds.append((field, op, [_filter_scalar(x) for x in operand]))
+                elif op == "exists":
+                    conds.append((field, op, bool(operand)))
+                elif op in ("gt", "gte", "lt", "lte"):
+                    conds.append((field, op, _filter_scalar(operand)))
+                else:
+                    conds.append((field, op, _filter_scalar(operand)))
+        else:
+            conds.append((field, "eq", _filter_scalar(cond)))
+    conds.sort(key=lambda c: c[0])
+    for field, op, operand in conds:
+        value = _meta_value(metadata.get(field)) if metadata else None
+        if op == "exists":
+            held = (value is not None) == operand
+        elif value is None:
+            held = False
+        elif op == "eq":
+            held = value[0] == operand[0] and value[1] == operand[1]
+        elif op == "ne":
+            held = not (value[0] == operand[0] and value[1] == operand[1])
+        elif op == "in":
+            held = any(value[0] == o[0] and value[1] == o[1] for o in operand)
+        else:
+            o = _number_compare(operand, value)
+            held = o is not None and {"gt": o == 1, "gte": o in (0, 1), "lt": o == -1, "lte": o in (-1, 0)}[op]
+        if not held:
+            return False
+    return True
+
+
+def slot_bitmap(accepted) -> np.ndarray:
+    """Bitmap over slots from one bool per slot (bit s & 63 of word s / 64)."""
+    a = np.asarray(accepted, dtype=bool)
+    words = np.zeros((a.size + 63) // 64, dtype=np.uint64)
+    if a.size:
+        packed = np.packbits(a, bitorder="little")
+        packed = np.concatenate([packed, np.zeros(words.size * 8 - packed.size, dtype=np.uint8)])
+        words[:] = packed.view(np.uint64)
+    return words

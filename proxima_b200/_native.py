@@ -70,6 +70,17 @@ class PxcRng(C.Structure):
     ]
 
 
+class PxcCondition(C.Structure):
+    """pxc_condition: one compiled MetadataFilter condition on one device column."""
+
+    _fields_ = [("column", C.c_uint32), ("op", C.c_uint32), ("tag", C.c_uint32), ("count", C.c_uint32),
+                ("value", C.c_int64)]
+
+
+class PxcOperand(C.Structure):
+    _fields_ = [("tag", C.c_uint32), ("reserved", C.c_uint32), ("value", C.c_int64)]
+
+
 class PxcIntRange(C.Structure):
     """pxc_int_range: lo <= value <= hi on an integer metadata column."""
 
@@ -105,6 +116,15 @@ SIGNATURES: dict[str, tuple] = {
     "pxc_topk_merge": (C.c_int32, [vp, vp, vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
                                    vp, vp, vp, vp, C.POINTER(PxcError)]),
     "pxc_ctx_set_option": (C.c_int32, [vp, C.c_char_p, C.c_int64, C.POINTER(PxcError)]),
+    "pxc_columns_create": (C.c_int32, [vp, C.POINTER(vp), C.POINTER(PxcError)]),
+    "pxc_columns_destroy": (None, [vp]),
+    "pxc_columns_set": (C.c_int32, [vp, C.c_uint32, vp, vp, C.c_uint64, C.c_uint64, C.POINTER(PxcError)]),
+    "pxc_columns_truncate": (C.c_int32, [vp, C.c_uint64, C.POINTER(PxcError)]),
+    "pxc_columns_eval": (C.c_int32, [vp, C.c_uint64, vp, C.c_uint32, vp, C.c_uint32, vp, vp, C.POINTER(PxcError)]),
+    "pxc_flat_search_where": (C.c_int32, [vp, vp, vp, C.c_uint32, vp, C.c_uint32, vp, C.c_uint32, C.c_uint32, vp, vp,
+                                          vp, C.POINTER(PxcError)]),
+    "pxc_ivfpq_search_where": (C.c_int32, [vp, vp, vp, C.c_uint32, vp, C.c_uint32, vp, C.c_uint32, C.c_uint32,
+                                           C.c_uint32, C.c_uint32, vp, vp, vp, C.POINTER(PxcError)]),
     "pxc_comm_unique_id": (C.c_int32, [vp, C.POINTER(PxcError)]),
     "pxc_ctx_init_comm": (C.c_int32, [vp, vp, C.c_int32, C.c_int32, C.c_uint32, C.POINTER(PxcError)]),
     "pxc_ctx_comm_size": (C.c_int32, [vp]),

@@ -1564,6 +1564,36 @@ pxc_status pxc_flat_search_sharded(pxc_flat* h, const float* d_queries, uint32_t
   });
 }
 
+}  // extern "C"
+
+namespace {
+// The host-buffer search, with the filter given as a HOST bitmap, or as
+// conditions evaluated on the device into the bitmap (where != nullptr).
+struct Where {
+  pxc_columns* cols;
+  const pxc_condition* conds;
+  uint32_t ncond;
+  const pxc_operand* ops;
+  uint32_t nops;
+};
+void flat_search_host(pxc_flat* h, const float* queries, uint32_t nq, uint32_t k, const uint64_t* bitmap,
+                      const Where* where, uint64_t* out_ids, float* out_dist, uint32_t* out_len);
+}  // namespace
+
+extern "C" {
+
+pxc_status pxc_flat_search_where(pxc_flat* h, pxc_columns* cols, const pxc_condition* conds, uint32_t ncond,
+                                 const pxc_operand* operands, uint32_t noperands, const float* queries, uint32_t nq,
+                                 uint32_t k, uint64_t* out_ids, float* out_dist, uint32_t* out_len, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(h != nullptr && cols != nullptr, "handle", 0, "null handle");
+    PXC_CONFIG(k <= PXC_MAX_K, "k", k, "exceeds the 16777216 result ceiling");
+    if (nq == 0) return;
+    const Where w{cols, conds, ncond, operands, noperands};
+    flat_search_host(h, queries, nq, k, nullptr, &w, out_ids, out_dist, out_len);
+  });
+}
+
 pxc_status pxc_flat_search(pxc_flat* h, const float* queries, uint32_t nq, uint32_t k,
                            const uint64_t* bitmap, uint64_t* out_ids, float* out_dist,
                            uint32_t* out_len, pxc_error* err) {
@@ -1571,6 +1601,16 @@ pxc_status pxc_flat_search(pxc_flat* h, const float* queries, uint32_t nq, uint3
     PXC_CONFIG(h != nullptr, "handle", 0, "null flat handle");
     PXC_CONFIG(k <= PXC_MAX_K, "k", k, "exceeds the 16777216 result ceiling");
     if (nq == 0) return;
+    flat_search_host(h, queries, nq, k, bitmap, nullptr, out_ids, out_dist, out_len);
+  });
+}
+
+}  // extern "C"
+
+namespace {
+void flat_search_host(pxc_flat* h, const float* queries, uint32_t nq, uint32_t k, const uint64_t* bitmap,
+                      const Where* where, uint64_t* out_ids, float* out_dist, uint32_t* out_len) {
+  {
     std::lock_guard<std::mutex> lock(h->mu);
     DeviceGuard g(h->ctx->device);
     cudaStream_t s = h->ctx->stream;
@@ -1588,15 +1628,21 @@ pxc_status pxc_flat_search(pxc_flat* h, const float* queries, uint32_t nq, uint3
       ddist.reserve((size_t)nq * k);
     }
     PXC_CUDA(cudaMemcpyAsync(dq.p, queries, (size_t)nq * dim * sizeof(float), cudaMemcpyHostToDevice, s));
-    if (bitmap) {
+    const bool filtered = bitmap != nullptr || where != nullptr;
+    if (filtered) {
       if (h->dirty) rebuild_mirror(h, s);
       uint64_t words = (h->nslots + 63) / 64;
-      if (words) {
-        dbm.reserve(words);
+      dbm.reserve(std::max<uint64_t>(words, 1));
+      if (words && bitmap)
         PXC_CUDA(cudaMemcpyAsync(dbm.p, bitmap, words * sizeof(uint64_t), cudaMemcpyHostToDevice, s));
+      if (words && where) {
+        pxc_error e{};
+        if (pxc_columns_eval(where->cols, h->nslots, where->conds, where->ncond, where->ops, where->nops, dbm.p, s,
+                             &e) != PXC_OK)
+          throw make_failure((pxc_status)e.code, e.a, e.b, e.parameter, "%s", e.detail);
       }
     }
-    search_device(h, dq.p, nq, k, bitmap ? dbm.p : nullptr, dids.p, ddist.p, dlen.p, s);
+    search_device(h, dq.p, nq, k, filtered ? dbm.p : nullptr, dids.p, ddist.p, dlen.p, s);
     if (k > 0) {
       PXC_CUDA(cudaMemcpyAsync(out_ids, dids.p, (size_t)nq * k * sizeof(uint64_t), cudaMemcpyDeviceToHost, s));
       PXC_CUDA(cudaMemcpyAsync(out_dist, ddist.p, (size_t)nq * k * sizeof(float), cudaMemcpyDeviceToHost, s));
@@ -1604,10 +1650,9 @@ pxc_status pxc_flat_search(pxc_flat* h, const float* queries, uint32_t nq, uint3
     PXC_CUDA(cudaMemcpyAsync(out_len, dlen.p, nq * sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
     handoff_done(h, s);
     PXC_CUDA(cudaStreamSynchronize(s));
-  });
+  }
 }
-
-}  // extern "C"
+}  // namespace
 
 // ---------------------------------------------------------------------------
 // Allocation-free flat search (no counterpart in the reference).

@@ -1246,9 +1246,35 @@ pxc_status pxc_ivfpq_search_sharded(pxc_ivfpq* h, const float* d_queries, uint32
   });
 }
 
+static pxc_status ivfpq_search_host(pxc_ivfpq* h, const float* queries, uint32_t nq, uint32_t k, uint32_t nprobe,
+                                    uint32_t rerank, const uint64_t* bitmap, pxc_columns* cols,
+                                    const pxc_condition* conds, uint32_t ncond, const pxc_operand* operands,
+                                    uint32_t noperands, uint64_t* out_ids, float* out_dist, uint32_t* out_len,
+                                    pxc_error* err);
+
 pxc_status pxc_ivfpq_search(pxc_ivfpq* h, const float* queries, uint32_t nq, uint32_t k, uint32_t nprobe,
                             uint32_t rerank, const uint64_t* bitmap, uint64_t* out_ids, float* out_dist,
                             uint32_t* out_len, pxc_error* err) {
+  return ivfpq_search_host(h, queries, nq, k, nprobe, rerank, bitmap, nullptr, nullptr, 0, nullptr, 0, out_ids,
+                           out_dist, out_len, err);
+}
+
+pxc_status pxc_ivfpq_search_where(pxc_ivfpq* h, pxc_columns* cols, const pxc_condition* conds, uint32_t ncond,
+                                  const pxc_operand* operands, uint32_t noperands, const float* queries, uint32_t nq,
+                                  uint32_t k, uint32_t nprobe, uint32_t rerank, uint64_t* out_ids, float* out_dist,
+                                  uint32_t* out_len, pxc_error* err) {
+  if (cols == nullptr) {
+    return report(make_failure(PXC_CONFIGURATION, 0, 0, "columns", "null columns handle"), err);
+  }
+  return ivfpq_search_host(h, queries, nq, k, nprobe, rerank, nullptr, cols, conds, ncond, operands, noperands,
+                           out_ids, out_dist, out_len, err);
+}
+
+static pxc_status ivfpq_search_host(pxc_ivfpq* h, const float* queries, uint32_t nq, uint32_t k, uint32_t nprobe,
+                                    uint32_t rerank, const uint64_t* bitmap, pxc_columns* cols,
+                                    const pxc_condition* conds, uint32_t ncond, const pxc_operand* operands,
+                                    uint32_t noperands, uint64_t* out_ids, float* out_dist, uint32_t* out_len,
+                                    pxc_error* err) {
   return guarded(err, [&] {
     PXC_CONFIG(h != nullptr, "h", 0, "null handle");
     PXC_CONFIG(k <= PXC_MAX_K, "k", k, "k exceeds the maximum");
@@ -1266,10 +1292,15 @@ pxc_status pxc_ivfpq_search(pxc_ivfpq* h, const float* queries, uint32_t nq, uin
     h->io_len.reserve(nq);
     ivf::handoff_wait(h, s);
     const uint64_t* db = nullptr;
-    if (bitmap) {
+    if (bitmap || cols) {
       const uint64_t words = (h->nslots + 63) / 64;
       h->bitmap.reserve(std::max<uint64_t>(1, words));
-      if (words) PXC_CUDA(cudaMemcpyAsync(h->bitmap.p, bitmap, words * 8, cudaMemcpyHostToDevice, s));
+      if (words && bitmap) PXC_CUDA(cudaMemcpyAsync(h->bitmap.p, bitmap, words * 8, cudaMemcpyHostToDevice, s));
+      if (words && cols) {  // the conditions evaluated on the device into the bitmap
+        pxc_error e{};
+        if (pxc_columns_eval(cols, h->nslots, conds, ncond, operands, noperands, h->bitmap.p, s, &e) != PXC_OK)
+          throw make_failure((pxc_status)e.code, e.a, e.b, e.parameter, "%s", e.detail);
+      }
       db = h->bitmap.p;
     }
     PXC_CUDA(cudaMemcpyAsync(h->q_buf.p, queries, (size_t)nq * h->dim * 4, cudaMemcpyHostToDevice, s));

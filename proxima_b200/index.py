@@ -127,6 +127,10 @@ class FlatIndex:
         handle = N.vp()
         N.call("pxc_flat_create", self.ctx.handle, space.dim, int(space.metric), C.byref(handle))
         self.handle = handle
+        # device columns of the metadata fields MetadataFilters read (typed filter pushdown)
+        self._columns = None
+        self._meta_version = 0
+        self._col_version: dict[str, tuple[int, int]] = {}
 
     # ---- construction helpers (flat.rs:216-236) ----
     @classmethod
@@ -149,6 +153,9 @@ class FlatIndex:
         return idx
 
     def close(self) -> None:
+        if getattr(self, "_columns", None) is not None:
+            self._columns.close()
+            self._columns = None
         if getattr(self, "handle", None):
             self._lib.pxc_flat_destroy(self.handle)
             self.handle = None
@@ -211,6 +218,7 @@ class FlatIndex:
         self._ids[slot] = id
         self._live[slot] = 1
         self._meta[slot] = dict(metadata or {})
+        self._meta_version += 1
         self._by_id[id] = slot
         self._mark(slot, slot + 1)
 
@@ -221,6 +229,7 @@ class FlatIndex:
             raise UnknownId(id)
         self._live[slot] = 0
         self._meta[slot] = dict()
+        self._meta_version += 1
         self._free.append(slot)
         self._mark(slot, slot + 1)
 
@@ -254,11 +263,13 @@ class FlatIndex:
         if slot is None:
             raise UnknownId(int(id))
         self._meta[slot] = dict(metadata)
+        self._meta_version += 1
 
     def ids(self) -> list[int]:
         return [int(self._ids[s]) for s in range(self._next) if self._live[s]]
 
     def clear(self) -> None:
+        self._meta_version += 1
         self._live[: self._next] = 0
         self._next = 0
         self._free.clear()
@@ -285,6 +296,35 @@ class FlatIndex:
             words[:] = packed.view(np.uint64)
         return words
 
+    def _device_columns(self, flt) -> "DeviceColumns":
+        """The device columns of the fields `flt` reads, re-uploaded when the metadata changed."""
+        from .filters import DeviceColumns
+
+        if self._columns is None:
+            self._columns = DeviceColumns(self.ctx)
+        for field in flt.fields():
+            if self._col_version.get(field) != (self._meta_version, self._next):
+                vals = [self._meta[s].get(field) if self._live[s] else None for s in range(self._next)]
+                self._columns.set_values(field, vals, 0)
+                self._columns.truncate(self._next)
+                self._col_version[field] = (self._meta_version, self._next)
+        return self._columns
+
+    def search_where_prepared(self, prepared: np.ndarray, k: int, flt):
+        """Batched search with a MetadataFilter evaluated on the device (pxc_flat_search_where)."""
+        check_k(k)
+        self._sync()
+        cols = self._device_columns(flt)
+        conds, nc, ops, no = flt.compile(cols)
+        nq = prepared.shape[0]
+        ids = np.zeros((nq, max(k, 1)), dtype=np.uint64)
+        dist = np.zeros((nq, max(k, 1)), dtype=np.float32)
+        lens = np.zeros(nq, dtype=np.uint32)
+        if nq:
+            N.call("pxc_flat_search_where", self.handle, cols.handle, conds, nc, ops, no, N.ptr(prepared), nq, k,
+                   N.ptr(ids), N.ptr(dist), N.ptr(lens))
+        return ids[:, :k], dist[:, :k], lens
+
     def search_prepared_batch(self, prepared: np.ndarray, k: int, bitmap: np.ndarray | None = None):
         """Batched search of already-prepared [nq, dim] queries; returns (ids, dist, lens)."""
         check_k(k)
@@ -299,17 +339,28 @@ class FlatIndex:
         return ids[:, :k], dist[:, :k], lens
 
     def search_batch(self, queries, k: int, filter=AcceptAll) -> list[list[SearchResult]]:
-        """search for every query of a flat or 2-D array (the batched trait method)."""
+        """search for every query of a flat or 2-D array (the batched trait method). A MetadataFilter
+        is evaluated on the device; any other filter closure once per live slot on the host."""
+        from .filters import MetadataFilter
+
         check_k(k)
         prepared = self.space.prepare_batch(queries)
-        ids, dist, lens = self.search_prepared_batch(prepared, k, self._bitmap(filter))
+        if isinstance(filter, MetadataFilter):
+            ids, dist, lens = self.search_where_prepared(prepared, k, filter)
+        else:
+            ids, dist, lens = self.search_prepared_batch(prepared, k, self._bitmap(filter))
         return [[SearchResult(int(ids[q, i]), float(dist[q, i])) for i in range(int(lens[q]))]
                 for q in range(prepared.shape[0])]
 
     def search(self, query, k: int, filter=AcceptAll) -> list[SearchResult]:
+        from .filters import MetadataFilter
+
         check_k(k)
         prepared = self.space.prepare(query)[None, :]
-        ids, dist, lens = self.search_prepared_batch(prepared, k, self._bitmap(filter))
+        if isinstance(filter, MetadataFilter):
+            ids, dist, lens = self.search_where_prepared(prepared, k, filter)
+        else:
+            ids, dist, lens = self.search_prepared_batch(prepared, k, self._bitmap(filter))
         return [SearchResult(int(ids[0, i]), float(dist[0, i])) for i in range(int(lens[0]))]
 
     def search_all(self, query, k: int) -> list[SearchResult]:

@@ -29,6 +29,9 @@ class IvfPqIndex:
         self.nslots = 0
 
     def close(self) -> None:
+        if getattr(self, "_columns", None) is not None:
+            self._columns.close()
+            self._columns = None
         if getattr(self, "handle", None):
             N.load().pxc_ivfpq_destroy(self.handle)
             self.handle = None
@@ -98,6 +101,33 @@ class IvfPqIndex:
         bm = None if bitmap is None else np.ascontiguousarray(bitmap, dtype=np.uint64)
         N.call("pxc_ivfpq_search", self.handle, N.ptr(q), nq, k, nprobe, rerank, N.ptr(bm), N.ptr(ids),
                N.ptr(dist), N.ptr(lens))
+        return ids[:, :k], dist[:, :k], lens
+
+    def set_metadata(self, metadata) -> None:
+        """Per-slot metadata dicts (None or {} for none), for MetadataFilter searches."""
+        self._metadata = list(metadata)
+        self._col_fields = set()
+
+    def search_where(self, queries, k: int, nprobe: int, rerank: int, flt):
+        """search_with_nprobe with a MetadataFilter evaluated on the device (pxc_ivfpq_search_where)."""
+        from .filters import DeviceColumns
+
+        meta = getattr(self, "_metadata", [])
+        if getattr(self, "_columns", None) is None:
+            self._columns = DeviceColumns(self.ctx)
+            self._col_fields = set()
+        for field in flt.fields():
+            if field not in self._col_fields:
+                self._columns.set_values(field, [(m or {}).get(field) for m in meta], 0)
+                self._col_fields.add(field)
+        conds, nc, ops, no = flt.compile(self._columns)
+        q = np.ascontiguousarray(queries, dtype=np.float32).reshape(-1, self.dim)
+        nq = len(q)
+        ids = np.zeros((nq, max(k, 1)), dtype=np.uint64)
+        dist = np.zeros((nq, max(k, 1)), dtype=np.float32)
+        lens = np.zeros(nq, dtype=np.uint32)
+        N.call("pxc_ivfpq_search_where", self.handle, self._columns.handle, conds, nc, ops, no, N.ptr(q), nq, k,
+               nprobe, rerank, N.ptr(ids), N.ptr(dist), N.ptr(lens))
         return ids[:, :k], dist[:, :k], lens
 
     def search_device(self, d_queries, k: int, nprobe: int, rerank: int, d_ids, d_dist, d_lens, stream: int,
