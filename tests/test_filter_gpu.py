@@ -99,6 +99,8 @@ def test_ivfpq_search_with_device_filters():
         gi, gd, gl = idx.search_where(queries, 10, 8, 200, MetadataFilter.parse(raw))
         bm = pxo.slot_bitmap([pxo.metadata_filter_accepts(raw, mm) for mm in metas])
         ri, rd, rl = pxo.ivfpq_search(data, cent, books, m, list_of, codes, queries, 10, 8, 200, bitmap=bm)
-        assert np.array_equal(gl, rl) and np.array_equal(gi, ri), raw
-        assert np.array_equal(gd.view(np.uint32), rd.view(np.uint32))
+        assert np.array_equal(gl, rl), raw
+        for q in range(len(queries)):
+            assert np.array_equal(gi[q, :rl[q]], ri[q, :rl[q]]), (raw, q)
+            assert np.array_equal(gd[q, :rl[q]].view(np.uint32), rd[q, :rl[q]].view(np.uint32)), (raw, q)
     idx.close()
