@@ -516,6 +516,89 @@ pxc_status pxc_ivfpq_search_sharded(pxc_ivfpq* h, const float* d_queries, uint32
                                     uint32_t rerank, const uint64_t* d_bitmap, uint64_t* d_out_ids, float* d_out_dist,
                                     uint32_t* d_out_len, void* stream, pxc_error* err);
 
+/* ---- Snapshots ----
+ * The snapshot file of crates/proxima-store/src/snapshot.rs (format version 1,
+ * little-endian codec of crates/proxima-store/src/codec.rs):
+ *   "PROXSNAP" | u32 version | u32 0x01020304 | u32 0 | u64 body_len | body | u32 crc32c(body)
+ * An IVF-PQ body (kind 3, snapshot.rs:150-186) holds the space, the
+ * IvfPqConfig, the slot ids, the metadata, then vectors, codes, list_of,
+ * centroids and codebooks as u32-counted arrays, and the TrainingReport.
+ * Errors: PXC_CORRUPTION with `parameter` naming the structure (as
+ * ProximaError::Corruption), PXC_CONFIGURATION for a body whose values
+ * IvfPqIndex::new rejects or that exceeds this build's device limits. */
+
+/* crc32c_append (crates/proxima-store/src/crc.rs:64-79): CRC-32C
+ * (Castagnoli) continued over `len` more HOST bytes; (0, b, n) is crc32c(b). */
+uint32_t pxc_crc32c_append(uint32_t crc, const void* bytes, uint64_t len);
+/* crc32c(A || B) from crc32c(A), crc32c(B) and the length of B. */
+uint32_t pxc_crc32c_combine(uint32_t crc_a, uint32_t crc_b, uint64_t len_b);
+/* crc32c of `len` DEVICE bytes, computed on the device, returned in *out
+ * (synchronises `stream`; NULL: the context stream). `d_bytes` may have any
+ * alignment but must lie in an allocation that starts 16-byte aligned
+ * (cudaMalloc and the caching allocators): the kernel reads from it rounded
+ * down to 16 bytes. */
+pxc_status pxc_crc32c_device(pxc_ctx* ctx, const void* d_bytes, uint64_t len, uint32_t* out, void* stream,
+                             pxc_error* err);
+
+/* IvfPqConfig (crates/proxima-index/src/ivfpq.rs:104-150) as the snapshot
+ * records it (snapshot.rs:469-479). */
+typedef struct pxc_ivfpq_config {
+  uint32_t nlist;
+  uint32_t subspaces;
+  uint32_t nprobe;
+  uint32_t rerank;
+  uint64_t seed;
+  uint32_t max_iterations;
+  uint32_t training_sample;
+  uint64_t train_threshold;
+  uint32_t retain_vectors; /* 0 or 1 */
+  uint32_t reserved;
+} pxc_ivfpq_config;
+
+/* What a snapshot says about itself (snapshot.rs:96-110 SnapshotHeader, and
+ * for IVF-PQ the rest of the body's small fields). */
+typedef struct pxc_snapshot_info {
+  uint32_t format_version;
+  uint32_t kind;             /* 1 flat, 2 hnsw, 3 ivfpq */
+  uint32_t dim;
+  int32_t metric;            /* PXC_EUCLIDEAN .. PXC_MANHATTAN */
+  uint64_t body_bytes;
+  uint64_t nslots;           /* entries of the id table */
+  uint64_t live;             /* slots holding an id: the index's len() */
+  uint64_t metadata_offset;  /* IVF-PQ: byte offset in the image of the metadata section (its u32 count first) */
+  uint64_t metadata_bytes;
+  pxc_ivfpq_config config;   /* IVF-PQ only */
+  uint32_t trained;          /* the centroids and codebooks are present */
+  uint32_t lists;            /* centroids / dim when trained, else config.nlist */
+  uint32_t has_vectors;      /* the full-precision vectors are present */
+  uint32_t has_report;
+  pxc_ivfpq_report report;   /* TrainingReport when has_report (produced and pq_iterations 0) */
+} pxc_snapshot_info;
+
+/* peek (snapshot.rs:271-299) of a HOST image: header, checksum (on the host),
+ * space and kind. An IVF-PQ body is decoded and checked in full, as decode
+ * does; of a flat or HNSW body only the id table is read. */
+pxc_status pxc_snapshot_peek(const uint8_t* bytes, uint64_t len, pxc_snapshot_info* info, pxc_error* err);
+/* decode (snapshot.rs:192-269) of an IVF-PQ snapshot straight into a new
+ * device index: the HOST image's arrays go by one copy each into the
+ * handle's device buffers, the checksum joins the host pieces' CRC with the
+ * arrays' CRC computed on the device, and the id ranks and the inverted
+ * lists are built on the device (IvfPqIndex::from_parts, ivfpq.rs:624-717).
+ * The errors and their precedence are decode's. Metadata stays in the image:
+ * info->metadata_offset / metadata_bytes locate it. *out is NULL on error. */
+pxc_status pxc_ivfpq_snapshot_load(pxc_ctx* ctx, const uint8_t* bytes, uint64_t len, pxc_ivfpq** out,
+                                   pxc_snapshot_info* info, pxc_error* err);
+/* encode (snapshot.rs:120-200) of a device index into the HOST buffer `out`
+ * of `capacity` bytes; *out_len = the snapshot's size (out NULL: size only).
+ * `config` is recorded as given (subspaces must equal the index's); `report`
+ * NULL records none. `metadata` is the encoded metadata section (u32 count =
+ * the slot count, then per slot the codec's Metadata with keys sorted;
+ * codec.rs:170-200), NULL for empty metadata on every slot. Slots without a
+ * live id are written as (0, 0). The arrays' CRC is computed on the device. */
+pxc_status pxc_ivfpq_snapshot_save(pxc_ivfpq* h, const pxc_ivfpq_config* config, const pxc_ivfpq_report* report,
+                                   const uint8_t* metadata, uint64_t metadata_bytes, uint8_t* out, uint64_t capacity,
+                                   uint64_t* out_len, pxc_error* err);
+
 /* ---- ScalarQuantizer ----
  * crates/proxima-quantize/src/scalar.rs. Range modes and code types in the
  * declaration order of RangeMode / CodeType. */

@@ -945,4 +945,22 @@ void pxo_ivfpq_search_csr(const float* vectors, const uint64_t* ids, const uint8
   });
 }
 
+// crc32c_append (crates/proxima-store/src/crc.rs:29-79): the byte table of
+// the reflected Castagnoli polynomial, one byte per step, register !crc in
+// and inverted out.
+uint32_t pxo_crc32c_append(uint32_t crc, const uint8_t* bytes, uint64_t len) {
+  static const std::vector<uint32_t> table = [] {
+    std::vector<uint32_t> t(256);
+    for (uint32_t b = 0; b < 256; ++b) {
+      uint32_t r = b;
+      for (int bit = 0; bit < 8; ++bit) r = (r & 1u) ? (r >> 1) ^ 0x82F63B78u : r >> 1;
+      t[b] = r;
+    }
+    return t;
+  }();
+  uint32_t r = ~crc;
+  for (uint64_t i = 0; i < len; ++i) r = table[(r ^ bytes[i]) & 0xFFu] ^ (r >> 8);
+  return ~r;
+}
+
 }  // extern "C"

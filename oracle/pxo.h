@@ -163,6 +163,9 @@ void pxo_ivfpq_search(const float* vectors, const uint64_t* ids, const uint8_t* 
                       const uint64_t* bitmap, uint64_t* out_ids, float* out_dist,
                       uint32_t* out_len, int threads);
 
+/* crc32c_append (crates/proxima-store/src/crc.rs:64-79), byte at a time. */
+uint32_t pxo_crc32c_append(uint32_t crc, const uint8_t* bytes, uint64_t len);
+
 #ifdef __cplusplus
 }
 #endif

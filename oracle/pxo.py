@@ -86,6 +86,7 @@ def lib():
             "pxo_ivfpq_encode_all": (None, [vp, vp, u64, u64, vp, u64, vp, u64, vp, vp, i32]),
             "pxo_ivfpq_search": (None, [vp, vp, vp, u64, u64, i32, vp, u64, vp, u64, vp, vp, vp, u64,
                                         u64, u64, u64, vp, vp, vp, vp, i32]),
+            "pxo_crc32c_append": (C.c_uint32, [C.c_uint32, vp, u64]),
             "pxo_ivfpq_search_csr": (None, [vp, vp, vp, u64, u64, i32, vp, u64, vp, u64, vp, vp, vp, vp, u64,
                                         u64, u64, u64, vp, vp, vp, vp, i32]),
         }
@@ -452,3 +453,256 @@ def slot_bitmap(accepted) -> np.ndarray:
         packed = np.concatenate([packed, np.zeros(words.size * 8 - packed.size, dtype=np.uint8)])
         words[:] = packed.view(np.uint64)
     return words
+
+
+# ---------------------------------------------------------------------------
+# Snapshot codec (crates/proxima-store/src/snapshot.rs, codec.rs, crc.rs)
+# ---------------------------------------------------------------------------
+import struct as _struct
+
+SNAP_MAGIC = b"PROXSNAP"
+_METRIC_TAG = {EUCLIDEAN: 1, COSINE: 2, INNER_PRODUCT: 3, MANHATTAN: 4}
+_TAG_METRIC = {v: k for k, v in _METRIC_TAG.items()}
+
+
+class SnapshotError(Exception):
+    """kind "corrupt" (ProximaError::Corruption, with the structure) or "config"
+    (ProximaError::Configuration, with the parameter)."""
+
+    def __init__(self, kind, where, detail):
+        super().__init__(f"{kind} {where}: {detail}")
+        self.kind, self.where, self.detail = kind, where, detail
+
+
+def crc32c(data, crc: int = 0) -> int:
+    """crc32c_append (crc.rs:64-79), the oracle's byte-at-a-time restatement."""
+    b = bytes(data)
+    return int(lib().pxo_crc32c_append(crc, b, len(b)))
+
+
+def encode_metadata_entry(m) -> bytes:
+    """Writer::metadata (codec.rs:170-200): field count, then (key, tag, value) with keys in byte order."""
+    m = m or {}
+    out = [_struct.pack("<I", len(m))]
+    for key in sorted(m, key=lambda k: k.encode("utf-8")):
+        kb = key.encode("utf-8")
+        out.append(_struct.pack("<I", len(kb)) + kb)
+        v = m[key]
+        if isinstance(v, bool):
+            out.append(_struct.pack("<BB", 4, int(v)))
+        elif isinstance(v, (int, np.integer)):
+            out.append(_struct.pack("<BQ", 2, int(v) & 0xFFFFFFFFFFFFFFFF))
+        elif isinstance(v, (float, np.floating)):
+            out.append(_struct.pack("<Bd", 3, float(v)))
+        else:
+            tb = str(v).encode("utf-8")
+            out.append(_struct.pack("<BI", 1, len(tb)) + tb)
+    return b"".join(out)
+
+
+def snapshot_encode_ivfpq(dim, metric, config, ids, metadata, vectors, codes, list_of, centroids, codebooks,
+                          report=None) -> bytes:
+    """encode (snapshot.rs:120-200, IVF-PQ arm) and the header (:190-199).
+    `config` is a dict of IvfPqConfig's fields, `ids` a list of VectorId or None
+    per slot, `metadata` a list of dicts, `report` a dict of TrainingReport's
+    fields or None."""
+    body = bytearray(_struct.pack("<IB", dim, _METRIC_TAG[metric]))
+    body += bytes([3])
+    c = config
+    body += _struct.pack("<IIIIQIIQB", c["nlist"], c["subspaces"], c["nprobe"], c["rerank"], c["seed"],
+                         c["max_iterations"], c["training_sample"], c["train_threshold"], int(bool(c["retain_vectors"])))
+    body += _struct.pack("<I", len(ids))
+    for i in ids:
+        body += _struct.pack("<BQ", 0, 0) if i is None else _struct.pack("<BQ", 1, int(i))
+    body += _struct.pack("<I", len(metadata))
+    for m in metadata:
+        body += encode_metadata_entry(m)
+    for arr, dt in ((vectors, "<f4"), (codes, "u1"), (list_of, "<u4"), (centroids, "<f4"), (codebooks, "<f4")):
+        a = np.ascontiguousarray(np.asarray(arr).reshape(-1), dtype=dt)
+        body += _struct.pack("<I", a.size) + a.tobytes()
+    if report is None:
+        body += b"\0"
+    else:
+        r = report
+        body += _struct.pack("<BIdIdII", 1, r["sampled"], r["coarse_inertia"], r["coarse_iterations"],
+                             r["residual_inertia"], r["populated_lists"], r["largest_list"])
+    head = SNAP_MAGIC + _struct.pack("<IIIQ", 1, 0x01020304, 0, len(body))
+    return bytes(head) + bytes(body) + _struct.pack("<I", crc32c(body))
+
+
+class _Reader:
+    """codec.rs Reader (:207-392): bounded reads, length prefixes checked against what remains."""
+
+    def __init__(self, b, structure):
+        self.b, self.pos, self.structure = b, 0, structure
+
+    def remaining(self):
+        return len(self.b) - self.pos
+
+    def take(self, n):
+        if self.remaining() < n:
+            raise SnapshotError("corrupt", self.structure,
+                                f"truncated at byte {self.pos}: wanted {n} more, {self.remaining()} remain")
+        out = self.b[self.pos:self.pos + n]
+        self.pos += n
+        return out
+
+    def u8(self):
+        return self.take(1)[0]
+
+    def u32(self):
+        return _struct.unpack("<I", self.take(4))[0]
+
+    def u64(self):
+        return _struct.unpack("<Q", self.take(8))[0]
+
+    def f64(self):
+        return _struct.unpack("<d", self.take(8))[0]
+
+    def len_prefix(self, elem):
+        n = self.u32()
+        if n * max(elem, 1) > self.remaining():
+            raise SnapshotError("corrupt", self.structure, f"length prefix at byte {self.pos - 4} claims {n} elements")
+        return n
+
+    def text(self):
+        b = self.take(self.len_prefix(1))
+        try:
+            return bytes(b).decode("utf-8")
+        except UnicodeDecodeError as e:
+            raise SnapshotError("corrupt", self.structure, f"field is not UTF-8: {e}") from None
+
+    def array(self, dt, elem):
+        n = self.len_prefix(elem)
+        return np.frombuffer(bytes(self.take(n * elem)), dtype=dt).copy()
+
+    def metadata(self):
+        m = {}
+        for _ in range(self.len_prefix(4)):
+            key = self.text()
+            tag = self.u8()
+            if tag == 1:
+                m[key] = self.text()
+            elif tag == 2:
+                m[key] = _struct.unpack("<q", self.take(8))[0]
+            elif tag == 3:
+                m[key] = self.f64()
+            elif tag == 4:
+                m[key] = self.u8() != 0
+            else:
+                raise SnapshotError("corrupt", self.structure, f"metadata value tag {tag} is not one of 1..=4")
+        return m
+
+
+def snapshot_decode_ivfpq(image) -> dict:
+    """decode (snapshot.rs:192-269) of an IVF-PQ snapshot with verify (:331-380)
+    and IvfPqIndex::new / IvfPqConfig::validate / from_parts (ivfpq.rs:259-302,
+    481-491, 624-717). Returns the parts as a dict; raises SnapshotError."""
+    b = bytes(image)
+    if len(b) < 32:
+        raise SnapshotError("corrupt", "snapshot header", f"{len(b)} bytes is shorter than the header plus checksum")
+    if b[:8] != SNAP_MAGIC:
+        raise SnapshotError("corrupt", "snapshot header", "bad magic")
+    version, order, reserved, body_len = _struct.unpack("<IIIQ", b[8:28])
+    if version != 1:
+        raise SnapshotError("corrupt", "snapshot header", f"format version {version}")
+    if reserved != 0:
+        raise SnapshotError("corrupt", "snapshot header", "reserved word is not zero")
+    if order != 0x01020304:
+        raise SnapshotError("corrupt", "snapshot header", "byte-order mark")
+    if len(b) != 28 + body_len + 4:
+        raise SnapshotError("corrupt", "snapshot", "header length disagrees with the file")
+    body = b[28:28 + body_len]
+    expected = _struct.unpack("<I", b[28 + body_len:])[0]
+    if crc32c(body) != expected:
+        raise SnapshotError("corrupt", "snapshot", "checksum mismatch")
+    rd = _Reader(body, "snapshot body")
+    dim = rd.u32()
+    tag = rd.u8()
+    if tag not in _TAG_METRIC:
+        raise SnapshotError("corrupt", "snapshot body", f"metric tag {tag} is not one of 1..=4")
+    metric = _TAG_METRIC[tag]
+    if dim < 1 or dim > 1 << 20:
+        raise SnapshotError("config", "dim", "out of range")
+    kind = rd.u8()
+    if kind not in (1, 2, 3):
+        raise SnapshotError("corrupt", "snapshot body", f"index kind {kind} is not one of 1..=3")
+    if kind != 3:
+        return {"kind": kind, "dim": dim, "metric": metric}
+    cfg = dict(zip(("nlist", "subspaces", "nprobe", "rerank"), (rd.u32(), rd.u32(), rd.u32(), rd.u32())))
+    cfg["seed"] = rd.u64()
+    cfg["max_iterations"], cfg["training_sample"] = rd.u32(), rd.u32()
+    cfg["train_threshold"] = rd.u64()
+    cfg["retain_vectors"] = rd.u8() != 0
+    ids = []
+    for _ in range(rd.len_prefix(9)):
+        present = rd.u8() != 0
+        raw = rd.u64()
+        ids.append(raw if present else None)
+    metadata = [rd.metadata() for _ in range(rd.len_prefix(4))]
+    vectors = rd.array("<f4", 4)
+    codes = rd.array("u1", 1)
+    list_of = rd.array("<u4", 4)
+    centroids = rd.array("<f4", 4)
+    codebooks = rd.array("<f4", 4)
+    report = None
+    if rd.u8() != 0:
+        report = {"sampled": rd.u32(), "coarse_inertia": rd.f64(), "coarse_iterations": rd.u32(),
+                  "residual_inertia": rd.f64(), "populated_lists": rd.u32(), "largest_list": rd.u32()}
+    # IvfPqIndex::new and IvfPqConfig::validate
+    if metric not in (EUCLIDEAN, COSINE):
+        raise SnapshotError("config", "metric", "IVF-PQ supports euclidean and cosine only")
+    for name, bad in (("nlist", cfg["nlist"] == 0),
+                      ("subspaces", cfg["subspaces"] == 0 or cfg["subspaces"] > dim),
+                      ("nprobe", cfg["nprobe"] == 0 or cfg["nprobe"] > cfg["nlist"]),
+                      ("max_iterations", cfg["max_iterations"] == 0),
+                      ("training_sample", cfg["training_sample"] == 0),
+                      ("rerank", cfg["rerank"] > 0 and not cfg["retain_vectors"])):
+        if bad:
+            raise SnapshotError("config", name, "rejected by IvfPqConfig::validate")
+    # from_parts
+    n, m = len(ids), cfg["subspaces"]
+    if len(metadata) != n:
+        raise SnapshotError("corrupt", "ivfpq index", "metadata count")
+    if vectors.size and vectors.size != n * dim:
+        raise SnapshotError("corrupt", "ivfpq index", "vectors length")
+    if codes.size and (codes.size != n * m or list_of.size != n):
+        raise SnapshotError("corrupt", "ivfpq index", "codes or list assignments length")
+    lists = cfg["nlist"]
+    if centroids.size:
+        if centroids.size % dim:
+            raise SnapshotError("corrupt", "ivfpq centroids", "not a multiple of the dimension")
+        if codebooks.size != 256 * dim:
+            raise SnapshotError("corrupt", "product quantizer", "codebook length")
+        lists = centroids.size // dim
+    seen = {}
+    for slot, i in enumerate(ids):
+        if i is not None:
+            if i in seen:
+                raise SnapshotError("corrupt", "ivfpq index", f"id {i} appears at two slots")
+            seen[i] = slot
+    for slot, lst in enumerate(list_of.tolist()):
+        if lst == 0xFFFFFFFF or ids[slot] is None:
+            continue
+        if lst >= lists:
+            raise SnapshotError("corrupt", "ivfpq index", f"slot {slot} names list {lst} of {lists}")
+    if rd.remaining():
+        raise SnapshotError("corrupt", "snapshot body", f"{rd.remaining()} trailing bytes after the final field")
+    return {"kind": 3, "dim": dim, "metric": metric, "config": cfg, "ids": ids, "metadata": metadata,
+            "vectors": vectors, "codes": codes, "list_of": list_of, "centroids": centroids, "codebooks": codebooks,
+            "report": report, "lists": lists}
+
+
+def snapshot_encode_flat(dim, metric, ids, data, metadata) -> bytes:
+    """encode (snapshot.rs:124-130) of a flat index: the store as encode_store (:383-405) writes it."""
+    body = bytearray(_struct.pack("<IB", dim, _METRIC_TAG[metric])) + bytes([1])
+    body += _struct.pack("<I", len(ids))
+    for i in ids:
+        body += _struct.pack("<BQ", 0, 0) if i is None else _struct.pack("<BQ", 1, int(i))
+    a = np.ascontiguousarray(np.asarray(data).reshape(-1), dtype="<f4")
+    body += _struct.pack("<I", a.size) + a.tobytes()
+    body += _struct.pack("<I", len(metadata))
+    for m in metadata:
+        body += encode_metadata_entry(m)
+    head = SNAP_MAGIC + _struct.pack("<IIIQ", 1, 0x01020304, 0, len(body))
+    return bytes(head) + bytes(body) + _struct.pack("<I", crc32c(body))

@@ -59,6 +59,41 @@ class PxcIvfpqReport(C.Structure):
     ]
 
 
+class PxcIvfpqConfig(C.Structure):
+    _fields_ = [
+        ("nlist", C.c_uint32),
+        ("subspaces", C.c_uint32),
+        ("nprobe", C.c_uint32),
+        ("rerank", C.c_uint32),
+        ("seed", C.c_uint64),
+        ("max_iterations", C.c_uint32),
+        ("training_sample", C.c_uint32),
+        ("train_threshold", C.c_uint64),
+        ("retain_vectors", C.c_uint32),
+        ("reserved", C.c_uint32),
+    ]
+
+
+class PxcSnapshotInfo(C.Structure):
+    _fields_ = [
+        ("format_version", C.c_uint32),
+        ("kind", C.c_uint32),
+        ("dim", C.c_uint32),
+        ("metric", C.c_int32),
+        ("body_bytes", C.c_uint64),
+        ("nslots", C.c_uint64),
+        ("live", C.c_uint64),
+        ("metadata_offset", C.c_uint64),
+        ("metadata_bytes", C.c_uint64),
+        ("config", PxcIvfpqConfig),
+        ("trained", C.c_uint32),
+        ("lists", C.c_uint32),
+        ("has_vectors", C.c_uint32),
+        ("has_report", C.c_uint32),
+        ("report", PxcIvfpqReport),
+    ]
+
+
 class PxcRng(C.Structure):
     """pxc_rng: a ChaCha8Rng as rand_chacha exposes it (seed, stream, word position)."""
 
@@ -180,6 +215,15 @@ SIGNATURES: dict[str, tuple] = {
                                              vp, vp, vp, C.POINTER(PxcError)]),
     "pxc_ivfpq_search_device": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, vp, vp,
                                             vp, vp, vp, C.POINTER(PxcError)]),
+    "pxc_crc32c_append": (C.c_uint32, [C.c_uint32, vp, C.c_uint64]),
+    "pxc_crc32c_combine": (C.c_uint32, [C.c_uint32, C.c_uint32, C.c_uint64]),
+    "pxc_crc32c_device": (C.c_int32, [vp, vp, C.c_uint64, C.POINTER(C.c_uint32), vp, C.POINTER(PxcError)]),
+    "pxc_snapshot_peek": (C.c_int32, [vp, C.c_uint64, C.POINTER(PxcSnapshotInfo), C.POINTER(PxcError)]),
+    "pxc_ivfpq_snapshot_load": (C.c_int32, [vp, vp, C.c_uint64, C.POINTER(vp), C.POINTER(PxcSnapshotInfo),
+                                            C.POINTER(PxcError)]),
+    "pxc_ivfpq_snapshot_save": (C.c_int32, [vp, C.POINTER(PxcIvfpqConfig), C.POINTER(PxcIvfpqReport), vp,
+                                            C.c_uint64, vp, C.c_uint64, C.POINTER(C.c_uint64),
+                                            C.POINTER(PxcError)]),
     "pxc_sq_train": (C.c_int32, [vp, vp, C.c_uint64, C.c_uint32, C.c_int32, vp, vp, vp, C.POINTER(PxcError)]),
     "pxc_sq_train_device": (C.c_int32, [vp, vp, C.c_uint64, C.c_uint32, C.c_int32, vp, vp, vp, vp,
                                         C.POINTER(PxcError)]),

@@ -154,6 +154,10 @@ struct pxc_ctx {
   unsigned char* x_send = nullptr;  // exchange buffers (device), grown on demand
   unsigned char* x_recv = nullptr;
   size_t x_send_bytes = 0, x_recv_bytes = 0;
+  // CRC-32C tables on the device (slicing tables and shift operators),
+  // uploaded on first use.
+  uint32_t* crc_tab = nullptr;
+  std::mutex crc_mu;
 };
 
 namespace pxc {

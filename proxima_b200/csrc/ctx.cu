@@ -337,6 +337,7 @@ void pxc_ctx_destroy(pxc_ctx* ctx) {
   if (ctx->comm && nccl_api().ok) nccl_api().comm_destroy(static_cast<ncclComm_t>(ctx->comm));
   if (ctx->x_send) cudaFree(ctx->x_send);
   if (ctx->x_recv) cudaFree(ctx->x_recv);
+  if (ctx->crc_tab) cudaFree(ctx->crc_tab);
   if (ctx->d_status) cudaFree(ctx->d_status);
   if (ctx->h_status) cudaFreeHost(ctx->h_status);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);

@@ -36,6 +36,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "ivfpq.cuh"
 #include "kmeans_api.h"
 #include "rng.h"
 #include "refdist.cuh"
@@ -46,11 +47,8 @@
 namespace pxc {
 namespace ivf {
 
-constexpr uint32_t UNASSIGNED = 0xFFFFFFFFu;
 constexpr uint32_t MAX_NPROBE = 128;
 constexpr uint32_t MAX_SHORTLIST = 4096;
-constexpr uint32_t MAX_M = 64;
-constexpr uint32_t MAX_DIM = 1024;
 constexpr uint32_t SCAN_THREADS = 256;
 constexpr uint32_t CB_MAX = 8192; // candidate buffer per query (shared memory), largest
 constexpr uint32_t CHUNK = 1024;  // codes scored between buffer checks
@@ -547,6 +545,17 @@ __global__ void list_rank_kernel(const uint32_t* __restrict__ list_slot, const u
   if (j < n) out[j] = slot_rank[list_slot[j]];
 }
 
+// slot_rank / rank_slot from the live slots sorted by (VectorId, slot): the
+// smallest slot whose id repeats an earlier slot's id goes to *dup.
+__global__ void rank_ids_kernel(const uint64_t* __restrict__ sorted_ids, const uint32_t* __restrict__ rank_slot,
+                                uint64_t nlive, uint32_t* __restrict__ slot_rank, uint32_t* __restrict__ dup) {
+  const uint64_t r = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (r >= nlive) return;
+  const uint32_t slot = rank_slot[r];
+  slot_rank[slot] = (uint32_t)r;
+  if (r > 0 && sorted_ids[r] == sorted_ids[r - 1]) atomicMin(dup, slot);
+}
+
 // Dead slots take no list.
 __global__ void mask_dead_kernel(uint32_t* __restrict__ list_of, const uint8_t* __restrict__ live, uint64_t n) {
   const uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
@@ -581,53 +590,6 @@ __global__ void gather_codes_kernel(const uint8_t* __restrict__ codes, uint32_t 
 
 }  // namespace ivf
 }  // namespace pxc
-
-// ---------------------------------------------------------------------------
-// Handle
-// ---------------------------------------------------------------------------
-struct pxc_ivfpq {
-  pxc_ctx* ctx = nullptr;
-  uint32_t dim = 0, nlist = 0, m = 0;
-  int32_t metric = 0;
-  std::vector<uint32_t> widths, offsets;
-  pxc::DBuf<uint32_t> woff;
-  pxc::DBuf<float> centroids, codebooks, vectors;
-  bool have_parts = false, have_vectors = false;
-  // u8 re-rank rows: 0 = not built since the store changed, 1 = built, 2 = not applicable
-  int u8_state = 0;
-  pxc::DBuf<uint8_t> vec_u8;
-  pxc::DBuf<int> u8_flag;
-  int* h_u8_flag = nullptr;  // pinned
-  uint64_t nslots = 0, nlive = 0;
-  std::vector<uint64_t> h_ids;
-  std::vector<uint8_t> h_live;
-  pxc::DBuf<uint64_t> ids;
-  pxc::DBuf<uint32_t> slot_rank, rank_slot;
-  pxc::DBuf<uint32_t> list_off, list_slot, list_of, list_rank;
-  pxc::DBuf<unsigned long long> scanned;
-  unsigned long long* h_scanned = nullptr;  // pinned
-  pxc::DBuf<uint8_t> list_codes, codes, live;
-  bool have_lists = false;
-  pxc::DBuf<float> q_buf;
-  pxc::DBuf<uint32_t> probes, coarse_d, coarse_len, coarse_zero;
-  pxc::DBuf<uint64_t> coarse_l, io_ids, bitmap;
-  pxc::DBuf<float> io_dist;
-  pxc::DBuf<uint32_t> io_len;
-  cudaEvent_t ev_begin = nullptr, ev_end = nullptr;  // scan timing when the context profiles
-  bool timed = false;
-  cudaEvent_t ev_done = nullptr;  // end of the last search's work (handoff of the scratch)
-  std::mutex mu;
-  ~pxc_ivfpq() {
-    if (ev_done) {
-      cudaEventSynchronize(ev_done);  // a search on another stream may still be running
-      cudaEventDestroy(ev_done);
-    }
-    if (h_scanned) cudaFreeHost(h_scanned);
-    if (h_u8_flag) cudaFreeHost(h_u8_flag);
-    if (ev_begin) cudaEventDestroy(ev_begin);
-    if (ev_end) cudaEventDestroy(ev_end);
-  }
-};
 
 namespace pxc {
 namespace ivf {
@@ -888,7 +850,14 @@ void encode_all(pxc_ivfpq* h, cudaStream_t s) {
         h->vectors.p, dim, n, h->list_of.p, h->centroids.p, dim, h->codebooks.p, h->woff.p, m, h->codes.p);
     ctx->launches += 2;
   }
-  // lists: stable sort of slots by list (unassigned last), boundaries, codes in list order
+  build_lists_device(h, h->list_of.p, s);
+}
+
+void build_lists_device(pxc_ivfpq* h, const uint32_t* d_keys, cudaStream_t s) {
+  pxc_ctx* ctx = h->ctx;
+  const uint64_t n = h->nslots;
+  const uint32_t m = h->m;
+  // stable sort of slots by list (unassigned last), boundaries, codes in list order
   DBuf<uint32_t> slots, keys_out;
   DBuf<unsigned char> tmp;
   slots.reserve(std::max<uint64_t>(1, n));
@@ -899,11 +868,10 @@ void encode_all(pxc_ivfpq* h, cudaStream_t s) {
   if (n) {
     iota_u32_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(slots.p, n);
     size_t tb = 0;
-    PXC_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, tb, h->list_of.p, keys_out.p, slots.p, h->list_slot.p, (int)n, 0,
-                                             32, s));
+    PXC_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, tb, d_keys, keys_out.p, slots.p, h->list_slot.p, (int)n, 0, 32,
+                                             s));
     tmp.reserve(tb);
-    PXC_CUDA(cub::DeviceRadixSort::SortPairs(tmp.p, tb, h->list_of.p, keys_out.p, slots.p, h->list_slot.p, (int)n, 0,
-                                             32, s));
+    PXC_CUDA(cub::DeviceRadixSort::SortPairs(tmp.p, tb, d_keys, keys_out.p, slots.p, h->list_slot.p, (int)n, 0, 32, s));
     list_bounds_kernel<<<(h->nlist + 256) / 256, 256, 0, s>>>(keys_out.p, n, h->nlist, h->list_off.p);
     gather_codes_kernel<<<(unsigned)((n * m + 255) / 256), 256, 0, s>>>(h->codes.p, m, h->list_slot.p, n,
                                                                        h->list_codes.p);
@@ -916,6 +884,31 @@ void encode_all(pxc_ivfpq* h, cudaStream_t s) {
   PXC_CUDA(cudaGetLastError());
   PXC_CUDA(cudaStreamSynchronize(s));
   h->have_lists = true;
+}
+
+void rank_ids_device(pxc_ivfpq* h, const uint32_t* d_live_slots, const uint64_t* d_live_ids, uint64_t nlive,
+                     uint32_t* d_dup, cudaStream_t s) {
+  const uint64_t n = h->nslots;
+  PXC_CONFIG(nlive < (1ull << 31), "nslots", nlive, "the device id ranking sorts fewer than 2^31 live slots");
+  h->slot_rank.reserve(std::max<uint64_t>(1, n));
+  h->rank_slot.reserve(std::max<uint64_t>(1, nlive));
+  if (n) PXC_CUDA(cudaMemsetAsync(h->slot_rank.p, 0xFF, n * 4, s));
+  h->nlive = nlive;
+  if (!nlive) return;
+  DBuf<uint64_t> ids_out;
+  DBuf<unsigned char> tmp;
+  ids_out.reserve(nlive);
+  size_t tb = 0;
+  PXC_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, tb, d_live_ids, ids_out.p, d_live_slots, h->rank_slot.p,
+                                           (int)nlive, 0, 64, s));
+  tmp.reserve(tb);
+  PXC_CUDA(cub::DeviceRadixSort::SortPairs(tmp.p, tb, d_live_ids, ids_out.p, d_live_slots, h->rank_slot.p, (int)nlive,
+                                           0, 64, s));
+  rank_ids_kernel<<<(unsigned)((nlive + 255) / 256), 256, 0, s>>>(ids_out.p, h->rank_slot.p, nlive, h->slot_rank.p,
+                                                                  d_dup);
+  PXC_CUDA(cudaGetLastError());
+  h->ctx->launches += 3;
+  PXC_CUDA(cudaStreamSynchronize(s));  // the sort's scratch is freed on return
 }
 
 }  // namespace ivf

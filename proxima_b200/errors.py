@@ -83,7 +83,7 @@ def raise_for_status(status: int, a: int, b: int, parameter: str, detail: str) -
     if status == 5:
         raise NonFinite(a)
     if status == 6:
-        raise Corruption("device mirror", detail)
+        raise Corruption(parameter or "device mirror", detail)
     if status == 7:
         raise Configuration(parameter, a, detail)
     if status == 11:

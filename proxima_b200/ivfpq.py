@@ -28,6 +28,17 @@ class IvfPqIndex:
         self.handle = h
         self.nslots = 0
 
+    @classmethod
+    def adopt(cls, handle, context, dim: int, nlist: int, subspaces: int, metric: Metric, nslots: int) -> "IvfPqIndex":
+        """An index around an existing pxc_ivfpq handle (a snapshot load's); it owns the handle."""
+        self = cls.__new__(cls)
+        self.ctx = context
+        self.dim, self.nlist, self.m = dim, nlist, subspaces
+        self.metric = Metric(metric)
+        self.handle = handle
+        self.nslots = nslots
+        return self
+
     def close(self) -> None:
         if getattr(self, "_columns", None) is not None:
             self._columns.close()
@@ -79,7 +90,8 @@ class IvfPqIndex:
         rep = N.PxcIvfpqReport()
         N.call("pxc_ivfpq_train", self.handle, training_sample, max_iterations, seed, C.byref(rep))
         self.nlist = int(rep.produced)
-        return {f: getattr(rep, f) for f, _ in N.PxcIvfpqReport._fields_}
+        self.report = {f: getattr(rep, f) for f, _ in N.PxcIvfpqReport._fields_}
+        return dict(self.report)
 
     def parts(self):
         """(centroids, codebooks, list_of, codes) as the index holds them."""
