@@ -47,7 +47,7 @@ def parse():
     p.add_argument("--dim", type=int, default=128)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
-    p.add_argument("--workload", choices=["flat", "kmeans", "ivfpq", "sq"], default="flat")
+    p.add_argument("--workload", choices=["flat", "kmeans", "ivfpq", "sq", "snapshot"], default="flat")
     p.add_argument("--flat-scaling", choices=["weak", "strong"], default="weak",
                    help="flat at N>1: weak = N x --nq queries per step over the row-sharded database (each GPU "
                         "scans the equivalent of --nq queries x --n rows); strong = --nq queries split N ways")
@@ -1025,6 +1025,145 @@ def flat_queries(args, nq: int) -> np.ndarray:
     return gen(nq, args.dim, 1024, fixtures.C2_CENTRES, fixtures.C2_QUERIES)
 
 
+SNAP_METRIC = "GB/s: IVF-PQ snapshot load (decode, snapshot.rs) of a 1M x 128, nlist 4096, m=16 index, host image -> device index"
+
+
+def run_snapshot(args):
+    """--workload snapshot: an IVF-PQ index (1M x 128 f32 integer rows, nlist 4096, m=16) trained on the GPU
+    (untimed) and saved once; one step = pxc_ivfpq_snapshot_load of the host image into a new device index
+    (header, checksum, sections, arrays to HBM, id ranks, inverted lists), timed on the host around the call.
+    Also reported: the save (device index -> host image) and the device CRC-32C kernel on the vectors."""
+    import torch
+
+    from oracle import pxo
+    from proxima_b200 import _native as N
+    from proxima_b200 import fixtures
+    from proxima_b200 import snapshot as S
+    from proxima_b200.index import Context
+    from proxima_b200.ivfpq import IvfPqIndex
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    n, dim, nlist, m = 1_000_000, 128, 4096, 16
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ctx = Context(local)
+    lib = N.load()
+    d_vec = torch.from_numpy(fixtures.blobs_u8(n, dim, 4096, fixtures.C4_CENTRES, fixtures.C4_BASE)).to(dev)
+    idx = IvfPqIndex(dim, nlist, m, context=ctx)
+    ids = np.arange(n, dtype=np.uint64) * 2 + 1
+    live = np.ones(n, np.uint8)
+    live[::97] = 0  # some removed slots
+    idx.set_store_device(d_vec, ids=ids, live=live)
+    idx.train(training_sample=200_000, max_iterations=10, seed=0x1FF9C0D)
+    cfg = S.IvfPqConfig(idx.nlist, m, nprobe=32, rerank=100)
+    image = np.frombuffer(S.save_ivfpq(idx, cfg), dtype=np.uint8)
+    nbytes = len(image)
+
+    def load_once(img):
+        h = N.vp()
+        info = N.PxcSnapshotInfo()
+        N.call("pxc_ivfpq_snapshot_load", ctx.handle, img.ctypes.data, len(img), C.byref(h), C.byref(info))
+        return h
+
+    for _ in range(max(3, args.warmup)):
+        lib.pxc_ivfpq_destroy(load_once(image))
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    sampler = ClockSampler(uuid)
+    sampler.start()
+    launches0 = lib.pxc_ctx_launch_count(ctx.handle)
+    load_s = []
+    for _ in range(args.steps):
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        h = load_once(image)
+        load_s.append(time.perf_counter() - t0)
+        lib.pxc_ivfpq_destroy(h)
+    launches = (lib.pxc_ctx_launch_count(ctx.handle) - launches0) // max(1, args.steps)
+    clocks = sampler.stop()
+    # the same load from a pinned copy of the image
+    pinned = torch.from_numpy(image.copy()).pin_memory().numpy()
+    lib.pxc_ivfpq_destroy(load_once(pinned))
+    pin_s = []
+    for _ in range(max(3, args.steps // 2)):
+        t0 = time.perf_counter()
+        h = load_once(pinned)
+        pin_s.append(time.perf_counter() - t0)
+        lib.pxc_ivfpq_destroy(h)
+    # save
+    save_s = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        again = S.save_ivfpq(idx, cfg)
+        save_s.append(time.perf_counter() - t0)
+    # the device CRC kernel on the vectors (CUDA events on the launching stream)
+    stream = torch.cuda.Stream(dev)
+    out = C.c_uint32()
+    vec_bytes = d_vec.numel() * 4
+    for _ in range(3):
+        N.call("pxc_crc32c_device", ctx.handle, d_vec.data_ptr(), vec_bytes, C.byref(out), stream.cuda_stream)
+    crc_ms = []
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    for _ in range(5):
+        flush.zero_()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        N.call("pxc_crc32c_device", ctx.handle, d_vec.data_ptr(), vec_bytes, C.byref(out), stream.cuda_stream)
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        crc_ms.append(a.elapsed_time(b))
+    crc_host = pxo.crc32c(d_vec.cpu().numpy().tobytes())
+    # parity: the loaded index re-saves to the same bytes, answers as the saved one, and the image's
+    # checksum (device-computed) verifies on the host
+    idx2, info = S.load_ivfpq(image, ctx, with_metadata=False)
+    resaved = np.frombuffer(S.save_ivfpq(idx2, cfg), dtype=np.uint8)
+    qs = fixtures.blobs_u8(200, dim, 4096, fixtures.C4_CENTRES, fixtures.C4_QUERIES)
+    r1, r2 = idx.search_batch(qs, 10, 32, 100), idx2.search_batch(qs, 10, 32, 100)
+    same_search = all(np.array_equal(x.view(np.uint8), y.view(np.uint8)) for x, y in zip(r1, r2))
+    peek_ok = S.peek(image).len == int(live.sum())
+    parity = {"resave_identical": bool(np.array_equal(resaved, image)), "search_identical_200q": bool(same_search),
+              "host_checksum_verifies": bool(peek_ok), "device_crc_equals_oracle": bool(out.value == crc_host),
+              "save_deterministic": again == image.tobytes()}
+    idx2.close()
+    mean_load = sum(load_s) / len(load_s)
+    hbm, bf16, src = peaks()
+    crc_mean = sum(crc_ms) / len(crc_ms)
+    achieved = vec_bytes / (crc_mean / 1e3) / 1e9
+    line = {"metric": SNAP_METRIC, "value": nbytes / mean_load / 1e9, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": mean_load * 1e3,
+            "higher_is_better": True, "scaling": "replicas", "vs_baseline": None, "dtype": "u8 (bytes)",
+            "data": "synthetic",
+            "config": {"workload": f"IVF-PQ snapshot of {n:,} x {dim} f32 rows (C4 blobs, integers), "
+                                   f"{int(live.sum()):,} live, nlist {idx.nlist}, m={m}, metadata empty; "
+                                   f"image {nbytes:,} bytes in pageable host memory",
+                       "image_bytes": nbytes, "pinned_image_gb_s": nbytes / (sum(pin_s) / len(pin_s)) / 1e9,
+                       "save_gb_s": nbytes / (sum(save_s) / len(save_s)) / 1e9,
+                       "l2": "inputs (the host image) larger than L2; the CRC kernel's vectors flushed between runs",
+                       "parity": parity, "parallelism": "single GPU"},
+            "clocks": clocks, "gpu_launches": int(launches),
+            "e2e": {"value": nbytes / mean_load / 1e9, "unit": "GB/s", "h2d_bytes_per_step": nbytes,
+                    "d2h_bytes_per_step": 32},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "traffic": None, "kernel": "crc::crc_step_kernel + crc_finish_kernel (device CRC-32C)",
+                         "kernel_ms": crc_mean, "peak_source": src, "algorithmic_bytes_per_launch": vec_bytes}}
+    if not args.no_cpu_baseline:
+        t0 = time.perf_counter()
+        dec = pxo.snapshot_decode_ivfpq(image.tobytes())
+        cpu_s = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": nbytes / cpu_s / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+                                "sample": "the whole image: the oracle's decode (byte-at-a-time CRC-32C as crc.rs, "
+                                          "sections, from_parts checks), one pass",
+                                "parts_equal": bool(np.array_equal(dec["codes"].reshape(-1, m), idx.parts()[3]))}
+    print(json.dumps(line), flush=True)
+    idx.close()
+    ctx.close()
+
+
 def run_extras(args) -> dict:
     """Sub-records of the other configurations, each from its own bench.py run (fresh process, the same GPU):
     C2 at k=100, real-valued C2 (euclidean and cosine: the f16 tensor-core screen), C3, C4 and C5."""
@@ -1035,6 +1174,7 @@ def run_extras(args) -> dict:
         "c3_kmeans": ["--workload", "kmeans"],
         "c4_ivfpq": ["--workload", "ivfpq"],
         "c5_sq": ["--workload", "sq"],
+        "c4_snapshot": ["--workload", "snapshot"],
     }
     out = {}
     for name, extra in runs.items():
@@ -1071,6 +1211,9 @@ def main():
         return
     if args.workload == "kmeans":
         run_kmeans(args)
+        return
+    if args.workload == "snapshot":
+        run_snapshot(args)
         return
     if args.impl == "reference":
         run_reference(args)

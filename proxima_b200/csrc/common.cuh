@@ -157,6 +157,8 @@ struct pxc_ctx {
   // CRC-32C tables on the device (slicing tables and shift operators),
   // uploaded on first use.
   uint32_t* crc_tab = nullptr;
+  uint32_t* crc_scratch = nullptr;  // block values + result of pxc_crc32c_device (device)
+  uint32_t* crc_host = nullptr;     // its result (pinned)
   std::mutex crc_mu;
 };
 

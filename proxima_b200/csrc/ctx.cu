@@ -338,6 +338,8 @@ void pxc_ctx_destroy(pxc_ctx* ctx) {
   if (ctx->x_send) cudaFree(ctx->x_send);
   if (ctx->x_recv) cudaFree(ctx->x_recv);
   if (ctx->crc_tab) cudaFree(ctx->crc_tab);
+  if (ctx->crc_scratch) cudaFree(ctx->crc_scratch);
+  if (ctx->crc_host) cudaFreeHost(ctx->crc_host);
   if (ctx->d_status) cudaFree(ctx->d_status);
   if (ctx->h_status) cudaFreeHost(ctx->h_status);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);

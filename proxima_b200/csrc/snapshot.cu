@@ -58,15 +58,16 @@ namespace crc {
 // byte tables or, for one vector per warp, as a XOR reduction over lanes.
 // ---------------------------------------------------------------------------
 constexpr uint32_t POLY = 0x82F63B78u;
-constexpr int UNIT = 256;     // bytes one thread folds per step
+constexpr int UNIT = 128;     // bytes one thread folds per step: two 64-byte halves, two chains
 constexpr int THREADS = 512;  // threads of the step kernel (16 warps)
 constexpr uint64_t STEP = (uint64_t)UNIT * THREADS;
 constexpr int LEVELS = 10;    // operators S_{UNIT << l}, l = 0..9 (the last one is S_STEP)
+constexpr int OPS = LEVELS + 1;  // and S_{UNIT / 2}, which joins the halves (stored first)
 constexpr int SLICE_WORDS = 4 * 256;
 constexpr int OP_WORDS = 4 * 256;
-constexpr int DEV_WORDS = SLICE_WORDS + LEVELS * OP_WORDS;
+constexpr int DEV_WORDS = SLICE_WORDS + OPS * OP_WORDS;
 // slicing tables with one copy per shared-memory bank, then the operators
-constexpr size_t STEP_SMEM = (size_t)SLICE_WORDS * 32 * 4 + (size_t)LEVELS * OP_WORDS * 4;
+constexpr size_t STEP_SMEM = (size_t)SLICE_WORDS * 32 * 4 + (size_t)OPS * OP_WORDS * 4;
 static_assert(THREADS == 512, "the step kernel's tree is 5 lane levels and 4 warp levels");
 static_assert((UNIT << (LEVELS - 1)) == (int)STEP, "the last operator joins whole steps");
 
@@ -106,7 +107,9 @@ struct Tables {
     dev.assign(DEV_WORDS, 0);
     for (int k = 0; k < 4; ++k)
       for (int b = 0; b < 256; ++b) dev[k * 256 + b] = t[k][b];
-    for (int l = 0; l < LEVELS; ++l) op_table(matrix((uint64_t)UNIT << l), dev.data() + SLICE_WORDS + l * OP_WORDS);
+    op_table(matrix(UNIT / 2), dev.data() + SLICE_WORDS);
+    for (int l = 0; l < LEVELS; ++l)
+      op_table(matrix((uint64_t)UNIT << l), dev.data() + SLICE_WORDS + (l + 1) * OP_WORDS);
   }
   Mat matrix(uint64_t n) const {  // S_n
     Mat r;
@@ -168,52 +171,70 @@ __device__ __forceinline__ uint32_t keep_from(uint32_t w, int first) {  // zero 
   return first <= 0 ? w : first >= 4 ? 0u : (w & ~((1u << (8 * first)) - 1u));
 }
 
-// Step kernel: every thread folds one UNIT-byte run per step, f(0, run); a
-// lane tree and a warp tree join the block's 512 runs into f(0, step) and the
-// block folds its q consecutive steps. Runs are numbered after `pad` virtual
-// zero runs in front, so every block covers exactly q steps and every join is
-// by a fixed length. `base` is 16-byte aligned; its first `lead` bytes lie
-// before the data and read as zero.
+// Step kernel: every thread folds one UNIT-byte run per step, f(0, run), as
+// two independent chains over its halves joined by S_{UNIT/2}; a lane tree
+// and a warp tree join the block's 512 runs into f(0, step) and the block
+// folds its q consecutive steps. The next step's run is loaded before the
+// current one is folded. Runs are numbered after `pad` virtual zero runs in
+// front, so every block covers exactly q steps and every join is by a fixed
+// length. `base` is 16-byte aligned; its first `lead` bytes lie before the
+// data and read as zero.
 __global__ void __launch_bounds__(THREADS, 1)
     crc_step_kernel(const uint8_t* __restrict__ base, uint32_t lead, uint64_t pad, uint32_t q,
                     const uint32_t* __restrict__ tabs, uint32_t* __restrict__ partial) {
   extern __shared__ __align__(16) uint32_t sm[];
   uint32_t* rep = sm;
-  uint32_t* ops = sm + SLICE_WORDS * 32;
+  uint32_t* ops = sm + SLICE_WORDS * 32;  // [0] S_{UNIT/2}, [1 + l] S_{UNIT << l}
   __shared__ uint32_t wv[THREADS / 32];
   const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
   for (uint32_t i = threadIdx.x; i < SLICE_WORDS * 32; i += THREADS) rep[i] = tabs[i >> 5];
-  for (uint32_t i = threadIdx.x; i < LEVELS * OP_WORDS; i += THREADS) ops[i] = tabs[SLICE_WORDS + i];
+  for (uint32_t i = threadIdx.x; i < OPS * OP_WORDS; i += THREADS) ops[i] = tabs[SLICE_WORDS + i];
   __syncthreads();
   const uint32_t* mine = rep + lane;
+  constexpr int V = UNIT / 16;
+  uint4 nxt[V];
+  auto fetch = [&](uint32_t st) -> bool {
+    const uint64_t vu = ((uint64_t)blockIdx.x * q + st) * THREADS + threadIdx.x;
+    if (vu < pad) return false;
+    const uint4* p = reinterpret_cast<const uint4*>(base + (vu - pad) * UNIT);
+#pragma unroll
+    for (int j = 0; j < V; ++j) nxt[j] = __ldg(p + j);
+    if (vu == pad) {  // run 0: the bytes before the data read as zero
+      nxt[0].x = keep_from(nxt[0].x, (int)lead);
+      nxt[0].y = keep_from(nxt[0].y, (int)lead - 4);
+      nxt[0].z = keep_from(nxt[0].z, (int)lead - 8);
+      nxt[0].w = keep_from(nxt[0].w, (int)lead - 12);
+    }
+    return true;
+  };
+  bool have_next = fetch(0);
   uint32_t acc = 0;
   for (uint32_t st = 0; st < q; ++st) {
-    const uint64_t vu = ((uint64_t)blockIdx.x * q + st) * THREADS + threadIdx.x;
+    uint4 cur[V];
+#pragma unroll
+    for (int j = 0; j < V; ++j) cur[j] = nxt[j];
+    const bool have = have_next;
+    have_next = st + 1 < q ? fetch(st + 1) : false;
     uint32_t c = 0;
-    if (vu >= pad) {
-      const uint64_t u = vu - pad;
-      const uint4* p = reinterpret_cast<const uint4*>(base + u * UNIT);
-      uint4 v[UNIT / 16];
+    if (have) {
+      uint32_t c0 = 0, c1 = 0;
 #pragma unroll
-      for (int j = 0; j < UNIT / 16; ++j) v[j] = __ldg(p + j);
-      if (u == 0) {
-        v[0].x = keep_from(v[0].x, (int)lead);
-        v[0].y = keep_from(v[0].y, (int)lead - 4);
-        v[0].z = keep_from(v[0].z, (int)lead - 8);
-        v[0].w = keep_from(v[0].w, (int)lead - 12);
+      for (int j = 0; j < V / 2; ++j) {
+        c0 = slice4(mine, c0 ^ cur[j].x);
+        c1 = slice4(mine, c1 ^ cur[j + V / 2].x);
+        c0 = slice4(mine, c0 ^ cur[j].y);
+        c1 = slice4(mine, c1 ^ cur[j + V / 2].y);
+        c0 = slice4(mine, c0 ^ cur[j].z);
+        c1 = slice4(mine, c1 ^ cur[j + V / 2].z);
+        c0 = slice4(mine, c0 ^ cur[j].w);
+        c1 = slice4(mine, c1 ^ cur[j + V / 2].w);
       }
-#pragma unroll
-      for (int j = 0; j < UNIT / 16; ++j) {
-        c = slice4(mine, c ^ v[j].x);
-        c = slice4(mine, c ^ v[j].y);
-        c = slice4(mine, c ^ v[j].z);
-        c = slice4(mine, c ^ v[j].w);
-      }
+      c = op_apply(ops, c0) ^ c1;
     }
 #pragma unroll
     for (int l = 0; l < 5; ++l) {  // lane pairs; the right run is UNIT << l bytes
       const uint32_t o = __shfl_down_sync(0xFFFFFFFFu, c, 1u << l);
-      if ((lane & ((2u << l) - 1u)) == 0) c = op_apply(ops + l * OP_WORDS, c) ^ o;
+      if ((lane & ((2u << l) - 1u)) == 0) c = op_apply(ops + (1 + l) * OP_WORDS, c) ^ o;
     }
     if (lane == 0) wv[warp] = c;
     __syncthreads();
@@ -222,9 +243,9 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
       for (int l = 0; l < 4; ++l) {  // warp pairs; the right run is 32 * UNIT << l bytes
         const uint32_t o = __shfl_down_sync(0xFFFFFFFFu, c, 1u << l);
-        if ((lane & ((2u << l) - 1u)) == 0) c = op_apply(ops + (5 + l) * OP_WORDS, c) ^ o;
+        if ((lane & ((2u << l) - 1u)) == 0) c = op_apply(ops + (6 + l) * OP_WORDS, c) ^ o;
       }
-      if (lane == 0) acc = op_apply(ops + 9 * OP_WORDS, acc) ^ c;
+      if (lane == 0) acc = op_apply(ops + 10 * OP_WORDS, acc) ^ c;
     }
     __syncthreads();
   }
@@ -295,9 +316,10 @@ uint32_t scratch_words(const pxc_ctx* ctx) { return (uint32_t)std::max(ctx->sm_c
 // `d` lies in a device allocation whose start is 16-byte aligned (cudaMalloc,
 // the caching allocators): the kernel reads from `d` rounded down to 16.
 // Returns the kernels launched.
-int device_crc(pxc_ctx* ctx, const void* d, uint64_t len, uint32_t* d_scratch, uint32_t* d_out, cudaStream_t s) {
+// `tabs` = device_tables(ctx).
+int device_crc(pxc_ctx* ctx, const uint32_t* tabs, const void* d, uint64_t len, uint32_t* d_scratch, uint32_t* d_out,
+               cudaStream_t s) {
   const Tables& T = tables();
-  const uint32_t* tabs = device_tables(ctx);
   const uintptr_t addr = reinterpret_cast<uintptr_t>(d);
   const uint32_t lead = (uint32_t)(addr & 15u);
   const uint8_t* base = reinterpret_cast<const uint8_t*>(addr - lead);
@@ -781,20 +803,15 @@ pxc_status pxc_crc32c_device(pxc_ctx* ctx, const void* d_bytes, uint64_t len, ui
     DeviceGuard g(ctx->device);
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
     const uint32_t sw = crc::scratch_words(ctx);
-    DBuf<uint32_t> scratch;
-    scratch.reserve(sw + 1);
-    uint32_t* h = nullptr;
-    PXC_CUDA(cudaMallocHost(&h, 4));
-    try {
-      ctx->launches += crc::device_crc(ctx, len ? d_bytes : scratch.p, len, scratch.p, scratch.p + sw, s);
-      PXC_CUDA(cudaMemcpyAsync(h, scratch.p + sw, 4, cudaMemcpyDeviceToHost, s));
-      PXC_CUDA(cudaStreamSynchronize(s));
-      *out = *h;
-    } catch (...) {
-      cudaFreeHost(h);
-      throw;
-    }
-    cudaFreeHost(h);
+    const uint32_t* tabs = crc::device_tables(ctx);
+    std::lock_guard<std::mutex> lock(ctx->crc_mu);  // the context's scratch and result word
+    if (!ctx->crc_scratch) PXC_CUDA(cudaMalloc(&ctx->crc_scratch, ((size_t)sw + 1) * 4));
+    if (!ctx->crc_host) PXC_CUDA(cudaMallocHost(&ctx->crc_host, 4));
+    ctx->launches += crc::device_crc(ctx, tabs, len ? d_bytes : ctx->crc_scratch, len, ctx->crc_scratch,
+                                     ctx->crc_scratch + sw, s);
+    PXC_CUDA(cudaMemcpyAsync(ctx->crc_host, ctx->crc_scratch + sw, 4, cudaMemcpyDeviceToHost, s));
+    PXC_CUDA(cudaStreamSynchronize(s));
+    *out = *ctx->crc_host;
   });
 }
 
@@ -875,6 +892,7 @@ pxc_status pxc_ivfpq_snapshot_load(pxc_ctx* ctx, const uint8_t* bytes, uint64_t 
     }
     const uint64_t nlive = live_slots.size();
     const uint32_t sw = crc::scratch_words(ctx);
+    const uint32_t* tabs = crc::device_tables(ctx);
     DBuf<uint32_t> scratch, d_live_slots, keys;
     DBuf<uint64_t> d_live_ids;
     scratch.reserve(5 * (size_t)sw + 8);
@@ -902,7 +920,7 @@ pxc_status pxc_ivfpq_snapshot_load(pxc_ctx* ctx, const uint8_t* bytes, uint64_t 
       at = sec.first + nb;
       if (!nb) return;
       PXC_CUDA(cudaMemcpyAsync(dst, body + sec.first, nb, cudaMemcpyHostToDevice, s));
-      ctx->launches += crc::device_crc(ctx, dst, nb, scratch.p + (size_t)next * sw, d_crc + next, s);
+      ctx->launches += crc::device_crc(ctx, tabs, dst, nb, scratch.p + (size_t)next * sw, d_crc + next, s);
       pieces.push_back({nb, next++, nullptr});
     };
     if (r.vectors.second) h->vectors.reserve(r.vectors.second);
@@ -1030,6 +1048,7 @@ pxc_status pxc_ivfpq_snapshot_save(pxc_ivfpq* h, const pxc_ivfpq_config* config,
       w.pos += 4 * n;
     }
     const uint32_t sw = crc::scratch_words(ctx);
+    const uint32_t* tabs = crc::device_tables(ctx);
     DBuf<uint32_t> scratch;
     scratch.reserve(5 * (size_t)sw + 8);
     uint32_t* d_crc = scratch.p + 5 * (size_t)sw;
@@ -1042,7 +1061,7 @@ pxc_status pxc_ivfpq_snapshot_save(pxc_ivfpq* h, const pxc_ivfpq_config* config,
       const uint64_t at = w.pos - snap::HEADER_BYTES;
       pieces.push_back({at - mark, -1, body + mark});
       if (nb) {
-        ctx->launches += crc::device_crc(ctx, src, nb, scratch.p + (size_t)next * sw, d_crc + next, s);
+        ctx->launches += crc::device_crc(ctx, tabs, src, nb, scratch.p + (size_t)next * sw, d_crc + next, s);
         PXC_CUDA(cudaMemcpyAsync(out + w.pos, src, nb, cudaMemcpyDeviceToHost, s));
         pieces.push_back({nb, next++, nullptr});
       }
