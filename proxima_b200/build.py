@@ -30,10 +30,10 @@ NVCC_FLAGS = [
     "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
     f"-I{INCLUDE}", f"-I{CSRC}",
 ]
-CUDA_SOURCES = ["ctx.cu", "flat.cu", "kmeans.cu", "ivfpq.cu", "sq.cu", "filter.cu", "snapshot.cu"]
+CUDA_SOURCES = ["ctx.cu", "flat.cu", "kmeans.cu", "ivfpq.cu", "sq.cu", "filter.cu", "snapshot.cu", "hostcopy.cu"]
 HEADERS = ["common.cuh", "sm100.cuh", "flat_tc.cuh", "topk.cuh", "tmap.cuh", "kmeans_tc.cuh",
            "seqsum.cuh", "rng.h", "kmeans_api.h", "select.cuh", "refdist.cuh", "sq_tc.cuh", "fp32scan.cuh",
-           "ivfpq.cuh"]
+           "ivfpq.cuh", "hostcopy.cuh"]
 CXX = os.environ.get("CXX", shutil.which("g++") or "g++")
 
 

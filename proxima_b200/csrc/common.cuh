@@ -160,6 +160,9 @@ struct pxc_ctx {
   uint32_t* crc_scratch = nullptr;  // block values + result of pxc_crc32c_device (device)
   uint32_t* crc_host = nullptr;     // its result (pinned)
   std::mutex crc_mu;
+  // pinned ring and copy threads for pageable host <-> device copies (hostcopy.cuh)
+  void* stager = nullptr;
+  void (*stager_free)(void*) = nullptr;
 };
 
 namespace pxc {

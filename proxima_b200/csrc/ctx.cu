@@ -337,6 +337,7 @@ void pxc_ctx_destroy(pxc_ctx* ctx) {
   if (ctx->comm && nccl_api().ok) nccl_api().comm_destroy(static_cast<ncclComm_t>(ctx->comm));
   if (ctx->x_send) cudaFree(ctx->x_send);
   if (ctx->x_recv) cudaFree(ctx->x_recv);
+  if (ctx->stager && ctx->stager_free) ctx->stager_free(ctx->stager);
   if (ctx->crc_tab) cudaFree(ctx->crc_tab);
   if (ctx->crc_scratch) cudaFree(ctx->crc_scratch);
   if (ctx->crc_host) cudaFreeHost(ctx->crc_host);

@@ -39,6 +39,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "hostcopy.cuh"
 #include "ivfpq.cuh"
 
 namespace pxc {
@@ -902,14 +903,10 @@ pxc_status pxc_ivfpq_snapshot_load(pxc_ctx* ctx, const uint8_t* bytes, uint64_t 
     h->live.reserve(std::max<uint64_t>(1, n));
     d_live_slots.reserve(std::max<uint64_t>(1, nlive));
     d_live_ids.reserve(std::max<uint64_t>(1, nlive));
-    if (n) {
-      PXC_CUDA(cudaMemcpyAsync(h->ids.p, h->h_ids.data(), n * 8, cudaMemcpyHostToDevice, s));
-      PXC_CUDA(cudaMemcpyAsync(h->live.p, h->h_live.data(), n, cudaMemcpyHostToDevice, s));
-    }
-    if (nlive) {
-      PXC_CUDA(cudaMemcpyAsync(d_live_slots.p, live_slots.data(), nlive * 4, cudaMemcpyHostToDevice, s));
-      PXC_CUDA(cudaMemcpyAsync(d_live_ids.p, live_ids.data(), nlive * 8, cudaMemcpyHostToDevice, s));
-    }
+    hostcopy::to_device(ctx, h->ids.p, h->h_ids.data(), n * 8, s);
+    hostcopy::to_device(ctx, h->live.p, h->h_live.data(), n, s);
+    hostcopy::to_device(ctx, d_live_slots.p, live_slots.data(), nlive * 4, s);
+    hostcopy::to_device(ctx, d_live_ids.p, live_ids.data(), nlive * 8, s);
     // the arrays: one copy each from the image, then their CRC on the device
     std::vector<Piece> pieces;
     uint64_t at = 0;
@@ -919,7 +916,7 @@ pxc_status pxc_ivfpq_snapshot_load(pxc_ctx* ctx, const uint8_t* bytes, uint64_t 
       const uint64_t nb = sec.second * elem;
       at = sec.first + nb;
       if (!nb) return;
-      PXC_CUDA(cudaMemcpyAsync(dst, body + sec.first, nb, cudaMemcpyHostToDevice, s));
+      hostcopy::to_device(ctx, dst, body + sec.first, nb, s);
       ctx->launches += crc::device_crc(ctx, tabs, dst, nb, scratch.p + (size_t)next * sw, d_crc + next, s);
       pieces.push_back({nb, next++, nullptr});
     };
@@ -1062,7 +1059,7 @@ pxc_status pxc_ivfpq_snapshot_save(pxc_ivfpq* h, const pxc_ivfpq_config* config,
       pieces.push_back({at - mark, -1, body + mark});
       if (nb) {
         ctx->launches += crc::device_crc(ctx, tabs, src, nb, scratch.p + (size_t)next * sw, d_crc + next, s);
-        PXC_CUDA(cudaMemcpyAsync(out + w.pos, src, nb, cudaMemcpyDeviceToHost, s));
+        hostcopy::to_host(ctx, out + w.pos, src, nb, s);
         pieces.push_back({nb, next++, nullptr});
       }
       w.pos += nb;

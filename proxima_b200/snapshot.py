@@ -235,8 +235,8 @@ def load_ivfpq(image, context=None, with_metadata: bool = True):
     return idx, out
 
 
-def save_ivfpq(index, config: IvfPqConfig | None = None, report: dict | None = None, metadata=None) -> bytes:
-    """encode (snapshot.rs:120-200) of a device IvfPqIndex. `config` defaults to
+def save_ivfpq(index, config: IvfPqConfig | None = None, report: dict | None = None, metadata=None) -> bytearray:
+    """encode (snapshot.rs:120-200) of a device IvfPqIndex, as a bytearray. `config` defaults to
     the index's own (or IvfPqConfig(nlist, subspaces)); `report` to the one its
     training produced; `metadata` to the per-slot metadata it holds."""
     cfg = config or getattr(index, "config", None) or IvfPqConfig(index.nlist, index.m)
@@ -254,9 +254,11 @@ def save_ivfpq(index, config: IvfPqConfig | None = None, report: dict | None = N
     args = (index.handle, C.byref(native_cfg), C.byref(native_rep) if native_rep is not None else None,
             N.ptr(sec), 0 if sec is None else len(sec))
     N.call("pxc_ivfpq_snapshot_save", *args, None, 0, C.byref(need))
-    out = np.empty(need.value, dtype=np.uint8)
-    N.call("pxc_ivfpq_snapshot_save", *args, out.ctypes.data, need.value, C.byref(need))
-    return out.tobytes()
+    out = bytearray(need.value)
+    buf = (C.c_char * need.value).from_buffer(out)
+    N.call("pxc_ivfpq_snapshot_save", *args, C.addressof(buf), need.value, C.byref(need))
+    del buf  # releases the export so the bytearray can be resized by its owner
+    return out
 
 
 def write_snapshot(path, image) -> int:
