@@ -59,7 +59,7 @@ namespace crc {
 // byte tables or, for one vector per warp, as a XOR reduction over lanes.
 // ---------------------------------------------------------------------------
 constexpr uint32_t POLY = 0x82F63B78u;
-constexpr int UNIT = 128;     // bytes one thread folds per step: two 64-byte halves, two chains
+constexpr int UNIT = 512;     // bytes one thread folds per step: two 256-byte halves, two chains
 constexpr int THREADS = 512;  // threads of the step kernel (16 warps)
 constexpr uint64_t STEP = (uint64_t)UNIT * THREADS;
 constexpr int LEVELS = 10;    // operators S_{UNIT << l}, l = 0..9 (the last one is S_STEP)
@@ -173,13 +173,13 @@ __device__ __forceinline__ uint32_t keep_from(uint32_t w, int first) {  // zero 
 }
 
 // Step kernel: every thread folds one UNIT-byte run per step, f(0, run), as
-// two independent chains over its halves joined by S_{UNIT/2}; a lane tree
-// and a warp tree join the block's 512 runs into f(0, step) and the block
-// folds its q consecutive steps. The next step's run is loaded before the
-// current one is folded. Runs are numbered after `pad` virtual zero runs in
-// front, so every block covers exactly q steps and every join is by a fixed
-// length. `base` is 16-byte aligned; its first `lead` bytes lie before the
-// data and read as zero.
+// two independent chains over its halves (64 bytes of each per iteration,
+// the next iteration's bytes loaded before the current ones are folded),
+// joined by S_{UNIT/2}; a lane tree and a warp tree join the block's 512 runs
+// into f(0, step) and the block folds its q consecutive steps. Runs are
+// numbered after `pad` virtual zero runs in front, so every block covers
+// exactly q steps and every join is by a fixed length. `base` is 16-byte
+// aligned; its first `lead` bytes lie before the data and read as zero.
 __global__ void __launch_bounds__(THREADS, 1)
     crc_step_kernel(const uint8_t* __restrict__ base, uint32_t lead, uint64_t pad, uint32_t q,
                     const uint32_t* __restrict__ tabs, uint32_t* __restrict__ partial) {
@@ -192,15 +192,20 @@ __global__ void __launch_bounds__(THREADS, 1)
   for (uint32_t i = threadIdx.x; i < OPS * OP_WORDS; i += THREADS) ops[i] = tabs[SLICE_WORDS + i];
   __syncthreads();
   const uint32_t* mine = rep + lane;
-  constexpr int V = UNIT / 16;
-  uint4 nxt[V];
-  auto fetch = [&](uint32_t st) -> bool {
+  constexpr int HALF = UNIT / 32;  // uint4 per half run
+  constexpr int IT = HALF / 4;     // iterations per step, 4 uint4 of each half each
+  uint4 nxt[8];
+  auto fetch = [&](uint32_t g) -> bool {
+    const uint32_t st = g / IT, it = g % IT;
     const uint64_t vu = ((uint64_t)blockIdx.x * q + st) * THREADS + threadIdx.x;
     if (vu < pad) return false;
-    const uint4* p = reinterpret_cast<const uint4*>(base + (vu - pad) * UNIT);
+    const uint4* p = reinterpret_cast<const uint4*>(base + (vu - pad) * UNIT) + 4 * it;
 #pragma unroll
-    for (int j = 0; j < V; ++j) nxt[j] = __ldg(p + j);
-    if (vu == pad) {  // run 0: the bytes before the data read as zero
+    for (int j = 0; j < 4; ++j) {
+      nxt[j] = __ldg(p + j);
+      nxt[4 + j] = __ldg(p + HALF + j);
+    }
+    if (vu == pad && it == 0) {  // run 0: the bytes before the data read as zero
       nxt[0].x = keep_from(nxt[0].x, (int)lead);
       nxt[0].y = keep_from(nxt[0].y, (int)lead - 4);
       nxt[0].z = keep_from(nxt[0].z, (int)lead - 8);
@@ -208,30 +213,34 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     return true;
   };
+  const uint32_t total = q * IT;
   bool have_next = fetch(0);
-  uint32_t acc = 0;
-  for (uint32_t st = 0; st < q; ++st) {
-    uint4 cur[V];
+  uint32_t c0 = 0, c1 = 0, acc = 0;
+  bool have_run = false;
+  for (uint32_t g = 0; g < total; ++g) {
+    uint4 cur[8];
 #pragma unroll
-    for (int j = 0; j < V; ++j) cur[j] = nxt[j];
+    for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
     const bool have = have_next;
-    have_next = st + 1 < q ? fetch(st + 1) : false;
-    uint32_t c = 0;
+    have_next = g + 1 < total ? fetch(g + 1) : false;
     if (have) {
-      uint32_t c0 = 0, c1 = 0;
+      have_run = true;
 #pragma unroll
-      for (int j = 0; j < V / 2; ++j) {
+      for (int j = 0; j < 4; ++j) {
         c0 = slice4(mine, c0 ^ cur[j].x);
-        c1 = slice4(mine, c1 ^ cur[j + V / 2].x);
+        c1 = slice4(mine, c1 ^ cur[4 + j].x);
         c0 = slice4(mine, c0 ^ cur[j].y);
-        c1 = slice4(mine, c1 ^ cur[j + V / 2].y);
+        c1 = slice4(mine, c1 ^ cur[4 + j].y);
         c0 = slice4(mine, c0 ^ cur[j].z);
-        c1 = slice4(mine, c1 ^ cur[j + V / 2].z);
+        c1 = slice4(mine, c1 ^ cur[4 + j].z);
         c0 = slice4(mine, c0 ^ cur[j].w);
-        c1 = slice4(mine, c1 ^ cur[j + V / 2].w);
+        c1 = slice4(mine, c1 ^ cur[4 + j].w);
       }
-      c = op_apply(ops, c0) ^ c1;
     }
+    if (g % IT != IT - 1) continue;
+    uint32_t c = have_run ? op_apply(ops, c0) ^ c1 : 0u;
+    c0 = c1 = 0;
+    have_run = false;
 #pragma unroll
     for (int l = 0; l < 5; ++l) {  // lane pairs; the right run is UNIT << l bytes
       const uint32_t o = __shfl_down_sync(0xFFFFFFFFu, c, 1u << l);

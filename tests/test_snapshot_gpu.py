@@ -25,8 +25,8 @@ from proxima_b200.ivfpq import IvfPqIndex
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("n", [0, 1, 3, 15, 16, 17, 255, 256, 257, 4095, 131071, 131072, 131073,
-                               (1 << 20) + 5, (3 << 20) + 77])
+@pytest.mark.parametrize("n", [0, 1, 3, 15, 16, 17, 255, 256, 257, 511, 512, 513, 4095, 131071, 131072, 131073,
+                               262143, 262144, 262145, (1 << 20) + 5, (3 << 20) + 77])
 def test_device_crc_equals_the_oracle(n):
     rng = np.random.default_rng(n)
     host = rng.integers(0, 256, n + 16, dtype=np.uint8)
