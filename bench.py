@@ -66,6 +66,17 @@ def parse():
     return p.parse_args()
 
 
+def k1_source_hash() -> str:
+    """SHA-256 of the sources that decide K1's memory traffic (the kernel and its launch), so that a
+    DRAM-traffic figure captured by ncu is reported only for the kernel it was measured on."""
+    import hashlib
+
+    h = hashlib.sha256()
+    for name in ("flat_tc.cuh", "flat.cu", "sm100.cuh"):
+        h.update((ROOT / "proxima_b200" / "csrc" / name).read_bytes())
+    return h.hexdigest()
+
+
 def peaks():
     f = ROOT / "MEASURED_PEAKS.json"
     if f.exists():
@@ -1362,10 +1373,13 @@ def main():
     traffic, traffic_src = None, None
     tf = ROOT / "profiles" / "traffic.json"
     if tf.exists() and world == 1 and path == 1 and k <= 32 and n == 1_000_000 and nq == 10_000:
-        t = json.loads(tf.read_text()).get("flat_u8_kernel_c2_bytes_per_launch")
-        if t:
+        rec = json.loads(tf.read_text())
+        t = rec.get("flat_u8_kernel_c2_bytes_per_launch")
+        if t and rec.get("kernel_source_sha256") == k1_source_hash():
             traffic, traffic_src = t, "ncu dram__bytes_read.sum + dram__bytes_write.sum of this launch shape " \
-                                      "(profiles/flat_u8_kernel_c2.md)"
+                                      "and this kernel source (profiles/flat_u8_kernel_c2.md)"
+        elif t:
+            traffic_src = "not reported: the K1 source changed since the ncu capture in profiles/traffic.json"
     kernel = {1: "flat_scan_kernel<KT, U8Scan> (K1)", 2: "flat_scan_kernel<32, F16Scan> (K2 screen)"}.get(
         path, "dist_chunk_kernel + select (K1g)")
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak,

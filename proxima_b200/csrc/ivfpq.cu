@@ -36,6 +36,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "hostcopy.cuh"
 #include "ivfpq.cuh"
 #include "kmeans_api.h"
 #include "rng.h"
@@ -911,6 +912,81 @@ void rank_ids_device(pxc_ivfpq* h, const uint32_t* d_live_slots, const uint64_t*
   PXC_CUDA(cudaStreamSynchronize(s));  // the sort's scratch is freed on return
 }
 
+// The slot store (pxc_ivfpq_set_store / _device): the vectors (host, staged,
+// or device) go to HBM and are checked there for non-finite components; the
+// VectorId ranks of the live slots are a radix sort on the device, which also
+// finds a VectorId live twice. Clears the lists.
+void set_store(pxc_ivfpq* h, const float* vectors, bool on_device, const uint64_t* ids, const uint8_t* live,
+               uint64_t nslots) {
+  PXC_CONFIG(nslots < 0xFFFFFFFFull, "nslots", nslots, "the device IVF-PQ supports fewer than 2^32 slots");
+  std::lock_guard<std::mutex> lock(h->mu);
+  pxc_ctx* ctx = h->ctx;
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = ctx->stream;
+  handoff_drain(h);
+  h->nslots = nslots;
+  h->h_ids.resize(nslots);
+  h->h_live.assign(nslots, 1);
+  std::vector<uint32_t> live_slots;
+  std::vector<uint64_t> live_ids;
+  live_slots.reserve(nslots);
+  live_ids.reserve(nslots);
+  for (uint64_t i = 0; i < nslots; ++i) {
+    h->h_ids[i] = ids ? ids[i] : i;
+    if (live) h->h_live[i] = live[i] ? 1 : 0;
+    if (h->h_live[i]) {
+      live_slots.push_back((uint32_t)i);
+      live_ids.push_back(h->h_ids[i]);
+    }
+  }
+  const uint64_t nlive = live_slots.size();
+  DBuf<uint32_t> d_slots, flags;
+  DBuf<uint64_t> d_ids;
+  DBuf<unsigned long long> first;
+  flags.reserve(1);
+  first.reserve(1);
+  PXC_CUDA(cudaMemsetAsync(flags.p, 0xFF, 4, s));
+  PXC_CUDA(cudaMemsetAsync(first.p, 0xFF, 8, s));
+  h->have_vectors = false;
+  if (vectors && nslots) {
+    h->vectors.reserve(nslots * h->dim);
+    if (on_device)
+      PXC_CUDA(cudaMemcpyAsync(h->vectors.p, vectors, nslots * h->dim * 4, cudaMemcpyDeviceToDevice, s));
+    else
+      hostcopy::to_device(ctx, h->vectors.p, vectors, nslots * h->dim * 4, s);
+    first_nonfinite_kernel<<<1184, 256, 0, s>>>(h->vectors.p, nslots * h->dim, first.p);
+    PXC_CUDA(cudaGetLastError());
+    ctx->launches += 1;
+  }
+  h->ids.reserve(std::max<uint64_t>(1, nslots));
+  h->live.reserve(std::max<uint64_t>(1, nslots));
+  d_slots.reserve(std::max<uint64_t>(1, nlive));
+  d_ids.reserve(std::max<uint64_t>(1, nlive));
+  hostcopy::to_device(ctx, h->ids.p, h->h_ids.data(), nslots * 8, s);
+  hostcopy::to_device(ctx, h->live.p, h->h_live.data(), nslots, s);
+  hostcopy::to_device(ctx, d_slots.p, live_slots.data(), nlive * 4, s);
+  hostcopy::to_device(ctx, d_ids.p, live_ids.data(), nlive * 8, s);
+  rank_ids_device(h, d_slots.p, d_ids.p, nlive, flags.p, s);  // returns synchronised
+  unsigned long long bad = 0;
+  uint32_t dup = 0;
+  PXC_CUDA(cudaMemcpy(&bad, first.p, 8, cudaMemcpyDeviceToHost));
+  PXC_CUDA(cudaMemcpy(&dup, flags.p, 4, cudaMemcpyDeviceToHost));
+  h->have_lists = false;
+  h->u8_state = 0;
+  if (bad != ~0ull) {
+    h->nslots = 0;
+    h->nlive = 0;
+    throw make_failure(PXC_NON_FINITE, bad, 0, "vectors", "vector component %llu is not finite", bad);
+  }
+  if (dup != 0xFFFFFFFFu) {
+    h->nslots = 0;
+    h->nlive = 0;
+    throw make_failure(PXC_DUPLICATE_ID, h->h_ids[dup], 0, "ids", "VectorId %llu is live twice",
+                       (unsigned long long)h->h_ids[dup]);
+  }
+  h->have_vectors = vectors != nullptr && nslots > 0;
+}
+
 }  // namespace ivf
 }  // namespace pxc
 
@@ -979,55 +1055,7 @@ pxc_status pxc_ivfpq_set_store(pxc_ivfpq* h, const float* vectors, const uint64_
                                uint64_t nslots, pxc_error* err) {
   return guarded(err, [&] {
     PXC_CONFIG(h != nullptr, "h", 0, "null handle");
-    PXC_CONFIG(nslots < 0xFFFFFFFFull, "nslots", nslots, "the device IVF-PQ supports fewer than 2^32 slots");
-    std::lock_guard<std::mutex> lock(h->mu);
-    DeviceGuard g(h->ctx->device);
-    cudaStream_t s = h->ctx->stream;
-    ivf::handoff_drain(h);
-    h->nslots = nslots;
-    h->h_ids.resize(nslots);
-    h->h_live.assign(nslots, 1);
-    for (uint64_t i = 0; i < nslots; ++i) {
-      h->h_ids[i] = ids ? ids[i] : i;
-      if (live) h->h_live[i] = live[i] ? 1 : 0;
-    }
-    if (vectors)
-      for (uint64_t i = 0; i < nslots * h->dim; ++i)
-        if (!std::isfinite(vectors[i]))
-          throw make_failure(PXC_NON_FINITE, i, 0, "vectors", "vector component %llu is not finite",
-                             (unsigned long long)i);
-    // rank of each live slot's VectorId: (score, rank) orders as (score, id)
-    std::vector<uint32_t> order;
-    order.reserve(nslots);
-    for (uint64_t i = 0; i < nslots; ++i)
-      if (h->h_live[i]) order.push_back((uint32_t)i);
-    std::sort(order.begin(), order.end(), [&](uint32_t a, uint32_t b) { return h->h_ids[a] < h->h_ids[b]; });
-    for (size_t r = 1; r < order.size(); ++r)
-      if (h->h_ids[order[r]] == h->h_ids[order[r - 1]])
-        throw make_failure(PXC_DUPLICATE_ID, h->h_ids[order[r]], 0, "ids", "VectorId %llu is live twice",
-                           (unsigned long long)h->h_ids[order[r]]);
-    std::vector<uint32_t> sr(std::max<uint64_t>(1, nslots), 0xFFFFFFFFu);
-    for (size_t r = 0; r < order.size(); ++r) sr[order[r]] = (uint32_t)r;
-    h->nlive = order.size();
-    h->ids.reserve(std::max<uint64_t>(1, nslots));
-    h->slot_rank.reserve(std::max<uint64_t>(1, nslots));
-    h->rank_slot.reserve(std::max<size_t>(1, order.size()));
-    if (nslots) {
-      PXC_CUDA(cudaMemcpyAsync(h->ids.p, h->h_ids.data(), nslots * 8, cudaMemcpyHostToDevice, s));
-      PXC_CUDA(cudaMemcpyAsync(h->slot_rank.p, sr.data(), nslots * 4, cudaMemcpyHostToDevice, s));
-    }
-    if (!order.empty())
-      PXC_CUDA(cudaMemcpyAsync(h->rank_slot.p, order.data(), order.size() * 4, cudaMemcpyHostToDevice, s));
-    h->live.reserve(std::max<uint64_t>(1, nslots));
-    if (nslots) PXC_CUDA(cudaMemcpyAsync(h->live.p, h->h_live.data(), nslots, cudaMemcpyHostToDevice, s));
-    h->have_vectors = vectors != nullptr;
-    if (vectors && nslots) {
-      h->vectors.reserve(nslots * h->dim);
-      PXC_CUDA(cudaMemcpyAsync(h->vectors.p, vectors, nslots * h->dim * 4, cudaMemcpyHostToDevice, s));
-    }
-    PXC_CUDA(cudaStreamSynchronize(s));
-    h->have_lists = false;
-    h->u8_state = 0;
+    ivf::set_store(h, vectors, false, ids, live, nslots);
   });
 }
 
@@ -1035,24 +1063,7 @@ pxc_status pxc_ivfpq_set_store_device(pxc_ivfpq* h, const float* d_vectors, cons
                                       const uint8_t* live, uint64_t nslots, pxc_error* err) {
   return guarded(err, [&] {
     PXC_CONFIG(h != nullptr, "h", 0, "null handle");
-    PXC_CONFIG(nslots < 0xFFFFFFFFull, "nslots", nslots, "the device IVF-PQ supports fewer than 2^32 slots");
-    {
-      // ids and live flags (host) as in pxc_ivfpq_set_store, no vectors yet
-      pxc_error e2{};
-      pxc_status st = pxc_ivfpq_set_store(h, nullptr, ids, live, nslots, &e2);
-      if (st != PXC_OK) throw make_failure(st, e2.a, e2.b, e2.parameter, "%s", e2.detail);
-    }
-    std::lock_guard<std::mutex> lock(h->mu);
-    DeviceGuard g(h->ctx->device);
-    cudaStream_t s = h->ctx->stream;
-    ivf::handoff_drain(h);
-    if (d_vectors && nslots) {
-      h->vectors.reserve(nslots * h->dim);
-      PXC_CUDA(cudaMemcpyAsync(h->vectors.p, d_vectors, nslots * h->dim * 4, cudaMemcpyDeviceToDevice, s));
-      PXC_CUDA(cudaStreamSynchronize(s));
-      h->have_vectors = true;
-    }
-    h->u8_state = 0;
+    ivf::set_store(h, d_vectors, true, ids, live, nslots);
   });
 }
 

@@ -83,5 +83,8 @@ void build_lists_device(pxc_ivfpq* h, const uint32_t* d_keys, cudaStream_t s);
 // earlier slot's goes to *d_dup (initialised by the caller). Enqueued on `s`.
 void rank_ids_device(pxc_ivfpq* h, const uint32_t* d_live_slots, const uint64_t* d_live_ids, uint64_t nlive,
                      uint32_t* d_dup, cudaStream_t s);
+// The slot store from host or device vectors (pxc_ivfpq_set_store / _device).
+void set_store(pxc_ivfpq* h, const float* vectors, bool on_device, const uint64_t* ids, const uint8_t* live,
+               uint64_t nslots);
 }  // namespace ivf
 }  // namespace pxc
