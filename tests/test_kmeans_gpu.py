@@ -164,3 +164,16 @@ def test_device_entry_point_matches_host_entry_point():
     assert np.array_equal(a.centroids.view(np.uint32), b.centroids.view(np.uint32))
     assert np.array_equal(a.assignment, b.assignment)
     assert a.inertia == b.inertia and a.iterations == b.iterations
+
+
+def test_c3_at_the_configuration_size():
+    """C3 exactly as bench.py trains it (1M x 96 unit-sphere blobs, k = 4096, the
+    seeded-sample start), cut to its first two Lloyd iterations so the oracle
+    finishes in about a minute on the host's cores: centroids, assignments and
+    inertia bit-identical to the oracle's."""
+    pts = fixtures.c3_points(1_000_000, 96)
+    init = fixtures.c3_init(pts, 4096)
+    cent, assign, inertia, iters = pxo.kmeans(pts, 4096, 2, init=init)
+    got = kmeans(pts, 96, 4096, 2, init=init, want_assignment=True)
+    assert got.path == 1  # the tensor-core screen with exact re-scoring
+    _same(got, cent, assign, inertia, iters, "C3 full size, 2 iterations")
