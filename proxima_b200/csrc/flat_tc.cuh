@@ -28,11 +28,10 @@
 //   warps 2-9   epilogue, one thread per query row (warps 2-5: first query
 //               half, 6-9: second): tcgen05.ld 32 columns at a time (two
 //               chunks in flight), r = h - 2*dot, a tree min against the
-//               thread's admission bound; a chunk where some lane has a
-//               candidate queues that lane's admitted (r, rank) pairs from
-//               the registers it already holds (no second TMEM read), and
-//               the queue is drained into a sorted register list of KT
-//               entries after the accumulator is released.
+//               thread's admission bound; only chunks where some lane has a
+//               candidate take the slow path, which re-reads just the
+//               candidate columns from TMEM and inserts into a sorted
+//               register list of KT entries.
 // The halves ping-pong: while the tensor core fills one half's accumulator
 // for tile t, the other half's epilogue drains tile t-1 (or t).
 // The CTAs of one query tile share a per-query bound in global memory (each
@@ -526,29 +525,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // the load's latency hides behind the scan
       const T fresh_bound = load_bound<P>(bound_ptr);
       uint32_t va[32], vb[32];
+      uint32_t hit = 0;  // bit c: chunk c holds a candidate for this lane
       tmem_ld_32x32b_x32(taddr, va);
       tmem_ld_wait();
 #pragma unroll 1
       for (uint32_t c = 0; c < BN / 32; c += 2) {
-        // chunk c from va while chunk c+1 loads into vb, then the reverse. A
-        // chunk where some lane has a candidate queues that lane's admitted
-        // pairs straight from the values just computed (warp-uniform branch).
+        // chunk c from va while chunk c+1 loads into vb, then the reverse
         tmem_ld_32x32b_x32(taddr + (c + 1) * 32, vb);
-        {
-          T r[32];
-          const T m = chunk_r<P>(va, nrm + c * 32, coef, r);
-          if (__any_sync(0xFFFFFFFFu, m < thr))
-            fifo_push_chunk<KT, P>(r, thr, rank_base + c * 32, wfifo, fifo_cnt, lane, lr, lk, shared_bound);
-        }
+        hit |= static_cast<uint32_t>(chunk_min<P>(va, nrm + c * 32, coef) < thr) << c;
         tmem_ld_wait();
         if (c + 2 < BN / 32) tmem_ld_32x32b_x32(taddr + (c + 2) * 32, va);
-        {
-          T r[32];
-          const T m = chunk_r<P>(vb, nrm + (c + 1) * 32, coef, r);
-          if (__any_sync(0xFFFFFFFFu, m < thr))
-            fifo_push_chunk<KT, P>(r, thr, rank_base + (c + 1) * 32, wfifo, fifo_cnt, lane, lr, lk, shared_bound);
-        }
+        hit |= static_cast<uint32_t>(chunk_min<P>(vb, nrm + (c + 1) * 32, coef) < thr) << (c + 1);
         tmem_ld_wait();
+      }
+      // Flagged chunks (one vote per tile) are re-read from TMEM and their
+      // admitted pairs queued; the accumulator is released right after.
+      uint32_t uhit = __reduce_or_sync(0xFFFFFFFFu, hit);
+      while (uhit) {
+        const uint32_t c = __ffs(uhit) - 1;
+        uhit &= uhit - 1;
+        T r[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, va);
+        tmem_ld_wait();
+        chunk_r<P>(va, nrm + c * 32, coef, r);
+        fifo_push_chunk<KT, P>(r, thr, rank_base + c * 32, wfifo, fifo_cnt, lane, lr, lk, shared_bound);
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[half]);
