@@ -539,16 +539,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tmem_ld_wait();
       }
       // Flagged chunks (one vote per tile) are re-read from TMEM and their
-      // admitted pairs queued; the accumulator is released right after.
+      // admitted pairs queued in rank order; the accumulator is released right
+      // after. With lists of up to 10 entries two chunks are read per wait;
+      // longer lists leave registers for one.
       uint32_t uhit = __reduce_or_sync(0xFFFFFFFFu, hit);
       while (uhit) {
-        const uint32_t c = __ffs(uhit) - 1;
+        const uint32_t ca = __ffs(uhit) - 1;
         uhit &= uhit - 1;
-        T r[32];
-        tmem_ld_32x32b_x32(taddr + c * 32, va);
+        uint32_t cb = BN / 32;
+        tmem_ld_32x32b_x32(taddr + ca * 32, va);
+        if constexpr (KT <= 10) {
+          if (uhit) {
+            cb = __ffs(uhit) - 1;
+            uhit &= uhit - 1;
+            tmem_ld_32x32b_x32(taddr + cb * 32, vb);
+          }
+        }
         tmem_ld_wait();
-        chunk_r<P>(va, nrm + c * 32, coef, r);
-        fifo_push_chunk<KT, P>(r, thr, rank_base + c * 32, wfifo, fifo_cnt, lane, lr, lk, shared_bound);
+        {
+          T r[32];
+          chunk_r<P>(va, nrm + ca * 32, coef, r);
+          fifo_push_chunk<KT, P>(r, thr, rank_base + ca * 32, wfifo, fifo_cnt, lane, lr, lk, shared_bound);
+        }
+        if (cb < BN / 32) {
+          T r[32];
+          chunk_r<P>(vb, nrm + cb * 32, coef, r);
+          fifo_push_chunk<KT, P>(r, thr, rank_base + cb * 32, wfifo, fifo_cnt, lane, lr, lk, shared_bound);
+        }
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[half]);
