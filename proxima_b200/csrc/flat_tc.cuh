@@ -100,6 +100,12 @@ struct U8Scan {
   __host__ __device__ static T unpack(uint32_t key) { return static_cast<int32_t>(key - R_OFFSET); }
   __device__ static T next_up(T r) { return r + 1; }
   __device__ static T value(uint32_t acc, T h, float) { return h - 2 * static_cast<int32_t>(acc); }
+  // A lower bound of value() over a chunk: the chunk's smallest row term less
+  // twice its largest product (the s32 products are non-negative, so their
+  // bit patterns order as the f32 values they spell).
+  __device__ static T lower_bound(uint32_t vmax_bits, T hmin, float) {
+    return hmin - 2 * static_cast<int32_t>(vmax_bits);
+  }
   // the value shared as the pruning bound: the list's k-th
   __device__ static T publish(T kth, T, float) { return kth; }
   __device__ static uint32_t idesc() { return sm100::idesc_u8_s32(UM, BN); }
@@ -117,6 +123,12 @@ struct F16Scan {
   __host__ __device__ static T unpack(uint32_t key) { return key_to_float(key); }
   __device__ static T next_up(T r) { return key_to_float(order_key(r) + 1u); }
   __device__ static T value(uint32_t acc, T h, float c) { return fmaf(__uint_as_float(acc), c, h); }
+  // A lower bound of value() over a chunk (c < 0 for every metric: it carries
+  // the -2 or -1 of the distance): the smallest row term plus c times the
+  // largest product; fmaf rounds monotonically, so the bound holds as computed.
+  __device__ static T lower_bound(uint32_t vmax_bits, T hmin, float c) {
+    return fmaf(__uint_as_float(vmax_bits), c, hmin);
+  }
   // the value shared as the pruning bound: the list's last entry, or its k-th
   // plus the query's margin when that is smaller (rows behind it cannot
   // change a provable answer)
@@ -127,10 +139,12 @@ struct F16Scan {
   }
 };
 
-// per-warp: two tiles of the per-row term, and the deferred-insertion FIFO
+// per-warp: two tiles of the per-row term and of its per-chunk minima, and
+// the deferred-insertion FIFO
+constexpr int CHUNKS = BN / 32;
 template <class P>
 __host__ __device__ constexpr size_t norm_bytes() {
-  return (size_t)NUM_EPI_WARPS * (2 * BN * 4 + P::FIFO_SLOTS * 32 * sizeof(uint2));
+  return (size_t)NUM_EPI_WARPS * (2 * BN * 4 + 2 * CHUNKS * 4 + P::FIFO_SLOTS * 32 * sizeof(uint2));
 }
 
 struct Params {
@@ -269,11 +283,62 @@ __device__ __forceinline__ typename P::T chunk_r(const uint32_t (&v)[32], const 
   return min(min(m[0], m[2]), min(m[1], m[3]));
 }
 
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+// Bit pattern of the largest of 32 accumulator values read as f32 (a tree of
+// three-input maxima).
+__device__ __forceinline__ uint32_t chunk_max_bits(const uint32_t (&v)[32]) {
+  float m[11];
+#pragma unroll
+  for (int j = 0; j < 10; ++j)
+    m[j] = fmax3(__uint_as_float(v[3 * j]), __uint_as_float(v[3 * j + 1]), __uint_as_float(v[3 * j + 2]));
+  m[10] = fmaxf(__uint_as_float(v[30]), __uint_as_float(v[31]));
+  const float a = fmax3(m[0], m[1], m[2]), b = fmax3(m[3], m[4], m[5]), c = fmax3(m[6], m[7], m[8]);
+  return __float_as_uint(fmax3(fmax3(a, b, c), m[9], m[10]));
+}
+
+// Writes one tile's row terms (a: columns 4*lane.., b: 128 + 4*lane..) and
+// the minimum of each 32-column chunk into this warp's slot.
+template <class P>
+__device__ __forceinline__ void stage_norms(typename P::T* slot, typename P::T* slot_min, int4 a, int4 b,
+                                            uint32_t lane) {
+  using T = typename P::T;
+  reinterpret_cast<int4*>(slot)[lane] = a;
+  reinterpret_cast<int4*>(slot)[32 + lane] = b;
+  const T* x = reinterpret_cast<const T*>(&a);
+  const T* y = reinterpret_cast<const T*>(&b);
+  T m0 = min(min(x[0], x[1]), min(x[2], x[3]));
+  T m1 = min(min(y[0], y[1]), min(y[2], y[3]));
+#pragma unroll
+  for (int off = 4; off > 0; off >>= 1) {
+    m0 = min(m0, __shfl_xor_sync(0xFFFFFFFFu, m0, off));
+    m1 = min(m1, __shfl_xor_sync(0xFFFFFFFFu, m1, off));
+  }
+  if ((lane & 7u) == 0) {
+    slot_min[lane >> 3] = m0;
+    slot_min[CHUNKS / 2 + (lane >> 3)] = m1;
+  }
+}
+
 // Minimum of r over one 32-column chunk without keeping r (fast path).
 template <class P>
 __device__ __forceinline__ typename P::T chunk_min(const uint32_t (&v)[32], const typename P::T* nrm, float c) {
   typename P::T r[32];
   return chunk_r<P>(v, nrm, c, r);
+}
+
+// Whether the chunk holds a value below thr for this lane. Most chunks are
+// ruled out by the lower bound (about 17 instructions); the exact minimum is
+// taken only when some lane of the warp cannot rule its chunk out.
+template <class P>
+__device__ __forceinline__ bool chunk_hit(const uint32_t (&v)[32], const typename P::T* nrm, typename P::T hmin,
+                                          float c, typename P::T thr) {
+  const bool maybe = P::lower_bound(chunk_max_bits(v), hmin, c) < thr;
+  if (!__any_sync(0xFFFFFFFFu, maybe)) return false;
+  return maybe && chunk_min<P>(v, nrm, c) < thr;
 }
 
 // Deferred insertion. A flagged chunk's admitted (r, rank) pairs are pushed
@@ -333,7 +398,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   unsigned char* sA = smem;
   unsigned char* sB = smem + (size_t)kblocks * A_BLOCK;
   T* sNorm = reinterpret_cast<T*>(sB + (size_t)stages * B_BLOCK);             // [warp][2][BN]
-  uint2* sFifo = reinterpret_cast<uint2*>(sNorm + NUM_EPI_WARPS * 2 * BN);    // [warp][slot][lane]
+  T* sNormMin = sNorm + NUM_EPI_WARPS * 2 * BN;                               // [warp][2][CHUNKS]
+  uint2* sFifo = reinterpret_cast<uint2*>(sNormMin + NUM_EPI_WARPS * 2 * CHUNKS);  // [warp][slot][lane]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sFifo + NUM_EPI_WARPS * P::FIFO_SLOTS * 32);
   uint64_t* full = bars;
   uint64_t* empty = bars + stages;
@@ -478,6 +544,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t q = qtile * BM + row;
     uint32_t* bound_ptr = p.bound + q;
     T* wnorm = sNorm + ew * 2 * BN;  // this warp's two tile slots
+    T* wmin = sNormMin + ew * 2 * CHUNKS;
     uint2* wfifo = sFifo + ew * P::FIFO_SLOTS * 32;  // this warp's deferred-insertion FIFO
     uint32_t fifo_cnt = 0;
     const float coef = (p.qcoef != nullptr && q < p.nq) ? p.qcoef[q] : 0.0f;
@@ -497,8 +564,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int4 nx0 = make_int4(0, 0, 0, 0), nx1 = nx0;
     if (ntile_local > 0) {
       const int4* src = reinterpret_cast<const int4*>(static_cast<const T*>(p.norms) + (size_t)t_begin * BN);
-      reinterpret_cast<int4*>(wnorm)[lane] = __ldg(src + lane);
-      reinterpret_cast<int4*>(wnorm)[32 + lane] = __ldg(src + 32 + lane);
+      stage_norms<P>(wnorm, wmin, __ldg(src + lane), __ldg(src + 32 + lane), lane);
     }
     __syncwarp();
     for (uint32_t t = 0; t < ntile_local; ++t) {
@@ -517,6 +583,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t rank_base = (t_begin + t) * BN;
       const uint32_t taddr = tmem_base + ((quarter * 32) << 16) + half * BN;
       const T* nrm = wnorm + (t & 1) * BN;
+      const T* nmin = wmin + (t & 1) * CHUNKS;
       // Fast path, branch-free over the whole tile: per chunk only the minimum
       // of r, compared with the admission bound taken at the start of the tile
       // (the list does not change within a tile: insertions are deferred).
@@ -532,10 +599,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (uint32_t c = 0; c < BN / 32; c += 2) {
         // chunk c from va while chunk c+1 loads into vb, then the reverse
         tmem_ld_32x32b_x32(taddr + (c + 1) * 32, vb);
-        hit |= static_cast<uint32_t>(chunk_min<P>(va, nrm + c * 32, coef) < thr) << c;
+        hit |= static_cast<uint32_t>(chunk_hit<P>(va, nrm + c * 32, nmin[c], coef, thr)) << c;
         tmem_ld_wait();
         if (c + 2 < BN / 32) tmem_ld_32x32b_x32(taddr + (c + 2) * 32, va);
-        hit |= static_cast<uint32_t>(chunk_min<P>(vb, nrm + (c + 1) * 32, coef) < thr) << (c + 1);
+        hit |= static_cast<uint32_t>(chunk_hit<P>(vb, nrm + (c + 1) * 32, nmin[c + 1], coef, thr)) << (c + 1);
         tmem_ld_wait();
       }
       // Flagged chunks (one vote per tile) are re-read from TMEM and their
@@ -570,11 +637,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_before();
       mbar_arrive(&acc_empty[half]);
       // This warp finished reading slot (t+1)&1 during tile t-1.
-      if (t + 1 < ntile_local) {
-        int4* dst = reinterpret_cast<int4*>(wnorm + ((t + 1) & 1) * BN);
-        dst[lane] = nx0;
-        dst[32 + lane] = nx1;
-      }
+      if (t + 1 < ntile_local) stage_norms<P>(wnorm + ((t + 1) & 1) * BN, wmin + ((t + 1) & 1) * CHUNKS, nx0, nx1, lane);
       // insertions happen while the tensor core fills the next tile
       if (fifo_cnt) fifo_drain<KT, P>(wfifo, fifo_cnt, lane, lr, lk, shared_bound);
       __syncwarp();
