@@ -27,11 +27,13 @@
 //               together (with N=128 they serialise and the tile rate halves);
 //   warps 2-9   epilogue, one thread per query row (warps 2-5: first query
 //               half, 6-9: second): tcgen05.ld 32 columns at a time (two
-//               chunks in flight), r = h - 2*dot, a tree min against the
-//               thread's admission bound; only chunks where some lane has a
-//               candidate take the slow path, which re-reads just the
-//               candidate columns from TMEM and inserts into a sorted
-//               register list of KT entries.
+//               chunks per wait); per chunk a lower bound of r (smallest
+//               row term, largest product) against the thread's admission
+//               bound, and r = h - 2*dot with a tree min only where some
+//               lane cannot rule its chunk out; chunks where some lane has
+//               a candidate take the slow path, which re-reads them from
+//               TMEM and queues their admitted pairs for insertion into a
+//               sorted register list of KT entries.
 // The halves ping-pong: while the tensor core fills one half's accumulator
 // for tile t, the other half's epilogue drains tile t-1 (or t).
 // The CTAs of one query tile share a per-query bound in global memory (each
@@ -593,17 +595,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const T fresh_bound = load_bound<P>(bound_ptr);
       uint32_t va[32], vb[32];
       uint32_t hit = 0;  // bit c: chunk c holds a candidate for this lane
-      tmem_ld_32x32b_x32(taddr, va);
-      tmem_ld_wait();
 #pragma unroll 1
       for (uint32_t c = 0; c < BN / 32; c += 2) {
-        // chunk c from va while chunk c+1 loads into vb, then the reverse
+        // two chunks per wait: the read latency, not the arithmetic, bounds
+        // this loop (and nothing runs while a read is in flight)
+        tmem_ld_32x32b_x32(taddr + c * 32, va);
         tmem_ld_32x32b_x32(taddr + (c + 1) * 32, vb);
+        tmem_ld_wait();
         hit |= static_cast<uint32_t>(chunk_hit<P>(va, nrm + c * 32, nmin[c], coef, thr)) << c;
-        tmem_ld_wait();
-        if (c + 2 < BN / 32) tmem_ld_32x32b_x32(taddr + (c + 2) * 32, va);
         hit |= static_cast<uint32_t>(chunk_hit<P>(vb, nrm + (c + 1) * 32, nmin[c + 1], coef, thr)) << (c + 1);
-        tmem_ld_wait();
       }
       // Flagged chunks (one vote per tile) are re-read from TMEM and their
       // admitted pairs queued in rank order; the accumulator is released right
