@@ -267,6 +267,18 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(const ScanParams p) 
     const float one_minus = cosine ? __fsub_rn(1.0f, qdc) : 0.0f;
     const uint32_t b = p.list_off[l], e = p.list_off[l + 1];
     if (t == 0 && p.scanned) atomicAdd(p.scanned, (unsigned long long)(e - b));
+    // m = 16 (one 16-byte code per row): the next chunk's codes are loaded
+    // while the current chunk's are looked up
+    constexpr int U = CHUNK / SCAN_THREADS;
+    uint4 pre[U];
+    auto fetch16 = [&](uint32_t j0f) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const uint32_t j = j0f + t + u * SCAN_THREADS;
+        pre[u] = j < e ? __ldg(reinterpret_cast<const uint4*>(p.list_codes) + j) : make_uint4(0u, 0u, 0u, 0u);
+      }
+    };
+    if (m == 16) fetch16(b);
     for (uint32_t j0 = b; j0 < e; j0 += CHUNK) {
       if (count > CB - CHUNK) {
         const uint64_t kth = select_keep<CB_MAX / SCAN_THREADS>(buf, count, p.shortlist, hist, sh);
@@ -279,7 +291,10 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(const ScanParams p) 
       const uint64_t th = thr;
       const uint32_t j1 = min(e, j0 + CHUNK);
       // four codes per thread at once: four independent lookup chains
-      constexpr int U = CHUNK / SCAN_THREADS;
+      uint4 cur[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) cur[u] = pre[u];
+      if (m == 16 && j0 + CHUNK < e) fetch16(j0 + CHUNK);
       uint32_t jj[U];
       bool on[U];
       float sum[U];
@@ -293,7 +308,19 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(const ScanParams p) 
           on[u] = (p.bitmap[slot >> 6] >> (slot & 63)) & 1ull;
         }
       }
-      if ((m & 15) == 0) {
+      if (m == 16) {
+#pragma unroll
+        for (int b = 0; b < 16; ++b) {
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const uint32_t word = (b >> 2) == 0 ? cur[u].x : (b >> 2) == 1 ? cur[u].y : (b >> 2) == 2 ? cur[u].z : cur[u].w;
+            // byte b & 3 of the word, zero-extended (one PRMT); rows switched off
+            // by the filter add their table entries and are dropped at admission
+            const uint32_t idx = __byte_perm(word, 0u, 0x4440u + (b & 3));
+            sum[u] = __fadd_rn(sum[u], lut[b * 256 + idx]);
+          }
+        }
+      } else if ((m & 15) == 0) {
         for (uint32_t s0 = 0; s0 < m; s0 += 16) {
           uint32_t w4[U][4];
 #pragma unroll
