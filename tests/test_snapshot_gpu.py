@@ -194,3 +194,30 @@ def test_damaged_images_fail_as_the_host_reader_says():
     with pytest.raises(Configuration):
         S.load_ivfpq(flat)
     idx.close()
+
+
+def test_large_arrays_take_the_staged_copies():
+    """Vectors of 12 MB move through the pinned ring in both directions (8 MiB
+    chunks, a partial last one): the image still equals the oracle's encoding
+    and the reload equals the saved index."""
+    n, dim, m = 48_000, 64, 16
+    data = fixtures.blobs_f32(n, dim, 64, 5, 6)
+    idx = IvfPqIndex(dim, 64, m)
+    idx.set_store(data)
+    idx.train(training_sample=8000, max_iterations=5, seed=9)
+    cfg = S.IvfPqConfig(idx.nlist, m)
+    img = S.save_ivfpq(idx, cfg)
+    cent, books, list_of, codes = idx.parts()
+    rep = {f: idx.report[f] for f in ("sampled", "coarse_inertia", "coarse_iterations", "residual_inertia",
+                                      "populated_lists", "largest_list")}
+    want = pxo.snapshot_encode_ivfpq(dim, pxo.EUCLIDEAN, vars(cfg), list(range(n)), [{}] * n, data, codes, list_of,
+                                     cent, books, rep)
+    assert img == want
+    idx2, _ = S.load_ivfpq(bytes(img))
+    for a, b in zip(idx.parts(), idx2.parts()):
+        assert np.array_equal(a, b)
+    q = fixtures.blobs_f32(100, dim, 64, 5, 7)
+    for x, y in zip(idx.search_batch(q, 10, 8, 100), idx2.search_batch(q, 10, 8, 100)):
+        assert np.array_equal(x, y)
+    idx.close()
+    idx2.close()
