@@ -218,6 +218,45 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_kernel(const ScanParams p) 
   const uint32_t* offs = woff + m;
   // table over a vector v (in shared memory): squared (or dot) per entry
   auto build_table = [&](const float* v, bool dot) {
+    if (dim == 8 * m && (m & 3) == 0) {
+      // every subspace 8 wide (C4's layout): four subspaces at a time, four
+      // independent chains per thread; each entry keeps its own sequential order
+      for (uint32_t s = 0; s < m; s += 4) {
+        float4 c[4][2];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4* cb = reinterpret_cast<const float4*>(p.codebooks + 256u * (8u * (s + i)) + t * 8u);
+          c[i][0] = __ldg(cb);
+          c[i][1] = __ldg(cb + 1);
+        }
+        float4 xv[4][2];  // the vector's 32 components of these subspaces (broadcast reads)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          xv[i][0] = reinterpret_cast<const float4*>(v + 8u * (s + i))[0];
+          xv[i][1] = reinterpret_cast<const float4*>(v + 8u * (s + i))[1];
+        }
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (uint32_t j = 0; j < 8; ++j) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float4 h = c[i][j >> 2];
+            const float cj = (j & 3) == 0 ? h.x : (j & 3) == 1 ? h.y : (j & 3) == 2 ? h.z : h.w;
+            const float4 g = xv[i][j >> 2];
+            const float x = (j & 3) == 0 ? g.x : (j & 3) == 1 ? g.y : (j & 3) == 2 ? g.z : g.w;
+            if (dot) {
+              acc[i] = __fadd_rn(acc[i], __fmul_rn(x, cj));
+            } else {
+              const float d = __fsub_rn(x, cj);
+              acc[i] = __fadd_rn(acc[i], __fmul_rn(d, d));
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) lut[(s + i) * 256 + t] = acc[i];
+      }
+      return;
+    }
     for (uint32_t s = 0; s < m; ++s) {
       const uint32_t w = widths[s], o = offs[s];
       const float* cb = p.codebooks + 256u * o + t * w;
