@@ -371,3 +371,22 @@ def test_c2_many_query_tiles_match_brute_force():
             assert dist[i].tolist() == [float(v) for v, _ in order], f"query {i}: distances"
     finally:
         N.load().pxc_flat_destroy(h)
+
+
+def test_c1_reproduces_the_reference_transcript():
+    """The reference's README prints the quickstart's run (README.md, "60-second
+    quickstart"): the filtered search of the first query (lang == "en", k = 10)
+    answers "10 hits, nearest 0 at 0.0000". The exact flat index over the same
+    5,000 vectors and metadata (every third id "en") must print the same line;
+    this pins C1 to output of the reference itself, not to the oracle."""
+    from proxima_b200.filters import MetadataFilter
+    from proxima_b200.index import FlatIndex
+    data = fixtures.quickstart()
+    idx = FlatIndex(VectorSpace(64, Metric.COSINE), capacity=5000)
+    for i in range(5000):
+        idx.insert(i, data[i], {"lang": "en" if i % 3 == 0 else "fr"})
+    hits = idx.search(data[0], 10, MetadataFilter.parse({"lang": "en"}))
+    line = f"{len(hits)} hits, nearest {hits[0].id} at {hits[0].distance:.4f}"
+    assert line == "10 hits, nearest 0 at 0.0000"
+    assert all(h.id % 3 == 0 for h in hits)
+    idx.close()
