@@ -11,11 +11,16 @@ constexpr uint32_t SENTINEL = 0xFFFFFFFFu;  // excluded candidate (filtered / pa
 
 // Block radix-select: the K-th smallest (1-based) of buf[0, cnt), then keeps
 // exactly the K keys <= it at the front (in no particular order). Keys are
-// unique. Returns the K-th. PER >= ceil(cnt / blockDim.x); hist: 256 words of
-// shared memory, sh: 4.
+// unique. Returns the K-th. hist: 256 words of shared memory, sh: 4.
+// Passes of 8 bits from the top; the passes stop as soon as the bin holding
+// the K-th is kept whole (then every key of that bin and below is kept, and
+// no lower bits need resolving). The kept keys are compacted in place in
+// rounds of blockDim keys: each round reads its keys, then writes them down
+// to positions no later than any key still unread.
 template <uint32_t PER>
 __device__ uint64_t select_keep(uint64_t* buf, uint32_t cnt, uint32_t K, uint32_t* hist, uint32_t* sh) {
-  uint64_t prefix = 0, mask = 0;
+  __shared__ unsigned long long s_kmax;
+  uint64_t prefix = 0, mask = 0, thr = ~0ull;
   uint32_t k = K;
   for (int shift = 56; shift >= 0; shift -= 8) {
     for (uint32_t b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
@@ -45,6 +50,7 @@ __device__ uint64_t select_keep(uint64_t* buf, uint32_t cnt, uint32_t K, uint32_
           if (acc + c[j] >= k) {
             sh[0] = lane * 8 + j;
             sh[1] = k - acc;
+            sh[3] = c[j];
             break;
           }
           acc += c[j];
@@ -52,22 +58,43 @@ __device__ uint64_t select_keep(uint64_t* buf, uint32_t cnt, uint32_t K, uint32_
       }
     }
     __syncthreads();
-    prefix |= (uint64_t)sh[0] << shift;
+    const uint32_t bin = sh[0], kr = sh[1], whole = sh[3];
+    prefix |= (uint64_t)bin << shift;
     mask |= 0xFFull << shift;
-    k = sh[1];
+    k = kr;
     __syncthreads();
+    if (whole == kr) {  // the K-th is the largest key of its bin: keep the bin whole
+      thr = shift == 0 ? prefix : (prefix | ((1ull << shift) - 1ull));
+      break;
+    }
   }
-  // keep the keys <= prefix (exactly K of them)
-  uint64_t mine[PER];
-  uint32_t nmine = 0;
-  for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x)
-    if (buf[i] <= prefix) mine[nmine++] = buf[i];
-  if (threadIdx.x == 0) sh[2] = 0;
+  if (threadIdx.x == 0) s_kmax = 0;
+  uint32_t written = 0;
+  const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5, nwarps = (blockDim.x + 31) >> 5;
+  unsigned long long kmax = 0;
+  for (uint32_t base = 0; base < cnt; base += blockDim.x) {
+    const uint32_t i = base + threadIdx.x;
+    const uint64_t key = i < cnt ? buf[i] : ~0ull;
+    const bool keep = i < cnt && key <= thr;
+    const uint32_t ball = __ballot_sync(0xFFFFFFFFu, keep);
+    if (lane == 0) hist[warp] = __popc(ball);
+    __syncthreads();  // every key of this round has been read
+    uint32_t pos = written + __popc(ball & ((1u << lane) - 1u)), total = 0;
+    for (uint32_t w = 0; w < nwarps; ++w) {
+      const uint32_t cw = hist[w];
+      pos += w < warp ? cw : 0u;
+      total += cw;
+    }
+    if (keep) {
+      buf[pos] = key;
+      kmax = max(kmax, (unsigned long long)key);
+    }
+    written += total;
+    __syncthreads();  // the counts are read before the next round writes them
+  }
+  atomicMax(&s_kmax, kmax);
   __syncthreads();
-  const uint32_t base = atomicAdd(&sh[2], nmine);
-  for (uint32_t j = 0; j < nmine; ++j) buf[base + j] = mine[j];
-  __syncthreads();
-  return prefix;
+  return s_kmax;
 }
 
 
