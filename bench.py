@@ -360,6 +360,9 @@ def run_kmeans(args):
 
 
 IVF_METRIC = "queries/s: IVF-PQ 20M×128 nlist=16384 m=16 k=10 @recall@10≥0.9 (IvfPqIndex::search_with_nprobe)"
+# the operating points swept; the line reports the fastest with recall@10 >= 0.9
+IVF_NPROBES = (16, 32, 48, 64, 96)
+IVF_RERANKS = (0, 300, 1000, 2000, 3000, 4000)
 
 
 def run_ivfpq(args):
@@ -458,8 +461,8 @@ def run_ivfpq(args):
         list_recall[nprobe] = round(hit.float().mean().item(), 4)
     del cd, cent_t, list_of_t
     sweep = []
-    for nprobe in (16, 32, 64):
-        for rerank in (0, 300, 1000, 4000):
+    for nprobe in IVF_NPROBES:
+        for rerank in IVF_RERANKS:
             ms = timed(nprobe, rerank, 3)
             rc = recall(ids.cpu().numpy().view(np.uint64))
             sweep.append({"nprobe": nprobe, "rerank": rerank, "recall@10": round(rc, 4), "ms": round(ms, 3),
@@ -639,8 +642,8 @@ def run_ivfpq_sharded(args):
         return t.item()
 
     sweep = []
-    for nprobe in (16, 32, 64):
-        for rerank in (0, 1000, 4000):
+    for nprobe in IVF_NPROBES:
+        for rerank in IVF_RERANKS:
             ms = timed(nprobe, rerank, 3)
             rc = recall(ids.cpu().numpy().view(np.uint64))
             sweep.append({"nprobe": nprobe, "rerank": rerank, "recall@10": round(rc, 4), "ms": round(ms, 3),
