@@ -1276,14 +1276,21 @@ def main():
     sp = stream.cuda_stream
     q_host = torch.from_numpy(queries).pin_memory()
     q_dev = q_host.to(dev)
-    ids = torch.empty((nq, k), dtype=torch.int64, device=dev)
-    dists = torch.empty((nq, k), dtype=torch.float32, device=dev)
-    lens = torch.empty(nq, dtype=torch.int32, device=dev)
+    # weak scaling: each rank owns its slice of the batch and receives only that slice's candidates
+    own_b, own_n = C.c_uint32(0), C.c_uint32(nq)
+    if weak:
+        lib.pxc_ctx_owned_range(ctx.handle, nq, C.byref(own_b), C.byref(own_n))
+    own_b, own_n = own_b.value, own_n.value
+    ids = torch.empty((own_n, k), dtype=torch.int64, device=dev)
+    dists = torch.empty((own_n, k), dtype=torch.float32, device=dev)
+    lens = torch.empty(own_n, dtype=torch.int32, device=dev)
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MiB > 126 MB L2
-    entry = "pxc_flat_search_sharded" if world > 1 else "pxc_flat_search_device"
+    entry = ("pxc_flat_search_sharded_owned" if weak else "pxc_flat_search_sharded") if world > 1 \
+        else "pxc_flat_search_device"
 
     def step(q_ptr):
-        # N > 1: local search, one packed NCCL allgather, merge (inside the library)
+        # N > 1: local search, then the candidate exchange and merge inside the library (weak: to each query's
+        # owner, grouped NCCL sends; strong: one packed allgather to every rank)
         N.call(entry, h, q_ptr, nq, k, None, ids.data_ptr(), dists.data_ptr(), lens.data_ptr(), sp)
 
     N.call("pxc_ctx_set_profiling", ctx.handle, 1)
@@ -1327,11 +1334,11 @@ def main():
     res_d = dists.cpu().numpy()
 
     # ---- e2e: host buffers in, host results out, every step ----
-    out_ids = torch.empty((nq, k), dtype=torch.int64).pin_memory()
-    out_d = torch.empty((nq, k), dtype=torch.float32).pin_memory()
-    out_l = torch.empty(nq, dtype=torch.int32).pin_memory()
+    out_ids = torch.empty((own_n, k), dtype=torch.int64).pin_memory()
+    out_d = torch.empty((own_n, k), dtype=torch.float32).pin_memory()
+    out_l = torch.empty(own_n, dtype=torch.int32).pin_memory()
     h2d = nq * dim * 4
-    d2h = nq * k * 12 + nq * 4
+    d2h = own_n * k * 12 + own_n * 4
     e2e_steps = max(3, min(args.steps, 50))
 
     def e2e_step():
@@ -1407,10 +1414,12 @@ def main():
             "data": "synthetic",
             "config": dict(CONFIG, workload=workload, n=n, queries=nq, k=k, metric=args.metric, rows=args.data,
                            l2="flushed (256 MiB write) between timed steps",
-                           parallelism=(f"row shards x{world}; the library's NCCL communicator: one packed "
-                                        f"allgather of k candidates per query, device merge"
-                                        + (f"; {args.nq:,} queries per GPU per step, so each GPU scans "
-                                           f"{args.nq:,} x {n:,} query-row pairs as on one GPU" if weak else ""))
+                           parallelism=(f"row shards x{world}; the library's NCCL communicator: "
+                                        + (f"each rank owns {args.nq:,} queries of the batch and receives only "
+                                           f"their k candidates from every rank (grouped sends), device merge; "
+                                           f"each GPU scans {nq:,} queries x {n // world:,} rows = "
+                                           f"{args.nq:,} x {n:,} query-row pairs as on one GPU" if weak else
+                                           "one packed allgather of k candidates per query, device merge"))
                            if world > 1 else "single GPU",
                            scan_path=scan_path, unproven_queries_rescanned=redone),
             "clocks": clocks, "gpu_launches": int(launches),
@@ -1423,8 +1432,8 @@ def main():
         from oracle import pxo
 
         full = space.prepare_batch(flat_rows(args, 0, n))
-        samp = np.linspace(0, nq - 1, num=min(args.parity_queries, nq)).astype(np.int64)
-        ri, rd, rl = pxo.flat_search(full, queries[samp], k, int(metric))
+        samp = np.linspace(0, own_n - 1, num=min(args.parity_queries, own_n)).astype(np.int64)  # rank 0's slice
+        ri, rd, rl = pxo.flat_search(full, queries[own_b + samp], k, int(metric))
         same = sum(int(np.array_equal(res_ids[q, :rl[i]], ri[i, :rl[i]]) and
                        np.array_equal(res_d[q, :rl[i]].view(np.uint32), rd[i, :rl[i]].view(np.uint32)))
                    for i, q in enumerate(samp))

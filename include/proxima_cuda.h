@@ -505,6 +505,19 @@ pxc_status pxc_ivfpq_search_device(pxc_ivfpq* h, const float* d_queries, uint32_
                                    uint64_t* d_out_ids, float* d_out_dist, uint32_t* d_out_len,
                                    void* stream, pxc_error* err);
 
+/* The owner-computes form of pxc_flat_search_sharded, for batches whose
+ * queries each belong to one rank: every rank searches all nq DEVICE queries
+ * on its shard, then each rank receives from every rank only the candidates of
+ * its own query slice [nq*rank/nranks, nq*(rank+1)/nranks) (grouped NCCL sends
+ * and receives, k candidates per query) and merges them; the outputs hold that
+ * slice's results (pxc_ctx_owned_range gives its bounds). Every rank calls it
+ * with the same nq and queries; returns after the exchange has finished. */
+pxc_status pxc_flat_search_sharded_owned(pxc_flat* h, const float* d_queries, uint32_t nq, uint32_t k,
+                                         const uint64_t* d_bitmap, uint64_t* d_out_ids, float* d_out_dist,
+                                         uint32_t* d_out_len, void* stream, pxc_error* err);
+/* The slice [*begin, *begin + *count) of nq queries this context's rank owns. */
+void pxc_ctx_owned_range(const pxc_ctx* ctx, uint32_t nq, uint32_t* begin, uint32_t* count);
+
 /* search_with_nprobe over an index whose rows are sharded across the ranks of
  * the context's communicator: every rank holds the same parts (centroids,
  * codebooks) and the lists of its own rows (global VectorIds as ids), probes

@@ -211,6 +211,9 @@ SIGNATURES: dict[str, tuple] = {
     "pxc_ivfpq_get_parts": (C.c_int32, [vp, vp, vp, vp, vp, C.POINTER(C.c_uint32), C.POINTER(PxcError)]),
     "pxc_ivfpq_search": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, vp, vp, vp, vp,
                                      C.POINTER(PxcError)]),
+    "pxc_flat_search_sharded_owned": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, vp, vp, vp, vp, vp,
+                                                  C.POINTER(PxcError)]),
+    "pxc_ctx_owned_range": (None, [vp, C.c_uint32, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]),
     "pxc_ivfpq_search_sharded": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, vp, vp,
                                              vp, vp, vp, C.POINTER(PxcError)]),
     "pxc_ivfpq_search_device": (C.c_int32, [vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, vp, vp,

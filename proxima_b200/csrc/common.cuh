@@ -229,6 +229,10 @@ void exchange_and_merge(pxc_ctx* ctx, const unsigned char* send, uint32_t nq, ui
                         uint64_t* d_out_ids, float* d_out_dist, uint32_t* d_out_len, cudaStream_t s);
 // The context's send buffer, grown to at least `bytes` (callers hold comm_mu).
 unsigned char* exchange_send_buffer(pxc_ctx* ctx, size_t bytes);
+uint32_t owner_begin(uint32_t nq, uint32_t nranks, uint32_t j);
+void exchange_to_owners(pxc_ctx* ctx, const uint64_t* ids, const float* dist, const uint32_t* lens, uint32_t nq,
+                        uint32_t k_in, uint32_t k, uint64_t* d_out_ids, float* d_out_dist, uint32_t* d_out_len,
+                        cudaStream_t s);
 // ncclAllGather of `bytes` per rank over the context's communicator (recv:
 // nranks * bytes, rank order), then the bounded wait of the exchange. With one
 // rank, a device copy. Callers hold comm_mu.

@@ -28,6 +28,10 @@ struct NcclApi {
   ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                              cudaStream_t) = nullptr;
+  ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*group_start)() = nullptr;
+  ncclResult_t (*group_end)() = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
 };
 
@@ -51,6 +55,10 @@ static NcclApi load_nccl() {
   a.comm_async_error = reinterpret_cast<decltype(a.comm_async_error)>(sym("ncclCommGetAsyncError"));
   a.all_gather = reinterpret_cast<decltype(a.all_gather)>(sym("ncclAllGather"));
   a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(sym("ncclAllReduce"));
+  a.send = reinterpret_cast<decltype(a.send)>(sym("ncclSend"));
+  a.recv = reinterpret_cast<decltype(a.recv)>(sym("ncclRecv"));
+  a.group_start = reinterpret_cast<decltype(a.group_start)>(sym("ncclGroupStart"));
+  a.group_end = reinterpret_cast<decltype(a.group_end)>(sym("ncclGroupEnd"));
   a.error_string = reinterpret_cast<decltype(a.error_string)>(sym("ncclGetErrorString"));
   a.ok = a.why.empty();
   return a;
@@ -288,6 +296,58 @@ void exchange_and_merge(pxc_ctx* ctx, const unsigned char* send, uint32_t nq, ui
   wait_comm(ctx, s, "candidate exchange");
 }
 
+// Queries [owner_begin(j), owner_begin(j+1)) belong to rank j: an even split.
+uint32_t owner_begin(uint32_t nq, uint32_t nranks, uint32_t j) {
+  return (uint32_t)(((uint64_t)nq * j) / nranks);
+}
+
+// The owner-computes exchange: every rank holds its k_in candidates for all nq
+// queries (ids, dist, lens as one search writes them); each rank sends every
+// owner only the owner's query slice (three grouped sends per peer) and
+// merges the ranks' lists of its own slice.
+void exchange_to_owners(pxc_ctx* ctx, const uint64_t* ids, const float* dist, const uint32_t* lens, uint32_t nq,
+                        uint32_t k_in, uint32_t k, uint64_t* d_out_ids, float* d_out_dist, uint32_t* d_out_len,
+                        cudaStream_t s) {
+  const uint32_t nranks = (uint32_t)ctx->nranks, me = (uint32_t)ctx->rank;
+  const uint32_t q0 = owner_begin(nq, nranks, me), nmine = owner_begin(nq, nranks, me + 1) - q0;
+  const size_t seg = exchange_segment_bytes(nmine, k_in);
+  if ((size_t)nranks * seg > ctx->x_recv_bytes) {
+    if (ctx->x_recv) cudaFree(ctx->x_recv);
+    ctx->x_recv = nullptr;
+    ctx->x_recv_bytes = 0;
+    PXC_CUDA(cudaMalloc(&ctx->x_recv, (size_t)nranks * seg));
+    ctx->x_recv_bytes = (size_t)nranks * seg;
+  }
+  unsigned char* all = ctx->x_recv;
+  const size_t id_off = 0, d_off = (size_t)nmine * k_in * 8, l_off = (size_t)nmine * k_in * 12;
+  ncclComm_t comm = static_cast<ncclComm_t>(ctx->comm);
+  PXC_NCCL(nccl().group_start());
+  for (uint32_t j = 0; j < nranks; ++j) {
+    const uint32_t b = owner_begin(nq, nranks, j), n = owner_begin(nq, nranks, j + 1) - b;
+    if (n) {
+      PXC_NCCL(nccl().send(ids + (size_t)b * k_in, (size_t)n * k_in * 8, ncclUint8, (int)j, comm, s));
+      PXC_NCCL(nccl().send(dist + (size_t)b * k_in, (size_t)n * k_in * 4, ncclUint8, (int)j, comm, s));
+      PXC_NCCL(nccl().send(lens + b, (size_t)n * 4, ncclUint8, (int)j, comm, s));
+    }
+    if (nmine) {
+      unsigned char* r = all + (size_t)j * seg;
+      PXC_NCCL(nccl().recv(r + id_off, (size_t)nmine * k_in * 8, ncclUint8, (int)j, comm, s));
+      PXC_NCCL(nccl().recv(r + d_off, (size_t)nmine * k_in * 4, ncclUint8, (int)j, comm, s));
+      PXC_NCCL(nccl().recv(r + l_off, (size_t)nmine * 4, ncclUint8, (int)j, comm, s));
+    }
+  }
+  PXC_NCCL(nccl().group_end());
+  if (nmine) {
+    merge_sorted_kernel<<<(nmine + 3) / 4, 128, 0, s>>>(
+        reinterpret_cast<const uint64_t*>(all + id_off), reinterpret_cast<const float*>(all + d_off),
+        reinterpret_cast<const uint32_t*>(all + l_off), nranks, nmine, k_in, k, seg / 8, seg / 4, seg / 4, d_out_ids,
+        d_out_dist, d_out_len);
+    PXC_CUDA(cudaGetLastError());
+    ctx->launches += 1;
+  }
+  wait_comm(ctx, s, "candidate exchange to owners");
+}
+
 }  // namespace pxc
 
 using namespace pxc;
@@ -421,6 +481,12 @@ pxc_status pxc_ctx_init_comm(pxc_ctx* ctx, const uint8_t id[128], int32_t nranks
 }
 
 int32_t pxc_ctx_comm_size(const pxc_ctx* ctx) { return ctx ? ctx->nranks : 0; }
+void pxc_ctx_owned_range(const pxc_ctx* ctx, uint32_t nq, uint32_t* begin, uint32_t* count) {
+  const uint32_t nranks = ctx && ctx->nranks > 0 ? (uint32_t)ctx->nranks : 1, me = ctx ? (uint32_t)ctx->rank : 0;
+  const uint32_t b = owner_begin(nq, nranks, me);
+  if (begin) *begin = b;
+  if (count) *count = owner_begin(nq, nranks, me + 1) - b;
+}
 int32_t pxc_ctx_comm_rank(const pxc_ctx* ctx) { return ctx ? ctx->rank : -1; }
 
 pxc_status pxc_topk_exchange(pxc_ctx* ctx, const uint64_t* d_ids, const float* d_dist, const uint32_t* d_lens,

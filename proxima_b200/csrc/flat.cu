@@ -1564,6 +1564,36 @@ pxc_status pxc_flat_search_sharded(pxc_flat* h, const float* d_queries, uint32_t
   });
 }
 
+pxc_status pxc_flat_search_sharded_owned(pxc_flat* h, const float* d_queries, uint32_t nq, uint32_t k,
+                                         const uint64_t* d_bitmap, uint64_t* d_out_ids, float* d_out_dist,
+                                         uint32_t* d_out_len, void* stream, pxc_error* err) {
+  return guarded(err, [&] {
+    PXC_CONFIG(h != nullptr, "handle", 0, "null flat handle");
+    PXC_CONFIG(k <= PXC_MAX_K, "k", k, "exceeds the 16777216 result ceiling");
+    pxc_ctx* ctx = h->ctx;
+    PXC_CONFIG((uint64_t)ctx->nranks * k <= 8192, "nranks*k", (uint64_t)ctx->nranks * k,
+               "the merge holds at most 8192 candidates per query");
+    if (nq == 0) return;
+    std::lock_guard<std::mutex> lock(h->mu);
+    DeviceGuard g(ctx->device);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    std::lock_guard<std::mutex> comm_lock(ctx->comm_mu);
+    handoff_wait(h, s);
+    if (ctx->nranks <= 1 || ctx->comm == nullptr) {  // one rank owns every query
+      search_device(h, d_queries, nq, k, d_bitmap, d_out_ids, d_out_dist, d_out_len, s);
+    } else {
+      unsigned char* send = exchange_send_buffer(ctx, exchange_segment_bytes(nq, k));
+      const size_t n = (size_t)nq * k;
+      uint64_t* ids = reinterpret_cast<uint64_t*>(send);
+      float* dist = reinterpret_cast<float*>(send + n * 8);
+      uint32_t* lens = reinterpret_cast<uint32_t*>(send + n * 12);
+      search_device(h, d_queries, nq, k, d_bitmap, ids, dist, lens, s);
+      exchange_to_owners(ctx, ids, dist, lens, nq, k, k, d_out_ids, d_out_dist, d_out_len, s);
+    }
+    handoff_done(h, s);
+  });
+}
+
 }  // extern "C"
 
 namespace {

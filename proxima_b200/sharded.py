@@ -102,6 +102,19 @@ class ShardedFlat:
                m_d.data_ptr(), m_l.data_ptr(), stream_ptr)
         return m_ids, m_d, m_l
 
+    def search_owned(self, q_dev: torch.Tensor, k: int, stream_ptr: int):
+        """Local search of every query, then each rank receives only the candidates of its own
+        query slice (pxc_flat_search_sharded_owned): returns (begin, ids, dist, lens) of that slice."""
+        nq = q_dev.shape[0]
+        b, n = C.c_uint32(), C.c_uint32()
+        self.lib.pxc_ctx_owned_range(self.ctx.handle, nq, C.byref(b), C.byref(n))
+        m_ids = torch.empty((max(n.value, 1), k), dtype=torch.int64, device=q_dev.device)
+        m_d = torch.empty((max(n.value, 1), k), dtype=torch.float32, device=q_dev.device)
+        m_l = torch.empty(max(n.value, 1), dtype=torch.int32, device=q_dev.device)
+        N.call("pxc_flat_search_sharded_owned", self.handle, q_dev.data_ptr(), nq, k, None, m_ids.data_ptr(),
+               m_d.data_ptr(), m_l.data_ptr(), stream_ptr)
+        return b.value, m_ids[:n.value], m_d[:n.value], m_l[:n.value]
+
     def close(self):
         if self.handle:
             self.lib.pxc_flat_destroy(self.handle)

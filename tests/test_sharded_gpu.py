@@ -66,6 +66,7 @@ def test_single_rank_communicator_and_exchange():
     got = _sharded_search("pxc_flat_search_sharded", h, ctx, q, 10)
     ref = pxo.flat_search(db, qh, 10, pxo.EUCLIDEAN, ids=ids)
     _same(got, ref, "sharded, one rank")
+    _same(_sharded_search("pxc_flat_search_sharded_owned", h, ctx, q, 10), ref, "owned, one rank")
     # the generic exchange of given lists (k_in = 10 -> k = 7)
     li = torch.from_numpy(got[0].view(np.int64)).cuda()
     ld = torch.from_numpy(got[1]).cuda()
@@ -114,10 +115,20 @@ def _rank(rank, world, port, out):
             lo, hi = shard_range(len(data), rank, world)
             sh = ShardedFlat(ctx, 96, int(metric), data[lo:hi], lo)
             got = sh.search_global(torch.from_numpy(qh).cuda(), 10, torch.cuda.current_stream().cuda_stream)
+            # the owner-computes exchange: this rank's slice of the same batch
+            b, oi, od, ol = sh.search_owned(torch.from_numpy(qh).cuda(), 10, torch.cuda.current_stream().cuda_stream)
             torch.cuda.synchronize()
             sh.close()
+            ri, rd, rl = pxo.flat_search(data, qh, 10, int(metric))
+            n = oi.shape[0]
+            own_ok = bool(n == (len(qh) * (rank + 1)) // world - b and b == (len(qh) * rank) // world and
+                          np.array_equal(ol.cpu().numpy().view(np.uint32), rl[b:b + n]) and
+                          np.array_equal(oi.cpu().numpy().view(np.uint64), ri[b:b + n]) and
+                          np.array_equal(od.cpu().numpy().view(np.uint32), rd[b:b + n].view(np.uint32)))
+            flag = torch.tensor([1 if own_ok else 0], dtype=torch.int32, device="cuda")
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+            results[label + " owned"] = bool(flag.item() == 1)
             if rank == 0:
-                ri, rd, rl = pxo.flat_search(data, qh, 10, int(metric))
                 gi = got[0].cpu().numpy().view(np.uint64)
                 gd = got[1].cpu().numpy()
                 gl = got[2].cpu().numpy().view(np.uint32)
@@ -146,7 +157,7 @@ def test_two_rank_sharded_flat_equals_unsharded():
         p.join(240)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     res = q.get(timeout=10)
-    assert res == {"u8": True, "real cosine": True}, res
+    assert res == {"u8": True, "real cosine": True, "u8 owned": True, "real cosine owned": True}, res
 
 
 def _merge_by_total_order(parts, k):
