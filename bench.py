@@ -1390,8 +1390,10 @@ def main():
                                       "and this kernel source (profiles/flat_u8_kernel_c2.md)"
         elif t:
             traffic_src = "not reported: the K1 source changed since the ncu capture in profiles/traffic.json"
-    kernel = {1: "flat_scan_kernel<KT, U8Scan> (K1)", 2: "flat_scan_kernel<32, F16Scan> (K2 screen)"}.get(
-        path, "dist_chunk_kernel + select (K1g)")
+    kernel = {1: ("flat_scan_kernel<KT, U8Scan> (K1)" if k <= 32 else
+                  "K1 sample pass (flat_scan_kernel<16, U8Scan>, own lists) + K1 collect launch "
+                  "(flat_scan_kernel<1, U8Scan, collect>) + candidate merge, timed together"),
+              2: "flat_scan_kernel<32, F16Scan> (K2 screen)"}.get(path, "dist_chunk_kernel + select (K1g)")
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak,
                 "unit": "TOPS" if path == 1 else "TFLOP/s",
                 "frac": (achieved / peak) if (achieved and peak) else None, "traffic": traffic,
@@ -1402,7 +1404,10 @@ def main():
     data_desc = ("integers in [0,255], 1,024 blobs, sigma 20" if args.data == "u8"
                  else "real-valued: the same 1,024 blobs, sigma 20, unrounded")
     workload = (f"C2 exact flat search: {n:,} x {dim} f32 ({data_desc}), {nq:,} queries, k={k}, {args.metric}")
-    scan_path = {1: ("tensor-core u8 (exact)" if k <= 32 else "tensor-core u8 over row groups, merged and proven exact"),
+    scan_path = {1: ("tensor-core u8 (exact)" if k <= 32 else
+                     "tensor-core u8: a sample pass bounds each query's k-th distance, one collect launch keeps "
+                     "every row within the bound, exact top k of those (queries whose candidates overflow: "
+                     "row groups, merged and proven exact)"),
                  2: "tensor-core f16 screen of 32 per query, exact f32 re-rank, proven per query"}.get(
         path, "fp32 reference order")
     line = {"metric": METRIC.replace("k=10", f"k={k}").replace("euclidean", args.metric) +

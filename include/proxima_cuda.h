@@ -100,8 +100,13 @@ pxc_status pxc_ctx_set_profiling(pxc_ctx* ctx, int32_t on, pxc_error* err);
  * buffers so that its exact fallback runs; "sq_spec_rank" (>= 1) forces the SQ
  * speculative admission rank; "kmeans_exact" (0/1) assigns k-means points
  * without the tensor-core screen; "kmeans_trace" (0/1) prints per-iteration
- * counters to stderr. A negative cap or rank restores the default. Unknown
- * names are PXC_CONFIGURATION. */
+ * counters to stderr; "flat_group_sample" (n >= 1) fixes the share 1/n of
+ * the rows that the flat search at 32 < k <= 128 samples for its admission
+ * bound (default, or negative: 800 / k), 0 skips the sample pass; "flat_collect_cap"
+ * (default 2048, rounded up to a power of two in [32, 2048]) sets the
+ * per-query candidate slots of that search's single collect launch, 0 runs
+ * the group launches instead. A negative SQ cap or rank restores the default.
+ * Unknown names are PXC_CONFIGURATION. */
 pxc_status pxc_ctx_set_option(pxc_ctx* ctx, const char* name, int64_t value, pxc_error* err);
 
 /* ---- FlatIndex: exact filtered top-k ----
@@ -163,11 +168,13 @@ int32_t pxc_flat_path(const pxc_flat* h);
 /* Duration of the last search's scan kernel (K1 or K1g), with profiling on;
  * -1 when not recorded. */
 float pxc_flat_last_scan_ms(pxc_flat* h);
-/* Queries of the last search that a tensor-core path could not prove exact
- * and that were searched again on the fp32 scan: with 32 < k <= 128 on the u8
- * path, those with 32 or more of their top k in one row group; on the f16
- * screen, those whose candidates' k-th exact distance was not provably ahead
- * of every row the screen left out; 0 otherwise. */
+/* Queries of the last search that the first tensor-core pass did not settle
+ * and that were answered again: with 32 < k <= 128 on the u8 path, those
+ * whose collect-launch candidates overflowed (answered by the row-group
+ * launches) plus those the row-group proof could not settle (32 or more of
+ * their top k in one group; answered by the fp32 scan); on the f16 screen,
+ * those whose candidates' k-th exact distance was not provably ahead of every
+ * row the screen left out (fp32 scan); 0 otherwise. */
 uint32_t pxc_flat_last_redone(const pxc_flat* h);
 
 /* Allocation-free variant of pxc_flat_search_device. No counterpart in the

@@ -137,11 +137,13 @@ struct pxc_ctx {
   bool profiling = false;
   unsigned long long launches = 0;  // kernels launched by this library on this context
   std::mutex mu;  // serialises use of the context stream and d_status (k-means, SQ)
-  // Diagnostic knobs set through pxc_ctx_set_option (tests only; all off by default).
+  // Diagnostic knobs set through pxc_ctx_set_option (tests only; defaults below).
   int64_t opt_sq_candidate_cap = -1;  // >= 0: shrink the SQ threshold-pass buffers (forces the fallback)
   int64_t opt_sq_spec_rank = -1;      // >= 1: force the SQ speculative admission rank
   bool opt_kmeans_exact = false;      // k-means assignment without the tensor-core screen
   bool opt_kmeans_trace = false;      // k-means prints per-iteration counters to stderr
+  int64_t opt_flat_group_sample = -1;  // grouped K1: 1/n of the rows sampled for the bound (-1: 800/k, 0: none)
+  int64_t opt_flat_collect_cap = 2048;  // grouped K1: collect-mode slots per query (0: the group launches)
   // k-means scratch kept between calls (grown on demand, freed with the context)
   void* kmeans_ws = nullptr;
   void (*kmeans_ws_free)(void*) = nullptr;

@@ -432,6 +432,13 @@ pxc_status pxc_ctx_set_option(pxc_ctx* ctx, const char* name, int64_t value, pxc
       ctx->opt_kmeans_exact = value != 0;
     } else if (std::strcmp(name, "kmeans_trace") == 0) {
       ctx->opt_kmeans_trace = value != 0;
+    } else if (std::strcmp(name, "flat_group_sample") == 0) {
+      ctx->opt_flat_group_sample = value < 0 ? -1 : value;
+    } else if (std::strcmp(name, "flat_collect_cap") == 0) {
+      // rounded up to a power of two in [32, 2048]; 0 keeps the group launches
+      int64_t cap = 32;
+      while (cap < value && cap < 2048) cap <<= 1;
+      ctx->opt_flat_collect_cap = value <= 0 ? 0 : cap;
     } else {
       throw make_failure(PXC_CONFIGURATION, 0, 0, "name", "unknown diagnostic option '%.64s'", name);
     }

@@ -199,20 +199,51 @@ __global__ void prep_queries_u8_kernel(const float* __restrict__ Q, uint32_t nq,
 // Merge of K1's per-split lists: per query, nsplit*KT packed (r, rank) keys,
 // sort, drop duplicates (a split may carry entries seeded from an earlier
 // split), keep k, distance = r + ||q||^2 (exact integer in f32).
-// Launched with 256 threads per block (one block per query).
+// With counts set (collect mode: per query nsplit unordered segments of KT
+// slots, counts [nq][nsplit]) the filled part of every segment is gathered,
+// at most cap keys (a query with more overflowed and is answered again).
+// Launched with 256 threads per block (one block per query); cap <= 2048, a
+// power of two; nsplit <= MERGE_MAX_SPLITS with counts.
+constexpr uint32_t MERGE_MAX_SPLITS = 64;
 __global__ void __launch_bounds__(256) merge_u8_kernel(const uint64_t* __restrict__ part, uint32_t nsplit, uint32_t KT,
                                 uint32_t cap, uint32_t k, const int32_t* __restrict__ qnorm,
                                 const uint64_t* __restrict__ rank_id, uint32_t nrank,
                                 uint64_t* __restrict__ out_ids, float* __restrict__ out_dist,
-                                uint32_t* __restrict__ out_len) {
+                                uint32_t* __restrict__ out_len, const uint32_t* __restrict__ counts) {
   extern __shared__ uint64_t sl[];
   const uint32_t q = blockIdx.x;
   const uint32_t n = nsplit * KT;
   const uint64_t empty_key = static_cast<uint64_t>(static_cast<uint32_t>(flat_tc::BIG) + flat_tc::R_OFFSET) << 32;
-  for (uint32_t i = threadIdx.x; i < cap; i += blockDim.x) {
-    uint64_t v = i < n ? part[(size_t)q * n + i] : ~0ull;
-    // empty slots, and (defensively) any rank outside the mirror, never reach the output
-    sl[i] = (v >= empty_key || static_cast<uint32_t>(v) >= nrank) ? ~0ull : v;
+  if (counts != nullptr) {
+    __shared__ uint32_t seg_off[MERGE_MAX_SPLITS + 1];
+    if (threadIdx.x == 0) {
+      uint32_t a = 0;
+      for (uint32_t sp = 0; sp < nsplit; ++sp) {
+        seg_off[sp] = a;
+        a += min(counts[(size_t)q * nsplit + sp], KT);
+      }
+      seg_off[nsplit] = a;
+    }
+    __syncthreads();
+    const uint32_t filled = min(seg_off[nsplit], cap);
+    uint32_t sz = 32;  // sort only the filled prefix, rounded up to a power of two (<= cap)
+    while (sz < filled) sz <<= 1;
+    cap = sz;
+    for (uint32_t i = threadIdx.x; i < cap; i += blockDim.x) sl[i] = ~0ull;
+    __syncthreads();
+    for (uint32_t sp = 0; sp < nsplit; ++sp) {
+      const uint32_t b = seg_off[sp], len = seg_off[sp + 1] - b;
+      for (uint32_t j = threadIdx.x; j < len && b + j < cap; j += blockDim.x) {
+        const uint64_t v = part[(size_t)q * n + (size_t)sp * KT + j];
+        sl[b + j] = (v >= empty_key || static_cast<uint32_t>(v) >= nrank) ? ~0ull : v;
+      }
+    }
+  } else {
+    for (uint32_t i = threadIdx.x; i < cap; i += blockDim.x) {
+      uint64_t v = i < n ? part[(size_t)q * n + i] : ~0ull;
+      // empty slots, and (defensively) any rank outside the mirror, never reach the output
+      sl[i] = (v >= empty_key || static_cast<uint32_t>(v) >= nrank) ? ~0ull : v;
+    }
   }
   __syncthreads();
   block_bitonic_sort_u64(sl, cap);
@@ -259,12 +290,15 @@ constexpr uint32_t GROUP_K = 32;
 constexpr uint32_t GROUPED_MAX_K = 128;
 
 // Exactness of a grouped search, per query. Each group list is that group's
-// own top GROUP_K, so every row missing from the union of the lists lies
-// behind the last entry of its group's list. When every full group list ends
-// at or behind the merged k-th entry (by (total_cmp(distance), id)), no missing
-// row can be among the first k and the merged list is the exact answer.
-// Otherwise (32 or more of the query's top k in one group, or fewer than k
-// merged entries while a group list is full) the query is flagged for K1g.
+// own top GROUP_K among its rows with r <= T (the shared starting bound, which
+// at least k rows meet; T is "none" without the sample pass), so every row
+// missing from the union of the lists lies behind the true k-th (r > T) or
+// behind the last entry of its group's full list. When every full group list
+// ends at or behind the merged k-th entry (by (total_cmp(distance), id)), no
+// missing row can be among the first k and the merged list is the exact
+// answer. Otherwise (32 or more of the query's top k in one group, or fewer
+// than k merged entries while a group list is full) the query is flagged for
+// K1g.
 __global__ void group_check_kernel(const uint64_t* __restrict__ gids, const float* __restrict__ gdist,
                                    const uint32_t* __restrict__ glen, uint32_t ngroups, uint32_t nq,
                                    const uint64_t* __restrict__ ids, const float* __restrict__ dist,
@@ -720,6 +754,13 @@ struct pxc_flat {
   DBuf<uint64_t> g_ids, g_redo_ids;
   DBuf<float> g_dist, g_redo_q, g_redo_dist;
   DBuf<uint32_t> g_len, g_redo_idx, g_redo_len;
+  DBuf<uint32_t> g_bound;  // [nq_pad] the sample pass's shared admission bound (packed keys)
+  DBuf<uint64_t> c_cand;   // collect mode: [nq][nsplit][seg] candidate keys
+  DBuf<uint32_t> c_cnt;    // collect mode: [nq][nsplit] candidates found
+  DBuf<uint8_t> c_over;    // collect mode: [nq] the query's segments overflowed
+  DBuf<uint32_t> c_idx, c_n, c_bound, c_len;  // the overflowed queries, gathered
+  DBuf<float> c_q, c_dist;
+  DBuf<uint64_t> c_ids;
   DBuf<uint8_t> g_redo;
   // buffers of the host-pointer entry point, kept across calls
   DBuf<float> io_q;
@@ -894,12 +935,12 @@ uint32_t choose_splits(uint32_t nqt, uint32_t ntiles, int sms, uint32_t KT) {
   return best_s;
 }
 
-template <int KT, class P = flat_tc::U8Scan>
+template <int KT, class P = flat_tc::U8Scan, bool COLLECT = false>
 void launch_tc(const CUtensorMap& tq, const CUtensorMap& tx, const flat_tc::Params& p, dim3 grid,
                size_t smem, cudaStream_t s) {
-  PXC_CUDA(cudaFuncSetAttribute(flat_tc::flat_scan_kernel<KT, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)smem));
-  flat_tc::flat_scan_kernel<KT, P><<<grid, flat_tc::NUM_THREADS, smem, s>>>(tq, tx, p);
+  PXC_CUDA(cudaFuncSetAttribute(flat_tc::flat_scan_kernel<KT, P, COLLECT>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  flat_tc::flat_scan_kernel<KT, P, COLLECT><<<grid, flat_tc::NUM_THREADS, smem, s>>>(tq, tx, p);
 }
 
 // The database side of one K1 search: the full mirror, or the accepted ranks of a filter.
@@ -912,8 +953,11 @@ struct TcOperand {
   const uint8_t* rows;  // [nrank_pad][dp] u8, the memory tmap_x describes
 };
 
+// One K1 search of nq queries over op. init_bound (optional, [nq_pad] packed
+// keys) replaces the "no bound yet" start of the shared admission bound.
 void search_tc(pxc_flat* h, const TcOperand& op, const float* d_q, uint32_t nq, uint32_t k, uint64_t* d_ids,
-               float* d_dist, uint32_t* d_len, cudaStream_t s, bool timed = true) {
+               float* d_dist, uint32_t* d_len, cudaStream_t s, bool timed = true,
+               const uint32_t* init_bound = nullptr) {
   const uint32_t KT = k <= 1 ? 1 : k <= 4 ? 4 : k <= 10 ? 10 : k <= 16 ? 16 : 32;
   const uint32_t nq_pad = (nq + flat_tc::BM - 1) / flat_tc::BM * flat_tc::BM;
   const uint32_t nqt = nq_pad / flat_tc::BM;
@@ -925,7 +969,10 @@ void search_tc(pxc_flat* h, const TcOperand& op, const float* d_q, uint32_t nq, 
   h->bound.reserve(nq_pad);
   h->done.reserve(nqt + (size_t)nqt * nsplit);
   // 0x3F3F3F3F: above every real r (|r| < 2^25) and below the padding sentinel
-  PXC_CUDA(cudaMemsetAsync(h->bound.p, 0x3F, nq_pad * sizeof(int32_t), s));
+  if (init_bound != nullptr)
+    PXC_CUDA(cudaMemcpyAsync(h->bound.p, init_bound, nq_pad * sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
+  else
+    PXC_CUDA(cudaMemsetAsync(h->bound.p, 0x3F, nq_pad * sizeof(int32_t), s));
   PXC_CUDA(cudaMemsetAsync(h->done.p, 0, nqt * sizeof(uint32_t), s));
   PXC_CUDA(cudaMemsetAsync(h->done.p + nqt, 0xFF, (size_t)nqt * nsplit * sizeof(uint32_t), s));
   flat_tc::Params p;
@@ -966,7 +1013,7 @@ void search_tc(pxc_flat* h, const TcOperand& op, const float* d_q, uint32_t nq, 
   if (msmem > 48 * 1024)
     PXC_CUDA(cudaFuncSetAttribute(merge_u8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msmem));
   merge_u8_kernel<<<nq, 256, msmem, s>>>(h->part.p, nsplit, KT, cap, k, h->q_norm.p, op.rank_id, (uint32_t)op.nrank,
-                                         d_ids, d_dist, d_len);
+                                         d_ids, d_dist, d_len, nullptr);
   PXC_CUDA(cudaGetLastError());
 }
 
@@ -1052,14 +1099,212 @@ void search_generic(pxc_flat* h, const float* d_q, uint32_t nq, uint32_t k, cons
 // Groups: ceil(0.08 k), so a group holds 1/12.5 of a query's top k on
 // average and reaching GROUP_K in one group is rare unless rows that are near
 // one another are also near in id order.
-void search_tc_grouped(pxc_flat* h, const TcOperand& op, const float* d_q, uint32_t nq, uint32_t k,
-                       const uint64_t* d_bitmap, uint64_t* d_ids, float* d_dist, uint32_t* d_len, cudaStream_t s) {
-  const uint64_t ntiles = op.nrank_pad / flat_tc::BN;
-  const uint32_t want = std::max<uint32_t>(2, (k * 2 + 24) / 25);
-  if (ntiles < want) {  // too few rows to split: the fp32 scan
-    search_generic(h, d_q, nq, k, d_bitmap, d_ids, d_dist, d_len, s);
+//
+// Every launch below starts from one admission bound T per query instead of
+// "no bound": a sample pass runs one K1 launch for the top SAMPLE_K over
+// about k / SAMPLE_TARGET of the rows, in ns = ceil(2k / SAMPLE_K) runs of
+// tiles spread evenly over the operand (one split each, keeping its own list:
+// Params::share = 0, no seeding, no shared bound), and T is the k-th smallest
+// r of the union of those lists. The
+// splits cover disjoint rows, so at least k distinct rows have r <= T, the
+// true k-th has r <= T, and a row turned away at T (r > T) is behind it. The
+// proof above is unchanged: a group list that is not full holds every row of
+// its group with r <= T.
+constexpr uint32_t SAMPLE_K = 16;
+constexpr uint32_t SAMPLE_TARGET = 800;  // rows of the operand per row of the sample's top k (k x divisor)
+constexpr uint32_t SAMPLE_MAX = 256;  // union entries per query: ns * SAMPLE_K <= 256 for k <= 128
+
+// T per query from the sample launch's lists ([nq_pad][nsplit][SAMPLE_K]
+// packed (r, rank) keys): the k-th smallest r key of the union, or "no bound"
+// (0x3F3F3F3F) when the lists hold fewer than k rows or q >= nq. One block of
+// SAMPLE_MAX threads per query (nq_pad blocks), nsplit * SAMPLE_K <= SAMPLE_MAX.
+__global__ void __launch_bounds__(SAMPLE_MAX) union_kth_kernel(const uint64_t* __restrict__ part, uint32_t nsplit,
+                                                               uint32_t nq, uint32_t k, uint32_t* __restrict__ T) {
+  __shared__ uint32_t key[SAMPLE_MAX];
+  __shared__ uint32_t total;
+  const uint32_t q = blockIdx.x;
+  if (q >= nq) {
+    if (threadIdx.x == 0) T[q] = 0x3F3F3F3Fu;
     return;
   }
+  if (threadIdx.x == 0) total = 0;
+  const uint32_t n = nsplit * SAMPLE_K;
+  const uint32_t empty = flat_tc::U8Scan::pack(flat_tc::BIG);
+  uint32_t v = 0xFFFFFFFFu;
+  if (threadIdx.x < n) {
+    const uint32_t r = static_cast<uint32_t>(part[(size_t)q * n + threadIdx.x] >> 32);
+    if (r < empty) v = r;
+  }
+  key[threadIdx.x] = v;
+  __syncthreads();
+  if (v != 0xFFFFFFFFu) atomicAdd(&total, 1u);
+  for (uint32_t size = 2; size <= SAMPLE_MAX; size <<= 1) {
+    for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+      __syncthreads();
+      const uint32_t i = threadIdx.x, o = i ^ stride;
+      if (o > i) {
+        const uint32_t a = key[i], b = key[o];
+        const bool up = (i & size) == 0;
+        if ((a > b) == up) {
+          key[i] = b;
+          key[o] = a;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) T[q] = total < k ? 0x3F3F3F3Fu : key[k - 1];
+}
+
+// The sample pass: one K1 launch (KT = SAMPLE_K, share = 0) in ns splits of
+// stiles tiles, split i starting at tile i * (ntiles / ns), then
+// union_kth_kernel into T [nq_pad].
+void sample_bound(pxc_flat* h, const TcOperand& op, uint32_t nq, uint32_t k, uint32_t ns, uint32_t stiles,
+                  uint32_t* T, cudaStream_t s) {
+  const uint32_t nq_pad = (nq + flat_tc::BM - 1) / flat_tc::BM * flat_tc::BM;
+  const uint32_t nqt = nq_pad / flat_tc::BM;
+  h->part.reserve((size_t)nq_pad * ns * SAMPLE_K);
+  h->bound.reserve(nq_pad);
+  h->done.reserve(nqt + (size_t)nqt * ns);
+  PXC_CUDA(cudaMemsetAsync(h->bound.p, 0x3F, nq_pad * sizeof(int32_t), s));
+  PXC_CUDA(cudaMemsetAsync(h->done.p, 0, nqt * sizeof(uint32_t), s));
+  PXC_CUDA(cudaMemsetAsync(h->done.p + nqt, 0xFF, (size_t)nqt * ns * sizeof(uint32_t), s));
+  flat_tc::Params p;
+  p.norms = op.norms;
+  p.qcoef = nullptr;
+  p.qdelta = nullptr;
+  p.bound = reinterpret_cast<uint32_t*>(h->bound.p);
+  p.done_count = h->done.p;
+  p.done_list = h->done.p + nqt;
+  p.out_part = h->part.p;
+  p.share = 0;
+  p.status = h->d_status;
+  p.nq = nq;
+  p.k = SAMPLE_K;
+  p.kblocks = h->dp / flat_tc::KB_BYTES;
+  p.ntiles = (uint32_t)(op.nrank_pad / flat_tc::BN);
+  p.tiles_per_split = stiles;  // <= ntiles / ns, so the runs do not overlap
+  p.split_stride = p.ntiles / ns;
+  p.nsplit = ns;
+  p.stages = flat_tc::pick_stages<flat_tc::U8Scan>(p.kblocks);
+  p.wait_ns = (uint64_t)h->ctx->wait_ms * 1000000ull;
+  CUtensorMap tmap_q;
+  make_tmap_u8_2d(&tmap_q, h->q_u8.p, h->dp, nq_pad, flat_tc::KB_BYTES, flat_tc::BM);
+  const size_t smem = flat_tc::smem_bytes<flat_tc::U8Scan>(p.kblocks, p.stages);
+  launch_tc<SAMPLE_K>(tmap_q, *op.tmap_x, p, dim3(nqt, ns), smem, s);
+  PXC_CUDA(cudaGetLastError());
+  union_kth_kernel<<<nq_pad, SAMPLE_MAX, 0, s>>>(h->part.p, ns, nq, k, T);
+  PXC_CUDA(cudaGetLastError());
+  h->ctx->launches += 2;
+}
+
+
+constexpr uint64_t COLLECT_MAX_ENTRIES = 1ull << 26;  // collect-mode candidate slots per search (512 MiB)
+
+// Collect mode (32 < k <= 128 once the sample pass has given T): ONE K1
+// launch over the whole operand with the fixed starting bound T appends every
+// (r, rank) with r <= T to the query's candidate row (cap slots), and the
+// merge sorts the filled prefix and keeps k. Every row of the true top k has
+// r <= T, so the result is exact for every query whose row did not overflow;
+// those that did are flagged in redo.
+__global__ void overflow_flags_kernel(const uint32_t* __restrict__ cnt, uint32_t nq, uint32_t nsplit, uint32_t seg,
+                                      uint32_t cap, uint8_t* __restrict__ redo) {
+  const uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= nq) return;
+  uint32_t total = 0;
+  bool over = false;
+  for (uint32_t sp = 0; sp < nsplit; ++sp) {
+    const uint32_t c = cnt[(size_t)q * nsplit + sp];
+    over |= c > seg;
+    total += min(c, seg);
+  }
+  redo[q] = (over || total > cap) ? 1 : 0;
+}
+
+// Slots per (query, split) segment: twice an even share of the query's cap,
+// a power of two in [256, cap].
+inline uint32_t collect_segment(uint32_t cap, uint32_t nsplit) {
+  uint32_t seg = 256;
+  while (seg < cap && seg * nsplit < 2 * cap) seg <<= 1;
+  return std::min(seg, cap);
+}
+
+// Returns false (nothing launched) when the segments would exceed
+// COLLECT_MAX_ENTRIES slots.
+bool search_tc_collect(pxc_flat* h, const TcOperand& op, uint32_t nq, uint32_t k, const uint32_t* T, uint32_t cap,
+                       uint64_t* d_ids, float* d_dist, uint32_t* d_len, uint8_t* redo, cudaStream_t s) {
+  const uint32_t nq_pad = (nq + flat_tc::BM - 1) / flat_tc::BM * flat_tc::BM;
+  const uint32_t nqt = nq_pad / flat_tc::BM;
+  const uint32_t ntiles = (uint32_t)(op.nrank_pad / flat_tc::BN);
+  // choose_splits with KT 32 keeps nsplit <= 2048 / 32 = MERGE_MAX_SPLITS
+  const uint32_t nsplit_req = choose_splits(nqt, ntiles, h->ctx->sm_count, 32);
+  const uint32_t tps = (ntiles + nsplit_req - 1) / nsplit_req;
+  const uint32_t nsplit = (ntiles + tps - 1) / tps;
+  const uint32_t seg = collect_segment(cap, nsplit);
+  if ((uint64_t)nq * nsplit * seg > COLLECT_MAX_ENTRIES) return false;
+  h->c_cand.reserve((size_t)nq * nsplit * seg);
+  h->c_cnt.reserve((size_t)nq * nsplit);
+  h->bound.reserve(nq_pad);
+  h->done.reserve(nqt + (size_t)nqt * nsplit);
+  PXC_CUDA(cudaMemcpyAsync(h->bound.p, T, nq_pad * sizeof(uint32_t), cudaMemcpyDeviceToDevice, s));
+  PXC_CUDA(cudaMemsetAsync(h->done.p, 0, nqt * sizeof(uint32_t), s));
+  PXC_CUDA(cudaMemsetAsync(h->done.p + nqt, 0xFF, (size_t)nqt * nsplit * sizeof(uint32_t), s));
+  flat_tc::Params p;
+  p.norms = op.norms;
+  p.qcoef = nullptr;
+  p.qdelta = nullptr;
+  p.bound = reinterpret_cast<uint32_t*>(h->bound.p);
+  p.done_count = h->done.p;
+  p.done_list = h->done.p + nqt;
+  p.out_part = nullptr;
+  p.cand = h->c_cand.p;
+  p.cand_cnt = h->c_cnt.p;
+  p.cand_cap = seg;
+  p.status = h->d_status;
+  p.nq = nq;
+  p.k = 1;  // the (empty) list never publishes: the bound stays T
+  p.kblocks = h->dp / flat_tc::KB_BYTES;
+  p.ntiles = ntiles;
+  p.tiles_per_split = tps;
+  p.nsplit = nsplit;
+  p.stages = flat_tc::pick_stages<flat_tc::U8Scan>(p.kblocks);
+  p.wait_ns = (uint64_t)h->ctx->wait_ms * 1000000ull;
+  CUtensorMap tmap_q;
+  make_tmap_u8_2d(&tmap_q, h->q_u8.p, h->dp, nq_pad, flat_tc::KB_BYTES, flat_tc::BM);
+  const size_t smem = flat_tc::smem_bytes<flat_tc::U8Scan>(p.kblocks, p.stages);
+  launch_tc<1, flat_tc::U8Scan, true>(tmap_q, *op.tmap_x, p, dim3(nqt, nsplit), smem, s);
+  PXC_CUDA(cudaGetLastError());
+  merge_u8_kernel<<<nq, 256, cap * sizeof(uint64_t), s>>>(h->c_cand.p, nsplit, seg, cap, k, h->q_norm.p, op.rank_id,
+                                                           (uint32_t)op.nrank, d_ids, d_dist, d_len, h->c_cnt.p);
+  PXC_CUDA(cudaGetLastError());
+  overflow_flags_kernel<<<grid1d(nq, 256), 256, 0, s>>>(h->c_cnt.p, nq, nsplit, seg, cap, redo);
+  PXC_CUDA(cudaGetLastError());
+  h->ctx->launches += 3;  // scan + merge + flags
+  return true;
+}
+
+// Queries of a 0/1 flag array ([n]) as an index list; returns how many.
+uint32_t flagged_queries(pxc_flat* h, const uint8_t* flags, uint32_t n, uint32_t* idx, uint32_t* count,
+                         cudaStream_t s) {
+  size_t tb = 0;
+  thrust::counting_iterator<uint32_t> it(0);
+  PXC_CUDA(cub::DeviceSelect::Flagged(nullptr, tb, it, flags, idx, count, (int64_t)n, s));
+  h->tmp.reserve(std::max<size_t>(tb, 1));
+  PXC_CUDA(cub::DeviceSelect::Flagged(h->tmp.p, tb, it, flags, idx, count, (int64_t)n, s));
+  PXC_CUDA(cudaMemcpyAsync(h->h_flag, count, sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
+  PXC_CUDA(cudaStreamSynchronize(s));
+  h->ctx->launches += 2;  // two select passes
+  return static_cast<uint32_t>(*h->h_flag);
+}
+
+// The group launches (K1 per group of tiles, starting from the bound T when
+// given), the merge, the proof, and K1g for the queries it cannot prove.
+// h->q_u8 / q_norm hold the queries d_q; sets h->last_redo to the K1g count.
+void group_launches(pxc_flat* h, const TcOperand& op, const float* d_q, uint32_t nq, uint32_t k,
+                    const uint32_t* shared_t, const uint64_t* d_bitmap, uint64_t* d_ids, float* d_dist,
+                    uint32_t* d_len, cudaStream_t s) {
+  const uint64_t ntiles = op.nrank_pad / flat_tc::BN;
+  const uint32_t want = std::max<uint32_t>(2, (k * 2 + 24) / 25);
   const uint64_t tpg = (ntiles + want - 1) / want;
   const uint32_t ng = (uint32_t)((ntiles + tpg - 1) / tpg);
   h->g_ids.reserve((size_t)ng * nq * GROUP_K);
@@ -1068,7 +1313,6 @@ void search_tc_grouped(pxc_flat* h, const TcOperand& op, const float* d_q, uint3
   h->g_redo.reserve(nq);
   h->g_redo_idx.reserve(nq);
   h->g_redo_len.reserve(1);  // the count first; resized below if queries need K1g
-  ScanTimer timer(h, s);
   for (uint32_t g = 0; g < ng; ++g) {
     const uint64_t t0 = (uint64_t)g * tpg;
     const uint64_t t1 = std::min<uint64_t>(ntiles, t0 + tpg);
@@ -1081,26 +1325,18 @@ void search_tc_grouped(pxc_flat* h, const TcOperand& op, const float* d_q, uint3
     TcOperand gop{&tm, op.norms + r0, rows_pad, op.rank_id + r0, nreal, op.rows + r0 * h->dp};
     const size_t off = (size_t)g * nq;
     search_tc(h, gop, d_q, nq, GROUP_K, h->g_ids.p + off * GROUP_K, h->g_dist.p + off * GROUP_K,
-              h->g_len.p + off, s, false);
+              h->g_len.p + off, s, false, shared_t);
   }
   pxc_error err{};
   if (pxc_topk_merge(h->ctx, h->g_ids.p, h->g_dist.p, h->g_len.p, ng, nq, GROUP_K, k, d_ids, d_dist, d_len, s,
                      &err) != PXC_OK)
     throw make_failure((pxc_status)err.code, err.a, err.b, nullptr, "group merge: %s", err.detail);
-  timer.stop();
   group_check_kernel<<<grid1d(nq, 256), 256, 0, s>>>(h->g_ids.p, h->g_dist.p, h->g_len.p, ng, nq, d_ids, d_dist,
                                                       d_len, k, h->g_redo.p);
   PXC_CUDA(cudaGetLastError());
-  size_t tb = 0;
-  thrust::counting_iterator<uint32_t> it(0);
-  PXC_CUDA(cub::DeviceSelect::Flagged(nullptr, tb, it, h->g_redo.p, h->g_redo_idx.p, h->g_redo_len.p, (int64_t)nq, s));
-  h->tmp.reserve(std::max<size_t>(tb, 1));
-  PXC_CUDA(cub::DeviceSelect::Flagged(h->tmp.p, tb, it, h->g_redo.p, h->g_redo_idx.p, h->g_redo_len.p, (int64_t)nq, s));
-  PXC_CUDA(cudaMemcpyAsync(h->h_flag, h->g_redo_len.p, sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
-  PXC_CUDA(cudaStreamSynchronize(s));
-  const uint32_t nredo = static_cast<uint32_t>(*h->h_flag);
+  h->ctx->launches += 1;
+  const uint32_t nredo = flagged_queries(h, h->g_redo.p, nq, h->g_redo_idx.p, h->g_redo_len.p, s);
   h->last_redo = nredo;
-  h->ctx->launches += 3;  // check + two select passes
   if (nredo == 0) return;
   h->g_redo_q.reserve((size_t)nredo * h->dim);
   h->g_redo_ids.reserve((size_t)nredo * k);
@@ -1113,6 +1349,75 @@ void search_tc_grouped(pxc_flat* h, const TcOperand& op, const float* d_q, uint3
                                                h->g_redo_idx.p, k, d_ids, d_dist, d_len);
   PXC_CUDA(cudaGetLastError());
   h->ctx->launches += 2;
+}
+
+// Entry i of out = T[idx[i]] for i < n, "no bound" for n <= i < n_pad.
+__global__ void gather_bound_kernel(const uint32_t* __restrict__ T, const uint32_t* __restrict__ idx, uint32_t n,
+                                    uint32_t n_pad, uint32_t* __restrict__ out) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n_pad) out[i] = i < n ? T[idx[i]] : 0x3F3F3F3Fu;
+}
+
+// The sample is 1/divisor of the rows: SAMPLE_TARGET / k, or the diagnostic
+// option's value when it is set (0: no sample pass).
+uint64_t sample_divisor(const pxc_ctx* ctx, uint32_t k) {
+  if (ctx->opt_flat_group_sample >= 0) return (uint64_t)ctx->opt_flat_group_sample;
+  return std::max<uint64_t>(2, SAMPLE_TARGET / k);
+}
+
+void search_tc_grouped(pxc_flat* h, const TcOperand& op, const float* d_q, uint32_t nq, uint32_t k,
+                       const uint64_t* d_bitmap, uint64_t* d_ids, float* d_dist, uint32_t* d_len, cudaStream_t s) {
+  const uint64_t ntiles = op.nrank_pad / flat_tc::BN;
+  const uint32_t want = std::max<uint32_t>(2, (k * 2 + 24) / 25);
+  if (ntiles < want) {  // too few rows to split: the fp32 scan
+    search_generic(h, d_q, nq, k, d_bitmap, d_ids, d_dist, d_len, s);
+    return;
+  }
+  ScanTimer timer(h, s);
+  const uint32_t* shared_t = nullptr;
+  const uint64_t ns = (2 * k + SAMPLE_K - 1) / SAMPLE_K;  // <= SAMPLE_MAX / SAMPLE_K for k <= 128
+  const uint64_t sdiv = sample_divisor(h->ctx, k);
+  const uint64_t stiles = sdiv > 0 ? ntiles / sdiv / ns : 0;  // tiles per sample split
+  if (stiles >= 1) {
+    const uint32_t nq_pad = (nq + flat_tc::BM - 1) / flat_tc::BM * flat_tc::BM;
+    h->g_bound.reserve(nq_pad);
+    sample_bound(h, op, nq, k, (uint32_t)ns, (uint32_t)stiles, h->g_bound.p, s);
+    shared_t = h->g_bound.p;
+  }
+  const uint64_t cap = (uint64_t)h->ctx->opt_flat_collect_cap;
+  h->c_over.reserve(nq);
+  if (shared_t == nullptr || cap < 32 ||
+      !search_tc_collect(h, op, nq, k, shared_t, (uint32_t)cap, d_ids, d_dist, d_len, h->c_over.p, s)) {
+    group_launches(h, op, d_q, nq, k, shared_t, d_bitmap, d_ids, d_dist, d_len, s);
+    timer.stop();
+    return;
+  }
+  timer.stop();
+  // Queries whose candidate segments overflowed: the group launches, from
+  // their own (valid, if loose) T, on the gathered queries.
+  h->c_idx.reserve(nq);
+  h->c_n.reserve(1);
+  const uint32_t nover = flagged_queries(h, h->c_over.p, nq, h->c_idx.p, h->c_n.p, s);
+  h->last_redo = 0;
+  if (nover == 0) return;
+  const uint32_t np = (nover + flat_tc::BM - 1) / flat_tc::BM * flat_tc::BM;
+  h->c_q.reserve((size_t)nover * h->dim);
+  h->c_ids.reserve((size_t)nover * k);
+  h->c_dist.reserve((size_t)nover * k);
+  h->c_len.reserve(nover);
+  h->c_bound.reserve(np);
+  gather_queries_kernel<<<nover, 128, 0, s>>>(d_q, h->c_idx.p, h->dim, h->c_q.p);
+  gather_bound_kernel<<<grid1d(np, 256), 256, 0, s>>>(h->g_bound.p, h->c_idx.p, nover, np, h->c_bound.p);
+  PXC_CUDA(cudaMemsetAsync(h->q_bad.p, 0, sizeof(int), s));
+  prep_queries_u8_kernel<<<np, 128, 0, s>>>(h->c_q.p, nover, h->dim, h->dp, h->q_u8.p, h->q_norm.p, h->q_bad.p);
+  PXC_CUDA(cudaGetLastError());
+  h->ctx->launches += 3;
+  group_launches(h, op, h->c_q.p, nover, k, h->c_bound.p, d_bitmap, h->c_ids.p, h->c_dist.p, h->c_len.p, s);
+  h->last_redo += nover;
+  scatter_results_kernel<<<nover, 128, 0, s>>>(h->c_ids.p, h->c_dist.p, h->c_len.p, h->c_idx.p, k, d_ids, d_dist,
+                                               d_len);
+  PXC_CUDA(cudaGetLastError());
+  h->ctx->launches += 1;
 }
 
 // The K2 operand of the current mirror: centre, ranges, scale, f16 rows and
@@ -1830,7 +2135,7 @@ extern "C" pxc_status pxc_flat_search_noalloc(pxc_flat* h, const float* d_querie
     if (msmem > 48 * 1024)
       PXC_CUDA(cudaFuncSetAttribute(merge_u8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msmem));
     merge_u8_kernel<<<nq, 256, msmem, s>>>(part, nsplit, KT, cap, k, q_norm, h->rank_id.p, (uint32_t)h->nrank,
-                                           d_out_ids, d_out_dist, d_out_len);
+                                           d_out_ids, d_out_dist, d_out_len, nullptr);
     PXC_CUDA(cudaGetLastError());
     h->ctx->launches += 3;
     check_status_word(h->d_status, h->h_status, s, "allocation-free flat search");  // synchronises the stream

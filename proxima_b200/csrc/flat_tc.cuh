@@ -157,6 +157,15 @@ struct Params {
   uint32_t* done_count;    // [nqt] finished splits per query tile
   uint32_t* done_list;     // [nqt][nsplit] finished split ids in finishing order (~0u = not yet)
   uint64_t* out_part;      // [nq_pad][nsplit][KT] packed P::pack(r)<<32 | rank
+  // collect mode only: every (r, rank) with r <= the starting bound, unordered,
+  // in one private segment per (query, split)
+  uint64_t* cand = nullptr;      // [nq][nsplit][cand_cap] packed P::pack(r)<<32 | rank
+  uint32_t* cand_cnt = nullptr;  // [nq][nsplit] entries found (may exceed cand_cap: overflow)
+  uint32_t cand_cap = 0;
+  // 0: every split keeps its own list (no seeding from finished splits, no
+  // shared bound published), so the splits' lists hold disjoint rows
+  uint32_t share = 1;
+  uint32_t split_stride = 0;  // tiles between the first tiles of consecutive splits (0: tiles_per_split)
   uint32_t* status;        // device error word
   uint32_t nq;
   uint32_t k;              // the list position whose value is shared as the pruning bound (<= KT, see P::publish)
@@ -351,24 +360,47 @@ __device__ __forceinline__ bool chunk_hit(const uint32_t (&v)[32], const typenam
 // with the strict '<' keeps the list exact.
 // A FIFO takes a flagged chunk in pieces of P::FIFO_SLOTS columns or fewer,
 // draining first when the piece's entries would not fit.
-template <int KT, class P>
+//
+// In collect mode (COLLECT) the list stays empty and the bound fixed: a drain
+// appends the queued pairs to this thread's own segment of candidates in
+// global memory instead (a register counter, no atomics; entries past the
+// segment's capacity are counted but not written, which the host reads as an
+// overflow).
+struct Sink {
+  uint64_t* dst;  // this (query, split)'s segment (nullptr: padding query)
+  uint32_t n;     // entries found so far
+  uint32_t cap;
+};
+
+template <int KT, class P, bool COLLECT>
 __device__ __forceinline__ void fifo_drain(const uint2* fifo, uint32_t& cnt, uint32_t lane,
                                            typename P::T (&lr)[KT], uint32_t (&lk)[KT],
-                                           typename P::T shared_bound) {
+                                           typename P::T shared_bound, Sink& sink) {
   using T = typename P::T;
-  const T above = P::next_up(shared_bound);  // admit r <= shared_bound
-  for (uint32_t i = 0; i < cnt; ++i) {
-    const uint2 e = fifo[i * 32 + lane];
-    const T r = *reinterpret_cast<const T*>(&e.x);
-    if (r < min(lr[KT - 1], above)) insert_sorted<KT, T>(lr, lk, r, e.y);
+  if constexpr (COLLECT) {
+    if (sink.dst != nullptr) {
+      for (uint32_t i = 0; i < cnt && sink.n + i < sink.cap; ++i) {
+        const uint2 e = fifo[i * 32 + lane];
+        const T r = *reinterpret_cast<const T*>(&e.x);
+        sink.dst[sink.n + i] = (static_cast<uint64_t>(P::pack(r)) << 32) | e.y;
+      }
+    }
+    sink.n += cnt;
+  } else {
+    const T above = P::next_up(shared_bound);  // admit r <= shared_bound
+    for (uint32_t i = 0; i < cnt; ++i) {
+      const uint2 e = fifo[i * 32 + lane];
+      const T r = *reinterpret_cast<const T*>(&e.x);
+      if (r < min(lr[KT - 1], above)) insert_sorted<KT, T>(lr, lk, r, e.y);
+    }
   }
   cnt = 0;
 }
 
-template <int KT, class P>
+template <int KT, class P, bool COLLECT>
 __device__ __forceinline__ void fifo_push_chunk(const typename P::T (&r)[32], typename P::T thr, uint32_t rank0,
                                                 uint2* fifo, uint32_t& cnt, uint32_t lane, typename P::T (&lr)[KT],
-                                                uint32_t (&lk)[KT], typename P::T shared_bound) {
+                                                uint32_t (&lk)[KT], typename P::T shared_bound, Sink& sink) {
   constexpr int PIECE = P::FIFO_SLOTS < 32 ? P::FIFO_SLOTS : 32;
   static_assert(32 % PIECE == 0, "FIFO pieces must tile the chunk");
 #pragma unroll
@@ -376,7 +408,8 @@ __device__ __forceinline__ void fifo_push_chunk(const typename P::T (&r)[32], ty
     uint32_t mask = 0;
 #pragma unroll
     for (int j = 0; j < PIECE; ++j) mask |= (r[j0 + j] < thr ? 1u : 0u) << j;
-    if (cnt + __popc(mask) > (uint32_t)P::FIFO_SLOTS) fifo_drain<KT, P>(fifo, cnt, lane, lr, lk, shared_bound);
+    if (cnt + __popc(mask) > (uint32_t)P::FIFO_SLOTS)
+      fifo_drain<KT, P, COLLECT>(fifo, cnt, lane, lr, lk, shared_bound, sink);
 #pragma unroll
     for (int j = 0; j < PIECE; ++j) {
       if (mask & (1u << j)) {
@@ -387,7 +420,22 @@ __device__ __forceinline__ void fifo_push_chunk(const typename P::T (&r)[32], ty
   }
 }
 
+// Collect mode's scan of one chunk: ruled out by the lower bound, or r is
+// formed once, its minimum taken and, for a lane with a value within thr,
+// the admitted pairs queued.
 template <int KT, class P>
+__device__ __forceinline__ void collect_chunk(const uint32_t (&v)[32], const typename P::T* nrm, typename P::T hmin,
+                                              float c, typename P::T thr, uint32_t rank0, uint2* fifo, uint32_t& cnt,
+                                              uint32_t lane, typename P::T (&lr)[KT], uint32_t (&lk)[KT],
+                                              typename P::T shared_bound, Sink& sink) {
+  const bool maybe = P::lower_bound(chunk_max_bits(v), hmin, c) < thr;
+  if (!__any_sync(0xFFFFFFFFu, maybe)) return;
+  typename P::T r[32];
+  const typename P::T m = chunk_r<P>(v, nrm, c, r);
+  if (maybe && m < thr) fifo_push_chunk<KT, P, true>(r, thr, rank0, fifo, cnt, lane, lr, lk, shared_bound, sink);
+}
+
+template <int KT, class P, bool COLLECT = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     flat_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
                      const __grid_constant__ CUtensorMap tmap_x, const Params p) {
@@ -414,7 +462,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t qtile = blockIdx.x, split = blockIdx.y;
-  const uint32_t t_begin = split * p.tiles_per_split;
+  const uint32_t t_begin = split * (p.split_stride != 0 ? p.split_stride : p.tiles_per_split);
   const uint32_t t_end = min(t_begin + p.tiles_per_split, p.ntiles);
   const uint32_t ntile_local = t_end > t_begin ? t_end - t_begin : 0;
 
@@ -558,7 +606,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       lr[i] = P::big();
       lk[i] = 0xFFFFFFFFu;
     }
-    if (q < p.nq) seed_from_finished<KT, P>(p, qtile, split, q, lr, lk);
+    Sink sink{nullptr, 0, 0};
+    if constexpr (COLLECT) {
+      if (q < p.nq) sink = Sink{p.cand + ((size_t)q * p.nsplit + split) * p.cand_cap, 0, p.cand_cap};
+    } else {
+      if (q < p.nq && p.share) seed_from_finished<KT, P>(p, qtile, split, q, lr, lk);
+    }
     T shared_bound = load_bound<P>(bound_ptr);  // prune r > shared_bound
     T published = P::big();
     // ||x||^2 of tile t sits in this warp's slot t & 1; tile t+1's is fetched
@@ -595,15 +648,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const T fresh_bound = load_bound<P>(bound_ptr);
       uint32_t va[32], vb[32];
       uint32_t hit = 0;  // bit c: chunk c holds a candidate for this lane
+      if constexpr (COLLECT) {
+        // Collect mode flags about 20 times more chunks (its bound is near the
+        // 100th row, not the 10th): a chunk's admitted pairs are queued from
+        // the values the exact minimum was taken on, instead of re-reading it.
 #pragma unroll 1
-      for (uint32_t c = 0; c < BN / 32; c += 2) {
-        // two chunks per wait: the read latency, not the arithmetic, bounds
-        // this loop (and nothing runs while a read is in flight)
-        tmem_ld_32x32b_x32(taddr + c * 32, va);
-        tmem_ld_32x32b_x32(taddr + (c + 1) * 32, vb);
-        tmem_ld_wait();
-        hit |= static_cast<uint32_t>(chunk_hit<P>(va, nrm + c * 32, nmin[c], coef, thr)) << c;
-        hit |= static_cast<uint32_t>(chunk_hit<P>(vb, nrm + (c + 1) * 32, nmin[c + 1], coef, thr)) << (c + 1);
+        for (uint32_t c = 0; c < BN / 32; c += 2) {
+          tmem_ld_32x32b_x32(taddr + c * 32, va);
+          tmem_ld_32x32b_x32(taddr + (c + 1) * 32, vb);
+          tmem_ld_wait();
+          collect_chunk<KT, P>(va, nrm + c * 32, nmin[c], coef, thr, rank_base + c * 32, wfifo, fifo_cnt, lane, lr,
+                               lk, shared_bound, sink);
+          collect_chunk<KT, P>(vb, nrm + (c + 1) * 32, nmin[c + 1], coef, thr, rank_base + (c + 1) * 32, wfifo,
+                               fifo_cnt, lane, lr, lk, shared_bound, sink);
+        }
+      } else {
+#pragma unroll 1
+        for (uint32_t c = 0; c < BN / 32; c += 2) {
+          // two chunks per wait: the read latency, not the arithmetic, bounds
+          // this loop (and nothing runs while a read is in flight)
+          tmem_ld_32x32b_x32(taddr + c * 32, va);
+          tmem_ld_32x32b_x32(taddr + (c + 1) * 32, vb);
+          tmem_ld_wait();
+          hit |= static_cast<uint32_t>(chunk_hit<P>(va, nrm + c * 32, nmin[c], coef, thr)) << c;
+          hit |= static_cast<uint32_t>(chunk_hit<P>(vb, nrm + (c + 1) * 32, nmin[c + 1], coef, thr)) << (c + 1);
+        }
       }
       // Flagged chunks (one vote per tile) are re-read from TMEM and their
       // admitted pairs queued in rank order; the accumulator is released right
@@ -626,12 +695,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         {
           T r[32];
           chunk_r<P>(va, nrm + ca * 32, coef, r);
-          fifo_push_chunk<KT, P>(r, thr, rank_base + ca * 32, wfifo, fifo_cnt, lane, lr, lk, shared_bound);
+          fifo_push_chunk<KT, P, COLLECT>(r, thr, rank_base + ca * 32, wfifo, fifo_cnt, lane, lr, lk, shared_bound,
+                                          sink);
         }
         if (cb < BN / 32) {
           T r[32];
           chunk_r<P>(vb, nrm + cb * 32, coef, r);
-          fifo_push_chunk<KT, P>(r, thr, rank_base + cb * 32, wfifo, fifo_cnt, lane, lr, lk, shared_bound);
+          fifo_push_chunk<KT, P, COLLECT>(r, thr, rank_base + cb * 32, wfifo, fifo_cnt, lane, lr, lk, shared_bound,
+                                          sink);
         }
       }
       tc_fence_before();
@@ -639,7 +710,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // This warp finished reading slot (t+1)&1 during tile t-1.
       if (t + 1 < ntile_local) stage_norms<P>(wnorm + ((t + 1) & 1) * BN, wmin + ((t + 1) & 1) * CHUNKS, nx0, nx1, lane);
       // insertions happen while the tensor core fills the next tile
-      if (fifo_cnt) fifo_drain<KT, P>(wfifo, fifo_cnt, lane, lr, lk, shared_bound);
+      if (fifo_cnt) fifo_drain<KT, P, COLLECT>(wfifo, fifo_cnt, lane, lr, lk, shared_bound, sink);
       __syncwarp();
       // Share the bound with the other splits of this query tile: the k-th
       // value of this split's list (k <= KT, selected without dynamic indexing).
@@ -647,13 +718,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
       for (int i = 0; i < KT; ++i) kth = (i + 1 == (int)p.k) ? lr[i] : kth;
       const T pub = P::publish(kth, lr[KT - 1], delta);
-      if (pub < published) {
+      if (pub < published && p.share) {
         published = pub;
         atomicMin(bound_ptr, P::pack(published));
       }
       shared_bound = min(shared_bound, fresh_bound);
     }
-    if (q < p.nq) {
+    if (COLLECT && q < p.nq) p.cand_cnt[(size_t)q * p.nsplit + split] = sink.n;
+    if (!COLLECT && q < p.nq) {
       uint64_t* dst = p.out_part + ((size_t)q * p.nsplit + split) * KT;
 #pragma unroll
       for (int i = 0; i < KT; ++i)

@@ -375,8 +375,8 @@ class FlatIndex:
         return int(self._lib.pxc_flat_path(self.handle))
 
     def last_redone(self) -> int:
-        """Queries of the last search (32 < k <= 128, tensor-core path) whose grouped answer was
-        searched again on the fp32 scan because it could not be proven exact."""
+        """Queries of the last search that the first tensor-core pass did not settle and that were
+        answered again (see pxc_flat_last_redone)."""
         return int(self._lib.pxc_flat_last_redone(self.handle))
 
 

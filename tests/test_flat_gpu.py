@@ -169,27 +169,70 @@ def test_c2_grouped_tensor_core_path_bit_exact(c2_small, k):
     got = idx.search_prepared_batch(q, k)
     ref = pxo.flat_search(db, q, k, pxo.EUCLIDEAN)
     _assert_same(got, ref, len(q))
-    assert idx.last_redone() <= 3  # blob rows are spread over the groups: nearly every query is proven
+    assert idx.last_redone() <= 3  # no collect row overflows; blob rows are spread over the groups
 
 
 def test_c2_grouped_redo_when_neighbours_share_a_group(c2_small):
     """Queries whose top 100 crowd into one row group (40 exact copies in consecutive
-    ids) fail the grouped proof and are answered by the fp32 scan; all stay exact."""
+    ids) fail the group launches' proof and are answered by the fp32 scan; the
+    collect launch (the default) needs no proof and answers all but those whose
+    candidate segments overflow. All stay exact."""
     db, q = c2_small
     rows = db[:40_000].copy()
     for i in range(24):
         rows[1000 + i * 1200:1000 + i * 1200 + 40] = q[i]
-    from proxima_b200.index import FlatIndex
-    idx = FlatIndex.from_array(VectorSpace(128, Metric.EUCLIDEAN), rows)
-    got = idx.search_prepared_batch(q[:200], 100)
+    from proxima_b200.index import Context, FlatIndex
     ref = pxo.flat_search(rows, q[:200], 100, pxo.EUCLIDEAN)
-    _assert_same(got, ref, 200)
+    ctx = Context(0)
+    ctx.set_option("flat_collect_cap", 0)  # the group launches
+    idx = FlatIndex.from_array(VectorSpace(128, Metric.EUCLIDEAN), rows, ctx=ctx)
+    _assert_same(idx.search_prepared_batch(q[:200], 100), ref, 200)
     assert idx.last_redone() >= 24
+    idx = FlatIndex.from_array(VectorSpace(128, Metric.EUCLIDEAN), rows)
+    _assert_same(idx.search_prepared_batch(q[:200], 100), ref, 200)
+    assert idx.last_redone() < 24  # only queries whose candidate segments overflowed
     # small stores (fewer tiles than groups) take the fp32 scan directly
     small = FlatIndex.from_array(VectorSpace(128, Metric.EUCLIDEAN), db[:700])
     got = small.search_prepared_batch(q[:50], 128)
     ref = pxo.flat_search(db[:700], q[:50], 128, pxo.EUCLIDEAN)
     _assert_same(got, ref, 50)
+
+
+@pytest.mark.parametrize("sample,cap", [(-1, 2048), (0, 2048), (1, 2048), (4, 2048), (64, 2048), (4, 0), (4, 32),
+                                        (-1, 256)])
+def test_c2_grouped_shared_bound_sample_pass(c2_small, sample, cap):
+    """32 < k <= 128. The sample pass (1/sample of the rows, -1 = 800/k, 0 =
+    none) gives the bound T that the single collect launch (cap slots per
+    query) or the group launches (cap 0) start from; with cap 32 every query
+    overflows its slots and is answered again by the group launches. Results
+    stay exact at any setting, also when many rows tie T exactly (copies of a
+    query spread over every group) and when the rows are stored sorted (a
+    sample far from a query's neighbours, many overflows)."""
+    db, q = c2_small
+    from proxima_b200.index import Context, FlatIndex
+    ctx = Context(0)  # a context of its own: the options stay off the shared default one
+    ctx.set_option("flat_group_sample", sample)
+    ctx.set_option("flat_collect_cap", cap)
+    idx = FlatIndex.from_array(VectorSpace(128, Metric.EUCLIDEAN), db, ctx=ctx)
+    for k in (33, 100, 128):
+        got = idx.search_prepared_batch(q[:128], k)
+        ref = pxo.flat_search(db, q[:128], k, pxo.EUCLIDEAN)
+        _assert_same(got, ref, 128)
+    rows = db.copy()
+    rows[::97] = q[0]  # 619 copies of query 0: its top 128 all tie at distance 0
+    rows[50::89] = q[1] + (q[1] < 255)  # near copies of query 1 at one equal distance
+    tie = FlatIndex.from_array(VectorSpace(128, Metric.EUCLIDEAN), rows, ctx=ctx)
+    for k in (100, 128):
+        got = tie.search_prepared_batch(q[:64], k)
+        ref = pxo.flat_search(rows, q[:64], k, pxo.EUCLIDEAN)
+        _assert_same(got, ref, 64)
+    if cap == 32 and sample:
+        assert tie.last_redone() >= 64  # every query's candidates overflowed
+    order = np.lexsort(db.T[::-1])  # rows sorted: neighbours sit together in id order
+    srt = FlatIndex.from_array(VectorSpace(128, Metric.EUCLIDEAN), db[order], ctx=ctx)
+    got = srt.search_prepared_batch(q[:96], 100)
+    ref = pxo.flat_search(db[order], q[:96], 100, pxo.EUCLIDEAN)
+    _assert_same(got, ref, 96)
 
 
 def test_c2_shuffled_ids_removed_slots_and_duplicates(c2_small):
