@@ -30,10 +30,13 @@
 //               chunks per wait); per chunk a lower bound of r (smallest
 //               row term, largest product) against the thread's admission
 //               bound, and r = h - 2*dot with a tree min only where some
-//               lane cannot rule its chunk out; chunks where some lane has
-//               a candidate take the slow path, which re-reads them from
-//               TMEM and queues their admitted pairs for insertion into a
-//               sorted register list of KT entries.
+//               lane cannot rule its chunk out, where a lane with a
+//               candidate queues its admitted pairs at once (KT <= 16; with
+//               KT = 32 the flagged chunks are re-read from TMEM after the
+//               scan instead) for insertion into a sorted register list of
+//               KT entries after the accumulator is released.
+// Collect mode (COLLECT) keeps no list: the bound stays the caller's T and
+// the admitted pairs go to a segment of HBM per (query, split).
 // The halves ping-pong: while the tensor core fills one half's accumulator
 // for tile t, the other half's epilogue drains tile t-1 (or t).
 // The CTAs of one query tile share a per-query bound in global memory (each
@@ -54,6 +57,7 @@
 // candidates, not answers: the caller re-ranks them exactly and proves each
 // query's answer with an error bound on the screen (flat.cu).
 #pragma once
+#include <type_traits>
 #include "common.cuh"
 #include "sm100.cuh"
 
@@ -420,11 +424,11 @@ __device__ __forceinline__ void fifo_push_chunk(const typename P::T (&r)[32], ty
   }
 }
 
-// Collect mode's scan of one chunk: ruled out by the lower bound, or r is
-// formed once, its minimum taken and, for a lane with a value within thr,
-// the admitted pairs queued.
-template <int KT, class P>
-__device__ __forceinline__ void collect_chunk(const uint32_t (&v)[32], const typename P::T* nrm, typename P::T hmin,
+// The scan of one chunk with the push inline: ruled out by the lower bound,
+// or r is formed once, its minimum taken and, for a lane with a value within
+// thr, the admitted pairs queued.
+template <int KT, class P, bool COLLECT>
+__device__ __forceinline__ void scan_push_chunk(const uint32_t (&v)[32], const typename P::T* nrm, typename P::T hmin,
                                               float c, typename P::T thr, uint32_t rank0, uint2* fifo, uint32_t& cnt,
                                               uint32_t lane, typename P::T (&lr)[KT], uint32_t (&lk)[KT],
                                               typename P::T shared_bound, Sink& sink) {
@@ -432,7 +436,7 @@ __device__ __forceinline__ void collect_chunk(const uint32_t (&v)[32], const typ
   if (!__any_sync(0xFFFFFFFFu, maybe)) return;
   typename P::T r[32];
   const typename P::T m = chunk_r<P>(v, nrm, c, r);
-  if (maybe && m < thr) fifo_push_chunk<KT, P, true>(r, thr, rank0, fifo, cnt, lane, lr, lk, shared_bound, sink);
+  if (maybe && m < thr) fifo_push_chunk<KT, P, COLLECT>(r, thr, rank0, fifo, cnt, lane, lr, lk, shared_bound, sink);
 }
 
 template <int KT, class P, bool COLLECT = false>
@@ -648,18 +652,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const T fresh_bound = load_bound<P>(bound_ptr);
       uint32_t va[32], vb[32];
       uint32_t hit = 0;  // bit c: chunk c holds a candidate for this lane
-      if constexpr (COLLECT) {
-        // Collect mode flags about 20 times more chunks (its bound is near the
-        // 100th row, not the 10th): a chunk's admitted pairs are queued from
-        // the values the exact minimum was taken on, instead of re-reading it.
+      if constexpr (COLLECT || (std::is_same<P, U8Scan>::value && KT <= 16)) {
+        // A chunk's admitted pairs are queued from the values its exact minimum
+        // was taken on instead of re-reading the chunk after the scan (K1 with
+        // lists of up to 16 entries, and collect mode, which flags far more
+        // chunks: its bound sits near the 800th row). Longer lists keep the
+        // re-read: their registers do not leave room for it.
 #pragma unroll 1
         for (uint32_t c = 0; c < BN / 32; c += 2) {
           tmem_ld_32x32b_x32(taddr + c * 32, va);
           tmem_ld_32x32b_x32(taddr + (c + 1) * 32, vb);
           tmem_ld_wait();
-          collect_chunk<KT, P>(va, nrm + c * 32, nmin[c], coef, thr, rank_base + c * 32, wfifo, fifo_cnt, lane, lr,
+          scan_push_chunk<KT, P, COLLECT>(va, nrm + c * 32, nmin[c], coef, thr, rank_base + c * 32, wfifo, fifo_cnt, lane, lr,
                                lk, shared_bound, sink);
-          collect_chunk<KT, P>(vb, nrm + (c + 1) * 32, nmin[c + 1], coef, thr, rank_base + (c + 1) * 32, wfifo,
+          scan_push_chunk<KT, P, COLLECT>(vb, nrm + (c + 1) * 32, nmin[c + 1], coef, thr, rank_base + (c + 1) * 32, wfifo,
                                fifo_cnt, lane, lr, lk, shared_bound, sink);
         }
       } else {
