@@ -1365,15 +1365,41 @@ uint64_t sample_divisor(const pxc_ctx* ctx, uint32_t k) {
   return std::max<uint64_t>(2, SAMPLE_TARGET / k);
 }
 
+// Query batches larger than this run in chunks, so that the collect launch's
+// segments (up to 2 x 2,048 slots per query) stay within COLLECT_MAX_ENTRIES.
+// Measured on C2 at k = 100: 10,000 queries as 8,192 + 1,808 take 5.33 ms,
+// in one piece 6.23 ms, in chunks of 4,096 5.90 ms.
+constexpr uint32_t GROUPED_CHUNK_Q = 8192;
+
 void search_tc_grouped(pxc_flat* h, const TcOperand& op, const float* d_q, uint32_t nq, uint32_t k,
-                       const uint64_t* d_bitmap, uint64_t* d_ids, float* d_dist, uint32_t* d_len, cudaStream_t s) {
+                       const uint64_t* d_bitmap, uint64_t* d_ids, float* d_dist, uint32_t* d_len, cudaStream_t s,
+                       bool timed = true) {
+  if (nq > GROUPED_CHUNK_Q) {
+    ScanTimer timer(h, s, timed);  // all chunks
+    uint32_t redone = 0;
+    for (uint32_t q0 = 0; q0 < nq; q0 += GROUPED_CHUNK_Q) {
+      const uint32_t n = std::min(GROUPED_CHUNK_Q, nq - q0);
+      const uint32_t np = (n + flat_tc::BM - 1) / flat_tc::BM * flat_tc::BM;
+      const float* q = d_q + (size_t)q0 * h->dim;
+      // this chunk's u8 queries and norms at the front of the query buffers
+      prep_queries_u8_kernel<<<np, 128, 0, s>>>(q, n, h->dim, h->dp, h->q_u8.p, h->q_norm.p, h->q_bad.p);
+      PXC_CUDA(cudaGetLastError());
+      h->ctx->launches += 1;
+      search_tc_grouped(h, op, q, n, k, d_bitmap, d_ids + (size_t)q0 * k, d_dist + (size_t)q0 * k, d_len + q0, s,
+                        false);
+      redone += h->last_redo;
+    }
+    timer.stop();
+    h->last_redo = redone;
+    return;
+  }
   const uint64_t ntiles = op.nrank_pad / flat_tc::BN;
   const uint32_t want = std::max<uint32_t>(2, (k * 2 + 24) / 25);
   if (ntiles < want) {  // too few rows to split: the fp32 scan
     search_generic(h, d_q, nq, k, d_bitmap, d_ids, d_dist, d_len, s);
     return;
   }
-  ScanTimer timer(h, s);
+  ScanTimer timer(h, s, timed);
   const uint32_t* shared_t = nullptr;
   const uint64_t ns = (2 * k + SAMPLE_K - 1) / SAMPLE_K;  // <= SAMPLE_MAX / SAMPLE_K for k <= 128
   const uint64_t sdiv = sample_divisor(h->ctx, k);

@@ -172,6 +172,20 @@ def test_c2_grouped_tensor_core_path_bit_exact(c2_small, k):
     assert idx.last_redone() <= 3  # no collect row overflows; blob rows are spread over the groups
 
 
+def test_c2_grouped_large_batch_runs_in_chunks(c2_small):
+    """More than 8,192 queries at 32 < k <= 128 run in chunks of 8,192 (each with
+    its own sample pass and collect launch); results stay exact across the
+    chunk boundary."""
+    db, _ = c2_small
+    q = fixtures.blobs_u8(8192 + 300, 128, 1024, fixtures.C2_CENTRES, fixtures.C2_QUERIES)
+    from proxima_b200.index import FlatIndex
+    idx = FlatIndex.from_array(VectorSpace(128, Metric.EUCLIDEAN), db)
+    gi, gd, gl = idx.search_prepared_batch(q, 48)
+    pick = np.unique(np.concatenate([np.arange(0, len(q), 97), np.arange(8150, 8250), np.arange(len(q) - 40, len(q))]))
+    ri, rd, rl = pxo.flat_search(db, q[pick], 48, pxo.EUCLIDEAN)
+    _assert_same((gi[pick], gd[pick], gl[pick]), (ri, rd, rl), len(pick))
+
+
 def test_c2_grouped_redo_when_neighbours_share_a_group(c2_small):
     """Queries whose top 100 crowd into one row group (40 exact copies in consecutive
     ids) fail the group launches' proof and are answered by the fp32 scan; the
