@@ -67,13 +67,18 @@ def parse():
 
 
 def k1_source_hash() -> str:
-    """SHA-256 of the sources that decide K1's memory traffic (the kernel and its launch), so that a
-    DRAM-traffic figure captured by ncu is reported only for the kernel it was measured on."""
+    """SHA-256 of the sources that decide K1's memory traffic (the kernel and its launch), comments
+    removed, so that a DRAM-traffic figure captured by ncu is reported only for the code it was
+    measured on."""
     import hashlib
+    import re
 
     h = hashlib.sha256()
     for name in ("flat_tc.cuh", "flat.cu", "sm100.cuh"):
-        h.update((ROOT / "proxima_b200" / "csrc" / name).read_bytes())
+        text = (ROOT / "proxima_b200" / "csrc" / name).read_text()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)  # block comments
+        text = re.sub(r"//[^\n]*", "", text)  # line comments
+        h.update(text.encode())
     return h.hexdigest()
 
 

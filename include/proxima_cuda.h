@@ -186,10 +186,10 @@ uint32_t pxc_flat_last_redone(const pxc_flat* h);
  * euclidean store of integers in [0,255] (the tensor-core scan), queries of
  * integers in [0,255], and a device mirror already built by an earlier
  * pxc_flat_len or search (PXC_CAPACITY / PXC_CONFIGURATION otherwise). The
- * first call on a device looks up the array's address; make it before any
- * stream capture. Each call synchronises `stream` twice (after checking that
- * the queries are integers, and at the end) and returns after its work has
- * finished. Calls share the array; within a process they are serialised.
+ * first call on a device looks up the array's address. Each call
+ * synchronises `stream` twice (after checking that the queries are integers,
+ * and at the end) and returns after its work has finished. Calls share the
+ * array; within a process they are serialised.
  * Device buffers. */
 pxc_status pxc_flat_search_noalloc(pxc_flat* h, const float* d_queries, uint32_t nq, uint32_t k,
                                    uint64_t* d_out_ids, float* d_out_dist, uint32_t* d_out_len,

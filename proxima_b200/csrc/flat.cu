@@ -2038,9 +2038,9 @@ void flat_search_host(pxc_flat* h, const float* queries, uint32_t nq, uint32_t k
 // serialises its calls and returns only after its work has finished.
 //
 // Set-up: the first call on a device looks up the array's device address with
-// cudaGetSymbolAddress (with that device current); make that first call
-// before any stream capture. Every call synchronises its stream (after the
-// query check and at the end), so it returns with its work finished.
+// cudaGetSymbolAddress (with that device current). Every call synchronises
+// its stream (after the query check and at the end), so it returns with its
+// work finished.
 // ---------------------------------------------------------------------------
 namespace {
 constexpr uint32_t NOALLOC_MAX_QUERIES = 2048;
