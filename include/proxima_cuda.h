@@ -150,7 +150,8 @@ pxc_status pxc_flat_search_where(pxc_flat* h, pxc_columns* cols, const pxc_condi
 /* Same, with DEVICE buffers on the context's device, ordered on `stream`
  * (a cudaStream_t; NULL = the context's stream). The call waits on the
  * stream for small host decisions (whether the queries are integers in
- * [0,255]; with 32 < k <= 128, which queries the grouped scan proved exact)
+ * [0,255]; with 32 < k <= 128, which queries overflowed their candidate
+ * slots or were not proven exact by the row-group launches)
  * and returns with the result kernels enqueued; the caller synchronises the
  * stream before reading the outputs. */
 pxc_status pxc_flat_search_device(pxc_flat* h, const float* d_queries, uint32_t nq,
