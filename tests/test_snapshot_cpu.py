@@ -6,8 +6,9 @@ host CRC (slicing-by-8) and its combine are checked against it. The oracle's
 codec restatement is checked against the fixed byte layouts the reference's
 codec and snapshot tests assert (codec.rs tests, snapshot.rs:120-200), and the
 library's host-only snapshot reader (pxc_snapshot_peek) is checked against the
-oracle's decode on valid images and on every class of damaged image,
-including which error wins when there are two.
+oracle's decode on valid images, on every class of damaged image (including
+which error wins when there are two), and on every truncation and single-byte
+change of a small image.
 """
 import os
 import struct
@@ -217,6 +218,51 @@ def test_from_parts_damage():
     _expect(_variant(centroids=p["centroids"].reshape(-1)[:-1]), Corruption, "ivfpq centroids")
     _expect(_variant(codebooks=p["codebooks"][:-8]), Corruption, "product quantizer")
     _expect(_variant(metric=pxo.INNER_PRODUCT), Configuration, "metric")
+
+
+def _outcome_library(img):
+    try:
+        S.peek(img)
+        return ("ok", None)
+    except Corruption as e:
+        return ("corrupt", e.structure)
+    except Configuration as e:
+        return ("config", e.parameter)
+
+
+def _outcome_oracle(img):
+    try:
+        pxo.snapshot_decode_ivfpq(img)
+        return ("ok", None)
+    except pxo.SnapshotError as e:
+        return (e.kind, e.where)
+
+
+@pytest.mark.parametrize("trained", [True, False])
+def test_every_truncation_and_byte_change_agrees_with_the_oracle(trained):
+    """Every truncation of the body and four changes of every body byte (two bit
+    flips, 0x00, 0xFF), each resealed with a valid length and checksum so that
+    the body parser and from_parts see them: the library's reader accepts
+    exactly what the oracle's decode accepts and names the same error class and
+    structure or parameter. The index-kind byte is left alone (kinds 1 and 2
+    are other bodies)."""
+    img, _ = _image(trained=trained)
+    body = img[28:-4]
+    differ = []
+    for cut in range(len(body)):
+        x = _reseal(img, body[:cut])
+        a, b = _outcome_library(x), _outcome_oracle(x)
+        if a != b:
+            differ.append(("truncated", cut, a, b))
+    for pos in range(len(body)):
+        if pos == 5:  # the index kind
+            continue
+        for v in {body[pos] ^ 0x01, body[pos] ^ 0x80, 0x00, 0xFF} - {body[pos]}:
+            x = _reseal(img, body[:pos] + bytes([v]) + body[pos + 1:])
+            a, b = _outcome_library(x), _outcome_oracle(x)
+            if a != b:
+                differ.append(("byte", pos, v, a, b))
+    assert not differ, differ[:10]
 
 
 def test_checksum_wins_over_a_body_error():
